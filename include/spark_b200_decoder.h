@@ -1,0 +1,109 @@
+/*
+ * spark_b200 decoder entry points: the fused steps of one decode step of the
+ * synthetic 4B-class decoder (RMSNorm + QKV + RoPE, INT8 KV append, INT8-KV
+ * attention with device-resident lengths, o_proj + residual, RMSNorm +
+ * gate/up + SwiGLU, down + residual, RMSNorm + lm_head + greedy argmax).
+ *
+ * They replace, in fused form, the per-layer graph the reference model builds
+ * from its operators: Attention.__call__ (spark_mlx_llm/model.py:172-207),
+ * TransformerBlock.__call__ (:249-262), the compiled residual/RMSNorm/FFN graph
+ * (spark_mlx_llm/ops/ffn.py:83-105) and the greedy sampler of the generation
+ * loop (spark_mlx_llm/generation.py:411-446 via mlx_lm). Same conventions as
+ * spark_b200.h: device pointers, caller-owned buffers, status codes, and
+ * per-step values (positions, lengths, tokens) read from device memory so a
+ * whole decode step can be captured once in a CUDA graph and replayed.
+ */
+#ifndef SPARK_B200_DECODER_H
+#define SPARK_B200_DECODER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#include "spark_b200.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Weight formats of sb_linear_ex. */
+#define SB_WEIGHT_AFFINE4 0 /* MLX affine 4-bit: uint32 [N, K/8], scales/biases [N, K/G] */
+#define SB_WEIGHT_AFFINE8 1 /* MLX affine 8-bit: uint32 [N, K/4], scales/biases [N, K/G] */
+#define SB_WEIGHT_INT8_PC 2 /* int8 [N, K] with fp32 scales [N] (biases unused)        */
+#define SB_WEIGHT_BF16 3    /* bf16 [N, K]                                             */
+
+/* Epilogues of sb_linear_ex. */
+#define SB_EPI_STORE 0  /* y[m, n] = T(acc)                                              */
+#define SB_EPI_RESID 1  /* y[m, n] = T(residual[m, n] + T(acc))                          */
+#define SB_EPI_SWIGLU 2 /* y[m, n] = T(silu(T(gate)) * T(up)); weight = gate, weight2 = up */
+#define SB_EPI_ROPE 3   /* QKV rows -> q/k/v [B, heads, L, head_dim], RoPE on q and k    */
+#define SB_EPI_ARGMAX 4 /* argmax_keys[m] = max over n of (fp32 logit, lowest index)     */
+
+typedef struct sb_linear_ex_desc {
+  const void* x; /* [M, ldx] activations */
+  int x_dtype;   /* SB_DTYPE_BF16 or SB_DTYPE_F16 */
+  int64_t ldx;   /* 0 = K */
+  int64_t M, N, K;
+  int weight_format;
+  const void* weight; /* see SB_WEIGHT_* */
+  const void* scales;
+  const void* biases;
+  const void* weight2; /* SB_EPI_SWIGLU: up projection (same format) */
+  const void* scales2;
+  const void* biases2;
+  int group_size;          /* affine formats */
+  const void* norm_weight; /* non-NULL: x is RMS-normalised first (fp32 stats) */
+  float norm_eps;
+  int epilogue;
+  void* y; /* STORE/RESID/SWIGLU output [M, ldy] */
+  int64_t ldy;
+  const void* residual; /* RESID (may alias y) */
+  int64_t ldr;
+  /* ROPE */
+  const int32_t* positions; /* [M] device */
+  int num_heads, num_kv_heads, head_dim, seq_len;
+  float rope_base;
+  void* q_out;
+  void* k_out;
+  void* v_out;
+  /* ARGMAX: [M] keys, zero before the launch */
+  unsigned long long* argmax_keys;
+  void* workspace;
+  size_t workspace_bytes;
+} sb_linear_ex_desc;
+
+/* Fused weight-streaming linear (1 <= M <= 8). */
+int sb_linear_ex(const sb_linear_ex_desc* desc, void* stream);
+size_t sb_linear_ex_workspace_size(const sb_linear_ex_desc* desc);
+
+/*
+ * Quantize new K/V rows ([B, KH, L, D] bf16) into the INT8 cache at positions
+ * start[b] + l: symmetric per token per head, fp16 scale = absmax / 127
+ * (1 for a zero row), code = clamp(rint(x / scale), -127, 127). Replaces the
+ * cache update of Attention.__call__ (spark_mlx_llm/model.py:192-193).
+ */
+int sb_kv_append_int8(const void* k_new, const void* v_new, int8_t* k_cache, void* k_scale, int8_t* v_cache,
+                      void* v_scale, int64_t batch, int num_kv_heads, int64_t seq_len, int head_dim,
+                      int64_t capacity, const int32_t* start, void* stream);
+
+/* INT8-KV decode attention with per-batch lengths lengths[b] + length_offset read on
+ * the device; max_length bounds them (it sizes the split-K workspace). */
+int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                            const void* v_scale, void* out, int64_t batch, int num_heads, int num_kv_heads,
+                            const int32_t* lengths, int length_offset, int64_t max_length, int64_t capacity,
+                            int head_dim, float scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[r, :] = table[ids[r], :] (bf16 embedding rows). Replaces nn.Embedding
+ * (spark_mlx_llm/model.py:296-305). */
+int sb_embed_rows(const void* table, const int32_t* ids, void* out, int64_t rows, int64_t hidden, int64_t vocab,
+                  void* stream);
+
+/* Greedy step bookkeeping: tokens[b] = index encoded in argmax_keys[b],
+ * argmax_keys[b] = 0, positions[b] += advance. */
+int sb_decode_advance(unsigned long long* argmax_keys, int32_t* tokens, int32_t* positions, int batch, int advance,
+                      void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARK_B200_DECODER_H */

@@ -1,0 +1,761 @@
+// Weight-streaming linear kernels (M <= 8) and their C-ABI entry points.
+// The design notes are in sb_gemv.cuh.
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "sb_gemv.cuh"
+
+namespace sb {
+
+template <typename TA>
+struct ActTraits;
+template <>
+struct ActTraits<__nv_bfloat16> {
+  static constexpr bool kHalf = false;
+  static constexpr uint32_t kMagic = 0x43004300u;  // bf16 128.0 | code
+  static constexpr uint32_t kOnes = 0x3F803F80u;   // bf16 pair (1.0, 1.0)
+  static constexpr float kOffset = 128.0f;
+};
+template <>
+struct ActTraits<__half> {
+  static constexpr bool kHalf = true;
+  static constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 | code
+  static constexpr uint32_t kOnes = 0x3C003C00u;   // fp16 pair (1.0, 1.0)
+  static constexpr float kOffset = 1024.0f;
+};
+
+template <typename TA, int WF>
+struct Fmt {
+  static constexpr bool kHalf = ActTraits<TA>::kHalf;
+  // Two exact nibble planes are needed for 8-bit codes with bf16 operands.
+  static constexpr int kPlanes = ((WF == W_AFF8 || WF == W_I8PC) && !kHalf) ? 2 : 1;
+  static constexpr int kBits = WF == W_AFF4 ? 4 : (WF == W_BF16 ? 16 : 8);
+  // sum(code * x) = C_lo + 16 * C_hi - kCodeOffset * sum(x)
+  static constexpr float kCodeOffset =
+      WF == W_BF16 ? 0.0f
+                   : (kPlanes == 2 ? ActTraits<TA>::kOffset * 17.0f : ActTraits<TA>::kOffset);
+};
+
+// Loads `kWords` consecutive uint32 words (streaming, 4..32 bytes).
+template <int kWords>
+__device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&out)[kWords]) {
+  if constexpr (kWords == 1) {
+    out[0] = ldg_stream4(p);
+  } else if constexpr (kWords == 2) {
+    uint2 v = ldg_stream8(p);
+    out[0] = v.x;
+    out[1] = v.y;
+  } else {
+#pragma unroll
+    for (int i = 0; i < kWords; i += 4) {
+      uint4 v = ldg_stream16(p + 4 * i);
+      out[i] = v.x;
+      out[i + 1] = v.y;
+      out[i + 2] = v.z;
+      out[i + 3] = v.w;
+    }
+  }
+}
+
+// Converts one row segment of packed codes into MMA A-operand pairs.
+// Pair order (shared with the x pairs below):
+//   4-bit : pair 4w+j holds values (8w+j, 8w+j+4) of the segment
+//   8-bit : pair 2w+i holds values (4w+2i, 4w+2i+1)
+//   bf16  : pair i holds values (2i, 2i+1)
+template <typename TA, int WF, int kWords, int kPairs>
+__device__ __forceinline__ void dequant_pairs(const uint32_t (&w)[kWords],
+                                              uint32_t (&lo)[kPairs], uint32_t (&hi)[kPairs]) {
+  constexpr uint32_t kMagic = ActTraits<TA>::kMagic;
+  if constexpr (WF == W_AFF4) {
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) {
+      lo[4 * i + 0] = lop_and_or(w[i], 0x000F000Fu, kMagic);
+      lo[4 * i + 1] = lop_and_or(w[i] >> 4, 0x000F000Fu, kMagic);
+      lo[4 * i + 2] = lop_and_or(w[i] >> 8, 0x000F000Fu, kMagic);
+      lo[4 * i + 3] = lop_and_or(w[i] >> 12, 0x000F000Fu, kMagic);
+    }
+  } else if constexpr (WF == W_AFF8 || WF == W_I8PC) {
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) {
+      const uint32_t u = (WF == W_I8PC) ? (w[i] ^ 0x80808080u) : w[i];
+      if constexpr (ActTraits<TA>::kHalf) {
+        lo[2 * i + 0] = prmt(u, 0x64646464u, 0x4140u);
+        lo[2 * i + 1] = prmt(u, 0x64646464u, 0x4342u);
+      } else {
+        const uint32_t t0 = prmt(u, 0u, 0x4140u);
+        const uint32_t t1 = prmt(u, 0u, 0x4342u);
+        lo[2 * i + 0] = lop_and_or(t0, 0x000F000Fu, kMagic);
+        lo[2 * i + 1] = lop_and_or(t1, 0x000F000Fu, kMagic);
+        hi[2 * i + 0] = lop_and_or(t0 >> 4, 0x000F000Fu, kMagic);
+        hi[2 * i + 1] = lop_and_or(t1 >> 4, 0x000F000Fu, kMagic);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kWords; ++i) lo[i] = w[i];
+  }
+}
+
+// x values (bf16/fp16 pairs as stored) -> B-operand pairs in the same order.
+template <int WF, int kXWords, int kPairs>
+__device__ __forceinline__ void x_pairs(const uint32_t (&xw)[kXWords], uint32_t (&xp)[kPairs]) {
+  if constexpr (WF == W_AFF4) {
+#pragma unroll
+    for (int w = 0; w < kXWords / 4; ++w) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xp[4 * w + j] = prmt(xw[4 * w + j / 2], xw[4 * w + 2 + j / 2], (j & 1) ? 0x7632u : 0x5410u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < kPairs; ++i) xp[i] = xw[i];
+  }
+}
+
+__device__ __forceinline__ unsigned long long argmax_key(float v, int index) {
+  uint32_t u = __float_as_uint(v);
+  if (v != v) u = 0x007FFFFFu;  // NaN ranks below every number
+  else u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(index));
+}
+
+template <typename TA>
+__device__ __forceinline__ void store_act(void* base, size_t index, float v) {
+  static_cast<TA*>(base)[index] = from_float<TA>(v);
+}
+template <typename TA>
+__device__ __forceinline__ float load_act(const void* base, size_t index) {
+  return to_float(static_cast<const TA*>(base)[index]);
+}
+template <typename TA>
+__device__ __forceinline__ float round_act(float v) {
+  return to_float(from_float<TA>(v));
+}
+
+// Physical weight row (and weight set) of row r16 (0..15) of m16 tile `tile`.
+template <int EPI>
+__device__ __forceinline__ int map_row(const GemvParams& p, int tile, int r16, int& set,
+                                       bool& valid) {
+  set = 0;
+  valid = true;
+  if constexpr (EPI == EPI_SWIGLU) {
+    set = r16 >> 3;
+    const int n = tile * 8 + (r16 & 7);
+    valid = n < p.N;
+    return min(n, p.N - 1);
+  } else if constexpr (EPI == EPI_ROPE) {
+    const int tph = p.head_dim / 16;  // tiles per head
+    const int h = tile / tph, j = tile % tph;
+    const int row = h * p.head_dim + (r16 < 8 ? 8 * j + r16 : p.head_dim / 2 + 8 * j + r16 - 8);
+    valid = row < p.N;
+    return min(row, p.N - 1);
+  } else {
+    const int row = tile * 16 + r16;
+    valid = row < p.N;
+    return min(row, p.N - 1);
+  }
+}
+
+template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
+__global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_kernel(const __grid_constant__ GemvParams p) {
+  using F = Fmt<TA, WF>;
+  constexpr int V = KC / 4;                      // values per lane per row per chunk
+  constexpr int kPairs = V / 2;                  // MMA operand pairs per row per chunk
+  constexpr int kMma = KC / 16;                  // k16 steps per chunk
+  constexpr int kWords = V * F::kBits / 32;      // weight words per lane per row per chunk
+  constexpr int kXWords = V / 2;                 // activation words per lane per chunk
+  constexpr int kRows = 2 * kGemvTiles;          // weight rows held per lane
+  constexpr bool kAffine = (WF == W_AFF4 || WF == W_AFF8);
+  constexpr int kGroupK = kAffine ? KC * GC : KC;  // K covered by one split unit
+
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  __shared__ float s_rms[8];
+  __shared__ float s_part[kGemvWarps][8];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2;
+  const int t = lane & 3;
+  const int split = blockIdx.y;
+  const int tiles = (EPI == EPI_SWIGLU) ? (p.N + 7) / 8
+                    : (EPI == EPI_ROPE)  ? p.N / 16
+                                         : (p.N + 15) / 16;
+  const int rowblocks = (tiles + kGemvTiles - 1) / kGemvTiles;
+  const int rb = blockIdx.x * kGemvWarps + warp;
+  const bool active = rb < rowblocks;
+
+  // K range of this split, in whole groups.
+  const int grp_begin = static_cast<int>((static_cast<long long>(p.groups_total) * split) / p.splits);
+  const int grp_end = static_cast<int>((static_cast<long long>(p.groups_total) * (split + 1)) / p.splits);
+  const int k_begin = grp_begin * kGroupK;
+  const int k_count = (grp_end - grp_begin) * kGroupK;
+  const int chunk_begin = k_begin / KC;
+  const int chunk_end = chunk_begin + k_count / KC;
+
+  // ---- per-lane row pointers (weights for all 4 rows; scale/bias for row t)
+  const uint8_t* wrow[kRows];
+  int my_set = 0, my_row = 0;
+#pragma unroll
+  for (int q = 0; q < kRows; ++q) {
+    const int tile = min(rb, rowblocks - 1) * kGemvTiles + (q >> 1);
+    int set;
+    bool valid;
+    const int row = map_row<EPI>(p, min(tile, tiles - 1), (q & 1) * 8 + g, set, valid);
+    const uint8_t* base = static_cast<const uint8_t*>(set ? p.w1 : p.w0);
+    const size_t row_bytes = static_cast<size_t>(p.K) * F::kBits / 8;
+    wrow[q] = base + row * row_bytes + static_cast<size_t>(t) * V * F::kBits / 8;
+    if (q == t) {
+      my_set = set;
+      my_row = row;
+    }
+  }
+
+  // ---- prefetch the first chunk of weights (independent of earlier kernels)
+  uint32_t wbuf[kRows][kWords];
+  if (active && chunk_begin < chunk_end) {
+#pragma unroll
+    for (int q = 0; q < kRows; ++q)
+      load_words<kWords>(wrow[q] + static_cast<size_t>(chunk_begin) * KC * F::kBits / 8, wbuf[q]);
+  }
+
+  // ---- activations depend on the previous kernel from here on
+  grid_dependency_wait();
+
+  TA* xs = reinterpret_cast<TA*>(smem_raw);
+  const int xs_ld = k_count + 8;
+  const int mcols = p.M;
+  if constexpr (NORM) {
+    // full-row sum of squares per column (fixed reduction order)
+    for (int m = 0; m < mcols; ++m) {
+      float ss = 0.f;
+      const TA* xr = static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx;
+      for (int k = threadIdx.x * 8; k < p.K; k += kGemvWarps * 32 * 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
+        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float a, b;
+          if constexpr (ActTraits<TA>::kHalf) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vv[i]));
+            a = f.x;
+            b = f.y;
+          } else {
+            a = bf16_lo(vv[i]);
+            b = bf16_hi(vv[i]);
+          }
+          ss = fmaf(a, a, ss);
+          ss = fmaf(b, b, ss);
+        }
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) s_part[warp][m] = ss;
+    }
+    __syncthreads();
+    if (threadIdx.x < mcols) {
+      float ss = 0.f;
+#pragma unroll
+      for (int w = 0; w < kGemvWarps; ++w) ss += s_part[w][threadIdx.x];
+      s_rms[threadIdx.x] = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
+    }
+    __syncthreads();
+  }
+  // stage x[:, k_begin : k_begin + k_count] (optionally normalized) into smem
+  {
+    const int vecs = k_count / 8;
+    for (int idx = threadIdx.x; idx < mcols * vecs; idx += kGemvWarps * 32) {
+      const int m = idx / vecs, v8 = idx % vecs;
+      const TA* src = static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + k_begin + v8 * 8;
+      uint4 v = *reinterpret_cast<const uint4*>(src);
+      if constexpr (NORM) {
+        const uint4 wv = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + k_begin + v8 * 8);
+        const TA* xv = reinterpret_cast<const TA*>(&v);
+        const TA* nv = reinterpret_cast<const TA*>(&wv);
+        TA out[8];
+        const float r = s_rms[m];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) out[i] = from_float<TA>(to_float(xv[i]) * r * to_float(nv[i]));
+        v = *reinterpret_cast<const uint4*>(out);
+      }
+      *reinterpret_cast<uint4*>(xs + m * xs_ld + v8 * 8) = v;
+    }
+  }
+  __syncthreads();
+  if (!active) return;
+
+  // ---- main loop
+  const TA* xcol = xs + min(g, mcols - 1) * xs_ld + t * V;
+  constexpr uint32_t kOnes = ActTraits<TA>::kOnes;
+  float acc[kGemvTiles][4];
+  float cacc[kGemvTiles][F::kPlanes][4];
+  float xsum[4];
+#pragma unroll
+  for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[r][e] = 0.f;
+#pragma unroll
+      for (int pl = 0; pl < F::kPlanes; ++pl) cacc[r][pl][e] = 0.f;
+    }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
+
+  const __nv_bfloat16* srow = nullptr;
+  const __nv_bfloat16* brow = nullptr;
+  if constexpr (kAffine) {
+    const int gpr = p.K / p.group_size;
+    srow = static_cast<const __nv_bfloat16*>(my_set ? p.s1 : p.s0) + static_cast<size_t>(my_row) * gpr;
+    brow = static_cast<const __nv_bfloat16*>(my_set ? p.b1 : p.b0) + static_cast<size_t>(my_row) * gpr;
+  }
+
+  for (int c = chunk_begin; c < chunk_end; ++c) {
+    // dequantize the current chunk, then issue the next chunk's loads
+    uint32_t lo[kRows][kPairs], hi[kRows][kPairs];
+#pragma unroll
+    for (int q = 0; q < kRows; ++q) dequant_pairs<TA, WF, kWords, kPairs>(wbuf[q], lo[q], hi[q]);
+    if (c + 1 < chunk_end) {
+#pragma unroll
+      for (int q = 0; q < kRows; ++q)
+        load_words<kWords>(wrow[q] + static_cast<size_t>(c + 1) * KC * F::kBits / 8, wbuf[q]);
+    }
+    uint32_t xw[kXWords];
+    const TA* xp_base = xcol + (c - chunk_begin) * KC;
+#pragma unroll
+    for (int i = 0; i < kXWords; i += 4) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xp_base + 2 * i);
+      xw[i] = v.x;
+      xw[i + 1] = v.y;
+      xw[i + 2] = v.z;
+      xw[i + 3] = v.w;
+    }
+    uint32_t xpair[kPairs];
+    x_pairs<WF, kXWords, kPairs>(xw, xpair);
+
+#pragma unroll
+    for (int j = 0; j < kMma; ++j) {
+      const uint32_t b0 = xpair[2 * j], b1 = xpair[2 * j + 1];
+#pragma unroll
+      for (int r = 0; r < kGemvTiles; ++r) {
+        const uint32_t a_lo[4] = {lo[2 * r][2 * j], lo[2 * r + 1][2 * j], lo[2 * r][2 * j + 1],
+                                  lo[2 * r + 1][2 * j + 1]};
+        mma_16816<F::kHalf>(cacc[r][0], a_lo, b0, b1);
+        if constexpr (F::kPlanes == 2) {
+          const uint32_t a_hi[4] = {hi[2 * r][2 * j], hi[2 * r + 1][2 * j], hi[2 * r][2 * j + 1],
+                                    hi[2 * r + 1][2 * j + 1]};
+          mma_16816<F::kHalf>(cacc[r][1], a_hi, b0, b1);
+        }
+      }
+      if constexpr (WF != W_BF16) {
+        const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+        mma_16816<F::kHalf>(xsum, ones, b0, b1);
+      }
+    }
+
+    if constexpr (kAffine) {
+      if ((c + 1) % GC == 0) {
+        // group epilogue: acc += scale * sum(code*x) + bias * sum(x)
+        const int grp = c / GC;
+        const uint32_t sb = static_cast<uint32_t>(__bfloat16_as_ushort(srow[grp])) |
+                            (static_cast<uint32_t>(__bfloat16_as_ushort(brow[grp])) << 16);
+#pragma unroll
+        for (int r = 0; r < kGemvTiles; ++r) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t v = __shfl_sync(0xffffffffu, sb, (lane & ~3) | (2 * r + h));
+            const float s = bf16_lo(v);
+            const float b = bf16_hi(v);
+            const float bb = fmaf(-F::kCodeOffset, s, b);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              float d = cacc[r][0][2 * h + e];
+              if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][2 * h + e], d);
+              acc[r][2 * h + e] = fmaf(s, d, fmaf(bb, xsum[e], acc[r][2 * h + e]));
+              cacc[r][0][2 * h + e] = 0.f;
+              if constexpr (F::kPlanes == 2) cacc[r][1][2 * h + e] = 0.f;
+            }
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
+      }
+    }
+  }
+
+  if constexpr (WF == W_I8PC) {
+    // signed value = unsigned code - 128:  sum(s8*x) = C - (offset + 128) * sum(x)
+#pragma unroll
+    for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float d = cacc[r][0][e];
+        if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][e], d);
+        acc[r][e] = fmaf(-(F::kCodeOffset + 128.0f), xsum[e & 1], d);
+      }
+  } else if constexpr (WF == W_BF16) {
+#pragma unroll
+    for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[r][e] = cacc[r][0][e];
+  }
+
+  grid_dependency_launch();
+
+  // ---- split-K: publish partials; the last warp of the row block reduces
+  if (p.splits > 1) {
+    float* part = p.partial + (static_cast<size_t>(split) * p.rows_padded + rb * 16 * kGemvTiles) * 8;
+#pragma unroll
+    for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        if (2 * t < mcols) {
+          float2 v = make_float2(acc[r][2 * h], acc[r][2 * h + 1]);
+          *reinterpret_cast<float2*>(part + (r * 16 + h * 8 + g) * 8 + 2 * t) = v;
+        }
+      }
+    __threadfence();
+    __syncwarp();
+    unsigned prev = 0;
+    if (lane == 0) prev = atomicAdd(p.counters + rb, 1u);
+    prev = __shfl_sync(0xffffffffu, prev, 0);
+    if (prev != static_cast<unsigned>(p.splits - 1)) return;
+    __threadfence();
+#pragma unroll
+    for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float* ps = p.partial + (static_cast<size_t>(s) * p.rows_padded + rb * 16 * kGemvTiles) * 8;
+#pragma unroll
+      for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          if (2 * t < mcols) {
+            const float2 v = __ldcg(reinterpret_cast<const float2*>(ps + (r * 16 + h * 8 + g) * 8 + 2 * t));
+            acc[r][2 * h] += v.x;
+            acc[r][2 * h + 1] += v.y;
+          }
+        }
+    }
+    if (lane == 0) p.counters[rb] = 0u;
+  }
+
+  // ---- final epilogue
+  if constexpr (EPI == EPI_ARGMAX) {
+    float best[2] = {-INFINITY, -INFINITY};
+    int best_i[2] = {0x7FFFFFFF, 0x7FFFFFFF};
+#pragma unroll
+    for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        int set;
+        bool valid;
+        const int row = map_row<EPI>(p, rb * kGemvTiles + r, h * 8 + g, set, valid);
+        if (!valid || rb * kGemvTiles + r >= tiles) continue;
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float v = acc[r][2 * h + e];
+          if (v > best[e] || (v == best[e] && row < best_i[e])) {
+            best[e] = v;
+            best_i[e] = row;
+          }
+        }
+      }
+#pragma unroll
+    for (int o = 4; o < 32; o <<= 1) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best[e], o);
+        const int oi = __shfl_xor_sync(0xffffffffu, best_i[e], o);
+        if (ov > best[e] || (ov == best[e] && oi < best_i[e])) {
+          best[e] = ov;
+          best_i[e] = oi;
+        }
+      }
+    }
+    if (g == 0) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int m = 2 * t + e;
+        if (m < mcols && best_i[e] != 0x7FFFFFFF) atomicMax(p.argmax_keys + m, argmax_key(best[e], best_i[e]));
+      }
+    }
+    return;
+  } else {
+    float scale_pc[kRows];
+    if constexpr (WF == W_I8PC) {
+#pragma unroll
+      for (int q = 0; q < kRows; ++q) {
+        int set;
+        bool valid;
+        const int row = map_row<EPI>(p, min(rb * kGemvTiles + (q >> 1), tiles - 1), (q & 1) * 8 + g, set, valid);
+        scale_pc[q] = static_cast<const float*>(set ? p.s1 : p.s0)[row];
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < kGemvTiles; ++r) {
+      const int tile = rb * kGemvTiles + r;
+      if (tile >= tiles) continue;
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int m = 2 * t + e;
+        if (m >= mcols) continue;
+        float v_lo = acc[r][e], v_hi = acc[r][2 + e];
+        if constexpr (WF == W_I8PC) {
+          v_lo *= scale_pc[2 * r];
+          v_hi *= scale_pc[2 * r + 1];
+        }
+        if constexpr (EPI == EPI_SWIGLU) {
+          const int n = tile * 8 + g;
+          if (n < p.N) {
+            const float gt = round_act<TA>(v_lo), up = round_act<TA>(v_hi);
+            const float silu = gt / (1.0f + expf(-gt));
+            store_act<TA>(p.y, static_cast<size_t>(m) * p.ldy + n, silu * up);
+          }
+        } else if constexpr (EPI == EPI_ROPE) {
+          const int tph = p.head_dim / 16;
+          const int head = tile / tph, j = tile % tph;
+          const int i = 8 * j + g;            // rotation pair index
+          const int half = p.head_dim / 2;
+          float a = round_act<TA>(v_lo), b = round_act<TA>(v_hi);
+          void* out;
+          int hh, nh;
+          if (head < p.heads_q) {
+            out = p.q_out;
+            hh = head;
+            nh = p.heads_q;
+          } else if (head < p.heads_q + p.heads_kv) {
+            out = p.k_out;
+            hh = head - p.heads_q;
+            nh = p.heads_kv;
+          } else {
+            out = p.v_out;
+            hh = head - p.heads_q - p.heads_kv;
+            nh = p.heads_kv;
+          }
+          if (head < p.heads_q + p.heads_kv) {
+            const float angle = static_cast<float>(p.positions[m]) * p.inv_freq[i];
+            float sn, cs;
+            sincosf(angle, &sn, &cs);
+            const float ra = a * cs - b * sn;
+            const float rb2 = b * cs + a * sn;
+            a = ra;
+            b = rb2;
+          }
+          const int bi = m / p.seq_len, l = m % p.seq_len;
+          const size_t base = ((static_cast<size_t>(bi) * nh + hh) * p.seq_len + l) * p.head_dim;
+          store_act<TA>(out, base + i, a);
+          store_act<TA>(out, base + half + i, b);
+        } else {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int row = tile * 16 + h * 8 + g;
+            if (row >= p.N) continue;
+            const float v = h ? v_hi : v_lo;
+            const size_t idx = static_cast<size_t>(m) * p.ldy + row;
+            if constexpr (EPI == EPI_RESID) {
+              const float res = load_act<TA>(p.residual, static_cast<size_t>(m) * p.ldr + row);
+              store_act<TA>(p.y, idx, res + round_act<TA>(v));
+            } else {
+              store_act<TA>(p.y, idx, v);
+            }
+          }
+        }
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+namespace {
+
+int sm_count() {
+  static int count = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
+      count = 148;
+  });
+  return count;
+}
+
+struct Plan {
+  int tiles, rowblocks, groups, splits, k_group;
+  size_t counter_bytes, partial_bytes;
+};
+
+Plan make_plan(int epi, int N, int K, int group_k, bool allow_split) {
+  Plan pl{};
+  pl.tiles = epi == EPI_SWIGLU ? (N + 7) / 8 : (epi == EPI_ROPE ? N / 16 : (N + 15) / 16);
+  pl.rowblocks = (pl.tiles + kGemvTiles - 1) / kGemvTiles;
+  pl.k_group = group_k;
+  pl.groups = K / group_k;
+  // Enough warps to cover the SMs ~12 warps deep; keep >= 2 groups per split
+  // and at most 4096 staged activation values per split.
+  const int target = sm_count() * 12;
+  int s = allow_split ? (target + pl.rowblocks - 1) / pl.rowblocks : 1;
+  s = std::min(s, std::max(1, pl.groups / 2));
+  const int min_s = (K + 4095) / 4096;
+  s = std::max(s, min_s);
+  s = std::min(s, pl.groups);
+  pl.splits = std::max(1, s);
+  pl.counter_bytes = ((static_cast<size_t>(pl.rowblocks) * 4 + 255) / 256) * 256;
+  pl.partial_bytes = pl.splits > 1
+                         ? static_cast<size_t>(pl.splits) * pl.rowblocks * 16 * kGemvTiles * 8 * sizeof(float)
+                         : 0;
+  return pl;
+}
+
+template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
+int launch_gemv(GemvParams& p, const Plan& pl, cudaStream_t stream) {
+  const int max_kunit = (pl.groups + pl.splits - 1) / pl.splits * pl.k_group;
+  const size_t smem = static_cast<size_t>(p.M) * (max_kunit + 8) * sizeof(TA);
+  auto kernel = gemv_kernel<TA, WF, KC, GC, EPI, NORM>;
+  if (smem > 48 * 1024) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+        cudaSuccess)
+      return fail(SB_ECUDA, "gemv: shared memory opt-in failed");
+  }
+  dim3 grid((pl.rowblocks + kGemvWarps - 1) / kGemvWarps, pl.splits);
+  return launch("gemv", kernel, grid, dim3(kGemvWarps * 32), smem, stream, p);
+}
+
+template <typename TA, int WF, int EPI, bool NORM>
+int dispatch_group(GemvParams& p, const Plan& pl, cudaStream_t stream) {
+  if constexpr (WF == W_AFF4 || WF == W_AFF8) {
+    switch (p.group_size) {
+      case 32:
+        return launch_gemv<TA, WF, 32, 1, EPI, NORM>(p, pl, stream);
+      case 64:
+        return launch_gemv<TA, WF, 64, 1, EPI, NORM>(p, pl, stream);
+      case 128:
+        return launch_gemv<TA, WF, 64, 2, EPI, NORM>(p, pl, stream);
+      default:
+        return fail(SB_EUNSUPPORTED, "group_size must be 32, 64 or 128");
+    }
+  } else {
+    return launch_gemv<TA, WF, 64, 1, EPI, NORM>(p, pl, stream);
+  }
+}
+
+template <int EPI, bool NORM>
+int dispatch_fmt(int wf, int x_dtype, GemvParams& p, const Plan& pl, cudaStream_t stream) {
+  if (x_dtype == SB_DTYPE_BF16) {
+    switch (wf) {
+      case W_AFF4: return dispatch_group<__nv_bfloat16, W_AFF4, EPI, NORM>(p, pl, stream);
+      case W_AFF8: return dispatch_group<__nv_bfloat16, W_AFF8, EPI, NORM>(p, pl, stream);
+      case W_I8PC: return dispatch_group<__nv_bfloat16, W_I8PC, EPI, NORM>(p, pl, stream);
+      case W_BF16: return dispatch_group<__nv_bfloat16, W_BF16, EPI, NORM>(p, pl, stream);
+    }
+  } else if (x_dtype == SB_DTYPE_F16) {
+    if constexpr (EPI == EPI_STORE || EPI == EPI_ROPE) {
+      switch (wf) {
+        case W_AFF4: return dispatch_group<__half, W_AFF4, EPI, NORM>(p, pl, stream);
+        case W_AFF8: return dispatch_group<__half, W_AFF8, EPI, NORM>(p, pl, stream);
+        case W_I8PC: return dispatch_group<__half, W_I8PC, EPI, NORM>(p, pl, stream);
+        default: break;
+      }
+    }
+  }
+  return fail(SB_EUNSUPPORTED, "unsupported activation dtype / weight format combination");
+}
+
+}  // namespace
+
+static int group_k_of(const LinearRequest& r) {
+  if (r.wf == W_AFF4 || r.wf == W_AFF8) return r.group_size;
+  return 64;
+}
+
+size_t linear_workspace_size(int epi, int N, int K, int group_k) {
+  if (group_k <= 0 || K % group_k) return 0;
+  const Plan pl = make_plan(epi, N, K, group_k, true);
+  return pl.counter_bytes + pl.partial_bytes;
+}
+
+int run_linear(const LinearRequest& r, cudaStream_t stream) {
+  SB_REQUIRE(r.M >= 1 && r.M <= 8, "weight-streaming linear supports 1..8 activation rows per call");
+  SB_REQUIRE(r.N > 0 && r.K > 0, "N and K must be positive");
+  const int gk = group_k_of(r);
+  SB_REQUIRE(r.K % gk == 0, "K must be a multiple of the group size (64 for per-channel/bf16 weights)");
+  SB_REQUIRE(r.ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(r.x) & 15) == 0,
+             "activations must be 16-byte aligned with a row stride that is a multiple of 8");
+  SB_REQUIRE((reinterpret_cast<uintptr_t>(r.w0) & 15) == 0, "weights must be 16-byte aligned");
+  if (r.epi == EPI_ROPE) {
+    SB_REQUIRE(r.head_dim % 16 == 0 && r.head_dim / 2 <= kMaxRopeHalf, "head_dim must be a multiple of 16, <= 256");
+    SB_REQUIRE(r.rope_dims == r.head_dim, "the fused RoPE epilogue rotates the full head_dim");
+    SB_REQUIRE(r.N == (r.heads_q + 2 * r.heads_kv) * r.head_dim, "QKV rows must equal (Hq + 2*Hkv) * head_dim");
+  }
+  if (r.epi == EPI_SWIGLU) SB_REQUIRE(r.N % 8 == 0, "SwiGLU width must be a multiple of 8");
+
+  Plan pl = make_plan(r.epi, r.N, r.K, gk, true);
+  const size_t need = pl.counter_bytes + pl.partial_bytes;
+  if (pl.splits > 1 && (r.workspace == nullptr || r.workspace_bytes < need)) {
+    // Fall back to no split when the caller gave no workspace.
+    pl = make_plan(r.epi, r.N, r.K, gk, false);
+    SB_REQUIRE(pl.splits == 1, "workspace too small for this shape (query sb_*_workspace_size)");
+  }
+
+  GemvParams p{};
+  p.x = r.x;
+  p.ldx = r.ldx;
+  p.M = r.M;
+  p.N = r.N;
+  p.K = r.K;
+  p.w0 = r.w0;
+  p.s0 = r.s0;
+  p.b0 = r.b0;
+  p.w1 = r.w1 ? r.w1 : r.w0;
+  p.s1 = r.s1 ? r.s1 : r.s0;
+  p.b1 = r.b1 ? r.b1 : r.b0;
+  p.group_size = r.group_size;
+  p.splits = pl.splits;
+  p.groups_total = pl.groups;
+  p.rows_padded = pl.rowblocks * 16 * kGemvTiles;
+  if (pl.splits > 1) {
+    p.counters = static_cast<unsigned*>(r.workspace);
+    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(r.workspace) + pl.counter_bytes);
+  }
+  p.norm_w = r.norm_w;
+  p.eps = r.eps;
+  p.y = r.y;
+  p.ldy = r.ldy;
+  p.residual = r.residual;
+  p.ldr = r.ldr;
+  p.positions = r.positions;
+  p.heads_q = r.heads_q;
+  p.heads_kv = r.heads_kv;
+  p.head_dim = r.head_dim;
+  p.seq_len = r.seq_len > 0 ? r.seq_len : 1;
+  p.q_out = r.q_out;
+  p.k_out = r.k_out;
+  p.v_out = r.v_out;
+  p.argmax_keys = r.argmax_keys;
+  if (r.epi == EPI_ROPE) {
+    for (int i = 0; i < r.rope_dims / 2; ++i)
+      p.inv_freq[i] = static_cast<float>(std::pow(static_cast<double>(r.rope_base), -2.0 * i / r.rope_dims));
+  }
+
+  switch (r.epi) {
+    case EPI_STORE:
+      return r.norm ? dispatch_fmt<EPI_STORE, true>(r.wf, r.x_dtype, p, pl, stream)
+                    : dispatch_fmt<EPI_STORE, false>(r.wf, r.x_dtype, p, pl, stream);
+    case EPI_RESID:
+      return dispatch_fmt<EPI_RESID, false>(r.wf, r.x_dtype, p, pl, stream);
+    case EPI_SWIGLU:
+      return r.norm ? dispatch_fmt<EPI_SWIGLU, true>(r.wf, r.x_dtype, p, pl, stream)
+                    : dispatch_fmt<EPI_SWIGLU, false>(r.wf, r.x_dtype, p, pl, stream);
+    case EPI_ROPE:
+      return r.norm ? dispatch_fmt<EPI_ROPE, true>(r.wf, r.x_dtype, p, pl, stream)
+                    : dispatch_fmt<EPI_ROPE, false>(r.wf, r.x_dtype, p, pl, stream);
+    case EPI_ARGMAX:
+      return r.norm ? dispatch_fmt<EPI_ARGMAX, true>(r.wf, r.x_dtype, p, pl, stream)
+                    : dispatch_fmt<EPI_ARGMAX, false>(r.wf, r.x_dtype, p, pl, stream);
+  }
+  return fail(SB_EINVAL, "unknown epilogue");
+}
+
+}  // namespace sb

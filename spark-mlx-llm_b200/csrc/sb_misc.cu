@@ -1,0 +1,369 @@
+// Small kernels of the decode step and the C-ABI wrappers of the linear family.
+#include <cmath>
+#include <cstring>
+#include <string>
+
+#include "sb_common.cuh"
+#include "sb_gemv.cuh"
+#include "spark_b200_decoder.h"
+
+namespace sb {
+
+// ------------------------------------------------------------ error state
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_error(const std::string& message) { g_last_error = message; }
+
+int fail(int status, const std::string& message) {
+  g_last_error = message;
+  return status;
+}
+
+size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int64_t length);
+
+// ------------------------------------------------------------------ RMSNorm
+template <typename T>
+__global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int dim,
+                                float eps) {
+  grid_dependency_wait();
+  const int row = blockIdx.x;
+  const T* xr = x + static_cast<size_t>(row) * dim;
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < dim; k += blockDim.x) {
+    const float v = to_float(xr[k]);
+    ss = fmaf(v, v, ss);
+  }
+  ss = warp_sum(ss);
+  __shared__ float part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x + 31) / 32 ? part[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) part[0] = 1.0f / sqrtf(v / static_cast<float>(dim) + eps);
+  }
+  __syncthreads();
+  const float r = part[0];
+  grid_dependency_launch();
+  for (int k = threadIdx.x; k < dim; k += blockDim.x)
+    y[static_cast<size_t>(row) * dim + k] = from_float<T>(to_float(xr[k]) * r * to_float(w[k]));
+}
+
+// ------------------------------------------- INT8 KV append (per token/head)
+// One warp per (batch, kv head, token): absmax over D, scale = fp16(absmax/127)
+// (fp16 1.0 for a zero row), code = clamp(rint(x / scale), -127, 127).
+__global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ k_new, const __nv_bfloat16* __restrict__ v_new,
+                                 int8_t* __restrict__ k_cache, __half* __restrict__ k_scale,
+                                 int8_t* __restrict__ v_cache, __half* __restrict__ v_scale, int kv_heads, int seq_len,
+                                 int head_dim, int capacity, const int* __restrict__ start) {
+  grid_dependency_wait();
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);  // (b, h, l)
+  const int l = item % seq_len;
+  const int bh = item / seq_len;
+  const int b = bh / kv_heads;
+  const int pos = start[b] + l;
+  if (pos >= capacity) return;
+#pragma unroll
+  for (int which = 0; which < 2; ++which) {
+    const __nv_bfloat16* src = (which ? v_new : k_new) + (static_cast<size_t>(bh) * seq_len + l) * head_dim;
+    int8_t* dst = (which ? v_cache : k_cache) + (static_cast<size_t>(bh) * capacity + pos) * head_dim;
+    __half* sdst = (which ? v_scale : k_scale) + static_cast<size_t>(bh) * capacity + pos;
+    float amax = 0.f;
+    for (int d = lane; d < head_dim; d += 32) amax = fmaxf(amax, fabsf(__bfloat162float(src[d])));
+    amax = warp_max(amax);
+    __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
+    if (__half2float(s16) == 0.f) s16 = __float2half_rn(1.0f);
+    const float s = __half2float(s16);
+    for (int d = lane; d < head_dim; d += 32) {
+      float r = rintf(__fdiv_rn(__bfloat162float(src[d]), s));
+      r = fminf(fmaxf(r, -127.0f), 127.0f);
+      dst[d] = static_cast<int8_t>(static_cast<int>(r));
+    }
+    if (lane == 0) *sdst = s16;
+  }
+}
+
+// -------------------------------------------------------- embedding gather
+__global__ void embed_kernel(const __nv_bfloat16* __restrict__ table, const int* __restrict__ ids,
+                             __nv_bfloat16* __restrict__ out, int hidden, int vocab) {
+  grid_dependency_wait();
+  const int row = blockIdx.x;
+  int id = ids[row];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+  const uint4* src = reinterpret_cast<const uint4*>(table + static_cast<size_t>(id) * hidden);
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * hidden);
+  for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// ------------------------------------------- greedy token + position advance
+// token[b] = argmax index decoded from keys[b]; keys reset; pos[b] += 1.
+__global__ void decode_advance_kernel(unsigned long long* keys, int* tokens, int* positions, int batch,
+                                      int advance) {
+  grid_dependency_wait();
+  const int b = threadIdx.x;
+  if (b < batch) {
+    const unsigned long long k = keys[b];
+    tokens[b] = static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull));
+    keys[b] = 0ull;
+    positions[b] += advance;
+  }
+}
+
+}  // namespace sb
+
+using namespace sb;
+
+// ------------------------------------------------------------------ C ABI
+extern "C" int sb_version(void) { return 100; }
+
+extern "C" const char* sb_last_error_message(void) { return g_last_error.c_str(); }
+
+extern "C" int sb_device_supported(int device) {
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return major == 10 ? 1 : 0;
+}
+
+namespace {
+
+int weight_format(int bits) {
+  if (bits == 4) return W_AFF4;
+  if (bits == 8) return W_AFF8;
+  return -1;
+}
+
+LinearRequest base_request(const void* x, int x_dtype, int64_t M, int64_t N, int64_t K) {
+  LinearRequest r{};
+  r.x = x;
+  r.x_dtype = x_dtype;
+  r.ldx = static_cast<int>(K);
+  r.M = static_cast<int>(M);
+  r.N = static_cast<int>(N);
+  r.K = static_cast<int>(K);
+  r.ldy = static_cast<int>(N);
+  r.epi = EPI_STORE;
+  return r;
+}
+
+int check_sizes(int64_t M, int64_t N, int64_t K) {
+  SB_REQUIRE(M > 0 && N > 0 && K > 0, "Expected nonempty x[M, K] and weight[N, K]");
+  SB_REQUIRE(N < (1LL << 31) && K < (1LL << 31) && M < (1LL << 31), "dimensions must fit in int32");
+  return SB_OK;
+}
+
+size_t act_size(int dtype) { return dtype == SB_DTYPE_F32 ? 4 : 2; }
+
+}  // namespace
+
+extern "C" size_t sb_affine_linear_workspace_size(int64_t M, int64_t N, int64_t K, int group_size, int bits) {
+  (void)M;
+  (void)bits;
+  if (N <= 0 || K <= 0 || group_size <= 0) return 0;
+  return linear_workspace_size(EPI_STORE, static_cast<int>(N), static_cast<int>(K), group_size);
+}
+
+extern "C" int sb_affine_linear(const void* x, int x_dtype, const uint32_t* w, const void* scales,
+                                const void* biases, void* y, int64_t M, int64_t N, int64_t K, int group_size,
+                                int bits, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int st = check_sizes(M, N, K)) return st;
+  SB_REQUIRE(x_dtype == SB_DTYPE_BF16 || x_dtype == SB_DTYPE_F16, "x must be bfloat16 or float16");
+  const int wf = weight_format(bits);
+  if (wf < 0) return fail(SB_EUNSUPPORTED, "affine bits must be 4 or 8");
+  SB_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128, "group_size must be 32, 64 or 128");
+  SB_REQUIRE(K % group_size == 0, "K must be a multiple of group_size");
+  for (int64_t m0 = 0; m0 < M; m0 += 8) {
+    LinearRequest r = base_request(static_cast<const uint8_t*>(x) + m0 * K * act_size(x_dtype), x_dtype,
+                                   std::min<int64_t>(8, M - m0), N, K);
+    r.wf = wf;
+    r.w0 = w;
+    r.s0 = scales;
+    r.b0 = biases;
+    r.group_size = group_size;
+    r.y = static_cast<uint8_t*>(y) + m0 * N * act_size(x_dtype);
+    r.workspace = workspace;
+    r.workspace_bytes = workspace_bytes;
+    if (int st = run_linear(r, as_stream(stream))) return st;
+  }
+  return SB_OK;
+}
+
+extern "C" size_t sb_w8a16_per_channel_workspace_size(int64_t M, int64_t N, int64_t K) {
+  (void)M;
+  if (N <= 0 || K <= 0) return 0;
+  return linear_workspace_size(EPI_STORE, static_cast<int>(N), static_cast<int>(K), 64);
+}
+
+extern "C" int sb_w8a16_per_channel(const void* x, int x_dtype, const int8_t* w, const float* scales, void* y,
+                                    int64_t M, int64_t N, int64_t K, void* workspace, size_t workspace_bytes,
+                                    void* stream) {
+  if (int st = check_sizes(M, N, K)) return st;
+  SB_REQUIRE(x_dtype == SB_DTYPE_BF16 || x_dtype == SB_DTYPE_F16,
+             "w8a16_per_channel x must have dtype bfloat16 or float16.");
+  if (K % 64) return fail(SB_EUNSUPPORTED, "this build requires K to be a multiple of 64");
+  for (int64_t m0 = 0; m0 < M; m0 += 8) {
+    LinearRequest r = base_request(static_cast<const uint8_t*>(x) + m0 * K * act_size(x_dtype), x_dtype,
+                                   std::min<int64_t>(8, M - m0), N, K);
+    r.wf = W_I8PC;
+    r.w0 = w;
+    r.s0 = scales;
+    r.y = static_cast<uint8_t*>(y) + m0 * N * act_size(x_dtype);
+    r.workspace = workspace;
+    r.workspace_bytes = workspace_bytes;
+    if (int st = run_linear(r, as_stream(stream))) return st;
+  }
+  return SB_OK;
+}
+
+extern "C" size_t sb_qkv_rope_workspace_size(int64_t batch, int64_t seq_len, int64_t hidden, int num_heads,
+                                             int num_kv_heads, int head_dim, int group_size, int bits) {
+  (void)batch;
+  (void)seq_len;
+  (void)bits;
+  const int64_t n = static_cast<int64_t>(num_heads + 2 * num_kv_heads) * head_dim;
+  if (n <= 0 || hidden <= 0 || group_size <= 0) return 0;
+  return linear_workspace_size(EPI_ROPE, static_cast<int>(n), static_cast<int>(hidden), group_size);
+}
+
+extern "C" int sb_qkv_rope(const void* x, int x_dtype, const uint32_t* w, const void* scales, const void* biases,
+                           const int32_t* positions, void* q_out, void* k_out, void* v_out, int64_t batch,
+                           int64_t seq_len, int64_t hidden, int num_heads, int num_kv_heads, int head_dim,
+                           int rope_dims, float rope_base, int group_size, int bits, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  SB_REQUIRE(batch > 0 && seq_len > 0 && hidden > 0, "x must have shape [B, L, hidden] with hidden > 0.");
+  SB_REQUIRE(batch * seq_len <= 8, "this build fuses QKV + RoPE for at most 8 tokens per call");
+  SB_REQUIRE(num_heads > 0 && num_kv_heads > 0 && head_dim > 0 && num_heads % num_kv_heads == 0,
+             "Invalid head counts, head_dim, q_size, or kv_size.");
+  SB_REQUIRE(rope_dims > 0 && rope_dims % 2 == 0 && rope_dims <= head_dim && std::isfinite(rope_base) &&
+                 rope_base > 0,
+             "rope_dims must be positive, even, and no larger than head_dim; rope_base must be positive and "
+             "finite.");
+  if (rope_dims != head_dim) return fail(SB_EUNSUPPORTED, "the fused kernel rotates the full head_dim");
+  SB_REQUIRE(x_dtype == SB_DTYPE_BF16 || x_dtype == SB_DTYPE_F16, "x must be bfloat16 or float16");
+  const int wf = weight_format(bits);
+  if (wf < 0) return fail(SB_EUNSUPPORTED, "bits must be 4 or 8 in this build");
+  SB_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128, "group_size must be 32, 64, or 128.");
+  SB_REQUIRE(hidden % group_size == 0, "Packed weight and quantization metadata shapes do not match x.");
+  LinearRequest r = base_request(x, x_dtype, batch * seq_len,
+                                 static_cast<int64_t>(num_heads + 2 * num_kv_heads) * head_dim, hidden);
+  r.wf = wf;
+  r.w0 = w;
+  r.s0 = scales;
+  r.b0 = biases;
+  r.group_size = group_size;
+  r.epi = EPI_ROPE;
+  r.positions = positions;
+  r.heads_q = num_heads;
+  r.heads_kv = num_kv_heads;
+  r.head_dim = head_dim;
+  r.seq_len = static_cast<int>(seq_len);
+  r.rope_dims = rope_dims;
+  r.rope_base = rope_base;
+  r.q_out = q_out;
+  r.k_out = k_out;
+  r.v_out = v_out;
+  r.workspace = workspace;
+  r.workspace_bytes = workspace_bytes;
+  return run_linear(r, as_stream(stream));
+}
+
+extern "C" int sb_rms_norm(const void* x, const void* weight, void* y, int x_dtype, int64_t rows, int64_t dim,
+                           float eps, void* stream) {
+  SB_REQUIRE(rows > 0 && dim > 0, "x must be nonempty");
+  const dim3 grid(static_cast<unsigned>(rows)), block(256);
+  switch (x_dtype) {
+    case SB_DTYPE_BF16:
+      return launch("rms_norm", rms_norm_kernel<__nv_bfloat16>, grid, block, 0, as_stream(stream),
+                    static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
+                    static_cast<__nv_bfloat16*>(y), static_cast<int>(dim), eps);
+    case SB_DTYPE_F16:
+      return launch("rms_norm", rms_norm_kernel<__half>, grid, block, 0, as_stream(stream),
+                    static_cast<const __half*>(x), static_cast<const __half*>(weight), static_cast<__half*>(y),
+                    static_cast<int>(dim), eps);
+    case SB_DTYPE_F32:
+      return launch("rms_norm", rms_norm_kernel<float>, grid, block, 0, as_stream(stream),
+                    static_cast<const float*>(x), static_cast<const float*>(weight), static_cast<float*>(y),
+                    static_cast<int>(dim), eps);
+  }
+  return fail(SB_EINVAL, "x must be bfloat16, float16 or float32");
+}
+
+// ------------------------------------------------------- decoder entry points
+extern "C" size_t sb_linear_ex_workspace_size(const sb_linear_ex_desc* d) {
+  if (!d || d->N <= 0 || d->K <= 0) return 0;
+  const int gk = (d->weight_format == SB_WEIGHT_AFFINE4 || d->weight_format == SB_WEIGHT_AFFINE8) ? d->group_size : 64;
+  if (gk <= 0) return 0;
+  return linear_workspace_size(d->epilogue, static_cast<int>(d->N), static_cast<int>(d->K), gk);
+}
+
+extern "C" int sb_linear_ex(const sb_linear_ex_desc* d, void* stream) {
+  SB_REQUIRE(d != nullptr, "null descriptor");
+  if (int st = check_sizes(d->M, d->N, d->K)) return st;
+  SB_REQUIRE(d->epilogue >= SB_EPI_STORE && d->epilogue <= SB_EPI_ARGMAX, "unknown epilogue");
+  SB_REQUIRE(d->weight_format >= SB_WEIGHT_AFFINE4 && d->weight_format <= SB_WEIGHT_BF16, "unknown weight format");
+  LinearRequest r = base_request(d->x, d->x_dtype, d->M, d->N, d->K);
+  r.ldx = d->ldx > 0 ? static_cast<int>(d->ldx) : static_cast<int>(d->K);
+  r.ldy = d->ldy > 0 ? static_cast<int>(d->ldy) : static_cast<int>(d->N);
+  r.wf = d->weight_format;
+  r.w0 = d->weight;
+  r.s0 = d->scales;
+  r.b0 = d->biases;
+  r.w1 = d->weight2;
+  r.s1 = d->scales2;
+  r.b1 = d->biases2;
+  r.group_size = d->group_size;
+  r.epi = d->epilogue;
+  r.norm = d->norm_weight != nullptr;
+  r.norm_w = d->norm_weight;
+  r.eps = d->norm_eps;
+  r.y = d->y;
+  r.residual = d->residual;
+  r.ldr = d->ldr > 0 ? static_cast<int>(d->ldr) : r.ldy;
+  r.positions = d->positions;
+  r.heads_q = d->num_heads;
+  r.heads_kv = d->num_kv_heads;
+  r.head_dim = d->head_dim;
+  r.seq_len = d->seq_len > 0 ? d->seq_len : 1;
+  r.rope_dims = d->head_dim;
+  r.rope_base = d->rope_base;
+  r.q_out = d->q_out;
+  r.k_out = d->k_out;
+  r.v_out = d->v_out;
+  r.argmax_keys = d->argmax_keys;
+  r.workspace = d->workspace;
+  r.workspace_bytes = d->workspace_bytes;
+  return run_linear(r, as_stream(stream));
+}
+
+extern "C" int sb_kv_append_int8(const void* k_new, const void* v_new, int8_t* k_cache, void* k_scale,
+                                 int8_t* v_cache, void* v_scale, int64_t batch, int num_kv_heads, int64_t seq_len,
+                                 int head_dim, int64_t capacity, const int32_t* start, void* stream) {
+  SB_REQUIRE(batch > 0 && num_kv_heads > 0 && seq_len > 0 && head_dim > 0 && capacity > 0, "empty KV append");
+  const int items = static_cast<int>(batch * num_kv_heads * seq_len);
+  const int warps = 4;
+  return launch("kv_append", kv_append_kernel, dim3((items + warps - 1) / warps), dim3(32 * warps), 0,
+                as_stream(stream), static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new),
+                k_cache, static_cast<__half*>(k_scale), v_cache, static_cast<__half*>(v_scale), num_kv_heads,
+                static_cast<int>(seq_len), head_dim, static_cast<int>(capacity), start);
+}
+
+extern "C" int sb_embed_rows(const void* table, const int32_t* ids, void* out, int64_t rows, int64_t hidden,
+                             int64_t vocab, void* stream) {
+  SB_REQUIRE(rows > 0 && hidden > 0 && hidden % 8 == 0 && vocab > 0, "bad embedding shape");
+  return launch("embed", embed_kernel, dim3(static_cast<unsigned>(rows)), dim3(128), 0, as_stream(stream),
+                static_cast<const __nv_bfloat16*>(table), ids, static_cast<__nv_bfloat16*>(out),
+                static_cast<int>(hidden), static_cast<int>(vocab));
+}
+
+extern "C" int sb_decode_advance(unsigned long long* argmax_keys, int32_t* tokens, int32_t* positions, int batch,
+                                 int advance, void* stream) {
+  SB_REQUIRE(batch > 0 && batch <= 1024, "batch must be in [1, 1024]");
+  return launch("decode_advance", decode_advance_kernel, dim3(1), dim3(((batch + 31) / 32) * 32), 0,
+                as_stream(stream), argmax_keys, tokens, positions, batch, advance);
+}
+

@@ -1,0 +1,402 @@
+// INT8-KV single-query decode attention (flash-decoding, split-K) for sm_100a.
+//
+// Reference: extensions/spark-mlx-ext/spark_mlx_ext/int8_quantized_sdpa.py:156-287
+// with the online-softmax kernel _int8_sdpa_sources.py:8-181 and its merge
+// :363-376. KV format here: int8 codes [B, KH, cap, D]
+// with one fp16 scale per token per head (K = code * scale).
+//
+// Design (B200): the KV stream is the HBM-bound part (260 bytes per token per
+// KV head); everything else lives in registers. One CTA handles one
+// (batch, kv head, token range); its 4 warps take 16-token blocks in turn.
+// Scores and P.V run on the tensor cores (mma.sync m16n8k16, fp16 operands,
+// fp32 accumulate): the G query heads sharing a KV head are the MMA rows
+// (GQA reuse: every K/V byte is loaded once for all G heads). int8 codes are
+// turned into the exact fp16 values 1024 + (code + 128) by byte permutes; the
+// constant 1152 they carry is removed exactly afterwards (for QK with the
+// precomputed sum of q, for PV with an MMA of the rounded probabilities
+// against ones). q is scaled by a power of two per head so its fp16 copy is
+// exact. The head dimension is permuted across lanes so every lane loads
+// whole 16-byte segments of K and V rows. Softmax is fp32 (exp2 with log2(e)
+// folded into the scale). Partial results of the warps merge in shared
+// memory, the CTAs' partials in a workspace; the last CTA of each (batch, kv
+// head) merges them in a fixed order (deterministic, one launch).
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+
+#include "sb_common.cuh"
+
+namespace sb {
+
+constexpr int kSdpaWarps = 4;
+constexpr int kSdpaD = 128;
+constexpr int kPartStride = kSdpaD + 4;  // O[D], then m, l
+
+struct SdpaParams {
+  const __nv_bfloat16* q;  // [B, H, D]
+  const int8_t* k;         // [B*KH, cap, D]
+  const __half* ks;        // [B*KH, cap]
+  const int8_t* v;
+  const __half* vs;
+  __nv_bfloat16* out;  // [B, H, D]
+  int kv_heads, length, capacity, splits;
+  const int* length_dev;  // optional per-batch lengths in device memory (+ length_offset)
+  int length_offset;
+  float scale_log2e;
+  float* partial;      // [B*KH][splits][G][kPartStride]
+  unsigned* counters;  // [B*KH]
+};
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const __grid_constant__ SdpaParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  const int bkv = blockIdx.x;
+  const int split = blockIdx.y;
+  const int b = bkv / p.kv_heads, kvh = bkv % p.kv_heads;
+  grid_dependency_wait();
+  const int N = p.length_dev ? min(p.length_dev[b] + p.length_offset, p.capacity) : p.length;
+  const int nblk = (N + 15) / 16;
+  const int blk_begin = static_cast<int>((static_cast<long long>(nblk) * split) / p.splits);
+  const int blk_end = static_cast<int>((static_cast<long long>(nblk) * (split + 1)) / p.splits);
+  const size_t kv_base = static_cast<size_t>(bkv) * p.capacity;
+  const int8_t* kbase = p.k + kv_base * kSdpaD;
+  const int8_t* vbase = p.v + kv_base * kSdpaD;
+  const __half* ksb = p.ks + kv_base;
+  const __half* vsb = p.vs + kv_base;
+
+  // ---- q fragments: row g = query head kvh*G + g, k-slot d = 32t + 4s + {0..3}
+  const bool head_ok = g < G;
+  const int head = kvh * G + (head_ok ? g : 0);
+  const __nv_bfloat16* qrow = p.q + (static_cast<size_t>(b) * p.kv_heads * G + head) * kSdpaD + 32 * t;
+  float qv[32];
+  {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 w = *reinterpret_cast<const uint4*>(qrow + 8 * i);
+      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        qv[8 * i + 2 * j] = bf16_lo(ww[j]);
+        qv[8 * i + 2 * j + 1] = bf16_hi(ww[j]);
+      }
+    }
+  }
+  float qmax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) qmax = fmaxf(qmax, fabsf(qv[i]));
+  qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
+  qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 2));
+  int qexp = 0;
+  frexpf(qmax, &qexp);  // qmax < 2^qexp
+  const float up = qmax > 0.f ? ldexpf(1.0f, 15 - qexp) : 1.0f;     // |q*up| < 2^15
+  const float down = qmax > 0.f ? ldexpf(1.0f, qexp - 15) : 1.0f;
+  // A operand: a0 = slots (2t, 2t+1) -> d = 32t+4s+{0,1}; a2 = slots (2t+8, 2t+9) -> d = 32t+4s+{2,3}
+  uint32_t aq[8], aq2[8];
+  float qsum = 0.f;
+#pragma unroll
+  for (int s = 0; s < 8; ++s) {
+    const __half2 lo = __floats2half2_rn(qv[4 * s] * up, qv[4 * s + 1] * up);
+    const __half2 hi = __floats2half2_rn(qv[4 * s + 2] * up, qv[4 * s + 3] * up);
+    aq[s] = head_ok ? *reinterpret_cast<const uint32_t*>(&lo) : 0u;
+    aq2[s] = head_ok ? *reinterpret_cast<const uint32_t*>(&hi) : 0u;
+    if (head_ok) {
+      const float2 fl = __half22float2(lo), fh = __half22float2(hi);
+      qsum += (fl.x + fl.y) + (fh.x + fh.y);
+    }
+  }
+  qsum += __shfl_xor_sync(0xffffffffu, qsum, 1);
+  qsum += __shfl_xor_sync(0xffffffffu, qsum, 2);
+  const float qoff = 1152.0f * qsum;                 // sum(q' * 1152) over D
+  const float fscale = down * p.scale_log2e;         // undo q scaling, softmax scale, log2(e)
+
+  // ---- running state (row g of the MMA tiles; rows g+8 are unused padding)
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[16][4];
+  float psum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+  constexpr uint32_t kOnes = 0x3C003C00u;
+
+  for (int blk = blk_begin + warp; blk < blk_end; blk += kSdpaWarps) {
+    const int tb = blk * 16;
+    // K rows for QK n-tiles u = 0, 1 (token tb + 8u + g), bytes 32t..32t+31
+    uint32_t kw[2][8];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int tok = min(tb + 8 * u + g, N - 1);
+      const int8_t* kp = kbase + static_cast<size_t>(tok) * kSdpaD + 32 * t;
+      const uint4 a = ldg_stream16(kp), c = ldg_stream16(kp + 16);
+      kw[u][0] = a.x; kw[u][1] = a.y; kw[u][2] = a.z; kw[u][3] = a.w;
+      kw[u][4] = c.x; kw[u][5] = c.y; kw[u][6] = c.z; kw[u][7] = c.w;
+    }
+    // V rows for tokens tb + {2t, 2t+1, 2t+8, 2t+9}, bytes 16g..16g+15
+    uint4 vr[4];
+    int vt[4] = {tb + 2 * t, tb + 2 * t + 1, tb + 2 * t + 8, tb + 2 * t + 9};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) vr[i] = ldg_stream16(vbase + static_cast<size_t>(min(vt[i], N - 1)) * kSdpaD + 16 * g);
+    float sk[4], sv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int tok = min(vt[i], N - 1);  // the same 4 tokens own this lane's scores
+      sk[i] = __half2float(ksb[tok]);
+      sv[i] = __half2float(vsb[tok]);
+    }
+
+    // QK^T: C[u] rows = heads, cols = tokens 8u + (2t, 2t+1)
+    float cqk[2][4];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) cqk[u][e] = 0.f;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const uint32_t w = kw[u][s] ^ 0x80808080u;
+        const uint32_t b0 = prmt(w, 0x64646464u, 0x4140u);
+        const uint32_t b1 = prmt(w, 0x64646464u, 0x4342u);
+        const uint32_t a[4] = {aq[s], 0u, aq2[s], 0u};
+        mma_16816<true>(cqk[u], a, b0, b1);
+      }
+    }
+    // scores (log2 domain) for tokens vt[0..3] = (u0: 2t, 2t+1), (u1: 2t+8, 2t+9)
+    float sc[4];
+    sc[0] = (cqk[0][0] - qoff) * fscale * sk[0];
+    sc[1] = (cqk[0][1] - qoff) * fscale * sk[1];
+    sc[2] = (cqk[1][0] - qoff) * fscale * sk[2];
+    sc[3] = (cqk[1][1] - qoff) * fscale * sk[3];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      if (vt[i] >= N) sc[i] = -INFINITY;
+    float mb = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+    mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+    mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
+    const float m_new = fmaxf(m_run, mb);
+    const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
+    float pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = (vt[i] < N) ? exp2f(sc[i] - m_new) : 0.f;
+    l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+    m_run = m_new;
+#pragma unroll
+    for (int j = 0; j < 16; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[j][e] *= alpha;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) psum[e] *= alpha;
+    // P' = p * v_scale as the fp16 A operand (rows = heads, k = tokens)
+    uint32_t ap[4];
+    ap[0] = head_ok ? pack_half2(pr[0] * sv[0], pr[1] * sv[1]) : 0u;
+    ap[1] = 0u;
+    ap[2] = head_ok ? pack_half2(pr[2] * sv[2], pr[3] * sv[3]) : 0u;
+    ap[3] = 0u;
+    mma_16816<true>(psum, ap, kOnes, kOnes);
+    // P'V: n-tile j covers d = 16n + j; lane's B column n = g -> bytes j of its V segments
+    const uint32_t* va = reinterpret_cast<const uint32_t*>(&vr[0]);
+    const uint32_t* vb = reinterpret_cast<const uint32_t*>(&vr[1]);
+    const uint32_t* vc = reinterpret_cast<const uint32_t*>(&vr[2]);
+    const uint32_t* vd = reinterpret_cast<const uint32_t*>(&vr[3]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t sel = static_cast<uint32_t>(j & 3) | (static_cast<uint32_t>(4 + (j & 3)) << 8);
+      uint32_t b0 = prmt(va[j >> 2], vb[j >> 2], sel);
+      uint32_t b1 = prmt(vc[j >> 2], vd[j >> 2], sel);
+      b0 = (b0 & 0x00FF00FFu) ^ 0x64806480u;
+      b1 = (b1 & 0x00FF00FFu) ^ 0x64806480u;
+      mma_16816<true>(acc[j], ap, b0, b1);
+    }
+  }
+
+  // ---- warp result: o[d] = acc - 1152 * sum(P'); d(j, c0) = 32t + j, d(j, c1) = 32t + 16 + j
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  __shared__ float s_m[kSdpaWarps][8], s_l[kSdpaWarps][8];
+  __shared__ float s_o[kSdpaWarps][8][kSdpaD];
+  if (head_ok) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      s_o[warp][g][32 * t + j] = acc[j][0] - 1152.0f * psum[0];
+      s_o[warp][g][32 * t + 16 + j] = acc[j][1] - 1152.0f * psum[1];
+    }
+    if (t == 0) {
+      s_m[warp][g] = m_run;
+      s_l[warp][g] = l_run;
+    }
+  }
+  __syncthreads();
+  grid_dependency_launch();
+
+  // ---- CTA merge (fixed warp order) -> partial or final output
+  const bool single = p.splits == 1;
+  float* part = p.partial + (static_cast<size_t>(bkv) * p.splits + split) * G * kPartStride;
+  for (int idx = threadIdx.x; idx < G * kSdpaD; idx += kSdpaWarps * 32) {
+    const int hh = idx / kSdpaD, d = idx % kSdpaD;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kSdpaWarps; ++w) mm = fmaxf(mm, s_m[w][hh]);
+    float ll = 0.f, oo = 0.f;
+    if (mm != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kSdpaWarps; ++w) {
+        const float f = s_m[w][hh] == -INFINITY ? 0.f : exp2f(s_m[w][hh] - mm);
+        ll += s_l[w][hh] * f;
+        oo += s_o[w][hh][d] * f;
+      }
+    }
+    if (single) {
+      const float o = ll > 0.f ? oo / ll : 0.f;
+      p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] = __float2bfloat16_rn(o);
+    } else {
+      part[hh * kPartStride + d] = oo;
+      if (d == 0) {
+        part[hh * kPartStride + kSdpaD] = mm;
+        part[hh * kPartStride + kSdpaD + 1] = ll;
+      }
+    }
+  }
+  if (single) return;
+
+  __threadfence();
+  __syncthreads();
+  __shared__ unsigned s_prev;
+  if (threadIdx.x == 0) s_prev = atomicAdd(p.counters + bkv, 1u);
+  __syncthreads();
+  if (s_prev != static_cast<unsigned>(p.splits - 1)) return;
+  __threadfence();
+  const float* all = p.partial + static_cast<size_t>(bkv) * p.splits * G * kPartStride;
+  for (int idx = threadIdx.x; idx < G * kSdpaD; idx += kSdpaWarps * 32) {
+    const int hh = idx / kSdpaD, d = idx % kSdpaD;
+    float mm = -INFINITY;
+    for (int s = 0; s < p.splits; ++s) mm = fmaxf(mm, __ldcg(all + (s * G + hh) * kPartStride + kSdpaD));
+    float ll = 0.f, oo = 0.f;
+    if (mm != -INFINITY) {
+      for (int s = 0; s < p.splits; ++s) {
+        const float* ps = all + (s * G + hh) * kPartStride;
+        const float ms = __ldcg(ps + kSdpaD);
+        if (ms == -INFINITY) continue;
+        const float f = exp2f(ms - mm);
+        ll += __ldcg(ps + kSdpaD + 1) * f;
+        oo += __ldcg(ps + d) * f;
+      }
+    }
+    const float o = ll > 0.f ? oo / ll : 0.f;
+    p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] = __float2bfloat16_rn(o);
+  }
+  if (threadIdx.x == 0) p.counters[bkv] = 0u;
+}
+
+namespace {
+
+int sdpa_sms() {
+  static int count = 0;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
+      count = 148;
+  });
+  return count;
+}
+
+int sdpa_splits(int64_t batch, int kv_heads, int64_t length) {
+  const int64_t bkv = batch * kv_heads;
+  const int64_t nblk = (length + 15) / 16;
+  int64_t s = (sdpa_sms() * 4 + bkv - 1) / bkv;
+  s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (2 * kSdpaWarps)));  // >= 2 blocks per warp
+  s = std::min<int64_t>(s, 64);
+  return static_cast<int>(std::max<int64_t>(1, s));
+}
+
+}  // namespace
+
+size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int64_t length) {
+  const int splits = sdpa_splits(batch, num_kv_heads, length);
+  const int64_t bkv = batch * num_kv_heads;
+  const int G = num_heads / num_kv_heads;
+  const size_t counters = ((static_cast<size_t>(bkv) * 4 + 255) / 256) * 256;
+  return counters + static_cast<size_t>(bkv) * splits * G * kPartStride * sizeof(float);
+}
+
+int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int8_t* v, const void* v_scale,
+                  void* out, int64_t batch, int num_heads, int num_kv_heads, int64_t length, int64_t capacity,
+                  int head_dim, float scale, void* workspace, size_t workspace_bytes, cudaStream_t stream,
+                  int force_splits, const int* length_dev, int length_offset) {
+  SB_REQUIRE(head_dim == kSdpaD, "this build supports head_dim 128");
+  SB_REQUIRE(batch > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
+             "Nonempty inputs and query heads divisible by KV heads required");
+  const int G = num_heads / num_kv_heads;
+  SB_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, "query heads per KV head must be 1, 2, 4 or 8");
+  SB_REQUIRE(length > 0 && length <= capacity && capacity < (1LL << 31), "need 0 < length <= capacity < 2^31");
+  SB_REQUIRE(std::isfinite(scale), "scale must be finite");
+  SB_REQUIRE(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) &
+              15) == 0,
+             "q, k and v must be 16-byte aligned");
+  int splits = force_splits > 0 ? force_splits : sdpa_splits(batch, num_kv_heads, length);
+  const int64_t bkv = batch * num_kv_heads;
+  const size_t counters = ((static_cast<size_t>(bkv) * 4 + 255) / 256) * 256;
+  const size_t need = counters + static_cast<size_t>(bkv) * splits * G * kPartStride * sizeof(float);
+  if (splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
+    SB_REQUIRE(force_splits <= 0, "workspace too small for the requested split count");
+    splits = 1;
+  }
+  SdpaParams p{};
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = k;
+  p.ks = static_cast<const __half*>(k_scale);
+  p.v = v;
+  p.vs = static_cast<const __half*>(v_scale);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.kv_heads = num_kv_heads;
+  p.length = static_cast<int>(length);
+  p.capacity = static_cast<int>(capacity);
+  p.splits = splits;
+  p.length_dev = length_dev;
+  p.length_offset = length_offset;
+  p.scale_log2e = scale * 1.4426950408889634f;
+  if (splits > 1) {
+    p.counters = static_cast<unsigned*>(workspace);
+    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
+  }
+  const dim3 grid(static_cast<unsigned>(bkv), splits);
+  const dim3 block(kSdpaWarps * 32);
+  switch (G) {
+    case 1: return launch("int8 sdpa", sdpa_int8_decode_kernel<1>, grid, block, 0, stream, p);
+    case 2: return launch("int8 sdpa", sdpa_int8_decode_kernel<2>, grid, block, 0, stream, p);
+    case 4: return launch("int8 sdpa", sdpa_int8_decode_kernel<4>, grid, block, 0, stream, p);
+    default: return launch("int8 sdpa", sdpa_int8_decode_kernel<8>, grid, block, 0, stream, p);
+  }
+}
+
+}  // namespace sb
+
+extern "C" size_t sb_int8_sdpa_workspace_size(int64_t batch, int num_heads, int num_kv_heads, int64_t length,
+                                              int head_dim) {
+  if (batch <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || length <= 0 || head_dim != sb::kSdpaD)
+    return 0;
+  return sb::sdpa_workspace_bytes(batch, num_heads, num_kv_heads, length);
+}
+
+extern "C" int sb_int8_sdpa_decode(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                                   const void* v_scale, void* out, int64_t batch, int num_heads, int num_kv_heads,
+                                   int64_t length, int64_t capacity, int head_dim, float scale, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+  return sb::run_sdpa_int8(q, k, k_scale, v, v_scale, out, batch, num_heads, num_kv_heads, length, capacity,
+                           head_dim, scale, workspace, workspace_bytes, sb::as_stream(stream), 0, nullptr, 0);
+}
+
+extern "C" int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                                       const void* v_scale, void* out, int64_t batch, int num_heads,
+                                       int num_kv_heads, const int32_t* lengths, int length_offset,
+                                       int64_t max_length, int64_t capacity, int head_dim, float scale,
+                                       void* workspace, size_t workspace_bytes, void* stream) {
+  SB_REQUIRE(lengths != nullptr, "lengths must be a device pointer");
+  return sb::run_sdpa_int8(q, k, k_scale, v, v_scale, out, batch, num_heads, num_kv_heads, max_length, capacity,
+                           head_dim, scale, workspace, workspace_bytes, sb::as_stream(stream), 0, lengths,
+                           length_offset);
+}
