@@ -1,0 +1,376 @@
+"""Benchmark of the B200 decode hot path (one JSON line on rank 0).
+
+Workload: BASELINE.json config 4, the synthetic 4B-class decoder (36 layers,
+hidden 2560, 32/8 heads, INT4-G64 MLP, INT8 attention projections, bf16
+embedding/lm_head, INT8 KV cache), greedy decode at batch 1 after a
+1024-token prompt of seeded uniform-random token ids. A step is one generated
+token (one CUDA-graph replay of the whole decode step). With
+``--gpus N`` the decoder is tensor parallel over N GPUs (launched by
+torch.distributed.run, NCCL).
+
+* ``value``   tokens/s with everything resident in HBM (CUDA events around K
+              replays, max over ranks).
+* ``e2e``     the same through the public decode API with a pinned host->device
+              copy of the input token and a device->host read of the output
+              token plus a stream sync every step.
+* ``roofline`` the dominant kernel (RMSNorm + gate/up W4A16 GEMV + SwiGLU),
+              timed alone over the 36 layers' weights (1 GB, L2-cold).
+* ``cpu_baseline`` the NumPy oracle on the host cores, bounded sample.
+
+``--impl reference`` times the reference arithmetic on the CPU (the oracle
+port of the reference's CPU path; the reference itself needs MLX, which is
+not installable here) and prints the same metric.
+"""
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [ROOT, os.path.join(ROOT, "spark-mlx-llm_b200")]
+
+METRIC = "W4A16 decode tok/s bs1 @1/2/4/8 B200; GEMV & INT8-KV SDPA HBM GB/s vs peak"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=256)
+    p.add_argument("--warmup", type=int, default=8)
+    p.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    p.add_argument("--batch", type=int, default=1)
+    p.add_argument("--prompt", type=int, default=1024)
+    p.add_argument("--layers", type=int, default=36, help="(debug) fewer layers")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            data = json.load(f)
+        return float(data["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic():
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "gateup_w4a16_gemv_decode_bs1.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                if line.strip().startswith("dram_bytes_per_launch:"):
+                    return int(float(line.split(":", 1)[1].strip().split()[0]))
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = float(r[2])
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, r[5:9]):
+                if "Active" in val and "Not" not in val:
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- CPU reference
+def cpu_reference(cfg, batch, context, layers_sample=2, head_fraction=16, reps=3):
+    """Decode tok/s of the NumPy oracle (reference arithmetic) on this host's cores.
+
+    Bounded sample: ``layers_sample`` decoder layers plus 1/``head_fraction`` of
+    the lm_head rows for one token at position ``context``, scaled to the full
+    model (36 layers, full vocabulary).
+    """
+    import numpy as np
+    import torch
+
+    from oracle import formats, ops
+    from oracle.model import OracleDecoder
+    from spark_b200 import quantize
+
+    torch.manual_seed(0)
+    d = cfg.head_dim
+    gen = torch.Generator().manual_seed(1234)
+
+    def randn(*shape, std):
+        return torch.randn(*shape, generator=gen) * std
+
+    def aff(w):
+        p, s, b = quantize.quantize_affine_minmax(w, cfg.mlp_group, 4)
+        return p.numpy().view(np.uint32), s.float().numpy(), b.float().numpy()
+
+    layers = []
+    for _ in range(layers_sample):
+        qkv_w, qkv_s = quantize.quantize_w8_per_channel(randn((cfg.num_heads + 2 * cfg.num_kv_heads) * d, cfg.hidden,
+                                                              std=cfg.weight_std))
+        o_w, o_s = quantize.quantize_w8_per_channel(randn(cfg.hidden, cfg.num_heads * d, std=cfg.weight_std))
+        layers.append(dict(qkv_w=qkv_w.numpy(), qkv_s=qkv_s.numpy(), o_w=o_w.numpy(), o_s=o_s.numpy(),
+                           gate=aff(randn(cfg.intermediate, cfg.hidden, std=cfg.weight_std)),
+                           up=aff(randn(cfg.intermediate, cfg.hidden, std=cfg.weight_std)),
+                           down=aff(randn(cfg.hidden, cfg.intermediate, std=cfg.weight_std)),
+                           in_norm=np.ones(cfg.hidden, np.float32), post_norm=np.ones(cfg.hidden, np.float32)))
+    vocab_sample = cfg.vocab // head_fraction
+    weights = dict(layers=layers,
+                   embed=formats.round_bf16(randn(vocab_sample, cfg.hidden, std=1.0).numpy()),
+                   head=formats.round_bf16(randn(vocab_sample, cfg.hidden, std=cfg.head_std).numpy()),
+                   final_norm=np.ones(cfg.hidden, np.float32))
+    orc = OracleDecoder(weights, num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=d,
+                        rope_theta=cfg.rope_theta, eps=cfg.rms_eps, group=cfg.mlp_group, capacity=context + 1,
+                        batch=batch)
+    rng = np.random.default_rng(0)
+    orc.kq[...] = rng.integers(-127, 128, orc.kq.shape, dtype=np.int8)
+    orc.vq[...] = rng.integers(-127, 128, orc.vq.shape, dtype=np.int8)
+    orc.ks[...] = np.float16(0.02)
+    orc.vs[...] = np.float16(0.02)
+    tokens = rng.integers(0, vocab_sample, batch)
+    # time the layers and the head separately
+    layer_times, head_times = [], []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        logits = orc.step(tokens, context)
+        t1 = time.perf_counter()
+        x = orc.last_x
+        xn = formats.round_bf16(ops.rms_norm(x, weights["final_norm"], cfg.rms_eps))
+        t2 = time.perf_counter()
+        _ = xn.astype(np.float64) @ weights["head"].astype(np.float64).T
+        t3 = time.perf_counter()
+        layer_times.append((t1 - t0) - (t3 - t2))
+        head_times.append(t3 - t2)
+        del logits
+    per_layer = min(layer_times) / layers_sample
+    head = min(head_times) * head_fraction
+    token_s = per_layer * cfg.num_layers + head
+    sample = (f"{layers_sample} of {cfg.num_layers} layers + 1/{head_fraction} of lm_head rows, one decode "
+              f"token at context {context}, batch {batch}, best of {reps}; scaled to the full model")
+    return batch / token_s, os.cpu_count(), sample
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from spark_b200.decoder import DecoderConfig
+
+    cfg = DecoderConfig(num_layers=args.layers)
+    vals = []
+    sample = cores = None
+    for _ in range(max(1, min(args.steps, 2))):
+        v, cores, sample = cpu_reference(cfg, args.batch, args.prompt)
+        vals.append(v)
+    value = statistics.median(vals)
+    out = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * args.batch / value,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": workload_config(args, "cpu"),
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "NumPy oracle restating the reference arithmetic (MLX, the reference's own CPU path, is not "
+                "installable offline)",
+    }
+    print(json.dumps(out), flush=True)
+
+
+def workload_config(args, parallel):
+    return {
+        "workload": "synthetic 4B-class decoder (BASELINE config 4): 36 layers, hidden 2560, 32/8 heads x 128, "
+                    "SwiGLU 9728 INT4-G64, INT8 per-channel attention, bf16 embedding/lm_head, INT8 KV; greedy "
+                    f"decode batch {args.batch} after a {args.prompt}-token prompt",
+        "batch": args.batch, "prompt_tokens": args.prompt, "layers": args.layers, "parallelism": parallel,
+        "l2": "inputs larger than L2: every step streams ~3.2 GB of weights (126 MB L2)",
+    }
+
+
+# -------------------------------------------------------------------- GPU arm
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        group = dist.group.WORLD
+
+    from spark_b200 import decoder as dec_mod
+    from spark_b200.decoder import DecoderConfig, SyntheticDecoder
+
+    cfg = DecoderConfig(num_layers=args.layers)
+    capacity = args.prompt + args.warmup + 2 * args.steps + 16
+    dec = SyntheticDecoder(cfg, batch=args.batch, capacity=capacity, device=device, seed=0, rank=rank, world=world,
+                           group=group)
+    gen = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab, (args.batch, args.prompt), generator=gen, dtype=torch.int32)
+    dec.prefill(prompt.to(device))
+    dec.capture()
+    for _ in range(args.warmup):
+        dec.graph.replay()
+    torch.cuda.synchronize(device)
+
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    # ---- device-resident throughput
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(args.steps):
+        dec.graph.replay()
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    value = args.batch * args.steps / (ms / 1000.0)
+
+    # ---- end to end: pinned H2D of the input token, replay, D2H of the output token, sync
+    host_tok = torch.empty((args.batch,), dtype=torch.int32, pin_memory=True)
+    host_tok.copy_(dec.tokens.cpu())
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        dec.tokens.copy_(host_tok, non_blocking=True)
+        dec.graph.replay()
+        host_tok.copy_(dec.tokens, non_blocking=True)
+        stream.synchronize()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1)
+    t = torch.tensor([e2e_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t.item())
+    clocks = sampler.stop()
+
+    # ---- dominant kernel alone: gate/up over all layers' weights (L2-cold), CUDA events
+    L = dec_mod.lib()
+    import ctypes
+
+    reps = 4
+    torch.cuda.synchronize(device)
+    k0, k1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(2):
+        for desc in dec.descs:
+            L.sb_linear_ex(ctypes.byref(desc[2]), stream.cuda_stream)
+    k0.record(stream)
+    for _ in range(reps):
+        for desc in dec.descs:
+            L.sb_linear_ex(ctypes.byref(desc[2]), stream.cuda_stream)
+    k1.record(stream)
+    torch.cuda.synchronize(device)
+    launches = reps * len(dec.descs)
+    kernel_us = k0.elapsed_time(k1) * 1000.0 / launches
+    inter, hid, g = dec.inter, cfg.hidden, cfg.mlp_group
+    algo_bytes = (2 * (inter * hid // 2 + inter * (hid // g) * 4)  # gate + up codes, scales, biases
+                  + args.batch * hid * 2 * 2 + hid * 2             # x + its full-row norm read, norm weight
+                  + args.batch * inter * 2)                         # output
+    achieved = algo_bytes / (kernel_us * 1e-6) / 1e9
+    peak, peak_kind = measured_peaks()
+    traffic = profile_traffic()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_v, cores, sample = cpu_reference(cfg, args.batch, args.prompt)
+        cpu = {"value": cpu_v, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, uniform random prompt)",
+            "config": workload_config(args, f"tp{world}"),
+            "e2e": {"value": args.batch * args.steps / (e2e_ms / 1000.0), "unit": "tok/s",
+                    "h2d_bytes_per_step": 4 * args.batch, "d2h_bytes_per_step": 4 * args.batch},
+            "gpu_launches": dec.kernels_per_step() * args.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "rmsnorm+gate/up W4A16 GEMV+SwiGLU (per layer, per rank)",
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6.65 TB/s", "algo_bytes_per_launch": algo_bytes,
+                         "avg_launch_us": kernel_us},
+            "weights_gb_per_step": cfg.weight_bytes() / 1e9,
+            "step_weight_gbs": cfg.weight_bytes() / world / (ms / args.steps * 1e-3) / 1e9,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        del dec.graph
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -65,10 +65,16 @@ typedef struct sb_linear_ex_desc {
   void* q_out;
   void* k_out;
   void* v_out;
-  /* ARGMAX: [M] keys, zero before the launch */
+  /* ARGMAX: [M] keys, zero before the launch; row indices are reported plus
+   * argmax_offset (the first vocabulary row of this shard) */
   unsigned long long* argmax_keys;
+  int argmax_offset;
   void* workspace;
   size_t workspace_bytes;
+  /* 1: weights/scales are not written by any kernel still in flight on the
+   * stream (model weights), so the kernel may start streaming them before the
+   * previous kernel has finished; 0: wait for the previous kernel first. */
+  int weights_constant;
 } sb_linear_ex_desc;
 
 /* Fused weight-streaming linear (1 <= M <= 8). */
@@ -96,6 +102,10 @@ int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const void* k_scale,
  * (spark_mlx_llm/model.py:296-305). */
 int sb_embed_rows(const void* table, const int32_t* ids, void* out, int64_t rows, int64_t hidden, int64_t vocab,
                   void* stream);
+
+/* x = T(x + y) elementwise over `count` bf16 values (the residual add after a
+ * tensor-parallel all-reduce; replaces `x + attention_output`, ops/ffn.py:98). */
+int sb_residual_add(void* x, const void* y, int64_t count, void* stream);
 
 /* Greedy step bookkeeping: tokens[b] = index encoded in argmax_keys[b],
  * argmax_keys[b] = 0, positions[b] += advance. */

@@ -24,6 +24,13 @@ int check_launch(const char* what);
 
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
 
+// Every workspace starts with a fixed-size region of arrival counters (zero
+// between calls), followed by the call's partial results. The fixed size keeps
+// one call's partials from ever overlapping another call's counters when
+// different operators share one workspace.
+constexpr size_t kCounterBytes = 128 * 1024;
+constexpr int kMaxCounters = static_cast<int>(kCounterBytes / sizeof(unsigned));
+
 // Launch helper: every kernel is launched with programmatic stream
 // serialization allowed, so a dependent kernel may start its weight prefetch
 // while the previous kernel drains (it waits with griddepcontrol.wait before

@@ -212,7 +212,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_kernel(const __grid_c
     }
   }
 
-  // ---- prefetch the first chunk of weights (independent of earlier kernels)
+  // ---- prefetch the first chunk of weights; with constant weights this may
+  // overlap the tail of the previous kernel in the stream
+  if (!p.early_prefetch) grid_dependency_wait();
   uint32_t wbuf[kRows][kWords];
   if (active && chunk_begin < chunk_end) {
 #pragma unroll
@@ -477,7 +479,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_kernel(const __grid_c
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int m = 2 * t + e;
-        if (m < mcols && best_i[e] != 0x7FFFFFFF) atomicMax(p.argmax_keys + m, argmax_key(best[e], best_i[e]));
+        if (m < mcols && best_i[e] != 0x7FFFFFFF)
+          atomicMax(p.argmax_keys + m, argmax_key(best[e], best_i[e] + p.argmax_offset));
       }
     }
     return;
@@ -602,7 +605,8 @@ Plan make_plan(int epi, int N, int K, int group_k, bool allow_split) {
   s = std::max(s, min_s);
   s = std::min(s, pl.groups);
   pl.splits = std::max(1, s);
-  pl.counter_bytes = ((static_cast<size_t>(pl.rowblocks) * 4 + 255) / 256) * 256;
+  if (pl.rowblocks > kMaxCounters) pl.splits = 1;
+  pl.counter_bytes = kCounterBytes;
   pl.partial_bytes = pl.splits > 1
                          ? static_cast<size_t>(pl.splits) * pl.rowblocks * 16 * kGemvTiles * 8 * sizeof(float)
                          : 0;
@@ -734,6 +738,8 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   p.k_out = r.k_out;
   p.v_out = r.v_out;
   p.argmax_keys = r.argmax_keys;
+  p.argmax_offset = r.argmax_offset;
+  p.early_prefetch = r.weights_constant ? 1 : 0;
   if (r.epi == EPI_ROPE) {
     for (int i = 0; i < r.rope_dims / 2; ++i)
       p.inv_freq[i] = static_cast<float>(std::pow(static_cast<double>(r.rope_base), -2.0 * i / r.rope_dims));

@@ -79,7 +79,11 @@ struct GemvParams {
   float inv_freq[kMaxRopeHalf];
   // argmax epilogue
   unsigned long long* argmax_keys;  // [M]
+  int argmax_offset;                // added to row indices (vocab-parallel shards)
   int x_stage_max;                  // max K values staged per split (smem)
+  // 1: the weights are constant across the stream (model weights), so the
+  // kernel may start streaming them before the previous kernel finishes.
+  int early_prefetch;
 };
 
 // Common request for every linear entry point.
@@ -105,8 +109,10 @@ struct LinearRequest {
   float rope_base;
   void *q_out, *k_out, *v_out;
   unsigned long long* argmax_keys;
+  int argmax_offset;
   void* workspace;
   size_t workspace_bytes;
+  bool weights_constant;
 };
 
 int run_linear(const LinearRequest& r, cudaStream_t stream);

@@ -98,6 +98,24 @@ __global__ void embed_kernel(const __nv_bfloat16* __restrict__ table, const int*
   for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) dst[i] = src[i];
 }
 
+// ------------------------------------------------------------ residual add
+__global__ void residual_add_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y, int n) {
+  grid_dependency_wait();
+  const int i = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (i >= n) return;
+  if (i + 8 <= n) {
+    uint4 a = *reinterpret_cast<uint4*>(x + i);
+    const uint4 b = *reinterpret_cast<const uint4*>(y + i);
+    __nv_bfloat16* av = reinterpret_cast<__nv_bfloat16*>(&a);
+    const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(&b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) av[j] = __float2bfloat16_rn(__bfloat162float(av[j]) + __bfloat162float(bv[j]));
+    *reinterpret_cast<uint4*>(x + i) = a;
+  } else {
+    for (int j = i; j < n; ++j) x[j] = __float2bfloat16_rn(__bfloat162float(x[j]) + __bfloat162float(y[j]));
+  }
+}
+
 // ------------------------------------------- greedy token + position advance
 // token[b] = argmax index decoded from keys[b]; keys reset; pos[b] += 1.
 __global__ void decode_advance_kernel(unsigned long long* keys, int* tokens, int* positions, int batch,
@@ -335,8 +353,10 @@ extern "C" int sb_linear_ex(const sb_linear_ex_desc* d, void* stream) {
   r.k_out = d->k_out;
   r.v_out = d->v_out;
   r.argmax_keys = d->argmax_keys;
+  r.argmax_offset = d->argmax_offset;
   r.workspace = d->workspace;
   r.workspace_bytes = d->workspace_bytes;
+  r.weights_constant = d->weights_constant != 0;
   return run_linear(r, as_stream(stream));
 }
 
@@ -367,3 +387,13 @@ extern "C" int sb_decode_advance(unsigned long long* argmax_keys, int32_t* token
                 as_stream(stream), argmax_keys, tokens, positions, batch, advance);
 }
 
+
+extern "C" int sb_residual_add(void* x, const void* y, int64_t count, void* stream) {
+  SB_REQUIRE(count > 0 && count < (1LL << 31), "bad element count");
+  SB_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15) == 0, "x and y must be 16-byte aligned");
+  const int threads = 256;
+  const int64_t vecs = (count + 7) / 8;
+  return launch("residual_add", residual_add_kernel, dim3(static_cast<unsigned>((vecs + threads - 1) / threads)),
+                dim3(threads), 0, as_stream(stream), static_cast<__nv_bfloat16*>(x),
+                static_cast<const __nv_bfloat16*>(y), static_cast<int>(count));
+}

@@ -319,7 +319,7 @@ size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int6
   const int splits = sdpa_splits(batch, num_kv_heads, length);
   const int64_t bkv = batch * num_kv_heads;
   const int G = num_heads / num_kv_heads;
-  const size_t counters = ((static_cast<size_t>(bkv) * 4 + 255) / 256) * 256;
+  const size_t counters = kCounterBytes;
   return counters + static_cast<size_t>(bkv) * splits * G * kPartStride * sizeof(float);
 }
 
@@ -339,7 +339,8 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
              "q, k and v must be 16-byte aligned");
   int splits = force_splits > 0 ? force_splits : sdpa_splits(batch, num_kv_heads, length);
   const int64_t bkv = batch * num_kv_heads;
-  const size_t counters = ((static_cast<size_t>(bkv) * 4 + 255) / 256) * 256;
+  const size_t counters = kCounterBytes;
+  if (bkv > kMaxCounters) force_splits = 1;
   const size_t need = counters + static_cast<size_t>(bkv) * splits * G * kPartStride * sizeof(float);
   if (splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
     SB_REQUIRE(force_splits <= 0, "workspace too small for the requested split count");

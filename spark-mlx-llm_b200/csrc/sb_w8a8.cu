@@ -35,6 +35,7 @@ struct I8Params {
   int* partial;    // [splits][rows_padded][8]
   unsigned* counters;
   int rows_padded;
+  int early_prefetch;  // 1: weights are constant, stream them before waiting
 };
 
 template <typename T>
@@ -104,6 +105,7 @@ __global__ void __launch_bounds__(kI8Warps * 32, 4) i8_gemv_kernel(const __grid_
     const int row = min((min(rb, rowblocks - 1) * kI8Tiles + (q >> 1)) * 16 + (q & 1) * 8 + g, p.N - 1);
     wrow[q] = p.w + static_cast<size_t>(row) * p.K + t * 16;
   }
+  if (!p.early_prefetch) grid_dependency_wait();
   uint32_t wbuf[kRows][4];
   if (active && c_begin < c_end) {
 #pragma unroll
@@ -276,9 +278,9 @@ I8Plan plan_i8(int N, int K, bool allow_split) {
   s = std::min(s, std::max(1, pl.groups / 2));
   s = std::max(s, (K + 8191) / 8192);
   s = std::max(1, std::min(s, pl.groups));
-  pl.splits = s;
-  pl.counter_bytes = ((static_cast<size_t>(pl.rowblocks) * 4 + 255) / 256) * 256;
-  pl.partial_bytes = s > 1 ? static_cast<size_t>(s) * pl.rowblocks * 16 * kI8Tiles * 8 * sizeof(int) : 0;
+  pl.splits = pl.rowblocks > kMaxCounters ? 1 : s;
+  pl.counter_bytes = kCounterBytes;
+  pl.partial_bytes = pl.splits > 1 ? static_cast<size_t>(pl.splits) * pl.rowblocks * 16 * kI8Tiles * 8 * sizeof(int) : 0;
   return pl;
 }
 

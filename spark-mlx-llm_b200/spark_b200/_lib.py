@@ -62,8 +62,10 @@ class sb_linear_ex_desc(ctypes.Structure):
         ("k_out", _c_void_p),
         ("v_out", _c_void_p),
         ("argmax_keys", _c_void_p),
+        ("argmax_offset", _int),
         ("workspace", _c_void_p),
         ("workspace_bytes", _size),
+        ("weights_constant", _int),
     ]
 
 
@@ -119,6 +121,7 @@ SIGNATURES = {
     ),
     "sb_embed_rows": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p]),
     "sb_decode_advance": (_int, [_c_void_p, _c_void_p, _c_void_p, _int, _int, _c_void_p]),
+    "sb_residual_add": (_int, [_c_void_p, _c_void_p, _i64, _c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -1,0 +1,341 @@
+"""Synthetic 4B-class decoder on the spark_b200 kernels (1 GPU or tensor parallel).
+
+Architecture: 36 layers, hidden 2560, 32 query / 8 KV
+heads, head_dim 128, SwiGLU MLP with intermediate 9728, RMSNorm eps 1e-6,
+vocab 151936, RoPE theta 1e6. Attention projections are per-channel INT8
+(the reference's default W8A16 backend, ``spark_mlx_llm/ops/linear.py:413-476``),
+the MLP is MLX affine INT4 with group 64, embedding and lm_head are bf16, and
+the KV cache is INT8 with one fp16 scale per token per head.
+
+One decode step is, per layer (``spark_mlx_llm/model.py:172-207,249-262``):
+  1. RMSNorm + QKV projection + RoPE        -> q, k_new, v_new   (one kernel)
+  2. INT8 KV append of the new token                             (one kernel)
+  3. INT8-KV attention over the cache                            (one kernel)
+  4. o_proj + residual add                                       (one kernel)
+  5. RMSNorm + gate/up + SwiGLU                                  (one kernel)
+  6. down projection + residual add                              (one kernel)
+then RMSNorm + lm_head + greedy argmax and the token/position update. Tensor
+parallel (Megatron layout): QKV/gate/up split by output rows (heads), o/down by
+input columns followed by an NCCL all-reduce, lm_head by vocabulary rows with
+an all-reduce(max) of packed (logit, index) keys. Every per-step value lives in
+device memory, so a whole step is captured once as a CUDA graph and replayed.
+
+Weights are random (seeded) and built on the GPU: the workload has the real
+shapes, formats and byte counts, not trained values.
+"""
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import quantize
+from ._lib import check, lib, sb_linear_ex_desc
+
+__all__ = ["DecoderConfig", "SyntheticDecoder"]
+
+SB_WEIGHT_AFFINE4, SB_WEIGHT_AFFINE8, SB_WEIGHT_INT8_PC, SB_WEIGHT_BF16 = 0, 1, 2, 3
+SB_EPI_STORE, SB_EPI_RESID, SB_EPI_SWIGLU, SB_EPI_ROPE, SB_EPI_ARGMAX = 0, 1, 2, 3, 4
+BF16 = 0
+
+
+@dataclass(frozen=True)
+class DecoderConfig:
+    num_layers: int = 36
+    hidden: int = 2560
+    num_heads: int = 32
+    num_kv_heads: int = 8
+    head_dim: int = 128
+    intermediate: int = 9728
+    vocab: int = 151936
+    rms_eps: float = 1e-6
+    rope_theta: float = 1e6
+    mlp_group: int = 64
+    # init scales of the synthetic weights
+    weight_std: float = 0.02
+    embed_std: float = 1.0
+    head_std: float = 0.02
+
+    @staticmethod
+    def small(**overrides):
+        """A reduced shape with the same kernels (tests)."""
+        base = dict(num_layers=2, hidden=512, num_heads=4, num_kv_heads=2, head_dim=128, intermediate=1024,
+                    vocab=1000)
+        base.update(overrides)
+        return DecoderConfig(**base)
+
+    def weight_bytes(self):
+        """HBM bytes of weights read per decode step (all shards together)."""
+        q = self.num_heads * self.head_dim
+        kv = self.num_kv_heads * self.head_dim
+        qkv = (q + 2 * kv) * self.hidden + (q + 2 * kv) * 4
+        o = self.hidden * q + self.hidden * 4
+        g = self.mlp_group
+        mlp_in = 2 * (self.intermediate * self.hidden // 2 + self.intermediate * (self.hidden // g) * 4)
+        mlp_out = self.hidden * self.intermediate // 2 + self.hidden * (self.intermediate // g) * 4
+        norms = 2 * self.hidden * 2
+        per_layer = qkv + o + mlp_in + mlp_out + norms
+        return self.num_layers * per_layer + self.vocab * self.hidden * 2 + self.hidden * 2
+
+
+def _ptr(t):
+    return 0 if t is None else t.data_ptr()
+
+
+class SyntheticDecoder:
+    """The decoder's weights, INT8 KV cache, device state and launch sequence.
+
+    ``rank``/``world`` select the tensor-parallel shard; ``group`` is the
+    ``torch.distributed`` process group used for the all-reduces (None for 1 GPU).
+    """
+
+    def __init__(self, config, *, batch, capacity, device="cuda", seed=0, rank=0, world=1, group=None):
+        cfg = config
+        self.cfg = cfg
+        self.batch = batch
+        self.capacity = ((capacity + 15) // 16) * 16
+        self.device = torch.device(device)
+        self.rank, self.world, self.group = rank, world, group
+        if cfg.num_kv_heads % world or cfg.num_heads % world or cfg.intermediate % (world * cfg.mlp_group):
+            raise ValueError("heads and intermediate size must divide across the tensor-parallel ranks")
+        if cfg.vocab % world:
+            raise ValueError("vocabulary must divide across the tensor-parallel ranks")
+        if batch < 1 or batch > 8:
+            raise ValueError("batch must be in [1, 8]")
+        self.hq = cfg.num_heads // world
+        self.hkv = cfg.num_kv_heads // world
+        self.inter = cfg.intermediate // world
+        self.vocab_shard = cfg.vocab // world
+        self._build_weights(seed)
+        self._alloc_state()
+        self.graph = None
+
+    # ------------------------------------------------------------------ weights
+    def _build_weights(self, seed):
+        cfg, dev = self.cfg, self.device
+        gen = torch.Generator(device=dev)
+        d = cfg.head_dim
+        r = self.rank
+
+        def randn(*shape, std, key):
+            gen.manual_seed(seed * 1_000_003 + key)
+            return torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32) * std
+
+        def rows(t, start, count):
+            return t[start:start + count]
+
+        self.layers = []
+        for li in range(cfg.num_layers):
+            base = 1000 * (li + 1)
+            layer = {}
+            # full matrices are generated identically on every rank, then sharded
+            wq = randn(cfg.num_heads * d, cfg.hidden, std=cfg.weight_std, key=base + 1)
+            wk = randn(cfg.num_kv_heads * d, cfg.hidden, std=cfg.weight_std, key=base + 2)
+            wv = randn(cfg.num_kv_heads * d, cfg.hidden, std=cfg.weight_std, key=base + 3)
+            qkv = torch.cat([rows(wq, r * self.hq * d, self.hq * d), rows(wk, r * self.hkv * d, self.hkv * d),
+                             rows(wv, r * self.hkv * d, self.hkv * d)])
+            del wq, wk, wv
+            layer["qkv_w"], layer["qkv_s"] = quantize.quantize_w8_per_channel(qkv)
+            del qkv
+            wo = randn(cfg.hidden, cfg.num_heads * d, std=cfg.weight_std, key=base + 4)
+            wo = wo[:, r * self.hq * d:(r + 1) * self.hq * d].contiguous()
+            layer["o_w"], layer["o_s"] = quantize.quantize_w8_per_channel(wo)
+            del wo
+            for name, key in (("gate", 5), ("up", 6)):
+                w = randn(cfg.intermediate, cfg.hidden, std=cfg.weight_std, key=base + key)
+                w = rows(w, r * self.inter, self.inter)
+                layer[name] = quantize.quantize_affine_minmax(w, cfg.mlp_group, 4)
+                del w
+            wd = randn(cfg.hidden, cfg.intermediate, std=cfg.weight_std, key=base + 7)
+            wd = wd[:, r * self.inter:(r + 1) * self.inter].contiguous()
+            layer["down"] = quantize.quantize_affine_minmax(wd, cfg.mlp_group, 4)
+            del wd
+            layer["in_norm"] = (1.0 + 0.1 * randn(cfg.hidden, std=1.0, key=base + 8)).to(torch.bfloat16)
+            layer["post_norm"] = (1.0 + 0.1 * randn(cfg.hidden, std=1.0, key=base + 9)).to(torch.bfloat16)
+            self.layers.append(layer)
+        self.embed = randn(cfg.vocab, cfg.hidden, std=cfg.embed_std, key=11).to(torch.bfloat16)
+        head = randn(cfg.vocab, cfg.hidden, std=cfg.head_std, key=12)
+        self.head = rows(head, r * self.vocab_shard, self.vocab_shard).to(torch.bfloat16).contiguous()
+        del head
+        self.final_norm = (1.0 + 0.1 * randn(cfg.hidden, std=1.0, key=13)).to(torch.bfloat16)
+        torch.cuda.synchronize(dev)
+
+    # -------------------------------------------------------------------- state
+    def _alloc_state(self):
+        cfg, dev, b = self.cfg, self.device, self.batch
+        d = cfg.head_dim
+        self.k_cache = [torch.zeros((b, self.hkv, self.capacity, d), dtype=torch.int8, device=dev)
+                        for _ in range(cfg.num_layers)]
+        self.v_cache = [torch.zeros_like(self.k_cache[0]) for _ in range(cfg.num_layers)]
+        self.k_scale = [torch.ones((b, self.hkv, self.capacity), dtype=torch.float16, device=dev)
+                        for _ in range(cfg.num_layers)]
+        self.v_scale = [torch.ones_like(self.k_scale[0]) for _ in range(cfg.num_layers)]
+        self.x = torch.zeros((b, cfg.hidden), dtype=torch.bfloat16, device=dev)
+        self.q = torch.zeros((b, self.hq, 1, d), dtype=torch.bfloat16, device=dev)
+        self.k_new = torch.zeros((b, self.hkv, 1, d), dtype=torch.bfloat16, device=dev)
+        self.v_new = torch.zeros_like(self.k_new)
+        self.attn = torch.zeros((b, self.hq * d), dtype=torch.bfloat16, device=dev)
+        self.act = torch.zeros((b, self.inter), dtype=torch.bfloat16, device=dev)
+        self.part = torch.zeros((b, cfg.hidden), dtype=torch.bfloat16, device=dev)
+        self.tokens = torch.zeros((b,), dtype=torch.int32, device=dev)
+        self.positions = torch.zeros((b,), dtype=torch.int32, device=dev)
+        self.keys = torch.zeros((b,), dtype=torch.int64, device=dev)
+        self._build_descs()
+        sizes = [lib().sb_linear_ex_workspace_size(ctypes.byref(desc)) for desc in self._descs_all()]
+        sizes.append(lib().sb_int8_sdpa_workspace_size(b, self.hq, self.hkv, self.capacity, d))
+        self.workspace = torch.zeros(max(sizes) + 256, dtype=torch.uint8, device=dev)
+        for desc in self._descs_all():
+            desc.workspace = self.workspace.data_ptr()
+            desc.workspace_bytes = self.workspace.numel()
+
+    def _desc(self, **kw):
+        desc = sb_linear_ex_desc()
+        desc.x_dtype = BF16
+        desc.norm_eps = self.cfg.rms_eps
+        desc.weights_constant = 1
+        for key, value in kw.items():
+            setattr(desc, key, value)
+        return desc
+
+    def _build_descs(self):
+        cfg, b = self.cfg, self.batch
+        d = cfg.head_dim
+        tp = self.world > 1
+        self.descs = []
+        for layer in self.layers:
+            qkv = self._desc(x=_ptr(self.x), M=b, N=(self.hq + 2 * self.hkv) * d, K=cfg.hidden,
+                             weight_format=SB_WEIGHT_INT8_PC, weight=_ptr(layer["qkv_w"]), scales=_ptr(layer["qkv_s"]),
+                             norm_weight=_ptr(layer["in_norm"]), epilogue=SB_EPI_ROPE,
+                             positions=_ptr(self.positions), num_heads=self.hq, num_kv_heads=self.hkv, head_dim=d,
+                             seq_len=1, rope_base=cfg.rope_theta, q_out=_ptr(self.q), k_out=_ptr(self.k_new),
+                             v_out=_ptr(self.v_new))
+            o = self._desc(x=_ptr(self.attn), M=b, N=cfg.hidden, K=self.hq * d, weight_format=SB_WEIGHT_INT8_PC,
+                           weight=_ptr(layer["o_w"]), scales=_ptr(layer["o_s"]),
+                           epilogue=SB_EPI_STORE if tp else SB_EPI_RESID,
+                           y=_ptr(self.part if tp else self.x), residual=_ptr(self.x))
+            gw, gs, gb = layer["gate"]
+            uw, us, ub = layer["up"]
+            gateup = self._desc(x=_ptr(self.x), M=b, N=self.inter, K=cfg.hidden, weight_format=SB_WEIGHT_AFFINE4,
+                                weight=_ptr(gw), scales=_ptr(gs), biases=_ptr(gb), weight2=_ptr(uw),
+                                scales2=_ptr(us), biases2=_ptr(ub), group_size=cfg.mlp_group,
+                                norm_weight=_ptr(layer["post_norm"]), epilogue=SB_EPI_SWIGLU, y=_ptr(self.act))
+            dw, ds, db = layer["down"]
+            down = self._desc(x=_ptr(self.act), M=b, N=cfg.hidden, K=self.inter, weight_format=SB_WEIGHT_AFFINE4,
+                              weight=_ptr(dw), scales=_ptr(ds), biases=_ptr(db), group_size=cfg.mlp_group,
+                              epilogue=SB_EPI_STORE if tp else SB_EPI_RESID,
+                              y=_ptr(self.part if tp else self.x), residual=_ptr(self.x))
+            self.descs.append((qkv, o, gateup, down))
+        self.head_desc = self._desc(x=_ptr(self.x), M=b, N=self.vocab_shard, K=cfg.hidden,
+                                    weight_format=SB_WEIGHT_BF16, weight=_ptr(self.head),
+                                    norm_weight=_ptr(self.final_norm), epilogue=SB_EPI_ARGMAX,
+                                    argmax_keys=_ptr(self.keys), argmax_offset=self.rank * self.vocab_shard)
+
+    def _descs_all(self):
+        out = [self.head_desc]
+        for group in self.descs:
+            out.extend(group)
+        return out
+
+    # ------------------------------------------------------------------- launch
+    def _allreduce(self, t, op=None):
+        import torch.distributed as dist
+
+        dist.all_reduce(t, op=op or dist.ReduceOp.SUM, group=self.group)
+
+    def step(self, *, lm_head=True, advance=True):
+        """Enqueue one decode step on the current stream (token in ``tokens``)."""
+        cfg, b = self.cfg, self.batch
+        L = lib()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        d = cfg.head_dim
+        tp = self.world > 1
+        check(L.sb_embed_rows(_ptr(self.embed), _ptr(self.tokens), _ptr(self.x), b, cfg.hidden, cfg.vocab, stream),
+              "embed")
+        scale = 1.0 / math.sqrt(d)
+        for li, (qkv, o, gateup, down) in enumerate(self.descs):
+            check(L.sb_linear_ex(ctypes.byref(qkv), stream), "qkv_rope")
+            check(L.sb_kv_append_int8(_ptr(self.k_new), _ptr(self.v_new), _ptr(self.k_cache[li]),
+                                      _ptr(self.k_scale[li]), _ptr(self.v_cache[li]), _ptr(self.v_scale[li]), b,
+                                      self.hkv, 1, d, self.capacity, _ptr(self.positions), stream), "kv_append")
+            check(L.sb_int8_sdpa_decode_dev(_ptr(self.q), _ptr(self.k_cache[li]), _ptr(self.k_scale[li]),
+                                            _ptr(self.v_cache[li]), _ptr(self.v_scale[li]), _ptr(self.attn), b,
+                                            self.hq, self.hkv, _ptr(self.positions), 1, self.capacity,
+                                            self.capacity, d, scale, self.workspace.data_ptr(),
+                                            self.workspace.numel(), stream), "int8_sdpa")
+            check(L.sb_linear_ex(ctypes.byref(o), stream), "o_proj")
+            if tp:
+                self._allreduce(self.part)
+                check(L.sb_residual_add(_ptr(self.x), _ptr(self.part), b * cfg.hidden, stream), "residual")
+            check(L.sb_linear_ex(ctypes.byref(gateup), stream), "gate_up")
+            check(L.sb_linear_ex(ctypes.byref(down), stream), "down")
+            if tp:
+                self._allreduce(self.part)
+                check(L.sb_residual_add(_ptr(self.x), _ptr(self.part), b * cfg.hidden, stream), "residual")
+        if lm_head:
+            check(L.sb_linear_ex(ctypes.byref(self.head_desc), stream), "lm_head")
+            if tp:
+                import torch.distributed as dist
+
+                self._allreduce(self.keys, dist.ReduceOp.MAX)
+        if advance:
+            check(L.sb_decode_advance(_ptr(self.keys), _ptr(self.tokens), _ptr(self.positions), b, 1, stream),
+                  "advance")
+
+    def kernels_per_step(self):
+        """Number of this library's kernel launches in one ``step()``."""
+        per_layer = 6 + (2 if self.world > 1 else 0)
+        return 1 + self.cfg.num_layers * per_layer + 2
+
+    # ------------------------------------------------------------------ drivers
+    def reset(self, first_tokens):
+        """Start a sequence: empty cache, position 0, first input tokens [batch]."""
+        self.positions.zero_()
+        self.keys.zero_()
+        self.tokens.copy_(torch.as_tensor(first_tokens, dtype=torch.int32, device=self.device).reshape(-1))
+
+    def prefill(self, prompt):
+        """Feed prompt[:, 0..P-1] token by token; leaves the greedy next token in ``tokens``.
+
+        ``prompt`` is an int32 device tensor [batch, P]. Runs decode steps (the
+        lm_head only on the last one); positions end at P.
+        """
+        prompt = prompt.to(device=self.device, dtype=torch.int32)
+        self.reset(prompt[:, 0])
+        for t in range(prompt.shape[1]):
+            last = t == prompt.shape[1] - 1
+            self.step(lm_head=last, advance=True)
+            if not last:
+                self.tokens.copy_(prompt[:, t + 1])
+        # positions[b] == P now; tokens holds the first generated token
+
+    def capture(self):
+        """Capture one decode step (lm_head, argmax and position advance included)."""
+        stream = torch.cuda.Stream(self.device)
+        stream.wait_stream(torch.cuda.current_stream(self.device))
+        graph = torch.cuda.CUDAGraph()
+        saved_pos = self.positions.clone()
+        saved_tok = self.tokens.clone()
+        with torch.cuda.stream(stream):
+            # warm up once outside the graph on the side stream (NCCL needs it), then restore state
+            self.step()
+            self.positions.copy_(saved_pos)
+            self.tokens.copy_(saved_tok)
+            self.keys.zero_()
+        torch.cuda.current_stream(self.device).wait_stream(stream)
+        torch.cuda.synchronize(self.device)
+        with torch.cuda.graph(graph, stream=stream):
+            self.step()
+        torch.cuda.synchronize(self.device)
+        self.graph = graph
+        return graph
+
+    def decode(self, steps):
+        """Replay the captured step ``steps`` times; returns generated tokens [batch, steps] (device)."""
+        if self.graph is None:
+            self.capture()
+        out = torch.empty((self.batch, steps), dtype=torch.int32, device=self.device)
+        for i in range(steps):
+            out[:, i] = self.tokens
+            self.graph.replay()
+        return out
