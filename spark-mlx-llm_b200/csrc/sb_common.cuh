@@ -29,7 +29,11 @@ inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(s
 // one call's partials from ever overlapping another call's counters when
 // different operators share one workspace.
 constexpr size_t kCounterBytes = 128 * 1024;
-constexpr int kMaxCounters = static_cast<int>(kCounterBytes / sizeof(unsigned));
+// The last 16 words of the counter region are reserved: word kStatusWord holds
+// a device-side status (nonzero when a bounded wait gave up).
+constexpr int kMaxCounters = static_cast<int>(kCounterBytes / sizeof(unsigned)) - 16;
+constexpr int kStatusWord = static_cast<int>(kCounterBytes / sizeof(unsigned)) - 1;
+constexpr unsigned kStatusTimeout = 1u;
 
 // Launch helper: every kernel is launched with programmatic stream
 // serialization allowed, so a dependent kernel may start its weight prefetch
@@ -64,6 +68,54 @@ __device__ __forceinline__ void grid_dependency_wait() {
 // Allow the next kernel in the stream to begin launching.
 __device__ __forceinline__ void grid_dependency_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ------------------------------------------------ mbarrier + bulk async copy
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+// Waits for the phase with parity `phase`; gives up after ~2^31 clock cycles
+// (about a second) and returns false instead of hanging.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, phase)) {
+    if (clock64() - start > (1LL << 31)) return false;
+  }
+  return true;
+}
+// Order earlier generic-proxy accesses of shared memory before later async-proxy ones.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 1-D bulk copy global -> shared, completing `bytes` on the mbarrier (16-B aligned, size % 16 == 0).
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
 }
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {

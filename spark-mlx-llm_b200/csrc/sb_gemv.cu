@@ -158,9 +158,21 @@ __device__ __forceinline__ int map_row(const GemvParams& p, int tile, int r16, i
   }
 }
 
+// Smem words of one stage row (bytes) and row pitch chosen so the lanes' 8-byte
+// (4-bit) or 16-byte (8-bit, bf16) reads of 8 rows hit distinct banks.
+template <int kBits>
+struct StageGeom {
+  static constexpr int kRowBytes = 128;                       // bytes of one weight row per stage
+  static constexpr int kStageK = kRowBytes * 8 / kBits;       // K values per stage
+  static constexpr int kPitch = kBits == 4 ? 160 : 192;       // smem row pitch
+  static constexpr int kStages = kBits == 4 ? 4 : 3;          // ring depth per warp
+  static constexpr int kStageBytes = 32 * kPitch;             // 32 weight rows per warp
+};
+
 template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
-__global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
   using F = Fmt<TA, WF>;
+  using SG = StageGeom<F::kBits>;
   constexpr int V = KC / 4;                      // values per lane per row per chunk
   constexpr int kPairs = V / 2;                  // MMA operand pairs per row per chunk
   constexpr int kMma = KC / 16;                  // k16 steps per chunk
@@ -169,8 +181,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_kernel(const __grid_c
   constexpr int kRows = 2 * kGemvTiles;          // weight rows held per lane
   constexpr bool kAffine = (WF == W_AFF4 || WF == W_AFF8);
   constexpr int kGroupK = kAffine ? KC * GC : KC;  // K covered by one split unit
+  constexpr int kChunkRowBytes = KC * F::kBits / 8;
+  constexpr int kChunksPerStage = SG::kStageK / KC;
+  constexpr int kGroupsPerStage = kAffine ? kChunksPerStage / GC : 0;
+  static_assert(!kAffine || kChunksPerStage % GC == 0, "a stage holds whole groups");
 
-  extern __shared__ __align__(16) uint8_t smem_raw[];
+  extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ float s_rms[8];
   __shared__ float s_part[kGemvWarps][8];
 
@@ -191,43 +207,62 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_kernel(const __grid_c
   const int grp_end = static_cast<int>((static_cast<long long>(p.groups_total) * (split + 1)) / p.splits);
   const int k_begin = grp_begin * kGroupK;
   const int k_count = (grp_end - grp_begin) * kGroupK;
-  const int chunk_begin = k_begin / KC;
-  const int chunk_end = chunk_begin + k_count / KC;
+  const int nstages = (k_count + SG::kStageK - 1) / SG::kStageK;
 
-  // ---- per-lane row pointers (weights for all 4 rows; scale/bias for row t)
-  const uint8_t* wrow[kRows];
-  int my_set = 0, my_row = 0;
-#pragma unroll
-  for (int q = 0; q < kRows; ++q) {
-    const int tile = min(rb, rowblocks - 1) * kGemvTiles + (q >> 1);
+  // ---- shared memory carve-up: barriers, per-warp weight rings, x segment
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw) + warp * SG::kStages;
+  uint8_t* ring = smem_raw + 128 + (warp * SG::kStages) * SG::kStageBytes;
+  TA* xs = reinterpret_cast<TA*>(smem_raw + 128 + kGemvWarps * SG::kStages * SG::kStageBytes);
+  const int mcols = p.M;
+  const int xs_ld = p.x_seg + 8;
+
+  // ---- row owned by this lane for the bulk copies, and the row whose scale/bias it loads
+  const size_t row_bytes = static_cast<size_t>(p.K) * F::kBits / 8;
+  const uint8_t* copy_src;
+  {
     int set;
     bool valid;
-    const int row = map_row<EPI>(p, min(tile, tiles - 1), (q & 1) * 8 + g, set, valid);
-    const uint8_t* base = static_cast<const uint8_t*>(set ? p.w1 : p.w0);
-    const size_t row_bytes = static_cast<size_t>(p.K) * F::kBits / 8;
-    wrow[q] = base + row * row_bytes + static_cast<size_t>(t) * V * F::kBits / 8;
-    if (q == t) {
-      my_set = set;
-      my_row = row;
-    }
+    const int tile = min(min(rb, rowblocks - 1) * kGemvTiles + (lane >> 4), tiles - 1);
+    const int row = map_row<EPI>(p, tile, lane & 15, set, valid);
+    copy_src = static_cast<const uint8_t*>(set ? p.w1 : p.w0) + row * row_bytes +
+               static_cast<size_t>(k_begin) * F::kBits / 8;
+  }
+  int my_set = 0, my_row = 0;
+  {
+    bool valid;
+    const int tile = min(min(rb, rowblocks - 1) * kGemvTiles + (t >> 1), tiles - 1);
+    my_row = map_row<EPI>(p, tile, (t & 1) * 8 + g, my_set, valid);
   }
 
-  // ---- prefetch the first chunk of weights; with constant weights this may
-  // overlap the tail of the previous kernel in the stream
+  auto stage_row_bytes = [&](int st) -> uint32_t {
+    const int kk = min(SG::kStageK, k_count - st * SG::kStageK);
+    return static_cast<uint32_t>(kk * F::kBits / 8);
+  };
+  auto issue_stage = [&](int st) {
+    const int slot = st % SG::kStages;
+    const uint32_t bytes = stage_row_bytes(st);
+    if (lane == 0) mbar_arrive_expect_tx(bars + slot, bytes * 32);
+    __syncwarp();
+    bulk_copy_g2s(ring + slot * SG::kStageBytes + lane * SG::kPitch,
+                  copy_src + static_cast<size_t>(st) * SG::kRowBytes, bytes, bars + slot);
+  };
+
+  if (active) {
+    if (lane < SG::kStages) mbar_init(bars + lane, 1);
+    mbar_fence_init();
+    __syncwarp();
+  }
+  // ---- start streaming weights; with constant weights this may overlap the
+  // tail of the previous kernel in the stream
   if (!p.early_prefetch) grid_dependency_wait();
-  uint32_t wbuf[kRows][kWords];
-  if (active && chunk_begin < chunk_end) {
+  if (active) {
 #pragma unroll
-    for (int q = 0; q < kRows; ++q)
-      load_words<kWords>(wrow[q] + static_cast<size_t>(chunk_begin) * KC * F::kBits / 8, wbuf[q]);
+    for (int st = 0; st < SG::kStages; ++st)
+      if (st < nstages) issue_stage(st);
   }
 
   // ---- activations depend on the previous kernel from here on
   grid_dependency_wait();
-
-  TA* xs = reinterpret_cast<TA*>(smem_raw);
-  const int xs_ld = k_count + 8;
-  const int mcols = p.M;
   if constexpr (NORM) {
     // full-row sum of squares per column (fixed reduction order)
     for (int m = 0; m < mcols; ++m) {
@@ -261,33 +296,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_kernel(const __grid_c
       for (int w = 0; w < kGemvWarps; ++w) ss += s_part[w][threadIdx.x];
       s_rms[threadIdx.x] = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
     }
-    __syncthreads();
   }
-  // stage x[:, k_begin : k_begin + k_count] (optionally normalized) into smem
-  {
-    const int vecs = k_count / 8;
-    for (int idx = threadIdx.x; idx < mcols * vecs; idx += kGemvWarps * 32) {
-      const int m = idx / vecs, v8 = idx % vecs;
-      const TA* src = static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + k_begin + v8 * 8;
-      uint4 v = *reinterpret_cast<const uint4*>(src);
-      if constexpr (NORM) {
-        const uint4 wv = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + k_begin + v8 * 8);
-        const TA* xv = reinterpret_cast<const TA*>(&v);
-        const TA* nv = reinterpret_cast<const TA*>(&wv);
-        TA out[8];
-        const float r = s_rms[m];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) out[i] = from_float<TA>(to_float(xv[i]) * r * to_float(nv[i]));
-        v = *reinterpret_cast<const uint4*>(out);
-      }
-      *reinterpret_cast<uint4*>(xs + m * xs_ld + v8 * 8) = v;
-    }
-  }
-  __syncthreads();
-  if (!active) return;
 
-  // ---- main loop
-  const TA* xcol = xs + min(g, mcols - 1) * xs_ld + t * V;
   constexpr uint32_t kOnes = ActTraits<TA>::kOnes;
   float acc[kGemvTiles][4];
   float cacc[kGemvTiles][F::kPlanes][4];
@@ -303,87 +313,182 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 4) gemv_kernel(const __grid_c
 #pragma unroll
   for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
 
-  const __nv_bfloat16* srow = nullptr;
-  const __nv_bfloat16* brow = nullptr;
-  if constexpr (kAffine) {
-    const int gpr = p.K / p.group_size;
-    srow = static_cast<const __nv_bfloat16*>(my_set ? p.s1 : p.s0) + static_cast<size_t>(my_row) * gpr;
-    brow = static_cast<const __nv_bfloat16*>(my_set ? p.b1 : p.b0) + static_cast<size_t>(my_row) * gpr;
-  }
-
-  for (int c = chunk_begin; c < chunk_end; ++c) {
-    // dequantize the current chunk, then issue the next chunk's loads
-    uint32_t lo[kRows][kPairs], hi[kRows][kPairs];
+  // scale/bias of this lane's row (q == t), one stage ahead in registers
+  const TA* srow = nullptr;
+  const TA* brow = nullptr;
+  uint32_t sb_cur[kGroupsPerStage > 0 ? kGroupsPerStage : 1];
+  uint32_t sb_nxt[kGroupsPerStage > 0 ? kGroupsPerStage : 1];
+  auto load_sb = [&](int st, uint32_t* dst) {
+    if constexpr (kAffine) {
+      const int g0 = (k_begin + st * SG::kStageK) / p.group_size;
+      const int gn = (min(SG::kStageK, k_count - st * SG::kStageK)) / p.group_size;
 #pragma unroll
-    for (int q = 0; q < kRows; ++q) dequant_pairs<TA, WF, kWords, kPairs>(wbuf[q], lo[q], hi[q]);
-    if (c + 1 < chunk_end) {
-#pragma unroll
-      for (int q = 0; q < kRows; ++q)
-        load_words<kWords>(wrow[q] + static_cast<size_t>(c + 1) * KC * F::kBits / 8, wbuf[q]);
-    }
-    uint32_t xw[kXWords];
-    const TA* xp_base = xcol + (c - chunk_begin) * KC;
-#pragma unroll
-    for (int i = 0; i < kXWords; i += 4) {
-      const uint4 v = *reinterpret_cast<const uint4*>(xp_base + 2 * i);
-      xw[i] = v.x;
-      xw[i + 1] = v.y;
-      xw[i + 2] = v.z;
-      xw[i + 3] = v.w;
-    }
-    uint32_t xpair[kPairs];
-    x_pairs<WF, kXWords, kPairs>(xw, xpair);
-
-#pragma unroll
-    for (int j = 0; j < kMma; ++j) {
-      const uint32_t b0 = xpair[2 * j], b1 = xpair[2 * j + 1];
-#pragma unroll
-      for (int r = 0; r < kGemvTiles; ++r) {
-        const uint32_t a_lo[4] = {lo[2 * r][2 * j], lo[2 * r + 1][2 * j], lo[2 * r][2 * j + 1],
-                                  lo[2 * r + 1][2 * j + 1]};
-        mma_16816<F::kHalf>(cacc[r][0], a_lo, b0, b1);
-        if constexpr (F::kPlanes == 2) {
-          const uint32_t a_hi[4] = {hi[2 * r][2 * j], hi[2 * r + 1][2 * j], hi[2 * r][2 * j + 1],
-                                    hi[2 * r + 1][2 * j + 1]};
-          mma_16816<F::kHalf>(cacc[r][1], a_hi, b0, b1);
+      for (int i = 0; i < kGroupsPerStage; ++i) {
+        if (i < gn) {
+          const uint16_t s = *reinterpret_cast<const uint16_t*>(srow + g0 + i);
+          const uint16_t b = *reinterpret_cast<const uint16_t*>(brow + g0 + i);
+          dst[i] = static_cast<uint32_t>(s) | (static_cast<uint32_t>(b) << 16);
         }
       }
-      if constexpr (WF != W_BF16) {
-        const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
-        mma_16816<F::kHalf>(xsum, ones, b0, b1);
-      }
     }
+  };
+  if constexpr (kAffine) {
+    const int gpr = p.K / p.group_size;
+    srow = static_cast<const TA*>(my_set ? p.s1 : p.s0) + static_cast<size_t>(my_row) * gpr;
+    brow = static_cast<const TA*>(my_set ? p.b1 : p.b0) + static_cast<size_t>(my_row) * gpr;
+    if (active && nstages > 0) load_sb(0, sb_cur);
+  }
+
+  bool failed = false;
+  for (int st = 0; st < nstages; ++st) {
+    // ---- activation segment staging (all warps of the CTA take part)
+    const int kst = st * SG::kStageK;  // offset inside the split
+    if (kst % p.x_seg == 0) {
+      __syncthreads();
+      const int seg_len = min(p.x_seg, k_count - kst);
+      const int vecs = seg_len / 8;
+      for (int idx = threadIdx.x; idx < mcols * vecs; idx += kGemvWarps * 32) {
+        const int m = idx / vecs, v8 = idx % vecs;
+        const int kg = k_begin + kst + v8 * 8;
+        uint4 v = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + kg);
+        if constexpr (NORM) {
+          const uint4 wv = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + kg);
+          const TA* xv = reinterpret_cast<const TA*>(&v);
+          const TA* nv = reinterpret_cast<const TA*>(&wv);
+          TA out[8];
+          const float r = s_rms[m];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) out[i] = from_float<TA>(to_float(xv[i]) * r * to_float(nv[i]));
+          v = *reinterpret_cast<const uint4*>(out);
+        }
+        *reinterpret_cast<uint4*>(xs + m * xs_ld + v8 * 8) = v;
+      }
+      __syncthreads();
+    }
+    if (!active || failed) continue;
 
     if constexpr (kAffine) {
-      if ((c + 1) % GC == 0) {
-        // group epilogue: acc += scale * sum(code*x) + bias * sum(x)
-        const int grp = c / GC;
-        const uint32_t sb = static_cast<uint32_t>(__bfloat16_as_ushort(srow[grp])) |
-                            (static_cast<uint32_t>(__bfloat16_as_ushort(brow[grp])) << 16);
+      if (st + 1 < nstages) load_sb(st + 1, sb_nxt);
+    }
+    const int slot = st % SG::kStages;
+    if (!mbar_wait_bounded(bars + slot, (st / SG::kStages) & 1)) {
+      failed = true;
+      continue;
+    }
+    const uint8_t* stage = ring + slot * SG::kStageBytes;
+    const int chunks = min(kChunksPerStage, (k_count - kst) / KC);
+    const TA* xbase = xs + min(g, mcols - 1) * xs_ld + (kst % p.x_seg) + t * V;
 #pragma unroll
-        for (int r = 0; r < kGemvTiles; ++r) {
+    for (int cc = 0; cc < kChunksPerStage; ++cc) {
+      if (cc < chunks) {
+        uint32_t wv[kRows][kWords];
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const uint32_t v = __shfl_sync(0xffffffffu, sb, (lane & ~3) | (2 * r + h));
-            const float s = bf16_lo(v);
-            const float b = bf16_hi(v);
-            const float bb = fmaf(-F::kCodeOffset, s, b);
+        for (int q = 0; q < kRows; ++q) {
+          const uint8_t* src = stage + ((q >> 1) * 16 + (q & 1) * 8 + g) * SG::kPitch + cc * kChunkRowBytes +
+                               t * (V * F::kBits / 8);
+          if constexpr (kWords == 1) {
+            wv[q][0] = *reinterpret_cast<const uint32_t*>(src);
+          } else if constexpr (kWords == 2) {
+            const uint2 v = *reinterpret_cast<const uint2*>(src);
+            wv[q][0] = v.x;
+            wv[q][1] = v.y;
+          } else {
 #pragma unroll
-            for (int e = 0; e < 2; ++e) {
-              float d = cacc[r][0][2 * h + e];
-              if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][2 * h + e], d);
-              acc[r][2 * h + e] = fmaf(s, d, fmaf(bb, xsum[e], acc[r][2 * h + e]));
-              cacc[r][0][2 * h + e] = 0.f;
-              if constexpr (F::kPlanes == 2) cacc[r][1][2 * h + e] = 0.f;
+            for (int i = 0; i < kWords; i += 4) {
+              const uint4 v = *reinterpret_cast<const uint4*>(src + 4 * i);
+              wv[q][i] = v.x;
+              wv[q][i + 1] = v.y;
+              wv[q][i + 2] = v.z;
+              wv[q][i + 3] = v.w;
             }
           }
         }
+        uint32_t lo[kRows][kPairs], hi[kRows][kPairs];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
+        for (int q = 0; q < kRows; ++q) dequant_pairs<TA, WF, kWords, kPairs>(wv[q], lo[q], hi[q]);
+        uint32_t xw[kXWords];
+#pragma unroll
+        for (int i = 0; i < kXWords; i += 4) {
+          const uint4 v = *reinterpret_cast<const uint4*>(xbase + cc * KC + 2 * i);
+          xw[i] = v.x;
+          xw[i + 1] = v.y;
+          xw[i + 2] = v.z;
+          xw[i + 3] = v.w;
+        }
+        uint32_t xpair[kPairs];
+        x_pairs<WF, kXWords, kPairs>(xw, xpair);
+#pragma unroll
+        for (int j = 0; j < kMma; ++j) {
+          const uint32_t b0 = xpair[2 * j], b1 = xpair[2 * j + 1];
+#pragma unroll
+          for (int r = 0; r < kGemvTiles; ++r) {
+            const uint32_t a_lo[4] = {lo[2 * r][2 * j], lo[2 * r + 1][2 * j], lo[2 * r][2 * j + 1],
+                                      lo[2 * r + 1][2 * j + 1]};
+            mma_16816<F::kHalf>(cacc[r][0], a_lo, b0, b1);
+            if constexpr (F::kPlanes == 2) {
+              const uint32_t a_hi[4] = {hi[2 * r][2 * j], hi[2 * r + 1][2 * j], hi[2 * r][2 * j + 1],
+                                        hi[2 * r + 1][2 * j + 1]};
+              mma_16816<F::kHalf>(cacc[r][1], a_hi, b0, b1);
+            }
+          }
+          if constexpr (WF != W_BF16) {
+            const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+            mma_16816<F::kHalf>(xsum, ones, b0, b1);
+          }
+        }
+        if constexpr (kAffine) {
+          if ((cc + 1) % GC == 0) {
+            // group epilogue: acc += scale * sum(code*x) + bias * sum(x)
+            const uint32_t sbv = sb_cur[cc / GC];
+#pragma unroll
+            for (int r = 0; r < kGemvTiles; ++r) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint32_t v = __shfl_sync(0xffffffffu, sbv, (lane & ~3) | (2 * r + h));
+                float s, b;
+                if constexpr (ActTraits<TA>::kHalf) {
+                  s = __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
+                  b = __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
+                } else {
+                  s = bf16_lo(v);
+                  b = bf16_hi(v);
+                }
+                const float bb = fmaf(-F::kCodeOffset, s, b);
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                  float d = cacc[r][0][2 * h + e];
+                  if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][2 * h + e], d);
+                  acc[r][2 * h + e] = fmaf(s, d, fmaf(bb, xsum[e], acc[r][2 * h + e]));
+                  cacc[r][0][2 * h + e] = 0.f;
+                  if constexpr (F::kPlanes == 2) cacc[r][1][2 * h + e] = 0.f;
+                }
+              }
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
+          }
+        }
       }
     }
+    if constexpr (kAffine) {
+#pragma unroll
+      for (int i = 0; i < kGroupsPerStage; ++i) sb_cur[i] = sb_nxt[i];
+    }
+    // refill this slot with the stage kStages ahead
+    if (st + SG::kStages < nstages) {
+      __syncwarp();
+      fence_proxy_async_smem();
+      issue_stage(st + SG::kStages);
+    }
   }
-
+  if (!active) return;
+  if (failed) {
+    // a bulk copy never completed: report, drain what is still in flight, stop
+    if (p.status && lane == 0) atomicOr(p.status, kStatusTimeout);
+    for (int st = max(0, nstages - SG::kStages); st < nstages; ++st)
+      mbar_wait_bounded(bars + st % SG::kStages, (st / SG::kStages) & 1);
+    return;
+  }
   if constexpr (WF == W_I8PC) {
     // signed value = unsigned code - 128:  sum(s8*x) = C - (offset + 128) * sum(x)
 #pragma unroll
@@ -596,16 +701,14 @@ Plan make_plan(int epi, int N, int K, int group_k, bool allow_split) {
   pl.rowblocks = (pl.tiles + kGemvTiles - 1) / kGemvTiles;
   pl.k_group = group_k;
   pl.groups = K / group_k;
-  // Enough warps to cover the SMs ~12 warps deep; keep >= 2 groups per split
-  // and at most 4096 staged activation values per split.
-  const int target = sm_count() * 12;
+  // Two CTAs of 4 warps per SM; split K only when the row blocks alone cannot
+  // fill that, keeping at least 2 groups per split.
+  const int target = sm_count() * 8;
   int s = allow_split ? (target + pl.rowblocks - 1) / pl.rowblocks : 1;
   s = std::min(s, std::max(1, pl.groups / 2));
-  const int min_s = (K + 4095) / 4096;
-  s = std::max(s, min_s);
   s = std::min(s, pl.groups);
+  if (pl.rowblocks > kMaxCounters) s = 1;
   pl.splits = std::max(1, s);
-  if (pl.rowblocks > kMaxCounters) pl.splits = 1;
   pl.counter_bytes = kCounterBytes;
   pl.partial_bytes = pl.splits > 1
                          ? static_cast<size_t>(pl.splits) * pl.rowblocks * 16 * kGemvTiles * 8 * sizeof(float)
@@ -615,14 +718,18 @@ Plan make_plan(int epi, int N, int K, int group_k, bool allow_split) {
 
 template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
 int launch_gemv(GemvParams& p, const Plan& pl, cudaStream_t stream) {
+  using SG = StageGeom<Fmt<TA, WF>::kBits>;
   const int max_kunit = (pl.groups + pl.splits - 1) / pl.splits * pl.k_group;
-  const size_t smem = static_cast<size_t>(p.M) * (max_kunit + 8) * sizeof(TA);
+  // activation segment: at most 32 KB of shared memory, whole stages
+  int seg = (32768 / (p.M * static_cast<int>(sizeof(TA)))) / SG::kStageK * SG::kStageK;
+  seg = std::max(seg, SG::kStageK);
+  p.x_seg = std::min(seg, ((max_kunit + SG::kStageK - 1) / SG::kStageK) * SG::kStageK);
+  const size_t smem = 128 + static_cast<size_t>(kGemvWarps) * SG::kStages * SG::kStageBytes +
+                      static_cast<size_t>(p.M) * (p.x_seg + 8) * sizeof(TA);
   auto kernel = gemv_kernel<TA, WF, KC, GC, EPI, NORM>;
-  if (smem > 48 * 1024) {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-        cudaSuccess)
-      return fail(SB_ECUDA, "gemv: shared memory opt-in failed");
-  }
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+      cudaSuccess)
+    return fail(SB_ECUDA, "gemv: shared memory opt-in failed");
   dim3 grid((pl.rowblocks + kGemvWarps - 1) / kGemvWarps, pl.splits);
   return launch("gemv", kernel, grid, dim3(kGemvWarps * 32), smem, stream, p);
 }
@@ -687,7 +794,10 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   SB_REQUIRE(r.K % gk == 0, "K must be a multiple of the group size (64 for per-channel/bf16 weights)");
   SB_REQUIRE(r.ldx % 8 == 0 && (reinterpret_cast<uintptr_t>(r.x) & 15) == 0,
              "activations must be 16-byte aligned with a row stride that is a multiple of 8");
-  SB_REQUIRE((reinterpret_cast<uintptr_t>(r.w0) & 15) == 0, "weights must be 16-byte aligned");
+  SB_REQUIRE((reinterpret_cast<uintptr_t>(r.w0) & 15) == 0 && (r.w1 == nullptr || (reinterpret_cast<uintptr_t>(r.w1) & 15) == 0),
+             "weights must be 16-byte aligned");
+  SB_REQUIRE((static_cast<int64_t>(r.K) * (r.wf == W_AFF4 ? 4 : (r.wf == W_BF16 ? 16 : 8)) / 8) % 16 == 0,
+             "weight rows must be a multiple of 16 bytes");
   if (r.epi == EPI_ROPE) {
     SB_REQUIRE(r.head_dim % 16 == 0 && r.head_dim / 2 <= kMaxRopeHalf, "head_dim must be a multiple of 16, <= 256");
     SB_REQUIRE(r.rope_dims == r.head_dim, "the fused RoPE epilogue rotates the full head_dim");
@@ -700,7 +810,6 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   if (pl.splits > 1 && (r.workspace == nullptr || r.workspace_bytes < need)) {
     // Fall back to no split when the caller gave no workspace.
     pl = make_plan(r.epi, r.N, r.K, gk, false);
-    SB_REQUIRE(pl.splits == 1, "workspace too small for this shape (query sb_*_workspace_size)");
   }
 
   GemvParams p{};
@@ -723,6 +832,8 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
     p.counters = static_cast<unsigned*>(r.workspace);
     p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(r.workspace) + pl.counter_bytes);
   }
+  if (r.workspace != nullptr && r.workspace_bytes >= kCounterBytes)
+    p.status = static_cast<unsigned*>(r.workspace) + kStatusWord;
   p.norm_w = r.norm_w;
   p.eps = r.eps;
   p.y = r.y;

@@ -80,7 +80,8 @@ struct GemvParams {
   // argmax epilogue
   unsigned long long* argmax_keys;  // [M]
   int argmax_offset;                // added to row indices (vocab-parallel shards)
-  int x_stage_max;                  // max K values staged per split (smem)
+  int x_seg;                        // K values of x staged in shared memory at a time
+  unsigned* status;                 // device status word (bounded-wait timeouts) or null
   // 1: the weights are constant across the stream (model weights), so the
   // kernel may start streaming them before the previous kernel finishes.
   int early_prefetch;

@@ -31,6 +31,10 @@ namespace sb {
 constexpr int kSdpaWarps = 4;
 constexpr int kSdpaD = 128;
 constexpr int kPartStride = kSdpaD + 4;  // O[D], then m, l
+constexpr int kSdpaStages = 4;           // 16-token blocks in flight per warp
+constexpr int kSdpaPitch = 144;          // smem row pitch (bank-conflict-free reads)
+constexpr int kSdpaStageBytes = 2 * 16 * kSdpaPitch;
+constexpr size_t kSdpaSmem = 128 + static_cast<size_t>(kSdpaWarps) * kSdpaStages * kSdpaStageBytes;
 
 struct SdpaParams {
   const __nv_bfloat16* q;  // [B, H, D]
@@ -45,6 +49,7 @@ struct SdpaParams {
   float scale_log2e;
   float* partial;      // [B*KH][splits][G][kPartStride]
   unsigned* counters;  // [B*KH]
+  unsigned* status;    // device status word or null
 };
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
@@ -124,40 +129,73 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
     for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
   constexpr uint32_t kOnes = 0x3C003C00u;
 
-  for (int blk = blk_begin + warp; blk < blk_end; blk += kSdpaWarps) {
-    const int tb = blk * 16;
-    // K rows for QK n-tiles u = 0, 1 (token tb + 8u + g), bytes 32t..32t+31
-    uint32_t kw[2][8];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      const int tok = min(tb + 8 * u + g, N - 1);
-      const int8_t* kp = kbase + static_cast<size_t>(tok) * kSdpaD + 32 * t;
-      const uint4 a = ldg_stream16(kp), c = ldg_stream16(kp + 16);
-      kw[u][0] = a.x; kw[u][1] = a.y; kw[u][2] = a.z; kw[u][3] = a.w;
-      kw[u][4] = c.x; kw[u][5] = c.y; kw[u][6] = c.z; kw[u][7] = c.w;
+  // ---- per-warp ring of 16-token K/V blocks in shared memory (bulk copies)
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw) + warp * kSdpaStages;
+  uint8_t* ring = smem_raw + 128 + warp * kSdpaStages * kSdpaStageBytes;
+  const int nb = blk_end - blk_begin;
+  const int my_blocks = nb > warp ? (nb - warp + kSdpaWarps - 1) / kSdpaWarps : 0;
+  auto block_of = [&](int i) { return blk_begin + warp + i * kSdpaWarps; };
+  auto issue = [&](int i) {
+    const int slot = i % kSdpaStages;
+    const int tb = block_of(i) * 16;
+    const int rows = min(16, N - tb);
+    if (lane == 0) mbar_arrive_expect_tx(bars + slot, static_cast<uint32_t>(rows) * 2 * kSdpaD);
+    __syncwarp();
+    const int r = lane & 15;
+    if (r < rows) {
+      const int8_t* src = (lane < 16 ? kbase : vbase) + static_cast<size_t>(tb + r) * kSdpaD;
+      uint8_t* dst = ring + slot * kSdpaStageBytes + (lane < 16 ? 0 : 16 * kSdpaPitch) + r * kSdpaPitch;
+      bulk_copy_g2s(dst, src, kSdpaD, bars + slot);
     }
-    // V rows for tokens tb + {2t, 2t+1, 2t+8, 2t+9}, bytes 16g..16g+15
-    uint4 vr[4];
-    int vt[4] = {tb + 2 * t, tb + 2 * t + 1, tb + 2 * t + 8, tb + 2 * t + 9};
+  };
+  if (lane < kSdpaStages) mbar_init(bars + lane, 1);
+  mbar_fence_init();
+  __syncwarp();
 #pragma unroll
-    for (int i = 0; i < 4; ++i) vr[i] = ldg_stream16(vbase + static_cast<size_t>(min(vt[i], N - 1)) * kSdpaD + 16 * g);
-    float sk[4], sv[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int tok = min(vt[i], N - 1);  // the same 4 tokens own this lane's scores
-      sk[i] = __half2float(ksb[tok]);
-      sv[i] = __half2float(vsb[tok]);
-    }
+  for (int i = 0; i < kSdpaStages; ++i)
+    if (i < my_blocks) issue(i);
 
-    // QK^T: C[u] rows = heads, cols = tokens 8u + (2t, 2t+1)
+  // scales of this lane's 4 tokens, one block ahead
+  float sk[4], sv[4], skn[4], svn[4];
+  auto load_scales = [&](int i, float* k4, float* v4) {
+    const int tb = block_of(i) * 16;
+    const int vt[4] = {tb + 2 * t, tb + 2 * t + 1, tb + 2 * t + 8, tb + 2 * t + 9};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int tok = min(vt[j], N - 1);
+      k4[j] = __half2float(ksb[tok]);
+      v4[j] = __half2float(vsb[tok]);
+    }
+  };
+  if (my_blocks > 0) load_scales(0, sk, sv);
+  bool failed = false;
+
+  for (int i = 0; i < my_blocks; ++i) {
+    const int tb = block_of(i) * 16;
+    if (i + 1 < my_blocks) load_scales(i + 1, skn, svn);
+    const int slot = i % kSdpaStages;
+    if (!mbar_wait_bounded(bars + slot, (i / kSdpaStages) & 1)) {
+      failed = true;
+      break;
+    }
+    const uint8_t* kst = ring + slot * kSdpaStageBytes;
+    const uint8_t* vst = kst + 16 * kSdpaPitch;
+    const int vt[4] = {tb + 2 * t, tb + 2 * t + 1, tb + 2 * t + 8, tb + 2 * t + 9};
+
+    // QK^T: C[u] rows = heads, cols = tokens 8u + (2t, 2t+1); K row (8u + g), bytes 32t..32t+31
     float cqk[2][4];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
+      const uint8_t* kp = kst + (8 * u + g) * kSdpaPitch + 32 * t;
+      const uint4 ka = *reinterpret_cast<const uint4*>(kp);
+      const uint4 kb = *reinterpret_cast<const uint4*>(kp + 16);
+      const uint32_t kw[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) cqk[u][e] = 0.f;
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
-        const uint32_t w = kw[u][s] ^ 0x80808080u;
+        const uint32_t w = kw[s] ^ 0x80808080u;
         const uint32_t b0 = prmt(w, 0x64646464u, 0x4140u);
         const uint32_t b1 = prmt(w, 0x64646464u, 0x4342u);
         const uint32_t a[4] = {aq[s], 0u, aq2[s], 0u};
@@ -171,8 +209,8 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
     sc[2] = (cqk[1][0] - qoff) * fscale * sk[2];
     sc[3] = (cqk[1][1] - qoff) * fscale * sk[3];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      if (vt[i] >= N) sc[i] = -INFINITY;
+    for (int j = 0; j < 4; ++j)
+      if (vt[j] >= N) sc[j] = -INFINITY;
     float mb = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
     mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
     mb = fmaxf(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
@@ -180,7 +218,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
     const float alpha = (m_run == -INFINITY) ? 0.f : exp2f(m_run - m_new);
     float pr[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) pr[i] = (vt[i] < N) ? exp2f(sc[i] - m_new) : 0.f;
+    for (int j = 0; j < 4; ++j) pr[j] = (vt[j] < N) ? exp2f(sc[j] - m_new) : 0.f;
     l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
     m_run = m_new;
 #pragma unroll
@@ -196,11 +234,13 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
     ap[2] = head_ok ? pack_half2(pr[2] * sv[2], pr[3] * sv[3]) : 0u;
     ap[3] = 0u;
     mma_16816<true>(psum, ap, kOnes, kOnes);
-    // P'V: n-tile j covers d = 16n + j; lane's B column n = g -> bytes j of its V segments
-    const uint32_t* va = reinterpret_cast<const uint32_t*>(&vr[0]);
-    const uint32_t* vb = reinterpret_cast<const uint32_t*>(&vr[1]);
-    const uint32_t* vc = reinterpret_cast<const uint32_t*>(&vr[2]);
-    const uint32_t* vd = reinterpret_cast<const uint32_t*>(&vr[3]);
+    // P'V: n-tile j covers d = 16n + j; the lane's B column n = g reads bytes 16g..16g+15
+    const uint4 vr0 = *reinterpret_cast<const uint4*>(vst + (2 * t) * kSdpaPitch + 16 * g);
+    const uint4 vr1 = *reinterpret_cast<const uint4*>(vst + (2 * t + 1) * kSdpaPitch + 16 * g);
+    const uint4 vr2 = *reinterpret_cast<const uint4*>(vst + (2 * t + 8) * kSdpaPitch + 16 * g);
+    const uint4 vr3 = *reinterpret_cast<const uint4*>(vst + (2 * t + 9) * kSdpaPitch + 16 * g);
+    const uint32_t va[4] = {vr0.x, vr0.y, vr0.z, vr0.w}, vb[4] = {vr1.x, vr1.y, vr1.z, vr1.w};
+    const uint32_t vc[4] = {vr2.x, vr2.y, vr2.z, vr2.w}, vd[4] = {vr3.x, vr3.y, vr3.z, vr3.w};
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
       const uint32_t sel = static_cast<uint32_t>(j & 3) | (static_cast<uint32_t>(4 + (j & 3)) << 8);
@@ -210,6 +250,23 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
       b1 = (b1 & 0x00FF00FFu) ^ 0x64806480u;
       mma_16816<true>(acc[j], ap, b0, b1);
     }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      sk[j] = skn[j];
+      sv[j] = svn[j];
+    }
+    if (i + kSdpaStages < my_blocks) {
+      __syncwarp();
+      fence_proxy_async_smem();
+      issue(i + kSdpaStages);
+    }
+  }
+  if (failed) {
+    if (p.status && lane == 0) atomicOr(p.status, kStatusTimeout);
+    for (int i = max(0, my_blocks - kSdpaStages); i < my_blocks; ++i)
+      mbar_wait_bounded(bars + i % kSdpaStages, (i / kSdpaStages) & 1);
+    m_run = -INFINITY;
+    l_run = 0.f;
   }
 
   // ---- warp result: o[d] = acc - 1152 * sum(P'); d(j, c0) = 32t + j, d(j, c1) = 32t + 16 + j
@@ -308,7 +365,7 @@ int sdpa_splits(int64_t batch, int kv_heads, int64_t length) {
   const int64_t bkv = batch * kv_heads;
   const int64_t nblk = (length + 15) / 16;
   int64_t s = (sdpa_sms() * 4 + bkv - 1) / bkv;
-  s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (2 * kSdpaWarps)));  // >= 2 blocks per warp
+  s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (4 * kSdpaWarps)));  // >= 4 blocks per warp
   s = std::min<int64_t>(s, 64);
   return static_cast<int>(std::max<int64_t>(1, s));
 }
@@ -364,13 +421,21 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
     p.counters = static_cast<unsigned*>(workspace);
     p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + counters);
   }
+  if (workspace != nullptr && workspace_bytes >= kCounterBytes)
+    p.status = static_cast<unsigned*>(workspace) + kStatusWord;
   const dim3 grid(static_cast<unsigned>(bkv), splits);
   const dim3 block(kSdpaWarps * 32);
+  auto go = [&](auto kernel) -> int {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSdpaSmem)) !=
+        cudaSuccess)
+      return fail(SB_ECUDA, "int8 sdpa: shared memory opt-in failed");
+    return launch("int8 sdpa", kernel, grid, block, kSdpaSmem, stream, p);
+  };
   switch (G) {
-    case 1: return launch("int8 sdpa", sdpa_int8_decode_kernel<1>, grid, block, 0, stream, p);
-    case 2: return launch("int8 sdpa", sdpa_int8_decode_kernel<2>, grid, block, 0, stream, p);
-    case 4: return launch("int8 sdpa", sdpa_int8_decode_kernel<4>, grid, block, 0, stream, p);
-    default: return launch("int8 sdpa", sdpa_int8_decode_kernel<8>, grid, block, 0, stream, p);
+    case 1: return go(sdpa_int8_decode_kernel<1>);
+    case 2: return go(sdpa_int8_decode_kernel<2>);
+    case 4: return go(sdpa_int8_decode_kernel<4>);
+    default: return go(sdpa_int8_decode_kernel<8>);
   }
 }
 

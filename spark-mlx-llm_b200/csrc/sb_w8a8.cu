@@ -21,6 +21,7 @@ namespace sb {
 
 constexpr int kI8Warps = 4;
 constexpr int kI8Tiles = 2;
+constexpr int kI8Seg = 4096;  // K values of activations staged in shared memory at a time
 
 struct I8Params {
   const void* x;  // [M][K] (int8 when x_dtype < 0, else float type to quantize)
@@ -119,9 +120,7 @@ __global__ void __launch_bounds__(kI8Warps * 32, 4) i8_gemv_kernel(const __grid_
   }
   grid_dependency_wait();
 
-  // stage int8 activations for this split's K range
-  int8_t* xs = reinterpret_cast<int8_t*>(smem_raw);
-  const int xs_ld = k_count + 16;
+  // per-token scales over the full row (quantizing path)
   if constexpr (kQuantize) {
     for (int m = 0; m < p.M; ++m) {
       float amax = 0.f;
@@ -137,57 +136,67 @@ __global__ void __launch_bounds__(kI8Warps * 32, 4) i8_gemv_kernel(const __grid_
       for (int w = 0; w < kI8Warps; ++w) amax = fmaxf(amax, s_part[w][threadIdx.x]);
       s_scale[threadIdx.x] = amax > 0.f ? __fdiv_rn(amax, 127.0f) : 1.0f;
     }
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < p.M * k_count; idx += kI8Warps * 32) {
-      const int m = idx / k_count, k = idx % k_count;
-      xs[m * xs_ld + k] = quantize_value(load_any(p.x, p.x_dtype, static_cast<size_t>(m) * p.K + k_begin + k),
-                                         s_scale[m]);
-    }
-  } else {
-    const int vecs = k_count / 16;
-    for (int idx = threadIdx.x; idx < p.M * vecs; idx += kI8Warps * 32) {
-      const int m = idx / vecs, v = idx % vecs;
-      *reinterpret_cast<uint4*>(xs + m * xs_ld + v * 16) = *reinterpret_cast<const uint4*>(
-          static_cast<const int8_t*>(p.x) + static_cast<size_t>(m) * p.K + k_begin + v * 16);
-    }
   }
-  __syncthreads();
-  if (!active) return;
 
+  int8_t* xs = reinterpret_cast<int8_t*>(smem_raw);
+  const int xs_ld = kI8Seg + 16;
   int acc[kI8Tiles][4];
 #pragma unroll
   for (int r = 0; r < kI8Tiles; ++r)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[r][e] = 0;
   const int8_t* xcol = xs + min(g, p.M - 1) * xs_ld + t * 16;
-  for (int c = c_begin; c < c_end; ++c) {
-    uint32_t cur[kRows][4];
-#pragma unroll
-    for (int q = 0; q < kRows; ++q)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) cur[q][i] = wbuf[q][i];
-    if (c + 1 < c_end) {
-#pragma unroll
-      for (int q = 0; q < kRows; ++q) {
-        const uint4 v = ldg_stream16(wrow[q] + static_cast<size_t>(c + 1) * 64);
-        wbuf[q][0] = v.x;
-        wbuf[q][1] = v.y;
-        wbuf[q][2] = v.z;
-        wbuf[q][3] = v.w;
+  for (int seg0 = 0; seg0 < k_count; seg0 += kI8Seg) {
+    // stage int8 activations of this K segment (all warps take part)
+    const int seg_len = min(kI8Seg, k_count - seg0);
+    __syncthreads();
+    if constexpr (kQuantize) {
+      for (int idx = threadIdx.x; idx < p.M * seg_len; idx += kI8Warps * 32) {
+        const int m = idx / seg_len, k = idx % seg_len;
+        xs[m * xs_ld + k] = quantize_value(
+            load_any(p.x, p.x_dtype, static_cast<size_t>(m) * p.K + k_begin + seg0 + k), s_scale[m]);
+      }
+    } else {
+      const int vecs = seg_len / 16;
+      for (int idx = threadIdx.x; idx < p.M * vecs; idx += kI8Warps * 32) {
+        const int m = idx / vecs, v = idx % vecs;
+        *reinterpret_cast<uint4*>(xs + m * xs_ld + v * 16) = *reinterpret_cast<const uint4*>(
+            static_cast<const int8_t*>(p.x) + static_cast<size_t>(m) * p.K + k_begin + seg0 + v * 16);
       }
     }
-    const uint4 xv = *reinterpret_cast<const uint4*>(xcol + (c - c_begin) * 64);
-    const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+    __syncthreads();
+    if (!active) continue;
+    const int cs = c_begin + seg0 / 64, ce = cs + seg_len / 64;
+    for (int c = cs; c < ce; ++c) {
+      uint32_t cur[kRows][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+      for (int q = 0; q < kRows; ++q)
 #pragma unroll
-      for (int r = 0; r < kI8Tiles; ++r) {
-        const uint32_t a[4] = {cur[2 * r][2 * j], cur[2 * r + 1][2 * j], cur[2 * r][2 * j + 1],
-                               cur[2 * r + 1][2 * j + 1]};
-        mma_s8_16832(acc[r], a, xw[2 * j], xw[2 * j + 1]);
+        for (int i = 0; i < 4; ++i) cur[q][i] = wbuf[q][i];
+      if (c + 1 < c_end) {
+#pragma unroll
+        for (int q = 0; q < kRows; ++q) {
+          const uint4 v = ldg_stream16(wrow[q] + static_cast<size_t>(c + 1) * 64);
+          wbuf[q][0] = v.x;
+          wbuf[q][1] = v.y;
+          wbuf[q][2] = v.z;
+          wbuf[q][3] = v.w;
+        }
+      }
+      const uint4 xv = *reinterpret_cast<const uint4*>(xcol + (c - cs) * 64);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+#pragma unroll
+        for (int r = 0; r < kI8Tiles; ++r) {
+          const uint32_t a[4] = {cur[2 * r][2 * j], cur[2 * r + 1][2 * j], cur[2 * r][2 * j + 1],
+                                 cur[2 * r + 1][2 * j + 1]};
+          mma_s8_16832(acc[r], a, xw[2 * j], xw[2 * j + 1]);
+        }
       }
     }
   }
+  if (!active) return;
   grid_dependency_launch();
 
   if (p.splits > 1) {
@@ -276,7 +285,6 @@ I8Plan plan_i8(int N, int K, bool allow_split) {
   pl.groups = K / 64;
   int s = allow_split ? (sms() * 12 + pl.rowblocks - 1) / pl.rowblocks : 1;
   s = std::min(s, std::max(1, pl.groups / 2));
-  s = std::max(s, (K + 8191) / 8192);
   s = std::max(1, std::min(s, pl.groups));
   pl.splits = pl.rowblocks > kMaxCounters ? 1 : s;
   pl.counter_bytes = kCounterBytes;
@@ -293,8 +301,7 @@ int launch_i8(I8Params& p, const I8Plan& pl, void* ws, size_t ws_bytes, cudaStre
     p.counters = static_cast<unsigned*>(ws);
     p.partial = reinterpret_cast<int*>(static_cast<uint8_t*>(ws) + pl.counter_bytes);
   }
-  const int max_k = (pl.groups + pl.splits - 1) / pl.splits * 64;
-  const size_t smem = static_cast<size_t>(p.M) * (max_k + 16);
+  const size_t smem = static_cast<size_t>(p.M) * (kI8Seg + 16);
   auto kernel = i8_gemv_kernel<kQuantize, kRaw>;
   if (smem > 48 * 1024 &&
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
