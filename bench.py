@@ -15,7 +15,8 @@ torch.distributed.run, NCCL).
               token plus a stream sync every step.
 * ``roofline`` the dominant kernel (RMSNorm + gate/up W4A16 GEMV + SwiGLU),
               timed alone over the 36 layers' weights (1 GB, L2-cold).
-* ``cpu_baseline`` the NumPy oracle on the host cores, bounded sample.
+* ``cpu_baseline`` the C restatement of the reference arithmetic (oracle/c) on
+              all host cores, bounded sample.
 
 ``--impl reference`` times the reference arithmetic on the CPU (the oracle
 port of the reference's CPU path; the reference itself needs MLX, which is
@@ -49,6 +50,8 @@ def parse_args():
     p.add_argument("--prompt", type=int, default=1024)
     p.add_argument("--layers", type=int, default=36, help="(debug) fewer layers")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--kernel-only", choices=["gateup", "sdpa"], default=None,
+                   help="launch one hot kernel --steps times on a config-sized case (for ncu)")
     return p.parse_args()
 
 
@@ -126,21 +129,23 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------- CPU reference
-def cpu_reference(cfg, batch, context, layers_sample=2, head_fraction=16, reps=3):
-    """Decode tok/s of the NumPy oracle (reference arithmetic) on this host's cores.
+def cpu_reference(cfg, batch, context, layers_sample=4, head_fraction=8, budget_s=12.0):
+    """Decode tok/s of the reference arithmetic on this host's cores.
 
-    Bounded sample: ``layers_sample`` decoder layers plus 1/``head_fraction`` of
-    the lm_head rows for one token at position ``context``, scaled to the full
-    model (36 layers, full vocabulary).
+    Runs the multithreaded C restatement (oracle/c, all host threads) of one
+    decode step. Bounded sample: ``layers_sample`` decoder layers plus
+    1/``head_fraction`` of the lm_head rows, one token at position ``context``,
+    repeated for about ``budget_s`` seconds; the best repetition is scaled to
+    the full model (all layers, full vocabulary).
     """
     import numpy as np
     import torch
 
-    from oracle import formats, ops
-    from oracle.model import OracleDecoder
+    from oracle import formats
+    from oracle.cpu_decoder import CDecoder, load_library
     from spark_b200 import quantize
 
-    torch.manual_seed(0)
+    lib = load_library()
     d = cfg.head_dim
     gen = torch.Generator().manual_seed(1234)
 
@@ -149,7 +154,8 @@ def cpu_reference(cfg, batch, context, layers_sample=2, head_fraction=16, reps=3
 
     def aff(w):
         p, s, b = quantize.quantize_affine_minmax(w, cfg.mlp_group, 4)
-        return p.numpy().view(np.uint32), s.float().numpy(), b.float().numpy()
+        return (p.numpy().view(np.uint32), s.view(torch.int16).numpy().view(np.uint16),
+                b.view(torch.int16).numpy().view(np.uint16))
 
     layers = []
     for _ in range(layers_sample):
@@ -162,39 +168,41 @@ def cpu_reference(cfg, batch, context, layers_sample=2, head_fraction=16, reps=3
                            down=aff(randn(cfg.hidden, cfg.intermediate, std=cfg.weight_std)),
                            in_norm=np.ones(cfg.hidden, np.float32), post_norm=np.ones(cfg.hidden, np.float32)))
     vocab_sample = cfg.vocab // head_fraction
-    weights = dict(layers=layers,
-                   embed=formats.round_bf16(randn(vocab_sample, cfg.hidden, std=1.0).numpy()),
-                   head=formats.round_bf16(randn(vocab_sample, cfg.hidden, std=cfg.head_std).numpy()),
+    weights = dict(layers=layers, embed_bits=formats.bf16_bits(randn(vocab_sample, cfg.hidden, std=1.0).numpy()),
+                   head_bits=formats.bf16_bits(randn(vocab_sample, cfg.hidden, std=cfg.head_std).numpy()),
                    final_norm=np.ones(cfg.hidden, np.float32))
-    orc = OracleDecoder(weights, num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=d,
-                        rope_theta=cfg.rope_theta, eps=cfg.rms_eps, group=cfg.mlp_group, capacity=context + 1,
-                        batch=batch)
+    dec = CDecoder(weights, num_heads=cfg.num_heads, num_kv_heads=cfg.num_kv_heads, head_dim=d,
+                   rope_theta=cfg.rope_theta, eps=cfg.rms_eps, group=cfg.mlp_group, capacity=context + 1, batch=batch)
     rng = np.random.default_rng(0)
-    orc.kq[...] = rng.integers(-127, 128, orc.kq.shape, dtype=np.int8)
-    orc.vq[...] = rng.integers(-127, 128, orc.vq.shape, dtype=np.int8)
-    orc.ks[...] = np.float16(0.02)
-    orc.vs[...] = np.float16(0.02)
+    dec.kq[...] = rng.integers(-127, 128, dec.kq.shape, dtype=np.int8)
+    dec.vq[...] = rng.integers(-127, 128, dec.vq.shape, dtype=np.int8)
+    dec.ks[...] = np.float16(0.02)
+    dec.vs[...] = np.float16(0.02)
     tokens = rng.integers(0, vocab_sample, batch)
-    # time the layers and the head separately
-    layer_times, head_times = [], []
-    for _ in range(reps):
+    head = weights["head_bits"]
+    xn = np.ascontiguousarray(rng.standard_normal((batch, cfg.hidden)), dtype=np.float32)
+    idx = np.empty(batch, np.int32)
+    best = np.empty(batch, np.float32)
+    import ctypes
+
+    layer_t, head_t = [], []
+    start = time.perf_counter()
+    while not layer_t or time.perf_counter() - start < budget_s:
         t0 = time.perf_counter()
-        logits = orc.step(tokens, context)
+        dec.step(tokens, context)
         t1 = time.perf_counter()
-        x = orc.last_x
-        xn = formats.round_bf16(ops.rms_norm(x, weights["final_norm"], cfg.rms_eps))
+        lib.oc_bf16_argmax(xn.ctypes.data_as(ctypes.c_void_p), batch, head.ctypes.data_as(ctypes.c_void_p),
+                           head.shape[0], head.shape[1], idx.ctypes.data_as(ctypes.c_void_p),
+                           best.ctypes.data_as(ctypes.c_void_p))
         t2 = time.perf_counter()
-        _ = xn.astype(np.float64) @ weights["head"].astype(np.float64).T
-        t3 = time.perf_counter()
-        layer_times.append((t1 - t0) - (t3 - t2))
-        head_times.append(t3 - t2)
-        del logits
-    per_layer = min(layer_times) / layers_sample
-    head = min(head_times) * head_fraction
-    token_s = per_layer * cfg.num_layers + head
-    sample = (f"{layers_sample} of {cfg.num_layers} layers + 1/{head_fraction} of lm_head rows, one decode "
-              f"token at context {context}, batch {batch}, best of {reps}; scaled to the full model")
-    return batch / token_s, os.cpu_count(), sample
+        head_t.append(t2 - t1)
+        layer_t.append((t1 - t0) - (t2 - t1))  # step() includes one head pass of the sample
+    per_layer = min(layer_t) / layers_sample
+    token_s = per_layer * cfg.num_layers + min(head_t) * head_fraction
+    sample = (f"C restatement (oracle/c, {lib.oc_threads()} threads): {layers_sample} of {cfg.num_layers} layers + "
+              f"1/{head_fraction} of lm_head rows, one decode token at context {context}, batch {batch}, best of "
+              f"{len(layer_t)} repetitions in {budget_s:.0f} s; scaled to the full model")
+    return batch / token_s, lib.oc_threads(), sample
 
 
 def run_reference(args):
@@ -204,12 +212,7 @@ def run_reference(args):
     from spark_b200.decoder import DecoderConfig
 
     cfg = DecoderConfig(num_layers=args.layers)
-    vals = []
-    sample = cores = None
-    for _ in range(max(1, min(args.steps, 2))):
-        v, cores, sample = cpu_reference(cfg, args.batch, args.prompt)
-        vals.append(v)
-    value = statistics.median(vals)
+    value, cores, sample = cpu_reference(cfg, args.batch, args.prompt)
     out = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * args.batch / value,
@@ -217,8 +220,8 @@ def run_reference(args):
         "config": workload_config(args, "cpu"),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        "note": "NumPy oracle restating the reference arithmetic (MLX, the reference's own CPU path, is not "
-                "installable offline)",
+        "note": "C restatement of the reference arithmetic on all host cores (the reference's own CPU path runs "
+                "through MLX, which is not installable offline)",
     }
     print(json.dumps(out), flush=True)
 
@@ -233,11 +236,65 @@ def workload_config(args, parallel):
     }
 
 
+def kernel_only(args):
+    """Launch one hot kernel ``--steps`` times (profiling target; prints its CUDA-event time)."""
+    import ctypes
+
+    import torch
+
+    from spark_b200 import quantize
+    from spark_b200._lib import check, lib, sb_linear_ex_desc
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    L = lib()
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    if args.kernel_only == "gateup":
+        n, k = 9728, 2560
+        gw, gs, gb = quantize.quantize_affine_minmax(torch.randn(n, k, generator=g, device=dev) * 0.02, 64, 4)
+        uw, us, ub = quantize.quantize_affine_minmax(torch.randn(n, k, generator=g, device=dev) * 0.02, 64, 4)
+        x = torch.randn(args.batch, k, generator=g, device=dev).bfloat16()
+        norm = torch.ones(k, device=dev).bfloat16()
+        y = torch.empty(args.batch, n, device=dev).bfloat16()
+        ws = torch.zeros(16 << 20, dtype=torch.uint8, device=dev)
+        d = sb_linear_ex_desc(x=x.data_ptr(), x_dtype=0, M=args.batch, N=n, K=k, weight_format=0,
+                              weight=gw.data_ptr(), scales=gs.data_ptr(), biases=gb.data_ptr(), weight2=uw.data_ptr(),
+                              scales2=us.data_ptr(), biases2=ub.data_ptr(), group_size=64,
+                              norm_weight=norm.data_ptr(), norm_eps=1e-6, epilogue=2, y=y.data_ptr(),
+                              workspace=ws.data_ptr(), workspace_bytes=ws.numel(), weights_constant=1)
+        launch = lambda: check(L.sb_linear_ex(ctypes.byref(d), stream), "gateup")  # noqa: E731
+    else:
+        b_, n = args.batch, 32768
+        q = torch.randn(b_, 32, 1, 128, generator=g, device=dev).bfloat16()
+        kc = torch.randint(-127, 128, (b_, 8, n, 128), generator=g, device=dev, dtype=torch.int8)
+        vc = torch.randint(-127, 128, (b_, 8, n, 128), generator=g, device=dev, dtype=torch.int8)
+        ks = torch.full((b_, 8, n), 0.02, device=dev).half()
+        vs = torch.full((b_, 8, n), 0.02, device=dev).half()
+        out = torch.empty_like(q)
+        ws = torch.zeros(64 << 20, dtype=torch.uint8, device=dev)
+        launch = lambda: check(L.sb_int8_sdpa_decode(q.data_ptr(), kc.data_ptr(), ks.data_ptr(), vc.data_ptr(),  # noqa: E731
+                                                     vs.data_ptr(), out.data_ptr(), b_, 32, 8, n, n, 128, 0.0884,
+                                                     ws.data_ptr(), ws.numel(), stream), "sdpa")
+    launch()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        launch()
+    e1.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel": args.kernel_only, "launches": args.steps, "avg_us": e0.elapsed_time(e1) * 1e3 / args.steps}))
+
+
 # -------------------------------------------------------------------- GPU arm
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.kernel_only:
+        kernel_only(args)
         return
     import torch
     import torch.distributed as dist

@@ -1,6 +1,7 @@
 // Shared device/host helpers for the spark_b200 CUDA library (sm_100a).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -23,6 +24,11 @@ int check_launch(const char* what);
   } while (0)
 
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+// 2-D TMA descriptor over a row-major byte matrix [rows][row_bytes] with a
+// [box_rows x 128 B] box and the 128-byte swizzle (16-byte units of row i are
+// permuted by XOR with i % 8 in shared memory). Out-of-range reads fill zeros.
+int make_tmap_rows(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows);
 
 // Every workspace starts with a fixed-size region of arrival counters (zero
 // between calls), followed by the call's partial results. The fixed size keeps
@@ -105,6 +111,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase)
   }
   return true;
 }
+// 2-D tiled TMA load (no multicast) of one box at (x bytes, y rows) into shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+// Byte `byte` of row `row` inside a 128-byte-swizzled box.
+__device__ __forceinline__ const uint8_t* swz128(const uint8_t* box, int row, int byte) {
+  return box + row * 128 + ((((byte >> 4) ^ (row & 7)) << 4) | (byte & 15));
+}
+
 // Order earlier generic-proxy accesses of shared memory before later async-proxy ones.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

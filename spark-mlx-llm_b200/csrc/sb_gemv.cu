@@ -134,39 +134,45 @@ __device__ __forceinline__ float round_act(float v) {
   return to_float(from_float<TA>(v));
 }
 
-// Physical weight row (and weight set) of row r16 (0..15) of m16 tile `tile`.
+// ---- warp row blocks
+// A warp owns 32 weight rows, fetched per stage as two TMA boxes (A and B) of
+// 16 rows x 128 bytes. MMA rows 0-7 of tile r come from box A rows 8r + sigma(g),
+// MMA rows 8-15 from box B rows 8r + sigma(g). sigma relabels the rows so the
+// lanes' reads of the 128-byte-swizzled boxes hit distinct banks.
+template <int kBits>
+__device__ __forceinline__ int sigma_row(int g) {
+  if constexpr (kBits == 4) return ((g & 3) << 1) | (g >> 2);   // 0,2,4,6,1,3,5,7
+  else if constexpr (kBits == 8) return ((g & 1) << 2) | (g >> 1);  // 0,4,1,5,2,6,3,7
+  else return g;
+}
+
+// number of 32-row warp blocks
 template <int EPI>
-__device__ __forceinline__ int map_row(const GemvParams& p, int tile, int r16, int& set,
-                                       bool& valid) {
-  set = 0;
-  valid = true;
+__device__ __forceinline__ int warp_blocks(const GemvParams& p) {
+  if constexpr (EPI == EPI_SWIGLU) return (p.N + 15) / 16;
+  else if constexpr (EPI == EPI_ROPE) return p.N / 32;
+  else return (p.N + 31) / 32;
+}
+
+// first weight row of box h (0 = A, 1 = B) of warp block rb
+template <int EPI>
+__device__ __forceinline__ int box_row0(const GemvParams& p, int rb, int h) {
   if constexpr (EPI == EPI_SWIGLU) {
-    set = r16 >> 3;
-    const int n = tile * 8 + (r16 & 7);
-    valid = n < p.N;
-    return min(n, p.N - 1);
+    return 16 * rb;  // gate rows in A, the same up rows in B
   } else if constexpr (EPI == EPI_ROPE) {
-    const int tph = p.head_dim / 16;  // tiles per head
-    const int h = tile / tph, j = tile % tph;
-    const int row = h * p.head_dim + (r16 < 8 ? 8 * j + r16 : p.head_dim / 2 + 8 * j + r16 - 8);
-    valid = row < p.N;
-    return min(row, p.N - 1);
+    const int wph = p.head_dim / 32;  // warp blocks per head
+    return (rb / wph) * p.head_dim + h * (p.head_dim / 2) + 16 * (rb % wph);
   } else {
-    const int row = tile * 16 + r16;
-    valid = row < p.N;
-    return min(row, p.N - 1);
+    return 32 * rb + 16 * h;
   }
 }
 
-// Smem words of one stage row (bytes) and row pitch chosen so the lanes' 8-byte
-// (4-bit) or 16-byte (8-bit, bf16) reads of 8 rows hit distinct banks.
 template <int kBits>
 struct StageGeom {
-  static constexpr int kRowBytes = 128;                       // bytes of one weight row per stage
-  static constexpr int kStageK = kRowBytes * 8 / kBits;       // K values per stage
-  static constexpr int kPitch = kBits == 4 ? 160 : 192;       // smem row pitch
-  static constexpr int kStages = kBits == 4 ? 4 : 3;          // ring depth per warp
-  static constexpr int kStageBytes = 32 * kPitch;             // 32 weight rows per warp
+  static constexpr int kRowBytes = 128;                  // bytes of one weight row per stage
+  static constexpr int kStageK = kRowBytes * 8 / kBits;  // K values per stage
+  static constexpr int kStages = kBits == 4 ? 5 : 4;     // ring depth per warp
+  static constexpr int kStageBytes = 32 * kRowBytes;     // two 16-row boxes
 };
 
 template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
@@ -182,11 +188,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
   constexpr bool kAffine = (WF == W_AFF4 || WF == W_AFF8);
   constexpr int kGroupK = kAffine ? KC * GC : KC;  // K covered by one split unit
   constexpr int kChunkRowBytes = KC * F::kBits / 8;
+  constexpr int kLaneBytes = V * F::kBits / 8;
   constexpr int kChunksPerStage = SG::kStageK / KC;
   constexpr int kGroupsPerStage = kAffine ? kChunksPerStage / GC : 0;
   static_assert(!kAffine || kChunksPerStage % GC == 0, "a stage holds whole groups");
 
-  extern __shared__ __align__(128) uint8_t smem_raw[];
+  extern __shared__ uint8_t smem_dyn[];
   __shared__ float s_rms[8];
   __shared__ float s_part[kGemvWarps][8];
 
@@ -194,13 +201,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2;
   const int t = lane & 3;
+  const int sg = sigma_row<F::kBits>(g);
   const int split = blockIdx.y;
-  const int tiles = (EPI == EPI_SWIGLU) ? (p.N + 7) / 8
-                    : (EPI == EPI_ROPE)  ? p.N / 16
-                                         : (p.N + 15) / 16;
-  const int rowblocks = (tiles + kGemvTiles - 1) / kGemvTiles;
+  const int rowblocks = warp_blocks<EPI>(p);
   const int rb = blockIdx.x * kGemvWarps + warp;
   const bool active = rb < rowblocks;
+  const int rbc = min(rb, rowblocks - 1);
 
   // K range of this split, in whole groups.
   const int grp_begin = static_cast<int>((static_cast<long long>(p.groups_total) * split) / p.splits);
@@ -208,57 +214,36 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
   const int k_begin = grp_begin * kGroupK;
   const int k_count = (grp_end - grp_begin) * kGroupK;
   const int nstages = (k_count + SG::kStageK - 1) / SG::kStageK;
+  const int kbyte0 = k_begin * F::kBits / 8;
 
-  // ---- shared memory carve-up: barriers, per-warp weight rings, x segment
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw) + warp * SG::kStages;
-  uint8_t* ring = smem_raw + 128 + (warp * SG::kStages) * SG::kStageBytes;
-  TA* xs = reinterpret_cast<TA*>(smem_raw + 128 + kGemvWarps * SG::kStages * SG::kStageBytes);
+  // ---- shared memory: barriers, per-warp weight rings (1 KB aligned), x segment
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base) + warp * SG::kStages;
+  uint8_t* ring = base + 1024 + (warp * SG::kStages) * SG::kStageBytes;
+  TA* xs = reinterpret_cast<TA*>(base + 1024 + kGemvWarps * SG::kStages * SG::kStageBytes);
   const int mcols = p.M;
   const int xs_ld = p.x_seg + 8;
+  const int rowA = box_row0<EPI>(p, rbc, 0), rowB = box_row0<EPI>(p, rbc, 1);
 
-  // ---- row owned by this lane for the bulk copies, and the row whose scale/bias it loads
-  const size_t row_bytes = static_cast<size_t>(p.K) * F::kBits / 8;
-  const uint8_t* copy_src;
-  {
-    int set;
-    bool valid;
-    const int tile = min(min(rb, rowblocks - 1) * kGemvTiles + (lane >> 4), tiles - 1);
-    const int row = map_row<EPI>(p, tile, lane & 15, set, valid);
-    copy_src = static_cast<const uint8_t*>(set ? p.w1 : p.w0) + row * row_bytes +
-               static_cast<size_t>(k_begin) * F::kBits / 8;
-  }
-  int my_set = 0, my_row = 0;
-  {
-    bool valid;
-    const int tile = min(min(rb, rowblocks - 1) * kGemvTiles + (t >> 1), tiles - 1);
-    my_row = map_row<EPI>(p, tile, (t & 1) * 8 + g, my_set, valid);
-  }
-
-  auto stage_row_bytes = [&](int st) -> uint32_t {
-    const int kk = min(SG::kStageK, k_count - st * SG::kStageK);
-    return static_cast<uint32_t>(kk * F::kBits / 8);
-  };
   auto issue_stage = [&](int st) {
     const int slot = st % SG::kStages;
-    const uint32_t bytes = stage_row_bytes(st);
-    if (lane == 0) mbar_arrive_expect_tx(bars + slot, bytes * 32);
-    __syncwarp();
-    bulk_copy_g2s(ring + slot * SG::kStageBytes + lane * SG::kPitch,
-                  copy_src + static_cast<size_t>(st) * SG::kRowBytes, bytes, bars + slot);
+    uint8_t* dst = ring + slot * SG::kStageBytes;
+    mbar_arrive_expect_tx(bars + slot, SG::kStageBytes);
+    const int x = kbyte0 + st * SG::kRowBytes;
+    tma_load_2d(dst, &p.tmap0, x, rowA, bars + slot);
+    tma_load_2d(dst + 16 * SG::kRowBytes, &p.tmap1, x, rowB, bars + slot);
   };
 
-  if (active) {
-    if (lane < SG::kStages) mbar_init(bars + lane, 1);
+  if (active && lane == 0) {
+    for (int i = 0; i < SG::kStages; ++i) mbar_init(bars + i, 1);
     mbar_fence_init();
-    __syncwarp();
   }
+  __syncwarp();
   // ---- start streaming weights; with constant weights this may overlap the
   // tail of the previous kernel in the stream
   if (!p.early_prefetch) grid_dependency_wait();
-  if (active) {
-#pragma unroll
-    for (int st = 0; st < SG::kStages; ++st)
-      if (st < nstages) issue_stage(st);
+  if (active && lane == 0) {
+    for (int st = 0; st < SG::kStages && st < nstages; ++st) issue_stage(st);
   }
 
   // ---- activations depend on the previous kernel from here on
@@ -313,7 +298,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
 #pragma unroll
   for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
 
-  // scale/bias of this lane's row (q == t), one stage ahead in registers
+  // scale/bias of the row q == t (tile t >> 1, box t & 1), one stage ahead in registers
   const TA* srow = nullptr;
   const TA* brow = nullptr;
   uint32_t sb_cur[kGroupsPerStage > 0 ? kGroupsPerStage : 1];
@@ -333,9 +318,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     }
   };
   if constexpr (kAffine) {
+    const int my_h = t & 1;
+    const int my_row = min((my_h ? rowB : rowA) + 8 * (t >> 1) + sg, p.N - 1);
+    const int set = (EPI == EPI_SWIGLU) ? my_h : 0;
     const int gpr = p.K / p.group_size;
-    srow = static_cast<const TA*>(my_set ? p.s1 : p.s0) + static_cast<size_t>(my_row) * gpr;
-    brow = static_cast<const TA*>(my_set ? p.b1 : p.b0) + static_cast<size_t>(my_row) * gpr;
+    srow = static_cast<const TA*>(set ? p.s1 : p.s0) + static_cast<size_t>(my_row) * gpr;
+    brow = static_cast<const TA*>(set ? p.b1 : p.b0) + static_cast<size_t>(my_row) * gpr;
     if (active && nstages > 0) load_sb(0, sb_cur);
   }
 
@@ -384,18 +372,19 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
         uint32_t wv[kRows][kWords];
 #pragma unroll
         for (int q = 0; q < kRows; ++q) {
-          const uint8_t* src = stage + ((q >> 1) * 16 + (q & 1) * 8 + g) * SG::kPitch + cc * kChunkRowBytes +
-                               t * (V * F::kBits / 8);
+          const uint8_t* box = stage + (q & 1) * 16 * SG::kRowBytes;
+          const int row = 8 * (q >> 1) + sg;
+          const int byte = cc * kChunkRowBytes + t * kLaneBytes;
           if constexpr (kWords == 1) {
-            wv[q][0] = *reinterpret_cast<const uint32_t*>(src);
+            wv[q][0] = *reinterpret_cast<const uint32_t*>(swz128(box, row, byte));
           } else if constexpr (kWords == 2) {
-            const uint2 v = *reinterpret_cast<const uint2*>(src);
+            const uint2 v = *reinterpret_cast<const uint2*>(swz128(box, row, byte));
             wv[q][0] = v.x;
             wv[q][1] = v.y;
           } else {
 #pragma unroll
             for (int i = 0; i < kWords; i += 4) {
-              const uint4 v = *reinterpret_cast<const uint4*>(src + 4 * i);
+              const uint4 v = *reinterpret_cast<const uint4*>(swz128(box, row, byte + 4 * i));
               wv[q][i] = v.x;
               wv[q][i + 1] = v.y;
               wv[q][i + 2] = v.z;
@@ -475,15 +464,15 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
       for (int i = 0; i < kGroupsPerStage; ++i) sb_cur[i] = sb_nxt[i];
     }
     // refill this slot with the stage kStages ahead
-    if (st + SG::kStages < nstages) {
-      __syncwarp();
+    __syncwarp();
+    if (st + SG::kStages < nstages && lane == 0) {
       fence_proxy_async_smem();
       issue_stage(st + SG::kStages);
     }
   }
   if (!active) return;
   if (failed) {
-    // a bulk copy never completed: report, drain what is still in flight, stop
+    // a TMA load never completed: report, drain what is still in flight, stop
     if (p.status && lane == 0) atomicOr(p.status, kStatusTimeout);
     for (int st = max(0, nstages - SG::kStages); st < nstages; ++st)
       mbar_wait_bounded(bars + st % SG::kStages, (st / SG::kStages) & 1);
@@ -510,7 +499,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
 
   // ---- split-K: publish partials; the last warp of the row block reduces
   if (p.splits > 1) {
-    float* part = p.partial + (static_cast<size_t>(split) * p.rows_padded + rb * 16 * kGemvTiles) * 8;
+    float* part = p.partial + (static_cast<size_t>(split) * p.rows_padded + rb * 32) * 8;
 #pragma unroll
     for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
@@ -532,7 +521,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
     for (int s = 0; s < p.splits; ++s) {
-      const float* ps = p.partial + (static_cast<size_t>(s) * p.rows_padded + rb * 16 * kGemvTiles) * 8;
+      const float* ps = p.partial + (static_cast<size_t>(s) * p.rows_padded + rb * 32) * 8;
 #pragma unroll
       for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
@@ -547,7 +536,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     if (lane == 0) p.counters[rb] = 0u;
   }
 
-  // ---- final epilogue
+  // ---- final epilogue: (tile r, box h) of this lane is weight row box_row0(h) + 8r + sigma(g)
   if constexpr (EPI == EPI_ARGMAX) {
     float best[2] = {-INFINITY, -INFINITY};
     int best_i[2] = {0x7FFFFFFF, 0x7FFFFFFF};
@@ -555,10 +544,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
-        int set;
-        bool valid;
-        const int row = map_row<EPI>(p, rb * kGemvTiles + r, h * 8 + g, set, valid);
-        if (!valid || rb * kGemvTiles + r >= tiles) continue;
+        const int row = (h ? rowB : rowA) + 8 * r + sg;
+        if (row >= p.N) continue;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const float v = acc[r][2 * h + e];
@@ -594,16 +581,14 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     if constexpr (WF == W_I8PC) {
 #pragma unroll
       for (int q = 0; q < kRows; ++q) {
-        int set;
-        bool valid;
-        const int row = map_row<EPI>(p, min(rb * kGemvTiles + (q >> 1), tiles - 1), (q & 1) * 8 + g, set, valid);
+        const int h = q & 1;
+        const int row = min((h ? rowB : rowA) + 8 * (q >> 1) + sg, p.N - 1);
+        const int set = (EPI == EPI_SWIGLU) ? h : 0;
         scale_pc[q] = static_cast<const float*>(set ? p.s1 : p.s0)[row];
       }
     }
 #pragma unroll
     for (int r = 0; r < kGemvTiles; ++r) {
-      const int tile = rb * kGemvTiles + r;
-      if (tile >= tiles) continue;
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int m = 2 * t + e;
@@ -614,16 +599,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
           v_hi *= scale_pc[2 * r + 1];
         }
         if constexpr (EPI == EPI_SWIGLU) {
-          const int n = tile * 8 + g;
+          const int n = rowA + 8 * r + sg;
           if (n < p.N) {
             const float gt = round_act<TA>(v_lo), up = round_act<TA>(v_hi);
             const float silu = gt / (1.0f + expf(-gt));
             store_act<TA>(p.y, static_cast<size_t>(m) * p.ldy + n, silu * up);
           }
         } else if constexpr (EPI == EPI_ROPE) {
-          const int tph = p.head_dim / 16;
-          const int head = tile / tph, j = tile % tph;
-          const int i = 8 * j + g;            // rotation pair index
+          const int wph = p.head_dim / 32;
+          const int head = rb / wph;
+          const int i = 16 * (rb % wph) + 8 * r + sg;  // rotation pair index
           const int half = p.head_dim / 2;
           float a = round_act<TA>(v_lo), b = round_act<TA>(v_hi);
           void* out;
@@ -651,13 +636,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
             b = rb2;
           }
           const int bi = m / p.seq_len, l = m % p.seq_len;
-          const size_t base = ((static_cast<size_t>(bi) * nh + hh) * p.seq_len + l) * p.head_dim;
-          store_act<TA>(out, base + i, a);
-          store_act<TA>(out, base + half + i, b);
+          const size_t obase = ((static_cast<size_t>(bi) * nh + hh) * p.seq_len + l) * p.head_dim;
+          store_act<TA>(out, obase + i, a);
+          store_act<TA>(out, obase + half + i, b);
         } else {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int row = tile * 16 + h * 8 + g;
+            const int row = (h ? rowB : rowA) + 8 * r + sg;
             if (row >= p.N) continue;
             const float v = h ? v_hi : v_lo;
             const size_t idx = static_cast<size_t>(m) * p.ldy + row;
@@ -697,8 +682,8 @@ struct Plan {
 
 Plan make_plan(int epi, int N, int K, int group_k, bool allow_split) {
   Plan pl{};
-  pl.tiles = epi == EPI_SWIGLU ? (N + 7) / 8 : (epi == EPI_ROPE ? N / 16 : (N + 15) / 16);
-  pl.rowblocks = (pl.tiles + kGemvTiles - 1) / kGemvTiles;
+  pl.tiles = 0;
+  pl.rowblocks = epi == EPI_SWIGLU ? (N + 15) / 16 : (epi == EPI_ROPE ? N / 32 : (N + 31) / 32);
   pl.k_group = group_k;
   pl.groups = K / group_k;
   // Two CTAs of 4 warps per SM; split K only when the row blocks alone cannot
@@ -720,11 +705,11 @@ template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
 int launch_gemv(GemvParams& p, const Plan& pl, cudaStream_t stream) {
   using SG = StageGeom<Fmt<TA, WF>::kBits>;
   const int max_kunit = (pl.groups + pl.splits - 1) / pl.splits * pl.k_group;
-  // activation segment: at most 32 KB of shared memory, whole stages
-  int seg = (32768 / (p.M * static_cast<int>(sizeof(TA)))) / SG::kStageK * SG::kStageK;
+  // activation segment: at most 16 KB of shared memory, whole stages
+  int seg = (16384 / (p.M * static_cast<int>(sizeof(TA)))) / SG::kStageK * SG::kStageK;
   seg = std::max(seg, SG::kStageK);
   p.x_seg = std::min(seg, ((max_kunit + SG::kStageK - 1) / SG::kStageK) * SG::kStageK);
-  const size_t smem = 128 + static_cast<size_t>(kGemvWarps) * SG::kStages * SG::kStageBytes +
+  const size_t smem = 2048 + static_cast<size_t>(kGemvWarps) * SG::kStages * SG::kStageBytes +
                       static_cast<size_t>(p.M) * (p.x_seg + 8) * sizeof(TA);
   auto kernel = gemv_kernel<TA, WF, KC, GC, EPI, NORM>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
@@ -827,7 +812,13 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   p.group_size = r.group_size;
   p.splits = pl.splits;
   p.groups_total = pl.groups;
-  p.rows_padded = pl.rowblocks * 16 * kGemvTiles;
+  p.rows_padded = pl.rowblocks * 32;
+  {
+    const int bits = r.wf == W_AFF4 ? 4 : (r.wf == W_BF16 ? 16 : 8);
+    const uint64_t row_bytes = static_cast<uint64_t>(r.K) * bits / 8;
+    if (int st = make_tmap_rows(&p.tmap0, r.w0, static_cast<uint64_t>(r.N), row_bytes, 16)) return st;
+    if (int st = make_tmap_rows(&p.tmap1, r.w1 ? r.w1 : r.w0, static_cast<uint64_t>(r.N), row_bytes, 16)) return st;
+  }
   if (pl.splits > 1) {
     p.counters = static_cast<unsigned*>(r.workspace);
     p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(r.workspace) + pl.counter_bytes);

@@ -44,6 +44,9 @@ constexpr int kGemvTiles = 2;   // m16 tiles per warp (32 weight rows)
 constexpr int kMaxRopeHalf = 128;
 
 struct GemvParams {
+  // TMA descriptors of weight set 0 and 1 ([rows][K*bits/8] bytes, 16x128 B boxes)
+  alignas(64) CUtensorMap tmap0;
+  alignas(64) CUtensorMap tmap1;
   // activations [M][ldx] (bf16 or fp16)
   const void* x;
   int ldx;

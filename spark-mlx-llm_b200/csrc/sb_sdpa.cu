@@ -32,11 +32,12 @@ constexpr int kSdpaWarps = 4;
 constexpr int kSdpaD = 128;
 constexpr int kPartStride = kSdpaD + 4;  // O[D], then m, l
 constexpr int kSdpaStages = 4;           // 16-token blocks in flight per warp
-constexpr int kSdpaPitch = 144;          // smem row pitch (bank-conflict-free reads)
-constexpr int kSdpaStageBytes = 2 * 16 * kSdpaPitch;
-constexpr size_t kSdpaSmem = 128 + static_cast<size_t>(kSdpaWarps) * kSdpaStages * kSdpaStageBytes;
+constexpr int kSdpaStageBytes = 2 * 16 * kSdpaD;  // swizzled K box + V box
+constexpr size_t kSdpaSmem = 2048 + static_cast<size_t>(kSdpaWarps) * kSdpaStages * kSdpaStageBytes;
 
 struct SdpaParams {
+  alignas(64) CUtensorMap kmap;  // K cache as [B*KH*cap rows][128 B], 16-row boxes, 128-B swizzle
+  alignas(64) CUtensorMap vmap;
   const __nv_bfloat16* q;  // [B, H, D]
   const int8_t* k;         // [B*KH, cap, D]
   const __half* ks;        // [B*KH, cap]
@@ -69,8 +70,6 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
   const int blk_begin = static_cast<int>((static_cast<long long>(nblk) * split) / p.splits);
   const int blk_end = static_cast<int>((static_cast<long long>(nblk) * (split + 1)) / p.splits);
   const size_t kv_base = static_cast<size_t>(bkv) * p.capacity;
-  const int8_t* kbase = p.k + kv_base * kSdpaD;
-  const int8_t* vbase = p.v + kv_base * kSdpaD;
   const __half* ksb = p.ks + kv_base;
   const __half* vsb = p.vs + kv_base;
 
@@ -129,32 +128,28 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
     for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
   constexpr uint32_t kOnes = 0x3C003C00u;
 
-  // ---- per-warp ring of 16-token K/V blocks in shared memory (bulk copies)
-  extern __shared__ __align__(128) uint8_t smem_raw[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem_raw) + warp * kSdpaStages;
-  uint8_t* ring = smem_raw + 128 + warp * kSdpaStages * kSdpaStageBytes;
+  // ---- per-warp ring of 16-token K/V blocks in shared memory (TMA boxes)
+  extern __shared__ uint8_t smem_dyn[];
+  uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase) + warp * kSdpaStages;
+  uint8_t* ring = sbase + 1024 + warp * kSdpaStages * kSdpaStageBytes;
   const int nb = blk_end - blk_begin;
   const int my_blocks = nb > warp ? (nb - warp + kSdpaWarps - 1) / kSdpaWarps : 0;
   auto block_of = [&](int i) { return blk_begin + warp + i * kSdpaWarps; };
   auto issue = [&](int i) {
     const int slot = i % kSdpaStages;
-    const int tb = block_of(i) * 16;
-    const int rows = min(16, N - tb);
-    if (lane == 0) mbar_arrive_expect_tx(bars + slot, static_cast<uint32_t>(rows) * 2 * kSdpaD);
-    __syncwarp();
-    const int r = lane & 15;
-    if (r < rows) {
-      const int8_t* src = (lane < 16 ? kbase : vbase) + static_cast<size_t>(tb + r) * kSdpaD;
-      uint8_t* dst = ring + slot * kSdpaStageBytes + (lane < 16 ? 0 : 16 * kSdpaPitch) + r * kSdpaPitch;
-      bulk_copy_g2s(dst, src, kSdpaD, bars + slot);
-    }
+    const int row = static_cast<int>(kv_base) + block_of(i) * 16;
+    uint8_t* dst = ring + slot * kSdpaStageBytes;
+    mbar_arrive_expect_tx(bars + slot, kSdpaStageBytes);
+    tma_load_2d(dst, &p.kmap, 0, row, bars + slot);
+    tma_load_2d(dst + 16 * kSdpaD, &p.vmap, 0, row, bars + slot);
   };
-  if (lane < kSdpaStages) mbar_init(bars + lane, 1);
-  mbar_fence_init();
+  if (lane == 0) {
+    for (int i = 0; i < kSdpaStages; ++i) mbar_init(bars + i, 1);
+    mbar_fence_init();
+    for (int i = 0; i < kSdpaStages && i < my_blocks; ++i) issue(i);
+  }
   __syncwarp();
-#pragma unroll
-  for (int i = 0; i < kSdpaStages; ++i)
-    if (i < my_blocks) issue(i);
 
   // scales of this lane's 4 tokens, one block ahead
   float sk[4], sv[4], skn[4], svn[4];
@@ -180,16 +175,15 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
       break;
     }
     const uint8_t* kst = ring + slot * kSdpaStageBytes;
-    const uint8_t* vst = kst + 16 * kSdpaPitch;
+    const uint8_t* vst = kst + 16 * kSdpaD;
     const int vt[4] = {tb + 2 * t, tb + 2 * t + 1, tb + 2 * t + 8, tb + 2 * t + 9};
 
     // QK^T: C[u] rows = heads, cols = tokens 8u + (2t, 2t+1); K row (8u + g), bytes 32t..32t+31
     float cqk[2][4];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const uint8_t* kp = kst + (8 * u + g) * kSdpaPitch + 32 * t;
-      const uint4 ka = *reinterpret_cast<const uint4*>(kp);
-      const uint4 kb = *reinterpret_cast<const uint4*>(kp + 16);
+      const uint4 ka = *reinterpret_cast<const uint4*>(swz128(kst, 8 * u + g, 32 * t));
+      const uint4 kb = *reinterpret_cast<const uint4*>(swz128(kst, 8 * u + g, 32 * t + 16));
       const uint32_t kw[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) cqk[u][e] = 0.f;
@@ -235,10 +229,10 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
     ap[3] = 0u;
     mma_16816<true>(psum, ap, kOnes, kOnes);
     // P'V: n-tile j covers d = 16n + j; the lane's B column n = g reads bytes 16g..16g+15
-    const uint4 vr0 = *reinterpret_cast<const uint4*>(vst + (2 * t) * kSdpaPitch + 16 * g);
-    const uint4 vr1 = *reinterpret_cast<const uint4*>(vst + (2 * t + 1) * kSdpaPitch + 16 * g);
-    const uint4 vr2 = *reinterpret_cast<const uint4*>(vst + (2 * t + 8) * kSdpaPitch + 16 * g);
-    const uint4 vr3 = *reinterpret_cast<const uint4*>(vst + (2 * t + 9) * kSdpaPitch + 16 * g);
+    const uint4 vr0 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t, 16 * g));
+    const uint4 vr1 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t + 1, 16 * g));
+    const uint4 vr2 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t + 8, 16 * g));
+    const uint4 vr3 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t + 9, 16 * g));
     const uint32_t va[4] = {vr0.x, vr0.y, vr0.z, vr0.w}, vb[4] = {vr1.x, vr1.y, vr1.z, vr1.w};
     const uint32_t vc[4] = {vr2.x, vr2.y, vr2.z, vr2.w}, vd[4] = {vr3.x, vr3.y, vr3.z, vr3.w};
 #pragma unroll
@@ -255,8 +249,8 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
       sk[j] = skn[j];
       sv[j] = svn[j];
     }
-    if (i + kSdpaStages < my_blocks) {
-      __syncwarp();
+    __syncwarp();
+    if (i + kSdpaStages < my_blocks && lane == 0) {
       fence_proxy_async_smem();
       issue(i + kSdpaStages);
     }
@@ -415,6 +409,12 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   p.capacity = static_cast<int>(capacity);
   p.splits = splits;
   p.length_dev = length_dev;
+  {
+    const uint64_t rows = static_cast<uint64_t>(bkv) * static_cast<uint64_t>(capacity);
+    if (rows >= (1ULL << 31)) return fail(SB_EINVAL, "KV cache too large for 32-bit TMA row coordinates");
+    if (int st = make_tmap_rows(&p.kmap, k, rows, kSdpaD, 16)) return st;
+    if (int st = make_tmap_rows(&p.vmap, v, rows, kSdpaD, 16)) return st;
+  }
   p.length_offset = length_offset;
   p.scale_log2e = scale * 1.4426950408889634f;
   if (splits > 1) {
