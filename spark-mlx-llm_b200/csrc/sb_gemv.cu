@@ -520,18 +520,34 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
-    for (int s = 0; s < p.splits; ++s) {
-      const float* ps = p.partial + (static_cast<size_t>(s) * p.rows_padded + rb * 32) * 8;
+    // partial sums in a fixed split order; 8 splits of loads in flight at a time
+    if (2 * t < mcols) {
+      for (int s0 = 0; s0 < p.splits; s0 += 8) {
+        float2 v[8][kGemvTiles][2];
 #pragma unroll
-      for (int r = 0; r < kGemvTiles; ++r)
+        for (int j = 0; j < 8; ++j) {
+          if (s0 + j < p.splits) {
+            const float* ps = p.partial + (static_cast<size_t>(s0 + j) * p.rows_padded + rb * 32) * 8;
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          if (2 * t < mcols) {
-            const float2 v = __ldcg(reinterpret_cast<const float2*>(ps + (r * 16 + h * 8 + g) * 8 + 2 * t));
-            acc[r][2 * h] += v.x;
-            acc[r][2 * h + 1] += v.y;
+            for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                v[j][r][h] = __ldcg(reinterpret_cast<const float2*>(ps + (r * 16 + h * 8 + g) * 8 + 2 * t));
           }
         }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (s0 + j < p.splits) {
+#pragma unroll
+            for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                acc[r][2 * h] += v[j][r][h].x;
+                acc[r][2 * h + 1] += v[j][r][h].y;
+              }
+          }
+        }
+      }
     }
     if (lane == 0) p.counters[rb] = 0u;
   }

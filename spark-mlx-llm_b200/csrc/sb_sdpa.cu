@@ -32,6 +32,7 @@ constexpr int kSdpaWarps = 4;
 constexpr int kSdpaD = 128;
 constexpr int kPartStride = kSdpaD + 4;  // O[D], then m, l
 constexpr int kSdpaStages = 4;           // 16-token blocks in flight per warp
+constexpr int kMaxSplits = 64;           // token splits per (batch, kv head)
 constexpr int kSdpaStageBytes = 2 * 16 * kSdpaD;  // swizzled K box + V box
 constexpr size_t kSdpaSmem = 2048 + static_cast<size_t>(kSdpaWarps) * kSdpaStages * kSdpaStageBytes;
 
@@ -320,23 +321,40 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
   if (s_prev != static_cast<unsigned>(p.splits - 1)) return;
   __threadfence();
   const float* all = p.partial + static_cast<size_t>(bkv) * p.splits * G * kPartStride;
+  // merge the CTAs' partials in split order: stage (m, l) in shared memory,
+  // per-split weights exp2(m_s - M), then O = sum_s w_s * O_s with loads batched
+  __shared__ float s_mw[kMaxSplits][8], s_ls[kMaxSplits][8], s_norm[8];
+  for (int idx = threadIdx.x; idx < p.splits * G; idx += kSdpaWarps * 32) {
+    const int s = idx / G, hh = idx % G;
+    s_mw[s][hh] = __ldcg(all + (s * G + hh) * kPartStride + kSdpaD);
+    s_ls[s][hh] = __ldcg(all + (s * G + hh) * kPartStride + kSdpaD + 1);
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int hh = threadIdx.x;
+    float mm = -INFINITY;
+    for (int s = 0; s < p.splits; ++s) mm = fmaxf(mm, s_mw[s][hh]);
+    float ll = 0.f;
+    for (int s = 0; s < p.splits; ++s) {
+      const float w = (mm == -INFINITY || s_mw[s][hh] == -INFINITY) ? 0.f : exp2f(s_mw[s][hh] - mm);
+      s_mw[s][hh] = w;
+      ll += s_ls[s][hh] * w;
+    }
+    s_norm[hh] = ll > 0.f ? 1.0f / ll : 0.f;
+  }
+  __syncthreads();
   for (int idx = threadIdx.x; idx < G * kSdpaD; idx += kSdpaWarps * 32) {
     const int hh = idx / kSdpaD, d = idx % kSdpaD;
-    float mm = -INFINITY;
-    for (int s = 0; s < p.splits; ++s) mm = fmaxf(mm, __ldcg(all + (s * G + hh) * kPartStride + kSdpaD));
-    float ll = 0.f, oo = 0.f;
-    if (mm != -INFINITY) {
-      for (int s = 0; s < p.splits; ++s) {
-        const float* ps = all + (s * G + hh) * kPartStride;
-        const float ms = __ldcg(ps + kSdpaD);
-        if (ms == -INFINITY) continue;
-        const float f = exp2f(ms - mm);
-        ll += __ldcg(ps + kSdpaD + 1) * f;
-        oo += __ldcg(ps + d) * f;
-      }
+    float oo = 0.f;
+    for (int s0 = 0; s0 < p.splits; s0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = s0 + j < p.splits ? __ldcg(all + ((s0 + j) * G + hh) * kPartStride + d) : 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (s0 + j < p.splits) oo += v[j] * s_mw[s0 + j][hh];
     }
-    const float o = ll > 0.f ? oo / ll : 0.f;
-    p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] = __float2bfloat16_rn(o);
+    p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] = __float2bfloat16_rn(oo * s_norm[hh]);
   }
   if (threadIdx.x == 0) p.counters[bkv] = 0u;
 }
@@ -389,6 +407,7 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
               15) == 0,
              "q, k and v must be 16-byte aligned");
   int splits = force_splits > 0 ? force_splits : sdpa_splits(batch, num_kv_heads, length);
+  SB_REQUIRE(splits <= kMaxSplits, "at most 64 token splits");
   const int64_t bkv = batch * num_kv_heads;
   const size_t counters = kCounterBytes;
   if (bkv > kMaxCounters) force_splits = 1;
