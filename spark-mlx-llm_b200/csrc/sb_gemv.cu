@@ -171,11 +171,11 @@ template <int kBits>
 struct StageGeom {
   static constexpr int kRowBytes = 128;                  // bytes of one weight row per stage
   static constexpr int kStageK = kRowBytes * 8 / kBits;  // K values per stage
-  static constexpr int kStages = kBits == 4 ? 5 : 4;     // ring depth per warp
+  static constexpr int kStages = 4;                      // ring depth per warp
   static constexpr int kStageBytes = 32 * kRowBytes;     // two 16-row boxes
 };
 
-template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
+template <typename TA, int WF, int KC, int GC, int EPI, bool NORM, int MC>
 __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
   using F = Fmt<TA, WF>;
   using SG = StageGeom<F::kBits>;
@@ -190,7 +190,12 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
   constexpr int kChunkRowBytes = KC * F::kBits / 8;
   constexpr int kLaneBytes = V * F::kBits / 8;
   constexpr int kChunksPerStage = SG::kStageK / KC;
-  constexpr int kGroupsPerStage = kAffine ? kChunksPerStage / GC : 0;
+  // The MMA's 8 n-columns carry (activation column m, group slot) pairs:
+  // column n -> m = n % MC, slot = n / MC. An affine "super-group" of kSlots
+  // consecutive groups accumulates in separate columns; its scales are applied
+  // once at its end. Non-affine formats use one slot (columns = activation rows).
+  constexpr int kSlots = kAffine ? 8 / MC : 1;
+  constexpr int kSuperChunks = kSlots * GC;
   static_assert(!kAffine || kChunksPerStage % GC == 0, "a stage holds whole groups");
 
   extern __shared__ uint8_t smem_dyn[];
@@ -207,6 +212,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
   const int rb = blockIdx.x * kGemvWarps + warp;
   const bool active = rb < rowblocks;
   const int rbc = min(rb, rowblocks - 1);
+  const int mcols = p.M;
 
   // K range of this split, in whole groups.
   const int grp_begin = static_cast<int>((static_cast<long long>(p.groups_total) * split) / p.splits);
@@ -214,15 +220,17 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
   const int k_begin = grp_begin * kGroupK;
   const int k_count = (grp_end - grp_begin) * kGroupK;
   const int nstages = (k_count + SG::kStageK - 1) / SG::kStageK;
+  const int nchunks = k_count / KC;
   const int kbyte0 = k_begin * F::kBits / 8;
 
-  // ---- shared memory: barriers, per-warp weight rings (1 KB aligned), x segment
+  // ---- shared memory: barriers, per-warp weight rings (1 KB aligned), x segment, x group sums
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base) + warp * SG::kStages;
   uint8_t* ring = base + 1024 + (warp * SG::kStages) * SG::kStageBytes;
   TA* xs = reinterpret_cast<TA*>(base + 1024 + kGemvWarps * SG::kStages * SG::kStageBytes);
-  const int mcols = p.M;
   const int xs_ld = p.x_seg + 8;
+  float* xgs = reinterpret_cast<float*>(xs + mcols * xs_ld);  // [M][x_seg / kGroupK]
+  const int xg_ld = p.x_seg / kGroupK;
   const int rowA = box_row0<EPI>(p, rbc, 0), rowB = box_row0<EPI>(p, rbc, 1);
 
   auto issue_stage = [&](int st) {
@@ -283,51 +291,51 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     }
   }
 
+  // B-operand column of this lane: activation column bm, group slot bslot
+  const int bm = g % MC;
+  const int bslot = g / MC;
+  const bool b_live = bm < mcols && (kAffine || bslot == 0);
+
   constexpr uint32_t kOnes = ActTraits<TA>::kOnes;
-  float acc[kGemvTiles][4];
   float cacc[kGemvTiles][F::kPlanes][4];
   float xsum[4];
+  float res[kGemvTiles][2][2];  // [tile][h][e] affine results per (row, column)
 #pragma unroll
   for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      acc[r][e] = 0.f;
 #pragma unroll
       for (int pl = 0; pl < F::kPlanes; ++pl) cacc[r][pl][e] = 0.f;
+      res[r][e >> 1][e & 1] = 0.f;
     }
 #pragma unroll
   for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
 
-  // scale/bias of the row q == t (tile t >> 1, box t & 1), one stage ahead in registers
-  const TA* srow = nullptr;
-  const TA* brow = nullptr;
-  uint32_t sb_cur[kGroupsPerStage > 0 ? kGroupsPerStage : 1];
-  uint32_t sb_nxt[kGroupsPerStage > 0 ? kGroupsPerStage : 1];
-  auto load_sb = [&](int st, uint32_t* dst) {
+  // scale/bias of this lane's rows (tile r, box h) for its two columns' groups
+  auto row_of = [&](int r, int h) { return min((h ? rowB : rowA) + 8 * r + sg, p.N - 1); };
+  auto set_of = [&](int h) { return (EPI == EPI_SWIGLU) ? h : 0; };
+  uint32_t sbv[kGemvTiles][2][2];  // packed (scale, bias) for [tile][h][e]
+  auto load_super_scales = [&](int grp0) {
     if constexpr (kAffine) {
-      const int g0 = (k_begin + st * SG::kStageK) / p.group_size;
-      const int gn = (min(SG::kStageK, k_count - st * SG::kStageK)) / p.group_size;
+      const int gpr = p.K / p.group_size;
 #pragma unroll
-      for (int i = 0; i < kGroupsPerStage; ++i) {
-        if (i < gn) {
-          const uint16_t s = *reinterpret_cast<const uint16_t*>(srow + g0 + i);
-          const uint16_t b = *reinterpret_cast<const uint16_t*>(brow + g0 + i);
-          dst[i] = static_cast<uint32_t>(s) | (static_cast<uint32_t>(b) << 16);
-        }
-      }
+      for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int grp = min(grp0 + (2 * t + e) / MC, grp_end - 1);
+            const size_t idx = static_cast<size_t>(row_of(r, h)) * gpr + grp;
+            const uint16_t s = *reinterpret_cast<const uint16_t*>(static_cast<const TA*>(set_of(h) ? p.s1 : p.s0) + idx);
+            const uint16_t b = *reinterpret_cast<const uint16_t*>(static_cast<const TA*>(set_of(h) ? p.b1 : p.b0) + idx);
+            sbv[r][h][e] = static_cast<uint32_t>(s) | (static_cast<uint32_t>(b) << 16);
+          }
     }
   };
-  if constexpr (kAffine) {
-    const int my_h = t & 1;
-    const int my_row = min((my_h ? rowB : rowA) + 8 * (t >> 1) + sg, p.N - 1);
-    const int set = (EPI == EPI_SWIGLU) ? my_h : 0;
-    const int gpr = p.K / p.group_size;
-    srow = static_cast<const TA*>(set ? p.s1 : p.s0) + static_cast<size_t>(my_row) * gpr;
-    brow = static_cast<const TA*>(set ? p.b1 : p.b0) + static_cast<size_t>(my_row) * gpr;
-    if (active && nstages > 0) load_sb(0, sb_cur);
-  }
+  if (active && nchunks > 0) load_super_scales(grp_begin);
 
   bool failed = false;
+  int chunk = 0;  // chunk index inside the split
   for (int st = 0; st < nstages; ++st) {
     // ---- activation segment staging (all warps of the CTA take part)
     const int kst = st * SG::kStageK;  // offset inside the split
@@ -351,13 +359,22 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
         }
         *reinterpret_cast<uint4*>(xs + m * xs_ld + v8 * 8) = v;
       }
+      if constexpr (kAffine) {
+        __syncthreads();
+        // per-group sums of the staged activations (fixed order)
+        const int ng = seg_len / kGroupK;
+        for (int idx = threadIdx.x; idx < mcols * ng; idx += kGemvWarps * 32) {
+          const int m = idx / ng, gi = idx % ng;
+          const TA* xp = xs + m * xs_ld + gi * kGroupK;
+          float sum = 0.f;
+          for (int i = 0; i < kGroupK; ++i) sum += to_float(xp[i]);
+          xgs[m * xg_ld + gi] = sum;
+        }
+      }
       __syncthreads();
     }
     if (!active || failed) continue;
 
-    if constexpr (kAffine) {
-      if (st + 1 < nstages) load_sb(st + 1, sb_nxt);
-    }
     const int slot = st % SG::kStages;
     if (!mbar_wait_bounded(bars + slot, (st / SG::kStages) & 1)) {
       failed = true;
@@ -365,7 +382,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     }
     const uint8_t* stage = ring + slot * SG::kStageBytes;
     const int chunks = min(kChunksPerStage, (k_count - kst) / KC);
-    const TA* xbase = xs + min(g, mcols - 1) * xs_ld + (kst % p.x_seg) + t * V;
+    const TA* xbase = xs + min(bm, mcols - 1) * xs_ld + (kst % p.x_seg) + t * V;
 #pragma unroll
     for (int cc = 0; cc < kChunksPerStage; ++cc) {
       if (cc < chunks) {
@@ -395,17 +412,25 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
         uint32_t lo[kRows][kPairs], hi[kRows][kPairs];
 #pragma unroll
         for (int q = 0; q < kRows; ++q) dequant_pairs<TA, WF, kWords, kPairs>(wv[q], lo[q], hi[q]);
-        uint32_t xw[kXWords];
-#pragma unroll
-        for (int i = 0; i < kXWords; i += 4) {
-          const uint4 v = *reinterpret_cast<const uint4*>(xbase + cc * KC + 2 * i);
-          xw[i] = v.x;
-          xw[i + 1] = v.y;
-          xw[i + 2] = v.z;
-          xw[i + 3] = v.w;
-        }
+        // B operand: this lane's column feeds only the group of its slot
+        const int gslot = (chunk / GC) % kSlots;
+        const bool feed = b_live && (bslot == gslot);
         uint32_t xpair[kPairs];
-        x_pairs<WF, kXWords, kPairs>(xw, xpair);
+        if (feed) {
+          uint32_t xw[kXWords];
+#pragma unroll
+          for (int i = 0; i < kXWords; i += 4) {
+            const uint4 v = *reinterpret_cast<const uint4*>(xbase + cc * KC + 2 * i);
+            xw[i] = v.x;
+            xw[i + 1] = v.y;
+            xw[i + 2] = v.z;
+            xw[i + 3] = v.w;
+          }
+          x_pairs<WF, kXWords, kPairs>(xw, xpair);
+        } else {
+#pragma unroll
+          for (int i = 0; i < kPairs; ++i) xpair[i] = 0u;
+        }
 #pragma unroll
         for (int j = 0; j < kMma; ++j) {
           const uint32_t b0 = xpair[2 * j], b1 = xpair[2 * j + 1];
@@ -420,48 +445,57 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
               mma_16816<F::kHalf>(cacc[r][1], a_hi, b0, b1);
             }
           }
-          if constexpr (WF != W_BF16) {
+          if constexpr (WF == W_I8PC) {
             const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
             mma_16816<F::kHalf>(xsum, ones, b0, b1);
           }
         }
+        ++chunk;
         if constexpr (kAffine) {
-          if ((cc + 1) % GC == 0) {
-            // group epilogue: acc += scale * sum(code*x) + bias * sum(x)
-            const uint32_t sbv = sb_cur[cc / GC];
+          if (chunk % kSuperChunks == 0 || chunk == nchunks) {
+            // super-group epilogue: res += scale * sum(code*x) + (bias - offset*scale) * sum(x)
+            const int grp0 = grp_begin + (chunk - 1) / kSuperChunks * kSlots;
 #pragma unroll
-            for (int r = 0; r < kGemvTiles; ++r) {
+            for (int e = 0; e < 2; ++e) {
+              const int n = 2 * t + e;
+              const int grp = grp0 + n / MC;
+              const int m = n % MC;
+              const bool ok = grp < grp_end && m < mcols;
+              float xg = 0.f;
+              if (ok) {
+                const int k_in_seg = (grp - grp_begin) * kGroupK - (kst / p.x_seg) * p.x_seg;
+                xg = xgs[m * xg_ld + k_in_seg / kGroupK];
+              }
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const uint32_t v = __shfl_sync(0xffffffffu, sbv, (lane & ~3) | (2 * r + h));
-                float s, b;
-                if constexpr (ActTraits<TA>::kHalf) {
-                  s = __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
-                  b = __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
-                } else {
-                  s = bf16_lo(v);
-                  b = bf16_hi(v);
-                }
-                const float bb = fmaf(-F::kCodeOffset, s, b);
+              for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
-                for (int e = 0; e < 2; ++e) {
+                for (int h = 0; h < 2; ++h) {
+                  const uint32_t v = sbv[r][h][e];
+                  float s, b;
+                  if constexpr (ActTraits<TA>::kHalf) {
+                    s = __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
+                    b = __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
+                  } else {
+                    s = bf16_lo(v);
+                    b = bf16_hi(v);
+                  }
                   float d = cacc[r][0][2 * h + e];
                   if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][2 * h + e], d);
-                  acc[r][2 * h + e] = fmaf(s, d, fmaf(bb, xsum[e], acc[r][2 * h + e]));
-                  cacc[r][0][2 * h + e] = 0.f;
-                  if constexpr (F::kPlanes == 2) cacc[r][1][2 * h + e] = 0.f;
+                  const float bb = fmaf(-F::kCodeOffset, s, b);
+                  res[r][h][e] = ok ? fmaf(s, d, fmaf(bb, xg, res[r][h][e])) : res[r][h][e];
                 }
-              }
             }
 #pragma unroll
-            for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
+            for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                cacc[r][0][e] = 0.f;
+                if constexpr (F::kPlanes == 2) cacc[r][1][e] = 0.f;
+              }
+            if (chunk < nchunks) load_super_scales(grp0 + kSlots);
           }
         }
       }
-    }
-    if constexpr (kAffine) {
-#pragma unroll
-      for (int i = 0; i < kGroupsPerStage; ++i) sb_cur[i] = sb_nxt[i];
     }
     // refill this slot with the stage kStages ahead
     __syncwarp();
@@ -478,22 +512,51 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
       mbar_wait_bounded(bars + st % SG::kStages, (st / SG::kStages) & 1);
     return;
   }
-  if constexpr (WF == W_I8PC) {
-    // signed value = unsigned code - 128:  sum(s8*x) = C - (offset + 128) * sum(x)
+
+  // ---- per-lane results: value[r][h][e] for activation column m = 2t + e
+  // (after reducing the lanes that hold other group slots of the same column)
+  float val[kGemvTiles][2][2];
+  if constexpr (kAffine) {
 #pragma unroll
     for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float d = cacc[r][0][e];
-        if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][e], d);
-        acc[r][e] = fmaf(-(F::kCodeOffset + 128.0f), xsum[e & 1], d);
+      for (int h = 0; h < 2; ++h) {
+        if constexpr (MC == 1) {
+          float v = res[r][h][0] + res[r][h][1];
+          v += __shfl_xor_sync(0xffffffffu, v, 1);
+          v += __shfl_xor_sync(0xffffffffu, v, 2);
+          val[r][h][0] = v;
+          val[r][h][1] = 0.f;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float v = res[r][h][e];
+            if constexpr (MC == 2) {
+              v += __shfl_xor_sync(0xffffffffu, v, 1);
+              v += __shfl_xor_sync(0xffffffffu, v, 2);
+            } else if constexpr (MC == 4) {
+              v += __shfl_xor_sync(0xffffffffu, v, 2);
+            }
+            val[r][h][e] = v;
+          }
+        }
       }
-  } else if constexpr (WF == W_BF16) {
+  } else {
 #pragma unroll
     for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[r][e] = cacc[r][0][e];
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float d = cacc[r][0][2 * h + e];
+          if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][2 * h + e], d);
+          if constexpr (WF == W_I8PC) d = fmaf(-(F::kCodeOffset + 128.0f), xsum[e], d);
+          val[r][h][e] = d;
+        }
   }
+  // owner lanes: t < MC/2 (MC == 1: t == 0, e == 0); column m = 2t + e
+  const bool owner = (MC == 1) ? (t == 0) : (2 * t < MC);
+  auto col_ok = [&](int e) { return owner && (MC == 1 ? e == 0 : true) && (2 * t + e) < mcols; };
 
   grid_dependency_launch();
 
@@ -503,12 +566,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
 #pragma unroll
     for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if (2 * t < mcols) {
-          float2 v = make_float2(acc[r][2 * h], acc[r][2 * h + 1]);
-          *reinterpret_cast<float2*>(part + (r * 16 + h * 8 + g) * 8 + 2 * t) = v;
-        }
-      }
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          if (col_ok(e)) part[(r * 16 + h * 8 + g) * 8 + 2 * t + e] = val[r][h][e];
     __threadfence();
     __syncwarp();
     unsigned prev = 0;
@@ -519,41 +580,38 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
 #pragma unroll
     for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[r][e] = 0.f;
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) val[r][h][e] = 0.f;
     // partial sums in a fixed split order; 8 splits of loads in flight at a time
-    if (2 * t < mcols) {
-      for (int s0 = 0; s0 < p.splits; s0 += 8) {
-        float2 v[8][kGemvTiles][2];
+    for (int s0 = 0; s0 < p.splits; s0 += 8) {
+      float v[8][kGemvTiles][2][2];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (s0 + j < p.splits) {
-            const float* ps = p.partial + (static_cast<size_t>(s0 + j) * p.rows_padded + rb * 32) * 8;
+      for (int j = 0; j < 8; ++j) {
+        const float* ps = p.partial + (static_cast<size_t>(s0 + j) * p.rows_padded + rb * 32) * 8;
 #pragma unroll
-            for (int r = 0; r < kGemvTiles; ++r)
+        for (int r = 0; r < kGemvTiles; ++r)
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
-                v[j][r][h] = __ldcg(reinterpret_cast<const float2*>(ps + (r * 16 + h * 8 + g) * 8 + 2 * t));
-          }
-        }
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          if (s0 + j < p.splits) {
-#pragma unroll
-            for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                acc[r][2 * h] += v[j][r][h].x;
-                acc[r][2 * h + 1] += v[j][r][h].y;
-              }
-          }
-        }
+            for (int e = 0; e < 2; ++e)
+              v[j][r][h][e] = (s0 + j < p.splits && col_ok(e)) ? __ldcg(ps + (r * 16 + h * 8 + g) * 8 + 2 * t + e) : 0.f;
       }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+#pragma unroll
+        for (int r = 0; r < kGemvTiles; ++r)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) val[r][h][e] += v[j][r][h][e];
     }
     if (lane == 0) p.counters[rb] = 0u;
   }
 
   // ---- final epilogue: (tile r, box h) of this lane is weight row box_row0(h) + 8r + sigma(g)
   if constexpr (EPI == EPI_ARGMAX) {
+    // per column m = 2t + e: best (value, row) over this lane's rows, then over g
     float best[2] = {-INFINITY, -INFINITY};
     int best_i[2] = {0x7FFFFFFF, 0x7FFFFFFF};
 #pragma unroll
@@ -564,7 +622,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
         if (row >= p.N) continue;
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const float v = acc[r][2 * h + e];
+          const float v = val[r][h][e];
           if (v > best[e] || (v == best[e] && row < best_i[e])) {
             best[e] = v;
             best_i[e] = row;
@@ -586,9 +644,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     if (g == 0) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        const int m = 2 * t + e;
-        if (m < mcols && best_i[e] != 0x7FFFFFFF)
-          atomicMax(p.argmax_keys + m, argmax_key(best[e], best_i[e] + p.argmax_offset));
+        if (col_ok(e) && best_i[e] != 0x7FFFFFFF)
+          atomicMax(p.argmax_keys + 2 * t + e, argmax_key(best[e], best_i[e] + p.argmax_offset));
       }
     }
     return;
@@ -596,20 +653,16 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     float scale_pc[kRows];
     if constexpr (WF == W_I8PC) {
 #pragma unroll
-      for (int q = 0; q < kRows; ++q) {
-        const int h = q & 1;
-        const int row = min((h ? rowB : rowA) + 8 * (q >> 1) + sg, p.N - 1);
-        const int set = (EPI == EPI_SWIGLU) ? h : 0;
-        scale_pc[q] = static_cast<const float*>(set ? p.s1 : p.s0)[row];
-      }
+      for (int q = 0; q < kRows; ++q)
+        scale_pc[q] = static_cast<const float*>(set_of(q & 1) ? p.s1 : p.s0)[row_of(q >> 1, q & 1)];
     }
 #pragma unroll
     for (int r = 0; r < kGemvTiles; ++r) {
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
+        if (!col_ok(e)) continue;
         const int m = 2 * t + e;
-        if (m >= mcols) continue;
-        float v_lo = acc[r][e], v_hi = acc[r][2 + e];
+        float v_lo = val[r][0][e], v_hi = val[r][1][e];
         if constexpr (WF == W_I8PC) {
           v_lo *= scale_pc[2 * r];
           v_hi *= scale_pc[2 * r + 1];
@@ -663,8 +716,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
             const float v = h ? v_hi : v_lo;
             const size_t idx = static_cast<size_t>(m) * p.ldy + row;
             if constexpr (EPI == EPI_RESID) {
-              const float res = load_act<TA>(p.residual, static_cast<size_t>(m) * p.ldr + row);
-              store_act<TA>(p.y, idx, res + round_act<TA>(v));
+              const float res_v = load_act<TA>(p.residual, static_cast<size_t>(m) * p.ldr + row);
+              store_act<TA>(p.y, idx, res_v + round_act<TA>(v));
             } else {
               store_act<TA>(p.y, idx, v);
             }
@@ -694,45 +747,77 @@ int sm_count() {
 struct Plan {
   int tiles, rowblocks, groups, splits, k_group;
   size_t counter_bytes, partial_bytes;
+  void* workspace;
+  size_t workspace_bytes;
 };
 
+constexpr int kMaxGemvSplits = 32;
+
+// Row blocks and groups of a request; the split count is chosen at launch from
+// the kernel's occupancy. partial_bytes covers the largest split count allowed.
 Plan make_plan(int epi, int N, int K, int group_k, bool allow_split) {
   Plan pl{};
   pl.tiles = 0;
   pl.rowblocks = epi == EPI_SWIGLU ? (N + 15) / 16 : (epi == EPI_ROPE ? N / 32 : (N + 31) / 32);
   pl.k_group = group_k;
   pl.groups = K / group_k;
-  // Two CTAs of 4 warps per SM; split K only when the row blocks alone cannot
-  // fill that, keeping at least 2 groups per split.
-  const int target = sm_count() * 8;
-  int s = allow_split ? (target + pl.rowblocks - 1) / pl.rowblocks : 1;
-  s = std::min(s, std::max(1, pl.groups / 2));
-  s = std::min(s, pl.groups);
-  if (pl.rowblocks > kMaxCounters) s = 1;
-  pl.splits = std::max(1, s);
+  const int max_s = (allow_split && pl.rowblocks <= kMaxCounters) ? std::max(1, std::min(kMaxGemvSplits, pl.groups / 2)) : 1;
+  pl.splits = max_s;
   pl.counter_bytes = kCounterBytes;
-  pl.partial_bytes = pl.splits > 1
-                         ? static_cast<size_t>(pl.splits) * pl.rowblocks * 16 * kGemvTiles * 8 * sizeof(float)
-                         : 0;
+  pl.partial_bytes = max_s > 1 ? static_cast<size_t>(max_s) * pl.rowblocks * 32 * 8 * sizeof(float) : 0;
   return pl;
+}
+
+template <typename TA, int WF, int KC, int GC, int EPI, bool NORM, int MC>
+int launch_gemv_mc(GemvParams& p, const Plan& plan, cudaStream_t stream) {
+  using SG = StageGeom<Fmt<TA, WF>::kBits>;
+  constexpr bool kAff = (WF == W_AFF4 || WF == W_AFF8);
+  auto kernel = gemv_kernel<TA, WF, KC, GC, EPI, NORM, MC>;
+  // activation segment: at most 8 KB of shared memory, whole stages and whole
+  // super-groups (so a super-group's group sums are staged together)
+  const int super_k = kAff ? (8 / MC) * p.group_size : SG::kStageK;
+  const int unit = std::max(SG::kStageK, super_k);
+  auto smem_for = [&](int splits) {
+    const int max_kunit = (plan.groups + splits - 1) / splits * plan.k_group;
+    int seg = (8192 / (p.M * static_cast<int>(sizeof(TA)))) / unit * unit;
+    seg = std::max(seg, unit);
+    p.x_seg = std::min(seg, ((max_kunit + unit - 1) / unit) * unit);
+    const size_t xg_bytes = static_cast<size_t>(p.M) * (p.x_seg / plan.k_group + 1) * sizeof(float);
+    return 2048 + static_cast<size_t>(kGemvWarps) * SG::kStages * SG::kStageBytes +
+           static_cast<size_t>(p.M) * (p.x_seg + 8) * sizeof(TA) + xg_bytes;
+  };
+  size_t smem = smem_for(1);
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+      cudaSuccess)
+    return fail(SB_ECUDA, "gemv: shared memory opt-in failed");
+  // splits: fill the resident CTA slots in one wave (no tail wave)
+  int splits = 1;
+  const int ctas_per_split = (plan.rowblocks + kGemvWarps - 1) / kGemvWarps;
+  if (plan.splits > 1 && plan.workspace != nullptr &&
+      plan.workspace_bytes >= plan.counter_bytes + plan.partial_bytes) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kGemvWarps * 32, smem) != cudaSuccess || occ < 1)
+      occ = 1;
+    const int slots = sm_count() * occ;
+    splits = std::max(1, std::min(plan.splits, slots / ctas_per_split));
+  }
+  smem = smem_for(splits);
+  p.splits = splits;
+  p.groups_total = plan.groups;
+  p.rows_padded = plan.rowblocks * 32;
+  if (splits > 1) {
+    p.counters = static_cast<unsigned*>(plan.workspace);
+    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(plan.workspace) + plan.counter_bytes);
+  }
+  dim3 grid(ctas_per_split, splits);
+  return launch("gemv", kernel, grid, dim3(kGemvWarps * 32), smem, stream, p);
 }
 
 template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
 int launch_gemv(GemvParams& p, const Plan& pl, cudaStream_t stream) {
-  using SG = StageGeom<Fmt<TA, WF>::kBits>;
-  const int max_kunit = (pl.groups + pl.splits - 1) / pl.splits * pl.k_group;
-  // activation segment: at most 16 KB of shared memory, whole stages
-  int seg = (16384 / (p.M * static_cast<int>(sizeof(TA)))) / SG::kStageK * SG::kStageK;
-  seg = std::max(seg, SG::kStageK);
-  p.x_seg = std::min(seg, ((max_kunit + SG::kStageK - 1) / SG::kStageK) * SG::kStageK);
-  const size_t smem = 2048 + static_cast<size_t>(kGemvWarps) * SG::kStages * SG::kStageBytes +
-                      static_cast<size_t>(p.M) * (p.x_seg + 8) * sizeof(TA);
-  auto kernel = gemv_kernel<TA, WF, KC, GC, EPI, NORM>;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-      cudaSuccess)
-    return fail(SB_ECUDA, "gemv: shared memory opt-in failed");
-  dim3 grid((pl.rowblocks + kGemvWarps - 1) / kGemvWarps, pl.splits);
-  return launch("gemv", kernel, grid, dim3(kGemvWarps * 32), smem, stream, p);
+  if (p.M == 1) return launch_gemv_mc<TA, WF, KC, GC, EPI, NORM, 1>(p, pl, stream);
+  if (p.M <= 4) return launch_gemv_mc<TA, WF, KC, GC, EPI, NORM, 4>(p, pl, stream);
+  return launch_gemv_mc<TA, WF, KC, GC, EPI, NORM, 8>(p, pl, stream);
 }
 
 template <typename TA, int WF, int EPI, bool NORM>
@@ -755,24 +840,28 @@ int dispatch_group(GemvParams& p, const Plan& pl, cudaStream_t stream) {
 
 template <int EPI, bool NORM>
 int dispatch_fmt(int wf, int x_dtype, GemvParams& p, const Plan& pl, cudaStream_t stream) {
+  constexpr bool kAffineEpi = EPI != EPI_ARGMAX;
+  constexpr bool kI8Epi = EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_ROPE;
+  constexpr bool kBf16Epi = EPI == EPI_STORE || EPI == EPI_ARGMAX;
   if (x_dtype == SB_DTYPE_BF16) {
-    switch (wf) {
-      case W_AFF4: return dispatch_group<__nv_bfloat16, W_AFF4, EPI, NORM>(p, pl, stream);
-      case W_AFF8: return dispatch_group<__nv_bfloat16, W_AFF8, EPI, NORM>(p, pl, stream);
-      case W_I8PC: return dispatch_group<__nv_bfloat16, W_I8PC, EPI, NORM>(p, pl, stream);
-      case W_BF16: return dispatch_group<__nv_bfloat16, W_BF16, EPI, NORM>(p, pl, stream);
+    if constexpr (kAffineEpi) {
+      if (wf == W_AFF4) return dispatch_group<__nv_bfloat16, W_AFF4, EPI, NORM>(p, pl, stream);
+      if (wf == W_AFF8) return dispatch_group<__nv_bfloat16, W_AFF8, EPI, NORM>(p, pl, stream);
+    }
+    if constexpr (kI8Epi) {
+      if (wf == W_I8PC) return dispatch_group<__nv_bfloat16, W_I8PC, EPI, NORM>(p, pl, stream);
+    }
+    if constexpr (kBf16Epi) {
+      if (wf == W_BF16) return dispatch_group<__nv_bfloat16, W_BF16, EPI, NORM>(p, pl, stream);
     }
   } else if (x_dtype == SB_DTYPE_F16) {
     if constexpr (EPI == EPI_STORE || EPI == EPI_ROPE) {
-      switch (wf) {
-        case W_AFF4: return dispatch_group<__half, W_AFF4, EPI, NORM>(p, pl, stream);
-        case W_AFF8: return dispatch_group<__half, W_AFF8, EPI, NORM>(p, pl, stream);
-        case W_I8PC: return dispatch_group<__half, W_I8PC, EPI, NORM>(p, pl, stream);
-        default: break;
-      }
+      if (wf == W_AFF4) return dispatch_group<__half, W_AFF4, EPI, NORM>(p, pl, stream);
+      if (wf == W_AFF8) return dispatch_group<__half, W_AFF8, EPI, NORM>(p, pl, stream);
+      if (wf == W_I8PC) return dispatch_group<__half, W_I8PC, EPI, NORM>(p, pl, stream);
     }
   }
-  return fail(SB_EUNSUPPORTED, "unsupported activation dtype / weight format combination");
+  return fail(SB_EUNSUPPORTED, "unsupported activation dtype / weight format / epilogue combination");
 }
 
 }  // namespace
@@ -807,11 +896,8 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   if (r.epi == EPI_SWIGLU) SB_REQUIRE(r.N % 8 == 0, "SwiGLU width must be a multiple of 8");
 
   Plan pl = make_plan(r.epi, r.N, r.K, gk, true);
-  const size_t need = pl.counter_bytes + pl.partial_bytes;
-  if (pl.splits > 1 && (r.workspace == nullptr || r.workspace_bytes < need)) {
-    // Fall back to no split when the caller gave no workspace.
-    pl = make_plan(r.epi, r.N, r.K, gk, false);
-  }
+  pl.workspace = r.workspace;
+  pl.workspace_bytes = r.workspace_bytes;
 
   GemvParams p{};
   p.x = r.x;
@@ -826,7 +912,6 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   p.s1 = r.s1 ? r.s1 : r.s0;
   p.b1 = r.b1 ? r.b1 : r.b0;
   p.group_size = r.group_size;
-  p.splits = pl.splits;
   p.groups_total = pl.groups;
   p.rows_padded = pl.rowblocks * 32;
   {
@@ -834,10 +919,6 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
     const uint64_t row_bytes = static_cast<uint64_t>(r.K) * bits / 8;
     if (int st = make_tmap_rows(&p.tmap0, r.w0, static_cast<uint64_t>(r.N), row_bytes, 16)) return st;
     if (int st = make_tmap_rows(&p.tmap1, r.w1 ? r.w1 : r.w0, static_cast<uint64_t>(r.N), row_bytes, 16)) return st;
-  }
-  if (pl.splits > 1) {
-    p.counters = static_cast<unsigned*>(r.workspace);
-    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(r.workspace) + pl.counter_bytes);
   }
   if (r.workspace != nullptr && r.workspace_bytes >= kCounterBytes)
     p.status = static_cast<unsigned*>(r.workspace) + kStatusWord;
