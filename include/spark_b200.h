@@ -153,6 +153,29 @@ size_t sb_int8_sdpa_workspace_size(int64_t batch, int num_heads, int num_kv_head
                                    int64_t length, int head_dim);
 
 /*
+ * Same computation as sb_int8_sdpa_decode, for callers that cannot allocate
+ * device memory and so cannot supply a workspace: code that only receives
+ * input/output buffers from a host runtime or plugin host that owns all device
+ * memory, and latency-bound services that allocate nothing after start-up
+ * (cudaMalloc synchronizes the device). This entry point has no counterpart in
+ * the reference.
+ *   Scratch: a 4 MiB array inside the library (one per GPU that loads it, kept
+ *   until the process exits). Shapes whose split-K scratch
+ *   (sb_int8_sdpa_workspace_size) exceeds 4 MiB are rejected with SB_EINVAL.
+ *   The first call on a device looks up the array's device address
+ *   (cudaGetSymbolAddress) with that device current; make that first call
+ *   before any stream capture. Each call clears the array's counters on
+ *   `stream` before its kernel. All calls on a device share the one array:
+ *   calls that overlap on the GPU (different streams, no ordering) race and
+ *   must not be issued.
+ *   Arguments and layouts are those of sb_int8_sdpa_decode.
+ */
+int sb_int8_sdpa_decode_static(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                               const void* v_scale, void* out, int64_t batch, int num_heads,
+                               int num_kv_heads, int64_t length, int64_t capacity, int head_dim,
+                               float scale, void* stream);
+
+/*
  * RMSNorm, y = T(x * rsqrt(mean(x^2) + eps) * weight), fp32 statistics.
  * Replaces mx.fast.rms_norm as used by dispatch_ffn (spark_mlx_llm/ops/ffn.py:99)
  * and nn.RMSNorm (spark_mlx_llm/model.py:240-243).

@@ -23,6 +23,7 @@
 #include <algorithm>
 #include <cmath>
 #include <mutex>
+#include <string>
 
 #include "sb_common.cuh"
 
@@ -473,6 +474,65 @@ extern "C" int sb_int8_sdpa_decode(const void* q, const int8_t* k, const void* k
                                    size_t workspace_bytes, void* stream) {
   return sb::run_sdpa_int8(q, k, k_scale, v, v_scale, out, batch, num_heads, num_kv_heads, length, capacity,
                            head_dim, scale, workspace, workspace_bytes, sb::as_stream(stream), 0, nullptr, 0);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the split-K scratch (arrival counters, status word,
+// per-split partial results) lives in a file-scope device array instead of a
+// caller workspace. Every GPU that loads this library keeps the array until the
+// process exits.
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB per device
+static __device__ __align__(256) unsigned char g_sdpa_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_scratch_mutex;
+void* g_static_scratch_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array on the current device. The host-side name
+// g_sdpa_static_scratch is only a stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+int static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return sb::fail(SB_ECUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(err));
+  if (dev < 0 || dev >= kMaxDevices) return sb::fail(SB_EUNSUPPORTED, "device index out of range for the static scratch");
+  std::lock_guard<std::mutex> lock(g_static_scratch_mutex);
+  if (g_static_scratch_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_sdpa_static_scratch);
+    if (err != cudaSuccess || ptr == nullptr)
+      return sb::fail(SB_ECUDA, std::string("cudaGetSymbolAddress(static scratch): ") + cudaGetErrorString(err));
+    g_static_scratch_ptr[dev] = ptr;
+  }
+  *out = g_static_scratch_ptr[dev];
+  return SB_OK;
+}
+
+}  // namespace
+
+extern "C" int sb_int8_sdpa_decode_static(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                                          const void* v_scale, void* out, int64_t batch, int num_heads,
+                                          int num_kv_heads, int64_t length, int64_t capacity, int head_dim,
+                                          float scale, void* stream) {
+  SB_REQUIRE(batch > 0 && num_kv_heads > 0 && num_heads > 0 && num_heads % num_kv_heads == 0 && length > 0,
+             "Nonempty inputs and query heads divisible by KV heads required");
+  SB_REQUIRE(head_dim == sb::kSdpaD, "this build supports head_dim 128");
+  const size_t need = sb::sdpa_workspace_bytes(batch, num_heads, num_kv_heads, length);
+  if (need > kStaticScratchBytes)
+    return sb::fail(SB_EINVAL, "sb_int8_sdpa_decode_static: this shape needs " + std::to_string(need) +
+                                   " bytes of scratch but the static scratch holds " +
+                                   std::to_string(kStaticScratchBytes) +
+                                   " bytes; use sb_int8_sdpa_decode with a caller workspace");
+  void* scratch = nullptr;
+  if (int st = static_scratch_address(&scratch)) return st;
+  // The array keeps the previous call's contents: clear the arrival counters and
+  // the status word (everything the kernel expects to start at zero).
+  cudaError_t err = cudaMemsetAsync(scratch, 0, sb::kCounterBytes, sb::as_stream(stream));
+  if (err != cudaSuccess) return sb::fail(SB_ECUDA, std::string("clearing static scratch: ") + cudaGetErrorString(err));
+  return sb::run_sdpa_int8(q, k, k_scale, v, v_scale, out, batch, num_heads, num_kv_heads, length, capacity,
+                           head_dim, scale, scratch, kStaticScratchBytes, sb::as_stream(stream), 0, nullptr, 0);
 }
 
 extern "C" int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
