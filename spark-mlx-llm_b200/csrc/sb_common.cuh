@@ -65,6 +65,32 @@ int launch(const char* what, Kernel kernel, dim3 grid, dim3 block, size_t smem,
   return SB_OK;
 }
 
+// Same, with the grid's x dimension grouped into thread-block clusters of
+// `cluster_x` CTAs (1 = no cluster attribute).
+template <typename Kernel, typename... Args>
+int launch_cluster(const char* what, Kernel kernel, dim3 grid, dim3 block, size_t smem, int cluster_x,
+                   cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = static_cast<unsigned>(cluster_x);
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  config.attrs = attr;
+  config.numAttrs = cluster_x > 1 ? 2 : 1;
+  cudaError_t err = cudaLaunchKernelEx(&config, kernel, args...);
+  if (err != cudaSuccess) {
+    return fail(SB_ECUDA, std::string(what) + ": " + cudaGetErrorString(err));
+  }
+  return SB_OK;
+}
+
 // -------------------------------------------------------------- device side
 // Wait until the previous kernel in the stream (launched with programmatic
 // serialization) has completed and its memory is visible.
@@ -137,6 +163,24 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       : "memory");
 }
 
+// ------------------------------------------------- thread-block cluster (DSMEM)
+// Address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t cluster_map(uint32_t local, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_shared_f32(uint32_t addr, float v) {
+  asm volatile("st.shared.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+// All threads of all CTAs in the cluster; release/acquire orders the
+// distributed shared-memory stores before the loads after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t d;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
@@ -176,13 +220,13 @@ template <bool kHalf>
 __device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                           uint32_t b1) {
   if constexpr (kHalf) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
         "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
   } else {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
         "{%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])

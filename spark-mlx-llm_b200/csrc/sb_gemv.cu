@@ -3,114 +3,101 @@
 #include <algorithm>
 #include <cmath>
 #include <mutex>
+#include <type_traits>
+#include <vector>
 
 #include "sb_gemv.cuh"
 
 namespace sb {
 
-template <typename TA>
-struct ActTraits;
-template <>
-struct ActTraits<__nv_bfloat16> {
-  static constexpr bool kHalf = false;
-  static constexpr uint32_t kMagic = 0x43004300u;  // bf16 128.0 | code
-  static constexpr uint32_t kOnes = 0x3F803F80u;   // bf16 pair (1.0, 1.0)
-  static constexpr float kOffset = 128.0f;
-};
-template <>
-struct ActTraits<__half> {
-  static constexpr bool kHalf = true;
-  static constexpr uint32_t kMagic = 0x64006400u;  // fp16 1024.0 | code
-  static constexpr uint32_t kOnes = 0x3C003C00u;   // fp16 pair (1.0, 1.0)
-  static constexpr float kOffset = 1024.0f;
-};
+constexpr int cmin(int a, int b) { return a < b ? a : b; }
 
-template <typename TA, int WF>
-struct Fmt {
-  static constexpr bool kHalf = ActTraits<TA>::kHalf;
-  // Two exact nibble planes are needed for 8-bit codes with bf16 operands.
-  static constexpr int kPlanes = ((WF == W_AFF8 || WF == W_I8PC) && !kHalf) ? 2 : 1;
+// Compile-time geometry of one (weight format, group size, column layout).
+//
+// A stage is 128 weight bytes of each of a warp's 32 rows. The MMA's 8 output
+// columns carry (activation row m = n % MC, group slot = n / MC); a stage holds
+// kU "super-groups" of kSlots groups each. Within a super-group the 8 operand
+// streams of a k16 step (lane quad t = 0..3, half h = 0/1 -> stream 2t+h) are
+// pieces of kPB bytes: stream s reads group slot s*kSlots/8, piece
+// s % (8/kSlots), so lane quad t always reads the contiguous bytes
+// [t*kLaneB, (t+1)*kLaneB) of the super-group, and the B operand of column n is
+// non-zero only on the lanes whose stream belongs to n's slot.
+template <int WF, int G, int MC>
+struct Geo {
   static constexpr int kBits = WF == W_AFF4 ? 4 : (WF == W_BF16 ? 16 : 8);
-  // sum(code * x) = C_lo + 16 * C_hi - kCodeOffset * sum(x)
-  static constexpr float kCodeOffset =
-      WF == W_BF16 ? 0.0f
-                   : (kPlanes == 2 ? ActTraits<TA>::kOffset * 17.0f : ActTraits<TA>::kOffset);
+  static constexpr bool kAffine = WF == W_AFF4 || WF == W_AFF8;
+  // fp16 operands with per-group power-of-two activation scaling (all but bf16 weights)
+  static constexpr bool kScaled = WF != W_BF16;
+  static constexpr int kGroupK = kAffine ? G : 64;  // per-channel/bf16: 64-wide pseudo-groups
+  static constexpr int kGB = kGroupK * kBits / 8;   // weight bytes of one group of one row
+  static constexpr int kStageK = 128 * 8 / kBits;
+  static constexpr int kGPS = 128 / kGB;  // groups per stage
+  static constexpr int kSlots = kScaled ? cmin(8 / MC, kGPS) : 1;
+  static constexpr int kU = kGPS / kSlots;
+  static constexpr int kSGB = kSlots * kGB;  // bytes per super-group per row
+  static constexpr int kPB = kSGB / 8;       // bytes per stream piece
+  static constexpr int kLaneB = 2 * kPB;     // bytes per lane quad per row per super-group
+  static constexpr int kPieceK = kPB * 8 / kBits;
+  static constexpr int kSteps = kPieceK / 2;  // k16 MMA steps per super-group
+  static constexpr int kQuads = kSteps / 4;   // 4 steps share one 16-byte activation load
+  static constexpr int kWQ = kBits / 4;       // weight words per stream per quad
+  static constexpr int kWords = kLaneB / 4;   // weight words per lane per row per super-group
+  static constexpr int kYG = kGroupK * 2 + 16;  // staged activation bytes per group (+16: bank rotation)
+  static_assert(kSteps % 4 == 0 && kLaneB >= 8, "geometry");
 };
 
-// Loads `kWords` consecutive uint32 words (streaming, 4..32 bytes).
-template <int kWords>
-__device__ __forceinline__ void load_words(const uint8_t* p, uint32_t (&out)[kWords]) {
-  if constexpr (kWords == 1) {
-    out[0] = ldg_stream4(p);
-  } else if constexpr (kWords == 2) {
-    uint2 v = ldg_stream8(p);
-    out[0] = v.x;
-    out[1] = v.y;
-  } else {
-#pragma unroll
-    for (int i = 0; i < kWords; i += 4) {
-      uint4 v = ldg_stream16(p + 4 * i);
-      out[i] = v.x;
-      out[i + 1] = v.y;
-      out[i + 2] = v.z;
-      out[i + 3] = v.w;
-    }
+// Operand encoding of the codes (A = offset + code, exact) and of the staged
+// activations, per k16 step j of a quad (4-bit: steps 0 and 2 carry the low
+// nibble of each byte, steps 1 and 3 the high nibble):
+//   4-bit, bf16 activations: low nibble  bf16 128+q   (0x4300 | q)      x staged as bf16
+//                            high nibble fp16 64+q    (0x5400 | q<<4)   x staged as fp16
+//   4-bit, fp16 activations: low nibble  fp16 1024+q  (0x6400 | q), high nibble as above
+//   8-bit                  : fp16 1024+u  (0x64 | byte; signed int8: u = code+128, offset 1152)
+//   bf16 weights           : bf16 as stored
+// acc = sum(code * xs) + sum(offset_k * xs_k); the second sum is staged per group.
+template <typename TA, int WF>
+struct Enc {
+  static constexpr bool kMixed = WF == W_AFF4 && !std::is_same<TA, __half>::value;
+  __host__ __device__ static constexpr bool half_step(int j) {
+    return WF == W_BF16 ? false : (kMixed ? (j & 1) != 0 : true);
   }
+  static constexpr uint32_t kLowMagic = kMixed ? 0x43004300u : 0x64006400u;
+  static constexpr float kOffEven = WF == W_AFF4 ? (kMixed ? 128.0f : 1024.0f) : (WF == W_I8PC ? 1152.0f : 1024.0f);
+  static constexpr float kOffOdd = WF == W_AFF4 ? 64.0f : kOffEven;
+};
+
+// Row relabeling inside each 8-row half of a box so that the lanes' reads of
+// the 128-byte-swizzled rows fall into distinct banks for their access width.
+template <int kLaneB>
+__device__ __forceinline__ int sigma_row(int g) {
+  if constexpr (kLaneB >= 32) return g;                           // 2 x 16 B per row
+  else if constexpr (kLaneB == 16) return ((g & 1) << 2) | (g >> 1);  // 16 B per row
+  else return ((g & 3) << 1) | (g >> 2);                          // 8 B per row
 }
 
-// Converts one row segment of packed codes into MMA A-operand pairs.
-// Pair order (shared with the x pairs below):
-//   4-bit : pair 4w+j holds values (8w+j, 8w+j+4) of the segment
-//   8-bit : pair 2w+i holds values (4w+2i, 4w+2i+1)
-//   bf16  : pair i holds values (2i, 2i+1)
-template <typename TA, int WF, int kWords, int kPairs>
-__device__ __forceinline__ void dequant_pairs(const uint32_t (&w)[kWords],
-                                              uint32_t (&lo)[kPairs], uint32_t (&hi)[kPairs]) {
-  constexpr uint32_t kMagic = ActTraits<TA>::kMagic;
+// Four k16 steps' worth of one stream's weight words -> operand pairs
+//   4-bit: word -> pairs (k0,k4) (k1,k5) (k2,k6) (k3,k7)
+//   8-bit: 2 words -> pairs (k0,k1) (k2,k3) per word
+//   bf16 : 4 words -> pairs as stored
+template <typename TA, int WF>
+__device__ __forceinline__ void dequant_quad(const uint32_t* w, uint32_t (&p)[4]) {
   if constexpr (WF == W_AFF4) {
-#pragma unroll
-    for (int i = 0; i < kWords; ++i) {
-      lo[4 * i + 0] = lop_and_or(w[i], 0x000F000Fu, kMagic);
-      lo[4 * i + 1] = lop_and_or(w[i] >> 4, 0x000F000Fu, kMagic);
-      lo[4 * i + 2] = lop_and_or(w[i] >> 8, 0x000F000Fu, kMagic);
-      lo[4 * i + 3] = lop_and_or(w[i] >> 12, 0x000F000Fu, kMagic);
-    }
+    constexpr uint32_t kLow = Enc<TA, WF>::kLowMagic;
+    const uint32_t s = w[0] >> 8;
+    p[0] = lop_and_or(w[0], 0x000F000Fu, kLow);
+    p[1] = lop_and_or(w[0], 0x00F000F0u, 0x54005400u);
+    p[2] = lop_and_or(s, 0x000F000Fu, kLow);
+    p[3] = lop_and_or(s, 0x00F000F0u, 0x54005400u);
   } else if constexpr (WF == W_AFF8 || WF == W_I8PC) {
 #pragma unroll
-    for (int i = 0; i < kWords; ++i) {
+    for (int i = 0; i < 2; ++i) {
       const uint32_t u = (WF == W_I8PC) ? (w[i] ^ 0x80808080u) : w[i];
-      if constexpr (ActTraits<TA>::kHalf) {
-        lo[2 * i + 0] = prmt(u, 0x64646464u, 0x4140u);
-        lo[2 * i + 1] = prmt(u, 0x64646464u, 0x4342u);
-      } else {
-        const uint32_t t0 = prmt(u, 0u, 0x4140u);
-        const uint32_t t1 = prmt(u, 0u, 0x4342u);
-        lo[2 * i + 0] = lop_and_or(t0, 0x000F000Fu, kMagic);
-        lo[2 * i + 1] = lop_and_or(t1, 0x000F000Fu, kMagic);
-        hi[2 * i + 0] = lop_and_or(t0 >> 4, 0x000F000Fu, kMagic);
-        hi[2 * i + 1] = lop_and_or(t1 >> 4, 0x000F000Fu, kMagic);
-      }
+      p[2 * i] = prmt(u, 0x64646464u, 0x4140u);
+      p[2 * i + 1] = prmt(u, 0x64646464u, 0x4342u);
     }
   } else {
 #pragma unroll
-    for (int i = 0; i < kWords; ++i) lo[i] = w[i];
-  }
-}
-
-// x values (bf16/fp16 pairs as stored) -> B-operand pairs in the same order.
-template <int WF, int kXWords, int kPairs>
-__device__ __forceinline__ void x_pairs(const uint32_t (&xw)[kXWords], uint32_t (&xp)[kPairs]) {
-  if constexpr (WF == W_AFF4) {
-#pragma unroll
-    for (int w = 0; w < kXWords / 4; ++w) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        xp[4 * w + j] = prmt(xw[4 * w + j / 2], xw[4 * w + 2 + j / 2], (j & 1) ? 0x7632u : 0x5410u);
-      }
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < kPairs; ++i) xp[i] = xw[i];
+    for (int i = 0; i < 4; ++i) p[i] = w[i];
   }
 }
 
@@ -133,20 +120,17 @@ template <typename TA>
 __device__ __forceinline__ float round_act(float v) {
   return to_float(from_float<TA>(v));
 }
+// 16-bit activation-typed value (bf16 or fp16 bits) -> float
+template <typename TA>
+__device__ __forceinline__ float bits_to_float(uint32_t b16) {
+  if constexpr (std::is_same<TA, __half>::value) return __half2float(__ushort_as_half(static_cast<unsigned short>(b16)));
+  else return __uint_as_float(b16 << 16);
+}
 
 // ---- warp row blocks
 // A warp owns 32 weight rows, fetched per stage as two TMA boxes (A and B) of
 // 16 rows x 128 bytes. MMA rows 0-7 of tile r come from box A rows 8r + sigma(g),
-// MMA rows 8-15 from box B rows 8r + sigma(g). sigma relabels the rows so the
-// lanes' reads of the 128-byte-swizzled boxes hit distinct banks.
-template <int kBits>
-__device__ __forceinline__ int sigma_row(int g) {
-  if constexpr (kBits == 4) return ((g & 3) << 1) | (g >> 2);   // 0,2,4,6,1,3,5,7
-  else if constexpr (kBits == 8) return ((g & 1) << 2) | (g >> 1);  // 0,4,1,5,2,6,3,7
-  else return g;
-}
-
-// number of 32-row warp blocks
+// MMA rows 8-15 from box B rows 8r + sigma(g).
 template <int EPI>
 __device__ __forceinline__ int warp_blocks(const GemvParams& p) {
   if constexpr (EPI == EPI_SWIGLU) return (p.N + 15) / 16;
@@ -167,83 +151,59 @@ __device__ __forceinline__ int box_row0(const GemvParams& p, int rb, int h) {
   }
 }
 
-template <int kBits>
-struct StageGeom {
-  static constexpr int kRowBytes = 128;                  // bytes of one weight row per stage
-  static constexpr int kStageK = kRowBytes * 8 / kBits;  // K values per stage
-  static constexpr int kStages = 4;                      // ring depth per warp
-  static constexpr int kStageBytes = 32 * kRowBytes;     // two 16-row boxes
-};
+constexpr int kStageBytes = 32 * 128;  // two 16-row boxes
 
-template <typename TA, int WF, int KC, int GC, int EPI, bool NORM, int MC>
-__global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_constant__ GemvParams p) {
-  using F = Fmt<TA, WF>;
-  using SG = StageGeom<F::kBits>;
-  constexpr int V = KC / 4;                      // values per lane per row per chunk
-  constexpr int kPairs = V / 2;                  // MMA operand pairs per row per chunk
-  constexpr int kMma = KC / 16;                  // k16 steps per chunk
-  constexpr int kWords = V * F::kBits / 32;      // weight words per lane per row per chunk
-  constexpr int kXWords = V / 2;                 // activation words per lane per chunk
-  constexpr int kRows = 2 * kGemvTiles;          // weight rows held per lane
-  constexpr bool kAffine = (WF == W_AFF4 || WF == W_AFF8);
-  constexpr int kGroupK = kAffine ? KC * GC : KC;  // K covered by one split unit
-  constexpr int kChunkRowBytes = KC * F::kBits / 8;
-  constexpr int kLaneBytes = V * F::kBits / 8;
-  constexpr int kChunksPerStage = SG::kStageK / KC;
-  // The MMA's 8 n-columns carry (activation column m, group slot) pairs:
-  // column n -> m = n % MC, slot = n / MC. An affine "super-group" of kSlots
-  // consecutive groups accumulates in separate columns; its scales are applied
-  // once at its end. Non-affine formats use one slot (columns = activation rows).
-  constexpr int kSlots = kAffine ? 8 / MC : 1;
-  constexpr int kSuperChunks = kSlots * GC;
-  static_assert(!kAffine || kChunksPerStage % GC == 0, "a stage holds whole groups");
+template <typename TA, int WF, int G, int EPI, bool NORM, int MC>
+__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_constant__ GemvParams p) {
+  using C = Geo<WF, G, MC>;
+  constexpr int kVG = C::kGroupK / 8;  // 8-value activation vectors per group
+  constexpr int kNT = kGemvWarps * 32;
 
   extern __shared__ uint8_t smem_dyn[];
   __shared__ float s_rms[8];
   __shared__ float s_part[kGemvWarps][8];
+  __shared__ unsigned long long s_keys[8];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = lane >> 2;
   const int t = lane & 3;
-  const int sg = sigma_row<F::kBits>(g);
-  const int split = blockIdx.y;
+  const int sg = sigma_row<C::kLaneB>(g);
+  const int part = blockIdx.x;  // K part = rank in the cluster
+  const int nparts = gridDim.x;
   const int rowblocks = warp_blocks<EPI>(p);
-  const int rb = blockIdx.x * kGemvWarps + warp;
+  const int rb = blockIdx.y * kGemvWarps + warp;
   const bool active = rb < rowblocks;
   const int rbc = min(rb, rowblocks - 1);
-  const int mcols = p.M;
+  const int M = p.M;
+  const int gpr = p.K / C::kGroupK;  // groups per row
 
-  // K range of this split, in whole groups.
-  const int grp_begin = static_cast<int>((static_cast<long long>(p.groups_total) * split) / p.splits);
-  const int grp_end = static_cast<int>((static_cast<long long>(p.groups_total) * (split + 1)) / p.splits);
-  const int k_begin = grp_begin * kGroupK;
-  const int k_count = (grp_end - grp_begin) * kGroupK;
-  const int nstages = (k_count + SG::kStageK - 1) / SG::kStageK;
-  const int nchunks = k_count / KC;
-  const int kbyte0 = k_begin * F::kBits / 8;
+  // stages [st0, st1) of this CTA
+  const int st0 = static_cast<int>((static_cast<long long>(p.stages_total) * part) / nparts);
+  const int st1 = static_cast<int>((static_cast<long long>(p.stages_total) * (part + 1)) / nparts);
+  const int nst = st1 - st0;
 
-  // ---- shared memory: barriers, per-warp weight rings (1 KB aligned), x segment, x group sums
+  // ---- shared memory: barriers + zero block, per-warp rings, staged x, group meta, reduction buffer
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base) + warp * SG::kStages;
-  uint8_t* ring = base + 1024 + (warp * SG::kStages) * SG::kStageBytes;
-  TA* xs = reinterpret_cast<TA*>(base + 1024 + kGemvWarps * SG::kStages * SG::kStageBytes);
-  const int xs_ld = p.x_seg + 8;
-  float* xgs = reinterpret_cast<float*>(xs + mcols * xs_ld);  // [M][x_seg / kGroupK]
-  const int xg_ld = p.x_seg / kGroupK;
-  const int rowA = box_row0<EPI>(p, rbc, 0), rowB = box_row0<EPI>(p, rbc, 1);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base) + warp * kGemvMaxRing;
+  const uint8_t* zero_blk = base + 512;
+  uint8_t* ring = base + 1024 + warp * p.ring * kStageBytes;
+  uint8_t* ys = base + 1024 + kGemvWarps * p.ring * kStageBytes;
+  float4* meta = reinterpret_cast<float4*>(ys + M * p.y_ld);
+  float* red = reinterpret_cast<float*>(meta + M * p.meta_ld);
 
+  const int rowA = box_row0<EPI>(p, rbc, 0), rowB = box_row0<EPI>(p, rbc, 1);
   auto issue_stage = [&](int st) {
-    const int slot = st % SG::kStages;
-    uint8_t* dst = ring + slot * SG::kStageBytes;
-    mbar_arrive_expect_tx(bars + slot, SG::kStageBytes);
-    const int x = kbyte0 + st * SG::kRowBytes;
+    const int slot = st % p.ring;
+    uint8_t* dst = ring + slot * kStageBytes;
+    mbar_arrive_expect_tx(bars + slot, kStageBytes);
+    const int x = (st0 + st) * 128;
     tma_load_2d(dst, &p.tmap0, x, rowA, bars + slot);
-    tma_load_2d(dst + 16 * SG::kRowBytes, &p.tmap1, x, rowB, bars + slot);
+    tma_load_2d(dst + 16 * 128, &p.tmap1, x, rowB, bars + slot);
   };
 
   if (active && lane == 0) {
-    for (int i = 0; i < SG::kStages; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < p.ring; ++i) mbar_init(bars + i, 1);
     mbar_fence_init();
   }
   __syncwarp();
@@ -251,39 +211,32 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
   // tail of the previous kernel in the stream
   if (!p.early_prefetch) grid_dependency_wait();
   if (active && lane == 0) {
-    for (int st = 0; st < SG::kStages && st < nstages; ++st) issue_stage(st);
+    for (int st = 0; st < p.ring && st < nst; ++st) issue_stage(st);
   }
+  if (threadIdx.x < 32) reinterpret_cast<uint4*>(base + 512)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
+  if (threadIdx.x < 8) s_keys[threadIdx.x] = 0ull;
 
   // ---- activations depend on the previous kernel from here on
   grid_dependency_wait();
   if constexpr (NORM) {
-    // full-row sum of squares per column (fixed reduction order)
-    for (int m = 0; m < mcols; ++m) {
+    // full-row sum of squares per activation row (fixed reduction order)
+    for (int m = 0; m < M; ++m) {
       float ss = 0.f;
       const TA* xr = static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx;
-      for (int k = threadIdx.x * 8; k < p.K; k += kGemvWarps * 32 * 8) {
+      for (int k = threadIdx.x * 8; k < p.K; k += kNT * 8) {
         const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-        const uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+        const TA* e = reinterpret_cast<const TA*>(&v);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float a, b;
-          if constexpr (ActTraits<TA>::kHalf) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vv[i]));
-            a = f.x;
-            b = f.y;
-          } else {
-            a = bf16_lo(vv[i]);
-            b = bf16_hi(vv[i]);
-          }
+        for (int i = 0; i < 8; ++i) {
+          const float a = to_float(e[i]);
           ss = fmaf(a, a, ss);
-          ss = fmaf(b, b, ss);
         }
       }
       ss = warp_sum(ss);
       if (lane == 0) s_part[warp][m] = ss;
     }
     __syncthreads();
-    if (threadIdx.x < mcols) {
+    if (threadIdx.x < M) {
       float ss = 0.f;
 #pragma unroll
       for (int w = 0; w < kGemvWarps; ++w) ss += s_part[w][threadIdx.x];
@@ -291,440 +244,420 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
     }
   }
 
-  // B-operand column of this lane: activation column bm, group slot bslot
-  const int bm = g % MC;
-  const int bslot = g / MC;
-  const bool b_live = bm < mcols && (kAffine || bslot == 0);
-
-  constexpr uint32_t kOnes = ActTraits<TA>::kOnes;
-  float cacc[kGemvTiles][F::kPlanes][4];
-  float xsum[4];
-  float res[kGemvTiles][2][2];  // [tile][h][e] affine results per (row, column)
-#pragma unroll
-  for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-#pragma unroll
-      for (int pl = 0; pl < F::kPlanes; ++pl) cacc[r][pl][e] = 0.f;
-      res[r][e >> 1][e & 1] = 0.f;
-    }
-#pragma unroll
-  for (int e = 0; e < 4; ++e) xsum[e] = 0.f;
-
-  // scale/bias of this lane's rows (tile r, box h) for its two columns' groups
-  auto row_of = [&](int r, int h) { return min((h ? rowB : rowA) + 8 * r + sg, p.N - 1); };
-  auto set_of = [&](int h) { return (EPI == EPI_SWIGLU) ? h : 0; };
-  uint32_t sbv[kGemvTiles][2][2];  // packed (scale, bias) for [tile][h][e]
-  auto load_super_scales = [&](int grp0) {
-    if constexpr (kAffine) {
-      const int gpr = p.K / p.group_size;
-#pragma unroll
-      for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int grp = min(grp0 + (2 * t + e) / MC, grp_end - 1);
-            const size_t idx = static_cast<size_t>(row_of(r, h)) * gpr + grp;
-            const uint16_t s = *reinterpret_cast<const uint16_t*>(static_cast<const TA*>(set_of(h) ? p.s1 : p.s0) + idx);
-            const uint16_t b = *reinterpret_cast<const uint16_t*>(static_cast<const TA*>(set_of(h) ? p.b1 : p.b0) + idx);
-            sbv[r][h][e] = static_cast<uint32_t>(s) | (static_cast<uint32_t>(b) << 16);
-          }
-    }
-  };
-  if (active && nchunks > 0) load_super_scales(grp_begin);
-
-  bool failed = false;
-  int chunk = 0;  // chunk index inside the split
-  for (int st = 0; st < nstages; ++st) {
-    // ---- activation segment staging (all warps of the CTA take part)
-    const int kst = st * SG::kStageK;  // offset inside the split
-    if (kst % p.x_seg == 0) {
-      __syncthreads();
-      const int seg_len = min(p.x_seg, k_count - kst);
-      const int vecs = seg_len / 8;
-      for (int idx = threadIdx.x; idx < mcols * vecs; idx += kGemvWarps * 32) {
-        const int m = idx / vecs, v8 = idx % vecs;
-        const int kg = k_begin + kst + v8 * 8;
-        uint4 v = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + kg);
+  // ---- activation staging of stages [sb, sb + seg_stages) (all threads):
+  // xs = x * 2^e per group in the operand type of its k (exact), laid out in
+  // the operand pair order; meta = {2^-e, sum(offset_k * xs_k), sum(x)} per group.
+  auto stage_x = [&](int sb) {
+    const int k0 = (st0 + sb) * C::kStageK;
+    const int k1 = min(min(st0 + sb + p.seg_stages, st1) * C::kStageK, p.K);
+    const int nvec = max(k1 - k0, 0) / 8;
+    const int total = M * nvec;
+    for (int b0 = 0; b0 < total; b0 += kNT) {
+      const int idx = b0 + threadIdx.x;
+      const bool ok = idx < total;
+      const int m = ok ? idx / nvec : 0;
+      const int v = ok ? idx - m * nvec : 0;
+      const int k = k0 + 8 * v;
+      float f[8];
+      if (ok) {
+        const uint4 xv = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + k);
+        const TA* xe = reinterpret_cast<const TA*>(&xv);
         if constexpr (NORM) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + kg);
-          const TA* xv = reinterpret_cast<const TA*>(&v);
-          const TA* nv = reinterpret_cast<const TA*>(&wv);
-          TA out[8];
+          const uint4 wv = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + k);
+          const TA* we = reinterpret_cast<const TA*>(&wv);
           const float r = s_rms[m];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) out[i] = from_float<TA>(to_float(xv[i]) * r * to_float(nv[i]));
-          v = *reinterpret_cast<const uint4*>(out);
+          for (int i = 0; i < 8; ++i) f[i] = round_act<TA>(to_float(xe[i]) * r * to_float(we[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = to_float(xe[i]);
         }
-        *reinterpret_cast<uint4*>(xs + m * xs_ld + v8 * 8) = v;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = 0.f;
       }
-      if constexpr (kAffine) {
-        __syncthreads();
-        // per-group sums of the staged activations (fixed order)
-        const int ng = seg_len / kGroupK;
-        for (int idx = threadIdx.x; idx < mcols * ng; idx += kGemvWarps * 32) {
-          const int m = idx / ng, gi = idx % ng;
-          const TA* xp = xs + m * xs_ld + gi * kGroupK;
-          float sum = 0.f;
-          for (int i = 0; i < kGroupK; ++i) sum += to_float(xp[i]);
-          xgs[m * xg_ld + gi] = sum;
+      const int grp = (8 * v) / C::kGroupK;  // group inside the segment
+      uint8_t* dst = ys + m * p.y_ld + grp * C::kYG + ((8 * v) % C::kGroupK) * 2;
+      if constexpr (C::kScaled) {
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+#pragma unroll
+        for (int o = 1; o < kVG; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        // power of two putting the group's largest |x| into [2^14, 2^15)
+        const int ex = static_cast<int>((__float_as_uint(amax) >> 23) & 0xFFu);
+        const int e = max(-126, min(126, 141 - ex));
+        const float sc = __uint_as_float(static_cast<uint32_t>(e + 127) << 23);
+        uint16_t hb[8];
+        float osum = 0.f, xsum = 0.f;  // sum(offset_k * xs_k), sum(x)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float ys = f[i] * sc;
+          float yv;
+          if (Enc<TA, WF>::kMixed && (i & 1) == 0) {
+            const __nv_bfloat16 b = __float2bfloat16_rn(ys);
+            hb[i] = __bfloat16_as_ushort(b);
+            yv = __bfloat162float(b);
+          } else {
+            const __half h = __float2half_rn(ys);
+            hb[i] = __half_as_ushort(h);
+            yv = __half2float(h);
+          }
+          osum = fmaf((i & 1) ? Enc<TA, WF>::kOffOdd : Enc<TA, WF>::kOffEven, yv, osum);
+          xsum += f[i];
+        }
+#pragma unroll
+        for (int o = 1; o < kVG; o <<= 1) {
+          osum += __shfl_xor_sync(0xffffffffu, osum, o);
+          xsum += __shfl_xor_sync(0xffffffffu, xsum, o);
+        }
+        uint4 out;
+        if constexpr (WF == W_AFF4) {
+          // pair order of the 4-bit operand: (k0,k4) (k1,k5) (k2,k6) (k3,k7)
+          out.x = static_cast<uint32_t>(hb[0]) | (static_cast<uint32_t>(hb[4]) << 16);
+          out.y = static_cast<uint32_t>(hb[1]) | (static_cast<uint32_t>(hb[5]) << 16);
+          out.z = static_cast<uint32_t>(hb[2]) | (static_cast<uint32_t>(hb[6]) << 16);
+          out.w = static_cast<uint32_t>(hb[3]) | (static_cast<uint32_t>(hb[7]) << 16);
+        } else {
+          out = *reinterpret_cast<const uint4*>(hb);
+        }
+        if (ok) {
+          *reinterpret_cast<uint4*>(dst) = out;
+          if ((v % kVG) == 0) {
+            const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
+            meta[m * p.meta_ld + grp] = make_float4(inv, osum, xsum, 0.f);
+          }
+        }
+      } else {
+        if (ok) {
+          __nv_bfloat16 hb[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) hb[i] = __float2bfloat16_rn(f[i]);
+          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(hb);
         }
       }
+    }
+  };
+
+  // ---- per-lane operand geometry
+  const int bm = g % MC;      // activation row of this lane's B column
+  const int bslot = g / MC;   // group slot of this lane's B column
+  const bool col_live = bm < M;
+  const int slot_lo = (2 * t) * C::kSlots / 8, slot_hi = (2 * t + 1) * C::kSlots / 8;
+  const int ypo_lo = ((2 * t) % (8 / C::kSlots)) * C::kPieceK * 2;
+  const int ypo_hi = ((2 * t + 1) % (8 / C::kSlots)) * C::kPieceK * 2;
+  const bool act_lo = col_live && bslot == slot_lo;
+  const bool act_hi = col_live && bslot == slot_hi;
+  // this lane's bytes of row 8r+sg of a box, per super-group u and 16-byte load i
+  constexpr int kLoads = C::kLaneB >= 16 ? C::kLaneB / 16 : 1;
+  int aoff[C::kU][kLoads];
+#pragma unroll
+  for (int u = 0; u < C::kU; ++u)
+#pragma unroll
+    for (int i = 0; i < kLoads; ++i) {
+      const int byte = u * C::kSGB + t * C::kLaneB + 16 * i;
+      aoff[u][i] = sg * 128 + ((((byte >> 4) ^ sg) << 4) | (byte & 15));
+    }
+
+  // scale/bias of the lane's rows for the groups of its two accumulator columns
+  const int ss0 = (MC == 1) ? 2 * t : (2 * t) / MC;  // slot of column 2t
+  constexpr bool kPairCols = (MC == 1) && (C::kSlots >= 2);  // columns 2t, 2t+1 = two groups
+  auto row_of = [&](int r, int h) { return min((h ? rowB : rowA) + 8 * r + sg, p.N - 1); };
+  auto set_of = [&](int h) { return (EPI == EPI_SWIGLU) ? h : 0; };
+  uint32_t sv[2][2], bv[2][2];  // [tile][h]: (s of col 2t) | (s of col 2t+1) << 16, same for bias
+  auto load_sb = [&](int gabs0) {
+    if constexpr (C::kAffine) {
+      const int gq = gabs0 + ss0;
+      const bool v0 = ss0 < C::kSlots && gq < gpr;
+      const bool v1 = kPairCols && ss0 + 1 < C::kSlots && gq + 1 < gpr;
+#pragma unroll
+      for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const size_t idx = static_cast<size_t>(row_of(r, h)) * gpr + gq;
+          const uint16_t* sp = static_cast<const uint16_t*>(set_of(h) ? p.s1 : p.s0) + idx;
+          const uint16_t* bp = static_cast<const uint16_t*>(set_of(h) ? p.b1 : p.b0) + idx;
+          uint32_t s = 0u, b = 0u;
+          if (kPairCols && v1 && p.pair_scales) {
+            s = *reinterpret_cast<const uint32_t*>(sp);
+            b = *reinterpret_cast<const uint32_t*>(bp);
+          } else {
+            if (v0) {
+              s = sp[0];
+              b = bp[0];
+            }
+            if (kPairCols && v1) {
+              s |= static_cast<uint32_t>(sp[1]) << 16;
+              b |= static_cast<uint32_t>(bp[1]) << 16;
+            }
+          }
+          sv[r][h] = s;
+          bv[r][h] = b;
+        }
+    }
+  };
+
+  float cacc[2][4];
+  float res[2][2][2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      cacc[r][e] = 0.f;
+      res[r][e >> 1][e & 1] = 0.f;
+    }
+  if (active && nst > 0) load_sb(st0 * C::kGPS);
+
+  bool failed = false;
+  int done = 0;  // stages consumed by this warp
+  int seg_first = 0;
+  for (int st = 0; st < nst; ++st) {
+    if (st % p.seg_stages == 0) {
       __syncthreads();
+      stage_x(st);
+      __syncthreads();
+      seg_first = st;
     }
     if (!active || failed) continue;
 
-    const int slot = st % SG::kStages;
-    if (!mbar_wait_bounded(bars + slot, (st / SG::kStages) & 1)) {
+    const int slot = st % p.ring;
+    if (!mbar_wait_bounded(bars + slot, (st / p.ring) & 1)) {
       failed = true;
       continue;
     }
-    const uint8_t* stage = ring + slot * SG::kStageBytes;
-    const int chunks = min(kChunksPerStage, (k_count - kst) / KC);
-    const TA* xbase = xs + min(bm, mcols - 1) * xs_ld + (kst % p.x_seg) + t * V;
+    done = st + 1;
+    const uint8_t* stage = ring + slot * kStageBytes;
 #pragma unroll
-    for (int cc = 0; cc < kChunksPerStage; ++cc) {
-      if (cc < chunks) {
-        uint32_t wv[kRows][kWords];
+    for (int u = 0; u < C::kU; ++u) {
+      // weight words of this super-group: rows q = 2r + h (tile r, box h)
+      uint32_t aw[4][C::kWords];
 #pragma unroll
-        for (int q = 0; q < kRows; ++q) {
-          const uint8_t* box = stage + (q & 1) * 16 * SG::kRowBytes;
-          const int row = 8 * (q >> 1) + sg;
-          const int byte = cc * kChunkRowBytes + t * kLaneBytes;
-          if constexpr (kWords == 1) {
-            wv[q][0] = *reinterpret_cast<const uint32_t*>(swz128(box, row, byte));
-          } else if constexpr (kWords == 2) {
-            const uint2 v = *reinterpret_cast<const uint2*>(swz128(box, row, byte));
-            wv[q][0] = v.x;
-            wv[q][1] = v.y;
-          } else {
+      for (int q = 0; q < 4; ++q) {
+        const uint8_t* rowp = stage + (q & 1) * 2048 + (q >> 1) * 1024;
+        if constexpr (C::kLaneB >= 16) {
 #pragma unroll
-            for (int i = 0; i < kWords; i += 4) {
-              const uint4 v = *reinterpret_cast<const uint4*>(swz128(box, row, byte + 4 * i));
-              wv[q][i] = v.x;
-              wv[q][i + 1] = v.y;
-              wv[q][i + 2] = v.z;
-              wv[q][i + 3] = v.w;
-            }
+          for (int i = 0; i < kLoads; ++i) {
+            const uint4 v = *reinterpret_cast<const uint4*>(rowp + aoff[u][i]);
+            aw[q][4 * i] = v.x;
+            aw[q][4 * i + 1] = v.y;
+            aw[q][4 * i + 2] = v.z;
+            aw[q][4 * i + 3] = v.w;
           }
-        }
-        uint32_t lo[kRows][kPairs], hi[kRows][kPairs];
-#pragma unroll
-        for (int q = 0; q < kRows; ++q) dequant_pairs<TA, WF, kWords, kPairs>(wv[q], lo[q], hi[q]);
-        // B operand: this lane's column feeds only the group of its slot
-        const int gslot = (chunk / GC) % kSlots;
-        const bool feed = b_live && (bslot == gslot);
-        uint32_t xpair[kPairs];
-        if (feed) {
-          uint32_t xw[kXWords];
-#pragma unroll
-          for (int i = 0; i < kXWords; i += 4) {
-            const uint4 v = *reinterpret_cast<const uint4*>(xbase + cc * KC + 2 * i);
-            xw[i] = v.x;
-            xw[i + 1] = v.y;
-            xw[i + 2] = v.z;
-            xw[i + 3] = v.w;
-          }
-          x_pairs<WF, kXWords, kPairs>(xw, xpair);
         } else {
+          const uint2 v = *reinterpret_cast<const uint2*>(rowp + aoff[u][0]);
+          aw[q][0] = v.x;
+          aw[q][1] = v.y;
+        }
+      }
+      // staged activations of the lane's two streams (zeros when the lane's column is elsewhere)
+      const int gseg = (st - seg_first) * C::kGPS + u * C::kSlots;  // group of slot 0 in the segment
+      const int gabs = (st0 + st) * C::kGPS + u * C::kSlots;        // absolute group of slot 0
+      const uint8_t* yrow = ys + bm * p.y_ld + gseg * C::kYG;
+      const uint8_t* yl = (act_lo && gabs + slot_lo < gpr) ? yrow + slot_lo * C::kYG + ypo_lo : zero_blk;
+      const uint8_t* yh = (act_hi && gabs + slot_hi < gpr) ? yrow + slot_hi * C::kYG + ypo_hi : zero_blk;
 #pragma unroll
-          for (int i = 0; i < kPairs; ++i) xpair[i] = 0u;
+      for (int qd = 0; qd < C::kQuads; ++qd) {
+        const uint4 bl = *reinterpret_cast<const uint4*>(yl + 16 * qd);
+        const uint4 bh = *reinterpret_cast<const uint4*>(yh + 16 * qd);
+        const uint32_t blv[4] = {bl.x, bl.y, bl.z, bl.w};
+        const uint32_t bhv[4] = {bh.x, bh.y, bh.z, bh.w};
+        uint32_t pl[4][4], ph[4][4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          dequant_quad<TA, WF>(&aw[q][qd * C::kWQ], pl[q]);
+          dequant_quad<TA, WF>(&aw[q][C::kWords / 2 + qd * C::kWQ], ph[q]);
         }
 #pragma unroll
-        for (int j = 0; j < kMma; ++j) {
-          const uint32_t b0 = xpair[2 * j], b1 = xpair[2 * j + 1];
+        for (int j = 0; j < 4; ++j)
 #pragma unroll
-          for (int r = 0; r < kGemvTiles; ++r) {
-            const uint32_t a_lo[4] = {lo[2 * r][2 * j], lo[2 * r + 1][2 * j], lo[2 * r][2 * j + 1],
-                                      lo[2 * r + 1][2 * j + 1]};
-            mma_16816<F::kHalf>(cacc[r][0], a_lo, b0, b1);
-            if constexpr (F::kPlanes == 2) {
-              const uint32_t a_hi[4] = {hi[2 * r][2 * j], hi[2 * r + 1][2 * j], hi[2 * r][2 * j + 1],
-                                        hi[2 * r + 1][2 * j + 1]};
-              mma_16816<F::kHalf>(cacc[r][1], a_hi, b0, b1);
-            }
+          for (int r = 0; r < 2; ++r) {
+            const uint32_t a[4] = {pl[2 * r][j], pl[2 * r + 1][j], ph[2 * r][j], ph[2 * r + 1][j]};
+            if (Enc<TA, WF>::half_step(j)) mma_16816<true>(cacc[r], a, blv[j], bhv[j]);
+            else mma_16816<false>(cacc[r], a, blv[j], bhv[j]);
           }
-          if constexpr (WF == W_I8PC) {
-            const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
-            mma_16816<F::kHalf>(xsum, ones, b0, b1);
-          }
+      }
+      if constexpr (C::kScaled) {
+        // super-group epilogue for the lane's columns 2t+e: group gabs + slot
+        float4 mt[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int n = 2 * t + e;
+          const int m = n % MC, sl = n / MC;
+          const bool ok = m < M && sl < C::kSlots && gabs + sl < gpr;
+          mt[e] = ok ? meta[m * p.meta_ld + gseg + sl] : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        ++chunk;
-        if constexpr (kAffine) {
-          if (chunk % kSuperChunks == 0 || chunk == nchunks) {
-            // super-group epilogue: res += scale * sum(code*x) + (bias - offset*scale) * sum(x)
-            const int grp0 = grp_begin + (chunk - 1) / kSuperChunks * kSlots;
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const int n = 2 * t + e;
-              const int grp = grp0 + n / MC;
-              const int m = n % MC;
-              const bool ok = grp < grp_end && m < mcols;
-              float xg = 0.f;
-              if (ok) {
-                const int k_in_seg = (grp - grp_begin) * kGroupK - (kst / p.x_seg) * p.x_seg;
-                xg = xgs[m * xg_ld + k_in_seg / kGroupK];
+              const float d = cacc[r][2 * h + e] - mt[e].y;
+              if constexpr (C::kAffine) {
+                const uint32_t s16 = (kPairCols && e) ? (sv[r][h] >> 16) : (sv[r][h] & 0xFFFFu);
+                const uint32_t b16 = (kPairCols && e) ? (bv[r][h] >> 16) : (bv[r][h] & 0xFFFFu);
+                const float s = bits_to_float<TA>(s16), b = bits_to_float<TA>(b16);
+                res[r][h][e] = fmaf(s * mt[e].x, d, fmaf(b, mt[e].z, res[r][h][e]));
+              } else {
+                res[r][h][e] = fmaf(mt[e].x, d, res[r][h][e]);
               }
-#pragma unroll
-              for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  const uint32_t v = sbv[r][h][e];
-                  float s, b;
-                  if constexpr (ActTraits<TA>::kHalf) {
-                    s = __half2float(__ushort_as_half(static_cast<unsigned short>(v & 0xFFFFu)));
-                    b = __half2float(__ushort_as_half(static_cast<unsigned short>(v >> 16)));
-                  } else {
-                    s = bf16_lo(v);
-                    b = bf16_hi(v);
-                  }
-                  float d = cacc[r][0][2 * h + e];
-                  if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][2 * h + e], d);
-                  const float bb = fmaf(-F::kCodeOffset, s, b);
-                  res[r][h][e] = ok ? fmaf(s, d, fmaf(bb, xg, res[r][h][e])) : res[r][h][e];
-                }
+              cacc[r][2 * h + e] = 0.f;
             }
-#pragma unroll
-            for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                cacc[r][0][e] = 0.f;
-                if constexpr (F::kPlanes == 2) cacc[r][1][e] = 0.f;
-              }
-            if (chunk < nchunks) load_super_scales(grp0 + kSlots);
-          }
-        }
+        if (C::kAffine && (st + 1 < nst || u + 1 < C::kU)) load_sb(gabs + C::kSlots);
       }
     }
-    // refill this slot with the stage kStages ahead
+    // refill this slot with the stage `ring` ahead
     __syncwarp();
-    if (st + SG::kStages < nstages && lane == 0) {
+    if (st + p.ring < nst && lane == 0) {
       fence_proxy_async_smem();
-      issue_stage(st + SG::kStages);
+      issue_stage(st + p.ring);
     }
   }
-  if (!active) return;
-  if (failed) {
-    // a TMA load never completed: report, drain what is still in flight, stop
+  if (active && failed) {
+    // a TMA load never completed: report and drain what is still in flight
     if (p.status && lane == 0) atomicOr(p.status, kStatusTimeout);
-    for (int st = max(0, nstages - SG::kStages); st < nstages; ++st)
-      mbar_wait_bounded(bars + st % SG::kStages, (st / SG::kStages) & 1);
-    return;
+    for (int st = done; st < min(nst, done + p.ring); ++st) mbar_wait_bounded(bars + st % p.ring, (st / p.ring) & 1);
   }
-
-  // ---- per-lane results: value[r][h][e] for activation column m = 2t + e
-  // (after reducing the lanes that hold other group slots of the same column)
-  float val[kGemvTiles][2][2];
-  if constexpr (kAffine) {
-#pragma unroll
-    for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        if constexpr (MC == 1) {
-          float v = res[r][h][0] + res[r][h][1];
-          v += __shfl_xor_sync(0xffffffffu, v, 1);
-          v += __shfl_xor_sync(0xffffffffu, v, 2);
-          val[r][h][0] = v;
-          val[r][h][1] = 0.f;
-        } else {
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            float v = res[r][h][e];
-            if constexpr (MC == 2) {
-              v += __shfl_xor_sync(0xffffffffu, v, 1);
-              v += __shfl_xor_sync(0xffffffffu, v, 2);
-            } else if constexpr (MC == 4) {
-              v += __shfl_xor_sync(0xffffffffu, v, 2);
-            }
-            val[r][h][e] = v;
-          }
-        }
-      }
-  } else {
-#pragma unroll
-    for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int e = 0; e < 2; ++e) {
-          float d = cacc[r][0][2 * h + e];
-          if constexpr (F::kPlanes == 2) d = fmaf(16.0f, cacc[r][1][2 * h + e], d);
-          if constexpr (WF == W_I8PC) d = fmaf(-(F::kCodeOffset + 128.0f), xsum[e], d);
-          val[r][h][e] = d;
-        }
-  }
-  // owner lanes: t < MC/2 (MC == 1: t == 0, e == 0); column m = 2t + e
-  const bool owner = (MC == 1) ? (t == 0) : (2 * t < MC);
-  auto col_ok = [&](int e) { return owner && (MC == 1 ? e == 0 : true) && (2 * t + e) < mcols; };
-
   grid_dependency_launch();
 
-  // ---- split-K: publish partials; the last warp of the row block reduces
-  if (p.splits > 1) {
-    float* part = p.partial + (static_cast<size_t>(split) * p.rows_padded + rb * 32) * 8;
+  // ---- per-lane results for activation row m of column 2t+e, summed over group slots
+  float val[2][2][2];
 #pragma unroll
-    for (int r = 0; r < kGemvTiles; ++r)
+  for (int r = 0; r < 2; ++r)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int e = 0; e < 2; ++e)
-          if (col_ok(e)) part[(r * 16 + h * 8 + g) * 8 + 2 * t + e] = val[r][h][e];
-    __threadfence();
-    __syncwarp();
-    unsigned prev = 0;
-    if (lane == 0) prev = atomicAdd(p.counters + rb, 1u);
-    prev = __shfl_sync(0xffffffffu, prev, 0);
-    if (prev != static_cast<unsigned>(p.splits - 1)) return;
-    __threadfence();
+      for (int e = 0; e < 2; ++e) val[r][h][e] = C::kScaled ? res[r][h][e] : cacc[r][2 * h + e];
 #pragma unroll
-    for (int r = 0; r < kGemvTiles; ++r)
+  for (int r = 0; r < 2; ++r)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < 2; ++h) {
+      if constexpr (MC == 1) {
+        float v = val[r][h][0] + val[r][h][1];
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        val[r][h][0] = v;
+      } else if constexpr (MC == 4) {
 #pragma unroll
-        for (int e = 0; e < 2; ++e) val[r][h][e] = 0.f;
-    // partial sums in a fixed split order; 8 splits of loads in flight at a time
-    for (int s0 = 0; s0 < p.splits; s0 += 8) {
-      float v[8][kGemvTiles][2][2];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float* ps = p.partial + (static_cast<size_t>(s0 + j) * p.rows_padded + rb * 32) * 8;
-#pragma unroll
-        for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int e = 0; e < 2; ++e)
-              v[j][r][h][e] = (s0 + j < p.splits && col_ok(e)) ? __ldcg(ps + (r * 16 + h * 8 + g) * 8 + 2 * t + e) : 0.f;
+        for (int e = 0; e < 2; ++e) val[r][h][e] += __shfl_xor_sync(0xffffffffu, val[r][h][e], 2);
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int r = 0; r < kGemvTiles; ++r)
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int e = 0; e < 2; ++e) val[r][h][e] += v[j][r][h][e];
     }
-    if (lane == 0) p.counters[rb] = 0u;
-  }
+  // owner lanes of activation row m = 2t + e (MC == 1: t == 0, e == 0)
+  auto own = [&](int e) {
+    if constexpr (MC == 1) return t == 0 && e == 0;
+    else return 2 * t < MC && 2 * t + e < M;
+  };
 
-  // ---- final epilogue: (tile r, box h) of this lane is weight row box_row0(h) + 8r + sigma(g)
-  if constexpr (EPI == EPI_ARGMAX) {
-    // per column m = 2t + e: best (value, row) over this lane's rows, then over g
-    float best[2] = {-INFINITY, -INFINITY};
-    int best_i[2] = {0x7FFFFFFF, 0x7FFFFFFF};
+  // ---- reduction over the K parts: pair P = warp*16 + 8r + g (rows of box A and B)
+  // of this CTA belongs to part P / ppc, which sums red[src][P % ppc][h][m] over src.
+  const int ppc = 64 / nparts;
+  if (active) {
+    const uint32_t red_u32 = smem_u32(red);
 #pragma unroll
-    for (int r = 0; r < kGemvTiles; ++r)
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int row = (h ? rowB : rowA) + 8 * r + sg;
-        if (row >= p.N) continue;
+      for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          const float v = val[r][h][e];
-          if (v > best[e] || (v == best[e] && row < best_i[e])) {
-            best[e] = v;
-            best_i[e] = row;
-          }
+          if (!own(e)) continue;
+          const int m = (MC == 1) ? 0 : 2 * t + e;
+          const int P = warp * 16 + 8 * r + g;
+          const int owner = P / ppc;
+          const uint32_t addr = red_u32 + static_cast<uint32_t>((((part * ppc + P % ppc) * 2 + h) * M + m) * 4);
+          if (nparts == 1) st_shared_f32(addr, val[r][h][e]);
+          else st_cluster_f32(cluster_map(addr, owner), val[r][h][e]);
         }
-      }
-#pragma unroll
-    for (int o = 4; o < 32; o <<= 1) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best[e], o);
-        const int oi = __shfl_xor_sync(0xffffffffu, best_i[e], o);
-        if (ov > best[e] || (ov == best[e] && oi < best_i[e])) {
-          best[e] = ov;
-          best_i[e] = oi;
-        }
-      }
+  }
+  if (nparts > 1) cluster_sync_all();
+  else __syncthreads();
+
+  // ---- final epilogue over this part's pairs
+  for (int idx = threadIdx.x; idx < ppc * M; idx += kNT) {
+    const int pl = idx / M, m = idx - (idx / M) * M;
+    const int P = part * ppc + pl;
+    const int w = P >> 4, r = (P >> 3) & 1, gg = P & 7;
+    const int rbx = blockIdx.y * kGemvWarps + w;
+    if (rbx >= rowblocks) continue;
+    float v_lo = 0.f, v_hi = 0.f;
+    for (int src = 0; src < nparts; ++src) {
+      v_lo += red[((src * ppc + pl) * 2 + 0) * M + m];
+      v_hi += red[((src * ppc + pl) * 2 + 1) * M + m];
     }
-    if (g == 0) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        if (col_ok(e) && best_i[e] != 0x7FFFFFFF)
-          atomicMax(p.argmax_keys + 2 * t + e, argmax_key(best[e], best_i[e] + p.argmax_offset));
-      }
-    }
-    return;
-  } else {
-    float scale_pc[kRows];
+    const int sgg = sigma_row<C::kLaneB>(gg);
+    const int row_lo = box_row0<EPI>(p, rbx, 0) + 8 * r + sgg;
+    const int row_hi = box_row0<EPI>(p, rbx, 1) + 8 * r + sgg;
     if constexpr (WF == W_I8PC) {
-#pragma unroll
-      for (int q = 0; q < kRows; ++q)
-        scale_pc[q] = static_cast<const float*>(set_of(q & 1) ? p.s1 : p.s0)[row_of(q >> 1, q & 1)];
+      if (row_lo < p.N) v_lo *= static_cast<const float*>(p.s0)[row_lo];
+      if (row_hi < p.N) v_hi *= static_cast<const float*>(p.s0)[row_hi];
     }
+    if constexpr (EPI == EPI_ARGMAX) {
+      unsigned long long best = 0ull;
+      if (row_lo < p.N) best = argmax_key(v_lo, row_lo + p.argmax_offset);
+      if (row_hi < p.N) {
+        const unsigned long long k2 = argmax_key(v_hi, row_hi + p.argmax_offset);
+        best = k2 > best ? k2 : best;
+      }
+      if (best) atomicMax(&s_keys[m], best);
+    } else if constexpr (EPI == EPI_SWIGLU) {
+      const int n = row_lo;  // gate row n (set 0) pairs with up row n (set 1)
+      if (n < p.N) {
+        const float gt = round_act<TA>(v_lo), up = round_act<TA>(v_hi);
+        const float silu = gt / (1.0f + expf(-gt));
+        store_act<TA>(p.y, static_cast<size_t>(m + p.m0) * p.ldy + n, silu * up);
+      }
+    } else if constexpr (EPI == EPI_ROPE) {
+      const int wph = p.head_dim / 32;
+      const int head = rbx / wph;
+      const int i = 16 * (rbx % wph) + 8 * r + sgg;  // rotation pair index
+      const int half = p.head_dim / 2;
+      float a = round_act<TA>(v_lo), b = round_act<TA>(v_hi);
+      void* out;
+      int hh, nh;
+      if (head < p.heads_q) {
+        out = p.q_out;
+        hh = head;
+        nh = p.heads_q;
+      } else if (head < p.heads_q + p.heads_kv) {
+        out = p.k_out;
+        hh = head - p.heads_q;
+        nh = p.heads_kv;
+      } else {
+        out = p.v_out;
+        hh = head - p.heads_q - p.heads_kv;
+        nh = p.heads_kv;
+      }
+      if (head < p.heads_q + p.heads_kv) {
+        const float angle = static_cast<float>(p.positions[m + p.m0]) * p.inv_freq[i];
+        float sn, cs;
+        sincosf(angle, &sn, &cs);
+        const float ra = a * cs - b * sn;
+        const float rb2 = b * cs + a * sn;
+        a = ra;
+        b = rb2;
+      }
+      const int bi = (m + p.m0) / p.seq_len, l = (m + p.m0) % p.seq_len;
+      const size_t obase = ((static_cast<size_t>(bi) * nh + hh) * p.seq_len + l) * p.head_dim;
+      store_act<TA>(out, obase + i, a);
+      store_act<TA>(out, obase + half + i, b);
+    } else {
 #pragma unroll
-    for (int r = 0; r < kGemvTiles; ++r) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        if (!col_ok(e)) continue;
-        const int m = 2 * t + e;
-        float v_lo = val[r][0][e], v_hi = val[r][1][e];
-        if constexpr (WF == W_I8PC) {
-          v_lo *= scale_pc[2 * r];
-          v_hi *= scale_pc[2 * r + 1];
-        }
-        if constexpr (EPI == EPI_SWIGLU) {
-          const int n = rowA + 8 * r + sg;
-          if (n < p.N) {
-            const float gt = round_act<TA>(v_lo), up = round_act<TA>(v_hi);
-            const float silu = gt / (1.0f + expf(-gt));
-            store_act<TA>(p.y, static_cast<size_t>(m) * p.ldy + n, silu * up);
-          }
-        } else if constexpr (EPI == EPI_ROPE) {
-          const int wph = p.head_dim / 32;
-          const int head = rb / wph;
-          const int i = 16 * (rb % wph) + 8 * r + sg;  // rotation pair index
-          const int half = p.head_dim / 2;
-          float a = round_act<TA>(v_lo), b = round_act<TA>(v_hi);
-          void* out;
-          int hh, nh;
-          if (head < p.heads_q) {
-            out = p.q_out;
-            hh = head;
-            nh = p.heads_q;
-          } else if (head < p.heads_q + p.heads_kv) {
-            out = p.k_out;
-            hh = head - p.heads_q;
-            nh = p.heads_kv;
-          } else {
-            out = p.v_out;
-            hh = head - p.heads_q - p.heads_kv;
-            nh = p.heads_kv;
-          }
-          if (head < p.heads_q + p.heads_kv) {
-            const float angle = static_cast<float>(p.positions[m]) * p.inv_freq[i];
-            float sn, cs;
-            sincosf(angle, &sn, &cs);
-            const float ra = a * cs - b * sn;
-            const float rb2 = b * cs + a * sn;
-            a = ra;
-            b = rb2;
-          }
-          const int bi = m / p.seq_len, l = m % p.seq_len;
-          const size_t obase = ((static_cast<size_t>(bi) * nh + hh) * p.seq_len + l) * p.head_dim;
-          store_act<TA>(out, obase + i, a);
-          store_act<TA>(out, obase + half + i, b);
+      for (int h = 0; h < 2; ++h) {
+        const int row = h ? row_hi : row_lo;
+        if (row >= p.N) continue;
+        const float v = h ? v_hi : v_lo;
+        const size_t o = static_cast<size_t>(m + p.m0) * p.ldy + row;
+        if constexpr (EPI == EPI_RESID) {
+          const float res_v = load_act<TA>(p.residual, static_cast<size_t>(m + p.m0) * p.ldr + row);
+          store_act<TA>(p.y, o, res_v + round_act<TA>(v));
         } else {
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int row = (h ? rowB : rowA) + 8 * r + sg;
-            if (row >= p.N) continue;
-            const float v = h ? v_hi : v_lo;
-            const size_t idx = static_cast<size_t>(m) * p.ldy + row;
-            if constexpr (EPI == EPI_RESID) {
-              const float res_v = load_act<TA>(p.residual, static_cast<size_t>(m) * p.ldr + row);
-              store_act<TA>(p.y, idx, res_v + round_act<TA>(v));
-            } else {
-              store_act<TA>(p.y, idx, v);
-            }
-          }
+          store_act<TA>(p.y, o, v);
         }
       }
     }
+  }
+  if constexpr (EPI == EPI_ARGMAX) {
+    __syncthreads();
+    if (threadIdx.x < M && s_keys[threadIdx.x]) atomicMax(p.argmax_keys + p.m0 + threadIdx.x, s_keys[threadIdx.x]);
   }
 }
 
@@ -732,133 +665,169 @@ __global__ void __launch_bounds__(kGemvWarps * 32, 2) gemv_kernel(const __grid_c
 
 namespace {
 
-int sm_count() {
-  static int count = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
-      count = 148;
-  });
-  return count;
-}
+constexpr int kMaxParts = 16;  // CTAs per cluster sharing one row group's K range
 
-struct Plan {
-  int tiles, rowblocks, groups, splits, k_group;
-  size_t counter_bytes, partial_bytes;
-  void* workspace;
-  size_t workspace_bytes;
+struct ClusterFit {
+  const void* kernel;
+  int parts;
+  size_t smem;
+  int clusters;
 };
 
-constexpr int kMaxGemvSplits = 32;
-
-// Row blocks and groups of a request; the split count is chosen at launch from
-// the kernel's occupancy. partial_bytes covers the largest split count allowed.
-Plan make_plan(int epi, int N, int K, int group_k, bool allow_split) {
-  Plan pl{};
-  pl.tiles = 0;
-  pl.rowblocks = epi == EPI_SWIGLU ? (N + 15) / 16 : (epi == EPI_ROPE ? N / 32 : (N + 31) / 32);
-  pl.k_group = group_k;
-  pl.groups = K / group_k;
-  const int max_s = (allow_split && pl.rowblocks <= kMaxCounters) ? std::max(1, std::min(kMaxGemvSplits, pl.groups / 2)) : 1;
-  pl.splits = max_s;
-  pl.counter_bytes = kCounterBytes;
-  pl.partial_bytes = max_s > 1 ? static_cast<size_t>(max_s) * pl.rowblocks * 32 * 8 * sizeof(float) : 0;
-  return pl;
+// Largest number of co-resident clusters of `parts` CTAs (cached per kernel and size).
+int max_active_clusters(const void* kernel, int parts, size_t smem, int row_groups) {
+  static std::mutex mu;
+  static std::vector<ClusterFit> cache;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (const ClusterFit& c : cache)
+      if (c.kernel == kernel && c.parts == parts && c.smem == smem) return c.clusters;
+  }
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(parts, std::max(1, row_groups));
+  config.blockDim = dim3(kGemvWarps * 32);
+  config.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(parts);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  config.attrs = attr;
+  config.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kernel, &config) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache.push_back({kernel, parts, smem, n});
+  return n;
 }
 
-template <typename TA, int WF, int KC, int GC, int EPI, bool NORM, int MC>
-int launch_gemv_mc(GemvParams& p, const Plan& plan, cudaStream_t stream) {
-  using SG = StageGeom<Fmt<TA, WF>::kBits>;
-  constexpr bool kAff = (WF == W_AFF4 || WF == W_AFF8);
-  auto kernel = gemv_kernel<TA, WF, KC, GC, EPI, NORM, MC>;
-  // activation segment: at most 8 KB of shared memory, whole stages and whole
-  // super-groups (so a super-group's group sums are staged together)
-  const int super_k = kAff ? (8 / MC) * p.group_size : SG::kStageK;
-  const int unit = std::max(SG::kStageK, super_k);
-  auto smem_for = [&](int splits) {
-    const int max_kunit = (plan.groups + splits - 1) / splits * plan.k_group;
-    int seg = (8192 / (p.M * static_cast<int>(sizeof(TA)))) / unit * unit;
-    seg = std::max(seg, unit);
-    p.x_seg = std::min(seg, ((max_kunit + unit - 1) / unit) * unit);
-    const size_t xg_bytes = static_cast<size_t>(p.M) * (p.x_seg / plan.k_group + 1) * sizeof(float);
-    return 2048 + static_cast<size_t>(kGemvWarps) * SG::kStages * SG::kStageBytes +
-           static_cast<size_t>(p.M) * (p.x_seg + 8) * sizeof(TA) + xg_bytes;
-  };
-  size_t smem = smem_for(1);
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
-      cudaSuccess)
+// One-time function attributes: the shared-memory opt-in and cluster sizes above 8.
+bool prepare_kernel(const void* kernel, bool* large_clusters) {
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, bool>> done;
+  std::lock_guard<std::mutex> lock(mu);
+  for (const auto& d : done)
+    if (d.first == kernel) {
+      *large_clusters = d.second;
+      return true;
+    }
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  bool large = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+  if (!large) cudaGetLastError();
+  done.emplace_back(kernel, large);
+  *large_clusters = large;
+  return true;
+}
+
+int rowblocks_of(int epi, int N) {
+  return epi == EPI_SWIGLU ? (N + 15) / 16 : (epi == EPI_ROPE ? N / 32 : (N + 31) / 32);
+}
+
+template <typename TA, int WF, int G, int EPI, bool NORM, int MC>
+int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
+  using C = Geo<WF, G, MC>;
+  auto kernel = gemv_kernel<TA, WF, G, EPI, NORM, MC>;
+  bool large_clusters = false;
+  if (!prepare_kernel(reinterpret_cast<const void*>(kernel), &large_clusters))
     return fail(SB_ECUDA, "gemv: shared memory opt-in failed");
-  // splits: fill the resident CTA slots in one wave (no tail wave)
-  int splits = 1;
-  const int ctas_per_split = (plan.rowblocks + kGemvWarps - 1) / kGemvWarps;
-  if (plan.splits > 1 && plan.workspace != nullptr &&
-      plan.workspace_bytes >= plan.counter_bytes + plan.partial_bytes) {
-    int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, kGemvWarps * 32, smem) != cudaSuccess || occ < 1)
-      occ = 1;
-    const int slots = sm_count() * occ;
-    splits = std::max(1, std::min(plan.splits, slots / ctas_per_split));
+  const int row_groups = (rowblocks_of(EPI, p.N) + kGemvWarps - 1) / kGemvWarps;
+  const int row_bytes = static_cast<int>(static_cast<int64_t>(p.K) * C::kBits / 8);
+  p.stages_total = (row_bytes + 127) / 128;
+
+  // Per candidate cluster size: ring depth, activation segment, shared memory.
+  auto configure = [&](int parts) {
+    const int per = (p.stages_total + parts - 1) / parts;  // most stages of one CTA
+    p.ring = std::max(1, std::min(per, 4));
+    const int per_stage = C::kGPS * (C::kYG + 16) * p.M;  // staged x + meta bytes per stage
+    p.seg_stages = std::max(1, std::min(per, (16 * 1024) / per_stage));
+    const int seg_groups = p.seg_stages * C::kGPS;
+    p.y_ld = seg_groups * C::kYG;
+    if (((p.y_ld / 16) & 1) == 0) p.y_ld += 16;  // rows of different m start in different banks
+    p.meta_ld = seg_groups;
+    return static_cast<size_t>(2048) + static_cast<size_t>(kGemvWarps) * p.ring * kStageBytes +
+           static_cast<size_t>(p.M) * p.y_ld + static_cast<size_t>(p.M) * p.meta_ld * 16 +
+           static_cast<size_t>(128) * p.M * sizeof(float);
+  };
+  // Largest cluster (K split) whose clusters are all co-resident, each CTA with
+  // at least two stages; 1 when the row groups alone fill the GPU.
+  int parts = 1;
+  size_t smem = 0;
+  for (int cand = kMaxParts; cand >= 1; cand >>= 1) {
+    if (cand > 1 && (p.stages_total < 2 * cand || (cand > 8 && !large_clusters))) continue;
+    smem = configure(cand);
+    if (cand == 1 || max_active_clusters(reinterpret_cast<const void*>(kernel), cand, smem, row_groups) >= row_groups) {
+      parts = cand;
+      break;
+    }
   }
-  smem = smem_for(splits);
-  p.splits = splits;
-  p.groups_total = plan.groups;
-  p.rows_padded = plan.rowblocks * 32;
-  if (splits > 1) {
-    p.counters = static_cast<unsigned*>(plan.workspace);
-    p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(plan.workspace) + plan.counter_bytes);
-  }
-  dim3 grid(ctas_per_split, splits);
-  return launch("gemv", kernel, grid, dim3(kGemvWarps * 32), smem, stream, p);
+  dim3 grid(parts, row_groups);
+  return launch_cluster("gemv", kernel, grid, dim3(kGemvWarps * 32), smem, parts, stream, p);
 }
 
-template <typename TA, int WF, int KC, int GC, int EPI, bool NORM>
-int launch_gemv(GemvParams& p, const Plan& pl, cudaStream_t stream) {
-  if (p.M == 1) return launch_gemv_mc<TA, WF, KC, GC, EPI, NORM, 1>(p, pl, stream);
-  if (p.M <= 4) return launch_gemv_mc<TA, WF, KC, GC, EPI, NORM, 4>(p, pl, stream);
-  return launch_gemv_mc<TA, WF, KC, GC, EPI, NORM, 8>(p, pl, stream);
+template <typename TA, int WF, int G, int EPI, bool NORM>
+int launch_gemv(GemvParams& p, cudaStream_t stream) {
+  if (p.M == 1) return launch_gemv_mc<TA, WF, G, EPI, NORM, 1>(p, stream);
+  if (p.M <= 4) return launch_gemv_mc<TA, WF, G, EPI, NORM, 4>(p, stream);
+  if constexpr (G == 32 && (WF == W_AFF4 || WF == W_AFF8)) {
+    // a 32-wide group has too few codes per lane for the 8-column layout:
+    // activation rows 0-3 and 4.. go as two launches of the 4-column layout
+    GemvParams hi = p;
+    p.M = 4;
+    if (int st = launch_gemv_mc<TA, WF, G, EPI, NORM, 4>(p, stream)) return st;
+    hi.M -= 4;
+    hi.m0 += 4;
+    hi.x = static_cast<const TA*>(hi.x) + static_cast<size_t>(4) * hi.ldx;
+    return launch_gemv_mc<TA, WF, G, EPI, NORM, 4>(hi, stream);
+  } else {
+    return launch_gemv_mc<TA, WF, G, EPI, NORM, 8>(p, stream);
+  }
 }
 
 template <typename TA, int WF, int EPI, bool NORM>
-int dispatch_group(GemvParams& p, const Plan& pl, cudaStream_t stream) {
+int dispatch_group(GemvParams& p, cudaStream_t stream) {
   if constexpr (WF == W_AFF4 || WF == W_AFF8) {
     switch (p.group_size) {
       case 32:
-        return launch_gemv<TA, WF, 32, 1, EPI, NORM>(p, pl, stream);
+        return launch_gemv<TA, WF, 32, EPI, NORM>(p, stream);
       case 64:
-        return launch_gemv<TA, WF, 64, 1, EPI, NORM>(p, pl, stream);
+        return launch_gemv<TA, WF, 64, EPI, NORM>(p, stream);
       case 128:
-        return launch_gemv<TA, WF, 64, 2, EPI, NORM>(p, pl, stream);
+        return launch_gemv<TA, WF, 128, EPI, NORM>(p, stream);
       default:
         return fail(SB_EUNSUPPORTED, "group_size must be 32, 64 or 128");
     }
   } else {
-    return launch_gemv<TA, WF, 64, 1, EPI, NORM>(p, pl, stream);
+    return launch_gemv<TA, WF, 64, EPI, NORM>(p, stream);
   }
 }
 
 template <int EPI, bool NORM>
-int dispatch_fmt(int wf, int x_dtype, GemvParams& p, const Plan& pl, cudaStream_t stream) {
+int dispatch_fmt(int wf, int x_dtype, GemvParams& p, cudaStream_t stream) {
   constexpr bool kAffineEpi = EPI != EPI_ARGMAX;
   constexpr bool kI8Epi = EPI == EPI_STORE || EPI == EPI_RESID || EPI == EPI_ROPE;
   constexpr bool kBf16Epi = EPI == EPI_STORE || EPI == EPI_ARGMAX;
   if (x_dtype == SB_DTYPE_BF16) {
     if constexpr (kAffineEpi) {
-      if (wf == W_AFF4) return dispatch_group<__nv_bfloat16, W_AFF4, EPI, NORM>(p, pl, stream);
-      if (wf == W_AFF8) return dispatch_group<__nv_bfloat16, W_AFF8, EPI, NORM>(p, pl, stream);
+      if (wf == W_AFF4) return dispatch_group<__nv_bfloat16, W_AFF4, EPI, NORM>(p, stream);
+      if (wf == W_AFF8) return dispatch_group<__nv_bfloat16, W_AFF8, EPI, NORM>(p, stream);
     }
     if constexpr (kI8Epi) {
-      if (wf == W_I8PC) return dispatch_group<__nv_bfloat16, W_I8PC, EPI, NORM>(p, pl, stream);
+      if (wf == W_I8PC) return dispatch_group<__nv_bfloat16, W_I8PC, EPI, NORM>(p, stream);
     }
     if constexpr (kBf16Epi) {
-      if (wf == W_BF16) return dispatch_group<__nv_bfloat16, W_BF16, EPI, NORM>(p, pl, stream);
+      if (wf == W_BF16) return dispatch_group<__nv_bfloat16, W_BF16, EPI, NORM>(p, stream);
     }
   } else if (x_dtype == SB_DTYPE_F16) {
     if constexpr (EPI == EPI_STORE || EPI == EPI_ROPE) {
-      if (wf == W_AFF4) return dispatch_group<__half, W_AFF4, EPI, NORM>(p, pl, stream);
-      if (wf == W_AFF8) return dispatch_group<__half, W_AFF8, EPI, NORM>(p, pl, stream);
-      if (wf == W_I8PC) return dispatch_group<__half, W_I8PC, EPI, NORM>(p, pl, stream);
+      if (wf == W_AFF4) return dispatch_group<__half, W_AFF4, EPI, NORM>(p, stream);
+      if (wf == W_AFF8) return dispatch_group<__half, W_AFF8, EPI, NORM>(p, stream);
+      if (wf == W_I8PC) return dispatch_group<__half, W_I8PC, EPI, NORM>(p, stream);
     }
   }
   return fail(SB_EUNSUPPORTED, "unsupported activation dtype / weight format / epilogue combination");
@@ -871,10 +840,13 @@ static int group_k_of(const LinearRequest& r) {
   return 64;
 }
 
+// The weight-streaming kernels need no scratch: the K split reduces through
+// distributed shared memory. The workspace only carries the status word.
 size_t linear_workspace_size(int epi, int N, int K, int group_k) {
+  (void)epi;
+  (void)N;
   if (group_k <= 0 || K % group_k) return 0;
-  const Plan pl = make_plan(epi, N, K, group_k, true);
-  return pl.counter_bytes + pl.partial_bytes;
+  return kCounterBytes;
 }
 
 int run_linear(const LinearRequest& r, cudaStream_t stream) {
@@ -888,16 +860,13 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
              "weights must be 16-byte aligned");
   SB_REQUIRE((static_cast<int64_t>(r.K) * (r.wf == W_AFF4 ? 4 : (r.wf == W_BF16 ? 16 : 8)) / 8) % 16 == 0,
              "weight rows must be a multiple of 16 bytes");
+  if (r.norm) SB_REQUIRE((reinterpret_cast<uintptr_t>(r.norm_w) & 15) == 0, "norm weight must be 16-byte aligned");
   if (r.epi == EPI_ROPE) {
-    SB_REQUIRE(r.head_dim % 16 == 0 && r.head_dim / 2 <= kMaxRopeHalf, "head_dim must be a multiple of 16, <= 256");
+    SB_REQUIRE(r.head_dim % 32 == 0 && r.head_dim / 2 <= kMaxRopeHalf, "head_dim must be a multiple of 32, <= 256");
     SB_REQUIRE(r.rope_dims == r.head_dim, "the fused RoPE epilogue rotates the full head_dim");
     SB_REQUIRE(r.N == (r.heads_q + 2 * r.heads_kv) * r.head_dim, "QKV rows must equal (Hq + 2*Hkv) * head_dim");
   }
   if (r.epi == EPI_SWIGLU) SB_REQUIRE(r.N % 8 == 0, "SwiGLU width must be a multiple of 8");
-
-  Plan pl = make_plan(r.epi, r.N, r.K, gk, true);
-  pl.workspace = r.workspace;
-  pl.workspace_bytes = r.workspace_bytes;
 
   GemvParams p{};
   p.x = r.x;
@@ -912,8 +881,11 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   p.s1 = r.s1 ? r.s1 : r.s0;
   p.b1 = r.b1 ? r.b1 : r.b0;
   p.group_size = r.group_size;
-  p.groups_total = pl.groups;
-  p.rows_padded = pl.rowblocks * 32;
+  {
+    const int gpr = r.K / gk;
+    auto al4 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 3) == 0; };
+    p.pair_scales = (gpr % 2 == 0) && al4(p.s0) && al4(p.b0) && al4(p.s1) && al4(p.b1) ? 1 : 0;
+  }
   {
     const int bits = r.wf == W_AFF4 ? 4 : (r.wf == W_BF16 ? 16 : 8);
     const uint64_t row_bytes = static_cast<uint64_t>(r.K) * bits / 8;
@@ -946,19 +918,19 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
 
   switch (r.epi) {
     case EPI_STORE:
-      return r.norm ? dispatch_fmt<EPI_STORE, true>(r.wf, r.x_dtype, p, pl, stream)
-                    : dispatch_fmt<EPI_STORE, false>(r.wf, r.x_dtype, p, pl, stream);
+      return r.norm ? dispatch_fmt<EPI_STORE, true>(r.wf, r.x_dtype, p, stream)
+                    : dispatch_fmt<EPI_STORE, false>(r.wf, r.x_dtype, p, stream);
     case EPI_RESID:
-      return dispatch_fmt<EPI_RESID, false>(r.wf, r.x_dtype, p, pl, stream);
+      return dispatch_fmt<EPI_RESID, false>(r.wf, r.x_dtype, p, stream);
     case EPI_SWIGLU:
-      return r.norm ? dispatch_fmt<EPI_SWIGLU, true>(r.wf, r.x_dtype, p, pl, stream)
-                    : dispatch_fmt<EPI_SWIGLU, false>(r.wf, r.x_dtype, p, pl, stream);
+      return r.norm ? dispatch_fmt<EPI_SWIGLU, true>(r.wf, r.x_dtype, p, stream)
+                    : dispatch_fmt<EPI_SWIGLU, false>(r.wf, r.x_dtype, p, stream);
     case EPI_ROPE:
-      return r.norm ? dispatch_fmt<EPI_ROPE, true>(r.wf, r.x_dtype, p, pl, stream)
-                    : dispatch_fmt<EPI_ROPE, false>(r.wf, r.x_dtype, p, pl, stream);
+      return r.norm ? dispatch_fmt<EPI_ROPE, true>(r.wf, r.x_dtype, p, stream)
+                    : dispatch_fmt<EPI_ROPE, false>(r.wf, r.x_dtype, p, stream);
     case EPI_ARGMAX:
-      return r.norm ? dispatch_fmt<EPI_ARGMAX, true>(r.wf, r.x_dtype, p, pl, stream)
-                    : dispatch_fmt<EPI_ARGMAX, false>(r.wf, r.x_dtype, p, pl, stream);
+      return r.norm ? dispatch_fmt<EPI_ARGMAX, true>(r.wf, r.x_dtype, p, stream)
+                    : dispatch_fmt<EPI_ARGMAX, false>(r.wf, r.x_dtype, p, stream);
   }
   return fail(SB_EINVAL, "unknown epilogue");
 }

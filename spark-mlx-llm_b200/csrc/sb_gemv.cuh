@@ -9,21 +9,29 @@
 //                     (w8a16_per_channel, src/spark_w8a16.cpp:80-110)
 //   W_BF16          : plain bf16 [N, K] (the synthetic model's lm_head)
 //
-// Design (B200): the path is HBM-bound, so each weight byte is read once with
-// coalesced 8/16-byte loads and dequantized in registers. The dot products
-// run on the tensor cores through mma.sync m16n8k16 using the RAW codes as the
-// A operand: a 4-bit code q becomes the exact bf16 value 128+q by OR-ing it
-// into the mantissa of 128.0 (0x4300), an 8-bit code is split into two exact
-// nibble planes, and fp16 activations use 1024+q (0x6400). Products are exact
-// and accumulate in fp32; the per-group scale and bias are applied in fp32
-// afterwards as  y += scale * sum(code*x) + bias * sum(x),  the same
-// reassociation the reference kernels use (spark_mlx_ext/_w4a16_sources.py:
-// 24-39). sum(x) per group comes from one extra MMA against a matrix of ones.
-// The activation columns (M <= 8) fill the MMA's n=8 dimension, so M = 1..8
-// costs the same instruction count. A warp owns 32 weight rows (two m16
-// tiles) over a K range; K is split across warps when N alone cannot fill the
-// 148 SMs, and the last warp to finish a row block reduces the partial sums
-// in a fixed order (deterministic, single launch).
+// Design (B200): the path is HBM-bound, so each weight byte is read once,
+// streamed by 2-D TMA (16 rows x 128 B boxes, 128-byte swizzle) into a
+// per-warp ring of shared-memory stages, and dequantized in registers. The dot
+// products run on the tensor cores (mma.sync m16n8k16) with the RAW codes as
+// the A operand: OR-ing a code into the mantissa of a power of two gives an
+// exact small integer (4-bit: low nibble bf16 128+q, high nibble fp16 64+q,
+// one shift and four LOP3 per 8 codes; 8-bit: fp16 1024+u, one byte permute
+// per 2 codes). The activations are staged once per CTA in the matching
+// operand type, scaled by a power of two per K group (exact; the group's
+// largest value lands in [2^14, 2^15) so fp16 cannot overflow), with the
+// group's sums sum(offset_k * xs_k) and sum(x). Products are exact and
+// accumulate in fp32; the group's scale and bias are applied afterwards as
+//     y += scale * 2^-e * (acc - sum(offset_k * xs_k)) + bias * sum(x),
+// the reassociation the reference kernels use (spark_mlx_ext/
+// _w4a16_sources.py:24-39). The MMA's 8 columns carry (activation row, group
+// slot) pairs, so at M = 1 one accumulator tile holds up to 8 groups and the
+// scale epilogue runs once per stage. bf16 weights (lm_head) multiply bf16
+// activations directly. A warp owns 32 weight rows (two m16 tiles); a CTA's 4
+// warps share one K range and one staged activation segment. When N alone
+// cannot fill the 148 SMs, K is split over the CTAs of a thread-block cluster,
+// and the partial sums meet in distributed shared memory: each CTA reduces a
+// slice of the rows from every rank in a fixed order (deterministic, one
+// launch, no global workspace).
 #pragma once
 
 #include "sb_common.cuh"
@@ -39,18 +47,20 @@ enum Epilogue : int {
   EPI_ARGMAX = 4,  // greedy token: argmax over rows of fp32 logits
 };
 
-constexpr int kGemvWarps = 4;   // warps per CTA (one work unit each)
-constexpr int kGemvTiles = 2;   // m16 tiles per warp (32 weight rows)
+constexpr int kGemvWarps = 4;   // warps per CTA (one 32-row block each)
+constexpr int kGemvMaxRing = 8; // TMA stages in flight per warp (upper bound)
 constexpr int kMaxRopeHalf = 128;
 
 struct GemvParams {
   // TMA descriptors of weight set 0 and 1 ([rows][K*bits/8] bytes, 16x128 B boxes)
   alignas(64) CUtensorMap tmap0;
   alignas(64) CUtensorMap tmap1;
-  // activations [M][ldx] (bf16 or fp16)
+  // activations [M][ldx] (bf16 or fp16); m0 = index of row 0 in the outputs
+  // (and positions / argmax keys) when one request is split into launches
   const void* x;
   int ldx;
   int M, N, K;
+  int m0;
   // weight set 0 and (EPI_SWIGLU) set 1
   const void* w0;
   const void* s0;
@@ -59,12 +69,14 @@ struct GemvParams {
   const void* s1;
   const void* b1;
   int group_size;  // affine group; 0 for per-channel / bf16
-  // split-K
-  int splits;
-  int groups_total;  // number of K groups (affine: K/G; others: K/64)
-  float* partial;    // [splits][rows_padded][8]
-  unsigned* counters;  // [rowblocks], zero on entry, left zero on exit
-  int rows_padded;
+  // K partition: stages (128 weight bytes per row) in total; gridDim.x CTAs of
+  // a cluster split them; each warp keeps `ring` stages in flight
+  int stages_total;
+  int ring;
+  int seg_stages;  // stages whose activations are staged in shared memory at a time
+  int y_ld;        // bytes per activation row of the staged segment
+  int meta_ld;     // groups per activation row of the staged segment
+  int pair_scales; // 1 when two consecutive groups' scales are 4-byte aligned
   // rms-norm prologue (optional)
   const void* norm_w;
   float eps;
@@ -83,7 +95,6 @@ struct GemvParams {
   // argmax epilogue
   unsigned long long* argmax_keys;  // [M]
   int argmax_offset;                // added to row indices (vocab-parallel shards)
-  int x_seg;                        // K values of x staged in shared memory at a time
   unsigned* status;                 // device status word (bounded-wait timeouts) or null
   // 1: the weights are constant across the stream (model weights), so the
   // kernel may start streaming them before the previous kernel finishes.

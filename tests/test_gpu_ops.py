@@ -76,6 +76,36 @@ def test_affine_linear_fp16_activations(sb):
     assert_close(to_f32(y), expected, what="affine fp16")
 
 
+@pytest.mark.parametrize("m,k,n,group,bits", [(1, 2496, 300, 64, 4), (2, 1088, 130, 64, 8), (6, 1216, 72, 64, 4),
+                                              (1, 576, 40, 32, 4), (3, 1280, 48, 128, 4)])
+def test_affine_linear_ragged_k_wide_range(sb, m, k, n, group, bits):
+    """K ending inside a 128-byte weight stage, partial row blocks, and activation
+    groups spread over nine decades (plus an all-zero group): the staged operands
+    are scaled per group by a power of two, which must stay exact."""
+    rng = np.random.default_rng(50 + m + k + n)
+    packed, s_bits, b_bits = make_affine(rng, n, k, group, bits)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x *= np.repeat(10.0 ** rng.uniform(-6, 3, size=(m, k // group)), group, axis=1).astype(np.float32)
+    x[:, :group] = 0.0
+    x = formats.round_bf16(x)
+    expected = ref.affine_linear(x, packed, formats.bf16_from_bits(s_bits), formats.bf16_from_bits(b_bits), group, bits)
+    y = sb.affine_linear(bf16_tensor(x), u32_tensor(packed), bf16_bits_tensor(s_bits), bf16_bits_tensor(b_bits),
+                         group, bits)
+    assert_close(to_f32(y), expected, what="affine ragged/wide")
+
+
+def test_w8a16_wide_range(sb):
+    rng = np.random.default_rng(77)
+    m, k, n = 2, 1088, 100
+    wq, ws = quant.quantize_w8_per_channel((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    x *= np.repeat(10.0 ** rng.uniform(-5, 3, size=(m, k // 64)), 64, axis=1).astype(np.float32)
+    x = formats.round_bf16(x)
+    expected = ref.w8a16_per_channel(x, wq, ws)
+    y = sb.w8a16_per_channel(bf16_tensor(x), torch.from_numpy(wq).cuda(), torch.from_numpy(ws).cuda())
+    assert_close(to_f32(y), expected, what="w8a16 wide")
+
+
 def test_w8a16_known_answer(sb):
     """extensions/spark-mlx-ext/README.md:32-48: ones x ones -> 32."""
     x = torch.ones(64, dtype=torch.bfloat16, device="cuda")
