@@ -29,6 +29,10 @@ inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(s
 // [box_rows x 128 B] box and the 128-byte swizzle (16-byte units of row i are
 // permuted by XOR with i % 8 in shared memory). Out-of-range reads fill zeros.
 int make_tmap_rows(CUtensorMap* map, const void* base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows);
+// 2-D TMA descriptor over a row-major uint16 matrix [rows][cols] (no swizzle),
+// box [box_rows x box_cols]; out-of-range reads fill zeros.
+int make_tmap_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                  uint32_t box_rows);
 
 // Every workspace starts with a fixed-size region of arrival counters (zero
 // between calls), followed by the call's partial results. The fixed size keeps
@@ -162,6 +166,13 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+
+// Ampere-style asynchronous 4-byte global -> shared copy (no registers held).
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 // ------------------------------------------------- thread-block cluster (DSMEM)
 // Address of the same shared-memory offset in CTA `rank` of this cluster.

@@ -66,6 +66,33 @@ struct Enc {
   static constexpr float kOffOdd = WF == W_AFF4 ? 64.0f : kOffEven;
 };
 
+// Staged-activation layout inside one group: the 8-value vector at k (a
+// multiple of 8) holds four operand pairs. When a lane's two streams are
+// adjacent pieces of one group (kSlots <= 4), the pairs of the two pieces are
+// interleaved (lo j, hi j, lo j+1, hi j+1, ...) so one 16-byte load yields the
+// B operands of two k16 steps in register order; otherwise vectors are stored
+// in place.
+template <typename C>
+__device__ __forceinline__ int y_offset(int k) {
+  if constexpr (C::kSlots <= 4) {
+    const int piece = k / C::kPieceK, qd = (k % C::kPieceK) / 8;
+    return (piece >> 1) * C::kPieceK * 4 + qd * 32 + (piece & 1) * 4;
+  } else {
+    return k * 2;
+  }
+}
+template <typename C>
+__device__ __forceinline__ void store_pairs(uint8_t* dst, uint4 v) {
+  if constexpr (C::kSlots <= 4) {
+    *reinterpret_cast<uint32_t*>(dst) = v.x;
+    *reinterpret_cast<uint32_t*>(dst + 8) = v.y;
+    *reinterpret_cast<uint32_t*>(dst + 16) = v.z;
+    *reinterpret_cast<uint32_t*>(dst + 24) = v.w;
+  } else {
+    *reinterpret_cast<uint4*>(dst) = v;
+  }
+}
+
 // Row relabeling inside each 8-row half of a box so that the lanes' reads of
 // the 128-byte-swizzled rows fall into distinct banks for their access width.
 template <int kLaneB>
@@ -187,14 +214,18 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(base) + warp * kGemvMaxRing;
   const uint8_t* zero_blk = base + 512;
+  uint64_t* scbar = reinterpret_cast<uint64_t*>(base + 256);  // scale/bias TMA barrier
   uint8_t* ring = base + 1024 + warp * p.ring * kStageBytes;
-  uint8_t* ys = base + 1024 + kGemvWarps * p.ring * kStageBytes;
+  // staged scales and biases (affine): [warp][row h*16 + i][sc_ld] of the current segment
+  uint16_t* scs = reinterpret_cast<uint16_t*>(base + 1024 + kGemvWarps * p.ring * kStageBytes);
+  uint16_t* scb = scs + kGemvWarps * 32 * p.sc_ld;
+  uint8_t* ys = reinterpret_cast<uint8_t*>(scb + kGemvWarps * 32 * p.sc_ld);
   float4* meta = reinterpret_cast<float4*>(ys + M * p.y_ld);
   float* red = reinterpret_cast<float*>(meta + M * p.meta_ld);
 
   const int rowA = box_row0<EPI>(p, rbc, 0), rowB = box_row0<EPI>(p, rbc, 1);
-  auto issue_stage = [&](int st) {
-    const int slot = st % p.ring;
+  auto set_of = [&](int h) { return (EPI == EPI_SWIGLU) ? h : 0; };
+  auto issue_stage = [&](int slot, int st) {
     uint8_t* dst = ring + slot * kStageBytes;
     mbar_arrive_expect_tx(bars + slot, kStageBytes);
     const int x = (st0 + st) * 128;
@@ -202,8 +233,83 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
     tma_load_2d(dst + 16 * 128, &p.tmap1, x, rowB, bars + slot);
   };
 
+  // Scales and biases of the CTA's 4 x 32 rows for the groups of stages
+  // [sb, sb + seg_stages) into shared memory: by TMA (boxes of 16 rows from the
+  // group G0 rounded down to 8; sc_off = G0 % 8) when the tables allow it, else
+  // by 4-byte asynchronous copies or plain loads, with the columns past the
+  // range zeroed. Completion: scbar (TMA) or cp.async.wait_all, both at the
+  // end of the segment's activation staging.
+  int sc_off = 0;
+  auto stage_scales = [&](int sb) {
+    if constexpr (C::kAffine) {
+      const int G0 = (st0 + sb) * C::kGPS;
+      if (p.sc_tma) {
+        sc_off = G0 & 7;
+        if (threadIdx.x == 0) {
+          fence_proxy_async_smem();
+          mbar_arrive_expect_tx(scbar, static_cast<uint32_t>(2 * kGemvWarps * 32 * p.sc_ld * 2));
+          for (int w = 0; w < kGemvWarps; ++w) {
+            const int rbw = min(static_cast<int>(blockIdx.y) * kGemvWarps + w, rowblocks - 1);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int row0 = box_row0<EPI>(p, rbw, h);
+              const int o = (w * 32 + h * 16) * p.sc_ld;
+              tma_load_2d(scs + o, set_of(h) ? &p.smap1 : &p.smap0, G0 - sc_off, row0, scbar);
+              tma_load_2d(scb + o, set_of(h) ? &p.bmap1 : &p.bmap0, G0 - sc_off, row0, scbar);
+            }
+          }
+        }
+        return;
+      }
+      const int G1 = min(min(st0 + sb + p.seg_stages, st1) * C::kGPS, gpr);
+      const int ng = max(G1 - G0, 0);
+      const bool async = (C::kGPS % 2 == 0) && p.pair_scales;
+      const int per_row = async ? ng / 2 : ng;  // copies per row and array
+      const int total = 2 * kGemvWarps * 32 * per_row;
+      for (int idx = threadIdx.x; idx < total; idx += kNT) {
+        const int which = idx / (kGemvWarps * 32 * per_row);  // 0 scales, 1 biases
+        const int rem = idx - which * (kGemvWarps * 32 * per_row);
+        const int wr = rem / per_row, c = rem - (rem / per_row) * per_row;
+        const int w = wr >> 5, row = wr & 31, h = row >> 4;
+        const int rbw = min(static_cast<int>(blockIdx.y) * kGemvWarps + w, rowblocks - 1);
+        const int grow = min(box_row0<EPI>(p, rbw, h) + (row & 15), p.N - 1);
+        const uint16_t* src = static_cast<const uint16_t*>(which ? (set_of(h) ? p.b1 : p.b0) : (set_of(h) ? p.s1 : p.s0)) +
+                              static_cast<size_t>(grow) * gpr + G0;
+        uint16_t* dst = (which ? scb : scs) + wr * p.sc_ld;
+        if (async) cp_async4(dst + 2 * c, src + 2 * c);
+        else dst[c] = src[c];
+      }
+      // zero the padding columns [ng, sc_ld) of every row
+      const int pad = p.sc_ld - ng;
+      for (int idx = threadIdx.x; idx < 2 * kGemvWarps * 32 * pad; idx += kNT) {
+        const int which = idx / (kGemvWarps * 32 * pad);
+        const int rem = idx - which * (kGemvWarps * 32 * pad);
+        const int wr = rem / pad, c = ng + rem - (rem / pad) * pad;
+        (which ? scb : scs)[wr * p.sc_ld + c] = 0;
+      }
+      cp_async_commit();
+    }
+  };
+  int sc_phase = 0;
+  auto wait_scales = [&]() {
+    if constexpr (C::kAffine) {
+      if (p.sc_tma) {
+        if (!mbar_wait_bounded(scbar, static_cast<uint32_t>(sc_phase))) {
+          if (p.status && threadIdx.x == 0) atomicOr(p.status, kStatusTimeout);
+        }
+        sc_phase ^= 1;
+      } else {
+        cp_async_wait_all();
+      }
+    }
+  };
+
   if (active && lane == 0) {
     for (int i = 0; i < p.ring; ++i) mbar_init(bars + i, 1);
+    mbar_fence_init();
+  }
+  if (C::kAffine && threadIdx.x == 0) {
+    mbar_init(scbar, 1);
     mbar_fence_init();
   }
   __syncwarp();
@@ -211,36 +317,75 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   // tail of the previous kernel in the stream
   if (!p.early_prefetch) grid_dependency_wait();
   if (active && lane == 0) {
-    for (int st = 0; st < p.ring && st < nst; ++st) issue_stage(st);
+    for (int st = 0; st < p.ring && st < nst; ++st) issue_stage(st, st);
   }
+  if (p.early_prefetch && nst > 0) stage_scales(0);
   if (threadIdx.x < 32) reinterpret_cast<uint4*>(base + 512)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
   if (threadIdx.x < 8) s_keys[threadIdx.x] = 0ull;
 
   // ---- activations depend on the previous kernel from here on
   grid_dependency_wait();
-  if constexpr (NORM) {
-    // full-row sum of squares per activation row (fixed reduction order)
-    for (int m = 0; m < M; ++m) {
-      float ss = 0.f;
-      const TA* xr = static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx;
-      for (int k = threadIdx.x * 8; k < p.K; k += kNT * 8) {
-        const uint4 v = *reinterpret_cast<const uint4*>(xr + k);
-        const TA* e = reinterpret_cast<const TA*>(&v);
+  // the first two staging passes of the first segment load their activations
+  // (and norm weights) now, together with the norm statistics' loads, so the
+  // prologue costs one memory round trip
+  uint4 pre_x[2], pre_w[2];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float a = to_float(e[i]);
-          ss = fmaf(a, a, ss);
-        }
+  for (int it = 0; it < 2; ++it) {
+    pre_x[it] = make_uint4(0u, 0u, 0u, 0u);
+    pre_w[it] = make_uint4(0u, 0u, 0u, 0u);
+    const int k0 = st0 * C::kStageK;
+    const int k1 = min(min(st0 + p.seg_stages, st1) * C::kStageK, p.K);
+    const int nvec = max(k1 - k0, 0) / 8;
+    const int idx = it * kNT + static_cast<int>(threadIdx.x);
+    if (idx < M * nvec) {
+      const int m = idx / nvec, k = k0 + 8 * (idx - m * nvec);
+      pre_x[it] = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + k);
+      if constexpr (NORM) pre_w[it] = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + k);
+    }
+  }
+  if constexpr (NORM) {
+    // full-row sum of squares per activation row (fixed reduction order); a
+    // thread's loads are issued together so the pass costs one round trip
+    constexpr int kU4 = 4;
+    const int nv = p.K / 8;  // 8-value vectors per row
+    float ss[MC];
+#pragma unroll
+    for (int m = 0; m < MC; ++m) ss[m] = 0.f;
+    for (int i0 = threadIdx.x; i0 < M * nv; i0 += kNT * kU4) {
+      uint4 v[kU4];
+#pragma unroll
+      for (int u = 0; u < kU4; ++u) {
+        const int i = i0 + u * kNT;
+        const int m = i / nv;
+        v[u] = i < M * nv ? *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx +
+                                                             8 * (i - m * nv))
+                          : make_uint4(0u, 0u, 0u, 0u);
       }
-      ss = warp_sum(ss);
-      if (lane == 0) s_part[warp][m] = ss;
+#pragma unroll
+      for (int u = 0; u < kU4; ++u) {
+        const int m = (i0 + u * kNT) / nv;
+        const TA* e = reinterpret_cast<const TA*>(&v[u]);
+        float a2 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a2 = fmaf(to_float(e[i]), to_float(e[i]), a2);
+#pragma unroll
+        for (int mm = 0; mm < MC; ++mm)
+          if (mm == m) ss[mm] += a2;
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < MC; ++m) {
+      if (m < M) {
+        const float w = warp_sum(ss[m]);
+        if (lane == 0) s_part[warp][m] = w;
+      }
     }
     __syncthreads();
     if (threadIdx.x < M) {
-      float ss = 0.f;
+      float t2 = 0.f;
 #pragma unroll
-      for (int w = 0; w < kGemvWarps; ++w) ss += s_part[w][threadIdx.x];
-      s_rms[threadIdx.x] = 1.0f / sqrtf(ss / static_cast<float>(p.K) + p.eps);
+      for (int w = 0; w < kGemvWarps; ++w) t2 += s_part[w][threadIdx.x];
+      s_rms[threadIdx.x] = 1.0f / sqrtf(t2 / static_cast<float>(p.K) + p.eps);
     }
   }
 
@@ -248,6 +393,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   // xs = x * 2^e per group in the operand type of its k (exact), laid out in
   // the operand pair order; meta = {2^-e, sum(offset_k * xs_k), sum(x)} per group.
   auto stage_x = [&](int sb) {
+    if (sb > 0 || !p.early_prefetch) stage_scales(sb);
     const int k0 = (st0 + sb) * C::kStageK;
     const int k1 = min(min(st0 + sb + p.seg_stages, st1) * C::kStageK, p.K);
     const int nvec = max(k1 - k0, 0) / 8;
@@ -260,10 +406,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
       const int k = k0 + 8 * v;
       float f[8];
       if (ok) {
-        const uint4 xv = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + k);
+        const bool pre = sb == 0 && b0 < 2 * kNT;
+        const uint4 xv = pre ? (b0 == 0 ? pre_x[0] : pre_x[1])
+                             : *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + k);
         const TA* xe = reinterpret_cast<const TA*>(&xv);
         if constexpr (NORM) {
-          const uint4 wv = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + k);
+          const uint4 wv = pre ? (b0 == 0 ? pre_w[0] : pre_w[1])
+                               : *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + k);
           const TA* we = reinterpret_cast<const TA*>(&wv);
           const float r = s_rms[m];
 #pragma unroll
@@ -277,7 +426,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
         for (int i = 0; i < 8; ++i) f[i] = 0.f;
       }
       const int grp = (8 * v) / C::kGroupK;  // group inside the segment
-      uint8_t* dst = ys + m * p.y_ld + grp * C::kYG + ((8 * v) % C::kGroupK) * 2;
+      uint8_t* dst = ys + m * p.y_ld + grp * C::kYG + y_offset<C>((8 * v) % C::kGroupK);
       if constexpr (C::kScaled) {
         float amax = 0.f;
 #pragma unroll
@@ -322,7 +471,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
           out = *reinterpret_cast<const uint4*>(hb);
         }
         if (ok) {
-          *reinterpret_cast<uint4*>(dst) = out;
+          store_pairs<C>(dst, out);
           if ((v % kVG) == 0) {
             const float inv = __uint_as_float(static_cast<uint32_t>(127 - e) << 23);
             meta[m * p.meta_ld + grp] = make_float4(inv, osum, xsum, 0.f);
@@ -333,21 +482,24 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
           __nv_bfloat16 hb[8];
 #pragma unroll
           for (int i = 0; i < 8; ++i) hb[i] = __float2bfloat16_rn(f[i]);
-          *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(hb);
+          store_pairs<C>(dst, *reinterpret_cast<const uint4*>(hb));
         }
       }
     }
+    wait_scales();
   };
 
   // ---- per-lane operand geometry
   const int bm = g % MC;      // activation row of this lane's B column
   const int bslot = g / MC;   // group slot of this lane's B column
   const bool col_live = bm < M;
+  constexpr bool kPaired = C::kSlots <= 4;  // a lane's two streams are adjacent pieces of one group
+  constexpr int kP8 = 8 / C::kSlots;        // pieces per group
   const int slot_lo = (2 * t) * C::kSlots / 8, slot_hi = (2 * t + 1) * C::kSlots / 8;
-  const int ypo_lo = ((2 * t) % (8 / C::kSlots)) * C::kPieceK * 2;
-  const int ypo_hi = ((2 * t + 1) % (8 / C::kSlots)) * C::kPieceK * 2;
   const bool act_lo = col_live && bslot == slot_lo;
   const bool act_hi = col_live && bslot == slot_hi;
+  // staged-activation byte offset of the lane's streams inside their group
+  const int ypo_lo = kPaired ? (((2 * t) % kP8) >> 1) * C::kPieceK * 4 : 0;
   // this lane's bytes of row 8r+sg of a box, per super-group u and 16-byte load i
   constexpr int kLoads = C::kLaneB >= 16 ? C::kLaneB / 16 : 1;
   int aoff[C::kU][kLoads];
@@ -362,66 +514,35 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   // scale/bias of the lane's rows for the groups of its two accumulator columns
   const int ss0 = (MC == 1) ? 2 * t : (2 * t) / MC;  // slot of column 2t
   constexpr bool kPairCols = (MC == 1) && (C::kSlots >= 2);  // columns 2t, 2t+1 = two groups
-  auto row_of = [&](int r, int h) { return min((h ? rowB : rowA) + 8 * r + sg, p.N - 1); };
-  auto set_of = [&](int h) { return (EPI == EPI_SWIGLU) ? h : 0; };
-  uint32_t sv[2][2], bv[2][2];  // [tile][h]: (s of col 2t) | (s of col 2t+1) << 16, same for bias
-  auto load_sb = [&](int gabs0) {
-    if constexpr (C::kAffine) {
-      const int gq = gabs0 + ss0;
-      const bool v0 = ss0 < C::kSlots && gq < gpr;
-      const bool v1 = kPairCols && ss0 + 1 < C::kSlots && gq + 1 < gpr;
-#pragma unroll
-      for (int r = 0; r < 2; ++r)
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const size_t idx = static_cast<size_t>(row_of(r, h)) * gpr + gq;
-          const uint16_t* sp = static_cast<const uint16_t*>(set_of(h) ? p.s1 : p.s0) + idx;
-          const uint16_t* bp = static_cast<const uint16_t*>(set_of(h) ? p.b1 : p.b0) + idx;
-          uint32_t s = 0u, b = 0u;
-          if (kPairCols && v1 && p.pair_scales) {
-            s = *reinterpret_cast<const uint32_t*>(sp);
-            b = *reinterpret_cast<const uint32_t*>(bp);
-          } else {
-            if (v0) {
-              s = sp[0];
-              b = bp[0];
-            }
-            if (kPairCols && v1) {
-              s |= static_cast<uint32_t>(sp[1]) << 16;
-              b |= static_cast<uint32_t>(bp[1]) << 16;
-            }
-          }
-          sv[r][h] = s;
-          bv[r][h] = b;
-        }
-    }
-  };
-
-  float cacc[2][4];
+  // two accumulator sets (even / odd k16 steps) halve the MMA dependency chains
+  float cacc[2][2][4];
   float res[2][2][2];
 #pragma unroll
   for (int r = 0; r < 2; ++r)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      cacc[r][e] = 0.f;
+      cacc[0][r][e] = 0.f;
+      cacc[1][r][e] = 0.f;
       res[r][e >> 1][e & 1] = 0.f;
     }
-  if (active && nst > 0) load_sb(st0 * C::kGPS);
 
   bool failed = false;
   int done = 0;  // stages consumed by this warp
-  int seg_first = 0;
+  int seg_first = 0, seg_left = 0;
+  int slot = 0;
+  uint32_t phase = 0;
   for (int st = 0; st < nst; ++st) {
-    if (st % p.seg_stages == 0) {
+    if (seg_left == 0) {
       __syncthreads();
       stage_x(st);
       __syncthreads();
       seg_first = st;
+      seg_left = p.seg_stages;
     }
+    --seg_left;
     if (!active || failed) continue;
 
-    const int slot = st % p.ring;
-    if (!mbar_wait_bounded(bars + slot, (st / p.ring) & 1)) {
+    if (!mbar_wait_bounded(bars + slot, phase)) {
       failed = true;
       continue;
     }
@@ -454,13 +575,21 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
       const int gabs = (st0 + st) * C::kGPS + u * C::kSlots;        // absolute group of slot 0
       const uint8_t* yrow = ys + bm * p.y_ld + gseg * C::kYG;
       const uint8_t* yl = (act_lo && gabs + slot_lo < gpr) ? yrow + slot_lo * C::kYG + ypo_lo : zero_blk;
-      const uint8_t* yh = (act_hi && gabs + slot_hi < gpr) ? yrow + slot_hi * C::kYG + ypo_hi : zero_blk;
+      const uint8_t* yh = (act_hi && gabs + slot_hi < gpr) ? yrow + slot_hi * C::kYG : zero_blk;
 #pragma unroll
       for (int qd = 0; qd < C::kQuads; ++qd) {
-        const uint4 bl = *reinterpret_cast<const uint4*>(yl + 16 * qd);
-        const uint4 bh = *reinterpret_cast<const uint4*>(yh + 16 * qd);
-        const uint32_t blv[4] = {bl.x, bl.y, bl.z, bl.w};
-        const uint32_t bhv[4] = {bh.x, bh.y, bh.z, bh.w};
+        uint32_t bvv[8];  // B operands: step j uses (bvv[2j], bvv[2j+1])
+        if constexpr (kPaired) {
+          const uint4 b0 = *reinterpret_cast<const uint4*>(yl + 32 * qd);
+          const uint4 b1 = *reinterpret_cast<const uint4*>(yl + 32 * qd + 16);
+          bvv[0] = b0.x; bvv[1] = b0.y; bvv[2] = b0.z; bvv[3] = b0.w;
+          bvv[4] = b1.x; bvv[5] = b1.y; bvv[6] = b1.z; bvv[7] = b1.w;
+        } else {
+          const uint4 bl = *reinterpret_cast<const uint4*>(yl + 16 * qd);
+          const uint4 bh = *reinterpret_cast<const uint4*>(yh + 16 * qd);
+          bvv[0] = bl.x; bvv[2] = bl.y; bvv[4] = bl.z; bvv[6] = bl.w;
+          bvv[1] = bh.x; bvv[3] = bh.y; bvv[5] = bh.z; bvv[7] = bh.w;
+        }
         uint32_t pl[4][4], ph[4][4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -472,8 +601,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
             const uint32_t a[4] = {pl[2 * r][j], pl[2 * r + 1][j], ph[2 * r][j], ph[2 * r + 1][j]};
-            if (Enc<TA, WF>::half_step(j)) mma_16816<true>(cacc[r], a, blv[j], bhv[j]);
-            else mma_16816<false>(cacc[r], a, blv[j], bhv[j]);
+            if (Enc<TA, WF>::half_step(j)) mma_16816<true>(cacc[j & 1][r], a, bvv[2 * j], bvv[2 * j + 1]);
+            else mma_16816<false>(cacc[j & 1][r], a, bvv[2 * j], bvv[2 * j + 1]);
           }
       }
       if constexpr (C::kScaled) {
@@ -484,7 +613,24 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
           const int n = 2 * t + e;
           const int m = n % MC, sl = n / MC;
           const bool ok = m < M && sl < C::kSlots && gabs + sl < gpr;
-          mt[e] = ok ? meta[m * p.meta_ld + gseg + sl] : make_float4(0.f, 0.f, 0.f, 0.f);
+          mt[e] = *reinterpret_cast<const float4*>(ok ? reinterpret_cast<const uint8_t*>(meta + m * p.meta_ld + gseg + sl)
+                                                      : zero_blk);
+        }
+        uint32_t sv[2][2], bv[2][2];  // [tile][h]: (s of col 2t) | (s of col 2t+1) << 16, same for bias
+        if constexpr (C::kAffine) {
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int o = (warp * 32 + h * 16 + 8 * r + sg) * p.sc_ld + gseg + ss0 + sc_off;
+              if constexpr (kPairCols) {
+                sv[r][h] = *reinterpret_cast<const uint32_t*>(scs + o);
+                bv[r][h] = *reinterpret_cast<const uint32_t*>(scb + o);
+              } else {
+                sv[r][h] = scs[o];
+                bv[r][h] = scb[o];
+              }
+            }
         }
 #pragma unroll
         for (int r = 0; r < 2; ++r)
@@ -492,25 +638,29 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
           for (int h = 0; h < 2; ++h)
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
-              const float d = cacc[r][2 * h + e] - mt[e].y;
+              const float d = (cacc[0][r][2 * h + e] + cacc[1][r][2 * h + e]) - mt[e].y;
               if constexpr (C::kAffine) {
                 const uint32_t s16 = (kPairCols && e) ? (sv[r][h] >> 16) : (sv[r][h] & 0xFFFFu);
                 const uint32_t b16 = (kPairCols && e) ? (bv[r][h] >> 16) : (bv[r][h] & 0xFFFFu);
-                const float s = bits_to_float<TA>(s16), b = bits_to_float<TA>(b16);
-                res[r][h][e] = fmaf(s * mt[e].x, d, fmaf(b, mt[e].z, res[r][h][e]));
+                const float sf = bits_to_float<TA>(s16), bf = bits_to_float<TA>(b16);
+                res[r][h][e] = fmaf(sf * mt[e].x, d, fmaf(bf, mt[e].z, res[r][h][e]));
               } else {
                 res[r][h][e] = fmaf(mt[e].x, d, res[r][h][e]);
               }
-              cacc[r][2 * h + e] = 0.f;
+              cacc[0][r][2 * h + e] = 0.f;
+              cacc[1][r][2 * h + e] = 0.f;
             }
-        if (C::kAffine && (st + 1 < nst || u + 1 < C::kU)) load_sb(gabs + C::kSlots);
       }
     }
     // refill this slot with the stage `ring` ahead
     __syncwarp();
     if (st + p.ring < nst && lane == 0) {
       fence_proxy_async_smem();
-      issue_stage(st + p.ring);
+      issue_stage(slot, st + p.ring);
+    }
+    if (++slot == p.ring) {
+      slot = 0;
+      phase ^= 1u;
     }
   }
   if (active && failed) {
@@ -527,7 +677,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
 #pragma unroll
     for (int h = 0; h < 2; ++h)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) val[r][h][e] = C::kScaled ? res[r][h][e] : cacc[r][2 * h + e];
+      for (int e = 0; e < 2; ++e)
+        val[r][h][e] = C::kScaled ? res[r][h][e] : cacc[0][r][2 * h + e] + cacc[1][r][2 * h + e];
 #pragma unroll
   for (int r = 0; r < 2; ++r)
 #pragma unroll
@@ -740,31 +891,63 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
   const int row_bytes = static_cast<int>(static_cast<int64_t>(p.K) * C::kBits / 8);
   p.stages_total = (row_bytes + 127) / 128;
 
-  // Per candidate cluster size: ring depth, activation segment, shared memory.
-  auto configure = [&](int parts) {
+  // Scales/biases come by TMA when each table row is a multiple of 16 bytes and
+  // the tables are 16-byte aligned.
+  const int gpr = C::kAffine ? p.K / C::kGroupK : 0;
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  const bool tma_ok = C::kAffine && gpr % 8 == 0 && al16(p.s0) && al16(p.b0) && al16(p.s1) && al16(p.b1);
+  // Per candidate cluster size and ring depth: activation segment, shared memory.
+  auto configure = [&](int parts, int ring) {
     const int per = (p.stages_total + parts - 1) / parts;  // most stages of one CTA
-    p.ring = std::max(1, std::min(per, 4));
-    const int per_stage = C::kGPS * (C::kYG + 16) * p.M;  // staged x + meta bytes per stage
+    p.ring = std::max(1, std::min(per, ring));
+    // staged x + meta (per activation row) and scales/biases (128 rows) per stage
+    const int per_stage = C::kGPS * (C::kYG + 16) * p.M + (C::kAffine ? C::kGPS * 128 * 4 : 0);
     p.seg_stages = std::max(1, std::min(per, (16 * 1024) / per_stage));
     const int seg_groups = p.seg_stages * C::kGPS;
     p.y_ld = seg_groups * C::kYG;
     if (((p.y_ld / 16) & 1) == 0) p.y_ld += 16;  // rows of different m start in different banks
     p.meta_ld = seg_groups;
+    // staged scales: lanes read up to column seg_groups - kSlots + 7 (M = 1);
+    // a multiple of 8 elements with an odd number of 8s makes the lanes' 4-byte
+    // reads of 8 rows x 4 columns hit 32 distinct banks
+    p.sc_ld = 0;
+    if (C::kAffine) {
+      // TMA boxes start at the group rounded down to 8 (up to 6 more columns)
+      const int need = seg_groups + (MC == 1 ? std::max(0, 8 - C::kSlots) : 0) + (tma_ok ? 6 : 0);
+      int q = (need + 7) / 8;
+      if ((q & 1) == 0) ++q;
+      p.sc_ld = 8 * q;
+    }
     return static_cast<size_t>(2048) + static_cast<size_t>(kGemvWarps) * p.ring * kStageBytes +
            static_cast<size_t>(p.M) * p.y_ld + static_cast<size_t>(p.M) * p.meta_ld * 16 +
-           static_cast<size_t>(128) * p.M * sizeof(float);
+           static_cast<size_t>(128) * p.M * sizeof(float) +
+           static_cast<size_t>(2) * kGemvWarps * 32 * p.sc_ld * sizeof(uint16_t);
   };
   // Largest cluster (K split) whose clusters are all co-resident, each CTA with
-  // at least two stages; 1 when the row groups alone fill the GPU.
+  // at least two stages, with the deepest ring (4..2) that still fits; one CTA
+  // per row group with a 4-deep ring when the row groups alone fill the GPU.
   int parts = 1;
   size_t smem = 0;
-  for (int cand = kMaxParts; cand >= 1; cand >>= 1) {
-    if (cand > 1 && (p.stages_total < 2 * cand || (cand > 8 && !large_clusters))) continue;
-    smem = configure(cand);
-    if (cand == 1 || max_active_clusters(reinterpret_cast<const void*>(kernel), cand, smem, row_groups) >= row_groups) {
-      parts = cand;
-      break;
+  bool chosen = false;
+  for (int cand = kMaxParts; cand >= 2 && !chosen; cand >>= 1) {
+    if (p.stages_total < 2 * cand || (cand > 8 && !large_clusters)) continue;
+    for (int ring = 4; ring >= 2 && !chosen; --ring) {
+      smem = configure(cand, ring);
+      if (max_active_clusters(reinterpret_cast<const void*>(kernel), cand, smem, row_groups) >= row_groups) {
+        parts = cand;
+        chosen = true;
+      }
     }
+  }
+  if (!chosen) smem = configure(1, 4);
+  p.sc_tma = 0;
+  if (tma_ok && p.sc_ld <= 256) {
+    p.sc_tma = 1;
+    const uint64_t n = static_cast<uint64_t>(p.N);
+    if (int st = make_tmap_u16(&p.smap0, p.s0, n, gpr, p.sc_ld, 16)) return st;
+    if (int st = make_tmap_u16(&p.bmap0, p.b0, n, gpr, p.sc_ld, 16)) return st;
+    if (int st = make_tmap_u16(&p.smap1, p.s1, n, gpr, p.sc_ld, 16)) return st;
+    if (int st = make_tmap_u16(&p.bmap1, p.b1, n, gpr, p.sc_ld, 16)) return st;
   }
   dim3 grid(parts, row_groups);
   return launch_cluster("gemv", kernel, grid, dim3(kGemvWarps * 32), smem, parts, stream, p);

@@ -55,6 +55,12 @@ struct GemvParams {
   // TMA descriptors of weight set 0 and 1 ([rows][K*bits/8] bytes, 16x128 B boxes)
   alignas(64) CUtensorMap tmap0;
   alignas(64) CUtensorMap tmap1;
+  // TMA descriptors of the scales and biases of sets 0 and 1 (affine, when
+  // sc_tma): uint16 [N][K/G], boxes of 16 rows x sc_ld groups
+  alignas(64) CUtensorMap smap0;
+  alignas(64) CUtensorMap bmap0;
+  alignas(64) CUtensorMap smap1;
+  alignas(64) CUtensorMap bmap1;
   // activations [M][ldx] (bf16 or fp16); m0 = index of row 0 in the outputs
   // (and positions / argmax keys) when one request is split into launches
   const void* x;
@@ -77,6 +83,8 @@ struct GemvParams {
   int y_ld;        // bytes per activation row of the staged segment
   int meta_ld;     // groups per activation row of the staged segment
   int pair_scales; // 1 when two consecutive groups' scales are 4-byte aligned
+  int sc_ld;       // staged scale/bias elements per weight row (affine formats)
+  int sc_tma;      // 1: scales/biases are staged by TMA (rows 16-byte multiples, aligned)
   // rms-norm prologue (optional)
   const void* norm_w;
   float eps;

@@ -59,6 +59,23 @@ int make_tmap_rows(CUtensorMap* map, const void* base, uint64_t rows, uint64_t r
   return SB_OK;
 }
 
+int make_tmap_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                  uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(SB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16 || (box_cols * 2) % 16 || box_cols > 256)
+    return fail(SB_EINVAL, "u16 TMA source must be 16-byte aligned with 16-byte rows and boxes");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, elem,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SB_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+  return SB_OK;
+}
+
 // ------------------------------------------------------------------ RMSNorm
 template <typename T>
 __global__ void rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int dim,
