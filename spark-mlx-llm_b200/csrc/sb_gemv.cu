@@ -181,14 +181,15 @@ __device__ __forceinline__ int box_row0(const GemvParams& p, int rb, int h) {
 constexpr int kStageBytes = 32 * 128;  // two 16-row boxes
 
 template <typename TA, int WF, int G, int EPI, bool NORM, int MC>
-__global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __grid_constant__ GemvParams p) {
   using C = Geo<WF, G, MC>;
   constexpr int kVG = C::kGroupK / 8;  // 8-value activation vectors per group
-  constexpr int kNT = kGemvWarps * 32;
+  const int kNT = static_cast<int>(blockDim.x);  // 32 x (4 row blocks x kSub K sub-parts)
+  const int nwarps = kNT >> 5;
 
   extern __shared__ uint8_t smem_dyn[];
   __shared__ float s_rms[8];
-  __shared__ float s_part[kGemvWarps][8];
+  __shared__ float s_part[kGemvMaxWarps][8];
   __shared__ unsigned long long s_keys[8];
 
   const int warp = threadIdx.x >> 5;
@@ -199,7 +200,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   const int part = blockIdx.x;  // K part = rank in the cluster
   const int nparts = gridDim.x;
   const int rowblocks = warp_blocks<EPI>(p);
-  const int rb = blockIdx.y * kGemvWarps + warp;
+  const int rbi = warp % kGemvWarps;  // row block of this warp inside the CTA
+  const int sub = warp / kGemvWarps;  // K sub-part of this warp inside the CTA
+  const int nsub = nwarps / kGemvWarps;
+  const int rb = blockIdx.y * kGemvWarps + rbi;
   const bool active = rb < rowblocks;
   const int rbc = min(rb, rowblocks - 1);
   const int M = p.M;
@@ -211,13 +215,14 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   const int nst = st1 - st0;
 
   // ---- shared memory: barriers + zero block, per-warp rings, staged x, group meta, reduction buffer
-  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  // 1 KB-aligned start (pointer arithmetic keeps the shared address space known to the compiler)
+  uint8_t* base = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(base) + warp * kGemvMaxRing;
-  const uint8_t* zero_blk = base + 512;
-  uint64_t* scbar = reinterpret_cast<uint64_t*>(base + 256);  // scale/bias TMA barrier
+  const uint8_t* zero_blk = base + 768;
+  uint64_t* scbar = reinterpret_cast<uint64_t*>(base + 512);  // scale/bias TMA barrier
   uint8_t* ring = base + 1024 + warp * p.ring * kStageBytes;
   // staged scales and biases (affine): [warp][row h*16 + i][sc_ld] of the current segment
-  uint16_t* scs = reinterpret_cast<uint16_t*>(base + 1024 + kGemvWarps * p.ring * kStageBytes);
+  uint16_t* scs = reinterpret_cast<uint16_t*>(base + 1024 + nwarps * p.ring * kStageBytes);
   uint16_t* scb = scs + kGemvWarps * 32 * p.sc_ld;
   uint8_t* ys = reinterpret_cast<uint8_t*>(scb + kGemvWarps * 32 * p.sc_ld);
   float4* meta = reinterpret_cast<float4*>(ys + M * p.y_ld);
@@ -316,11 +321,13 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   // ---- start streaming weights; with constant weights this may overlap the
   // tail of the previous kernel in the stream
   if (!p.early_prefetch) grid_dependency_wait();
+  // this warp's stages [ws0, ws1) of the CTA's range
+  const int ws0 = nst * sub / nsub, ws1 = nst * (sub + 1) / nsub;
   if (active && lane == 0) {
-    for (int st = 0; st < p.ring && st < nst; ++st) issue_stage(st, st);
+    for (int i = 0; i < p.ring && ws0 + i < ws1; ++i) issue_stage(i, ws0 + i);
   }
   if (p.early_prefetch && nst > 0) stage_scales(0);
-  if (threadIdx.x < 32) reinterpret_cast<uint4*>(base + 512)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
+  if (threadIdx.x < 16) reinterpret_cast<uint4*>(base + 768)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
   if (threadIdx.x < 8) s_keys[threadIdx.x] = 0ull;
 
   // ---- activations depend on the previous kernel from here on
@@ -384,7 +391,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
     if (threadIdx.x < M) {
       float t2 = 0.f;
 #pragma unroll
-      for (int w = 0; w < kGemvWarps; ++w) t2 += s_part[w][threadIdx.x];
+      for (int w = 0; w < kGemvMaxWarps; ++w)
+        if (w < nwarps) t2 += s_part[w][threadIdx.x];
       s_rms[threadIdx.x] = 1.0f / sqrtf(t2 / static_cast<float>(p.K) + p.eps);
     }
   }
@@ -527,11 +535,17 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
     }
 
   bool failed = false;
-  int done = 0;  // stages consumed by this warp
-  int seg_first = 0, seg_left = 0;
+  int done = ws0;  // stages consumed by this warp (the next one to wait for)
+  // The first activation segment is staged before the loop by all threads; a
+  // CTA whose K sub-parts split its range (nsub > 1) has a single segment, so
+  // only single-part CTAs meet the in-loop segment barriers (uniform trip count).
+  __syncthreads();
+  stage_x(0);
+  __syncthreads();
+  int seg_first = 0, seg_left = p.seg_stages;
   int slot = 0;
   uint32_t phase = 0;
-  for (int st = 0; st < nst; ++st) {
+  for (int st = ws0; st < ws1; ++st) {
     if (seg_left == 0) {
       __syncthreads();
       stage_x(st);
@@ -622,7 +636,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
           for (int r = 0; r < 2; ++r)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int o = (warp * 32 + h * 16 + 8 * r + sg) * p.sc_ld + gseg + ss0 + sc_off;
+              const int o = (rbi * 32 + h * 16 + 8 * r + sg) * p.sc_ld + gseg + ss0 + sc_off;
               if constexpr (kPairCols) {
                 sv[r][h] = *reinterpret_cast<const uint32_t*>(scs + o);
                 bv[r][h] = *reinterpret_cast<const uint32_t*>(scb + o);
@@ -654,7 +668,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
     }
     // refill this slot with the stage `ring` ahead
     __syncwarp();
-    if (st + p.ring < nst && lane == 0) {
+    if (st + p.ring < ws1 && lane == 0) {
       fence_proxy_async_smem();
       issue_stage(slot, st + p.ring);
     }
@@ -666,7 +680,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
   if (active && failed) {
     // a TMA load never completed: report and drain what is still in flight
     if (p.status && lane == 0) atomicOr(p.status, kStatusTimeout);
-    for (int st = done; st < min(nst, done + p.ring); ++st) mbar_wait_bounded(bars + st % p.ring, (st / p.ring) & 1);
+    for (int st = done; st < min(ws1, done + p.ring); ++st)
+      mbar_wait_bounded(bars + (st - ws0) % p.ring, ((st - ws0) / p.ring) & 1);
   }
   grid_dependency_launch();
 
@@ -712,9 +727,10 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
         for (int e = 0; e < 2; ++e) {
           if (!own(e)) continue;
           const int m = (MC == 1) ? 0 : 2 * t + e;
-          const int P = warp * 16 + 8 * r + g;
+          const int P = rbi * 16 + 8 * r + g;
           const int owner = P / ppc;
-          const uint32_t addr = red_u32 + static_cast<uint32_t>((((part * ppc + P % ppc) * 2 + h) * M + m) * 4);
+          const int src = part * nsub + sub;
+          const uint32_t addr = red_u32 + static_cast<uint32_t>((((src * ppc + P % ppc) * 2 + h) * M + m) * 4);
           if (nparts == 1) st_shared_f32(addr, val[r][h][e]);
           else st_cluster_f32(cluster_map(addr, owner), val[r][h][e]);
         }
@@ -730,7 +746,7 @@ __global__ void __launch_bounds__(kGemvWarps * 32) gemv_kernel(const __grid_cons
     const int rbx = blockIdx.y * kGemvWarps + w;
     if (rbx >= rowblocks) continue;
     float v_lo = 0.f, v_hi = 0.f;
-    for (int src = 0; src < nparts; ++src) {
+    for (int src = 0; src < nparts * nsub; ++src) {
       v_lo += red[((src * ppc + pl) * 2 + 0) * M + m];
       v_hi += red[((src * ppc + pl) * 2 + 1) * M + m];
     }
@@ -820,23 +836,23 @@ constexpr int kMaxParts = 16;  // CTAs per cluster sharing one row group's K ran
 
 struct ClusterFit {
   const void* kernel;
-  int parts;
+  int parts, threads;
   size_t smem;
   int clusters;
 };
 
 // Largest number of co-resident clusters of `parts` CTAs (cached per kernel and size).
-int max_active_clusters(const void* kernel, int parts, size_t smem, int row_groups) {
+int max_active_clusters(const void* kernel, int parts, int threads, size_t smem, int row_groups) {
   static std::mutex mu;
   static std::vector<ClusterFit> cache;
   {
     std::lock_guard<std::mutex> lock(mu);
     for (const ClusterFit& c : cache)
-      if (c.kernel == kernel && c.parts == parts && c.smem == smem) return c.clusters;
+      if (c.kernel == kernel && c.parts == parts && c.threads == threads && c.smem == smem) return c.clusters;
   }
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(parts, std::max(1, row_groups));
-  config.blockDim = dim3(kGemvWarps * 32);
+  config.blockDim = dim3(threads);
   config.dynamicSmemBytes = smem;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -851,7 +867,7 @@ int max_active_clusters(const void* kernel, int parts, size_t smem, int row_grou
     n = 0;
   }
   std::lock_guard<std::mutex> lock(mu);
-  cache.push_back({kernel, parts, smem, n});
+  cache.push_back({kernel, parts, threads, smem, n});
   return n;
 }
 
@@ -896,13 +912,16 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
   const int gpr = C::kAffine ? p.K / C::kGroupK : 0;
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   const bool tma_ok = C::kAffine && gpr % 8 == 0 && al16(p.s0) && al16(p.b0) && al16(p.s1) && al16(p.b1);
-  // Per candidate cluster size and ring depth: activation segment, shared memory.
-  auto configure = [&](int parts, int ring) {
+  // Per candidate (cluster size, K sub-parts per CTA, ring depth): activation
+  // segment and shared memory; 0 when the sub-parts cannot share one segment.
+  auto configure = [&](int parts, int nsub, int ring) -> size_t {
     const int per = (p.stages_total + parts - 1) / parts;  // most stages of one CTA
-    p.ring = std::max(1, std::min(per, ring));
+    const int per_warp = (per + nsub - 1) / nsub;
+    p.ring = std::max(1, std::min(per_warp, ring));
     // staged x + meta (per activation row) and scales/biases (128 rows) per stage
     const int per_stage = C::kGPS * (C::kYG + 16) * p.M + (C::kAffine ? C::kGPS * 128 * 4 : 0);
     p.seg_stages = std::max(1, std::min(per, (16 * 1024) / per_stage));
+    if (nsub > 1 && (p.seg_stages < per || per < nsub)) return 0;
     const int seg_groups = p.seg_stages * C::kGPS;
     p.y_ld = seg_groups * C::kYG;
     if (((p.y_ld / 16) & 1) == 0) p.y_ld += 16;  // rows of different m start in different banks
@@ -918,28 +937,33 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
       if ((q & 1) == 0) ++q;
       p.sc_ld = 8 * q;
     }
-    return static_cast<size_t>(2048) + static_cast<size_t>(kGemvWarps) * p.ring * kStageBytes +
+    return static_cast<size_t>(2048) + static_cast<size_t>(kGemvWarps) * nsub * p.ring * kStageBytes +
            static_cast<size_t>(p.M) * p.y_ld + static_cast<size_t>(p.M) * p.meta_ld * 16 +
-           static_cast<size_t>(128) * p.M * sizeof(float) +
+           static_cast<size_t>(128) * p.M * nsub * sizeof(float) +
            static_cast<size_t>(2) * kGemvWarps * 32 * p.sc_ld * sizeof(uint16_t);
   };
-  // Largest cluster (K split) whose clusters are all co-resident, each CTA with
-  // at least two stages, with the deepest ring (4..2) that still fits; one CTA
-  // per row group with a 4-deep ring when the row groups alone fill the GPU.
-  int parts = 1;
+  // Largest cluster (K split across CTAs) whose clusters are all co-resident,
+  // each CTA with at least two stages; within it, two K sub-parts per CTA (8
+  // warps) when they fit, and the deepest ring (4..2) that fits. One CTA of 4
+  // warps per row group when the row groups alone fill the GPU.
+  int parts = 1, nsub = 1;
   size_t smem = 0;
   bool chosen = false;
   for (int cand = kMaxParts; cand >= 2 && !chosen; cand >>= 1) {
     if (p.stages_total < 2 * cand || (cand > 8 && !large_clusters)) continue;
-    for (int ring = 4; ring >= 2 && !chosen; --ring) {
-      smem = configure(cand, ring);
-      if (max_active_clusters(reinterpret_cast<const void*>(kernel), cand, smem, row_groups) >= row_groups) {
-        parts = cand;
-        chosen = true;
+    for (int ns = 2; ns >= 1 && !chosen; --ns)
+      for (int ring = 4; ring >= 2 && !chosen; --ring) {
+        smem = configure(cand, ns, ring);
+        if (smem == 0) continue;
+        if (max_active_clusters(reinterpret_cast<const void*>(kernel), cand, 32 * kGemvWarps * ns, smem, row_groups) >=
+            row_groups) {
+          parts = cand;
+          nsub = ns;
+          chosen = true;
+        }
       }
-    }
   }
-  if (!chosen) smem = configure(1, 4);
+  if (!chosen) smem = configure(1, 1, 4);
   p.sc_tma = 0;
   if (tma_ok && p.sc_ld <= 256) {
     p.sc_tma = 1;
@@ -950,7 +974,7 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
     if (int st = make_tmap_u16(&p.bmap1, p.b1, n, gpr, p.sc_ld, 16)) return st;
   }
   dim3 grid(parts, row_groups);
-  return launch_cluster("gemv", kernel, grid, dim3(kGemvWarps * 32), smem, parts, stream, p);
+  return launch_cluster("gemv", kernel, grid, dim3(kGemvWarps * 32 * nsub), smem, parts, stream, p);
 }
 
 template <typename TA, int WF, int G, int EPI, bool NORM>

@@ -47,7 +47,8 @@ enum Epilogue : int {
   EPI_ARGMAX = 4,  // greedy token: argmax over rows of fp32 logits
 };
 
-constexpr int kGemvWarps = 4;   // warps per CTA (one 32-row block each)
+constexpr int kGemvWarps = 4;   // 32-row blocks per CTA (one warp each per K sub-part)
+constexpr int kGemvMaxWarps = 8; // warps per CTA: 4 row blocks x 1 or 2 K sub-parts
 constexpr int kGemvMaxRing = 8; // TMA stages in flight per warp (upper bound)
 constexpr int kMaxRopeHalf = 128;
 

@@ -132,7 +132,8 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
 
   // ---- per-warp ring of 16-token K/V blocks in shared memory (TMA boxes)
   extern __shared__ uint8_t smem_dyn[];
-  uint8_t* sbase = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_dyn) + 1023) & ~uintptr_t(1023));
+  // 1 KB-aligned start (pointer arithmetic keeps the shared address space known to the compiler)
+  uint8_t* sbase = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sbase) + warp * kSdpaStages;
   uint8_t* ring = sbase + 1024 + warp * kSdpaStages * kSdpaStageBytes;
   const int nb = blk_end - blk_begin;
