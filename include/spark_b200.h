@@ -176,6 +176,28 @@ int sb_int8_sdpa_decode_static(const void* q, const int8_t* k, const void* k_sca
                                float scale, void* stream);
 
 /*
+ * Attention over MLX affine-quantized KV tuples: the int8_quantized_sdpa input
+ * format (spark_mlx_ext/int8_quantized_sdpa.py:156-287, staged recipe
+ * _fallback :122-153). Replaces int8_quantized_sdpa for its affine tuples.
+ *   q        [B, H, L, dk] in `dtype` (SB_DTYPE_BF16 / F16 / F32)
+ *   k_packed [B, KH, N, dk*bits/32] uint32, k_scales/k_biases [B, KH, N, dk/G]
+ *   v_packed [B, KH, N, dv*bits/32] uint32, v_scales/v_biases [B, KH, N, dv/G]
+ *   out      [B, H, L, dv] in `dtype`
+ * K[n,d] = scale_k[n,d/G] * code + bias_k[n,d/G] (V likewise); scores
+ * scale * q.K, softmax and P.V accumulate in fp32; causal != 0 applies the
+ * bottom-right causal mask (query l of L sees keys [0, N-L+l]). bits 2/4/8,
+ * group 32/64/128, dk/dv multiples of the group <= 256, H % KH == 0.
+ * Workspace: sb_affine_sdpa_workspace_size bytes (0 = single-split launch).
+ */
+int sb_affine_sdpa(const void* q, int dtype, const void* k_packed, const void* k_scales,
+                   const void* k_biases, const void* v_packed, const void* v_scales,
+                   const void* v_biases, void* out, int64_t batch, int num_heads, int num_kv_heads,
+                   int64_t length, int64_t n, int dk, int dv, int group_size, int bits, float scale,
+                   int causal, void* workspace, size_t workspace_bytes, void* stream);
+size_t sb_affine_sdpa_workspace_size(int64_t batch, int num_heads, int64_t length, int64_t n,
+                                     int dv);
+
+/*
  * RMSNorm, y = T(x * rsqrt(mean(x^2) + eps) * weight), fp32 statistics.
  * Replaces mx.fast.rms_norm as used by dispatch_ffn (spark_mlx_llm/ops/ffn.py:99)
  * and nn.RMSNorm (spark_mlx_llm/model.py:240-243).

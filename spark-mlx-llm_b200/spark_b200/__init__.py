@@ -9,7 +9,7 @@ All compute runs in ``lib/libsparkb200.so`` (C ABI in include/spark_b200.h);
 importing an operator without the library raises ``RuntimeError``.
 """
 
-from . import ops  # noqa: F401  (registers torch.ops.spark_b200.*)
+from . import dispatch, ext, ops  # noqa: F401  (ops registers torch.ops.spark_b200.*)
 from ._lib import LIB_PATH, lib  # noqa: F401
 
 __version__ = "0.1.0"

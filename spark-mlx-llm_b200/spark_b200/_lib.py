@@ -110,6 +110,12 @@ SIGNATURES = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _i64, _i64, _int,
          _float, _c_void_p],
     ),
+    "sb_affine_sdpa": (
+        _int,
+        [_c_void_p, _int, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int,
+         _int, _i64, _i64, _int, _int, _int, _int, _float, _int, _c_void_p, _size, _c_void_p],
+    ),
+    "sb_affine_sdpa_workspace_size": (_size, [_i64, _int, _i64, _i64, _int]),
     "sb_rms_norm": (_int, [_c_void_p, _c_void_p, _c_void_p, _int, _i64, _i64, _float, _c_void_p]),
     # decoder header
     "sb_linear_ex": (_int, [ctypes.POINTER(sb_linear_ex_desc), _c_void_p]),

@@ -1,0 +1,199 @@
+"""The ``spark_mlx_llm.ops`` dispatch layer over the B200 kernels.
+
+Mirrors the reference's operator entry points for the decode path:
+
+* ``dispatch_linear(x, projection, *, config=None)``      (ops/linear.py:84-94)
+* ``AffineParameters`` (``native``, ``from_module``, ``accepts``) (:97-191)
+* ``dispatch_qkv(x, projection, rope, *, q_size, kv_size, n_heads,
+  n_kv_heads, head_dim, offset, config=None)``               (ops/qkv.py:18-87)
+* ``dispatch_sdpa(queries, keys, values, *, cache, scale, mask, config=None,
+  is_sliding=False)``                                        (ops/sdpa.py:39-78)
+
+A ``projection`` is any object exposing the MLX ``nn.QuantizedLinear``
+attributes ``weight / scales / biases / group_size / bits / mode`` (affine,
+no linear bias) holding torch CUDA tensors - :class:`QuantizedLinear` is one -
+or a W8 per-channel module (:class:`W8A16PerChannelLinear`,
+``ext.W8A8Linear``), or any callable. ``rope`` is an object with the
+``nn.RoPE`` attributes ``dims / traditional / base / scale`` (:class:`RoPE`).
+KV for ``dispatch_sdpa`` is either the B200 INT8 cache pair ``(int8 codes
+[B,KH,N,D], fp16 scales [B,KH,N])`` or the reference's affine tuple
+``(packed, scales, biases)``.
+"""
+
+from dataclasses import dataclass, fields
+from typing import NamedTuple
+
+import torch
+
+from . import ext, ops
+
+__all__ = [
+    "AffineParameters",
+    "LinearConfig",
+    "QuantizedLinear",
+    "RoPE",
+    "SDPAConfig",
+    "W8A16PerChannelLinear",
+    "dispatch_linear",
+    "dispatch_qkv",
+    "dispatch_sdpa",
+]
+
+
+class _Config:
+    """Field validation shared by the configs (ops/base.py OperatorConfig role)."""
+
+    _choices: dict = {}
+
+    def __post_init__(self):
+        for f in fields(self):
+            value = getattr(self, f.name)
+            allowed = self._choices.get(f.name)
+            if allowed is not None and value not in allowed:
+                raise ValueError(f"{f.name} must be one of {allowed}, got {value!r}")
+            if allowed is None and not isinstance(value, bool):
+                raise ValueError(f"{f.name} must be bool")
+
+
+@dataclass(kw_only=True)
+class LinearConfig(_Config):
+    """Implementation policy for existing W8/W4 layers (ops/linear.py:56-81).
+
+    On B200 every W4/W8 layer runs the same weight-streaming kernel family;
+    the backend names are accepted and validated for compatibility."""
+
+    w8_qmv_backend: str = "w8a16"
+    w4_qmv_backend: str = "native"
+    _choices = {"w8_qmv_backend": ("auto", "native", "w8a16", "w8a8", "multirow"),
+                "w4_qmv_backend": ("native", "splitk", "multirow", "multirow_packed")}
+
+
+@dataclass(kw_only=True)
+class SDPAConfig(_Config):
+    """Kernel preferences for attention (ops/sdpa.py:13-20)."""
+
+    fused_quantized_sdpa: bool = True
+    fused_quantized_sdpa_prefill: bool = False
+    tuned_bf16_sdpa: bool = False
+    verification_bf16_sdpa: bool = False
+
+
+class AffineParameters(NamedTuple):
+    """Affine tensors and metadata passed explicitly to the projection (ops/linear.py:97-191)."""
+
+    weight: torch.Tensor
+    scales: torch.Tensor
+    biases: torch.Tensor
+    group_size: int
+    bits: int
+
+    @classmethod
+    def from_module(cls, layer):
+        return cls(layer.weight, layer.scales, layer.biases, layer.group_size, layer.bits)
+
+    @staticmethod
+    def accepts(layer):
+        return (getattr(layer, "mode", None) == "affine" and getattr(layer, "biases", None) is not None
+                and getattr(layer, "bias", None) is None and hasattr(layer, "weight") and hasattr(layer, "scales"))
+
+    @staticmethod
+    def native(x, weight, scales, biases, group_size, bits):
+        """``mx.quantized_matmul(x, w, scales, biases, transpose=True, mode="affine")``."""
+        return ops.affine_linear(x, weight, scales, biases, group_size, bits)
+
+
+class QuantizedLinear(torch.nn.Module):
+    """Affine-quantized projection with the ``nn.QuantizedLinear`` attributes."""
+
+    mode = "affine"
+
+    def __init__(self, weight, scales, biases, group_size=64, bits=4):
+        super().__init__()
+        self.register_buffer("weight", weight)
+        self.register_buffer("scales", scales)
+        self.register_buffer("biases", biases)
+        self.bias = None
+        self.group_size = group_size
+        self.bits = bits
+
+    def forward(self, x):
+        return AffineParameters.native(x, *AffineParameters.from_module(self))
+
+
+class W8A16PerChannelLinear(torch.nn.Module):
+    """Signed INT8 weights with an FP32 scale per output row (ops/linear.py:413-476)."""
+
+    def __init__(self, weight, scales):
+        super().__init__()
+        self.register_buffer("weight", weight)
+        self.register_buffer("scales", scales)
+
+    def forward(self, x):
+        return ext.w8a16_per_channel(x, self.weight, self.scales)
+
+
+class RoPE:
+    """The ``nn.RoPE`` attributes used by ``dispatch_qkv`` (half-split rotation)."""
+
+    def __init__(self, dims, traditional=False, base=10000.0, scale=1.0):
+        self.dims, self.traditional, self.base, self.scale = dims, traditional, base, scale
+
+
+def dispatch_linear(x, projection, *, config=None):
+    """Run an affine projection on the weight-streaming kernels, else call it."""
+    config = config if config is not None else LinearConfig()
+    if not isinstance(config, LinearConfig):
+        raise TypeError("config must be a LinearConfig")
+    if AffineParameters.accepts(projection):
+        return AffineParameters.native(x, *AffineParameters.from_module(projection))
+    return projection(x)
+
+
+def dispatch_qkv(x, projection, rope, *, q_size, kv_size, n_heads, n_kv_heads, head_dim, offset, config=None):
+    """Project, split heads and apply RoPE; returns ``(queries, keys, values)``
+    shaped ``[B, H, L, D]``. Affine W4/W8 projections with a half-split RoPE of
+    scale 1 over the full head run as one fused kernel (``spark_qkv_rope``,
+    ops/qkv.py:40-66); ``offset`` is a Python int or an int32 tensor of
+    per-token positions ``[B, L]``."""
+    config = config if config is not None else LinearConfig()
+    if not isinstance(config, LinearConfig):
+        raise TypeError("config must be a LinearConfig")
+    bsz, length, _ = x.shape
+    fused = (AffineParameters.accepts(projection) and projection.bits in (4, 8)
+             and projection.group_size in (32, 64, 128) and not rope.traditional and rope.scale == 1.0
+             and rope.dims == head_dim and q_size == n_heads * head_dim and kv_size == n_kv_heads * head_dim)
+    if fused:
+        if isinstance(offset, torch.Tensor):
+            positions = offset.to(device=x.device, dtype=torch.int32).reshape(-1)
+        else:
+            positions = (int(offset) + torch.arange(length, device=x.device, dtype=torch.int32)).repeat(bsz)
+        return ops.qkv_rope(x, projection.weight, projection.scales, projection.biases, positions, n_heads,
+                            n_kv_heads, head_dim, rope.dims, float(rope.base), projection.group_size,
+                            projection.bits)
+    raise ValueError("dispatch_qkv on B200 needs an affine W4/W8 projection with a half-split, scale-1 RoPE "
+                     "over the full head dimension")
+
+
+def dispatch_sdpa(queries, keys, values, *, cache, scale, mask, config=None, is_sliding=False):
+    """Decode attention over a quantized KV cache (ops/sdpa.py:39-78).
+
+    * INT8 pair ``(codes [B,KH,N,D] int8, scales [B,KH,N] fp16)``, one query
+      token (``L == 1``, the last position attends to all N keys): the B200
+      INT8-KV kernel.
+    * Affine tuple ``(packed, scales, biases)`` with ``cache.bits`` /
+      ``cache.group_size``: ``int8_quantized_sdpa`` (decode or causal prefill).
+    """
+    config = config if config is not None else SDPAConfig()
+    if not isinstance(config, SDPAConfig):
+        raise TypeError("config must be an SDPAConfig")
+    if isinstance(keys, (tuple, list)) and len(keys) == 2 and len(values) == 2:
+        if queries.shape[2] != 1 or mask not in (None, "causal"):
+            raise ValueError("the INT8 KV pair path serves single-token decode with no mask or 'causal'")
+        n = keys[0].shape[2]
+        return ops.int8_sdpa_decode(queries, keys[0], keys[1], values[0], values[1], n, float(scale))
+    if isinstance(keys, (tuple, list)) and len(keys) == 3 and len(values) == 3:
+        return ext.int8_quantized_sdpa(queries, keys, values, scale=scale,
+                                       group_size=getattr(cache, "group_size", 32), bits=getattr(cache, "bits", 8),
+                                       mask=mask)
+    raise ValueError("dispatch_sdpa on B200 serves quantized KV caches: an (int8, fp16 scale) pair or an "
+                     "affine (packed, scales, biases) tuple")
