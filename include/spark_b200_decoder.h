@@ -75,6 +75,16 @@ typedef struct sb_linear_ex_desc {
    * stream (model weights), so the kernel may start streaming them before the
    * previous kernel has finished; 0: wait for the previous kernel first. */
   int weights_constant;
+  /* ROPE, optional fused cache append (head_dim 64 or 128): when kv_k_cache is
+   * non-NULL the K and V heads are not stored to k_out/v_out; instead each
+   * (token m, KV head) row is rounded to the activation dtype and quantized
+   * like sb_kv_append_int8 into the INT8 cache [B, KH, kv_capacity, D] at
+   * position positions[m] (fp16 scale [B, KH, kv_capacity]). */
+  int8_t* kv_k_cache;
+  void* kv_k_scale;
+  int8_t* kv_v_cache;
+  void* kv_v_scale;
+  int64_t kv_capacity;
 } sb_linear_ex_desc;
 
 /* Fused weight-streaming linear (1 <= M <= 8). */

@@ -191,6 +191,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
   __shared__ float s_rms[8];
   __shared__ float s_part[kGemvMaxWarps][8];
   __shared__ unsigned long long s_keys[8];
+  __shared__ unsigned s_kvmax[2][8];  // fused cache append: |K/V| max per (head in group, m)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -329,6 +330,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
   if (p.early_prefetch && nst > 0) stage_scales(0);
   if (threadIdx.x < 16) reinterpret_cast<uint4*>(base + 768)[threadIdx.x] = make_uint4(0u, 0u, 0u, 0u);
   if (threadIdx.x < 8) s_keys[threadIdx.x] = 0ull;
+  if (threadIdx.x < 16) s_kvmax[threadIdx.x >> 3][threadIdx.x & 7] = 0u;
 
   // ---- activations depend on the previous kernel from here on
   grid_dependency_wait();
@@ -716,7 +718,10 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
 
   // ---- reduction over the K parts: pair P = warp*16 + 8r + g (rows of box A and B)
   // of this CTA belongs to part P / ppc, which sums red[src][P % ppc][h][m] over src.
-  const int ppc = 64 / nparts;
+  // With the fused cache append every pair belongs to part 0 (a head's
+  // absolute maximum needs all of its pairs in one CTA).
+  const bool kv_fused = (EPI == EPI_ROPE) && p.kv_k_cache != nullptr;
+  const int ppc = kv_fused ? 64 : 64 / nparts;
   if (active) {
     const uint32_t red_u32 = smem_u32(red);
 #pragma unroll
@@ -728,7 +733,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
           if (!own(e)) continue;
           const int m = (MC == 1) ? 0 : 2 * t + e;
           const int P = rbi * 16 + 8 * r + g;
-          const int owner = P / ppc;
+          const int owner = kv_fused ? 0 : P / ppc;
           const int src = part * nsub + sub;
           const uint32_t addr = red_u32 + static_cast<uint32_t>((((src * ppc + P % ppc) * 2 + h) * M + m) * 4);
           if (nparts == 1) st_shared_f32(addr, val[r][h][e]);
@@ -739,9 +744,10 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
   else __syncthreads();
 
   // ---- final epilogue over this part's pairs
-  for (int idx = threadIdx.x; idx < ppc * M; idx += kNT) {
+  const int own_pairs = (kv_fused && part != 0) ? 0 : ppc;
+  for (int idx = threadIdx.x; idx < own_pairs * M; idx += kNT) {
     const int pl = idx / M, m = idx - (idx / M) * M;
-    const int P = part * ppc + pl;
+    const int P = (kv_fused ? 0 : part * ppc) + pl;
     const int w = P >> 4, r = (P >> 3) & 1, gg = P & 7;
     const int rbx = blockIdx.y * kGemvWarps + w;
     if (rbx >= rowblocks) continue;
@@ -802,6 +808,15 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
         a = ra;
         b = rb2;
       }
+      if (kv_fused && head >= p.heads_q) {
+        // stash the stored-precision values in this pair's own slot of source 0
+        a = round_act<TA>(a);
+        b = round_act<TA>(b);
+        red[((0 * ppc + pl) * 2 + 0) * M + m] = a;
+        red[((0 * ppc + pl) * 2 + 1) * M + m] = b;
+        atomicMax(&s_kvmax[w / wph][m], __float_as_uint(fmaxf(fabsf(a), fabsf(b))));
+        continue;
+      }
       const int bi = (m + p.m0) / p.seq_len, l = (m + p.m0) % p.seq_len;
       const size_t obase = ((static_cast<size_t>(bi) * nh + hh) * p.seq_len + l) * p.head_dim;
       store_act<TA>(out, obase + i, a);
@@ -825,6 +840,38 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
   if constexpr (EPI == EPI_ARGMAX) {
     __syncthreads();
     if (threadIdx.x < M && s_keys[threadIdx.x]) atomicMax(p.argmax_keys + p.m0 + threadIdx.x, s_keys[threadIdx.x]);
+  }
+  if constexpr (EPI == EPI_ROPE) {
+    if (kv_fused) {
+      // symmetric INT8 per (token, KV head): scale = fp16(max|x| / 127) (1 for
+      // a zero row), code = clamp(rint(x / scale), -127, 127) - the arithmetic
+      // of sb_kv_append_int8 on the values k_out / v_out would have held
+      __syncthreads();
+      const int wph = p.head_dim / 32, half = p.head_dim / 2;
+      for (int idx = threadIdx.x; idx < own_pairs * M; idx += kNT) {
+        const int pl = idx / M, m = idx - (idx / M) * M;
+        const int P = pl, w = P >> 4, r = (P >> 3) & 1;
+        const int rbx = blockIdx.y * kGemvWarps + w;
+        if (rbx >= rowblocks) continue;
+        const int head = rbx / wph;
+        if (head < p.heads_q) continue;
+        const bool is_k = head < p.heads_q + p.heads_kv;
+        const int kh = head - p.heads_q - (is_k ? 0 : p.heads_kv);
+        const int bi = (m + p.m0) / p.seq_len;
+        const int pos = p.positions[m + p.m0];
+        if (pos < 0 || pos >= p.kv_capacity) continue;
+        const int i = 16 * (rbx % wph) + 8 * r + sigma_row<C::kLaneB>(P & 7);
+        __half s16 = __float2half_rn(__fdiv_rn(__uint_as_float(s_kvmax[w / wph][m]), 127.0f));
+        if (__half2float(s16) == 0.f) s16 = __float2half_rn(1.0f);
+        const float sc = __half2float(s16);
+        const size_t row = (static_cast<size_t>(bi) * p.heads_kv + kh) * p.kv_capacity + pos;
+        int8_t* codes = (is_k ? p.kv_k_cache : p.kv_v_cache) + row * p.head_dim;
+        const float a = red[((0 * ppc + pl) * 2 + 0) * M + m], b = red[((0 * ppc + pl) * 2 + 1) * M + m];
+        codes[i] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(a, sc)), -127.f), 127.f)));
+        codes[half + i] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(b, sc)), -127.f), 127.f)));
+        if (i == 0) (is_k ? p.kv_k_scale : p.kv_v_scale)[row] = s16;
+      }
+    }
   }
 }
 
@@ -939,7 +986,7 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
     }
     return static_cast<size_t>(2048) + static_cast<size_t>(kGemvWarps) * nsub * p.ring * kStageBytes +
            static_cast<size_t>(p.M) * p.y_ld + static_cast<size_t>(p.M) * p.meta_ld * 16 +
-           static_cast<size_t>(128) * p.M * nsub * sizeof(float) +
+           static_cast<size_t>(128) * p.M * nsub * (p.kv_k_cache != nullptr ? parts : 1) * sizeof(float) +
            static_cast<size_t>(2) * kGemvWarps * 32 * p.sc_ld * sizeof(uint16_t);
   };
   // Largest cluster (K split across CTAs) whose clusters are all co-resident,
@@ -1074,6 +1121,13 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
     SB_REQUIRE(r.N == (r.heads_q + 2 * r.heads_kv) * r.head_dim, "QKV rows must equal (Hq + 2*Hkv) * head_dim");
   }
   if (r.epi == EPI_SWIGLU) SB_REQUIRE(r.N % 8 == 0, "SwiGLU width must be a multiple of 8");
+  if (r.kv_k_cache != nullptr) {
+    SB_REQUIRE(r.epi == EPI_ROPE, "the fused cache append belongs to the RoPE epilogue");
+    SB_REQUIRE(r.head_dim == 64 || r.head_dim == 128, "the fused cache append needs head_dim 64 or 128");
+    SB_REQUIRE(r.kv_k_scale && r.kv_v_cache && r.kv_v_scale && r.kv_capacity > 0 && r.kv_capacity < (1LL << 31),
+               "fused cache append: every cache pointer and a positive capacity are required");
+    SB_REQUIRE(r.positions != nullptr, "fused cache append needs positions");
+  }
 
   GemvParams p{};
   p.x = r.x;
@@ -1115,6 +1169,11 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   p.q_out = r.q_out;
   p.k_out = r.k_out;
   p.v_out = r.v_out;
+  p.kv_k_cache = r.kv_k_cache;
+  p.kv_k_scale = static_cast<__half*>(r.kv_k_scale);
+  p.kv_v_cache = r.kv_v_cache;
+  p.kv_v_scale = static_cast<__half*>(r.kv_v_scale);
+  p.kv_capacity = static_cast<int>(r.kv_capacity);
   p.argmax_keys = r.argmax_keys;
   p.argmax_offset = r.argmax_offset;
   p.early_prefetch = r.weights_constant ? 1 : 0;

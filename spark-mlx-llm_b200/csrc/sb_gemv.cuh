@@ -100,6 +100,12 @@ struct GemvParams {
   void* q_out;
   void* k_out;
   void* v_out;
+  // fused INT8 cache append of the K/V heads (kv_k_cache != null)
+  int8_t* kv_k_cache;
+  __half* kv_k_scale;
+  int8_t* kv_v_cache;
+  __half* kv_v_scale;
+  int kv_capacity;
   float inv_freq[kMaxRopeHalf];
   // argmax epilogue
   unsigned long long* argmax_keys;  // [M]
@@ -132,6 +138,11 @@ struct LinearRequest {
   int heads_q, heads_kv, head_dim, seq_len, rope_dims;
   float rope_base;
   void *q_out, *k_out, *v_out;
+  int8_t* kv_k_cache;
+  void* kv_k_scale;
+  int8_t* kv_v_cache;
+  void* kv_v_scale;
+  int64_t kv_capacity;
   unsigned long long* argmax_keys;
   int argmax_offset;
   void* workspace;

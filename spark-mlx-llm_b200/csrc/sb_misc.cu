@@ -405,6 +405,11 @@ extern "C" int sb_linear_ex(const sb_linear_ex_desc* d, void* stream) {
   r.q_out = d->q_out;
   r.k_out = d->k_out;
   r.v_out = d->v_out;
+  r.kv_k_cache = d->kv_k_cache;
+  r.kv_k_scale = d->kv_k_scale;
+  r.kv_v_cache = d->kv_v_cache;
+  r.kv_v_scale = d->kv_v_scale;
+  r.kv_capacity = d->kv_capacity;
   r.argmax_keys = d->argmax_keys;
   r.argmax_offset = d->argmax_offset;
   r.workspace = d->workspace;

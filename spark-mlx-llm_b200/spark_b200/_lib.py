@@ -66,6 +66,11 @@ class sb_linear_ex_desc(ctypes.Structure):
         ("workspace", _c_void_p),
         ("workspace_bytes", _size),
         ("weights_constant", _int),
+        ("kv_k_cache", _c_void_p),
+        ("kv_k_scale", _c_void_p),
+        ("kv_v_cache", _c_void_p),
+        ("kv_v_scale", _c_void_p),
+        ("kv_capacity", _i64),
     ]
 
 

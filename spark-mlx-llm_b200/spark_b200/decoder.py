@@ -107,6 +107,8 @@ class SyntheticDecoder:
         self.hkv = cfg.num_kv_heads // world
         self.inter = cfg.intermediate // world
         self.vocab_shard = cfg.vocab // world
+        # K/V quantized into the cache by the QKV kernel's epilogue (head_dim 64/128)
+        self.fused_append = cfg.head_dim in (64, 128)
         self._build_weights(seed)
         self._alloc_state()
         self.graph = None
@@ -210,6 +212,14 @@ class SyntheticDecoder:
                              positions=_ptr(self.positions), num_heads=self.hq, num_kv_heads=self.hkv, head_dim=d,
                              seq_len=1, rope_base=cfg.rope_theta, q_out=_ptr(self.q), k_out=_ptr(self.k_new),
                              v_out=_ptr(self.v_new))
+            if self.fused_append:
+                # the QKV kernel quantizes K/V straight into this layer's INT8 cache
+                li = len(self.descs)
+                qkv.kv_k_cache = _ptr(self.k_cache[li])
+                qkv.kv_k_scale = _ptr(self.k_scale[li])
+                qkv.kv_v_cache = _ptr(self.v_cache[li])
+                qkv.kv_v_scale = _ptr(self.v_scale[li])
+                qkv.kv_capacity = self.capacity
             o = self._desc(x=_ptr(self.attn), M=b, N=cfg.hidden, K=self.hq * d, weight_format=SB_WEIGHT_INT8_PC,
                            weight=_ptr(layer["o_w"]), scales=_ptr(layer["o_s"]),
                            epilogue=SB_EPI_STORE if tp else SB_EPI_RESID,
@@ -255,9 +265,10 @@ class SyntheticDecoder:
         scale = 1.0 / math.sqrt(d)
         for li, (qkv, o, gateup, down) in enumerate(self.descs):
             check(L.sb_linear_ex(ctypes.byref(qkv), stream), "qkv_rope")
-            check(L.sb_kv_append_int8(_ptr(self.k_new), _ptr(self.v_new), _ptr(self.k_cache[li]),
-                                      _ptr(self.k_scale[li]), _ptr(self.v_cache[li]), _ptr(self.v_scale[li]), b,
-                                      self.hkv, 1, d, self.capacity, _ptr(self.positions), stream), "kv_append")
+            if not self.fused_append:
+                check(L.sb_kv_append_int8(_ptr(self.k_new), _ptr(self.v_new), _ptr(self.k_cache[li]),
+                                          _ptr(self.k_scale[li]), _ptr(self.v_cache[li]), _ptr(self.v_scale[li]), b,
+                                          self.hkv, 1, d, self.capacity, _ptr(self.positions), stream), "kv_append")
             check(L.sb_int8_sdpa_decode_dev(_ptr(self.q), _ptr(self.k_cache[li]), _ptr(self.k_scale[li]),
                                             _ptr(self.v_cache[li]), _ptr(self.v_scale[li]), _ptr(self.attn), b,
                                             self.hq, self.hkv, _ptr(self.positions), 1, self.capacity,
@@ -284,7 +295,7 @@ class SyntheticDecoder:
 
     def kernels_per_step(self):
         """Number of this library's kernel launches in one ``step()``."""
-        per_layer = 6 + (2 if self.world > 1 else 0)
+        per_layer = (5 if self.fused_append else 6) + (2 if self.world > 1 else 0)
         return 1 + self.cfg.num_layers * per_layer + 2
 
     # ------------------------------------------------------------------ drivers
