@@ -102,11 +102,17 @@ int sb_kv_append_int8(const void* k_new, const void* v_new, int8_t* k_cache, voi
                       int64_t capacity, const int32_t* start, void* stream);
 
 /* INT8-KV decode attention with per-batch lengths lengths[b] + length_offset read on
- * the device; max_length bounds them (it sizes the split-K workspace). */
+ * the device; max_length bounds them (it sizes the split-K workspace).
+ * prefix_constant = 1 promises that `lengths` and every cache row except the
+ * newest one (position lengths[b] + length_offset - 1) were written before the
+ * kernel that precedes this launch in the stream; the kernel then streams those
+ * rows while that kernel still runs (programmatic dependent launch). 0 waits
+ * for the previous kernel before reading anything. */
 int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
                             const void* v_scale, void* out, int64_t batch, int num_heads, int num_kv_heads,
                             const int32_t* lengths, int length_offset, int64_t max_length, int64_t capacity,
-                            int head_dim, float scale, void* workspace, size_t workspace_bytes, void* stream);
+                            int head_dim, float scale, int prefix_constant, void* workspace,
+                            size_t workspace_bytes, void* stream);
 
 /* out[r, :] = table[ids[r], :] (bf16 embedding rows). Replaces nn.Embedding
  * (spark_mlx_llm/model.py:296-305). */

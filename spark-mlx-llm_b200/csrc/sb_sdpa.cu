@@ -50,10 +50,16 @@ struct SdpaParams {
   const int* length_dev;  // optional per-batch lengths in device memory (+ length_offset)
   int length_offset;
   float scale_log2e;
-  float* partial;      // [B*KH][splits][G][kPartStride]
+  float* partial;      // [B*KH][splits][G][kPartStride] (global merge)
   unsigned* counters;  // [B*KH]
   unsigned* status;    // device status word or null
+  int cluster;         // 1: the splits of a (b, kv head) form a cluster and merge in shared memory
+  int early;           // 1: lengths and every cache row but the newest are final before this kernel
 };
+
+constexpr int kSdpaMaxClusterSplits = 16;
+// cluster merge buffer: [split][G][slice + 2] floats, slice = ceil(128 / splits)
+constexpr int kSdpaClusterBuf = 8 * kSdpaD + 3 * 8 * kSdpaMaxClusterSplits;
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
@@ -63,10 +69,12 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
 template <int G>
 __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const __grid_constant__ SdpaParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int bkv = blockIdx.x;
-  const int split = blockIdx.y;
+  const int split = blockIdx.x;
+  const int bkv = blockIdx.y;
   const int b = bkv / p.kv_heads, kvh = bkv % p.kv_heads;
-  grid_dependency_wait();
+  // With `early`, the KV blocks that do not hold the newest token stream in
+  // while the previous kernel (which writes that token) still runs.
+  if (!p.early) grid_dependency_wait();
   const int N = p.length_dev ? min(p.length_dev[b] + p.length_offset, p.capacity) : p.length;
   const int nblk = (N + 15) / 16;
   const int blk_begin = static_cast<int>((static_cast<long long>(nblk) * split) / p.splits);
@@ -74,6 +82,49 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
   const size_t kv_base = static_cast<size_t>(bkv) * p.capacity;
   const __half* ksb = p.ks + kv_base;
   const __half* vsb = p.vs + kv_base;
+
+  // ---- running state (row g of the MMA tiles; rows g+8 are unused padding)
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[16][4];
+  float psum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int j = 0; j < 16; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+  constexpr uint32_t kOnes = 0x3C003C00u;
+
+  // ---- per-warp ring of 16-token K/V blocks in shared memory (TMA boxes)
+  extern __shared__ uint8_t smem_dyn[];
+  // 1 KB-aligned start (pointer arithmetic keeps the shared address space known to the compiler)
+  uint8_t* sbase = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase) + warp * kSdpaStages;
+  uint8_t* ring = sbase + 1024 + warp * kSdpaStages * kSdpaStageBytes;
+  const int nb = blk_end - blk_begin;
+  const int my_blocks = nb > warp ? (nb - warp + kSdpaWarps - 1) / kSdpaWarps : 0;
+  auto block_of = [&](int i) { return blk_begin + warp + i * kSdpaWarps; };
+  auto issue = [&](int i) {
+    const int slot = i % kSdpaStages;
+    const int row = static_cast<int>(kv_base) + block_of(i) * 16;
+    uint8_t* dst = ring + slot * kSdpaStageBytes;
+    mbar_arrive_expect_tx(bars + slot, kSdpaStageBytes);
+    tma_load_2d(dst, &p.kmap, 0, row, bars + slot);
+    tma_load_2d(dst + 16 * kSdpaD, &p.vmap, 0, row, bars + slot);
+  };
+  const int last_blk = nblk - 1;  // holds token N-1, written by the previous kernel
+  if (lane == 0) {
+    for (int i = 0; i < kSdpaStages; ++i) mbar_init(bars + i, 1);
+    mbar_fence_init();
+    for (int i = 0; i < kSdpaStages && i < my_blocks; ++i)
+      if (!p.early || block_of(i) != last_blk) issue(i);
+  }
+  __syncwarp();
+  if (p.early) {
+    grid_dependency_wait();
+    if (lane == 0)
+      for (int i = 0; i < kSdpaStages && i < my_blocks; ++i)
+        if (block_of(i) == last_blk) issue(i);
+    __syncwarp();
+  }
 
   // ---- q fragments: row g = query head kvh*G + g, k-slot d = 32t + 4s + {0..3}
   const bool head_ok = g < G;
@@ -120,39 +171,6 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
   const float qoff = 1152.0f * qsum;                 // sum(q' * 1152) over D
   const float fscale = down * p.scale_log2e;         // undo q scaling, softmax scale, log2(e)
 
-  // ---- running state (row g of the MMA tiles; rows g+8 are unused padding)
-  float m_run = -INFINITY, l_run = 0.f;
-  float acc[16][4];
-  float psum[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int j = 0; j < 16; ++j)
-#pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
-  constexpr uint32_t kOnes = 0x3C003C00u;
-
-  // ---- per-warp ring of 16-token K/V blocks in shared memory (TMA boxes)
-  extern __shared__ uint8_t smem_dyn[];
-  // 1 KB-aligned start (pointer arithmetic keeps the shared address space known to the compiler)
-  uint8_t* sbase = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase) + warp * kSdpaStages;
-  uint8_t* ring = sbase + 1024 + warp * kSdpaStages * kSdpaStageBytes;
-  const int nb = blk_end - blk_begin;
-  const int my_blocks = nb > warp ? (nb - warp + kSdpaWarps - 1) / kSdpaWarps : 0;
-  auto block_of = [&](int i) { return blk_begin + warp + i * kSdpaWarps; };
-  auto issue = [&](int i) {
-    const int slot = i % kSdpaStages;
-    const int row = static_cast<int>(kv_base) + block_of(i) * 16;
-    uint8_t* dst = ring + slot * kSdpaStageBytes;
-    mbar_arrive_expect_tx(bars + slot, kSdpaStageBytes);
-    tma_load_2d(dst, &p.kmap, 0, row, bars + slot);
-    tma_load_2d(dst + 16 * kSdpaD, &p.vmap, 0, row, bars + slot);
-  };
-  if (lane == 0) {
-    for (int i = 0; i < kSdpaStages; ++i) mbar_init(bars + i, 1);
-    mbar_fence_init();
-    for (int i = 0; i < kSdpaStages && i < my_blocks; ++i) issue(i);
-  }
-  __syncwarp();
 
   // scales of this lane's 4 tokens, one block ahead
   float sk[4], sv[4], skn[4], svn[4];
@@ -285,6 +303,58 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
   __syncthreads();
   grid_dependency_launch();
 
+  // ---- splits of one (b, kv head) in a cluster: reduce-scatter of the CTAs'
+  // (m, l, o) over the head dimension in distributed shared memory; rank r
+  // merges dims [r*SL, (r+1)*SL) of every head in split order
+  if (p.cluster) {
+    __shared__ float s_cred[kSdpaClusterBuf];
+    const int S = p.splits, SL = (kSdpaD + S - 1) / S, stride = SL + 2;
+    const uint32_t cred = smem_u32(s_cred);
+    for (int idx = threadIdx.x; idx < G * kSdpaD; idx += kSdpaWarps * 32) {
+      const int hh = idx / kSdpaD, d = idx % kSdpaD;
+      float mm = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kSdpaWarps; ++w) mm = fmaxf(mm, s_m[w][hh]);
+      float ll = 0.f, oo = 0.f;
+      if (mm != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < kSdpaWarps; ++w) {
+          const float f = s_m[w][hh] == -INFINITY ? 0.f : exp2f(s_m[w][hh] - mm);
+          ll += s_l[w][hh] * f;
+          oo += s_o[w][hh][d] * f;
+        }
+      }
+      const int r = d / SL;
+      const int base = (split * G + hh) * stride;
+      st_cluster_f32(cluster_map(cred + 4u * static_cast<uint32_t>(base + d - r * SL), r), oo);
+      if (d == 0) {
+        for (int rr = 0; rr < S; ++rr) {
+          st_cluster_f32(cluster_map(cred + 4u * static_cast<uint32_t>(base + SL), rr), mm);
+          st_cluster_f32(cluster_map(cred + 4u * static_cast<uint32_t>(base + SL + 1), rr), ll);
+        }
+      }
+    }
+    cluster_sync_all();
+    for (int idx = threadIdx.x; idx < G * SL; idx += kSdpaWarps * 32) {
+      const int hh = idx / SL, dl = idx % SL, d = split * SL + dl;
+      if (d >= kSdpaD) continue;
+      float mm = -INFINITY;
+      for (int src = 0; src < S; ++src) mm = fmaxf(mm, s_cred[(src * G + hh) * stride + SL]);
+      float ll = 0.f, oo = 0.f;
+      if (mm != -INFINITY) {
+        for (int src = 0; src < S; ++src) {
+          const float ms = s_cred[(src * G + hh) * stride + SL];
+          const float w = ms == -INFINITY ? 0.f : exp2f(ms - mm);
+          ll += s_cred[(src * G + hh) * stride + SL + 1] * w;
+          oo += s_cred[(src * G + hh) * stride + dl] * w;
+        }
+      }
+      p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] =
+          __float2bfloat16_rn(ll > 0.f ? oo / ll : 0.f);
+    }
+    return;
+  }
+
   // ---- CTA merge (fixed warp order) -> partial or final output
   const bool single = p.splits == 1;
   float* part = p.partial + (static_cast<size_t>(bkv) * p.splits + split) * G * kPartStride;
@@ -379,7 +449,7 @@ int sdpa_splits(int64_t batch, int kv_heads, int64_t length) {
   const int64_t bkv = batch * kv_heads;
   const int64_t nblk = (length + 15) / 16;
   int64_t s = (sdpa_sms() * 4 + bkv - 1) / bkv;
-  s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (4 * kSdpaWarps)));  // >= 4 blocks per warp
+  s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (2 * kSdpaWarps)));  // >= 2 blocks per warp
   s = std::min<int64_t>(s, 64);
   return static_cast<int>(std::max<int64_t>(1, s));
 }
@@ -397,7 +467,7 @@ size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int6
 int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int8_t* v, const void* v_scale,
                   void* out, int64_t batch, int num_heads, int num_kv_heads, int64_t length, int64_t capacity,
                   int head_dim, float scale, void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                  int force_splits, const int* length_dev, int length_offset) {
+                  int force_splits, const int* length_dev, int length_offset, int early = 0) {
   SB_REQUIRE(head_dim == kSdpaD, "this build supports head_dim 128");
   SB_REQUIRE(batch > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
              "Nonempty inputs and query heads divisible by KV heads required");
@@ -444,12 +514,24 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   }
   if (workspace != nullptr && workspace_bytes >= kCounterBytes)
     p.status = static_cast<unsigned*>(workspace) + kStatusWord;
-  const dim3 grid(static_cast<unsigned>(bkv), splits);
+  p.early = early ? 1 : 0;
+  const dim3 grid(splits, static_cast<unsigned>(bkv));
   const dim3 block(kSdpaWarps * 32);
   auto go = [&](auto kernel) -> int {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSdpaSmem)) !=
         cudaSuccess)
       return fail(SB_ECUDA, "int8 sdpa: shared memory opt-in failed");
+    // splits of one (batch, kv head) merge inside a thread-block cluster when it can hold them
+    p.cluster = 0;
+    if (splits > 1 && splits <= kSdpaMaxClusterSplits) {
+      bool ok = splits <= 8;
+      if (!ok) {
+        ok = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+        if (!ok) cudaGetLastError();
+      }
+      p.cluster = ok ? 1 : 0;
+    }
+    if (p.cluster) return launch_cluster("int8 sdpa", kernel, grid, block, kSdpaSmem, splits, stream, p);
     return launch("int8 sdpa", kernel, grid, block, kSdpaSmem, stream, p);
   };
   switch (G) {
@@ -540,9 +622,9 @@ extern "C" int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const voi
                                        const void* v_scale, void* out, int64_t batch, int num_heads,
                                        int num_kv_heads, const int32_t* lengths, int length_offset,
                                        int64_t max_length, int64_t capacity, int head_dim, float scale,
-                                       void* workspace, size_t workspace_bytes, void* stream) {
+                                       int prefix_constant, void* workspace, size_t workspace_bytes, void* stream) {
   SB_REQUIRE(lengths != nullptr, "lengths must be a device pointer");
   return sb::run_sdpa_int8(q, k, k_scale, v, v_scale, out, batch, num_heads, num_kv_heads, max_length, capacity,
                            head_dim, scale, workspace, workspace_bytes, sb::as_stream(stream), 0, lengths,
-                           length_offset);
+                           length_offset, prefix_constant);
 }

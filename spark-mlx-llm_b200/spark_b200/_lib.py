@@ -133,7 +133,7 @@ SIGNATURES = {
     "sb_int8_sdpa_decode_dev": (
         _int,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _c_void_p, _int,
-         _i64, _i64, _int, _float, _c_void_p, _size, _c_void_p],
+         _i64, _i64, _int, _float, _int, _c_void_p, _size, _c_void_p],
     ),
     "sb_embed_rows": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p]),
     "sb_decode_advance": (_int, [_c_void_p, _c_void_p, _c_void_p, _int, _int, _c_void_p]),

@@ -272,7 +272,7 @@ class SyntheticDecoder:
             check(L.sb_int8_sdpa_decode_dev(_ptr(self.q), _ptr(self.k_cache[li]), _ptr(self.k_scale[li]),
                                             _ptr(self.v_cache[li]), _ptr(self.v_scale[li]), _ptr(self.attn), b,
                                             self.hq, self.hkv, _ptr(self.positions), 1, self.capacity,
-                                            self.capacity, d, scale, self.workspace.data_ptr(),
+                                            self.capacity, d, scale, 1, self.workspace.data_ptr(),
                                             self.workspace.numel(), stream), "int8_sdpa")
             check(L.sb_linear_ex(ctypes.byref(o), stream), "o_proj")
             if tp:
