@@ -31,6 +31,7 @@ from dataclasses import dataclass
 import torch
 
 from . import quantize
+from . import tp as tensor_parallel
 from ._lib import check, lib, sb_linear_ex_desc
 
 __all__ = ["DecoderConfig", "SyntheticDecoder"]
@@ -97,16 +98,13 @@ class SyntheticDecoder:
         self.capacity = ((capacity + 15) // 16) * 16
         self.device = torch.device(device)
         self.rank, self.world, self.group = rank, world, group
-        if cfg.num_kv_heads % world or cfg.num_heads % world or cfg.intermediate % (world * cfg.mlp_group):
-            raise ValueError("heads and intermediate size must divide across the tensor-parallel ranks")
-        if cfg.vocab % world:
-            raise ValueError("vocabulary must divide across the tensor-parallel ranks")
         if batch < 1 or batch > 8:
             raise ValueError("batch must be in [1, 8]")
-        self.hq = cfg.num_heads // world
-        self.hkv = cfg.num_kv_heads // world
-        self.inter = cfg.intermediate // world
-        self.vocab_shard = cfg.vocab // world
+        self.plan = tensor_parallel.plan(cfg, rank, world)
+        self.hq = self.plan.heads
+        self.hkv = self.plan.kv_heads
+        self.inter = self.plan.inter
+        self.vocab_shard = self.plan.vocab
         # K/V quantized into the cache by the QKV kernel's epilogue (head_dim 64/128)
         self.fused_append = cfg.head_dim in (64, 128)
         self._build_weights(seed)
@@ -118,7 +116,7 @@ class SyntheticDecoder:
         cfg, dev = self.cfg, self.device
         gen = torch.Generator(device=dev)
         d = cfg.head_dim
-        r = self.rank
+        sp = self.plan
 
         def randn(*shape, std, key):
             gen.manual_seed(seed * 1_000_003 + key)
@@ -135,22 +133,21 @@ class SyntheticDecoder:
             wq = randn(cfg.num_heads * d, cfg.hidden, std=cfg.weight_std, key=base + 1)
             wk = randn(cfg.num_kv_heads * d, cfg.hidden, std=cfg.weight_std, key=base + 2)
             wv = randn(cfg.num_kv_heads * d, cfg.hidden, std=cfg.weight_std, key=base + 3)
-            qkv = torch.cat([rows(wq, r * self.hq * d, self.hq * d), rows(wk, r * self.hkv * d, self.hkv * d),
-                             rows(wv, r * self.hkv * d, self.hkv * d)])
+            qkv = torch.cat([rows(wq, *sp.q_rows), rows(wk, *sp.kv_rows), rows(wv, *sp.kv_rows)])
             del wq, wk, wv
             layer["qkv_w"], layer["qkv_s"] = quantize.quantize_w8_per_channel(qkv)
             del qkv
             wo = randn(cfg.hidden, cfg.num_heads * d, std=cfg.weight_std, key=base + 4)
-            wo = wo[:, r * self.hq * d:(r + 1) * self.hq * d].contiguous()
+            wo = wo[:, sp.o_cols[0]:sp.o_cols[0] + sp.o_cols[1]].contiguous()
             layer["o_w"], layer["o_s"] = quantize.quantize_w8_per_channel(wo)
             del wo
             for name, key in (("gate", 5), ("up", 6)):
                 w = randn(cfg.intermediate, cfg.hidden, std=cfg.weight_std, key=base + key)
-                w = rows(w, r * self.inter, self.inter)
+                w = rows(w, *sp.inter_rows)
                 layer[name] = quantize.quantize_affine_minmax(w, cfg.mlp_group, 4)
                 del w
             wd = randn(cfg.hidden, cfg.intermediate, std=cfg.weight_std, key=base + 7)
-            wd = wd[:, r * self.inter:(r + 1) * self.inter].contiguous()
+            wd = wd[:, sp.down_cols[0]:sp.down_cols[0] + sp.down_cols[1]].contiguous()
             layer["down"] = quantize.quantize_affine_minmax(wd, cfg.mlp_group, 4)
             del wd
             layer["in_norm"] = (1.0 + 0.1 * randn(cfg.hidden, std=1.0, key=base + 8)).to(torch.bfloat16)
@@ -158,7 +155,7 @@ class SyntheticDecoder:
             self.layers.append(layer)
         self.embed = randn(cfg.vocab, cfg.hidden, std=cfg.embed_std, key=11).to(torch.bfloat16)
         head = randn(cfg.vocab, cfg.hidden, std=cfg.head_std, key=12)
-        self.head = rows(head, r * self.vocab_shard, self.vocab_shard).to(torch.bfloat16).contiguous()
+        self.head = rows(head, *sp.vocab_rows).to(torch.bfloat16).contiguous()
         del head
         self.final_norm = (1.0 + 0.1 * randn(cfg.hidden, std=1.0, key=13)).to(torch.bfloat16)
         torch.cuda.synchronize(dev)
@@ -239,7 +236,7 @@ class SyntheticDecoder:
         self.head_desc = self._desc(x=_ptr(self.x), M=b, N=self.vocab_shard, K=cfg.hidden,
                                     weight_format=SB_WEIGHT_BF16, weight=_ptr(self.head),
                                     norm_weight=_ptr(self.final_norm), epilogue=SB_EPI_ARGMAX,
-                                    argmax_keys=_ptr(self.keys), argmax_offset=self.rank * self.vocab_shard)
+                                    argmax_keys=_ptr(self.keys), argmax_offset=self.plan.vocab_rows[0])
 
     def _descs_all(self):
         out = [self.head_desc]
@@ -288,7 +285,10 @@ class SyntheticDecoder:
             if tp:
                 import torch.distributed as dist
 
+                # the keys compare unsigned; the collective compares int64: flip the top bit around it
+                self.keys.bitwise_xor_(tensor_parallel.SIGN_FLIP)
                 self._allreduce(self.keys, dist.ReduceOp.MAX)
+                self.keys.bitwise_xor_(tensor_parallel.SIGN_FLIP)
         if advance:
             check(L.sb_decode_advance(_ptr(self.keys), _ptr(self.tokens), _ptr(self.positions), b, 1, stream),
                   "advance")
