@@ -426,6 +426,8 @@ def main():
     if world > 1:
         del dec.graph
         dist.barrier()
+        dec.close()
+        dist.barrier()
         dist.destroy_process_group()
 
 

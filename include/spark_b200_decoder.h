@@ -85,6 +85,19 @@ typedef struct sb_linear_ex_desc {
   int8_t* kv_v_cache;
   void* kv_v_scale;
   int64_t kv_capacity;
+  /* RESID, optional fused tensor-parallel all-reduce (ar_world 2..8): y is
+   * T(residual + T(sum over ranks of the fp32 partial products)). Each rank
+   * stores its partial rows into every rank's exchange buffer over NVLink,
+   * signals per CTA, waits (bounded) for the other ranks' same CTA and sums in
+   * rank order - this replaces all-reduce + residual-add after the row-split
+   * o/down projections. ar_buffers[r] is rank r's exchange buffer as mapped in
+   * this process (sb_peer_buffer_alloc / _open), sb_tp_exchange_bytes(ar_world,
+   * N) bytes, zeroed at creation; consecutive exchanges alternate ar_channel
+   * 0/1. Every rank must launch the same shapes in the same order. */
+  int ar_world;
+  int ar_rank;
+  int ar_channel;
+  void* ar_buffers[8];
 } sb_linear_ex_desc;
 
 /* Fused weight-streaming linear (1 <= M <= 8). */
@@ -113,6 +126,16 @@ int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const void* k_scale,
                             const int32_t* lengths, int length_offset, int64_t max_length, int64_t capacity,
                             int head_dim, float scale, int prefix_constant, void* workspace,
                             size_t workspace_bytes, void* stream);
+
+/* Exchange buffers of the fused tensor-parallel all-reduce (sb_linear_ex
+ * ar_*): size for `world` ranks and N output rows; a zeroed device buffer
+ * exported as a 64-byte CUDA IPC handle; mapping another rank's buffer into
+ * this process (peer access over NVLink); unmapping; freeing. */
+size_t sb_tp_exchange_bytes(int world, int64_t n);
+int sb_peer_buffer_alloc(size_t bytes, void** ptr, void* handle64);
+int sb_peer_buffer_open(const void* handle64, void** ptr);
+int sb_peer_buffer_close(void* ptr);
+int sb_peer_buffer_free(void* ptr);
 
 /* out[r, :] = table[ids[r], :] (bf16 embedding rows). Replaces nn.Embedding
  * (spark_mlx_llm/model.py:296-305). */

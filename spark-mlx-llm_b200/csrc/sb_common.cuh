@@ -174,6 +174,20 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// ------------------------------------ 8-byte (value, epoch) slots between GPUs
+// A naturally aligned 64-bit access is single-copy atomic, so a reader that
+// sees the expected epoch in a slot also sees the value stored with it: no
+// fence or flag is needed (volatile accesses bypass the non-coherent L1).
+__device__ __forceinline__ void st_slot(void* addr, float v, unsigned epoch) {
+  const unsigned long long w = (static_cast<unsigned long long>(epoch) << 32) | __float_as_uint(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(addr), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_slot(const void* addr) {
+  unsigned long long w;
+  asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(w) : "l"(addr) : "memory");
+  return w;
+}
+
 // ------------------------------------------------- thread-block cluster (DSMEM)
 // Address of the same shared-memory offset in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t cluster_map(uint32_t local, int rank) {

@@ -745,6 +745,17 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
 
   // ---- final epilogue over this part's pairs
   const int own_pairs = (kv_fused && part != 0) ? 0 : ppc;
+  // fused all-reduce: this CTA's exchange epoch (the same on every rank)
+  const size_t ar_chan_bytes = static_cast<size_t>(p.ar_world) * p.ar_np * 64 + static_cast<size_t>(kArCtas) * 4;
+  __shared__ unsigned s_epoch;
+  unsigned* ar_seen = nullptr;
+  if (EPI == EPI_RESID && p.ar_world > 1) {
+    ar_seen = reinterpret_cast<unsigned*>(p.ar_buf[p.ar_rank] + p.ar_channel * ar_chan_bytes +
+                                          static_cast<size_t>(p.ar_world) * p.ar_np * 64) +
+              (blockIdx.y * gridDim.x + blockIdx.x);
+    if (threadIdx.x == 0) s_epoch = *ar_seen + 1u;
+    __syncthreads();
+  }
   for (int idx = threadIdx.x; idx < own_pairs * M; idx += kNT) {
     const int pl = idx / M, m = idx - (idx / M) * M;
     const int P = (kv_fused ? 0 : part * ppc) + pl;
@@ -829,6 +840,39 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
         const float v = h ? v_hi : v_lo;
         const size_t o = static_cast<size_t>(m + p.m0) * p.ldy + row;
         if constexpr (EPI == EPI_RESID) {
+          if (p.ar_world > 1) {
+            // fused all-reduce: post this rank's fp32 partial with the epoch in
+            // slot [ar_rank] of every other rank, wait for the other ranks'
+            // partials of the same output element here, sum in rank order
+            const unsigned epoch = s_epoch;
+            const size_t col = (static_cast<size_t>(row) * 8 + m + p.m0) * 8;
+            const size_t chan = p.ar_channel * ar_chan_bytes;
+            for (int q = 0; q < p.ar_world; ++q)
+              if (q != p.ar_rank)
+                st_slot(p.ar_buf[q] + chan + static_cast<size_t>(p.ar_rank) * p.ar_np * 64 + col, v, epoch);
+            float sum = 0.f;
+            for (int q = 0; q < p.ar_world; ++q) {
+              if (q == p.ar_rank) {
+                sum += v;
+                continue;
+              }
+              const uint8_t* slot = p.ar_buf[p.ar_rank] + chan + static_cast<size_t>(q) * p.ar_np * 64 + col;
+              unsigned long long w = ld_slot(slot);
+              if (static_cast<unsigned>(w >> 32) != epoch) {
+                const long long start = clock64();
+                while (static_cast<unsigned>((w = ld_slot(slot)) >> 32) != epoch) {
+                  if (clock64() - start > (1LL << 31)) {
+                    if (p.status) atomicOr(p.status, kStatusTimeout);
+                    break;
+                  }
+                }
+              }
+              sum += __uint_as_float(static_cast<unsigned>(w));
+            }
+            const float res_v = load_act<TA>(p.residual, static_cast<size_t>(m + p.m0) * p.ldr + row);
+            store_act<TA>(p.y, o, res_v + round_act<TA>(sum));
+            continue;
+          }
           const float res_v = load_act<TA>(p.residual, static_cast<size_t>(m + p.m0) * p.ldr + row);
           store_act<TA>(p.y, o, res_v + round_act<TA>(v));
         } else {
@@ -841,6 +885,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
     __syncthreads();
     if (threadIdx.x < M && s_keys[threadIdx.x]) atomicMax(p.argmax_keys + p.m0 + threadIdx.x, s_keys[threadIdx.x]);
   }
+  if (EPI == EPI_RESID && p.ar_world > 1 && threadIdx.x == 0) *ar_seen = s_epoch;
   if constexpr (EPI == EPI_ROPE) {
     if (kv_fused) {
       // symmetric INT8 per (token, KV head): scale = fp16(max|x| / 127) (1 for
@@ -1020,6 +1065,8 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
     if (int st = make_tmap_u16(&p.smap1, p.s1, n, gpr, p.sc_ld, 16)) return st;
     if (int st = make_tmap_u16(&p.bmap1, p.b1, n, gpr, p.sc_ld, 16)) return st;
   }
+  if (p.ar_world > 1 && parts * row_groups > kArCtas)
+    return fail(SB_EUNSUPPORTED, "fused all-reduce: too many CTAs for the exchange counters");
   dim3 grid(parts, row_groups);
   return launch_cluster("gemv", kernel, grid, dim3(kGemvWarps * 32 * nsub), smem, parts, stream, p);
 }
@@ -1121,6 +1168,12 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
     SB_REQUIRE(r.N == (r.heads_q + 2 * r.heads_kv) * r.head_dim, "QKV rows must equal (Hq + 2*Hkv) * head_dim");
   }
   if (r.epi == EPI_SWIGLU) SB_REQUIRE(r.N % 8 == 0, "SwiGLU width must be a multiple of 8");
+  if (r.ar_world > 1) {
+    SB_REQUIRE(r.epi == EPI_RESID, "the fused all-reduce belongs to the residual epilogue");
+    SB_REQUIRE(r.ar_world <= 8 && r.ar_rank >= 0 && r.ar_rank < r.ar_world, "ar_world must be 2..8, 0 <= ar_rank < ar_world");
+    SB_REQUIRE(r.ar_channel == 0 || r.ar_channel == 1, "ar_channel must be 0 or 1");
+    for (int q = 0; q < r.ar_world; ++q) SB_REQUIRE(r.ar_buffers[q] != nullptr, "every rank's exchange buffer is required");
+  }
   if (r.kv_k_cache != nullptr) {
     SB_REQUIRE(r.epi == EPI_ROPE, "the fused cache append belongs to the RoPE epilogue");
     SB_REQUIRE(r.head_dim == 64 || r.head_dim == 128, "the fused cache append needs head_dim 64 or 128");
@@ -1174,6 +1227,11 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   p.kv_v_cache = r.kv_v_cache;
   p.kv_v_scale = static_cast<__half*>(r.kv_v_scale);
   p.kv_capacity = static_cast<int>(r.kv_capacity);
+  p.ar_world = r.ar_world > 1 ? r.ar_world : 0;
+  p.ar_rank = r.ar_rank;
+  p.ar_channel = r.ar_channel;
+  p.ar_np = static_cast<int>(ar_np(r.N));
+  for (int q = 0; q < 8; ++q) p.ar_buf[q] = static_cast<uint8_t*>(r.ar_buffers[q]);
   p.argmax_keys = r.argmax_keys;
   p.argmax_offset = r.argmax_offset;
   p.early_prefetch = r.weights_constant ? 1 : 0;

@@ -106,6 +106,9 @@ struct GemvParams {
   int8_t* kv_v_cache;
   __half* kv_v_scale;
   int kv_capacity;
+  // fused tensor-parallel all-reduce of a RESID epilogue (ar_world > 1)
+  int ar_world, ar_rank, ar_channel, ar_np;
+  uint8_t* ar_buf[8];
   float inv_freq[kMaxRopeHalf];
   // argmax epilogue
   unsigned long long* argmax_keys;  // [M]
@@ -143,6 +146,8 @@ struct LinearRequest {
   int8_t* kv_v_cache;
   void* kv_v_scale;
   int64_t kv_capacity;
+  int ar_world, ar_rank, ar_channel;
+  void* ar_buffers[8];
   unsigned long long* argmax_keys;
   int argmax_offset;
   void* workspace;
@@ -151,6 +156,15 @@ struct LinearRequest {
 };
 
 int run_linear(const LinearRequest& r, cudaStream_t stream);
+
+// Exchange-buffer layout of the fused tensor-parallel all-reduce, per channel
+// (2 channels): 8-byte slots [world][np][8] holding (fp32 partial, epoch), then
+// one epoch counter per CTA [kArCtas]. np = N rounded up to 64.
+constexpr int kArCtas = 2048;
+inline size_t ar_np(int64_t n) { return static_cast<size_t>((n + 63) / 64 * 64); }
+inline size_t ar_channel_bytes(int world, int64_t n) {
+  return static_cast<size_t>(world) * ar_np(n) * 8 * 8 + static_cast<size_t>(kArCtas) * 4;
+}
 size_t linear_workspace_size(int epi, int N, int K, int group_k);
 
 }  // namespace sb

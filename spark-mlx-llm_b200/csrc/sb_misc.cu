@@ -410,6 +410,10 @@ extern "C" int sb_linear_ex(const sb_linear_ex_desc* d, void* stream) {
   r.kv_v_cache = d->kv_v_cache;
   r.kv_v_scale = d->kv_v_scale;
   r.kv_capacity = d->kv_capacity;
+  r.ar_world = d->ar_world;
+  r.ar_rank = d->ar_rank;
+  r.ar_channel = d->ar_channel;
+  for (int i = 0; i < 8; ++i) r.ar_buffers[i] = d->ar_buffers[i];
   r.argmax_keys = d->argmax_keys;
   r.argmax_offset = d->argmax_offset;
   r.workspace = d->workspace;
@@ -454,4 +458,47 @@ extern "C" int sb_residual_add(void* x, const void* y, int64_t count, void* stre
   return launch("residual_add", residual_add_kernel, dim3(static_cast<unsigned>((vecs + threads - 1) / threads)),
                 dim3(threads), 0, as_stream(stream), static_cast<__nv_bfloat16*>(x),
                 static_cast<const __nv_bfloat16*>(y), static_cast<int>(count));
+}
+
+// ------------------------------------------------------ peer exchange buffers
+extern "C" size_t sb_tp_exchange_bytes(int world, int64_t n) {
+  if (world < 2 || world > 8 || n <= 0) return 0;
+  return 2 * ar_channel_bytes(world, n);
+}
+
+extern "C" int sb_peer_buffer_alloc(size_t bytes, void** ptr, void* handle64) {
+  SB_REQUIRE(bytes > 0 && ptr != nullptr && handle64 != nullptr, "bad peer buffer request");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  void* p = nullptr;
+  cudaError_t err = cudaMalloc(&p, bytes);
+  if (err != cudaSuccess) return fail(SB_ECUDA, std::string("peer buffer cudaMalloc: ") + cudaGetErrorString(err));
+  err = cudaMemset(p, 0, bytes);
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle64), p);
+  if (err != cudaSuccess) {
+    cudaFree(p);
+    return fail(SB_ECUDA, std::string("peer buffer export: ") + cudaGetErrorString(err));
+  }
+  *ptr = p;
+  return SB_OK;
+}
+
+extern "C" int sb_peer_buffer_open(const void* handle64, void** ptr) {
+  SB_REQUIRE(handle64 != nullptr && ptr != nullptr, "bad peer buffer handle");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  const cudaError_t err = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return fail(SB_ECUDA, std::string("cudaIpcOpenMemHandle: ") + cudaGetErrorString(err));
+  return SB_OK;
+}
+
+extern "C" int sb_peer_buffer_close(void* ptr) {
+  const cudaError_t err = cudaIpcCloseMemHandle(ptr);
+  if (err != cudaSuccess) return fail(SB_ECUDA, std::string("cudaIpcCloseMemHandle: ") + cudaGetErrorString(err));
+  return SB_OK;
+}
+
+extern "C" int sb_peer_buffer_free(void* ptr) {
+  const cudaError_t err = cudaFree(ptr);
+  if (err != cudaSuccess) return fail(SB_ECUDA, std::string("peer buffer cudaFree: ") + cudaGetErrorString(err));
+  return SB_OK;
 }

@@ -71,6 +71,10 @@ class sb_linear_ex_desc(ctypes.Structure):
         ("kv_v_cache", _c_void_p),
         ("kv_v_scale", _c_void_p),
         ("kv_capacity", _i64),
+        ("ar_world", _int),
+        ("ar_rank", _int),
+        ("ar_channel", _int),
+        ("ar_buffers", _c_void_p * 8),
     ]
 
 
@@ -138,6 +142,11 @@ SIGNATURES = {
     "sb_embed_rows": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p]),
     "sb_decode_advance": (_int, [_c_void_p, _c_void_p, _c_void_p, _int, _int, _c_void_p]),
     "sb_residual_add": (_int, [_c_void_p, _c_void_p, _i64, _c_void_p]),
+    "sb_tp_exchange_bytes": (_size, [_int, _i64]),
+    "sb_peer_buffer_alloc": (_int, [_size, ctypes.POINTER(_c_void_p), _c_void_p]),
+    "sb_peer_buffer_open": (_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "sb_peer_buffer_close": (_int, [_c_void_p]),
+    "sb_peer_buffer_free": (_int, [_c_void_p]),
 }
 
 _lock = threading.Lock()

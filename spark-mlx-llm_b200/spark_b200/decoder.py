@@ -107,6 +107,9 @@ class SyntheticDecoder:
         self.vocab_shard = self.plan.vocab
         # K/V quantized into the cache by the QKV kernel's epilogue (head_dim 64/128)
         self.fused_append = cfg.head_dim in (64, 128)
+        # TP: o/down partial sums meet inside the GEMV epilogue (NVLink peer
+        # stores) instead of an NCCL all-reduce and a residual-add launch
+        self.fused_allreduce = world > 1 and world <= 8
         self._build_weights(seed)
         self._alloc_state()
         self.graph = None
@@ -180,6 +183,7 @@ class SyntheticDecoder:
         self.tokens = torch.zeros((b,), dtype=torch.int32, device=dev)
         self.positions = torch.zeros((b,), dtype=torch.int32, device=dev)
         self.keys = torch.zeros((b,), dtype=torch.int64, device=dev)
+        self._setup_exchange()
         self._build_descs()
         sizes = [lib().sb_linear_ex_workspace_size(ctypes.byref(desc)) for desc in self._descs_all()]
         sizes.append(lib().sb_int8_sdpa_workspace_size(b, self.hq, self.hkv, self.capacity, d))
@@ -187,6 +191,57 @@ class SyntheticDecoder:
         for desc in self._descs_all():
             desc.workspace = self.workspace.data_ptr()
             desc.workspace_bytes = self.workspace.numel()
+
+    def _setup_exchange(self):
+        """Tensor parallel: every rank allocates a zeroed exchange buffer, exports
+        it as a CUDA IPC handle and maps the other ranks' buffers (NVLink peer
+        access), for the all-reduce fused into the o/down GEMV epilogues."""
+        self.ar_buffers = []
+        self._own_buffer = None
+        self._mapped = []
+        if not self.fused_allreduce:
+            return
+        import torch.distributed as dist
+
+        L = lib()
+        nbytes = L.sb_tp_exchange_bytes(self.world, self.cfg.hidden)
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * 64)()
+        check(L.sb_peer_buffer_alloc(nbytes, ctypes.byref(ptr), handle), "exchange buffer")
+        self._own_buffer = ptr.value
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=self.group)
+        for r in range(self.world):
+            if r == self.rank:
+                self.ar_buffers.append(self._own_buffer)
+                continue
+            peer = ctypes.c_void_p()
+            h = (ctypes.c_ubyte * 64).from_buffer_copy(handles[r])
+            check(L.sb_peer_buffer_open(h, ctypes.byref(peer)), "map peer exchange buffer")
+            self._mapped.append(peer.value)
+            self.ar_buffers.append(peer.value)
+        dist.barrier(group=self.group)
+
+    def close(self):
+        """Unmap the peers' exchange buffers and free this rank's (tensor parallel)."""
+        L = lib()
+        for ptr in self._mapped:
+            L.sb_peer_buffer_close(ptr)
+        self._mapped = []
+        if self._own_buffer:
+            L.sb_peer_buffer_free(self._own_buffer)
+            self._own_buffer = None
+
+    def _allreduce_desc(self, desc, channel):
+        """o/down epilogue: residual add with the ranks' partial sums reduced in-kernel."""
+        desc.epilogue = SB_EPI_RESID
+        desc.y = _ptr(self.x)
+        desc.residual = _ptr(self.x)
+        desc.ar_world = self.world
+        desc.ar_rank = self.rank
+        desc.ar_channel = channel
+        for r, ptr in enumerate(self.ar_buffers):
+            desc.ar_buffers[r] = ptr
 
     def _desc(self, **kw):
         desc = sb_linear_ex_desc()
@@ -232,6 +287,9 @@ class SyntheticDecoder:
                               weight=_ptr(dw), scales=_ptr(ds), biases=_ptr(db), group_size=cfg.mlp_group,
                               epilogue=SB_EPI_STORE if tp else SB_EPI_RESID,
                               y=_ptr(self.part if tp else self.x), residual=_ptr(self.x))
+            if self.fused_allreduce:
+                self._allreduce_desc(o, 0)
+                self._allreduce_desc(down, 1)
             self.descs.append((qkv, o, gateup, down))
         self.head_desc = self._desc(x=_ptr(self.x), M=b, N=self.vocab_shard, K=cfg.hidden,
                                     weight_format=SB_WEIGHT_BF16, weight=_ptr(self.head),
@@ -272,12 +330,12 @@ class SyntheticDecoder:
                                             self.capacity, d, scale, 1, self.workspace.data_ptr(),
                                             self.workspace.numel(), stream), "int8_sdpa")
             check(L.sb_linear_ex(ctypes.byref(o), stream), "o_proj")
-            if tp:
+            if tp and not self.fused_allreduce:
                 self._allreduce(self.part)
                 check(L.sb_residual_add(_ptr(self.x), _ptr(self.part), b * cfg.hidden, stream), "residual")
             check(L.sb_linear_ex(ctypes.byref(gateup), stream), "gate_up")
             check(L.sb_linear_ex(ctypes.byref(down), stream), "down")
-            if tp:
+            if tp and not self.fused_allreduce:
                 self._allreduce(self.part)
                 check(L.sb_residual_add(_ptr(self.x), _ptr(self.part), b * cfg.hidden, stream), "residual")
         if lm_head:
@@ -295,7 +353,7 @@ class SyntheticDecoder:
 
     def kernels_per_step(self):
         """Number of this library's kernel launches in one ``step()``."""
-        per_layer = (5 if self.fused_append else 6) + (2 if self.world > 1 else 0)
+        per_layer = (5 if self.fused_append else 6) + (2 if self.world > 1 and not self.fused_allreduce else 0)
         return 1 + self.cfg.num_layers * per_layer + 2
 
     # ------------------------------------------------------------------ drivers

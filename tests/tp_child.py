@@ -29,6 +29,9 @@ def predictions(world, rank, group, device, steps=24, prompt_len=8, batch=2):
         dec.step()
         out.append(dec.tokens.cpu().numpy().copy())
     torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+        dec.close()
     return np.stack(out)
 
 
