@@ -50,7 +50,7 @@ def parse_args():
     p.add_argument("--prompt", type=int, default=1024)
     p.add_argument("--layers", type=int, default=36, help="(debug) fewer layers")
     p.add_argument("--no-cpu-baseline", action="store_true")
-    p.add_argument("--kernel-only", choices=["gateup", "sdpa"], default=None,
+    p.add_argument("--kernel-only", choices=["gateup", "sdpa", "tc"], default=None,
                    help="launch one hot kernel --steps times on a config-sized case (for ncu)")
     return p.parse_args()
 
@@ -264,6 +264,21 @@ def kernel_only(args):
                               norm_weight=norm.data_ptr(), norm_eps=1e-6, epilogue=2, y=y.data_ptr(),
                               workspace=ws.data_ptr(), workspace_bytes=ws.numel(), weights_constant=1)
         launch = lambda: check(L.sb_linear_ex(ctypes.byref(d), stream), "gateup")  # noqa: E731
+    elif args.kernel_only == "tc":
+        # tensor-core W4A16 linear (config 1): M = --batch rows, K 2560, N 9728, group 64;
+        # weights rotate over 8 copies (> L2) so every launch streams from HBM
+        n, k, m = 9728, 2560, args.batch
+        copies = [quantize.quantize_affine_minmax(torch.randn(n, k, generator=g, device=dev) * 0.02, 64, 4)
+                  for _ in range(8)]
+        x = torch.randn(m, k, generator=g, device=dev).bfloat16()
+        y = torch.empty(m, n, device=dev).bfloat16()
+        it = [0]
+
+        def launch():
+            w, s, b = copies[it[0] % len(copies)]
+            it[0] += 1
+            check(L.sb_affine_linear(x.data_ptr(), 0, w.data_ptr(), s.data_ptr(), b.data_ptr(), y.data_ptr(), m, n,
+                                     k, 64, 4, None, 0, stream), "tc")
     else:
         b_, n = args.batch, 32768
         q = torch.randn(b_, 32, 1, 128, generator=g, device=dev).bfloat16()
@@ -284,7 +299,13 @@ def kernel_only(args):
         launch()
     e1.record()
     torch.cuda.synchronize()
-    print(json.dumps({"kernel": args.kernel_only, "launches": args.steps, "avg_us": e0.elapsed_time(e1) * 1e3 / args.steps}))
+    out = {"kernel": args.kernel_only, "launches": args.steps, "avg_us": e0.elapsed_time(e1) * 1e3 / args.steps}
+    if args.kernel_only == "tc":
+        m = args.batch
+        out["M"] = m
+        out["tflops"] = 2.0 * m * 9728 * 2560 / (out["avg_us"] * 1e-6) / 1e12
+        out["gbs"] = (9728 * 2560 // 2 + 9728 * 40 * 4 + m * 2560 * 2 + m * 9728 * 2) / (out["avg_us"] * 1e-6) / 1e9
+    print(json.dumps(out))
 
 
 # -------------------------------------------------------------------- GPU arm

@@ -25,7 +25,7 @@ __all__ = [
 ]
 
 
-def affine_linear(x, packed, scales, biases, group_size, bits):
+def affine_linear(x, packed, scales, biases, group_size, bits, weight_round=None):
     """``y = x @ W^T`` with MLX-affine ``W = scale * q + bias``, float64.
 
     The arithmetic of ``mx.quantized_matmul(x, w, scales, biases,
@@ -35,9 +35,19 @@ def affine_linear(x, packed, scales, biases, group_size, bits):
     (``spark_mlx_ext/_w4a16_sources.py:24-39``), which equals this up to fp32
     rounding. ``scales``/``biases`` are float values. Returns float64
     ``[..., N]`` (unrounded).
+
+    ``weight_round`` ("bf16" or "f16") rounds the dequantized weights to the
+    activation dtype first: the multi-row (GEMM) path of mx.quantized_matmul
+    (mlx 0.32.4, a dependency pinned at ``uv.lock:421-422``) dequantizes each
+    weight tile into the activation type before its matrix multiply, and the
+    tensor-core kernel for more than 8 rows does the same.
     """
     x = np.asarray(x, dtype=np.float64)
     w = dequantize_affine(packed, scales, biases, group_size, bits)
+    if weight_round == "bf16":
+        w = round_bf16(w.astype(np.float32)).astype(np.float64)
+    elif weight_round == "f16":
+        w = w.astype(np.float16).astype(np.float64)
     return x @ w.T
 
 
@@ -111,7 +121,7 @@ def rope(x, positions, dims, base):
 
 
 def qkv_rope(x, packed, scales, biases, group_size, bits, n_heads, n_kv_heads,
-             head_dim, rope_dims, rope_base, positions):
+             head_dim, rope_dims, rope_base, positions, weight_round=None):
     """Fused QKV projection + head split + RoPE (``src/spark_qkv_rope.cpp:83-101``).
 
     ``x[B, L, H]``; ``positions[B, L]`` integers. The projection is rounded to
@@ -122,7 +132,7 @@ def qkv_rope(x, packed, scales, biases, group_size, bits, n_heads, n_kv_heads,
     """
     x = np.asarray(x, dtype=np.float32)
     bsz, length, _ = x.shape
-    qkv = round_bf16(affine_linear(x, packed, scales, biases, group_size, bits))
+    qkv = round_bf16(affine_linear(x, packed, scales, biases, group_size, bits, weight_round))
     q_size, kv_size = n_heads * head_dim, n_kv_heads * head_dim
 
     def heads(part, n):

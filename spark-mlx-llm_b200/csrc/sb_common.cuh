@@ -33,6 +33,12 @@ int make_tmap_rows(CUtensorMap* map, const void* base, uint64_t rows, uint64_t r
 // box [box_rows x box_cols]; out-of-range reads fill zeros.
 int make_tmap_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t cols, uint32_t box_cols,
                   uint32_t box_rows);
+// General 2-D TMA descriptor over a row-major matrix [rows][cols] of 1- or
+// 2-byte elements with row stride `ld` elements, box [box_rows x box_cols],
+// optional 128-byte swizzle (box_cols * elem_bytes must then be 128); reads
+// outside the matrix fill zeros.
+int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint32_t box_cols, uint32_t box_rows, bool swizzle128);
 
 // Every workspace starts with a fixed-size region of arrival counters (zero
 // between calls), followed by the call's partial results. The fixed size keeps

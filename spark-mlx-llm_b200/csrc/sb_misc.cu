@@ -6,6 +6,7 @@
 
 #include "sb_common.cuh"
 #include "sb_gemv.cuh"
+#include "sb_tcgemm.cuh"
 #include "spark_b200_decoder.h"
 
 namespace sb {
@@ -72,6 +73,26 @@ int make_tmap_u16(CUtensorMap* map, const void* base, uint64_t rows, uint64_t co
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base), dims, strides, box, elem,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(SB_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+  return SB_OK;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, uint64_t rows, uint64_t cols, uint64_t ld,
+                 uint32_t box_cols, uint32_t box_rows, bool swizzle128) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return fail(SB_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * elem_bytes) % 16 || (box_cols * elem_bytes) % 16 ||
+      box_cols * elem_bytes > 128 || box_rows > 256 || (swizzle128 && box_cols * elem_bytes != 128))
+    return fail(SB_EINVAL, "TMA source must be 16-byte aligned with rows and boxes a multiple of 16 bytes");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * static_cast<uint64_t>(elem_bytes)};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r =
+      fn(map, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+         const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(SB_ECUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
   return SB_OK;
 }
@@ -248,6 +269,23 @@ extern "C" int sb_affine_linear(const void* x, int x_dtype, const uint32_t* w, c
   if (wf < 0) return fail(SB_EUNSUPPORTED, "affine bits must be 4 or 8");
   SB_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128, "group_size must be 32, 64 or 128");
   SB_REQUIRE(K % group_size == 0, "K must be a multiple of group_size");
+  if (M > 8) {  // tensor-core (tcgen05) kernel when the shapes allow it
+    TcRequest t;
+    t.tw = bits == 4 ? TW_AFF4 : TW_AFF8;
+    t.te = TE_STORE;
+    t.act_dtype = x_dtype;
+    t.x = x;
+    t.M = static_cast<int>(M);
+    t.N = static_cast<int>(N);
+    t.K = static_cast<int>(K);
+    t.w = w;
+    t.scales = scales;
+    t.biases = biases;
+    t.group_size = group_size;
+    t.y = y;
+    t.ldy = static_cast<int>(N);
+    if (tc_linear_supported(t)) return run_tc_linear(t, as_stream(stream));
+  }
   for (int64_t m0 = 0; m0 < M; m0 += 8) {
     LinearRequest r = base_request(static_cast<const uint8_t*>(x) + m0 * K * act_size(x_dtype), x_dtype,
                                    std::min<int64_t>(8, M - m0), N, K);
@@ -277,6 +315,21 @@ extern "C" int sb_w8a16_per_channel(const void* x, int x_dtype, const int8_t* w,
   SB_REQUIRE(x_dtype == SB_DTYPE_BF16 || x_dtype == SB_DTYPE_F16,
              "w8a16_per_channel x must have dtype bfloat16 or float16.");
   if (K % 64) return fail(SB_EUNSUPPORTED, "this build requires K to be a multiple of 64");
+  if (M > 8) {  // tensor-core (tcgen05) kernel when the shapes allow it
+    TcRequest t;
+    t.tw = TW_I8;
+    t.te = TE_CHSCALE;
+    t.act_dtype = x_dtype;
+    t.x = x;
+    t.M = static_cast<int>(M);
+    t.N = static_cast<int>(N);
+    t.K = static_cast<int>(K);
+    t.w = w;
+    t.wscale = scales;
+    t.y = y;
+    t.ldy = static_cast<int>(N);
+    if (tc_linear_supported(t)) return run_tc_linear(t, as_stream(stream));
+  }
   for (int64_t m0 = 0; m0 < M; m0 += 8) {
     LinearRequest r = base_request(static_cast<const uint8_t*>(x) + m0 * K * act_size(x_dtype), x_dtype,
                                    std::min<int64_t>(8, M - m0), N, K);
@@ -307,7 +360,6 @@ extern "C" int sb_qkv_rope(const void* x, int x_dtype, const uint32_t* w, const 
                            int rope_dims, float rope_base, int group_size, int bits, void* workspace,
                            size_t workspace_bytes, void* stream) {
   SB_REQUIRE(batch > 0 && seq_len > 0 && hidden > 0, "x must have shape [B, L, hidden] with hidden > 0.");
-  SB_REQUIRE(batch * seq_len <= 8, "this build fuses QKV + RoPE for at most 8 tokens per call");
   SB_REQUIRE(num_heads > 0 && num_kv_heads > 0 && head_dim > 0 && num_heads % num_kv_heads == 0,
              "Invalid head counts, head_dim, q_size, or kv_size.");
   SB_REQUIRE(rope_dims > 0 && rope_dims % 2 == 0 && rope_dims <= head_dim && std::isfinite(rope_base) &&
@@ -320,6 +372,33 @@ extern "C" int sb_qkv_rope(const void* x, int x_dtype, const uint32_t* w, const 
   if (wf < 0) return fail(SB_EUNSUPPORTED, "bits must be 4 or 8 in this build");
   SB_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128, "group_size must be 32, 64, or 128.");
   SB_REQUIRE(hidden % group_size == 0, "Packed weight and quantization metadata shapes do not match x.");
+  if (batch * seq_len > 8) {  // tensor-core (tcgen05) kernel, one 128-row weight tile per head
+    TcRequest t;
+    t.tw = bits == 4 ? TW_AFF4 : TW_AFF8;
+    t.te = TE_ROPE;
+    t.act_dtype = x_dtype;
+    t.x = x;
+    t.M = static_cast<int>(batch * seq_len);
+    t.N = (num_heads + 2 * num_kv_heads) * head_dim;
+    t.K = static_cast<int>(hidden);
+    t.w = w;
+    t.scales = scales;
+    t.biases = biases;
+    t.group_size = group_size;
+    t.positions = positions;
+    t.heads_q = num_heads;
+    t.heads_kv = num_kv_heads;
+    t.seq_len = static_cast<int>(seq_len);
+    t.rope_base = rope_base;
+    t.q_out = q_out;
+    t.k_out = k_out;
+    t.v_out = v_out;
+    SB_REQUIRE(positions != nullptr, "positions are required");
+    if (head_dim != 128 || !tc_linear_supported(t))
+      return fail(SB_EUNSUPPORTED, "QKV + RoPE for more than 8 tokens needs head_dim 128, hidden / group_size a "
+                                   "multiple of 8 and 16-byte aligned tensors");
+    return run_tc_linear(t, as_stream(stream));
+  }
   LinearRequest r = base_request(x, x_dtype, batch * seq_len,
                                  static_cast<int64_t>(num_heads + 2 * num_kv_heads) * head_dim, hidden);
   r.wf = wf;

@@ -7,7 +7,9 @@
 //
 // Design (B200): the KV stream is the HBM-bound part (260 bytes per token per
 // KV head); everything else lives in registers. One CTA handles one
-// (batch, kv head, token range); its 4 warps take 16-token blocks in turn.
+// (batch, kv head, token range); its 8 warps take 16-token blocks in turn,
+// each keeping 3 blocks (K box, V box and the blocks' fp16 scales) in flight
+// in its own shared-memory ring (two CTAs per SM: 48 blocks in flight).
 // Scores and P.V run on the tensor cores (mma.sync m16n8k16, fp16 operands,
 // fp32 accumulate): the G query heads sharing a KV head are the MMA rows
 // (GQA reuse: every K/V byte is loaded once for all G heads). int8 codes are
@@ -29,13 +31,14 @@
 
 namespace sb {
 
-constexpr int kSdpaWarps = 4;
+constexpr int kSdpaWarps = 8;
 constexpr int kSdpaD = 128;
 constexpr int kPartStride = kSdpaD + 4;  // O[D], then m, l
-constexpr int kSdpaStages = 4;           // 16-token blocks in flight per warp
+constexpr int kSdpaStages = 3;           // 16-token blocks in flight per warp
 constexpr int kMaxSplits = 64;           // token splits per (batch, kv head)
 constexpr int kSdpaStageBytes = 2 * 16 * kSdpaD;  // swizzled K box + V box
-constexpr size_t kSdpaSmem = 2048 + static_cast<size_t>(kSdpaWarps) * kSdpaStages * kSdpaStageBytes;
+constexpr int kSdpaScaleBytes = 64;                 // the block's 16 K scales + 16 V scales (fp16)
+constexpr size_t kSdpaSmem = 2048 + static_cast<size_t>(kSdpaWarps) * kSdpaStages * (kSdpaStageBytes + kSdpaScaleBytes);
 
 struct SdpaParams {
   alignas(64) CUtensorMap kmap;  // K cache as [B*KH*cap rows][128 B], 16-row boxes, 128-B swizzle
@@ -55,19 +58,31 @@ struct SdpaParams {
   unsigned* status;    // device status word or null
   int cluster;         // 1: the splits of a (b, kv head) form a cluster and merge in shared memory
   int early;           // 1: lengths and every cache row but the newest are final before this kernel
+  int scale_bulk;      // 1: the blocks' scales stream with the K/V boxes (capacity % 16 == 0, aligned)
 };
 
 constexpr int kSdpaMaxClusterSplits = 16;
 // cluster merge buffer: [split][G][slice + 2] floats, slice = ceil(128 / splits)
 constexpr int kSdpaClusterBuf = 8 * kSdpaD + 3 * 8 * kSdpaMaxClusterSplits;
 
+// m16n8k16 fp16 MMA keeping only rows 0-7 of the accumulator tile: rows 8-15
+// (zero A rows here) start from zero and are discarded, so they hold no
+// registers across the loop.
+__device__ __forceinline__ void mma_16816_top(float (&d)[2], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  float j0, j1;
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%10,%11,%12,%12};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(j0), "=f"(j1)
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(d[0]), "f"(d[1]), "f"(0.0f));
+}
+
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int G>
-__global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const __grid_constant__ SdpaParams p) {
+template <int G, bool kBulk>
+__global__ void __launch_bounds__(kSdpaWarps * 32, 2) sdpa_int8_decode_kernel(const __grid_constant__ SdpaParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int split = blockIdx.x;
   const int bkv = blockIdx.y;
@@ -85,12 +100,12 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
 
   // ---- running state (row g of the MMA tiles; rows g+8 are unused padding)
   float m_run = -INFINITY, l_run = 0.f;
-  float acc[16][4];
-  float psum[4] = {0.f, 0.f, 0.f, 0.f};
+  float acc[16][2];  // rows g (the heads) of each 16 x 8 tile; rows g + 8 are padding
+  float psum[2] = {0.f, 0.f};
 #pragma unroll
   for (int j = 0; j < 16; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) acc[j][e] = 0.f;
+    for (int e = 0; e < 2; ++e) acc[j][e] = 0.f;
   constexpr uint32_t kOnes = 0x3C003C00u;
 
   // ---- per-warp ring of 16-token K/V blocks in shared memory (TMA boxes)
@@ -99,6 +114,8 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
   uint8_t* sbase = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(sbase) + warp * kSdpaStages;
   uint8_t* ring = sbase + 1024 + warp * kSdpaStages * kSdpaStageBytes;
+  // per-warp ring of the blocks' scales: [stage][k 16 x fp16 | v 16 x fp16]
+  uint8_t* sring = sbase + 1024 + kSdpaWarps * kSdpaStages * kSdpaStageBytes + warp * kSdpaStages * kSdpaScaleBytes;
   const int nb = blk_end - blk_begin;
   const int my_blocks = nb > warp ? (nb - warp + kSdpaWarps - 1) / kSdpaWarps : 0;
   auto block_of = [&](int i) { return blk_begin + warp + i * kSdpaWarps; };
@@ -106,9 +123,14 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
     const int slot = i % kSdpaStages;
     const int row = static_cast<int>(kv_base) + block_of(i) * 16;
     uint8_t* dst = ring + slot * kSdpaStageBytes;
-    mbar_arrive_expect_tx(bars + slot, kSdpaStageBytes);
+    mbar_arrive_expect_tx(bars + slot, kSdpaStageBytes + (kBulk ? kSdpaScaleBytes : 0));
     tma_load_2d(dst, &p.kmap, 0, row, bars + slot);
     tma_load_2d(dst + 16 * kSdpaD, &p.vmap, 0, row, bars + slot);
+    if constexpr (kBulk) {
+      uint8_t* sdst = sring + slot * kSdpaScaleBytes;
+      bulk_copy_g2s(sdst, p.ks + row, 32, bars + slot);
+      bulk_copy_g2s(sdst + 32, p.vs + row, 32, bars + slot);
+    }
   };
   const int last_blk = nblk - 1;  // holds token N-1, written by the previous kernel
   if (lane == 0) {
@@ -184,37 +206,56 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
       v4[j] = __half2float(vsb[tok]);
     }
   };
-  if (my_blocks > 0) load_scales(0, sk, sv);
+  if (my_blocks > 0 && !kBulk) load_scales(0, sk, sv);
   bool failed = false;
 
   for (int i = 0; i < my_blocks; ++i) {
     const int tb = block_of(i) * 16;
-    if (i + 1 < my_blocks) load_scales(i + 1, skn, svn);
+    if (!kBulk && i + 1 < my_blocks) load_scales(i + 1, skn, svn);
     const int slot = i % kSdpaStages;
     if (!mbar_wait_bounded(bars + slot, (i / kSdpaStages) & 1)) {
       failed = true;
       break;
+    }
+    if constexpr (kBulk) {
+      // this lane's tokens (2t, 2t+1) and (2t+8, 2t+9) of the block
+      const uint8_t* ssl = sring + slot * kSdpaScaleBytes;
+      const __half2 k01 = *reinterpret_cast<const __half2*>(ssl + 4 * t);
+      const __half2 k89 = *reinterpret_cast<const __half2*>(ssl + 16 + 4 * t);
+      const __half2 v01 = *reinterpret_cast<const __half2*>(ssl + 32 + 4 * t);
+      const __half2 v89 = *reinterpret_cast<const __half2*>(ssl + 48 + 4 * t);
+      sk[0] = __low2float(k01);
+      sk[1] = __high2float(k01);
+      sk[2] = __low2float(k89);
+      sk[3] = __high2float(k89);
+      sv[0] = __low2float(v01);
+      sv[1] = __high2float(v01);
+      sv[2] = __low2float(v89);
+      sv[3] = __high2float(v89);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (tb + (j < 2 ? 2 * t + j : 2 * t + 6 + j) >= N) sv[j] = 0.f;  // rows past the length: any bits
     }
     const uint8_t* kst = ring + slot * kSdpaStageBytes;
     const uint8_t* vst = kst + 16 * kSdpaD;
     const int vt[4] = {tb + 2 * t, tb + 2 * t + 1, tb + 2 * t + 8, tb + 2 * t + 9};
 
     // QK^T: C[u] rows = heads, cols = tokens 8u + (2t, 2t+1); K row (8u + g), bytes 32t..32t+31
-    float cqk[2][4];
+    float cqk[2][2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
       const uint4 ka = *reinterpret_cast<const uint4*>(swz128(kst, 8 * u + g, 32 * t));
       const uint4 kb = *reinterpret_cast<const uint4*>(swz128(kst, 8 * u + g, 32 * t + 16));
       const uint32_t kw[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
-      for (int e = 0; e < 4; ++e) cqk[u][e] = 0.f;
+      for (int e = 0; e < 2; ++e) cqk[u][e] = 0.f;
 #pragma unroll
       for (int s = 0; s < 8; ++s) {
         const uint32_t w = kw[s] ^ 0x80808080u;
         const uint32_t b0 = prmt(w, 0x64646464u, 0x4140u);
         const uint32_t b1 = prmt(w, 0x64646464u, 0x4342u);
         const uint32_t a[4] = {aq[s], 0u, aq2[s], 0u};
-        mma_16816<true>(cqk[u], a, b0, b1);
+        mma_16816_top(cqk[u], a, b0, b1);
       }
     }
     // scores (log2 domain) for tokens vt[0..3] = (u0: 2t, 2t+1), (u1: 2t+8, 2t+9)
@@ -236,19 +277,22 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
     for (int j = 0; j < 4; ++j) pr[j] = (vt[j] < N) ? exp2f(sc[j] - m_new) : 0.f;
     l_run = l_run * alpha + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
     m_run = m_new;
+    // rescale only when some row's running maximum moved (alpha == 1 exactly otherwise)
+    if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j)
+      for (int j = 0; j < 16; ++j)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[j][e] *= alpha;
+        for (int e = 0; e < 2; ++e) acc[j][e] *= alpha;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) psum[e] *= alpha;
+      for (int e = 0; e < 2; ++e) psum[e] *= alpha;
+    }
     // P' = p * v_scale as the fp16 A operand (rows = heads, k = tokens)
     uint32_t ap[4];
     ap[0] = head_ok ? pack_half2(pr[0] * sv[0], pr[1] * sv[1]) : 0u;
     ap[1] = 0u;
     ap[2] = head_ok ? pack_half2(pr[2] * sv[2], pr[3] * sv[3]) : 0u;
     ap[3] = 0u;
-    mma_16816<true>(psum, ap, kOnes, kOnes);
+    mma_16816_top(psum, ap, kOnes, kOnes);
     // P'V: n-tile j covers d = 16n + j; the lane's B column n = g reads bytes 16g..16g+15
     const uint4 vr0 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t, 16 * g));
     const uint4 vr1 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t + 1, 16 * g));
@@ -263,12 +307,14 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
       uint32_t b1 = prmt(vc[j >> 2], vd[j >> 2], sel);
       b0 = (b0 & 0x00FF00FFu) ^ 0x64806480u;
       b1 = (b1 & 0x00FF00FFu) ^ 0x64806480u;
-      mma_16816<true>(acc[j], ap, b0, b1);
+      mma_16816_top(acc[j], ap, b0, b1);
     }
+    if constexpr (!kBulk) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      sk[j] = skn[j];
-      sv[j] = svn[j];
+      for (int j = 0; j < 4; ++j) {
+        sk[j] = skn[j];
+        sv[j] = svn[j];
+      }
     }
     __syncwarp();
     if (i + kSdpaStages < my_blocks && lane == 0) {
@@ -288,12 +334,17 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
   l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
   __shared__ float s_m[kSdpaWarps][8], s_l[kSdpaWarps][8];
-  __shared__ float s_o[kSdpaWarps][8][kSdpaD];
+  // the warp's partial O [8][D] goes to its own (drained) ring: warp w at ring_of(w)
+  auto o_of = [&](int w) {
+    return reinterpret_cast<float*>(sbase + 1024 + w * kSdpaStages * kSdpaStageBytes);
+  };
+  __syncwarp();
   if (head_ok) {
+    float* ow = o_of(warp) + g * kSdpaD;
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      s_o[warp][g][32 * t + j] = acc[j][0] - 1152.0f * psum[0];
-      s_o[warp][g][32 * t + 16 + j] = acc[j][1] - 1152.0f * psum[1];
+      ow[32 * t + j] = acc[j][0] - 1152.0f * psum[0];
+      ow[32 * t + 16 + j] = acc[j][1] - 1152.0f * psum[1];
     }
     if (t == 0) {
       s_m[warp][g] = m_run;
@@ -321,7 +372,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
         for (int w = 0; w < kSdpaWarps; ++w) {
           const float f = s_m[w][hh] == -INFINITY ? 0.f : exp2f(s_m[w][hh] - mm);
           ll += s_l[w][hh] * f;
-          oo += s_o[w][hh][d] * f;
+          oo += o_of(w)[hh * kSdpaD + d] * f;
         }
       }
       const int r = d / SL;
@@ -369,7 +420,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32) sdpa_int8_decode_kernel(const
       for (int w = 0; w < kSdpaWarps; ++w) {
         const float f = s_m[w][hh] == -INFINITY ? 0.f : exp2f(s_m[w][hh] - mm);
         ll += s_l[w][hh] * f;
-        oo += s_o[w][hh][d] * f;
+        oo += o_of(w)[hh * kSdpaD + d] * f;
       }
     }
     if (single) {
@@ -445,12 +496,18 @@ int sdpa_sms() {
   return count;
 }
 
+// Token splits per (batch, kv head): one wave of CTAs (two per SM), at most 16
+// (one thread-block cluster, merged in distributed shared memory) when that
+// still puts a CTA on most SMs, at least two blocks per warp.
 int sdpa_splits(int64_t batch, int kv_heads, int64_t length) {
   const int64_t bkv = batch * kv_heads;
   const int64_t nblk = (length + 15) / 16;
-  int64_t s = (sdpa_sms() * 4 + bkv - 1) / bkv;
+  const int64_t slots = static_cast<int64_t>(sdpa_sms()) * 2;
+  int64_t s = (slots + bkv - 1) / bkv;
+  if (s > kSdpaMaxClusterSplits && bkv * kSdpaMaxClusterSplits * 5 >= static_cast<int64_t>(sdpa_sms()) * 4)
+    s = kSdpaMaxClusterSplits;
   s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (2 * kSdpaWarps)));  // >= 2 blocks per warp
-  s = std::min<int64_t>(s, 64);
+  s = std::min<int64_t>(s, kMaxSplits);
   return static_cast<int>(std::max<int64_t>(1, s));
 }
 
@@ -507,6 +564,7 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
     if (int st = make_tmap_rows(&p.vmap, v, rows, kSdpaD, 16)) return st;
   }
   p.length_offset = length_offset;
+  p.scale_bulk = (capacity % 16 == 0 && ((reinterpret_cast<uintptr_t>(k_scale) | reinterpret_cast<uintptr_t>(v_scale)) & 15) == 0) ? 1 : 0;
   p.scale_log2e = scale * 1.4426950408889634f;
   if (splits > 1) {
     p.counters = static_cast<unsigned*>(workspace);
@@ -535,10 +593,10 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
     return launch("int8 sdpa", kernel, grid, block, kSdpaSmem, stream, p);
   };
   switch (G) {
-    case 1: return go(sdpa_int8_decode_kernel<1>);
-    case 2: return go(sdpa_int8_decode_kernel<2>);
-    case 4: return go(sdpa_int8_decode_kernel<4>);
-    default: return go(sdpa_int8_decode_kernel<8>);
+    case 1: return p.scale_bulk ? go(sdpa_int8_decode_kernel<1, true>) : go(sdpa_int8_decode_kernel<1, false>);
+    case 2: return p.scale_bulk ? go(sdpa_int8_decode_kernel<2, true>) : go(sdpa_int8_decode_kernel<2, false>);
+    case 4: return p.scale_bulk ? go(sdpa_int8_decode_kernel<4, true>) : go(sdpa_int8_decode_kernel<4, false>);
+    default: return p.scale_bulk ? go(sdpa_int8_decode_kernel<8, true>) : go(sdpa_int8_decode_kernel<8, false>);
   }
 }
 

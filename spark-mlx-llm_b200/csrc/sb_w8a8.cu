@@ -16,6 +16,7 @@
 #include <mutex>
 
 #include "sb_common.cuh"
+#include "sb_tcgemm.cuh"
 
 namespace sb {
 
@@ -345,9 +346,11 @@ extern "C" int sb_quantize_per_token(const void* x, int x_dtype, int8_t* q, floa
 
 extern "C" size_t sb_w8a8_linear_workspace_size(int64_t M, int64_t N, int64_t K) {
   if (M <= 0 || N <= 0 || K <= 0 || K % 64) return 0;
-  (void)M;
   const I8Plan pl = plan_i8(static_cast<int>(N), static_cast<int>(K), true);
-  return pl.counter_bytes + pl.partial_bytes;
+  size_t need = pl.counter_bytes + pl.partial_bytes;
+  // M > 8: per-token INT8 activations and their scales for the tensor-core kernel
+  if (M > 8) need = std::max(need, tc_w8a8_bytes(M, K));
+  return need;
 }
 
 extern "C" int sb_int8_matmul_int32(const int8_t* x, const int8_t* w, int32_t* out, int64_t M, int64_t N,
@@ -356,6 +359,19 @@ extern "C" int sb_int8_matmul_int32(const int8_t* x, const int8_t* w, int32_t* o
   SB_REQUIRE(K % 64 == 0, "this build requires K to be a multiple of 64");
   SB_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0,
              "x and weight must be 16-byte aligned");
+  if (M > 8) {  // tensor-core (tcgen05 kind::i8) kernel, exact int32 accumulators
+    TcRequest t;
+    t.tw = TW_S8;
+    t.te = TE_I32;
+    t.x = x;
+    t.M = static_cast<int>(M);
+    t.N = static_cast<int>(N);
+    t.K = static_cast<int>(K);
+    t.w = w;
+    t.y = out;
+    t.ldy = static_cast<int>(N);
+    if (tc_linear_supported(t)) return run_tc_linear(t, as_stream(stream));
+  }
   I8Plan pl = plan_i8(static_cast<int>(N), static_cast<int>(K), false);
   for (int64_t m0 = 0; m0 < M; m0 += 8) {
     I8Params p{};
@@ -383,6 +399,31 @@ extern "C" int sb_w8a8_linear(const void* x, int x_dtype, const int8_t* w, const
                  bias_dtype == SB_DTYPE_F32,
              "bias must have a real floating dtype.");
   SB_REQUIRE((reinterpret_cast<uintptr_t>(w) & 15) == 0, "weight must be 16-byte aligned");
+  if (M > 8 && workspace != nullptr && workspace_bytes >= tc_w8a8_bytes(M, K)) {
+    // per-token quantization into the workspace (past its counter region), then
+    // the tensor-core kernel with the W8A8 epilogue
+    int8_t* xq = static_cast<int8_t*>(workspace) + kCounterBytes;
+    float* sa = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes + ((M * K + 255) / 256) * 256);
+    TcRequest t;
+    t.tw = TW_S8;
+    t.te = TE_W8A8;
+    t.x = xq;
+    t.M = static_cast<int>(M);
+    t.N = static_cast<int>(N);
+    t.K = static_cast<int>(K);
+    t.w = w;
+    t.y = y;
+    t.ldy = static_cast<int>(N);
+    t.y_dtype = x_dtype;
+    t.wscale = scales;
+    t.ascale = sa;
+    t.bias = bias;
+    t.bias_dtype = bias ? bias_dtype : -1;
+    if (tc_linear_supported(t)) {
+      if (int st = sb_quantize_per_token(x, x_dtype, xq, sa, M, K, stream)) return st;
+      return run_tc_linear(t, as_stream(stream));
+    }
+  }
   I8Plan pl = plan_i8(static_cast<int>(N), static_cast<int>(K), true);
   if (pl.splits > 1 && (workspace == nullptr || workspace_bytes < pl.counter_bytes + pl.partial_bytes))
     pl = plan_i8(static_cast<int>(N), static_cast<int>(K), false);

@@ -44,7 +44,7 @@ def make_affine(rng, n, k, group, bits):
         (1, 2560, 6144, 64, 8),
         (5, 1024, 96, 32, 8),
         (7, 512, 64, 128, 8),
-        (16, 1024, 256, 64, 4),  # M > 8: the host splits into row blocks
+        (16, 1024, 256, 64, 4),  # M > 8: tensor-core kernel
     ],
 )
 def test_affine_linear_matches_oracle(sb, m, k, n, group, bits):
@@ -57,9 +57,12 @@ def test_affine_linear_matches_oracle(sb, m, k, n, group, bits):
     torch.cuda.synchronize()
     assert y.dtype == torch.bfloat16 and tuple(y.shape) == (m, n)
     assert_close(to_f32(y), expected, what="affine_linear")
-    # almost every output equals the correctly rounded bf16 value
-    exact = np.mean(to_f32(y) == formats.round_bf16(expected.astype(np.float32)))
-    assert exact > 0.97, exact
+    if m <= 8:
+        # the weight-streaming kernel multiplies the exact codes: almost every
+        # output equals the correctly rounded bf16 value (M > 8 runs the
+        # tensor-core kernel, which rounds the dequantized weights to bf16)
+        exact = np.mean(to_f32(y) == formats.round_bf16(expected.astype(np.float32)))
+        assert exact > 0.97, exact
 
 
 def test_affine_linear_fp16_activations(sb):
