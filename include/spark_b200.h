@@ -63,7 +63,11 @@ int sb_device_supported(int device);
  *   w        : [N, K*bits/32] uint32 words, code j of a word at bits [j*bits, j*bits+bits)
  *   scales, biases : [N, K/G] of x_dtype
  *   y        : [M, N] of x_dtype
- *   bits 4 or 8; group_size 32, 64 or 128; 1 <= M <= 8.
+ *   bits 4 or 8; group_size 32, 64 or 128; M >= 1. M <= 8 runs the
+ *   weight-streaming kernel (exact products of the codes); M > 8 runs the
+ *   tensor-core kernel (tcgen05, dequantized weight tiles rounded to x_dtype,
+ *   as MLX's multi-row path does) when K/group_size is a multiple of 8 and
+ *   x, w, scales and biases are 16-byte aligned, else blocks of 8 rows.
  */
 int sb_affine_linear(const void* x, int x_dtype, const uint32_t* w, const void* scales,
                      const void* biases, void* y, int64_t M, int64_t N, int64_t K,
@@ -76,7 +80,8 @@ size_t sb_affine_linear_workspace_size(int64_t M, int64_t N, int64_t K, int grou
  * Per-channel int8 weight linear, y = x(dtype) . ((sum_k x*w) * scales[n]).
  * Replaces w8a16_per_channel (extensions/spark-mlx-ext/src/spark_w8a16.cpp:80-110,
  * bindings.cpp:13-30) and w8a16_multirow (spark_mlx_ext/w8a16_multirow.py:44-129).
- *   x [M,K] BF16/F16, w [N,K] int8, scales [N] fp32, y [M,N] of x_dtype; 1 <= M <= 8.
+ *   x [M,K] BF16/F16, w [N,K] int8, scales [N] fp32, y [M,N] of x_dtype; M >= 1
+ *   (M > 8: tensor-core kernel, int8 converted exactly to x_dtype).
  */
 int sb_w8a16_per_channel(const void* x, int x_dtype, const int8_t* w, const float* scales,
                          void* y, int64_t M, int64_t N, int64_t K, void* workspace,
@@ -95,7 +100,8 @@ int sb_quantize_per_token(const void* x, int x_dtype, int8_t* q, float* scales, 
 /*
  * Exact int8 GEMM with int32 accumulation, out[M,N] = x[M,K] @ w[N,K]^T.
  * Replaces int8_matmul_int32 (extensions/spark-mlx-ext/src/spark_w8a8.cpp:218-228).
- *   K a multiple of 32 and <= 131040 (no int32 overflow).
+ *   K a multiple of 32 and <= 131040 (no int32 overflow). M > 8 runs the
+ *   tcgen05 kind::i8 kernel (int32 accumulators in TMEM, exact).
  */
 int sb_int8_matmul_int32(const int8_t* x, const int8_t* w, int32_t* out, int64_t M, int64_t N,
                          int64_t K, void* stream);
@@ -107,6 +113,8 @@ int sb_int8_matmul_int32(const int8_t* x, const int8_t* w, int32_t* out, int64_t
  * spark_mlx_ext/linear.py:9-55).
  *   x [M,K] BF16/F16/F32 (y has the same dtype), w [N,K] int8, scales [N] fp32,
  *   bias [N] of bias_dtype or NULL. K a multiple of 32 and <= 131040.
+ *   M > 8 (with a workspace of sb_w8a8_linear_workspace_size bytes): per-token
+ *   quantization into the workspace, then the tcgen05 kind::i8 kernel.
  */
 int sb_w8a8_linear(const void* x, int x_dtype, const int8_t* w, const float* scales,
                    const void* bias, int bias_dtype, void* y, int64_t M, int64_t N, int64_t K,
@@ -122,7 +130,8 @@ size_t sb_w8a8_linear_workspace_size(int64_t M, int64_t N, int64_t K);
  *   N = (num_heads + 2*num_kv_heads) * head_dim rows; positions [B*L] int32
  *   (absolute token positions; the reference's scalar `offset` is positions = offset + l).
  *   q_out [B, num_heads, L, head_dim], k_out/v_out [B, num_kv_heads, L, head_dim].
- *   B*L <= 8 per call.
+ *   B*L <= 8: weight-streaming kernel; B*L > 8: tensor-core kernel (head_dim
+ *   128, hidden/group_size a multiple of 8, 16-byte aligned tensors).
  */
 int sb_qkv_rope(const void* x, int x_dtype, const uint32_t* w, const void* scales,
                 const void* biases, const int32_t* positions, void* q_out, void* k_out,

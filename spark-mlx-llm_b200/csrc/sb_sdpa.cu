@@ -31,14 +31,20 @@
 
 namespace sb {
 
-constexpr int kSdpaWarps = 8;
+// Warps per CTA. The kernel is written for 8 (two CTAs per SM) or 16 (one CTA
+// per SM); on B200 the 8-warp form measured faster at every batch size of the
+// 32K-token case (16 warps: fewer CTAs and one 200 KB ring per SM), so the
+// launch plan uses 8.
+constexpr int kSdpaWarpsUsed = 8;
 constexpr int kSdpaD = 128;
 constexpr int kPartStride = kSdpaD + 4;  // O[D], then m, l
 constexpr int kSdpaStages = 3;           // 16-token blocks in flight per warp
 constexpr int kMaxSplits = 64;           // token splits per (batch, kv head)
 constexpr int kSdpaStageBytes = 2 * 16 * kSdpaD;  // swizzled K box + V box
 constexpr int kSdpaScaleBytes = 64;                 // the block's 16 K scales + 16 V scales (fp16)
-constexpr size_t kSdpaSmem = 2048 + static_cast<size_t>(kSdpaWarps) * kSdpaStages * (kSdpaStageBytes + kSdpaScaleBytes);
+constexpr size_t sdpa_smem(int warps) {
+  return 2048 + static_cast<size_t>(warps) * kSdpaStages * (kSdpaStageBytes + kSdpaScaleBytes);
+}
 
 struct SdpaParams {
   alignas(64) CUtensorMap kmap;  // K cache as [B*KH*cap rows][128 B], 16-row boxes, 128-B swizzle
@@ -81,8 +87,8 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int G, bool kBulk>
-__global__ void __launch_bounds__(kSdpaWarps * 32, 2) sdpa_int8_decode_kernel(const __grid_constant__ SdpaParams p) {
+template <int G, bool kBulk, int kSdpaWarps>
+__global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_decode_kernel(const __grid_constant__ SdpaParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int split = blockIdx.x;
   const int bkv = blockIdx.y;
@@ -119,8 +125,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 2) sdpa_int8_decode_kernel(co
   const int nb = blk_end - blk_begin;
   const int my_blocks = nb > warp ? (nb - warp + kSdpaWarps - 1) / kSdpaWarps : 0;
   auto block_of = [&](int i) { return blk_begin + warp + i * kSdpaWarps; };
-  auto issue = [&](int i) {
-    const int slot = i % kSdpaStages;
+  auto issue = [&](int i, int slot) {
     const int row = static_cast<int>(kv_base) + block_of(i) * 16;
     uint8_t* dst = ring + slot * kSdpaStageBytes;
     mbar_arrive_expect_tx(bars + slot, kSdpaStageBytes + (kBulk ? kSdpaScaleBytes : 0));
@@ -137,14 +142,14 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 2) sdpa_int8_decode_kernel(co
     for (int i = 0; i < kSdpaStages; ++i) mbar_init(bars + i, 1);
     mbar_fence_init();
     for (int i = 0; i < kSdpaStages && i < my_blocks; ++i)
-      if (!p.early || block_of(i) != last_blk) issue(i);
+      if (!p.early || block_of(i) != last_blk) issue(i, i);
   }
   __syncwarp();
   if (p.early) {
     grid_dependency_wait();
     if (lane == 0)
       for (int i = 0; i < kSdpaStages && i < my_blocks; ++i)
-        if (block_of(i) == last_blk) issue(i);
+        if (block_of(i) == last_blk) issue(i, i);
     __syncwarp();
   }
 
@@ -209,11 +214,12 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 2) sdpa_int8_decode_kernel(co
   if (my_blocks > 0 && !kBulk) load_scales(0, sk, sv);
   bool failed = false;
 
+  int slot = 0;
+  uint32_t phase = 0u;
   for (int i = 0; i < my_blocks; ++i) {
     const int tb = block_of(i) * 16;
     if (!kBulk && i + 1 < my_blocks) load_scales(i + 1, skn, svn);
-    const int slot = i % kSdpaStages;
-    if (!mbar_wait_bounded(bars + slot, (i / kSdpaStages) & 1)) {
+    if (!mbar_wait_bounded(bars + slot, phase)) {
       failed = true;
       break;
     }
@@ -319,7 +325,11 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 2) sdpa_int8_decode_kernel(co
     __syncwarp();
     if (i + kSdpaStages < my_blocks && lane == 0) {
       fence_proxy_async_smem();
-      issue(i + kSdpaStages);
+      issue(i + kSdpaStages, slot);
+    }
+    if (++slot == kSdpaStages) {
+      slot = 0;
+      phase ^= 1u;
     }
   }
   if (failed) {
@@ -496,19 +506,32 @@ int sdpa_sms() {
   return count;
 }
 
-// Token splits per (batch, kv head): one wave of CTAs (two per SM), at most 16
-// (one thread-block cluster, merged in distributed shared memory) when that
-// still puts a CTA on most SMs, at least two blocks per warp.
-int sdpa_splits(int64_t batch, int kv_heads, int64_t length) {
+// Launch plan: warps per CTA (16 allowed for long contexts when max_warps is
+// 16, one CTA per SM; else 8, two CTAs per SM) and token splits per (batch,
+// kv head): one wave of CTAs, raised to 16 splits (one thread-block cluster,
+// merged in distributed shared memory) when that still puts a CTA on most SMs,
+// at least two 16-token blocks per warp. (Measured on B200 at 32K tokens:
+// minimising waves per unit of work instead picked 9-15 splits for batch 8-32
+// and lost 0-45% to cluster placement and merge cost.)
+struct SdpaPlan {
+  int warps, splits;
+};
+SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int max_warps) {
   const int64_t bkv = batch * kv_heads;
   const int64_t nblk = (length + 15) / 16;
-  const int64_t slots = static_cast<int64_t>(sdpa_sms()) * 2;
+  SdpaPlan pl{nblk >= 512 && max_warps >= 16 ? 16 : 8, 1};
+  const int64_t sms = sdpa_sms();
+  const int64_t slots = sms * (16 / pl.warps);
   int64_t s = (slots + bkv - 1) / bkv;
-  if (s > kSdpaMaxClusterSplits && bkv * kSdpaMaxClusterSplits * 5 >= static_cast<int64_t>(sdpa_sms()) * 4)
-    s = kSdpaMaxClusterSplits;
-  s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (2 * kSdpaWarps)));  // >= 2 blocks per warp
+  if (s > kSdpaMaxClusterSplits && bkv * kSdpaMaxClusterSplits * 5 >= sms * 4) s = kSdpaMaxClusterSplits;
+  s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (2 * pl.warps)));
   s = std::min<int64_t>(s, kMaxSplits);
-  return static_cast<int>(std::max<int64_t>(1, s));
+  pl.splits = static_cast<int>(std::max<int64_t>(1, s));
+  return pl;
+}
+// splits of the plan the launch uses (workspace sizing)
+int sdpa_splits(int64_t batch, int kv_heads, int64_t length) {
+  return sdpa_plan(batch, kv_heads, length, kSdpaWarpsUsed).splits;
 }
 
 }  // namespace
@@ -535,7 +558,10 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   SB_REQUIRE(((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v)) &
               15) == 0,
              "q, k and v must be 16-byte aligned");
-  int splits = force_splits > 0 ? force_splits : sdpa_splits(batch, num_kv_heads, length);
+  const bool bulk = capacity % 16 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(k_scale) | reinterpret_cast<uintptr_t>(v_scale)) & 15) == 0;
+  const SdpaPlan plan = sdpa_plan(batch, num_kv_heads, length, kSdpaWarpsUsed);
+  int splits = force_splits > 0 ? force_splits : plan.splits;
   SB_REQUIRE(splits <= kMaxSplits, "at most 64 token splits");
   const int64_t bkv = batch * num_kv_heads;
   const size_t counters = kCounterBytes;
@@ -564,7 +590,7 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
     if (int st = make_tmap_rows(&p.vmap, v, rows, kSdpaD, 16)) return st;
   }
   p.length_offset = length_offset;
-  p.scale_bulk = (capacity % 16 == 0 && ((reinterpret_cast<uintptr_t>(k_scale) | reinterpret_cast<uintptr_t>(v_scale)) & 15) == 0) ? 1 : 0;
+  p.scale_bulk = bulk ? 1 : 0;
   p.scale_log2e = scale * 1.4426950408889634f;
   if (splits > 1) {
     p.counters = static_cast<unsigned*>(workspace);
@@ -574,9 +600,10 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
     p.status = static_cast<unsigned*>(workspace) + kStatusWord;
   p.early = early ? 1 : 0;
   const dim3 grid(splits, static_cast<unsigned>(bkv));
-  const dim3 block(kSdpaWarps * 32);
+  const dim3 block(plan.warps * 32);
+  const size_t smem = sdpa_smem(plan.warps);
   auto go = [&](auto kernel) -> int {
-    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSdpaSmem)) !=
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
       return fail(SB_ECUDA, "int8 sdpa: shared memory opt-in failed");
     // splits of one (batch, kv head) merge inside a thread-block cluster when it can hold them
@@ -589,14 +616,17 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
       }
       p.cluster = ok ? 1 : 0;
     }
-    if (p.cluster) return launch_cluster("int8 sdpa", kernel, grid, block, kSdpaSmem, splits, stream, p);
-    return launch("int8 sdpa", kernel, grid, block, kSdpaSmem, stream, p);
+    if (p.cluster) return launch_cluster("int8 sdpa", kernel, grid, block, smem, splits, stream, p);
+    return launch("int8 sdpa", kernel, grid, block, smem, stream, p);
   };
   switch (G) {
-    case 1: return p.scale_bulk ? go(sdpa_int8_decode_kernel<1, true>) : go(sdpa_int8_decode_kernel<1, false>);
-    case 2: return p.scale_bulk ? go(sdpa_int8_decode_kernel<2, true>) : go(sdpa_int8_decode_kernel<2, false>);
-    case 4: return p.scale_bulk ? go(sdpa_int8_decode_kernel<4, true>) : go(sdpa_int8_decode_kernel<4, false>);
-    default: return p.scale_bulk ? go(sdpa_int8_decode_kernel<8, true>) : go(sdpa_int8_decode_kernel<8, false>);
+#define SB_SDPA_GO(GG) \
+  return bulk ? go(sdpa_int8_decode_kernel<GG, true, 8>) : go(sdpa_int8_decode_kernel<GG, false, 8>);
+    case 1: SB_SDPA_GO(1)
+    case 2: SB_SDPA_GO(2)
+    case 4: SB_SDPA_GO(4)
+    default: SB_SDPA_GO(8)
+#undef SB_SDPA_GO
   }
 }
 

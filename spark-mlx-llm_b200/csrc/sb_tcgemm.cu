@@ -34,12 +34,14 @@ namespace sb {
 namespace {
 
 constexpr int kBM = 128;          // weight rows per tile
-constexpr int kConvWarps = 8;     // conversion + epilogue warps
-constexpr int kProducerWarp = 8;
+constexpr int kConvWarps = 8;      // conversion + epilogue warps
+constexpr int kWProducerWarp = 8;  // weight stages + scale chunks
 constexpr int kMmaWarp = 9;
-constexpr int kTcThreads = 320;
+constexpr int kXProducerWarp = 10;  // activation stages
+constexpr int kTcThreads = 352;
 constexpr int kATile = kBM * 128;  // one 128-byte-swizzled A operand tile (bytes)
 constexpr int kMaxSplit = 8;
+constexpr size_t kTcSmemMax = 202u << 10;  // above every plan (one-CTA plans are built within 200 KB)
 
 struct TcParams {
   alignas(64) CUtensorMap wmap;  // weight rows [N][row bytes]: box {wraw bytes, 128} (TW_S8: SW128 {128, 128})
@@ -47,7 +49,7 @@ struct TcParams {
   alignas(64) CUtensorMap bmap;  // biases, same
   alignas(64) CUtensorMap xmap;  // activations [M][K], SW128 box {128 bytes, BN}
   int M, N, K, G;
-  int bn, stages, ksteps;
+  int bn, na, nx, nw, ksteps;
   void* y;
   int ldy, y_dtype;
   const float* wscale;
@@ -151,6 +153,37 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&h);
   }
 }
+// Eight 4-bit codes (one uint32 word, code e at bits 4e) -> eight 16-bit
+// values scale * q + bias, each rounded once (fused multiply-add in the
+// operand type), in K order. The codes become exact 16-bit numbers by OR-ing
+// them into the mantissa of 128 (bf16) or 1024 (fp16) and subtracting it.
+// s2 / b2 hold the scale / bias bits in both halves.
+template <bool kHalf>
+__device__ __forceinline__ uint4 dequant8_w4(uint32_t w, uint32_t s2, uint32_t b2) {
+  constexpr uint32_t kMagic = kHalf ? 0x64006400u : 0x43004300u;
+  uint32_t t[4];
+  t[0] = lop_and_or(w, 0x000F000Fu, kMagic);        // (q0, q4)
+  t[1] = lop_and_or(w >> 4, 0x000F000Fu, kMagic);   // (q1, q5)
+  t[2] = lop_and_or(w >> 8, 0x000F000Fu, kMagic);   // (q2, q6)
+  t[3] = lop_and_or(w >> 12, 0x000F000Fu, kMagic);  // (q3, q7)
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if constexpr (kHalf) {
+      const __half2 q = __hsub2(*reinterpret_cast<const __half2*>(&t[i]), *reinterpret_cast<const __half2*>(&kMagic));
+      const __half2 r = __hfma2(q, *reinterpret_cast<const __half2*>(&s2), *reinterpret_cast<const __half2*>(&b2));
+      t[i] = *reinterpret_cast<const uint32_t*>(&r);
+    } else {
+      const __nv_bfloat162 q =
+          __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&t[i]), *reinterpret_cast<const __nv_bfloat162*>(&kMagic));
+      const __nv_bfloat162 r = __hfma2(q, *reinterpret_cast<const __nv_bfloat162*>(&s2),
+                                       *reinterpret_cast<const __nv_bfloat162*>(&b2));
+      t[i] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+  }
+  return make_uint4(prmt(t[0], t[1], 0x5410u), prmt(t[2], t[3], 0x5410u), prmt(t[0], t[1], 0x7632u),
+                    prmt(t[2], t[3], 0x7632u));
+}
+
 // exact float of an unsigned integer below 2^23
 __device__ __forceinline__ float u2f(uint32_t c) { return __uint_as_float(0x4B000000u | c) - 8388608.0f; }
 
@@ -176,39 +209,57 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
   constexpr bool kS8 = TW == TW_S8;
   constexpr bool kAffine = TW == TW_AFF4 || TW == TW_AFF8;
   constexpr int kWRaw = wraw_bytes<TW>();
-  constexpr int kRawTile = kS8 ? 0 : kBM * kWRaw;  // separate raw stage (converted kinds)
-  constexpr int kScTile = kAffine ? 2 * kBM * 16 : 0;
+  constexpr int kRawTile = kS8 ? 0 : kBM * kWRaw;  // streamed weight stage (converted kinds)
+  constexpr int kScTile = 2 * kBM * 16;             // scales + biases of 8 groups x 128 rows
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = gridDim.x, rank = blockIdx.x;
   const int n0 = blockIdx.y * kBM, m0 = blockIdx.z * p.bn;
   const int ks0 = static_cast<int>(static_cast<long long>(p.ksteps) * rank / S);
   const int ks1 = static_cast<int>(static_cast<long long>(p.ksteps) * (rank + 1) / S);
   const int nk = ks1 - ks0;
-  const int BN = p.bn, NS = p.stages;
+  const int BN = p.bn, NA = p.na, NX = p.nx, NW = p.nw;
 
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* base = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
-  uint8_t* a_ring = base;                                   // NS x 16 KB (SW128 A operand)
-  uint8_t* b_ring = a_ring + NS * kATile;                   // NS x BN * 128 (SW128 activations)
-  uint8_t* w_ring = b_ring + NS * BN * 128;                 // NS x raw weight stage
-  uint8_t* sc_ring = w_ring + NS * kRawTile;                // NS x (scales, biases) [2][128][8] u16
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sc_ring + NS * kScTile);
-  uint64_t* full = bars;
-  uint64_t* conv = bars + NS;
-  uint64_t* empty = bars + 2 * NS;
-  uint64_t* done = bars + 3 * NS;
-  uint32_t* red = reinterpret_cast<uint32_t*>(a_ring);     // epilogue: [128][BN + 1] 32-bit
+  uint8_t* a_ring = base;                     // NA x 16 KB: SW128 A operand (TW_S8: loaded by TMA, NA = NX)
+  uint8_t* x_ring = a_ring + NA * kATile;     // NX x BN * 128: SW128 activations
+  uint8_t* w_ring = x_ring + NX * BN * 128;   // NW x streamed weight stage
+  uint8_t* sc_ring = w_ring + NW * kRawTile;  // 2 x scale/bias chunk [2][128][8] u16 (affine)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sc_ring + (kAffine ? 2 * kScTile : 0));
+  uint64_t* xfull = bars;           // activation (+ TW_S8 weight) stage landed
+  uint64_t* xempty = xfull + NX;    // MMAs of the stage done
+  uint64_t* afull = xempty + NX;    // A slot converted (8 warps)
+  uint64_t* aempty = afull + NA;    // MMAs reading the A slot done
+  uint64_t* wfull = aempty + NA;    // weight stage landed
+  uint64_t* wempty = wfull + NW;    // weight stage converted (8 warps)
+  uint64_t* scfull = wempty + NW;   // scale chunk landed
+  uint64_t* scempty = scfull + 2;   // scale chunk used up (8 warps)
+  uint64_t* done = scempty + 2;     // every MMA done
+  uint32_t* red = reinterpret_cast<uint32_t*>(a_ring);  // epilogue: [128][BN + 1] 32-bit over the drained rings
   const int rs = BN + 1;
   __shared__ uint32_t s_tmem;
   __shared__ int s_abort;
   volatile int* abort_flag = &s_abort;
   const uint32_t tmem_cols = BN <= 32 ? 32u : (BN <= 64 ? 64u : (BN <= 128 ? 128u : 256u));
+  // scale chunk (8 groups) of K stage ks (64 K values per stage)
+  auto chunk_of = [&](int ks) { return ((ks * 64) / p.G) >> 3; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(full + s, 1);
-      mbar_init(conv + s, kConvWarps);
-      mbar_init(empty + s, 1);
+    for (int s = 0; s < NX; ++s) {
+      mbar_init(xfull + s, 1);
+      mbar_init(xempty + s, 1);
+    }
+    for (int s = 0; s < NA; ++s) {
+      mbar_init(afull + s, kConvWarps);
+      mbar_init(aempty + s, 1);
+    }
+    for (int s = 0; s < NW; ++s) {
+      mbar_init(wfull + s, 1);
+      mbar_init(wempty + s, kConvWarps);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(scfull + s, 1);
+      mbar_init(scempty + s, kConvWarps);
     }
     mbar_init(done, 1);
     mbar_fence_init();
@@ -227,105 +278,143 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
   // activations (and positions) may come from the previous kernel in the stream
   grid_dependency_wait();
 
-  if (warp == kProducerWarp) {
-    if (lane == 0) {
-      const uint32_t bytes = static_cast<uint32_t>((kS8 ? kATile : kRawTile) + kScTile + BN * 128);
-      int issued = 0;
+  if (warp == kWProducerWarp) {
+    // ---- weight stages (and scale chunks) into their rings, as far ahead as the rings allow
+    if (lane == 0 && !kS8) {
+      int issued = 0, chunks = 0, cur = -1;
       for (int i = 0; i < nk; ++i) {
-        const int s = i % NS, u = i / NS;
-        if (u > 0 && !tc_wait(empty + s, (u - 1) & 1, abort_flag, p.status)) break;
         const int ks = ks0 + i;
-        mbar_arrive_expect_tx(full + s, bytes);
-        if constexpr (kS8) {
-          tma_load_2d(a_ring + s * kATile, &p.wmap, ks * 128, n0, full + s);
-        } else {
-          tma_load_2d(w_ring + s * kRawTile, &p.wmap, ks * kWRaw, n0, full + s);
-        }
         if constexpr (kAffine) {
-          const int g0 = ((ks * 64) / p.G) & ~7;
-          uint8_t* sc = sc_ring + s * kScTile;
-          tma_load_2d(sc, &p.smap, g0, n0, full + s);
-          tma_load_2d(sc + kBM * 16, &p.bmap, g0, n0, full + s);
+          const int ch = chunk_of(ks);
+          if (ch != cur) {
+            cur = ch;
+            const int cs = chunks & 1, cu = chunks >> 1;
+            if (cu > 0 && !tc_wait(scempty + cs, (cu - 1) & 1, abort_flag, p.status)) break;
+            mbar_arrive_expect_tx(scfull + cs, kScTile);
+            tma_load_2d(sc_ring + cs * kScTile, &p.smap, ch * 8, n0, scfull + cs);
+            tma_load_2d(sc_ring + cs * kScTile + kBM * 16, &p.bmap, ch * 8, n0, scfull + cs);
+            ++chunks;
+          }
         }
-        tma_load_2d(b_ring + s * BN * 128, &p.xmap, kS8 ? ks * 128 : ks * 64, m0, full + s);
+        const int s = i % NW, u = i / NW;
+        if (u > 0 && !tc_wait(wempty + s, (u - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(wfull + s, kRawTile);
+        tma_load_2d(w_ring + s * kRawTile, &p.wmap, ks * kWRaw, n0, wfull + s);
         ++issued;
       }
       // copies still in flight (only after an abort) land before the memory is reused
-      for (int s = 0; s < NS && s < issued; ++s) {
-        const int uses = (issued - 1 - s) / NS + 1;
-        mbar_wait_bounded(full + s, (uses - 1) & 1);
+      for (int s = 0; s < NW && s < issued; ++s) mbar_wait_bounded(wfull + s, ((issued - 1 - s) / NW) & 1);
+      for (int c = 0; c < 2 && c < chunks; ++c) mbar_wait_bounded(scfull + c, ((chunks - 1 - c) / 2) & 1);
+    }
+  } else if (warp == kXProducerWarp) {
+    // ---- activation stages (TW_S8: with the int8 weight tile)
+    if (lane == 0) {
+      const uint32_t bytes = static_cast<uint32_t>(BN * 128 + (kS8 ? kATile : 0));
+      int issued = 0;
+      for (int i = 0; i < nk; ++i) {
+        const int ks = ks0 + i;
+        const int s = i % NX, u = i / NX;
+        if (u > 0 && !tc_wait(xempty + s, (u - 1) & 1, abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(xfull + s, bytes);
+        if constexpr (kS8) tma_load_2d(a_ring + s * kATile, &p.wmap, ks * 128, n0, xfull + s);
+        tma_load_2d(x_ring + s * BN * 128, &p.xmap, kS8 ? ks * 128 : ks * 64, m0, xfull + s);
+        ++issued;
       }
+      for (int s = 0; s < NX && s < issued; ++s) mbar_wait_bounded(xfull + s, ((issued - 1 - s) / NX) & 1);
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = kS8 ? umma_idesc(2, 1, BN, kBM) : umma_idesc(1, kHalf ? 0 : 1, BN, kBM);
       for (int i = 0; i < nk; ++i) {
-        const int s = i % NS, u = i / NS;
-        if (!tc_wait(kS8 ? full + s : conv + s, u & 1, abort_flag, p.status)) break;
+        const int sx = i % NX, sa = kS8 ? sx : i % NA;
+        if (!tc_wait(xfull + sx, (i / NX) & 1, abort_flag, p.status)) break;
+        if (!kS8 && !tc_wait(afull + sa, (i / NA) & 1, abort_flag, p.status)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(a_ring + s * kATile), b0 = smem_u32(b_ring + s * BN * 128);
+        const uint32_t a0 = smem_u32(a_ring + sa * kATile), b0 = smem_u32(x_ring + sx * BN * 128);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)  // 4 MMA K steps of 32 bytes inside the 128-byte atom
           tc_mma<kS8>(tmem, umma_desc_sw128(a0 + 32 * kk), umma_desc_sw128(b0 + 32 * kk), idesc,
                       (i > 0 || kk > 0) ? 1u : 0u);
-        tc_commit(empty + s);
+        tc_commit(xempty + sx);
+        if (!kS8) tc_commit(aempty + sa);
       }
       tc_commit(done);
     }
     __syncwarp();
   } else if constexpr (!kS8) {
-    // ---- conversion: thread -> (row r, half h) = 32 K values of the 64 in a stage
-    const int r = threadIdx.x & (kBM - 1), h = threadIdx.x >> 7;
+    // ---- conversion: thread -> (row r, half h) = 32 K values of the 64 in a stage;
+    // two threads per row read 32 contiguous bytes of the streamed stage
+    const int r = threadIdx.x >> 1, h = threadIdx.x & 1;
+    int chunks = 0, cur = -1;
     for (int i = 0; i < nk; ++i) {
-      const int s = i % NS, u = i / NS;
-      if (!tc_wait(full + s, u & 1, abort_flag, p.status)) break;
-      const uint8_t* raw = w_ring + s * kRawTile + r * kWRaw;
-      uint8_t* arow = a_ring + s * kATile + r * 128;
-      float sc[2] = {1.f, 1.f}, bi[2] = {0.f, 0.f};
+      const int ks = ks0 + i;
+      const int sw = i % NW, sa = i % NA;
+      if (!tc_wait(wfull + sw, (i / NW) & 1, abort_flag, p.status)) break;
+      int ch = 0;
       if constexpr (kAffine) {
-        const int kel = (ks0 + i) * 64;
-        const int g0 = (kel / p.G) & ~7;
-        const uint16_t* st = reinterpret_cast<const uint16_t*>(sc_ring + s * kScTile);
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int gi = (kel + 32 * h + 16 * q) / p.G - g0;  // group of K values [32h + 16q, +16)
-          sc[q] = bits16_to_float(st[r * 8 + gi], kHalf);
-          bi[q] = bits16_to_float(st[kBM * 8 + r * 8 + gi], kHalf);
+        ch = chunk_of(ks);
+        if (ch != cur) {
+          cur = ch;
+          if (!tc_wait(scfull + (chunks & 1), (chunks >> 1) & 1, abort_flag, p.status)) break;
+          ++chunks;
         }
       }
+      if (i >= NA && !tc_wait(aempty + sa, ((i / NA) - 1) & 1, abort_flag, p.status)) break;
+      const uint8_t* raw = w_ring + sw * kRawTile + r * kWRaw + h * (kWRaw / 2);
+      uint8_t* arow = a_ring + sa * kATile + r * 128;
+      // scale / bias of this thread's 32 K values [32h, 32h + 32) (one group: G >= 32)
+      float sc = 1.f, bi = 0.f;
+      uint32_t s2 = 0u, b2 = 0u;
+      if constexpr (kAffine) {
+        const int gi = (ks * 64 + 32 * h) / p.G - ch * 8;
+        const uint16_t* st = reinterpret_cast<const uint16_t*>(sc_ring + ((chunks - 1) & 1) * kScTile);
+        const uint32_t sb = st[r * 8 + gi], bb = st[kBM * 8 + r * 8 + gi];
+        sc = bits16_to_float(sb, kHalf);
+        bi = bits16_to_float(bb, kHalf);
+        s2 = sb | (sb << 16);
+        b2 = bb | (bb << 16);
+      }
+      if constexpr (TW == TW_AFF4) {
+        const uint4 w = *reinterpret_cast<const uint4*>(raw);
+        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // output chunk j = 4h + c: K values 8j .. 8j+7
-        const int j = 4 * h + c;
-        float f[8];
-        if constexpr (TW == TW_AFF4) {
-          const uint32_t w = *reinterpret_cast<const uint32_t*>(raw + 4 * j);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = fmaf(u2f((w >> (4 * e)) & 15u), sc[c >> 1], bi[c >> 1]);
-        } else if constexpr (TW == TW_AFF8) {
-          const uint2 w = *reinterpret_cast<const uint2*>(raw + 8 * j);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            f[e] = fmaf(u2f((w.x >> (8 * e)) & 255u), sc[c >> 1], bi[c >> 1]);
-            f[4 + e] = fmaf(u2f((w.y >> (8 * e)) & 255u), sc[c >> 1], bi[c >> 1]);
-          }
-        } else {  // TW_I8: signed bytes, exact
-          const uint2 w = *reinterpret_cast<const uint2*>(raw + 8 * j);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            f[e] = static_cast<float>(static_cast<int8_t>((w.x >> (8 * e)) & 255u));
-            f[4 + e] = static_cast<float>(static_cast<int8_t>((w.y >> (8 * e)) & 255u));
-          }
+        for (int c = 0; c < 4; ++c) {
+          const int j = 4 * h + c;
+          *reinterpret_cast<uint4*>(arow + ((j ^ (r & 7)) << 4)) = dequant8_w4<kHalf>(ww[c], s2, b2);
         }
-        uint4 o;
-        o.x = pack2<kHalf>(f[0], f[1]);
-        o.y = pack2<kHalf>(f[2], f[3]);
-        o.z = pack2<kHalf>(f[4], f[5]);
-        o.w = pack2<kHalf>(f[6], f[7]);
-        *reinterpret_cast<uint4*>(arow + ((j ^ (r & 7)) << 4)) = o;
+      } else {
+        const uint4 wa = *reinterpret_cast<const uint4*>(raw);
+        const uint4 wb = *reinterpret_cast<const uint4*>(raw + 16);
+        const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = 4 * h + c;
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            if constexpr (TW == TW_AFF8) {
+              f[e] = fmaf(u2f((ww[2 * c] >> (8 * e)) & 255u), sc, bi);
+              f[4 + e] = fmaf(u2f((ww[2 * c + 1] >> (8 * e)) & 255u), sc, bi);
+            } else {  // TW_I8: signed bytes, exact
+              f[e] = static_cast<float>(static_cast<int8_t>((ww[2 * c] >> (8 * e)) & 255u));
+              f[4 + e] = static_cast<float>(static_cast<int8_t>((ww[2 * c + 1] >> (8 * e)) & 255u));
+            }
+          }
+          uint4 o;
+          o.x = pack2<kHalf>(f[0], f[1]);
+          o.y = pack2<kHalf>(f[2], f[3]);
+          o.z = pack2<kHalf>(f[4], f[5]);
+          o.w = pack2<kHalf>(f[6], f[7]);
+          *reinterpret_cast<uint4*>(arow + ((j ^ (r & 7)) << 4)) = o;
+        }
       }
       fence_proxy_async_smem();  // generic-proxy stores -> visible to the tensor core
       __syncwarp();
-      if (lane == 0) mbar_arrive(conv + s);
+      if (lane == 0) {
+        mbar_arrive(afull + sa);
+        mbar_arrive(wempty + sw);
+        if (kAffine && (i + 1 == nk || chunk_of(ks + 1) != ch)) mbar_arrive(scempty + ((chunks - 1) & 1));
+      }
     }
   }
   __syncthreads();
@@ -459,7 +548,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
 
 // ---------------------------------------------------------------- host side
 struct TcPlan {
-  int bn, stages, split, tiles_n, tiles_m;
+  int bn, na, nx, nw, split, tiles_n, tiles_m;
   size_t smem;
 };
 
@@ -473,35 +562,54 @@ int sm_count() {
   return count;
 }
 
-size_t tc_smem_bytes(int tw, int bn, int stages) {
-  const int raw = tw == TW_S8 ? 0 : kBM * (tw == TW_AFF4 ? 32 : 64);
-  const int sc = (tw == TW_AFF4 || tw == TW_AFF8) ? 2 * kBM * 16 : 0;
-  const size_t ring = static_cast<size_t>(stages) * (kATile + bn * 128 + raw + sc);
-  return 1024 + ring + static_cast<size_t>(3 * stages + 1) * 8;
+int raw_tile_bytes(int tw) { return tw == TW_S8 ? 0 : kBM * (tw == TW_AFF4 ? 32 : 64); }
+
+size_t tc_smem_bytes(int tw, int bn, int na, int nx, int nw) {
+  const bool affine = tw == TW_AFF4 || tw == TW_AFF8;
+  return 1024 + static_cast<size_t>(na) * kATile + static_cast<size_t>(nx) * bn * 128 +
+         static_cast<size_t>(nw) * raw_tile_bytes(tw) + (affine ? 2 * 2 * kBM * 16 : 0) +
+         static_cast<size_t>(2 * nx + 2 * na + 2 * nw + 5) * 8;
 }
 
+// Tile and ring plan. Tiles up to 128 activation rows run two CTAs per SM
+// (<= 110 KB of shared memory each), 256-row tiles one. The weight ring is
+// deepest (it streams from HBM), then the activation ring (L2-resident), then
+// the converted-operand ring. The epilogue's [128][bn + 1] staging reuses the
+// drained rings.
 TcPlan plan_tc(const TcRequest& r) {
   TcPlan pl{};
   const int kstage = r.tw == TW_S8 ? 128 : 64;
   const int ksteps = (r.K + kstage - 1) / kstage;
   pl.tiles_n = (r.N + kBM - 1) / kBM;
-  // activation tile: one tile up to 256 rows; larger M tiles by 256 (or 128 when that fills the SMs better)
   int bn = r.M <= 256 ? ((r.M + 15) / 16) * 16 : 256;
   if (r.M > 128 && pl.tiles_n * ((r.M + 255) / 256) < sm_count()) bn = 128;
   pl.bn = bn;
   pl.tiles_m = (r.M + bn - 1) / bn;
-  // ring depth: two CTAs per SM for tiles up to 128 columns, one for 256
-  int occ = 2;
-  if (bn > 128) {
-    pl.stages = 3;
-    occ = 1;
+  int occ = bn <= 128 ? 2 : 1;
+  const size_t budget = occ == 2 ? (110u << 10) : (200u << 10);
+  const bool s8 = r.tw == TW_S8;
+  int na = 2, nx = 2, nw = s8 ? 0 : 4;
+  auto size = [&](int a, int x, int w) { return tc_smem_bytes(r.tw, bn, s8 ? x : a, x, w); };
+  auto fits = [&](int a, int x, int w) { return size(a, x, w) <= budget; };
+  if (s8) {
+    while (nx < 8 && fits(0, nx + 1, 0)) ++nx;
+    na = nx;
   } else {
-    const size_t per = tc_smem_bytes(r.tw, bn, 1) - tc_smem_bytes(r.tw, bn, 0);
-    pl.stages = static_cast<int>(std::max<size_t>(2, std::min<size_t>(6, (110u << 10) / per)));
+    if (fits(na, nx + 1, nw)) ++nx;
+    while (nw < 8 && fits(na, nx, nw + 1)) ++nw;
+    if (fits(na, nx + 1, nw)) ++nx;
+    if (fits(na + 1, nx, nw)) ++na;
+    while (nx < 6 && fits(na, nx + 1, nw)) ++nx;
   }
-  // the epilogue's [128][bn + 1] staging must fit in the A + B rings
-  while (static_cast<size_t>(kBM) * (bn + 1) * 4 > static_cast<size_t>(pl.stages) * (kATile + bn * 128)) ++pl.stages;
-  pl.smem = tc_smem_bytes(r.tw, bn, pl.stages);
+  const size_t ring_bytes = static_cast<size_t>(s8 ? nx : na) * kATile + static_cast<size_t>(nx) * bn * 128 +
+                            static_cast<size_t>(nw) * raw_tile_bytes(r.tw);
+  size_t red = static_cast<size_t>(kBM) * (bn + 1) * 4;
+  for (int extra = 0; red > ring_bytes + static_cast<size_t>(extra) * bn * 128; ++extra) nx = nx + 1;
+  if (s8) na = nx;
+  pl.na = na;
+  pl.nx = nx;
+  pl.nw = nw;
+  pl.smem = tc_smem_bytes(r.tw, bn, na, nx, nw);
   if (pl.smem > (113u << 10)) occ = 1;
   // K split over a cluster: fill one wave of CTAs, at least two stages per CTA
   const int tiles = pl.tiles_n * pl.tiles_m;
@@ -515,9 +623,17 @@ TcPlan plan_tc(const TcRequest& r) {
 template <int TW, bool kHalf, int TE>
 int launch_tc(const TcParams& p, const TcPlan& pl, cudaStream_t stream) {
   auto kernel = tc_linear_kernel<TW, kHalf, TE>;
-  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(pl.smem)) !=
-      cudaSuccess)
-    return fail(SB_ECUDA, "tensor-core linear: shared memory opt-in failed");
+  // opt in to the largest dynamic shared memory any plan uses (kTcSmemMax), once per device
+  if (pl.smem > kTcSmemMax) return fail(SB_EINVAL, "tensor-core linear: tile plan exceeds shared memory");
+  static int opted[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !opted[dev]) {
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kTcSmemMax)) !=
+        cudaSuccess)
+      return fail(SB_ECUDA, "tensor-core linear: shared memory opt-in failed");
+    if (dev >= 0 && dev < 64) opted[dev] = 1;
+  }
   const dim3 grid(pl.split, pl.tiles_n, pl.tiles_m);
   return launch_cluster("tensor-core linear", kernel, grid, dim3(kTcThreads), pl.smem, pl.split, stream, p);
 }
@@ -550,7 +666,9 @@ int run_tc_linear(const TcRequest& r, cudaStream_t stream) {
   p.K = r.K;
   p.G = r.group_size > 0 ? r.group_size : 64;
   p.bn = pl.bn;
-  p.stages = pl.stages;
+  p.na = pl.na;
+  p.nx = pl.nx;
+  p.nw = pl.nw;
   const int kstage = r.tw == TW_S8 ? 128 : 64;
   p.ksteps = (r.K + kstage - 1) / kstage;
   // weights
