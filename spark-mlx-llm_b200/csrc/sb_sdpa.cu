@@ -42,8 +42,8 @@ constexpr int kSdpaStages = 3;           // 16-token blocks in flight per warp
 constexpr int kMaxSplits = 64;           // token splits per (batch, kv head)
 constexpr int kSdpaStageBytes = 2 * 16 * kSdpaD;  // swizzled K box + V box
 constexpr int kSdpaScaleBytes = 64;                 // the block's 16 K scales + 16 V scales (fp16)
-constexpr size_t sdpa_smem(int warps) {
-  return 2048 + static_cast<size_t>(warps) * kSdpaStages * (kSdpaStageBytes + kSdpaScaleBytes);
+constexpr size_t sdpa_smem(int warps, int stages) {
+  return 2048 + static_cast<size_t>(warps) * stages * (kSdpaStageBytes + kSdpaScaleBytes);
 }
 
 struct SdpaParams {
@@ -65,6 +65,7 @@ struct SdpaParams {
   int cluster;         // 1: the splits of a (b, kv head) form a cluster and merge in shared memory
   int early;           // 1: lengths and every cache row but the newest are final before this kernel
   int scale_bulk;      // 1: the blocks' scales stream with the K/V boxes (capacity % 16 == 0, aligned)
+  int stages;          // ring depth per warp
 };
 
 constexpr int kSdpaMaxClusterSplits = 16;
@@ -118,10 +119,11 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   extern __shared__ uint8_t smem_dyn[];
   // 1 KB-aligned start (pointer arithmetic keeps the shared address space known to the compiler)
   uint8_t* sbase = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase) + warp * kSdpaStages;
-  uint8_t* ring = sbase + 1024 + warp * kSdpaStages * kSdpaStageBytes;
+  const int NS = p.stages;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbase) + warp * NS;
+  uint8_t* ring = sbase + 1024 + warp * NS * kSdpaStageBytes;
   // per-warp ring of the blocks' scales: [stage][k 16 x fp16 | v 16 x fp16]
-  uint8_t* sring = sbase + 1024 + kSdpaWarps * kSdpaStages * kSdpaStageBytes + warp * kSdpaStages * kSdpaScaleBytes;
+  uint8_t* sring = sbase + 1024 + kSdpaWarps * NS * kSdpaStageBytes + warp * NS * kSdpaScaleBytes;
   const int nb = blk_end - blk_begin;
   const int my_blocks = nb > warp ? (nb - warp + kSdpaWarps - 1) / kSdpaWarps : 0;
   auto block_of = [&](int i) { return blk_begin + warp + i * kSdpaWarps; };
@@ -139,16 +141,16 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   };
   const int last_blk = nblk - 1;  // holds token N-1, written by the previous kernel
   if (lane == 0) {
-    for (int i = 0; i < kSdpaStages; ++i) mbar_init(bars + i, 1);
+    for (int i = 0; i < NS; ++i) mbar_init(bars + i, 1);
     mbar_fence_init();
-    for (int i = 0; i < kSdpaStages && i < my_blocks; ++i)
+    for (int i = 0; i < NS && i < my_blocks; ++i)
       if (!p.early || block_of(i) != last_blk) issue(i, i);
   }
   __syncwarp();
   if (p.early) {
     grid_dependency_wait();
     if (lane == 0)
-      for (int i = 0; i < kSdpaStages && i < my_blocks; ++i)
+      for (int i = 0; i < NS && i < my_blocks; ++i)
         if (block_of(i) == last_blk) issue(i, i);
     __syncwarp();
   }
@@ -323,19 +325,18 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
       }
     }
     __syncwarp();
-    if (i + kSdpaStages < my_blocks && lane == 0) {
+    if (i + NS < my_blocks && lane == 0) {
       fence_proxy_async_smem();
-      issue(i + kSdpaStages, slot);
+      issue(i + NS, slot);
     }
-    if (++slot == kSdpaStages) {
+    if (++slot == NS) {
       slot = 0;
       phase ^= 1u;
     }
   }
   if (failed) {
     if (p.status && lane == 0) atomicOr(p.status, kStatusTimeout);
-    for (int i = max(0, my_blocks - kSdpaStages); i < my_blocks; ++i)
-      mbar_wait_bounded(bars + i % kSdpaStages, (i / kSdpaStages) & 1);
+    for (int i = max(0, my_blocks - NS); i < my_blocks; ++i) mbar_wait_bounded(bars + i % NS, (i / NS) & 1);
     m_run = -INFINITY;
     l_run = 0.f;
   }
@@ -346,7 +347,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   __shared__ float s_m[kSdpaWarps][8], s_l[kSdpaWarps][8];
   // the warp's partial O [8][D] goes to its own (drained) ring: warp w at ring_of(w)
   auto o_of = [&](int w) {
-    return reinterpret_cast<float*>(sbase + 1024 + w * kSdpaStages * kSdpaStageBytes);
+    return reinterpret_cast<float*>(sbase + 1024 + w * NS * kSdpaStageBytes);
   };
   __syncwarp();
   if (head_ok) {
@@ -523,6 +524,9 @@ SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int max_warps) {
   const int64_t sms = sdpa_sms();
   const int64_t slots = sms * (16 / pl.warps);
   int64_t s = (slots + bkv - 1) / bkv;
+  // a second wave of a few CTAs costs a whole CTA time: drop to one split less
+  // when that still fills three quarters of the slots
+  if (s > 1 && bkv * s > slots && bkv * (s - 1) * 4 >= slots * 3) --s;
   if (s > kSdpaMaxClusterSplits && bkv * kSdpaMaxClusterSplits * 5 >= sms * 4) s = kSdpaMaxClusterSplits;
   s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (2 * pl.warps)));
   s = std::min<int64_t>(s, kMaxSplits);
@@ -601,7 +605,10 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   p.early = early ? 1 : 0;
   const dim3 grid(splits, static_cast<unsigned>(bkv));
   const dim3 block(plan.warps * 32);
-  const size_t smem = sdpa_smem(plan.warps);
+  // Ring depth: 3 blocks per warp. (A 6-deep ring when the grid leaves one CTA
+  // per SM measured slower on B200 at batch 1 / 32K tokens: 52 vs 40 us.)
+  p.stages = kSdpaStages;
+  const size_t smem = sdpa_smem(plan.warps, p.stages);
   auto go = [&](auto kernel) -> int {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
