@@ -199,7 +199,7 @@ __device__ __forceinline__ float load_typed(const void* base, size_t i, int dtyp
 }
 
 template <int TW>
-constexpr int wraw_bytes() {  // streamed weight bytes per row per stage (16-bit kinds: 64 K values)
+constexpr int wraw_bytes() {  // weight bytes per row per MMA stage (16-bit kinds: 64 K values)
   return TW == TW_AFF4 ? 32 : (TW == TW_S8 ? 128 : 64);
 }
 
@@ -208,8 +208,11 @@ template <int TW, bool kHalf, int TE>
 __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_constant__ TcParams p) {
   constexpr bool kS8 = TW == TW_S8;
   constexpr bool kAffine = TW == TW_AFF4 || TW == TW_AFF8;
-  constexpr int kWRaw = wraw_bytes<TW>();
-  constexpr int kRawTile = kS8 ? 0 : kBM * kWRaw;  // streamed weight stage (converted kinds)
+  // converted kinds stream the weights in 128-byte-wide, 128-byte-swizzled boxes
+  // of 128 rows, each covering kSub MMA stages of kWStage bytes per row
+  constexpr int kWStage = wraw_bytes<TW>();
+  constexpr int kSub = kS8 ? 1 : 128 / kWStage;
+  constexpr int kRawTile = kS8 ? 0 : kBM * 128;
   constexpr int kScTile = 2 * kBM * 16;             // scales + biases of 8 groups x 128 rows
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int S = gridDim.x, rank = blockIdx.x;
@@ -265,6 +268,18 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
     mbar_fence_init();
     s_abort = 0;
   }
+  // the producers' tensor maps: fetch the descriptors while TMEM and the barriers are set up
+  if (threadIdx.x == kWProducerWarp * 32 && !kS8) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.wmap)) : "memory");
+    if (kAffine) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.smap)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.bmap)) : "memory");
+    }
+  }
+  if (threadIdx.x == kXProducerWarp * 32) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.xmap)) : "memory");
+    if (kS8) asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&p.wmap)) : "memory");
+  }
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
                  "r"(tmem_cols)
@@ -282,24 +297,32 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
     // ---- weight stages (and scale chunks) into their rings, as far ahead as the rings allow
     if (lane == 0 && !kS8) {
       int issued = 0, chunks = 0, cur = -1;
-      for (int i = 0; i < nk; ++i) {
-        const int ks = ks0 + i;
+      bool stop = false;
+      const int nbox = (nk + kSub - 1) / kSub;
+      for (int bx = 0; bx < nbox && !stop; ++bx) {
+        const int i0 = bx * kSub;
         if constexpr (kAffine) {
-          const int ch = chunk_of(ks);
-          if (ch != cur) {
+          // scale chunks of the box's stages, in stage order
+          for (int i = i0; i < min(nk, i0 + kSub); ++i) {
+            const int ch = chunk_of(ks0 + i);
+            if (ch == cur) continue;
             cur = ch;
             const int cs = chunks & 1, cu = chunks >> 1;
-            if (cu > 0 && !tc_wait(scempty + cs, (cu - 1) & 1, abort_flag, p.status)) break;
+            if (cu > 0 && !tc_wait(scempty + cs, (cu - 1) & 1, abort_flag, p.status)) {
+              stop = true;
+              break;
+            }
             mbar_arrive_expect_tx(scfull + cs, kScTile);
             tma_load_2d(sc_ring + cs * kScTile, &p.smap, ch * 8, n0, scfull + cs);
             tma_load_2d(sc_ring + cs * kScTile + kBM * 16, &p.bmap, ch * 8, n0, scfull + cs);
             ++chunks;
           }
+          if (stop) break;
         }
-        const int s = i % NW, u = i / NW;
+        const int s = bx % NW, u = bx / NW;
         if (u > 0 && !tc_wait(wempty + s, (u - 1) & 1, abort_flag, p.status)) break;
         mbar_arrive_expect_tx(wfull + s, kRawTile);
-        tma_load_2d(w_ring + s * kRawTile, &p.wmap, ks * kWRaw, n0, wfull + s);
+        tma_load_2d(w_ring + s * kRawTile, &p.wmap, (ks0 + i0) * kWStage, n0, wfull + s);
         ++issued;
       }
       // copies still in flight (only after an abort) land before the memory is reused
@@ -343,13 +366,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
     __syncwarp();
   } else if constexpr (!kS8) {
     // ---- conversion: thread -> (row r, half h) = 32 K values of the 64 in a stage;
-    // two threads per row read 32 contiguous bytes of the streamed stage
+    // the two threads of a row read its stage bytes from the swizzled weight box
     const int r = threadIdx.x >> 1, h = threadIdx.x & 1;
     int chunks = 0, cur = -1;
     for (int i = 0; i < nk; ++i) {
       const int ks = ks0 + i;
-      const int sw = i % NW, sa = i % NA;
-      if (!tc_wait(wfull + sw, (i / NW) & 1, abort_flag, p.status)) break;
+      const int bx = i / kSub, sub = i - bx * kSub;
+      const int sw = bx % NW, sa = i % NA;
+      if (sub == 0 && !tc_wait(wfull + sw, (bx / NW) & 1, abort_flag, p.status)) break;
       int ch = 0;
       if constexpr (kAffine) {
         ch = chunk_of(ks);
@@ -360,7 +384,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
         }
       }
       if (i >= NA && !tc_wait(aempty + sa, ((i / NA) - 1) & 1, abort_flag, p.status)) break;
-      const uint8_t* raw = w_ring + sw * kRawTile + r * kWRaw + h * (kWRaw / 2);
+      // 16-byte chunk c of row r sits at chunk c ^ (r % 8) (128-byte swizzle)
+      const uint8_t* wrow = w_ring + sw * kRawTile + r * 128;
+      const int c16 = (sub * kWStage + h * (kWStage / 2)) >> 4;
       uint8_t* arow = a_ring + sa * kATile + r * 128;
       // scale / bias of this thread's 32 K values [32h, 32h + 32) (one group: G >= 32)
       float sc = 1.f, bi = 0.f;
@@ -375,7 +401,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
         b2 = bb | (bb << 16);
       }
       if constexpr (TW == TW_AFF4) {
-        const uint4 w = *reinterpret_cast<const uint4*>(raw);
+        const uint4 w = *reinterpret_cast<const uint4*>(wrow + ((c16 ^ (r & 7)) << 4));
         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -383,8 +409,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
           *reinterpret_cast<uint4*>(arow + ((j ^ (r & 7)) << 4)) = dequant8_w4<kHalf>(ww[c], s2, b2);
         }
       } else {
-        const uint4 wa = *reinterpret_cast<const uint4*>(raw);
-        const uint4 wb = *reinterpret_cast<const uint4*>(raw + 16);
+        const uint4 wa = *reinterpret_cast<const uint4*>(wrow + ((c16 ^ (r & 7)) << 4));
+        const uint4 wb = *reinterpret_cast<const uint4*>(wrow + (((c16 + 1) ^ (r & 7)) << 4));
         const uint32_t ww[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -412,7 +438,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
       __syncwarp();
       if (lane == 0) {
         mbar_arrive(afull + sa);
-        mbar_arrive(wempty + sw);
+        if (sub == kSub - 1 || i + 1 == nk) mbar_arrive(wempty + sw);
         if (kAffine && (i + 1 == nk || chunk_of(ks + 1) != ch)) mbar_arrive(scempty + ((chunks - 1) & 1));
       }
     }
@@ -562,7 +588,7 @@ int sm_count() {
   return count;
 }
 
-int raw_tile_bytes(int tw) { return tw == TW_S8 ? 0 : kBM * (tw == TW_AFF4 ? 32 : 64); }
+int raw_tile_bytes(int tw) { return tw == TW_S8 ? 0 : kBM * 128; }
 
 size_t tc_smem_bytes(int tw, int bn, int na, int nx, int nw) {
   const bool affine = tw == TW_AFF4 || tw == TW_AFF8;
@@ -581,14 +607,15 @@ TcPlan plan_tc(const TcRequest& r) {
   const int kstage = r.tw == TW_S8 ? 128 : 64;
   const int ksteps = (r.K + kstage - 1) / kstage;
   pl.tiles_n = (r.N + kBM - 1) / kBM;
-  int bn = r.M <= 256 ? ((r.M + 15) / 16) * 16 : 256;
-  if (r.M > 128 && pl.tiles_n * ((r.M + 255) / 256) < sm_count()) bn = 128;
+  const int bn = r.M <= 256 ? ((r.M + 15) / 16) * 16 : 256;
   pl.bn = bn;
   pl.tiles_m = (r.M + bn - 1) / bn;
-  int occ = bn <= 128 ? 2 : 1;
+  // small activation tiles (HBM-bound) run two CTAs per SM; larger ones one,
+  // with deeper rings
+  int occ = bn <= 64 ? 2 : 1;
   const size_t budget = occ == 2 ? (110u << 10) : (200u << 10);
   const bool s8 = r.tw == TW_S8;
-  int na = 2, nx = 2, nw = s8 ? 0 : 4;
+  int na = 2, nx = 2, nw = s8 ? 0 : 2;
   auto size = [&](int a, int x, int w) { return tc_smem_bytes(r.tw, bn, s8 ? x : a, x, w); };
   auto fits = [&](int a, int x, int w) { return size(a, x, w) <= budget; };
   if (s8) {
@@ -596,8 +623,7 @@ TcPlan plan_tc(const TcRequest& r) {
     na = nx;
   } else {
     if (fits(na, nx + 1, nw)) ++nx;
-    while (nw < 8 && fits(na, nx, nw + 1)) ++nw;
-    if (fits(na, nx + 1, nw)) ++nx;
+    while (nw < 4 && fits(na, nx, nw + 1)) ++nw;
     if (fits(na + 1, nx, nw)) ++na;
     while (nx < 6 && fits(na, nx + 1, nw)) ++nx;
   }
@@ -676,8 +702,7 @@ int run_tc_linear(const TcRequest& r, cudaStream_t stream) {
     if (int st = make_tmap_2d(&p.wmap, r.w, 1, r.N, r.K, r.K, 128, kBM, true)) return st;
   } else {
     const int row_bytes = r.tw == TW_AFF4 ? r.K / 2 : r.K;
-    const int box = r.tw == TW_AFF4 ? 32 : 64;
-    if (int st = make_tmap_2d(&p.wmap, r.w, 1, r.N, row_bytes, row_bytes, box, kBM, false)) return st;
+    if (int st = make_tmap_2d(&p.wmap, r.w, 1, r.N, row_bytes, row_bytes, 128, kBM, true)) return st;
   }
   if (r.tw == TW_AFF4 || r.tw == TW_AFF8) {
     const int gpr = r.K / r.group_size;
