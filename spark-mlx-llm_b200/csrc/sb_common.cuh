@@ -155,6 +155,11 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
       : "memory");
 }
+// Start fetching a TMA descriptor (kernel parameter) into the descriptor cache,
+// so the first copy that uses it does not wait for the fetch.
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
 // Byte `byte` of row `row` inside a 128-byte-swizzled box.
 __device__ __forceinline__ const uint8_t* swz128(const uint8_t* box, int row, int byte) {
   return box + row * 128 + ((((byte >> 4) ^ (row & 7)) << 4) | (byte & 15));

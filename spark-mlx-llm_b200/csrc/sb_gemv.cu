@@ -310,6 +310,18 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
     }
   };
 
+  // the weight (and scale/bias) tensor maps: start the descriptor fetches
+  // before the barriers are set up (a first copy otherwise waits for them)
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&p.tmap0);
+    prefetch_tmap(&p.tmap1);
+    if (C::kAffine && p.sc_tma) {
+      prefetch_tmap(&p.smap0);
+      prefetch_tmap(&p.bmap0);
+      prefetch_tmap(&p.smap1);
+      prefetch_tmap(&p.bmap1);
+    }
+  }
   if (active && lane == 0) {
     for (int i = 0; i < p.ring; ++i) mbar_init(bars + i, 1);
     mbar_fence_init();

@@ -94,6 +94,10 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   const int split = blockIdx.x;
   const int bkv = blockIdx.y;
   const int b = bkv / p.kv_heads, kvh = bkv % p.kv_heads;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&p.kmap);
+    prefetch_tmap(&p.vmap);
+  }
   // With `early`, the KV blocks that do not hold the newest token stream in
   // while the previous kernel (which writes that token) still runs.
   if (!p.early) grid_dependency_wait();
