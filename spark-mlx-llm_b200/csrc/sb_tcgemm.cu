@@ -49,6 +49,7 @@ struct TcParams {
   alignas(64) CUtensorMap bmap;  // biases, same
   alignas(64) CUtensorMap xmap;  // activations [M][K], SW128 box {128 bytes, BN}
   int M, N, K, G;
+  int lg_g;  // log2(G): groups are 32, 64 or 128 K values
   int bn, na, nx, nw, ksteps;
   void* y;
   int ldy, y_dtype;
@@ -245,7 +246,9 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
   volatile int* abort_flag = &s_abort;
   const uint32_t tmem_cols = BN <= 32 ? 32u : (BN <= 64 ? 64u : (BN <= 128 ? 128u : 256u));
   // scale chunk (8 groups) of K stage ks (64 K values per stage)
-  auto chunk_of = [&](int ks) { return ((ks * 64) / p.G) >> 3; };
+  // (ring slots and phases advance incrementally: no division by a runtime
+  // ring depth or group size in the loops)
+  auto chunk_of = [&](int ks) { return ((ks * 64) >> p.lg_g) >> 3; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NX; ++s) {
@@ -297,6 +300,8 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
     // ---- weight stages (and scale chunks) into their rings, as far ahead as the rings allow
     if (lane == 0 && !kS8) {
       int issued = 0, chunks = 0, cur = -1;
+      int s = 0;
+      uint32_t ph = 0u;
       bool stop = false;
       const int nbox = (nk + kSub - 1) / kSub;
       for (int bx = 0; bx < nbox && !stop; ++bx) {
@@ -319,11 +324,14 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
           }
           if (stop) break;
         }
-        const int s = bx % NW, u = bx / NW;
-        if (u > 0 && !tc_wait(wempty + s, (u - 1) & 1, abort_flag, p.status)) break;
+        if (bx >= NW && !tc_wait(wempty + s, ph ^ 1u, abort_flag, p.status)) break;
         mbar_arrive_expect_tx(wfull + s, kRawTile);
         tma_load_2d(w_ring + s * kRawTile, &p.wmap, (ks0 + i0) * kWStage, n0, wfull + s);
         ++issued;
+        if (++s == NW) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       // copies still in flight (only after an abort) land before the memory is reused
       for (int s = 0; s < NW && s < issued; ++s) mbar_wait_bounded(wfull + s, ((issued - 1 - s) / NW) & 1);
@@ -333,25 +341,30 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
     // ---- activation stages (TW_S8: with the int8 weight tile)
     if (lane == 0) {
       const uint32_t bytes = static_cast<uint32_t>(BN * 128 + (kS8 ? kATile : 0));
-      int issued = 0;
+      int issued = 0, s = 0;
+      uint32_t ph = 0u;
       for (int i = 0; i < nk; ++i) {
         const int ks = ks0 + i;
-        const int s = i % NX, u = i / NX;
-        if (u > 0 && !tc_wait(xempty + s, (u - 1) & 1, abort_flag, p.status)) break;
+        if (i >= NX && !tc_wait(xempty + s, ph ^ 1u, abort_flag, p.status)) break;
         mbar_arrive_expect_tx(xfull + s, bytes);
         if constexpr (kS8) tma_load_2d(a_ring + s * kATile, &p.wmap, ks * 128, n0, xfull + s);
         tma_load_2d(x_ring + s * BN * 128, &p.xmap, kS8 ? ks * 128 : ks * 64, m0, xfull + s);
         ++issued;
+        if (++s == NX) {
+          s = 0;
+          ph ^= 1u;
+        }
       }
       for (int s = 0; s < NX && s < issued; ++s) mbar_wait_bounded(xfull + s, ((issued - 1 - s) / NX) & 1);
     }
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
       const uint32_t idesc = kS8 ? umma_idesc(2, 1, BN, kBM) : umma_idesc(1, kHalf ? 0 : 1, BN, kBM);
+      int sx = 0, sa = 0;
+      uint32_t px = 0u, pa = 0u;
       for (int i = 0; i < nk; ++i) {
-        const int sx = i % NX, sa = kS8 ? sx : i % NA;
-        if (!tc_wait(xfull + sx, (i / NX) & 1, abort_flag, p.status)) break;
-        if (!kS8 && !tc_wait(afull + sa, (i / NA) & 1, abort_flag, p.status)) break;
+        if (!tc_wait(xfull + sx, px, abort_flag, p.status)) break;
+        if (!kS8 && !tc_wait(afull + sa, pa, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t a0 = smem_u32(a_ring + sa * kATile), b0 = smem_u32(x_ring + sx * BN * 128);
 #pragma unroll
@@ -360,6 +373,16 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
                       (i > 0 || kk > 0) ? 1u : 0u);
         tc_commit(xempty + sx);
         if (!kS8) tc_commit(aempty + sa);
+        if (++sx == NX) {
+          sx = 0;
+          px ^= 1u;
+        }
+        if (kS8) {
+          sa = sx;
+        } else if (++sa == NA) {
+          sa = 0;
+          pa ^= 1u;
+        }
       }
       tc_commit(done);
     }
@@ -369,11 +392,11 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
     // the two threads of a row read its stage bytes from the swizzled weight box
     const int r = threadIdx.x >> 1, h = threadIdx.x & 1;
     int chunks = 0, cur = -1;
+    int sw = 0, sub = 0, sa = 0;
+    uint32_t pw = 0u, pa = 0u;
     for (int i = 0; i < nk; ++i) {
       const int ks = ks0 + i;
-      const int bx = i / kSub, sub = i - bx * kSub;
-      const int sw = bx % NW, sa = i % NA;
-      if (sub == 0 && !tc_wait(wfull + sw, (bx / NW) & 1, abort_flag, p.status)) break;
+      if (sub == 0 && !tc_wait(wfull + sw, pw, abort_flag, p.status)) break;
       int ch = 0;
       if constexpr (kAffine) {
         ch = chunk_of(ks);
@@ -383,7 +406,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
           ++chunks;
         }
       }
-      if (i >= NA && !tc_wait(aempty + sa, ((i / NA) - 1) & 1, abort_flag, p.status)) break;
+      if (i >= NA && !tc_wait(aempty + sa, pa ^ 1u, abort_flag, p.status)) break;
       // 16-byte chunk c of row r sits at chunk c ^ (r % 8) (128-byte swizzle)
       const uint8_t* wrow = w_ring + sw * kRawTile + r * 128;
       const int c16 = (sub * kWStage + h * (kWStage / 2)) >> 4;
@@ -392,7 +415,7 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
       float sc = 1.f, bi = 0.f;
       uint32_t s2 = 0u, b2 = 0u;
       if constexpr (kAffine) {
-        const int gi = (ks * 64 + 32 * h) / p.G - ch * 8;
+        const int gi = ((ks * 64 + 32 * h) >> p.lg_g) & 7;  // group inside the chunk
         const uint16_t* st = reinterpret_cast<const uint16_t*>(sc_ring + ((chunks - 1) & 1) * kScTile);
         const uint32_t sb = st[r * 8 + gi], bb = st[kBM * 8 + r * 8 + gi];
         sc = bits16_to_float(sb, kHalf);
@@ -440,6 +463,17 @@ __global__ void __launch_bounds__(kTcThreads, 2) tc_linear_kernel(const __grid_c
         mbar_arrive(afull + sa);
         if (sub == kSub - 1 || i + 1 == nk) mbar_arrive(wempty + sw);
         if (kAffine && (i + 1 == nk || chunk_of(ks + 1) != ch)) mbar_arrive(scempty + ((chunks - 1) & 1));
+      }
+      if (++sub == kSub) {
+        sub = 0;
+        if (++sw == NW) {
+          sw = 0;
+          pw ^= 1u;
+        }
+      }
+      if (++sa == NA) {
+        sa = 0;
+        pa ^= 1u;
       }
     }
   }
@@ -613,7 +647,7 @@ TcPlan plan_tc(const TcRequest& r) {
   // small activation tiles (HBM-bound) run two CTAs per SM; larger ones one,
   // with deeper rings
   int occ = bn <= 64 ? 2 : 1;
-  const size_t budget = occ == 2 ? (110u << 10) : (200u << 10);
+  const size_t budget = occ == 2 ? (112u << 10) : (200u << 10);
   const bool s8 = r.tw == TW_S8;
   int na = 2, nx = 2, nw = s8 ? 0 : 2;
   auto size = [&](int a, int x, int w) { return tc_smem_bytes(r.tw, bn, s8 ? x : a, x, w); };
@@ -622,10 +656,17 @@ TcPlan plan_tc(const TcRequest& r) {
     while (nx < 8 && fits(0, nx + 1, 0)) ++nx;
     na = nx;
   } else {
-    if (fits(na, nx + 1, nw)) ++nx;
-    while (nw < 4 && fits(na, nx, nw + 1)) ++nw;
+    // The converted-operand ring bounds the rate: a slot returns only after
+    // conversion -> MMA issue -> MMA completion -> commit (about 2 us per round
+    // trip measured on B200), so it gets depth first, then the activation ring
+    // (L2-resident boxes), then the weight ring (each slot covers 2-4 stages).
     if (fits(na + 1, nx, nw)) ++na;
+    if (fits(na, nx + 1, nw)) ++nx;
+    if (fits(na + 1, nx, nw)) ++na;
+    while (nx < 4 && fits(na, nx + 1, nw)) ++nx;
+    while (na < 6 && fits(na + 1, nx, nw)) ++na;
     while (nx < 6 && fits(na, nx + 1, nw)) ++nx;
+    while (nw < 4 && fits(na, nx, nw + 1)) ++nw;
   }
   const size_t ring_bytes = static_cast<size_t>(s8 ? nx : na) * kATile + static_cast<size_t>(nx) * bn * 128 +
                             static_cast<size_t>(nw) * raw_tile_bytes(r.tw);
@@ -691,6 +732,7 @@ int run_tc_linear(const TcRequest& r, cudaStream_t stream) {
   p.N = r.N;
   p.K = r.K;
   p.G = r.group_size > 0 ? r.group_size : 64;
+  p.lg_g = p.G == 32 ? 5 : (p.G == 128 ? 7 : 6);
   p.bn = pl.bn;
   p.na = pl.na;
   p.nx = pl.nx;
