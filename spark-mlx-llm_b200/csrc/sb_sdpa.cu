@@ -481,18 +481,38 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
     s_norm[hh] = ll > 0.f ? 1.0f / ll : 0.f;
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < G * kSdpaD; idx += kSdpaWarps * 32) {
-    const int hh = idx / kSdpaD, d = idx % kSdpaD;
-    float oo = 0.f;
-    for (int s0 = 0; s0 < p.splits; s0 += 8) {
-      float v[8];
+  // every output of this thread loads its next kBatch splits together: one
+  // round trip per kBatch splits, not per split and output
+  constexpr int kOut = (G * kSdpaD + kSdpaWarps * 32 - 1) / (kSdpaWarps * 32);
+  constexpr int kBatch = 32 / kOut;
+  float oo[kOut];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = s0 + j < p.splits ? __ldcg(all + ((s0 + j) * G + hh) * kPartStride + d) : 0.f;
+  for (int o = 0; o < kOut; ++o) oo[o] = 0.f;
+  for (int s0 = 0; s0 < p.splits; s0 += kBatch) {
+    float v[kOut][kBatch];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (s0 + j < p.splits) oo += v[j] * s_mw[s0 + j][hh];
+    for (int o = 0; o < kOut; ++o) {
+      const int idx = threadIdx.x + o * kSdpaWarps * 32;
+      const int hh = idx / kSdpaD, d = idx % kSdpaD;
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        v[o][j] = (idx < G * kSdpaD && s0 + j < p.splits) ? __ldcg(all + ((s0 + j) * G + hh) * kPartStride + d) : 0.f;
     }
-    p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] = __float2bfloat16_rn(oo * s_norm[hh]);
+#pragma unroll
+    for (int o = 0; o < kOut; ++o) {
+      const int hh = min((threadIdx.x + o * kSdpaWarps * 32) / kSdpaD, G - 1);
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j)
+        if (s0 + j < p.splits) oo[o] += v[o][j] * s_mw[s0 + j][hh];
+    }
+  }
+#pragma unroll
+  for (int o = 0; o < kOut; ++o) {
+    const int idx = threadIdx.x + o * kSdpaWarps * 32;
+    if (idx >= G * kSdpaD) continue;
+    const int hh = idx / kSdpaD, d = idx % kSdpaD;
+    p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] =
+        __float2bfloat16_rn(oo[o] * s_norm[hh]);
   }
   if (threadIdx.x == 0) p.counters[bkv] = 0u;
 }
@@ -531,7 +551,10 @@ SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int max_warps) {
   // a second wave of a few CTAs costs a whole CTA time: drop to one split less
   // when that still fills three quarters of the slots
   if (s > 1 && bkv * s > slots && bkv * (s - 1) * 4 >= slots * 3) --s;
-  if (s > kSdpaMaxClusterSplits && bkv * kSdpaMaxClusterSplits * 5 >= sms * 4) s = kSdpaMaxClusterSplits;
+  // more splits than a cluster holds: keep them (two CTAs per SM, partials
+  // merged through the workspace by the last CTA) unless 16 splits already
+  // fill nine tenths of the slots (one cluster, merged in shared memory)
+  if (s > kSdpaMaxClusterSplits && bkv * kSdpaMaxClusterSplits * 10 >= slots * 9) s = kSdpaMaxClusterSplits;
   s = std::min<int64_t>(s, std::max<int64_t>(1, nblk / (2 * pl.warps)));
   s = std::min<int64_t>(s, kMaxSplits);
   pl.splits = static_cast<int>(std::max<int64_t>(1, s));
