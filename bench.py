@@ -24,6 +24,7 @@ not installable here) and prints the same metric.
 """
 
 import argparse
+import hashlib
 import json
 import math
 import os
@@ -38,6 +39,7 @@ sys.path[:0] = [ROOT, os.path.join(ROOT, "spark-mlx-llm_b200")]
 
 METRIC = "W4A16 decode tok/s bs1 @1/2/4/8 B200; GEMV & INT8-KV SDPA HBM GB/s vs peak"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TFLOPS = 1590.0
 
 
 def parse_args():
@@ -50,6 +52,9 @@ def parse_args():
     p.add_argument("--prompt", type=int, default=1024)
     p.add_argument("--layers", type=int, default=36, help="(debug) fewer layers")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-ops", action="store_true", help="skip the per-operator roofline section")
+    p.add_argument("--digest-steps", type=int, default=256,
+                   help="greedy tokens hashed into tokens_sha256 (decoded from the state after the prompt)")
     p.add_argument("--kernel-only", choices=["gateup", "sdpa", "tc"], default=None,
                    help="launch one hot kernel --steps times on a config-sized case (for ncu)")
     return p.parse_args()
@@ -63,6 +68,15 @@ def measured_peaks():
         return float(data["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
         return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tflops():
+    """Burst bf16 dense TFLOP/s (kernels timed in isolation)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_TFLOPS, "fallback"
 
 
 def profile_traffic():
@@ -323,6 +337,204 @@ def kernel_only(args):
     print(json.dumps(out))
 
 
+def decode_batch8(cfg, device, args, steps=64, warmup=4):
+    """Config 4 at batch 8 on one GPU: greedy decode tok/s (8 sequences x steps)
+    after a 1024-token prompt per sequence, CUDA events around graph replays."""
+    import torch
+
+    from spark_b200.decoder import SyntheticDecoder
+
+    dec = SyntheticDecoder(cfg, batch=8, capacity=args.prompt + warmup + steps + 16, device=device, seed=0)
+    gen = torch.Generator().manual_seed(8)
+    prompt = torch.randint(0, cfg.vocab, (8, args.prompt), generator=gen, dtype=torch.int32)
+    dec.prefill(prompt.to(device))
+    dec.capture()
+    for _ in range(warmup):
+        dec.graph.replay()
+    torch.cuda.synchronize(device)
+    stream = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        dec.graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    dec.check_status()
+    ms = e0.elapsed_time(e1)
+    out = {"tok_s": 8 * steps / (ms / 1000.0), "ms_per_step": ms / steps, "batch": 8, "steps": steps,
+           "prompt_tokens": args.prompt,
+           "weight_gbs": cfg.weight_bytes() / (ms / steps * 1e-3) / 1e9}
+    del dec
+    torch.cuda.empty_cache()
+    return out
+
+
+# ------------------------------------------------------------ per-op rooflines
+L2_ROTATE_BYTES = 2 * 126 * 1024 * 1024 + (8 << 20)  # rotate buffer sets totalling more than 2 x L2
+
+
+def _graph_us(dev, launch, copies, reps=4):
+    """Average device time (us) of one launch, from CUDA events around CUDA-graph
+    replays of ``len(copies) * rounds`` launches that rotate over ``copies``
+    (distinct buffer sets totalling more than 2 x L2, so every launch streams
+    from HBM). ``launch(copy, stream_handle)`` enqueues one launch."""
+    import torch
+
+    side = torch.cuda.Stream(dev)
+    rounds = max(1, 64 // len(copies))
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(side):
+        for c in copies:  # first use outside the graph (lazy tensor maps, attributes)
+            launch(c, side.cuda_stream)
+        torch.cuda.synchronize(dev)
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(rounds):
+                for c in copies:
+                    launch(c, side.cuda_stream)
+    graph.replay()
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream(dev)
+    e0.record(cur)
+    for _ in range(reps):
+        graph.replay()
+    e1.record(cur)
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1000.0 / (reps * rounds * len(copies))
+    del graph
+    return us
+
+
+def measure_ops(dev, peak_gbs, peak_tflops, peak_kind):
+    """Per-operator device time and roofline fraction at BASELINE configs 0-3.
+
+    Algorithmic bytes / flops per call are those of BASELINE.md section 2.
+    Each op runs in a CUDA graph with its weights (or KV cache) rotating over
+    enough copies to exceed 2 x L2 (252 MB)."""
+    import ctypes
+
+    import torch
+
+    from spark_b200 import quantize
+    from spark_b200._lib import check, lib
+
+    L = lib()
+    g = torch.Generator(device=dev).manual_seed(7)
+    out = {}
+
+    def rec(name, algo_bytes, us, flops=None, bound="hbm", **extra):
+        e = {"bound": bound, "us": us, "algo_bytes": algo_bytes, "gbs": algo_bytes / (us * 1e-6) / 1e9}
+        e["hbm_frac"] = e["gbs"] / peak_gbs
+        if flops is not None:
+            e["tflops"] = flops / (us * 1e-6) / 1e12
+            e["tensor_frac"] = e["tflops"] / peak_tflops
+        e["frac"] = e["tensor_frac"] if bound == "tensor" else e["hbm_frac"]
+        e.update(extra)
+        out[name] = e
+
+    def ncopies(nbytes):
+        return max(2, -(-L2_ROTATE_BYTES // nbytes))
+
+    # ---- configs 0 and 1: affine W4 linear (K 2560, N 9728, G 64), M 1/4/16/64/256
+    n, k, grp = 9728, 2560, 64
+    wbytes = n * k // 2 + n * (k // grp) * 4
+    base = quantize.quantize_affine_minmax(torch.randn(n, k, generator=g, device=dev) * 0.02, grp, 4)
+    w4 = [base] + [tuple(t.clone() for t in base) for _ in range(ncopies(wbytes) - 1)]
+    for m in (1, 4, 16, 64, 256):
+        x = torch.randn(m, k, generator=g, device=dev).bfloat16()
+        y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        wsb = L.sb_affine_linear_workspace_size(m, n, k, grp, 4)
+        ws = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+        def launch(c, st, x=x, y=y, ws=ws, wsb=wsb, m=m):
+            w, sc, bi = c
+            check(L.sb_affine_linear(x.data_ptr(), 0, w.data_ptr(), sc.data_ptr(), bi.data_ptr(), y.data_ptr(), m,
+                                     n, k, grp, 4, ws.data_ptr() if wsb else None, wsb, st), "w4 linear")
+
+        us = _graph_us(dev, launch, w4)
+        algo = wbytes + m * k * 2 + m * n * 2
+        flops = 2.0 * m * n * k
+        name = "cfg0_w4a16_gemv_m1" if m == 1 else f"cfg1_w4a16_m{m}"
+        rec(name, algo, us, flops, bound="tensor" if m >= 256 else "hbm", M=m, K=k, N=n,
+            kernel="gemv (mma.sync exact codes)" if m <= 8 else "tcgen05 linear (TMEM accumulators)")
+    del w4, base
+    # ---- config 1: W8A8 (per-channel int8 weights, per-token int8 activations), K 2560, N 9728
+    w8bytes = n * k + 4 * n
+    base = quantize.quantize_w8_per_channel(torch.randn(n, k, generator=g, device=dev) * 0.02, scale_to_bf16=False)
+    w8 = [base] + [tuple(t.clone() for t in base) for _ in range(ncopies(w8bytes) - 1)]
+    for m in (1, 16, 64, 256):
+        x = torch.randn(m, k, generator=g, device=dev).bfloat16()
+        y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+        wsb = L.sb_w8a8_linear_workspace_size(m, n, k)
+        ws = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+        def launch(c, st, x=x, y=y, ws=ws, wsb=wsb, m=m):
+            w, sc = c
+            check(L.sb_w8a8_linear(x.data_ptr(), 0, w.data_ptr(), sc.data_ptr(), None, 0, y.data_ptr(), m, n, k,
+                                   ws.data_ptr() if wsb else None, wsb, st), "w8a8 linear")
+
+        us = _graph_us(dev, launch, w8)
+        rec(f"cfg1_w8a8_m{m}", w8bytes + m * k * 2 + m * n * 2, us, 2.0 * m * n * k,
+            bound="hbm", M=m, K=k, N=n, note="int8 tensor work; HBM bytes are the bound through M=256")
+    del w8, base
+    # ---- config 2: fused QKV + RoPE (hidden 2560, 32/8 heads x 128, W4 G64), B x L in 1x1, 8x1, 1x1024
+    nq = (32 + 2 * 8) * 128
+    qbytes = nq * k // 2 + nq * (k // grp) * 4
+    base = quantize.quantize_affine_minmax(torch.randn(nq, k, generator=g, device=dev) * 0.02, grp, 4)
+    wq = [base] + [tuple(t.clone() for t in base) for _ in range(ncopies(qbytes) - 1)]
+    for bsz, seq in ((1, 1), (8, 1), (1, 1024)):
+        m = bsz * seq
+        x = torch.randn(m, k, generator=g, device=dev).bfloat16()
+        pos = torch.randint(0, 32768, (m,), generator=g, device=dev, dtype=torch.int32)
+        q = torch.empty(bsz, 32, seq, 128, device=dev, dtype=torch.bfloat16)
+        kk = torch.empty(bsz, 8, seq, 128, device=dev, dtype=torch.bfloat16)
+        vv = torch.empty_like(kk)
+        wsb = L.sb_qkv_rope_workspace_size(bsz, seq, k, 32, 8, 128, grp, 4)
+        ws = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+        def launch(c, st, x=x, pos=pos, q=q, kk=kk, vv=vv, ws=ws, wsb=wsb, bsz=bsz, seq=seq):
+            w, sc, bi = c
+            check(L.sb_qkv_rope(x.data_ptr(), 0, w.data_ptr(), sc.data_ptr(), bi.data_ptr(), pos.data_ptr(),
+                                q.data_ptr(), kk.data_ptr(), vv.data_ptr(), bsz, seq, k, 32, 8, 128, 128, 1e6, grp,
+                                4, ws.data_ptr() if wsb else None, wsb, st), "qkv rope")
+
+        us = _graph_us(dev, launch, wq)
+        rec(f"cfg2_qkv_rope_{bsz}x{seq}", qbytes + m * k * 2 + m * nq * 2, us, 2.0 * m * nq * k,
+            bound="tensor" if m >= 1024 else "hbm", batch=bsz, seq=seq)
+    del wq, base
+    # ---- config 3: INT8-KV decode SDPA at 32K tokens, batch 1/8/32, 32/8 heads x 128
+    ctx = 32768
+    for bsz in (1, 8, 32):
+        cache = bsz * 8 * ctx * 260
+        copies = []
+        for _ in range(ncopies(cache) if cache < L2_ROTATE_BYTES else 1):
+            kc = torch.randint(-127, 128, (bsz, 8, ctx, 128), generator=g, device=dev, dtype=torch.int8)
+            vc = torch.randint(-127, 128, (bsz, 8, ctx, 128), generator=g, device=dev, dtype=torch.int8)
+            ks = (torch.rand(bsz, 8, ctx, generator=g, device=dev) * 0.02 + 0.005).half()
+            vs = (torch.rand(bsz, 8, ctx, generator=g, device=dev) * 0.02 + 0.005).half()
+            copies.append((kc, ks, vc, vs))
+        qv = torch.randn(bsz, 32, 1, 128, generator=g, device=dev).bfloat16()
+        o = torch.empty_like(qv)
+        wsb = L.sb_int8_sdpa_workspace_size(bsz, 32, 8, ctx, 128)
+        ws = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+        def launch(c, st, qv=qv, o=o, ws=ws, wsb=wsb, bsz=bsz):
+            kc, ks, vc, vs = c
+            check(L.sb_int8_sdpa_decode(qv.data_ptr(), kc.data_ptr(), ks.data_ptr(), vc.data_ptr(), vs.data_ptr(),
+                                        o.data_ptr(), bsz, 32, 8, ctx, ctx, 128, 128 ** -0.5, ws.data_ptr(), wsb,
+                                        st), "int8 sdpa")
+
+        us = _graph_us(dev, launch, copies)
+        rec(f"cfg3_int8_sdpa_b{bsz}_32k", cache + bsz * 32 * 128 * 4, us, 4.0 * bsz * 32 * ctx * 128,
+            bound="hbm", batch=bsz, context=ctx, l2_copies=len(copies))
+        del copies
+    torch.cuda.synchronize(dev)
+    out["_method"] = (f"CUDA-graph replays, device time per launch from CUDA events; inputs rotate over buffer sets "
+                      f"> 2 x L2 (252 MB); frac against {peak_kind} HBM {peak_gbs:.1f} GB/s or bf16 "
+                      f"{peak_tflops:.1f} TFLOP/s (MEASURED_PEAKS.json)")
+    return out
+
+
 # -------------------------------------------------------------------- GPU arm
 def main():
     args = parse_args()
@@ -358,6 +570,13 @@ def main():
     prompt = torch.randint(0, cfg.vocab, (args.batch, args.prompt), generator=gen, dtype=torch.int32)
     dec.prefill(prompt.to(device))
     dec.capture()
+    # greedy tokens from the state after the prompt, hashed: identical digests
+    # across --gpus N mean the tensor-parallel runs generate the TP1 tokens
+    snap_tok, snap_pos = dec.tokens.clone(), dec.positions.clone()
+    digest_tokens = dec.decode(args.digest_steps).cpu().numpy()
+    digest = hashlib.sha256(digest_tokens.astype("<i4").tobytes()).hexdigest()
+    dec.tokens.copy_(snap_tok)
+    dec.positions.copy_(snap_pos)
     for _ in range(args.warmup):
         dec.graph.replay()
     torch.cuda.synchronize(device)
@@ -433,6 +652,16 @@ def main():
     peak, peak_kind = measured_peaks()
     traffic = profile_traffic()
 
+    dec.check_status()
+    ops = None
+    if world == 1 and not args.no_ops:
+        tflops, _ = measured_tflops()
+        del dec.graph
+        dec.graph = None
+        ops = measure_ops(device, peak, tflops, peak_kind)
+        if args.batch == 1:
+            ops["decode_bs8"] = decode_batch8(cfg, device, args)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu_v, cores, sample = cpu_reference(cfg, args.batch, args.prompt)
@@ -457,6 +686,10 @@ def main():
             "step_weight_gbs": cfg.weight_bytes() / world / (ms / args.steps * 1e-3) / 1e9,
             "cpu_baseline": cpu,
             "clocks": clocks,
+            "tokens_sha256": digest,
+            "tokens_digest_steps": args.digest_steps,
+            "tokens_head": digest_tokens[0, :16].tolist(),
+            "ops": ops,
         }
         print(json.dumps(out), flush=True)
     if world > 1:

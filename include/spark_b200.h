@@ -177,6 +177,12 @@ size_t sb_int8_sdpa_workspace_size(int64_t batch, int num_heads, int num_kv_head
  *   `stream` before its kernel. All calls on a device share the one array:
  *   calls that overlap on the GPU (different streams, no ordering) race and
  *   must not be issued.
+ *   Failure reporting: this call returns before its kernel runs, and the
+ *   device status word that a timed-out bounded wait sets lives in the
+ *   library array, which the next call clears - so on this entry point such
+ *   a timeout is NOT reported (the output is then incomplete). Callers that
+ *   must detect it use sb_int8_sdpa_decode with their own workspace and read
+ *   its status word.
  *   Arguments and layouts are those of sb_int8_sdpa_decode.
  */
 int sb_int8_sdpa_decode_static(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,

@@ -15,6 +15,7 @@
  *                      symmetric INT8 K/V with fp16 scales
  *   oc_rms_norm        mx.fast.rms_norm (spark_mlx_llm/ops/ffn.py:99), fp32 output
  *   oc_bf16_argmax     bf16 lm_head GEMV + greedy argmax (lowest index on ties)
+ *   oc_bf16_logits     the same GEMV, returning the fp32 logits
  * Outputs are fp32; the caller rounds to bf16 where the reference stores bf16.
  */
 #include <math.h>
@@ -254,6 +255,12 @@ static void head_rows(const void* vctx, long n0, long n1) {
       c->logits[(size_t)m * c->N + n] = dot;
     }
   }
+}
+
+/* logits [M, N] = x [M, K] . w [N, K]^T (bf16 bits), fp32 */
+void oc_bf16_logits(const float* x, int M, const uint16_t* w, int N, int K, float* logits) {
+  head_ctx ctx = {x, M, w, N, K, logits};
+  oc_parallel(N, head_rows, &ctx);
 }
 
 /* logits = x [M, K] . w [N, K]^T (bf16 bits); idx[m] = argmax (lowest index on ties) */

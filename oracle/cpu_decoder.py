@@ -34,6 +34,7 @@ def load_library():
         lib.oc_w8a16.argtypes = [p, i, p, p, i, i, p]
         lib.oc_sdpa_int8.argtypes = [p, p, p, p, p, i, i, i, i, i, i, f, p]
         lib.oc_bf16_argmax.argtypes = [p, i, p, i, i, p, p]
+        lib.oc_bf16_logits.argtypes = [p, i, p, i, i, p]
         lib.oc_threads.restype = i
         _lib = lib
     return _lib
@@ -75,6 +76,67 @@ class CDecoder:
                           w.shape[1], _p(y))
         return y
 
+    def prefill_chunk(self, tokens, start, *, want_argmax=False):
+        """Feed consecutive tokens of sequence 0 at positions start..start+c-1
+        (c <= 8) through the layers in one pass over the weights.
+
+        Row r is the decode step of position start + r: the same arithmetic
+        and bf16 rounding points as ``step`` (every GEMV row is computed
+        independently), attention causal over positions <= start + r. Returns
+        the greedy next token after the last row when ``want_argmax``."""
+        w = self.w
+        toks = np.asarray(tokens).reshape(-1)
+        c = toks.shape[0]
+        if not 1 <= c <= 8:
+            raise ValueError("chunks of 1 to 8 tokens")
+        x = bf16_from_bits(w["embed_bits"][toks])
+        d = self.d
+        pos = np.arange(start, start + c)
+        for li, layer in enumerate(w["layers"]):
+            xn = round_bf16(ops.rms_norm(x, layer["in_norm"], self.eps))
+            qkv = round_bf16(self._w8(xn, layer["qkv_w"], layer["qkv_s"]))
+            q = qkv[:, : self.hq * d].reshape(c, self.hq, 1, d)
+            k = qkv[:, self.hq * d:(self.hq + self.hkv) * d].reshape(c, self.hkv, 1, d)
+            v = qkv[:, (self.hq + self.hkv) * d:].reshape(c, self.hkv, 1, d)
+            q = round_bf16(ops.rope(q, pos.reshape(c, 1, 1), d, self.theta))
+            k = round_bf16(ops.rope(k, pos.reshape(c, 1, 1), d, self.theta))
+            kq, ks = quantize_kv_symmetric(k[:, :, 0])
+            vq, vs = quantize_kv_symmetric(v[:, :, 0])
+            self.kq[li, 0, :, start:start + c] = kq.transpose(1, 0, 2)
+            self.ks[li, 0, :, start:start + c] = ks.T
+            self.vq[li, 0, :, start:start + c] = vq.transpose(1, 0, 2)
+            self.vs[li, 0, :, start:start + c] = vs.T
+            out = np.empty((c, self.hq, d), np.float32)
+            for r in range(c):
+                qr = np.ascontiguousarray(q[r, :, 0], np.float32)
+                self.lib.oc_sdpa_int8(_p(qr), _p(self.kq[li]), _p(self.ks[li].view(np.uint16)), _p(self.vq[li]),
+                                      _p(self.vs[li].view(np.uint16)), 1, self.hq, self.hkv, start + r + 1,
+                                      self.capacity, d, float(1.0 / np.sqrt(d)), _p(out[r]))
+            attn = round_bf16(out.reshape(c, self.hq * d))
+            o = round_bf16(self._w8(attn, layer["o_w"], layer["o_s"]))
+            x = round_bf16(x + o)
+            xn = round_bf16(ops.rms_norm(x, layer["post_norm"], self.eps))
+            g = round_bf16(self._affine(xn, layer["gate"]))
+            u = round_bf16(self._affine(xn, layer["up"]))
+            act = round_bf16(ops.swiglu(g, u))
+            x = round_bf16(x + round_bf16(self._affine(act, layer["down"])))
+        self.last_x = x
+        if not want_argmax:
+            return None
+        return self._head(x[-1:])[0]
+
+    def _head(self, x):
+        """RMSNorm + bf16 lm_head of rows x: greedy tokens (lowest index on
+        ties); the fp32 logits stay in ``last_logits`` for margin diagnostics."""
+        w = self.w
+        xn = np.ascontiguousarray(round_bf16(ops.rms_norm(x, w["final_norm"], self.eps)), np.float32)
+        head = w["head_bits"]
+        bsz = xn.shape[0]
+        logits = np.empty((bsz, head.shape[0]), np.float32)
+        self.lib.oc_bf16_logits(_p(xn), bsz, _p(head), head.shape[0], head.shape[1], _p(logits))
+        self.last_logits = logits
+        return np.argmax(logits, axis=-1).astype(np.int32)
+
     def step(self, tokens, position):
         """One decode step; returns the greedy next tokens [B]."""
         w = self.w
@@ -108,9 +170,4 @@ class CDecoder:
             act = round_bf16(ops.swiglu(g, u))
             x = round_bf16(x + round_bf16(self._affine(act, layer["down"])))
         self.last_x = x
-        xn = np.ascontiguousarray(round_bf16(ops.rms_norm(x, w["final_norm"], self.eps)), np.float32)
-        idx = np.empty(bsz, np.int32)
-        best = np.empty(bsz, np.float32)
-        head = w["head_bits"]
-        self.lib.oc_bf16_argmax(_p(xn), bsz, _p(head), head.shape[0], head.shape[1], _p(idx), _p(best))
-        return idx
+        return self._head(x)

@@ -199,6 +199,13 @@ __device__ __forceinline__ unsigned long long ld_slot(const void* addr) {
   return w;
 }
 
+// Uncached 32-bit load of a word other threads or launches may have written.
+__device__ __forceinline__ unsigned ld_volatile_u32(const unsigned* addr) {
+  unsigned v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
 // ------------------------------------------------- thread-block cluster (DSMEM)
 // Address of the same shared-memory offset in CTA `rank` of this cluster.
 __device__ __forceinline__ uint32_t cluster_map(uint32_t local, int rank) {

@@ -768,6 +768,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
     if (threadIdx.x == 0) s_epoch = *ar_seen + 1u;
     __syncthreads();
   }
+  bool gave_up = false;  // fused all-reduce: a wait of this thread ran out
   for (int idx = threadIdx.x; idx < own_pairs * M; idx += kNT) {
     const int pl = idx / M, m = idx - (idx / M) * M;
     const int P = (kv_fused ? 0 : part * ppc) + pl;
@@ -870,12 +871,24 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
               }
               const uint8_t* slot = p.ar_buf[p.ar_rank] + chan + static_cast<size_t>(q) * p.ar_np * 64 + col;
               unsigned long long w = ld_slot(slot);
-              if (static_cast<unsigned>(w >> 32) != epoch) {
-                const long long start = clock64();
-                while (static_cast<unsigned>((w = ld_slot(slot)) >> 32) != epoch) {
-                  if (clock64() - start > (1LL << 31)) {
-                    if (p.status) atomicOr(p.status, kStatusTimeout);
-                    break;
+              if (static_cast<unsigned>(w >> 32) != epoch && !gave_up) {
+                // once any wait of this or an earlier launch has run out (the
+                // status word persists in the workspace), every later wait is
+                // skipped: a dead peer costs one bound, not one per element
+                if (p.status && (ld_volatile_u32(p.status) & kStatusTimeout)) {
+                  gave_up = true;
+                } else {
+                  const long long start = clock64();
+                  while (static_cast<unsigned>((w = ld_slot(slot)) >> 32) != epoch) {
+                    if (clock64() - start > (1LL << 31)) {
+                      if (p.status) atomicOr(p.status, kStatusTimeout);
+                      gave_up = true;
+                      break;
+                    }
+                    if (p.status && (ld_volatile_u32(p.status) & kStatusTimeout)) {
+                      gave_up = true;
+                      break;
+                    }
                   }
                 }
               }

@@ -519,15 +519,18 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
 
 namespace {
 
+// Multiprocessor count of the current device (cached per device index: one
+// process may drive GPUs with different SM counts).
 int sdpa_sms() {
-  static int count = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
-      count = 148;
-  });
+  constexpr int kDevs = 64;
+  static int counts[kDevs] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  if (dev >= 0 && dev < kDevs && counts[dev] > 0) return counts[dev];
+  int count = 0;
+  if (dev < 0 || cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
+    count = 148;
+  if (dev >= 0 && dev < kDevs) counts[dev] = count;  // benign race: every writer stores the same value
   return count;
 }
 
@@ -596,7 +599,12 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   SB_REQUIRE(splits <= kMaxSplits, "at most 64 token splits");
   const int64_t bkv = batch * num_kv_heads;
   const size_t counters = kCounterBytes;
-  if (bkv > kMaxCounters) force_splits = 1;
+  // one arrival counter per (batch, kv head): more of them than the counter
+  // region holds run unsplit
+  if (bkv > kMaxCounters) {
+    SB_REQUIRE(force_splits <= 1, "a forced split count needs at most 32752 (batch x kv head) rows");
+    splits = 1;
+  }
   const size_t need = counters + static_cast<size_t>(bkv) * splits * G * kPartStride * sizeof(float);
   if (splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
     SB_REQUIRE(force_splits <= 0, "workspace too small for the requested split count");

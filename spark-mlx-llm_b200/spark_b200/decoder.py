@@ -32,13 +32,16 @@ import torch
 
 from . import quantize
 from . import tp as tensor_parallel
-from ._lib import check, lib, sb_linear_ex_desc
+from ._lib import SBError, check, lib, sb_linear_ex_desc
 
 __all__ = ["DecoderConfig", "SyntheticDecoder"]
 
 SB_WEIGHT_AFFINE4, SB_WEIGHT_AFFINE8, SB_WEIGHT_INT8_PC, SB_WEIGHT_BF16 = 0, 1, 2, 3
 SB_EPI_STORE, SB_EPI_RESID, SB_EPI_SWIGLU, SB_EPI_ROPE, SB_EPI_ARGMAX = 0, 1, 2, 3, 4
 BF16 = 0
+# device status word: the last 32-bit word of a workspace's 128 KiB counter
+# region (nonzero when a bounded device-side wait gave up)
+STATUS_WORD = 128 * 1024 // 4 - 1
 
 
 @dataclass(frozen=True)
@@ -140,10 +143,12 @@ class SyntheticDecoder:
             del wq, wk, wv
             layer["qkv_w"], layer["qkv_s"] = quantize.quantize_w8_per_channel(qkv)
             del qkv
+            # the checkpoint is quantized once (per-row scales over the full K);
+            # a tensor-parallel rank keeps its columns of the same codes
             wo = randn(cfg.hidden, cfg.num_heads * d, std=cfg.weight_std, key=base + 4)
-            wo = wo[:, sp.o_cols[0]:sp.o_cols[0] + sp.o_cols[1]].contiguous()
-            layer["o_w"], layer["o_s"] = quantize.quantize_w8_per_channel(wo)
-            del wo
+            o_w, layer["o_s"] = quantize.quantize_w8_per_channel(wo)
+            layer["o_w"] = o_w[:, sp.o_cols[0]:sp.o_cols[0] + sp.o_cols[1]].contiguous()
+            del wo, o_w
             for name, key in (("gate", 5), ("up", 6)):
                 w = randn(cfg.intermediate, cfg.hidden, std=cfg.weight_std, key=base + key)
                 w = rows(w, *sp.inter_rows)
@@ -400,11 +405,32 @@ class SyntheticDecoder:
         return graph
 
     def decode(self, steps):
-        """Replay the captured step ``steps`` times; returns generated tokens [batch, steps] (device)."""
+        """Replay the captured step ``steps`` times; returns generated tokens [batch, steps] (device).
+
+        Raises ``SBError`` when a bounded device-side wait gave up during these
+        steps (``check_status``); the tokens are then not returned."""
         if self.graph is None:
             self.capture()
         out = torch.empty((self.batch, steps), dtype=torch.int32, device=self.device)
         for i in range(steps):
             out[:, i] = self.tokens
             self.graph.replay()
+        self.check_status()
         return out
+
+    def check_status(self):
+        """Read (synchronizing) and clear the workspace status word.
+
+        A kernel whose bounded wait ran out (a tensor-parallel peer that stopped
+        posting its partial sums, or a copy that never landed) records the
+        timeout there and returns with incomplete outputs; the fused exchange
+        then skips every later wait. The tokens of such steps are invalid, so
+        this raises ``SBError`` (status SB_ETIMEOUT) after clearing the word.
+        ``decode`` calls it; callers driving ``step()`` themselves call it
+        after synchronizing."""
+        words = self.workspace[: 128 * 1024].view(torch.int32)
+        status = int(words[STATUS_WORD].item())
+        if status:
+            words[STATUS_WORD] = 0
+            raise SBError(f"decode step: a bounded device-side wait gave up (status {status:#x}); a "
+                          "tensor-parallel peer stopped responding - the tokens of these steps are invalid")

@@ -33,10 +33,12 @@ __all__ = [
     "QuantizedLinear",
     "RoPE",
     "SDPAConfig",
+    "PreparedW8",
     "W8A16PerChannelLinear",
     "dispatch_linear",
     "dispatch_qkv",
     "dispatch_sdpa",
+    "unpack_affine_w8",
 ]
 
 
@@ -120,6 +122,42 @@ class QuantizedLinear(torch.nn.Module):
         return AffineParameters.native(x, *AffineParameters.from_module(self))
 
 
+def unpack_affine_w8(layer, name, *, allow_fallback=False):
+    """Per-channel INT8 parameters of an MLX affine 8-bit layer.
+
+    Restates ``_unpack_affine_w8`` (``spark_mlx_llm/ops/linear.py:299-324``):
+    the layer must hold uint32-packed affine W8 (``weight [N, K/4]`` as
+    int32/uint32 words, ``scales``/``biases [N, K/G]``) written as "symmetric
+    in affine clothing" - every scale of a row equal, finite and positive, and
+    ``biases == -128 * scales`` (``conversion.py:585-592``). Returns
+    ``(weight int8 [N, K], scales float32 [N])``: the codes are the packed
+    bytes XOR 0x80 (code = int8 + 128), the scale is the row's repeated
+    scale. Raises ``ValueError`` for anything else, or returns ``None`` when
+    ``allow_fallback`` and only the symmetric/per-channel check fails.
+    Load-time work (torch ops on the weight's device), not the hot path.
+    """
+    weight, scales, biases = layer.weight, layer.scales, layer.biases
+    if weight.ndim != 2:
+        raise ValueError(f"{name}: QMV requires UINT32-packed affine W8 parameters")
+    n, packed_k = weight.shape
+    group = getattr(layer, "group_size", None)
+    if (getattr(layer, "mode", "affine") != "affine" or weight.dtype not in (torch.int32, torch.uint32)
+            or biases is None or not group or scales.ndim != 2
+            or tuple(scales.shape) != (n, packed_k * 4 // group) or tuple(biases.shape) != tuple(scales.shape)):
+        raise ValueError(f"{name}: QMV requires UINT32-packed affine W8 parameters")
+    s = scales.float()
+    b = biases.float()
+    ok = bool((torch.isfinite(s) & (s > 0)).all() & (s == s[:, :1]).all() & (b == -128 * s).all())
+    if not ok:
+        if allow_fallback:
+            return None
+        raise ValueError(f"{name}: QMV requires repeated positive per-channel scales and "
+                         "affine biases=-128*scales; groupwise/asymmetric W8 is unsupported")
+    words = weight.contiguous().view(torch.int32) ^ torch.tensor(-0x7F7F7F80, dtype=torch.int32,
+                                                                 device=weight.device)  # 0x80808080
+    return words.view(torch.int8).reshape(n, packed_k * 4).contiguous(), s[:, 0].contiguous()
+
+
 class W8A16PerChannelLinear(torch.nn.Module):
     """Signed INT8 weights with an FP32 scale per output row (ops/linear.py:413-476)."""
 
@@ -128,8 +166,35 @@ class W8A16PerChannelLinear(torch.nn.Module):
         self.register_buffer("weight", weight)
         self.register_buffer("scales", scales)
 
+    @classmethod
+    def from_affine(cls, layer, name="projection"):
+        """Build from an MLX affine W8 layer (the load-time conversion of
+        ``QuantizedProjections.prepare``, ``ops/linear.py:725-731``)."""
+        weight, scales = unpack_affine_w8(layer, name)
+        return cls(weight, scales)
+
     def forward(self, x):
         return ext.w8a16_per_channel(x, self.weight, self.scales)
+
+
+class PreparedW8:
+    """Derived INT8 buffers of an affine W8 layer, cached against the identity
+    of its source tensors (``W8A8QuantizedLinear.prepare_parameters``,
+    ``ops/linear.py:338-369``): repeated calls with the same ``weight``,
+    ``scales`` and ``biases`` objects return the cached pair; new source
+    tensors are validated and unpacked again."""
+
+    def __init__(self):
+        self._cache = None
+
+    def __call__(self, layer, name="projection"):
+        sources = (layer.weight, layer.scales, layer.biases)
+        cached = self._cache
+        if cached is not None and all(old is new for old, new in zip(cached[0], sources)):
+            return cached[1]
+        pair = unpack_affine_w8(layer, name)
+        self._cache = (sources, pair)
+        return pair
 
 
 class RoPE:

@@ -8,7 +8,7 @@ quantizer (``_rows``, :551-608). The outputs are written to
 restatement against them bit for bit.
 
 Run (where the reference tree is present):
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH
 The GPU box does not have the reference; it uses the committed ``.npz``.
 """
 
@@ -63,7 +63,7 @@ def write_tensor(directory, name, data, dtype, shape):
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="path of the reference project tree")
     args = parser.parse_args()
     conv = load_conversion(args.reference)
     rng = np.random.default_rng(20260101)

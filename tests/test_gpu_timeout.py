@@ -77,3 +77,31 @@ def test_fused_allreduce_wait_gives_up_and_reports_timeout():
     part = formats.round_bf16((acc * s.cpu().numpy().astype(np.float64)).astype(np.float32))
     expected = resid.float().cpu().numpy() + part
     assert_close(y.float().cpu().numpy(), expected, what="linear after a timed-out exchange")
+
+
+def test_tp_decoder_raises_when_a_peer_never_posts(monkeypatch):
+    """A tensor-parallel decoder whose peer never posts its o/down partial sums
+    raises instead of returning tokens, and within a few seconds: the first
+    wait that runs out sets the status word and every later wait (also in
+    later launches) is skipped. One process plays rank 0 of 2; the 'peer'
+    exchange buffer is a local buffer that nobody writes."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from spark_b200._lib import SBError, lib
+    from spark_b200.decoder import DecoderConfig, SyntheticDecoder
+
+    def local_exchange(self):
+        nbytes = lib().sb_tp_exchange_bytes(self.world, self.cfg.hidden)
+        self._fake_buffers = [torch.zeros(nbytes, dtype=torch.uint8, device=self.device) for _ in range(2)]
+        self.ar_buffers = [b.data_ptr() for b in self._fake_buffers]
+        self._own_buffer, self._mapped = None, []
+
+    monkeypatch.setattr(SyntheticDecoder, "_setup_exchange", local_exchange)
+    monkeypatch.setattr(SyntheticDecoder, "_allreduce", lambda self, t, op=None: None)
+    dec = SyntheticDecoder(DecoderConfig.small(num_layers=4), batch=1, capacity=32, rank=0, world=2, group=None)
+    dec.reset([1])
+    t0 = time.perf_counter()
+    with pytest.raises(SBError, match="gave up"):
+        dec.decode(3)
+    assert time.perf_counter() - t0 < 30.0
+    dec.check_status()  # cleared by the raise: no second report

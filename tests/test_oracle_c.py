@@ -82,3 +82,35 @@ def test_decoder_step_matches_numpy_oracle(lib):
         decisive = (top2[:, 1] - top2[:, 0]) > 1e-3
         assert np.all(c_next[decisive] == ndec.greedy(logits)[decisive])
         toks = c_next
+
+
+def test_prefill_chunk_equals_sequential_steps(lib):
+    """The oracle's chunked prompt pass (8 positions per weight pass) gives the
+    same cache, hidden state and greedy token as one decode step per position."""
+    rng = np.random.default_rng(5)
+    hidden, hq, hkv, d, inter, vocab = 256, 4, 2, 128, 512, 300
+
+    def aff(n, k):
+        return quant.quantize_affine_minmax((rng.standard_normal((n, k)) * 0.02).astype(np.float32), 64, 4)
+
+    layers = []
+    for _ in range(2):
+        qw, qs = quant.quantize_w8_per_channel((rng.standard_normal(((hq + 2 * hkv) * d, hidden)) * 0.02).astype(np.float32))
+        ow, os_ = quant.quantize_w8_per_channel((rng.standard_normal((hidden, hq * d)) * 0.02).astype(np.float32))
+        norm = (1 + 0.1 * rng.standard_normal(hidden)).astype(np.float32)
+        layers.append(dict(qkv_w=qw, qkv_s=qs, o_w=ow, o_s=os_, gate=aff(inter, hidden), up=aff(inter, hidden),
+                           down=aff(hidden, inter), in_norm=norm, post_norm=norm))
+    w = dict(layers=layers, embed_bits=formats.bf16_bits(rng.standard_normal((vocab, hidden)).astype(np.float32)),
+             head_bits=formats.bf16_bits((rng.standard_normal((vocab, hidden)) * 0.02).astype(np.float32)),
+             final_norm=np.ones(hidden, np.float32))
+    kw = dict(num_heads=hq, num_kv_heads=hkv, head_dim=d, rope_theta=1e6, eps=1e-6, group=64, capacity=32, batch=1)
+    seq, chunked = CDecoder(w, **kw), CDecoder(w, **kw)
+    prompt = rng.integers(0, vocab, 13)
+    for t in range(13):
+        tok = seq.step(prompt[t:t + 1], t)
+    for start in range(0, 13, 8):
+        got = chunked.prefill_chunk(prompt[start:start + 8], start, want_argmax=start + 8 >= 13)
+    assert int(got) == int(tok[0])
+    np.testing.assert_array_equal(chunked.last_x[-1], seq.last_x[0])
+    np.testing.assert_array_equal(chunked.kq, seq.kq)
+    np.testing.assert_array_equal(chunked.vs, seq.vs)

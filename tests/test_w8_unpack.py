@@ -1,0 +1,83 @@
+"""Load-time affine W8 -> per-channel INT8 unpack of the product
+(``spark_b200.dispatch.unpack_affine_w8``, restating
+``spark_mlx_llm/ops/linear.py:299-324``) against the reference's own W8
+checkpoint rows (``tests/golden/conversion_vectors.npz``, written by the
+reference's ``conversion.py``) and the oracle's unpack. CPU only: the unpack
+is torch bit arithmetic that runs on whatever device holds the weights.
+"""
+
+import os
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from oracle import formats, quant  # noqa: E402
+from spark_b200 import dispatch  # noqa: E402
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "conversion_vectors.npz")
+
+
+def _layer(words, s_bits, b_bits, group):
+    def bf16(bits):
+        return torch.from_numpy(np.asarray(bits, np.uint16).view(np.int16).copy()).view(torch.bfloat16)
+
+    return SimpleNamespace(weight=torch.from_numpy(np.asarray(words, np.uint32).view(np.int32).copy()),
+                           scales=bf16(s_bits), biases=bf16(b_bits), group_size=group, bits=8, mode="affine")
+
+
+@pytest.fixture(scope="module")
+def golden():
+    with np.load(GOLDEN) as data:
+        return {k: data[k] for k in data.files}
+
+
+def test_unpack_matches_reference_channel_rows(golden):
+    words = golden["rows_chan_weight"]
+    k = words.shape[1] * 4
+    group = k // golden["rows_chan_scales"].shape[1]
+    layer = _layer(words, golden["rows_chan_scales"], golden["rows_chan_biases"], group)
+    w_int8, scale = dispatch.unpack_affine_w8(layer, "o_proj")
+    # the reference converter's input codes come back bit for bit
+    np.testing.assert_array_equal(w_int8.numpy(), golden["chan_codes"])
+    np.testing.assert_array_equal(scale.numpy(), formats.bf16_from_bits(golden["chan_scale_bf16_bits"])[:, 0])
+    # and the oracle's restatement agrees
+    ow, os_ = quant.unpack_affine_w8(words, formats.bf16_from_bits(golden["rows_chan_scales"]),
+                                     formats.bf16_from_bits(golden["rows_chan_biases"]))
+    np.testing.assert_array_equal(w_int8.numpy(), ow)
+    np.testing.assert_array_equal(scale.numpy(), os_)
+
+
+def test_unpack_rejects_groupwise_and_allows_fallback(golden):
+    # the reference's W8 rows with one group's scale and bias changed: group-wise, not per-channel
+    words = golden["rows_w8_weight"]
+    group = words.shape[1] * 4 // golden["rows_w8_scales"].shape[1]
+    s = formats.bf16_from_bits(golden["rows_w8_scales"]).copy()
+    s[0, 1] *= 2
+    layer = _layer(words, formats.bf16_bits(s), formats.bf16_bits(-128 * s), group)
+    assert dispatch.unpack_affine_w8(_layer(words, golden["rows_w8_scales"], golden["rows_w8_biases"], group),
+                                     "qkv_proj") is not None
+    with pytest.raises(ValueError, match="groupwise/asymmetric"):
+        dispatch.unpack_affine_w8(layer, "qkv_proj")
+    assert dispatch.unpack_affine_w8(layer, "qkv_proj", allow_fallback=True) is None
+    bad = SimpleNamespace(weight=layer.weight.view(torch.int8), scales=layer.scales, biases=layer.biases,
+                          group_size=group, bits=8, mode="affine")
+    with pytest.raises(ValueError, match="UINT32-packed affine W8"):
+        dispatch.unpack_affine_w8(bad, "qkv_proj")
+
+
+def test_prepared_w8_caches_by_source_identity(golden):
+    words = golden["rows_chan_weight"]
+    group = words.shape[1] * 4 // golden["rows_chan_scales"].shape[1]
+    layer = _layer(words, golden["rows_chan_scales"], golden["rows_chan_biases"], group)
+    prep = dispatch.PreparedW8()
+    first = prep(layer)
+    assert prep(layer) is first
+    layer.weight = layer.weight.clone()  # new source tensor: unpacked again
+    second = prep(layer)
+    assert second is not first
+    assert torch.equal(second[0], first[0])
+    module = dispatch.W8A16PerChannelLinear.from_affine(layer)
+    assert module.weight.dtype == torch.int8 and module.scales.dtype == torch.float32
