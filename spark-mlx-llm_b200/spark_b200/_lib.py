@@ -78,6 +78,32 @@ class sb_linear_ex_desc(ctypes.Structure):
     ]
 
 
+class sb_step_layer(ctypes.Structure):
+    """Mirror of ``sb_step_layer`` (include/spark_b200_step.h)."""
+
+    _fields_ = [(name, ctypes.c_void_p) for name in
+                ("qkv", "qkv_scale", "o", "o_scale", "gateup", "down", "in_norm", "post_norm", "k_cache", "k_scale",
+                 "v_cache", "v_scale")]
+
+
+class sb_step_desc(ctypes.Structure):
+    """Mirror of ``sb_step_desc`` (include/spark_b200_step.h)."""
+
+    _fields_ = [
+        ("layers", ctypes.c_void_p), ("num_layers", ctypes.c_int), ("hidden", ctypes.c_int),
+        ("num_heads", ctypes.c_int), ("num_kv_heads", ctypes.c_int), ("head_dim", ctypes.c_int),
+        ("inter", ctypes.c_int), ("inter_total", ctypes.c_int), ("vocab", ctypes.c_int),
+        ("vocab_offset", ctypes.c_int), ("capacity", ctypes.c_int), ("rms_eps", ctypes.c_float),
+        ("rope_theta", ctypes.c_float), ("embed", ctypes.c_void_p), ("vocab_total", ctypes.c_int),
+        ("head", ctypes.c_void_p), ("final_norm", ctypes.c_void_p), ("tokens", ctypes.c_void_p),
+        ("positions", ctypes.c_void_p), ("x", ctypes.c_void_p), ("q", ctypes.c_void_p), ("kv_new", ctypes.c_void_p),
+        ("attn", ctypes.c_void_p), ("act", ctypes.c_void_p), ("argmax_key", ctypes.c_void_p),
+        ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t), ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+    ]
+
+
+
 # name -> (restype, argtypes); every symbol declared in include/*.h.
 SIGNATURES = {
     "sb_version": (_int, []),
@@ -147,6 +173,10 @@ SIGNATURES = {
     "sb_peer_buffer_open": (_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
     "sb_peer_buffer_close": (_int, [_c_void_p]),
     "sb_peer_buffer_free": (_int, [_c_void_p]),
+    # persistent decode step header
+    "sb_step_workspace_size": (_size, [ctypes.POINTER(sb_step_desc)]),
+    "sb_step_tile_bytes": (_int, [ctypes.POINTER(sb_step_desc), ctypes.POINTER(_i64)]),
+    "sb_step_run": (_int, [ctypes.POINTER(sb_step_desc), _c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -94,7 +94,8 @@ class SyntheticDecoder:
     ``torch.distributed`` process group used for the all-reduces (None for 1 GPU).
     """
 
-    def __init__(self, config, *, batch, capacity, device="cuda", seed=0, rank=0, world=1, group=None):
+    def __init__(self, config, *, batch, capacity, device="cuda", seed=0, rank=0, world=1, group=None,
+                 engine="auto"):
         cfg = config
         self.cfg = cfg
         self.batch = batch
@@ -113,9 +114,21 @@ class SyntheticDecoder:
         # TP: o/down partial sums meet inside the GEMV epilogue (NVLink peer
         # stores) instead of an NCCL all-reduce and a residual-add launch
         self.fused_allreduce = world > 1 and world <= 8
+        if engine not in ("auto", "step", "launches"):
+            raise ValueError("engine must be 'auto', 'step' or 'launches'")
         self._build_weights(seed)
         self._alloc_state()
         self.graph = None
+        # "step": the whole decode step is one persistent kernel (batch 1, one
+        # rank, spark_b200_step.h); "launches": one fused kernel per operator
+        if engine == "auto":
+            engine = "step" if (batch == 1 and world == 1 and cfg.head_dim == 128) else "launches"
+        self.engine = engine
+        self.stepper = None
+        if engine == "step":
+            from .step import StepStreams
+
+            self.stepper = StepStreams(self)
 
     # ------------------------------------------------------------------ weights
     def _build_weights(self, seed):
@@ -318,6 +331,13 @@ class SyntheticDecoder:
         cfg, b = self.cfg, self.batch
         L = lib()
         stream = torch.cuda.current_stream(self.device).cuda_stream
+        if self.engine == "step":
+            # one persistent kernel: every layer, the lm_head and the argmax key
+            self.stepper.run(stream)
+            if advance:
+                check(L.sb_decode_advance(_ptr(self.keys), _ptr(self.tokens), _ptr(self.positions), b, 1, stream),
+                      "advance")
+            return
         d = cfg.head_dim
         tp = self.world > 1
         check(L.sb_embed_rows(_ptr(self.embed), _ptr(self.tokens), _ptr(self.x), b, cfg.hidden, cfg.vocab, stream),
@@ -358,6 +378,8 @@ class SyntheticDecoder:
 
     def kernels_per_step(self):
         """Number of this library's kernel launches in one ``step()``."""
+        if self.engine == "step":
+            return 2  # the decode-step kernel + the token/position advance
         per_layer = (5 if self.fused_append else 6) + (2 if self.world > 1 and not self.fused_allreduce else 0)
         return 1 + self.cfg.num_layers * per_layer + 2
 
@@ -430,6 +452,9 @@ class SyntheticDecoder:
         after synchronizing."""
         words = self.workspace[: 128 * 1024].view(torch.int32)
         status = int(words[STATUS_WORD].item())
+        if self.stepper is not None:
+            status |= self.stepper.status()
+            self.stepper.clear_status()
         if status:
             words[STATUS_WORD] = 0
             raise SBError(f"decode step: a bounded device-side wait gave up (status {status:#x}); a "
