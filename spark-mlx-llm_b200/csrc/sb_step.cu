@@ -43,7 +43,7 @@
 namespace sb {
 namespace step {
 
-constexpr int kConsumers = 12;               // consumer warps per CTA
+constexpr int kConsumers = 11;               // consumer warps per CTA (+1 producer: 384 threads at <= 160 registers)
 constexpr int kConsumerThreads = kConsumers * 32;
 constexpr int kThreads = kConsumerThreads + 32;  // + the producer warp
 constexpr int kMaxSlots = 16;                // ring slots (upper bound)
@@ -836,7 +836,7 @@ __device__ void produce_op(const Params& p, const Smem& s, const Stream& st, con
   }
 }
 
-__global__ void __maxnreg__(152) step_kernel(const __grid_constant__ Params p) {
+__global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   Smem s;
@@ -1089,8 +1089,25 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(attr_once, [&] {
     attr_err = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+    if (attr_err == cudaSuccess)
+      attr_err = cudaFuncSetAttribute(step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared);
   });
   if (attr_err != cudaSuccess) return fail(SB_ECUDA, std::string("step kernel attribute: ") + cudaGetErrorString(attr_err));
+  {
+    // every CTA must be resident at once (grid-wide joins): one per SM
+    int per_sm = 0;
+    cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, step_kernel, kThreads, smem);
+    if (oe != cudaSuccess || per_sm < 1) {
+      cudaFuncAttributes fa{};
+      cudaFuncGetAttributes(&fa, step_kernel);
+      return fail(SB_ECUDA, "decode step kernel does not fit on an SM (" + std::to_string(per_sm) +
+                                " per SM; " + std::to_string(fa.numRegs) + " registers x " +
+                                std::to_string(kThreads) + " threads, max threads " +
+                                std::to_string(fa.maxThreadsPerBlock) + ", " + std::to_string(smem) +
+                                " B dynamic + " + std::to_string(fa.sharedSizeBytes) + " B static shared memory)");
+    }
+  }
   // the arrival counter starts at zero for every step
   cudaError_t err = cudaMemsetAsync(d->workspace, 0, 4, as_stream(stream));
   if (err != cudaSuccess) return fail(SB_ECUDA, std::string("step counter reset: ") + cudaGetErrorString(err));
