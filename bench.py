@@ -563,7 +563,9 @@ def main():
     from spark_b200.decoder import DecoderConfig, SyntheticDecoder
 
     cfg = DecoderConfig(num_layers=args.layers)
-    capacity = args.prompt + args.warmup + 2 * args.steps + 16
+    # KV positions used after the prompt: the digest run (restarted from the
+    # post-prompt state) or warm-up + timed + end-to-end steps, whichever is longer
+    capacity = args.prompt + max(args.digest_steps, args.warmup + 2 * args.steps) + 16
     dec = SyntheticDecoder(cfg, batch=args.batch, capacity=capacity, device=device, seed=0, rank=rank, world=world,
                            group=group)
     gen = torch.Generator().manual_seed(0)

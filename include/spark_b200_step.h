@@ -44,8 +44,10 @@
  * Conventions as spark_b200.h: device pointers, caller-owned buffers, a status
  * code, no allocation, no synchronization. The workspace (sb_step_workspace_size
  * bytes) must be zero-filled before the first launch; launches leave it ready
- * for the next one. Bounded device-side waits: a wait that gives up sets the
- * status word (uint32 index 1 of the workspace) and the kernel returns early.
+ * for the next one. Status word (uint32 index 1 of the workspace, sticky until
+ * the caller clears it): bit 0 - a bounded device-side wait gave up and the
+ * kernel returned early; bit 1 - positions[0] was outside [0, capacity), so
+ * the step did nothing (no cache row is ever written out of bounds).
  */
 #ifndef SPARK_B200_STEP_H
 #define SPARK_B200_STEP_H
@@ -80,7 +82,7 @@ typedef struct sb_step_desc {
   int num_layers;
   int hidden;     /* multiple of 512 */
   int num_heads;  /* this rank's query heads */
-  int num_kv_heads; /* this rank's KV heads; num_heads / num_kv_heads in {1, 2, 4, 8} */
+  int num_kv_heads; /* this rank's KV heads; num_heads / num_kv_heads in {1, 2, 4} */
   int head_dim;   /* 128 */
   int inter;      /* this rank's intermediate rows (multiple of 16) */
   int inter_total; /* all ranks' intermediate size (down K), multiple of 512 */
@@ -105,7 +107,14 @@ typedef struct sb_step_desc {
   size_t workspace_bytes;
   int world;   /* tensor-parallel degree (1 in this build) */
   int rank;
+  /* Optional (NULL = off): per-CTA timestamps (globaltimer, ns) of every
+   * join between operators, [grid CTAs][sb_step_trace_slots][2] uint64 -
+   * arrival (this CTA's operator done) and release (all CTAs arrived). */
+  unsigned long long* trace;
 } sb_step_desc;
+
+/* Join slots per CTA in sb_step_desc.trace (5 per layer + the lm_head + 1). */
+int sb_step_trace_slots(int num_layers);
 
 /* Bytes of the workspace for `desc` (0 if the shape is unsupported). */
 size_t sb_step_workspace_size(const sb_step_desc* desc);

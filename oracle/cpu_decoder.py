@@ -137,13 +137,32 @@ class CDecoder:
         self.last_logits = logits
         return np.argmax(logits, axis=-1).astype(np.int32)
 
+    def layer(self, li, x, position):
+        """Decoder layer ``li`` for hidden states x [B, H] (bf16 values) at
+        ``position``: appends the new K/V rows to the cache and returns the
+        layer's output residual stream (the loop body of ``step``)."""
+        return self._layers(x, position, li, li + 1)
+
+    def head(self, x):
+        """Final RMSNorm + lm_head + greedy argmax of hidden states x [B, H]
+        (logits kept in ``last_logits``)."""
+        self.last_x = x
+        return self._head(x)
+
     def step(self, tokens, position):
         """One decode step; returns the greedy next tokens [B]."""
         w = self.w
         x = bf16_from_bits(w["embed_bits"][np.asarray(tokens)])
+        x = self._layers(x, position, 0, len(w["layers"]))
+        self.last_x = x
+        return self._head(x)
+
+    def _layers(self, x, position, l0, l1):
+        w = self.w
         bsz = x.shape[0]
         d = self.d
-        for li, layer in enumerate(w["layers"]):
+        for li in range(l0, l1):
+            layer = w["layers"][li]
             xn = round_bf16(ops.rms_norm(x, layer["in_norm"], self.eps))
             qkv = round_bf16(self._w8(xn, layer["qkv_w"], layer["qkv_s"]))
             q = qkv[:, : self.hq * d].reshape(bsz, self.hq, 1, d)
@@ -169,5 +188,4 @@ class CDecoder:
             u = round_bf16(self._affine(xn, layer["up"]))
             act = round_bf16(ops.swiglu(g, u))
             x = round_bf16(x + round_bf16(self._affine(act, layer["down"])))
-        self.last_x = x
-        return self._head(x)
+        return x

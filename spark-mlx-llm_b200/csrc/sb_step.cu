@@ -50,10 +50,12 @@ constexpr int kMaxSlots = 16;                // ring slots (upper bound)
 constexpr int kPartSlots = 64;               // per-tile partial slots
 constexpr int kRbSlots = 128;                // row-block completion counters
 constexpr int kMaxK = 10240;                 // staged activation values
+constexpr int kMaxHidden = 4096;             // residual stream kept in shared memory
 constexpr int kMaxGroups = kMaxK / 64;
 constexpr int kChunks = 8;                   // K chunks of o/down/lm_head (tensor-parallel unit)
-constexpr int kAttnChunk = 128;              // tokens per attention work item
+constexpr int kAttnChunk = 32;               // tokens per attention work item (one warp)
 constexpr int kMaxLayers = 128;
+constexpr unsigned kStatusRange = 2u;        // status bit: position outside the KV cache
 
 // shared-memory layout (offsets from a 1024-byte aligned base)
 constexpr int kOffBars = 0;            // full[16], empty[16]
@@ -62,9 +64,14 @@ constexpr int kOffReady = 768;         // u32 [64]: next tile index allowed into
 constexpr int kOffZero = 1024;         // 256 zero bytes
 constexpr int kOffMisc = 1280;         // abort, rms, key, warp sums
 constexpr int kOffMeta = 2048;         // float2 [kMaxGroups] (O, X) per staged group
-constexpr int kOffPart = kOffMeta + kMaxGroups * 8;               // float [64][32]
+constexpr int kOffXres = ((kOffMeta + kMaxGroups * 8 + 255) / 256) * 256;  // bf16 [kMaxHidden] residual stream
+constexpr int kOffPart = kOffXres + kMaxHidden * 2;                // float [64][32] (lm_head partials)
 constexpr int kOffXs = kOffPart + kPartSlots * 32 * 4;             // staged activations
 constexpr int kOffRing = ((kOffXs + kMaxK * 2 + 1023) / 1024) * 1024;
+// attention scratch per warp (aliases part + xs, unused during attention):
+// q of the G heads as fp16 [4][128], then the new K/V row / probabilities
+constexpr int kAttnWarpBytes = 2048;
+static_assert(kOffPart + kConsumers * kAttnWarpBytes <= kOffRing, "attention scratch");
 
 struct Misc {
   int abort;
@@ -115,13 +122,20 @@ struct Params {
   unsigned long long* keys;
   unsigned* sync;     // workspace word 0: grid arrival counter
   unsigned* status;   // workspace word 1
-  unsigned* gcount;   // row-block counters of split row blocks
+  unsigned* gcount;   // lm_head: counters of row blocks split between CTAs
   unsigned* acount;   // attention per-KV-head counters
-  float* gpart;       // split row-block partials [rb][kChunks][32]
+  float* gpart;       // lm_head: split row-block partials [rb][kChunks][32]
   float* apart;       // attention partials [kv head][chunk][G][132]
+  // per-chunk partial sums of the projections (L2): [row][8] (gate/up: [row][2][8])
+  float* pqkv;
+  float* po;
+  float* pgu;
+  float* pdn;
   int attn_max_chunks;
   Stream sq, so, sgu, sdn, slm;
   int slot_bytes, slots;
+  unsigned long long* trace;  // optional [CTA][trace_slots][2] globaltimer stamps
+  int trace_slots;
 };
 
 // ------------------------------------------------------------- small helpers
@@ -184,9 +198,20 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const P
 // Grid-wide join between operators: all consumer threads of the CTA finish
 // the operator, thread 0 adds this CTA's arrival, waits (bounded) until every
 // CTA has arrived `target` times in total, and releases the consumers.
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 __device__ void grid_join(const Params& p, Misc* misc, unsigned target) {
   named_sync();
   if (threadIdx.x == 0) {
+    const unsigned slot = target / gridDim.x - 1;
+    unsigned long long* tr = (p.trace != nullptr && static_cast<int>(slot) < p.trace_slots)
+                                 ? p.trace + (static_cast<size_t>(blockIdx.x) * p.trace_slots + slot) * 2
+                                 : nullptr;
+    if (tr) tr[0] = global_ns();
     __threadfence();
     atomicAdd(p.sync, 1u);
     if (!*reinterpret_cast<volatile int*>(&misc->abort)) {
@@ -200,6 +225,7 @@ __device__ void grid_join(const Params& p, Misc* misc, unsigned target) {
       }
     }
     __threadfence();
+    if (tr) tr[1] = global_ns();
   }
   named_sync();
 }
@@ -350,21 +376,19 @@ __device__ __forceinline__ void w4_tile(const uint8_t* tile, int ngroups, const 
 }
 
 // ---------------------------------------------------------------- staging
-// Sum of squares of x[0..n) over the consumer threads in a fixed order, then
-// r = 1/sqrt(mean + eps) in misc->rms (every CTA computes the same value).
-__device__ void rms_stat(const __nv_bfloat16* x, int n, float eps, Misc* misc, bool from_l2) {
+__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
+  return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(a))) |
+         (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(b))) << 16);
+}
+__device__ __forceinline__ uint32_t pack_b2(float a, float b) {
+  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a))) |
+         (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(b))) << 16);
+}
+
+// RMS of the residual from the per-thread sums of squares: fixed reduction
+// order, so every CTA computes the same value.
+__device__ void finish_rms(float ss, int n, float eps, Misc* misc) {
   const int tid = threadIdx.x;
-  float ss = 0.f;
-  for (int v = tid; v < n / 8; v += kConsumerThreads) {
-    const uint4 w = from_l2 ? ldcg16(x + v * 8) : *reinterpret_cast<const uint4*>(x + v * 8);
-    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const float a = bf16_lo(u[i]), b = bf16_hi(u[i]);
-      ss = fmaf(a, a, ss);
-      ss = fmaf(b, b, ss);
-    }
-  }
   ss = warp_sum(ss);
   if ((tid & 31) == 0) misc->warp_ss[tid >> 5] = ss;
   named_sync();
@@ -376,91 +400,102 @@ __device__ void rms_stat(const __nv_bfloat16* x, int n, float eps, Misc* misc, b
   named_sync();
 }
 
-// 8 activation values of vector v (optionally RMS-normalised and rounded to bf16)
-__device__ __forceinline__ void load8(const __nv_bfloat16* x, const __nv_bfloat16* w, float r, int v, bool from_l2,
+// Residual stream <- embedding row (layer 0), with its RMS.
+__device__ void load_residual(const __nv_bfloat16* src, int n, float eps, __nv_bfloat16* xres, Misc* misc) {
+  float ss = 0.f;
+  for (int v = threadIdx.x; v < n / 8; v += kConsumerThreads) {
+    const uint4 w = *reinterpret_cast<const uint4*>(src + v * 8);
+    *reinterpret_cast<uint4*>(xres + v * 8) = w;
+    const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = bf16_lo(u[i]), b = bf16_hi(u[i]);
+      ss = fmaf(a, a, ss);
+      ss = fmaf(b, b, ss);
+    }
+  }
+  finish_rms(ss, n, eps, misc);
+}
+
+// Residual stream += a row-split projection: x[n] = bf16(x[n] + bf16(S)) with
+// S = (sum over the 8 K chunks, in chunk order, of P[n][c]) (* scale[n]), then
+// the RMS of the new stream. Every CTA folds the same partials identically.
+__device__ void fold_residual(const float* P, const float* scale, int n, float eps, __nv_bfloat16* xres, Misc* misc) {
+  float ss = 0.f;
+  for (int r = threadIdx.x; r < n; r += kConsumerThreads) {
+    const float4 a = __ldcg(reinterpret_cast<const float4*>(P + r * 8));
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(P + r * 8 + 4));
+    float acc = ((((((a.x + a.y) + a.z) + a.w) + b.x) + b.y) + b.z) + b.w;
+    if (scale != nullptr) acc *= scale[r];
+    const float x = bfr(__bfloat162float(xres[r]) + bfr(acc));
+    xres[r] = __float2bfloat16_rn(x);
+    ss = fmaf(x, x, ss);
+  }
+  named_sync();  // xres complete before anyone stages from it
+  finish_rms(ss, n, eps, misc);
+}
+
+// 8 values of word v of the residual, RMS-normalised with weight w and rounded to bf16.
+__device__ __forceinline__ void norm8(const __nv_bfloat16* xres, const __nv_bfloat16* w, float r, int v,
                                       float (&f)[8]) {
-  const uint4 xv = from_l2 ? ldcg16(x + v * 8) : *reinterpret_cast<const uint4*>(x + v * 8);
+  const uint4 xv = *reinterpret_cast<const uint4*>(xres + v * 8);
+  const uint4 wv = *reinterpret_cast<const uint4*>(w + v * 8);
   const uint32_t u[4] = {xv.x, xv.y, xv.z, xv.w};
-  if (w != nullptr) {
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + v * 8);
-    const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+  const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      f[2 * i] = bfr(bf16_lo(u[i]) * r * bf16_lo(wu[i]));
-      f[2 * i + 1] = bfr(bf16_hi(u[i]) * r * bf16_hi(wu[i]));
-    }
-  } else {
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = bfr(bf16_lo(u[i]) * r * bf16_lo(wu[i]));
+    f[2 * i + 1] = bfr(bf16_hi(u[i]) * r * bf16_hi(wu[i]));
+  }
+}
+// 8 values of word v of a bf16 vector in global memory (written by other CTAs).
+__device__ __forceinline__ void plain8(const __nv_bfloat16* x, int v, float (&f)[8]) {
+  const uint4 xv = ldcg16(x + v * 8);
+  const uint32_t u[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      f[2 * i] = bf16_lo(u[i]);
-      f[2 * i + 1] = bf16_hi(u[i]);
-    }
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = bf16_lo(u[i]);
+    f[2 * i + 1] = bf16_hi(u[i]);
   }
 }
 
-__device__ __forceinline__ uint32_t pack_h2(float a, float b) {
-  return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(a))) |
-         (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(b))) << 16);
+// W8 tiles read fp16 activations in natural order.
+__device__ __forceinline__ void put_w8(uint8_t* xs, int v, const float (&f)[8]) {
+  *reinterpret_cast<uint4*>(xs + v * 16) =
+      make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]), pack_h2(f[6], f[7]));
 }
-__device__ __forceinline__ uint32_t pack_b2(float a, float b) {
-  return static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a))) |
-         (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(b))) << 16);
+// BF16 tiles read bf16 activations in natural order.
+__device__ __forceinline__ void put_bf16(uint8_t* xs, int v, const float (&f)[8]) {
+  *reinterpret_cast<uint4*>(xs + v * 16) =
+      make_uint4(pack_b2(f[0], f[1]), pack_b2(f[2], f[3]), pack_b2(f[4], f[5]), pack_b2(f[6], f[7]));
 }
-
-// Stage x[0..n) for W8 tiles: fp16 in natural order.
-__device__ void stage_w8(const __nv_bfloat16* x, const __nv_bfloat16* w, int n, bool from_l2, float r, uint8_t* xs) {
-  for (int v = threadIdx.x; v < n / 8; v += kConsumerThreads) {
-    float f[8];
-    load8(x, w, r, v, from_l2, f);
+// W4 tiles read per 8-value word [bf16 (x0,x4) | bf16 (x2,x6) | fp16 (x1,x5) |
+// fp16 (x3,x7)] and per group of 64 the offset sum O = 128*sum(even) +
+// 64*sum(odd) and X = sum(x). Called by all consumer threads for words
+// v0 + tid (v0 a multiple of kConsumerThreads, itself a multiple of 8, so the 8
+// words of a group sit in 8 consecutive lanes); `valid` is false past the end.
+__device__ __forceinline__ void put_w4(uint8_t* xs, float2* om, int v, bool valid, const float (&f)[8]) {
+  float O = 0.f, X = 0.f;
+  if (valid) {
+    float h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = (i & 1) ? __half2float(__float2half_rn(f[i])) : f[i];
     *reinterpret_cast<uint4*>(xs + v * 16) =
-        make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]), pack_h2(f[6], f[7]));
-  }
-}
-
-// Stage x[0..n) for BF16 tiles: bf16 in natural order.
-__device__ void stage_bf16(const __nv_bfloat16* x, const __nv_bfloat16* w, int n, bool from_l2, float r,
-                           uint8_t* xs) {
-  for (int v = threadIdx.x; v < n / 8; v += kConsumerThreads) {
-    float f[8];
-    load8(x, w, r, v, from_l2, f);
-    *reinterpret_cast<uint4*>(xs + v * 16) =
-        make_uint4(pack_b2(f[0], f[1]), pack_b2(f[2], f[3]), pack_b2(f[4], f[5]), pack_b2(f[6], f[7]));
-  }
-}
-
-// Stage x[0..n) for W4 tiles: per 8-value word [bf16 (x0,x4) | bf16 (x2,x6) |
-// fp16 (x1,x5) | fp16 (x3,x7)], and per group of 64 the offset sum
-// O = 128*sum(even) + 64*sum(odd) and X = sum(x) (fixed reduction order).
-__device__ void stage_w4(const __nv_bfloat16* x, const __nv_bfloat16* w, int n, bool from_l2, float r, uint8_t* xs,
-                         float2* om) {
-  // kConsumerThreads is a multiple of 8, so the 8 words of a group sit in 8 consecutive lanes
-  for (int v0 = 0; v0 < n / 8; v0 += kConsumerThreads) {
-    const int v = v0 + threadIdx.x;
-    float O = 0.f, X = 0.f;
-    if (v < n / 8) {
-      float f[8];
-      load8(x, w, r, v, from_l2, f);
-      float h[8];
+        make_uint4(pack_b2(f[0], f[4]), pack_b2(f[2], f[6]), pack_h2(f[1], f[5]), pack_h2(f[3], f[7]));
+    O = 128.f * (((h[0] + h[2]) + h[4]) + h[6]) + 64.f * (((h[1] + h[3]) + h[5]) + h[7]);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) h[i] = (i & 1) ? __half2float(__float2half_rn(f[i])) : f[i];
-      *reinterpret_cast<uint4*>(xs + v * 16) =
-          make_uint4(pack_b2(f[0], f[4]), pack_b2(f[2], f[6]), pack_h2(f[1], f[5]), pack_h2(f[3], f[7]));
-      O = 128.f * (((h[0] + h[2]) + h[4]) + h[6]) + 64.f * (((h[1] + h[3]) + h[5]) + h[7]);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) X += f[i];
-    }
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) {
-      O += __shfl_xor_sync(0xffffffffu, O, o);
-      X += __shfl_xor_sync(0xffffffffu, X, o);
-    }
-    if (v < n / 8 && (v & 7) == 0) om[v >> 3] = make_float2(O, X);
+    for (int i = 0; i < 8; ++i) X += f[i];
   }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    O += __shfl_xor_sync(0xffffffffu, O, o);
+    X += __shfl_xor_sync(0xffffffffu, X, o);
+  }
+  if (valid && (v & 7) == 0) om[v >> 3] = make_float2(O, X);
 }
 
 // -------------------------------------------------------------- operators
 enum Kind : int { K_W8 = 0, K_W4 = 1, K_W4PAIR = 2, K_BF16 = 3 };
-enum Epi : int { E_QKV = 0, E_OPROJ = 1, E_SWIGLU = 2, E_DOWN = 3, E_ARGMAX = 4 };
 
 struct Smem {
   uint64_t* full;
@@ -470,83 +505,30 @@ struct Smem {
   const uint8_t* zero;
   Misc* misc;
   float2* om;
+  __nv_bfloat16* xres;
   float* part;
   uint8_t* xs;
   uint8_t* ring;
 };
 
-// Epilogue of a finished row block: lane r < rows holds the chunk-ordered sum of row r.
-template <int EPI>
-__device__ void finish_rows(const Params& p, const Layer& L, int rb, float total, int lane, int pos, Misc* misc) {
-  if constexpr (EPI == E_QKV) {
-    // rows g and g+8 of the block are dims d and d+64 of one head (d = 8*(rb%8) + g)
-    const int hd = rb >> 3, i0 = (rb & 7) * 8;
-    const float s = L.qkv_scale[rb * 16 + (lane & 15)];
-    const float v = bfr(total * s);
-    const float partner = __shfl_down_sync(0xffffffffu, v, 8);
-    if (lane < 8) {
-      const int d = i0 + lane;
-      float a = v, b = partner;
-      if (hd < p.heads + p.kv_heads) {
-        const float angle = static_cast<float>(pos) * p.inv_freq[d];
-        float sn, cs;
-        sincosf(angle, &sn, &cs);
-        const float ra = a * cs - b * sn;
-        const float rb2 = b * cs + a * sn;
-        a = ra;
-        b = rb2;
-      }
-      __nv_bfloat16* dst;
-      if (hd < p.heads) dst = p.q + hd * 128;
-      else if (hd < p.heads + p.kv_heads) dst = p.kv_new + (hd - p.heads) * 128;
-      else dst = p.kv_new + (p.kv_heads + hd - p.heads - p.kv_heads) * 128;
-      dst[d] = __float2bfloat16_rn(a);
-      dst[d + 64] = __float2bfloat16_rn(b);
-    }
-  } else if constexpr (EPI == E_OPROJ) {
-    if (lane < 16) {
-      const int n = rb * 16 + lane;
-      const float v = bfr(total * L.o_scale[n]);
-      p.x[n] = __float2bfloat16_rn(ldcg_bf(p.x + n) + v);
-    }
-  } else if constexpr (EPI == E_SWIGLU) {
-    const float v = bfr(total);
-    const float up = __shfl_down_sync(0xffffffffu, v, 16);
-    if (lane < 16) {
-      const float silu = v / (1.0f + expf(-v));
-      p.act[rb * 16 + lane] = __float2bfloat16_rn(silu * up);
-    }
-  } else if constexpr (EPI == E_DOWN) {
-    if (lane < 16) {
-      const int n = rb * 16 + lane;
-      p.x[n] = __float2bfloat16_rn(ldcg_bf(p.x + n) + bfr(total));
-    }
-  } else {  // E_ARGMAX
-    const int n = rb * 16 + lane;
-    unsigned long long key = (lane < 16 && n < p.vocab) ? argmax_key(total, n + p.vocab_offset) : 0ull;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
-      key = k2 > key ? k2 : key;
-    }
-    if (lane == 0 && key) atomicMax(&misc->key, key);
-  }
+// Tile range [t0, t1) of this CTA in a stream of T tiles (balanced, contiguous).
+__device__ __forceinline__ void cta_range(int T, int& t0, int& t1) {
+  t0 = static_cast<int>((static_cast<long long>(T) * blockIdx.x) / gridDim.x);
+  t1 = static_cast<int>((static_cast<long long>(T) * (blockIdx.x + 1)) / gridDim.x);
 }
 
-// One operator over this CTA's share of a weight stream.
-template <int KIND, int EPI>
-__device__ void run_op(const Params& p, const Layer& L, const Smem& s, const Stream& st, const uint8_t* stream,
-                       uint32_t& seq, int pos) {
+// One projection over this CTA's share of its weight stream: every tile's
+// per-row partial sums go to P[row * pstride + matrix * 8 + chunk] in L2 (the
+// consumer of the projection sums the chunks in order). Tiles are taken
+// round-robin by the consumer warps in stream order (the ring order).
+template <int KIND>
+__device__ void run_partials(const Params& p, const Smem& s, const Stream& st, bool chunk_major, float* P,
+                             int pstride, int chunk0, uint32_t& seq) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int W = gridDim.x, cta = blockIdx.x;
   const int T = st.rbs * st.chunks;
-  const int t0 = static_cast<int>((static_cast<long long>(T) * cta) / W);
-  const int t1 = static_cast<int>((static_cast<long long>(T) * (cta + 1)) / W);
-  constexpr int kRows = (KIND == K_W4PAIR) ? 32 : 16;
-  // reset the partial-slot gates for this operator
-  for (int i = threadIdx.x; i < kPartSlots; i += kConsumerThreads) s.ready[i] = i;
-  named_sync();
-  const int rb_first = t0 / max(st.chunks, 1);
+  int t0, t1;
+  cta_range(T, t0, t1);
+  const int g = lane >> 2;
   for (int t = t0; t < t1; ++t) {
     const uint32_t q = seq + static_cast<uint32_t>(t - t0);
     if (static_cast<int>(q % kConsumers) != warp) continue;
@@ -554,12 +536,11 @@ __device__ void run_op(const Params& p, const Layer& L, const Smem& s, const Str
     const int slot = static_cast<int>(q % static_cast<uint32_t>(p.slots));
     if (!wait_bar(s.full + slot, (q / static_cast<uint32_t>(p.slots)) & 1u, p, s.misc)) break;
     const uint8_t* tile = s.ring + static_cast<size_t>(slot) * p.slot_bytes;
-    const int rb = t / st.chunks, ch = t % st.chunks;
+    const int rb = chunk_major ? t % st.rbs : t / st.chunks;
+    const int ch = chunk_major ? t / st.rbs : t % st.chunks;
     float vals[2][2];
     if constexpr (KIND == K_W8) {
       w8_tile(tile, s.xs + ch * st.ck * 2, st.ck / 32, lane, vals[0][0], vals[0][1]);
-    } else if constexpr (KIND == K_BF16) {
-      bf16_tile(tile, s.xs + ch * st.ck * 2, st.ck / 16, lane, vals[0][0], vals[0][1]);
     } else if constexpr (KIND == K_W4) {
       float o[1][2];
       w4_tile<1>(tile, st.ck, s.xs + ch * st.ck * 128, s.om + ch * st.ck, s.zero, lane, o);
@@ -568,6 +549,43 @@ __device__ void run_op(const Params& p, const Layer& L, const Smem& s, const Str
     } else {
       w4_tile<2>(tile, st.ck, s.xs + ch * st.ck * 128, s.om + ch * st.ck, s.zero, lane, vals);
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(s.empty + slot);
+    if ((lane & 3) == 0) {
+      float* out = P + static_cast<size_t>(rb * 16 + g) * pstride + chunk0 + ch;
+      out[0] = vals[0][0];
+      out[8 * pstride] = vals[0][1];
+      if constexpr (KIND == K_W4PAIR) {
+        out[8] = vals[1][0];
+        out[8 * pstride + 8] = vals[1][1];
+      }
+    }
+  }
+  seq += static_cast<uint32_t>(t1 - t0);
+}
+
+// lm_head + greedy argmax: the warp that completes a row block sums its chunk
+// partials in chunk order; a block split between CTAs is finished by the CTA
+// that brings its global counter to the chunk count.
+__device__ void run_lm(const Params& p, const Smem& s, uint32_t& seq) {
+  const Stream& st = p.slm;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int T = st.rbs * st.chunks;
+  int t0, t1;
+  cta_range(T, t0, t1);
+  for (int i = threadIdx.x; i < kPartSlots; i += kConsumerThreads) s.ready[i] = i;
+  named_sync();
+  const int rb_first = t0 / st.chunks;
+  for (int t = t0; t < t1; ++t) {
+    const uint32_t q = seq + static_cast<uint32_t>(t - t0);
+    if (static_cast<int>(q % kConsumers) != warp) continue;
+    if (*reinterpret_cast<volatile int*>(&s.misc->abort)) break;
+    const int slot = static_cast<int>(q % static_cast<uint32_t>(p.slots));
+    if (!wait_bar(s.full + slot, (q / static_cast<uint32_t>(p.slots)) & 1u, p, s.misc)) break;
+    const uint8_t* tile = s.ring + static_cast<size_t>(slot) * p.slot_bytes;
+    const int rb = t / st.chunks, ch = t % st.chunks;
+    float og, oh;
+    bf16_tile(tile, s.xs + ch * st.ck * 2, st.ck / 16, lane, og, oh);
     __syncwarp();
     if (lane == 0) mbar_arrive(s.empty + slot);
     // partials of this tile into its slot (after the slot's previous tile was consumed)
@@ -585,18 +603,12 @@ __device__ void run_op(const Params& p, const Layer& L, const Smem& s, const Str
     }
     __syncwarp();
     float* part = s.part + ps * 32;
-    const int g = lane >> 2;
     if ((lane & 3) == 0) {
-      part[g] = vals[0][0];
-      part[g + 8] = vals[0][1];
-      if constexpr (kRows == 32) {
-        part[16 + g] = vals[1][0];
-        part[16 + g + 8] = vals[1][1];
-      }
+      part[lane >> 2] = og;
+      part[(lane >> 2) + 8] = oh;
     }
     __threadfence_block();
     __syncwarp();
-    // local tiles of this row block inside [t0, t1)
     const int cl0 = max(rb * st.chunks, t0), cl1 = min((rb + 1) * st.chunks, t1);
     const int need = cl1 - cl0;
     unsigned done = 0;
@@ -610,11 +622,10 @@ __device__ void run_op(const Params& p, const Layer& L, const Smem& s, const Str
     const bool split = need != st.chunks;
     bool last = true;
     if (split) {
-      // publish the local chunk partials; the CTA that brings the row block's count to `chunks` finishes it
       float* gp = p.gpart + static_cast<size_t>(rb) * kChunks * 32;
       for (int c = cl0; c < cl1; ++c) {
         const float v = s.part[((c - t0) % kPartSlots) * 32 + lane];
-        if (lane < kRows) gp[(c - rb * st.chunks) * 32 + lane] = v;
+        if (lane < 16) gp[(c - rb * st.chunks) * 32 + lane] = v;
       }
       __threadfence();
       __syncwarp();
@@ -643,146 +654,245 @@ __device__ void run_op(const Params& p, const Layer& L, const Smem& s, const Str
         s.ready[l % kPartSlots] = static_cast<unsigned>(l + kPartSlots);
       }
     }
-    if (last) finish_rows<EPI>(p, L, rb, total, lane, pos, s.misc);
+    if (last) {
+      const int n = rb * 16 + lane;
+      unsigned long long key = (lane < 16 && n < p.vocab) ? argmax_key(total, n + p.vocab_offset) : 0ull;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long k2 = __shfl_xor_sync(0xffffffffu, key, o);
+        key = k2 > key ? k2 : key;
+      }
+      if (lane == 0 && key) atomicMax(&s.misc->key, key);
+    }
   }
   seq += static_cast<uint32_t>(t1 - t0);
 }
 
+// Sum, in chunk order, of the first n (<= 8) per-chunk partials of a row
+// stored as 8 floats (written by other CTAs: read through L2).
+__device__ __forceinline__ float sum_chunks(const float* row, int n) {
+  const float4 a = __ldcg(reinterpret_cast<const float4*>(row));
+  float v[8] = {a.x, a.y, a.z, a.w, 0.f, 0.f, 0.f, 0.f};
+  if (n > 4) {
+    const float4 b = __ldcg(reinterpret_cast<const float4*>(row + 4));
+    v[4] = b.x;
+    v[5] = b.y;
+    v[6] = b.z;
+    v[7] = b.w;
+  }
+  float acc = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i)
+    if (i < n) acc += v[i];
+  return acc;
+}
+
 // ------------------------------------------------------------- attention
-// INT8-KV attention of the new token (position pos) for every (KV head,
-// 128-token chunk) work item, one warp per item; the items of a KV head are
-// merged in chunk order by the warp that completes the last one. The warp
-// holding the newest position quantizes the new K/V row into the cache
-// (symmetric per token per head, fp16 scale = absmax / 127).
+// The row pairs (d, d+64) of one head from the QKV partials (stream row order:
+// block 8*hd + i holds dims 8i..8i+7 in rows 0-7 and their partners in rows
+// 8-15): the 5 K chunks summed in order, the per-row scale, bf16 rounding, and
+// for query/key heads the rotation at position pos. Lane L covers dims
+// d = 8*(L>>2) + 2*(L&3) + {0, 1} and d + 64.
+__device__ __forceinline__ void head_rows(const Params& p, const Layer& L, int hd, bool rope, const float (&cs)[2],
+                                          const float (&sn)[2], int lane, float (&lo)[2], float (&hi)[2]) {
+  const int i = lane >> 2, gg = (lane & 3) * 2;
+  const int base = (hd * 8 + i) * 16;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int r0 = base + gg + e, r1 = r0 + 8;
+    float x0 = bfr(sum_chunks(p.pqkv + r0 * 8, p.sq.chunks) * L.qkv_scale[r0]);
+    float x1 = bfr(sum_chunks(p.pqkv + r1 * 8, p.sq.chunks) * L.qkv_scale[r1]);
+    if (rope) {
+      const float ra = x0 * cs[e] - x1 * sn[e];
+      const float rb2 = x1 * cs[e] + x0 * sn[e];
+      x0 = bfr(ra);
+      x1 = bfr(rb2);
+    }
+    lo[e] = x0;
+    hi[e] = x1;
+  }
+}
+
+// INT8 K/V row quantization (symmetric per token per head, fp16 scale =
+// absmax / 127, 1 for a zero row; code = clamp(rint(x / scale), +-127)) of
+// the lane's 4 values of a head, written to the cache at position pos.
+__device__ __forceinline__ void quantize_row(const float (&lo)[2], const float (&hi)[2], int lane, int8_t* row,
+                                             __half* scale_slot) {
+  float amax = fmaxf(fmaxf(fabsf(lo[0]), fabsf(lo[1])), fmaxf(fabsf(hi[0]), fabsf(hi[1])));
+  amax = warp_max(amax);
+  __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
+  if (__half2float(s16) == 0.f) s16 = __float2half_rn(1.0f);
+  const float sf = __half2float(s16);
+  auto q = [&](float v) {
+    return static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(v, sf)), -127.f), 127.f)));
+  };
+  const int d = 8 * (lane >> 2) + 2 * (lane & 3);
+  row[d] = q(lo[0]);
+  row[d + 1] = q(lo[1]);
+  row[d + 64] = q(hi[0]);
+  row[d + 65] = q(hi[1]);
+  if (lane == 0) *scale_slot = s16;
+}
+
+// Attention of the new token (position pos) over the INT8 cache: work items
+// (KV head, 32-token chunk), one warp each. q of the head's G query heads is
+// rebuilt from the QKV partials; the item holding pos also builds the new K/V
+// row and writes it into the cache. QK^T on the tensor cores (K rows as the A
+// operand, exact int8 -> fp16; q as B with one column per head), softmax
+// partials per head, P.V on the CUDA cores (lane = 4 dims); the KV head's
+// items merge in chunk order in the warp that completes the last one.
 template <int G>
-__device__ void attention_items(const Params& p, const Layer& L, int pos, float* qs_all) {
+__device__ void attention_step(const Params& p, const Layer& L, int pos, uint8_t* scratch) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
   const int n = pos + 1;
-  const int nchunks = (n + kAttnChunk - 1) / kAttnChunk;
-  const int items = p.kv_heads * nchunks;
-  const int gw = blockIdx.x * kConsumers + warp;
+  const int nch = (n + kAttnChunk - 1) / kAttnChunk;
+  const int items = p.kv_heads * nch;
   const int stride = gridDim.x * kConsumers;
-  float* qs = qs_all + warp * G * 128;
+  __half* qs = reinterpret_cast<__half*>(scratch + warp * kAttnWarpBytes);        // [4][128] fp16
+  float* pw = reinterpret_cast<float*>(scratch + warp * kAttnWarpBytes + 1024);   // [32][4]
   const size_t cap = static_cast<size_t>(p.capacity);
-  for (int item = gw; item < items; item += stride) {
-    const int h = item / nchunks, ck = item % nchunks;
+  // rotation angles of the lane's two dims (shared by all heads)
+  float cs[2], sn[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int d = 8 * (lane >> 2) + 2 * (lane & 3) + e;
+    sincosf(static_cast<float>(pos) * p.inv_freq[d], &sn[e], &cs[e]);
+  }
+  for (int item = blockIdx.x * kConsumers + warp; item < items; item += stride) {
+    const int h = item / nch, ck = item % nch;
     const int tb = ck * kAttnChunk;
-    // queries of the G heads sharing KV head h (fp32 in shared memory)
-    for (int i = lane; i < G * 128; i += 32) qs[i] = ldcg_bf(p.q + (h * G) * 128 + i);
     int8_t* kc = L.k_cache + static_cast<size_t>(h) * cap * 128;
     int8_t* vc = L.v_cache + static_cast<size_t>(h) * cap * 128;
     __half* ksc = L.k_scale + static_cast<size_t>(h) * cap;
     __half* vsc = L.v_scale + static_cast<size_t>(h) * cap;
-    if (pos >= tb && pos < tb + kAttnChunk) {
-      // the new token's row: quantize K and V into the cache
+    // ---- q of the G query heads (fp16, exact for these bf16 values)
+    const int d0 = 8 * (lane >> 2) + 2 * (lane & 3);
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        const __nv_bfloat16* src = p.kv_new + (which * p.kv_heads + h) * 128;
-        float v4[4];
-        float amax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          v4[i] = ldcg_bf(src + lane * 4 + i);
-          amax = fmaxf(amax, fabsf(v4[i]));
-        }
-        amax = warp_max(amax);
-        __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
-        if (__half2float(s16) == 0.f) s16 = __float2half_rn(1.0f);
-        const float sf = __half2float(s16);
-        char4 q4;
-        int8_t* qq = reinterpret_cast<int8_t*>(&q4);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float rr = fminf(fmaxf(rintf(__fdiv_rn(v4[i], sf)), -127.f), 127.f);
-          qq[i] = static_cast<int8_t>(static_cast<int>(rr));
-        }
-        int8_t* dst = (which ? vc : kc) + static_cast<size_t>(pos) * 128;
-        *reinterpret_cast<char4*>(dst + lane * 4) = q4;
-        if (lane == 0) (which ? vsc : ksc)[pos] = s16;
-      }
-      __syncwarp();
-      __threadfence_block();
+    for (int j = 0; j < G; ++j) {
+      float lo[2], hi[2];
+      head_rows(p, L, G * h + j, true, cs, sn, lane, lo, hi);
+      *reinterpret_cast<__half2*>(qs + j * 128 + d0) = __floats2half2_rn(lo[0], lo[1]);
+      *reinterpret_cast<__half2*>(qs + j * 128 + d0 + 64) = __floats2half2_rn(hi[0], hi[1]);
+    }
+    const bool newest = pos >= tb && pos < tb + kAttnChunk;
+    if (newest) {
+      float lo[2], hi[2];
+      head_rows(p, L, p.heads + h, true, cs, sn, lane, lo, hi);
+      quantize_row(lo, hi, lane, kc + static_cast<size_t>(pos) * 128, ksc + pos);
+      head_rows(p, L, p.heads + p.kv_heads + h, false, cs, sn, lane, lo, hi);
+      quantize_row(lo, hi, lane, vc + static_cast<size_t>(pos) * 128, vsc + pos);
+      __threadfence();
     }
     __syncwarp();
-    // scores: lane owns tokens tb + lane + 32*i
-    float sc[4][G];
+    // ---- B fragments: column g < G is query head g; dims of MMA s for lane quad c: 32c + 4s + {0..3}
+    uint32_t bq[8][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int t = tb + lane + 32 * i;
-#pragma unroll
-      for (int hh = 0; hh < G; ++hh) sc[i][hh] = -INFINITY;
-      if (t < n) {
-        const int8_t* krow = kc + static_cast<size_t>(t) * 128;
-        float dot[G];
-#pragma unroll
-        for (int hh = 0; hh < G; ++hh) dot[hh] = 0.f;
-#pragma unroll
-        for (int seg = 0; seg < 8; ++seg) {
-          const uint4 kv = (t == pos) ? ldcg16(krow + seg * 16) : *reinterpret_cast<const uint4*>(krow + seg * 16);
-          const int8_t* kb = reinterpret_cast<const int8_t*>(&kv);
-#pragma unroll
-          for (int e = 0; e < 16; ++e) {
-            const float kf = static_cast<float>(kb[e]);
-#pragma unroll
-            for (int hh = 0; hh < G; ++hh) dot[hh] = fmaf(qs[hh * 128 + seg * 16 + e], kf, dot[hh]);
-          }
-        }
-        const float ks = __half2float(t == pos ? __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(ksc + t)))
-                                               : ksc[t]);
-#pragma unroll
-        for (int hh = 0; hh < G; ++hh) sc[i][hh] = dot[hh] * ks * p.attn_scale;
+    for (int s = 0; s < 8; ++s) {
+      if (g < G) {
+        const uint2 v = *reinterpret_cast<const uint2*>(qs + g * 128 + 32 * c + 4 * s);
+        bq[s][0] = v.x;
+        bq[s][1] = v.y;
+      } else {
+        bq[s][0] = bq[s][1] = 0u;
       }
     }
-    float m[G], l[G];
+    // ---- scores of the chunk's 32 tokens (two 16-token MMA row blocks)
+    float sc[2][4];
 #pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
-      float mx = fmaxf(fmaxf(sc[0][hh], sc[1][hh]), fmaxf(sc[2][hh], sc[3][hh]));
-      m[hh] = warp_max(mx);
+    for (int rbk = 0; rbk < 2; ++rbk) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int tg = tb + rbk * 16 + g, th = tg + 8;
+      uint4 kg0 = make_uint4(0u, 0u, 0u, 0u), kg1 = kg0, kh0 = kg0, kh1 = kg0;
+      if (tg < n) {
+        const int8_t* r = kc + static_cast<size_t>(tg) * 128 + 32 * c;
+        kg0 = tg == pos ? ldcg16(r) : *reinterpret_cast<const uint4*>(r);
+        kg1 = tg == pos ? ldcg16(r + 16) : *reinterpret_cast<const uint4*>(r + 16);
+      }
+      if (th < n) {
+        const int8_t* r = kc + static_cast<size_t>(th) * 128 + 32 * c;
+        kh0 = th == pos ? ldcg16(r) : *reinterpret_cast<const uint4*>(r);
+        kh1 = th == pos ? ldcg16(r + 16) : *reinterpret_cast<const uint4*>(r + 16);
+      }
+      const uint32_t wg[8] = {kg0.x, kg0.y, kg0.z, kg0.w, kg1.x, kg1.y, kg1.z, kg1.w};
+      const uint32_t wh[8] = {kh0.x, kh0.y, kh0.z, kh0.w, kh1.x, kh1.y, kh1.z, kh1.w};
+      constexpr uint32_t kMagic = 0x64646464u, kOff = 0x64806480u;
+#pragma unroll
+      for (int s = 0; s < 8; ++s) {
+        const uint32_t ug = wg[s] ^ 0x80808080u, uh = wh[s] ^ 0x80808080u;
+        const uint32_t a[4] = {hsub2_u32(prmt(ug, kMagic, 0x4140u), kOff), hsub2_u32(prmt(uh, kMagic, 0x4140u), kOff),
+                               hsub2_u32(prmt(ug, kMagic, 0x4342u), kOff), hsub2_u32(prmt(uh, kMagic, 0x4342u), kOff)};
+        mma_16816<true>(acc, a, bq[s][0], bq[s][1]);
+      }
+      // lane holds tokens tg (acc 0,1) and th (acc 2,3) for heads 2c, 2c+1
+      const float kgs = tg < n ? __half2float(tg == pos ? __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(ksc + tg))) : ksc[tg]) : 0.f;
+      const float khs = th < n ? __half2float(th == pos ? __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(ksc + th))) : ksc[th]) : 0.f;
+      sc[rbk][0] = tg < n ? acc[0] * kgs * p.attn_scale : -INFINITY;
+      sc[rbk][1] = tg < n ? acc[1] * kgs * p.attn_scale : -INFINITY;
+      sc[rbk][2] = th < n ? acc[2] * khs * p.attn_scale : -INFINITY;
+      sc[rbk][3] = th < n ? acc[3] * khs * p.attn_scale : -INFINITY;
+    }
+    // ---- softmax partials per head (column 2c + e), over the 32 tokens
+    float m2[2], l2[2];
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float mx = fmaxf(fmaxf(sc[0][e], sc[0][e + 2]), fmaxf(sc[1][e], sc[1][e + 2]));
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      m2[e] = mx;
       float sum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        sc[i][hh] = (sc[i][hh] == -INFINITY) ? 0.f : expf(sc[i][hh] - m[hh]);
-        sum += sc[i][hh];
-      }
-      l[hh] = warp_sum(sum);
+      for (int rbk = 0; rbk < 2; ++rbk)
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const float v = sc[rbk][e + 2 * hh];
+          const float pe = v == -INFINITY ? 0.f : expf(v - mx);
+          sc[rbk][e + 2 * hh] = pe;
+          sum += pe;
+        }
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      l2[e] = sum;
     }
-    // P.V: lane owns dims 4*lane .. 4*lane+3
+    // probabilities to shared memory: pw[token][head]
+    if (2 * c < G) {
+#pragma unroll
+      for (int rbk = 0; rbk < 2; ++rbk)
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          if (2 * c + e < G) {
+            pw[(rbk * 16 + g) * 4 + 2 * c + e] = sc[rbk][e];
+            pw[(rbk * 16 + g + 8) * 4 + 2 * c + e] = sc[rbk][e + 2];
+          }
+    }
+    __syncwarp();
+    // ---- P.V: lane owns dims 4*lane .. 4*lane+3
     float acc[G][4];
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = acc[hh][2] = acc[hh][3] = 0.f;
     const int tend = min(n - tb, kAttnChunk);
     for (int tt = 0; tt < tend; ++tt) {
       const int t = tb + tt;
-      const int owner = tt & 31, idx = tt >> 5;
-      const char4 v4 = (t == pos) ? *reinterpret_cast<const char4*>(&reinterpret_cast<const int*>(vc + static_cast<size_t>(t) * 128)[lane])
-                                  : reinterpret_cast<const char4*>(vc + static_cast<size_t>(t) * 128)[lane];
-      const float vs = __half2float(vsc[t]);
-      float pv[G];
-#pragma unroll
-      for (int hh = 0; hh < G; ++hh) {
-        float pt = 0.f;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const float cand = __shfl_sync(0xffffffffu, sc[i][hh], owner);
-          if (i == idx) pt = cand;
-        }
-        pv[hh] = pt * vs;
-      }
-      const float vf[4] = {static_cast<float>(v4.x), static_cast<float>(v4.y), static_cast<float>(v4.z),
-                           static_cast<float>(v4.w)};
+      const int8_t* vr = vc + static_cast<size_t>(t) * 128 + lane * 4;
+      const int vw = t == pos ? __ldcg(reinterpret_cast<const int*>(vr)) : *reinterpret_cast<const int*>(vr);
+      const float vs = __half2float(t == pos ? __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(vsc + t))) : vsc[t]);
+      const float4 p4 = *reinterpret_cast<const float4*>(pw + tt * 4);
+      const float pr[4] = {p4.x * vs, p4.y * vs, p4.z * vs, p4.w * vs};
+      const float vf[4] = {static_cast<float>(static_cast<int8_t>(vw & 0xFF)), static_cast<float>(static_cast<int8_t>((vw >> 8) & 0xFF)),
+                           static_cast<float>(static_cast<int8_t>((vw >> 16) & 0xFF)), static_cast<float>(static_cast<int8_t>(vw >> 24))};
 #pragma unroll
       for (int hh = 0; hh < G; ++hh)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[hh][e] = fmaf(pv[hh], vf[e], acc[hh][e]);
+        for (int e = 0; e < 4; ++e) acc[hh][e] = fmaf(pr[hh], vf[e], acc[hh][e]);
     }
-    // partial of this item
+    // ---- this item's partial: per head (m, l) from the lanes of quad 2c+e and the lane's 4 dims
     float* ap = p.apart + (static_cast<size_t>(h) * p.attn_max_chunks + ck) * G * 132;
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) {
       *reinterpret_cast<float4*>(ap + hh * 132 + lane * 4) = make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
-      if (lane == 0) {
-        ap[hh * 132 + 128] = m[hh];
-        ap[hh * 132 + 129] = l[hh];
+      if (lane == hh / 2) {  // lane (g = 0, c = hh/2) holds column hh = 2c + e
+        ap[hh * 132 + 128] = m2[hh & 1];
+        ap[hh * 132 + 129] = l2[hh & 1];
       }
     }
     __threadfence();
@@ -790,18 +900,18 @@ __device__ void attention_items(const Params& p, const Layer& L, int pos, float*
     unsigned old = 0;
     if (lane == 0) old = atomicAdd(p.acount + h, 1u);
     old = __shfl_sync(0xffffffffu, old, 0);
-    if (static_cast<int>(old) + 1 != nchunks) continue;
-    // ---- last item of KV head h: merge the chunks in order
+    if (static_cast<int>(old) + 1 != nch) continue;
+    // ---- last item of KV head h: merge its chunks in order
     __threadfence();
     if (lane == 0) p.acount[h] = 0u;
     const float* base = p.apart + static_cast<size_t>(h) * p.attn_max_chunks * G * 132;
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) {
       float M = -INFINITY;
-      for (int c = 0; c < nchunks; ++c) M = fmaxf(M, ldcg_f(base + (c * G + hh) * 132 + 128));
+      for (int c2 = 0; c2 < nch; ++c2) M = fmaxf(M, ldcg_f(base + (c2 * G + hh) * 132 + 128));
       float Lsum = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int c = 0; c < nchunks; ++c) {
-        const float* e = base + (c * G + hh) * 132;
+      for (int c2 = 0; c2 < nch; ++c2) {
+        const float* e = base + (c2 * G + hh) * 132;
         const float w = expf(ldcg_f(e + 128) - M);
         Lsum = fmaf(ldcg_f(e + 129), w, Lsum);
         const float4 a = __ldcg(reinterpret_cast<const float4*>(e + lane * 4));
@@ -812,8 +922,8 @@ __device__ void attention_items(const Params& p, const Layer& L, int pos, float*
       }
       const float inv = Lsum > 0.f ? 1.0f / Lsum : 0.f;
       __nv_bfloat16* dst = p.attn + (h * G + hh) * 128 + lane * 4;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) dst[e] = __float2bfloat16_rn(o[e] * inv);
+      *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
+      *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
     }
   }
 }
@@ -847,6 +957,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
   s.zero = base + kOffZero;
   s.misc = reinterpret_cast<Misc*>(base + kOffMisc);
   s.om = reinterpret_cast<float2*>(base + kOffMeta);
+  s.xres = reinterpret_cast<__nv_bfloat16*>(base + kOffXres);
   s.part = reinterpret_cast<float*>(base + kOffPart);
   s.xs = base + kOffXs;
   s.ring = base + kOffRing;
@@ -866,6 +977,12 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
   __syncthreads();
 
   const int pos = p.positions[0];
+  if (pos < 0 || pos >= p.capacity) {
+    // the new token's K/V row would fall outside the cache: nothing is read or
+    // written; the step reports it (uniform for every thread of every CTA)
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(p.status, kStatusRange);
+    return;
+  }
   if (warp == kConsumers) {
     // ---------------- producer warp (one lane issues)
     if (lane == 0) {
@@ -891,66 +1008,118 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
 
   // ---------------- consumer warps
   const int W = gridDim.x;
+  const int tid = threadIdx.x;
+  if (p.trace != nullptr && tid == 0)
+    p.trace[(static_cast<size_t>(blockIdx.x) * p.trace_slots + p.trace_slots - 1) * 2] = global_ns();
   const int token = p.tokens[0];
   const __nv_bfloat16* emb = p.embed + static_cast<size_t>(min(max(token, 0), p.vocab_total - 1)) * p.hidden;
-  if (blockIdx.x == 0) {
-    for (int v = threadIdx.x; v < p.hidden / 8; v += kConsumerThreads)
-      reinterpret_cast<uint4*>(p.x)[v] = reinterpret_cast<const uint4*>(emb)[v];
-  }
   uint32_t seq = 0;
   unsigned joins = 0;
   const int G = p.heads / p.kv_heads;
+  const int nwords = p.hidden / 8;
+  load_residual(emb, p.hidden, p.eps, s.xres, s.misc);
   for (int l = 0; l < p.num_layers; ++l) {
     const Layer& L = p.layers[l];
-    // RMSNorm + QKV + RoPE
-    const bool first = l == 0;
-    const __nv_bfloat16* xin = first ? emb : p.x;
-    rms_stat(xin, p.hidden, p.eps, s.misc, !first);
-    stage_w8(xin, L.in_norm, p.hidden, !first, s.misc->rms, s.xs);
-    named_sync();
-    run_op<K_W8, E_QKV>(p, L, s, p.sq, L.qkv, seq, pos);
-    grid_join(p, s.misc, (++joins) * W);
-    // attention (q/k/v of all heads are final)
-    float* qs = reinterpret_cast<float*>(base + kOffPart);
-    switch (G) {
-      case 1: attention_items<1>(p, L, pos, qs); break;
-      case 2: attention_items<2>(p, L, pos, qs); break;
-      case 4: attention_items<4>(p, L, pos, qs); break;
-      default: attention_items<8>(p, L, pos, qs); break;
+    // ---- RMSNorm + QKV projection (per-chunk partials; RoPE happens in the attention items)
+    if (l > 0) fold_residual(p.pdn, nullptr, p.hidden, p.eps, s.xres, s.misc);
+    for (int v = tid; v < nwords; v += kConsumerThreads) {
+      float f[8];
+      norm8(s.xres, L.in_norm, s.misc->rms, v, f);
+      put_w8(s.xs, v, f);
     }
-    grid_join(p, s.misc, (++joins) * W);
-    // o_proj + residual
-    stage_w8(p.attn, nullptr, p.heads * 128, true, 1.f, s.xs);
     named_sync();
-    run_op<K_W8, E_OPROJ>(p, L, s, p.so, L.o, seq, pos);
+    run_partials<K_W8>(p, s, p.sq, false, p.pqkv, 8, 0, seq);
     grid_join(p, s.misc, (++joins) * W);
-    // RMSNorm + gate/up + SwiGLU
-    rms_stat(p.x, p.hidden, p.eps, s.misc, true);
-    stage_w4(p.x, L.post_norm, p.hidden, true, s.misc->rms, s.xs, s.om);
-    named_sync();
-    run_op<K_W4PAIR, E_SWIGLU>(p, L, s, p.sgu, L.gateup, seq, pos);
+    // ---- attention of the new token
+    uint8_t* scratch = base + kOffPart;
+    if (G == 1) attention_step<1>(p, L, pos, scratch);
+    else if (G == 2) attention_step<2>(p, L, pos, scratch);
+    else attention_step<4>(p, L, pos, scratch);
     grid_join(p, s.misc, (++joins) * W);
-    // down + residual
-    stage_w4(p.act, nullptr, p.inter, true, 1.f, s.xs, s.om);
+    // ---- o_proj (partials; the residual add happens in the next prologue)
+    for (int v = tid; v < p.heads * 16; v += kConsumerThreads) {
+      float f[8];
+      plain8(p.attn, v, f);
+      put_w8(s.xs, v, f);
+    }
     named_sync();
-    run_op<K_W4, E_DOWN>(p, L, s, p.sdn, L.down, seq, pos);
+    run_partials<K_W8>(p, s, p.so, false, p.po, 8, 0, seq);
+    grid_join(p, s.misc, (++joins) * W);
+    // ---- residual += o; RMSNorm + gate/up (partials)
+    fold_residual(p.po, L.o_scale, p.hidden, p.eps, s.xres, s.misc);
+    for (int v0 = 0; v0 < nwords; v0 += kConsumerThreads) {
+      const int v = v0 + tid;
+      float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (v < nwords) norm8(s.xres, L.post_norm, s.misc->rms, v, f);
+      put_w4(s.xs, s.om, v, v < nwords, f);
+    }
+    named_sync();
+    run_partials<K_W4PAIR>(p, s, p.sgu, false, p.pgu, 16, 0, seq);
+    grid_join(p, s.misc, (++joins) * W);
+    // ---- SwiGLU of the K chunks this CTA's down tiles read, then down (partials)
+    {
+      const Stream& st = p.sdn;
+      int t0, t1;
+      cta_range(st.rbs * st.chunks, t0, t1);
+      if (t1 > t0) {
+        const int ck = st.ck * 64;  // activation values per chunk
+        const int w0 = (t0 / st.rbs) * ck / 8, w1 = ((t1 - 1) / st.rbs + 1) * ck / 8;
+        for (int v0 = w0 & ~7; v0 < w1; v0 += kConsumerThreads) {
+          const int v = v0 + tid;
+          const bool valid = v >= w0 && v < w1;
+          float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float* pr = p.pgu + static_cast<size_t>(v * 8 + i) * 16;
+              const float gt = bfr(sum_chunks(pr, p.sgu.chunks));
+              const float up = bfr(sum_chunks(pr + 8, p.sgu.chunks));
+              f[i] = bfr(gt / (1.0f + expf(-gt)) * up);
+            }
+          }
+          put_w4(s.xs, s.om, v, valid, f);
+        }
+      }
+    }
+    named_sync();
+    run_partials<K_W4>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
     grid_join(p, s.misc, (++joins) * W);
   }
-  // final RMSNorm + lm_head + greedy argmax
-  rms_stat(p.x, p.hidden, p.eps, s.misc, true);
-  stage_bf16(p.x, p.final_norm, p.hidden, true, s.misc->rms, s.xs);
+  // ---- residual += down; final RMSNorm + lm_head + greedy argmax
+  fold_residual(p.pdn, nullptr, p.hidden, p.eps, s.xres, s.misc);
+  for (int v = tid; v < nwords; v += kConsumerThreads) {
+    float f[8];
+    norm8(s.xres, p.final_norm, s.misc->rms, v, f);
+    put_bf16(s.xs, v, f);
+  }
   named_sync();
-  run_op<K_BF16, E_ARGMAX>(p, p.layers[0], s, p.slm, p.head, seq, pos);
+  run_lm(p, s, seq);
   named_sync();
-  if (threadIdx.x == 0 && s.misc->key) atomicMax(p.keys, s.misc->key);
+  if (tid == 0) {
+    if (s.misc->key) atomicMax(p.keys, s.misc->key);
+    if (p.trace != nullptr) {
+      const int slot = static_cast<int>(joins);
+      if (slot < p.trace_slots) p.trace[(static_cast<size_t>(blockIdx.x) * p.trace_slots + slot) * 2] = global_ns();
+    }
+  }
+  // the residual stream of this step, for callers that inspect it (CTA 0)
+  if (blockIdx.x == 0)
+    for (int v = tid; v < nwords; v += kConsumerThreads)
+      reinterpret_cast<uint4*>(p.x)[v] = reinterpret_cast<const uint4*>(s.xres)[v];
 }
 
 // ------------------------------------------------------------------- host
+// Workspace layout (byte offsets): header words (arrival counter, status),
+// lm_head split-block counters and partials, attention counters and
+// partials, and the projections' per-chunk partial sums.
+struct Workspace {
+  size_t gcount, acount, gpart, apart, pqkv, po, pgu, pdn, total;
+};
+
 struct Geometry {
   Stream sq, so, sgu, sdn, slm;
-  int max_rbs;
   int attn_chunks;
-  size_t ws_bytes;
+  Workspace ws;
   int slot_bytes;
 };
 
@@ -959,10 +1128,11 @@ int geometry(const sb_step_desc* d, Geometry* g) {
   SB_REQUIRE(d->head_dim == 128, "the decode-step kernel supports head_dim 128");
   SB_REQUIRE(d->world == 1 && d->rank == 0, "the decode-step kernel in this build runs one rank");
   SB_REQUIRE(d->num_layers > 0 && d->num_layers <= kMaxLayers, "1..128 layers");
-  SB_REQUIRE(d->hidden > 0 && d->hidden % 512 == 0 && d->hidden <= kMaxK, "hidden must be a multiple of 512, <= 10240");
+  SB_REQUIRE(d->hidden > 0 && d->hidden % 512 == 0 && d->hidden <= kMaxHidden,
+             "hidden must be a multiple of 512, <= 4096");
   SB_REQUIRE(d->num_heads > 0 && d->num_kv_heads > 0 && d->num_heads % d->num_kv_heads == 0, "heads");
   const int G = d->num_heads / d->num_kv_heads;
-  SB_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, "query heads per KV head must be 1, 2, 4 or 8");
+  SB_REQUIRE(G == 1 || G == 2 || G == 4, "query heads per KV head must be 1, 2 or 4");
   const int qk = d->num_heads * 128;  // o_proj K (this rank)
   SB_REQUIRE(qk <= kMaxK && qk % (kChunks * 32 / d->world) == 0, "o_proj K must split into 8 chunks of 32-multiples");
   SB_REQUIRE(d->inter > 0 && d->inter % 16 == 0 && d->inter <= kMaxK, "inter must be a multiple of 16, <= 10240");
@@ -981,16 +1151,23 @@ int geometry(const sb_step_desc* d, Geometry* g) {
   int tmax = 0;
   for (const Stream* st : {&g->sq, &g->so, &g->sgu, &g->sdn, &g->slm}) tmax = tmax > st->tile ? tmax : st->tile;
   g->slot_bytes = (tmax + 127) / 128 * 128;
-  g->max_rbs = std::max({g->sq.rbs, g->so.rbs, g->sgu.rbs, g->sdn.rbs, g->slm.rbs});
   g->attn_chunks = (d->capacity + kAttnChunk - 1) / kAttnChunk;
+  Workspace& w = g->ws;
   size_t off = 256;  // header words
-  off += static_cast<size_t>(g->max_rbs) * 4;  // gcount
-  off = (off + 255) / 256 * 256;
-  off += 64 * 4;  // acount
-  off = (off + 255) / 256 * 256;
-  off += static_cast<size_t>(g->max_rbs) * kChunks * 32 * 4;  // gpart
-  off += static_cast<size_t>(d->num_kv_heads) * g->attn_chunks * G * 132 * 4;  // apart
-  g->ws_bytes = off;
+  auto take = [&](size_t bytes) {
+    const size_t at = off;
+    off = (off + bytes + 255) / 256 * 256;
+    return at;
+  };
+  w.gcount = take(static_cast<size_t>(g->slm.rbs) * 4);
+  w.acount = take(64 * 4);
+  w.gpart = take(static_cast<size_t>(g->slm.rbs) * kChunks * 32 * 4);
+  w.apart = take(static_cast<size_t>(d->num_kv_heads) * g->attn_chunks * G * 132 * 4);
+  w.pqkv = take(static_cast<size_t>(g->sq.rbs) * 16 * 8 * 4);
+  w.po = take(static_cast<size_t>(d->hidden) * 8 * 4);
+  w.pgu = take(static_cast<size_t>(d->inter) * 16 * 4);
+  w.pdn = take(static_cast<size_t>(d->hidden) * 8 * 4);
+  w.total = off;
   return SB_OK;
 }
 
@@ -1007,10 +1184,12 @@ int sm_count() {
 using namespace sb;
 using namespace sb::step;
 
+extern "C" int sb_step_trace_slots(int num_layers) { return num_layers * 5 + 2; }
+
 extern "C" size_t sb_step_workspace_size(const sb_step_desc* d) {
   Geometry g;
   if (geometry(d, &g) != SB_OK) return 0;
-  return g.ws_bytes;
+  return g.ws.total;
 }
 
 extern "C" int sb_step_tile_bytes(const sb_step_desc* d, int64_t out[5]) {
@@ -1027,7 +1206,7 @@ extern "C" int sb_step_tile_bytes(const sb_step_desc* d, int64_t out[5]) {
 extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   Geometry g;
   if (int st = geometry(d, &g)) return st;
-  SB_REQUIRE(d->workspace != nullptr && d->workspace_bytes >= g.ws_bytes, "workspace too small");
+  SB_REQUIRE(d->workspace != nullptr && d->workspace_bytes >= g.ws.total, "workspace too small");
   SB_REQUIRE(d->layers && d->embed && d->head && d->final_norm && d->tokens && d->positions && d->x && d->q &&
                  d->kv_new && d->attn && d->act && d->argmax_key,
              "null pointer in the step descriptor");
@@ -1061,16 +1240,14 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   p.sync = ws;
   p.status = ws + 1;
   uint8_t* wb = static_cast<uint8_t*>(d->workspace);
-  size_t off = 256;
-  p.gcount = reinterpret_cast<unsigned*>(wb + off);
-  off += static_cast<size_t>(g.max_rbs) * 4;
-  off = (off + 255) / 256 * 256;
-  p.acount = reinterpret_cast<unsigned*>(wb + off);
-  off += 64 * 4;
-  off = (off + 255) / 256 * 256;
-  p.gpart = reinterpret_cast<float*>(wb + off);
-  off += static_cast<size_t>(g.max_rbs) * kChunks * 32 * 4;
-  p.apart = reinterpret_cast<float*>(wb + off);
+  p.gcount = reinterpret_cast<unsigned*>(wb + g.ws.gcount);
+  p.acount = reinterpret_cast<unsigned*>(wb + g.ws.acount);
+  p.gpart = reinterpret_cast<float*>(wb + g.ws.gpart);
+  p.apart = reinterpret_cast<float*>(wb + g.ws.apart);
+  p.pqkv = reinterpret_cast<float*>(wb + g.ws.pqkv);
+  p.po = reinterpret_cast<float*>(wb + g.ws.po);
+  p.pgu = reinterpret_cast<float*>(wb + g.ws.pgu);
+  p.pdn = reinterpret_cast<float*>(wb + g.ws.pdn);
   p.attn_max_chunks = g.attn_chunks;
   p.sq = g.sq;
   p.so = g.so;
@@ -1078,6 +1255,8 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   p.sdn = g.sdn;
   p.slm = g.slm;
   p.slot_bytes = g.slot_bytes;
+  p.trace = d->trace;
+  p.trace_slots = d->num_layers * 5 + 2;
   int max_smem = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);

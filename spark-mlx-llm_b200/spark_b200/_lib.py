@@ -99,7 +99,7 @@ class sb_step_desc(ctypes.Structure):
         ("positions", ctypes.c_void_p), ("x", ctypes.c_void_p), ("q", ctypes.c_void_p), ("kv_new", ctypes.c_void_p),
         ("attn", ctypes.c_void_p), ("act", ctypes.c_void_p), ("argmax_key", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p), ("workspace_bytes", ctypes.c_size_t), ("world", ctypes.c_int),
-        ("rank", ctypes.c_int),
+        ("rank", ctypes.c_int), ("trace", ctypes.c_void_p),
     ]
 
 
@@ -177,6 +177,7 @@ SIGNATURES = {
     "sb_step_workspace_size": (_size, [ctypes.POINTER(sb_step_desc)]),
     "sb_step_tile_bytes": (_int, [ctypes.POINTER(sb_step_desc), ctypes.POINTER(_i64)]),
     "sb_step_run": (_int, [ctypes.POINTER(sb_step_desc), _c_void_p]),
+    "sb_step_trace_slots": (_int, [_int]),
 }
 
 _lock = threading.Lock()

@@ -457,5 +457,8 @@ class SyntheticDecoder:
             self.stepper.clear_status()
         if status:
             words[STATUS_WORD] = 0
+            if status & 2:
+                raise SBError(f"decode step: position outside the KV cache capacity {self.capacity} "
+                              f"(status {status:#x}); the steps beyond it did nothing")
             raise SBError(f"decode step: a bounded device-side wait gave up (status {status:#x}); a "
                           "tensor-parallel peer stopped responding - the tokens of these steps are invalid")

@@ -53,7 +53,7 @@ def pack_w8(w_int8, chunk_k, row_order=None):
     return t.permute(0, 3, 4, 2, 5, 6, 1, 7).contiguous().view(-1)
 
 
-def pack_w4(mats, groups_per_chunk):
+def pack_w4(mats, groups_per_chunk, chunk_major=False):
     """MLX affine 4-bit, group 64 -> W4 tile stream (uint8).
 
     ``mats`` is a list of 1 or 2 ``(packed int32 [N, K/8], scales bf16
@@ -61,7 +61,9 @@ def pack_w4(mats, groups_per_chunk):
     tiles). A tile is, per group, per matrix, 512 bytes where lane (g, c)
     holds words [row g word c, row g+8 word c, row g word c+4, row g+8 word
     c+4] of the group; then scales as [round of 8 groups][matrix][16 rows][8]
-    bf16 and biases likewise (zero padded)."""
+    bf16 and biases likewise (zero padded). Tiles are ordered row-block-major,
+    or K-chunk-major with ``chunk_major`` (down_proj: a CTA's run of tiles then
+    reads one or two K chunks of the activations)."""
     packed0 = mats[0][0]
     n, kw = packed0.shape
     k = kw * 8
@@ -85,7 +87,10 @@ def pack_w4(mats, groups_per_chunk):
         t = t.view(nm, rb, 16, ch, rounds, 8).permute(1, 3, 4, 0, 2, 5).contiguous()  # [rb, ch, round, mat, row, 8]
         return t.view(rb, ch, -1).view(torch.uint8)
 
-    return torch.cat([codes, meta(1), meta(2)], -1).contiguous().view(-1)
+    tiles = torch.cat([codes, meta(1), meta(2)], -1)  # [rb, ch, bytes]
+    if chunk_major:
+        tiles = tiles.transpose(0, 1)
+    return tiles.contiguous().view(-1)
 
 
 def pack_bf16(w_bf16, chunk_k):
@@ -127,7 +132,7 @@ class StepStreams:
             qkv_s = layer["qkv_s"][order].contiguous()
             o = pack_w8(layer["o_w"], (dec.hq * d) // CHUNKS)
             gu = pack_w4([layer["gate"], layer["up"]], 8)
-            dn = pack_w4([layer["down"]], down_groups)
+            dn = pack_w4([layer["down"]], down_groups, chunk_major=True)
             self.keep += [qkv, qkv_s, o, gu, dn]
             L = layers[li]
             L.qkv, L.qkv_scale, L.o, L.o_scale = qkv.data_ptr(), qkv_s.data_ptr(), o.data_ptr(), layer["o_s"].data_ptr()
@@ -167,6 +172,17 @@ class StepStreams:
 
     def run(self, stream):
         check(lib().sb_step_run(ctypes.byref(self.desc), stream), "decode step")
+
+    def run_layers(self, layers, stream):
+        """Inspection aid: run the step with only the first ``layers`` layers
+        (plus the lm_head); the residual stream after them lands in ``x``.
+        Writes the same K/V rows at the current position as a full step."""
+        full = self.desc.num_layers
+        self.desc.num_layers = layers
+        try:
+            self.run(stream)
+        finally:
+            self.desc.num_layers = full
 
     def status(self):
         """Device status word of the step kernel (nonzero: a bounded wait gave up)."""

@@ -115,3 +115,22 @@ def test_step_kernel_graph_replay_matches_eager(pair):
     dec.graph = None
     replayed = dec.decode(12).cpu().numpy()[0].tolist()
     assert replayed == eager
+
+
+def test_step_kernel_rejects_positions_beyond_the_cache():
+    """A step whose position is outside the KV cache writes nothing and reports it."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from spark_b200._lib import SBError
+
+    dec = _decoder("step", layers=1, capacity=16)
+    dec.reset(torch.tensor([5], dtype=torch.int32))
+    dec.positions.fill_(dec.capacity)
+    before = [t.clone() for t in (dec.k_cache[0], dec.v_cache[0], dec.k_scale[0])]
+    dec.step()
+    torch.cuda.synchronize()
+    with pytest.raises(SBError, match="outside the KV cache"):
+        dec.check_status()
+    for a, b in zip(before, (dec.k_cache[0], dec.v_cache[0], dec.k_scale[0])):
+        assert torch.equal(a, b)
+    dec.check_status()  # cleared
