@@ -107,9 +107,11 @@ typedef struct sb_step_desc {
   size_t workspace_bytes;
   int world;   /* tensor-parallel degree (1 in this build) */
   int rank;
-  /* Optional (NULL = off): per-CTA timestamps (globaltimer, ns) of every
-   * join between operators, [grid CTAs][sb_step_trace_slots][2] uint64 -
-   * arrival (this CTA's operator done) and release (all CTAs arrived). */
+  /* Optional (NULL = off): per-CTA timing of every join between operators,
+   * [grid CTAs][sb_step_trace_slots][4] uint64: arrival (this CTA's operator
+   * done) and release (all CTAs arrived) as globaltimer ns, then the time the
+   * CTA's consumer warps spent waiting for weight tiles and computing them
+   * during the operator (ns, summed over warps). */
   unsigned long long* trace;
 } sb_step_desc;
 

@@ -56,6 +56,15 @@ constexpr int kChunks = 8;                   // K chunks of o/down/lm_head (tens
 constexpr int kAttnChunk = 32;               // tokens per attention work item (one warp)
 constexpr int kMaxLayers = 128;
 constexpr unsigned kStatusRange = 2u;        // status bit: position outside the KV cache
+// Workspace header (zeroed before every launch): word 0 the grid arrival
+// counter, word 1 the status; words [64, 128) QKV tiles finished per head
+// (stream order), [128, 192) attention finished per KV head (layer + 1),
+// [192, 256) gate/up tiles finished per down K chunk; then one 128-byte
+// release flag per CTA (written by the last CTA to arrive at a join).
+constexpr int kHdrQkv = 64, kHdrAttn = 128, kHdrGu = 192;
+constexpr int kMaxCtas = 256;
+constexpr size_t kHdrBytes = 1024 + static_cast<size_t>(kMaxCtas) * 128;
+constexpr int kMarksPerLayer = 9;  // trace marks per layer
 
 // shared-memory layout (offsets from a 1024-byte aligned base)
 constexpr int kOffBars = 0;            // full[16], empty[16]
@@ -68,16 +77,19 @@ constexpr int kOffXres = ((kOffMeta + kMaxGroups * 8 + 255) / 256) * 256;  // bf
 constexpr int kOffPart = kOffXres + kMaxHidden * 2;                // float [64][32] (lm_head partials)
 constexpr int kOffXs = kOffPart + kPartSlots * 32 * 4;             // staged activations
 constexpr int kOffRing = ((kOffXs + kMaxK * 2 + 1023) / 1024) * 1024;
-// attention scratch per warp (aliases part + xs, unused during attention):
-// q of the G heads as fp16 [4][128], then the new K/V row / probabilities
-constexpr int kAttnWarpBytes = 2048;
-static_assert(kOffPart + kConsumers * kAttnWarpBytes <= kOffRing, "attention scratch");
+// attention scratch (aliases part + xs, unused during attention): q of the
+// G heads as fp16 [4][128], then per warp its partial [4 heads][132] floats
+// (the warp's probabilities [32][4] live there until the partial is written)
+static_assert(kOffPart + 1024 + kConsumers * 4 * 132 * 4 <= kOffRing, "attention scratch");
 
 struct Misc {
   int abort;
   float rms;
   unsigned long long key;
   float warp_ss[kConsumers];
+  int last;                    // attention: this CTA merges the KV head's spans
+  unsigned long long wait_ns;  // tracing: consumer time waiting for tiles (sum over warps)
+  unsigned long long busy_ns;  // tracing: consumer time computing tiles
 };
 
 struct Layer {
@@ -122,6 +134,8 @@ struct Params {
   unsigned long long* keys;
   unsigned* sync;     // workspace word 0: grid arrival counter
   unsigned* status;   // workspace word 1
+  unsigned* hdr;      // workspace header words (per-head / per-chunk progress counters)
+  unsigned* release;  // per-CTA release flags (stride 32 words)
   unsigned* gcount;   // lm_head: counters of row blocks split between CTAs
   unsigned* acount;   // attention per-KV-head counters
   float* gpart;       // lm_head: split row-block partials [rb][kChunks][32]
@@ -195,37 +209,82 @@ __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const P
   return true;
 }
 
-// Grid-wide join between operators: all consumer threads of the CTA finish
-// the operator, thread 0 adds this CTA's arrival, waits (bounded) until every
-// CTA has arrived `target` times in total, and releases the consumers.
 __device__ __forceinline__ unsigned long long global_ns() {
   unsigned long long t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+__device__ __forceinline__ void st_volatile_u32(unsigned* addr, unsigned v) {
+  asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
 
-__device__ void grid_join(const Params& p, Misc* misc, unsigned target) {
-  named_sync();
-  if (threadIdx.x == 0) {
-    const unsigned slot = target / gridDim.x - 1;
-    unsigned long long* tr = (p.trace != nullptr && static_cast<int>(slot) < p.trace_slots)
-                                 ? p.trace + (static_cast<size_t>(blockIdx.x) * p.trace_slots + slot) * 2
-                                 : nullptr;
-    if (tr) tr[0] = global_ns();
-    __threadfence();
-    atomicAdd(p.sync, 1u);
-    if (!*reinterpret_cast<volatile int*>(&misc->abort)) {
-      const long long start = clock64();
-      while (ld_volatile_u32(p.sync) < target) {
-        if (clock64() - start > (1LL << 31) || ld_volatile_u32(p.status) != 0u) {
-          atomicOr(p.status, kStatusTimeout);
-          misc->abort = 1;
-          break;
-        }
+// Bounded wait until *addr >= target (another CTA's progress), then acquire
+// ordering for the loads that follow. On timeout, or when another CTA has
+// already recorded a failure, records it and raises the CTA's abort flag.
+__device__ bool spin_geq(const Params& p, Misc* misc, const unsigned* addr, unsigned target) {
+  if (*reinterpret_cast<volatile int*>(&misc->abort)) return false;
+  if (ld_volatile_u32(addr) < target) {
+    const long long start = clock64();
+    while (ld_volatile_u32(addr) < target) {
+      if (clock64() - start > (1LL << 31) || ld_volatile_u32(p.status) != 0u) {
+        atomicOr(p.status, kStatusTimeout);
+        *reinterpret_cast<volatile int*>(&misc->abort) = 1;
+        return false;
       }
     }
-    __threadfence();
-    if (tr) tr[1] = global_ns();
+  }
+  __threadfence();
+  return true;
+}
+
+// Tracing (thread 0): mark `slot` of this CTA with (t0, t1) and the tile
+// wait/compute time accumulated since the previous mark.
+__device__ void trace_mark(const Params& p, Misc* misc, int slot, unsigned long long t0, unsigned long long t1) {
+  if (p.trace == nullptr || slot >= p.trace_slots) return;
+  unsigned long long* tr = p.trace + (static_cast<size_t>(blockIdx.x) * p.trace_slots + slot) * 4;
+  tr[0] = t0;
+  tr[1] = t1;
+  tr[2] = misc->wait_ns;
+  tr[3] = misc->busy_ns;
+  misc->wait_ns = 0;
+  misc->busy_ns = 0;
+}
+// A trace mark at a point where the CTA's warps are not otherwise joined.
+__device__ void mark(const Params& p, Misc* misc, int slot) {
+  if (p.trace == nullptr) return;
+  named_sync();
+  if (threadIdx.x == 0) {
+    const unsigned long long t = global_ns();
+    trace_mark(p, misc, slot, t, t);
+  }
+}
+
+// Grid-wide join between operators (join `idx`, 1-based, monotonic within a
+// launch): the CTA's consumer threads finish the operator; thread 0 adds the
+// CTA's arrival; the CTA whose arrival completes the join writes every CTA's
+// release flag (one line each, so the waiters do not poll a shared line);
+// then the CTA waits (bounded) for its own flag and releases its consumers.
+__device__ void grid_join(const Params& p, Misc* misc, unsigned idx, int slot) {
+  named_sync();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    unsigned long long t0 = 0;
+    unsigned old = 0;
+    if (lane == 0) {
+      if (p.trace != nullptr) t0 = global_ns();
+      __threadfence();
+      old = atomicAdd(p.sync, 1u);
+    }
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + 1u == idx * gridDim.x) {
+      __threadfence();
+      for (int c = lane; c < static_cast<int>(gridDim.x); c += 32) st_volatile_u32(p.release + c * 32, idx);
+    }
+    if (lane == 0) {
+      spin_geq(p, misc, p.release + blockIdx.x * 32, idx);
+      if (p.trace != nullptr) trace_mark(p, misc, slot, t0, global_ns());
+    }
+    __syncwarp();
   }
   named_sync();
 }
@@ -307,9 +366,12 @@ __device__ __forceinline__ void w4_tile(const uint8_t* tile, int ngroups, const 
 #pragma unroll
   for (int m = 0; m < MATS; ++m) res[m][0] = res[m][1] = 0.f;
   for (int r = 0; r < rounds; ++r) {
-    float acc[MATS][4];
+    // two accumulator chains per matrix (bf16 and fp16 MMAs), summed in the epilogue
+    float acc[MATS][4], acc2[MATS][4];
 #pragma unroll
-    for (int m = 0; m < MATS; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0.f;
+    for (int m = 0; m < MATS; ++m)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[m][e] = acc2[m][e] = 0.f;
     const int jn = min(8, ngroups - 8 * r);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -318,29 +380,35 @@ __device__ __forceinline__ void w4_tile(const uint8_t* tile, int ngroups, const 
         const uint8_t* bp = (g == j) ? xs + gi * 128 : zero;
         const uint4 b0 = lds128(bp + c * 16);
         const uint4 b1 = lds128(bp + 64 + c * 16);
+        uint4 a[MATS];
+#pragma unroll
+        for (int m = 0; m < MATS; ++m) a[m] = lds128(a_ptr + (gi * MATS + m) * 512);
 #pragma unroll
         for (int m = 0; m < MATS; ++m) {
-          const uint4 a = lds128(a_ptr + (gi * MATS + m) * 512);
           uint32_t tg[4], th[4];
-          w4_convert(a.x, tg);
-          w4_convert(a.y, th);
+          w4_convert(a[m].x, tg);
+          w4_convert(a[m].y, th);
           {
             const uint32_t fa[4] = {tg[0], th[0], tg[2], th[2]};
             const uint32_t fb[4] = {tg[1], th[1], tg[3], th[3]};
             mma_16816<false>(acc[m], fa, b0.x, b0.y);
-            mma_16816<true>(acc[m], fb, b0.z, b0.w);
+            mma_16816<true>(acc2[m], fb, b0.z, b0.w);
           }
-          w4_convert(a.z, tg);
-          w4_convert(a.w, th);
+          w4_convert(a[m].z, tg);
+          w4_convert(a[m].w, th);
           {
             const uint32_t fa[4] = {tg[0], th[0], tg[2], th[2]};
             const uint32_t fb[4] = {tg[1], th[1], tg[3], th[3]};
             mma_16816<false>(acc[m], fa, b1.x, b1.y);
-            mma_16816<true>(acc[m], fb, b1.z, b1.w);
+            mma_16816<true>(acc2[m], fb, b1.z, b1.w);
           }
         }
       }
     }
+#pragma unroll
+    for (int m = 0; m < MATS; ++m)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) acc[m][e] += acc2[m][e];
     // affine epilogue of this round: the lane's columns 2c, 2c+1 = groups 8r+2c, 8r+2c+1
     float4 o4 = make_float4(0.f, 0.f, 0.f, 0.f);
     if (2 * c < jn) {
@@ -422,14 +490,30 @@ __device__ void load_residual(const __nv_bfloat16* src, int n, float eps, __nv_b
 // the RMS of the new stream. Every CTA folds the same partials identically.
 __device__ void fold_residual(const float* P, const float* scale, int n, float eps, __nv_bfloat16* xres, Misc* misc) {
   float ss = 0.f;
-  for (int r = threadIdx.x; r < n; r += kConsumerThreads) {
-    const float4 a = __ldcg(reinterpret_cast<const float4*>(P + r * 8));
-    const float4 b = __ldcg(reinterpret_cast<const float4*>(P + r * 8 + 4));
-    float acc = ((((((a.x + a.y) + a.z) + a.w) + b.x) + b.y) + b.z) + b.w;
-    if (scale != nullptr) acc *= scale[r];
-    const float x = bfr(__bfloat162float(xres[r]) + bfr(acc));
-    xres[r] = __float2bfloat16_rn(x);
-    ss = fmaf(x, x, ss);
+  // rows r = tid + k * threads, 4 per batch; all loads of a batch are issued before any is used
+  constexpr int kBatch = 4;
+  for (int r0 = 0; r0 < n; r0 += kBatch * kConsumerThreads) {
+    float4 a[kBatch], b[kBatch];
+    float sc[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int r = r0 + threadIdx.x + k * kConsumerThreads;
+      if (r < n) {
+        a[k] = __ldcg(reinterpret_cast<const float4*>(P + r * 8));
+        b[k] = __ldcg(reinterpret_cast<const float4*>(P + r * 8 + 4));
+        sc[k] = scale != nullptr ? scale[r] : 1.f;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int r = r0 + threadIdx.x + k * kConsumerThreads;
+      if (r >= n) break;
+      float acc = ((((((a[k].x + a[k].y) + a[k].z) + a[k].w) + b[k].x) + b[k].y) + b[k].z) + b[k].w;
+      if (scale != nullptr) acc *= sc[k];
+      const float x = bfr(__bfloat162float(xres[r]) + bfr(acc));
+      xres[r] = __float2bfloat16_rn(x);
+      ss = fmaf(x, x, ss);
+    }
   }
   named_sync();  // xres complete before anyone stages from it
   finish_rms(ss, n, eps, misc);
@@ -521,9 +605,11 @@ __device__ __forceinline__ void cta_range(int T, int& t0, int& t1) {
 // per-row partial sums go to P[row * pstride + matrix * 8 + chunk] in L2 (the
 // consumer of the projection sums the chunks in order). Tiles are taken
 // round-robin by the consumer warps in stream order (the ring order).
+// When `cnt` is set, each finished tile also adds one to cnt[rb / cnt_rbs]
+// (progress that the next operator's consumers wait for).
 template <int KIND>
 __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, bool chunk_major, float* P,
-                             int pstride, int chunk0, uint32_t& seq) {
+                             int pstride, int chunk0, uint32_t& seq, unsigned* cnt = nullptr, int cnt_rbs = 1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int T = st.rbs * st.chunks;
   int t0, t1;
@@ -534,7 +620,9 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
     if (static_cast<int>(q % kConsumers) != warp) continue;
     if (*reinterpret_cast<volatile int*>(&s.misc->abort)) break;
     const int slot = static_cast<int>(q % static_cast<uint32_t>(p.slots));
+    const unsigned long long tw0 = p.trace != nullptr ? global_ns() : 0ull;
     if (!wait_bar(s.full + slot, (q / static_cast<uint32_t>(p.slots)) & 1u, p, s.misc)) break;
+    const unsigned long long tw1 = p.trace != nullptr ? global_ns() : 0ull;
     const uint8_t* tile = s.ring + static_cast<size_t>(slot) * p.slot_bytes;
     const int rb = chunk_major ? t % st.rbs : t / st.chunks;
     const int ch = chunk_major ? t / st.rbs : t % st.chunks;
@@ -551,6 +639,10 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(s.empty + slot);
+    if (p.trace != nullptr && lane == 0) {
+      atomicAdd(&s.misc->wait_ns, tw1 - tw0);
+      atomicAdd(&s.misc->busy_ns, global_ns() - tw1);
+    }
     if ((lane & 3) == 0) {
       float* out = P + static_cast<size_t>(rb * 16 + g) * pstride + chunk0 + ch;
       out[0] = vals[0][0];
@@ -558,6 +650,13 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
       if constexpr (KIND == K_W4PAIR) {
         out[8] = vals[1][0];
         out[8 * pstride + 8] = vals[1][1];
+      }
+    }
+    if (cnt != nullptr) {
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence();
+        atomicAdd(cnt + rb / cnt_rbs, 1u);
       }
     }
   }
@@ -717,7 +816,7 @@ __device__ __forceinline__ void head_rows(const Params& p, const Layer& L, int h
 // absmax / 127, 1 for a zero row; code = clamp(rint(x / scale), +-127)) of
 // the lane's 4 values of a head, written to the cache at position pos.
 __device__ __forceinline__ void quantize_row(const float (&lo)[2], const float (&hi)[2], int lane, int8_t* row,
-                                             __half* scale_slot) {
+                                             __half* scale_slot, int8_t* srow, __half* sscale) {
   float amax = fmaxf(fmaxf(fabsf(lo[0]), fabsf(lo[1])), fmaxf(fabsf(hi[0]), fabsf(hi[1])));
   amax = warp_max(amax);
   __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
@@ -727,208 +826,350 @@ __device__ __forceinline__ void quantize_row(const float (&lo)[2], const float (
     return static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(v, sf)), -127.f), 127.f)));
   };
   const int d = 8 * (lane >> 2) + 2 * (lane & 3);
-  row[d] = q(lo[0]);
-  row[d + 1] = q(lo[1]);
-  row[d + 64] = q(hi[0]);
-  row[d + 65] = q(hi[1]);
-  if (lane == 0) *scale_slot = s16;
+  const int8_t q0 = q(lo[0]), q1 = q(lo[1]), q2 = q(hi[0]), q3 = q(hi[1]);
+  row[d] = q0;
+  row[d + 1] = q1;
+  row[d + 64] = q2;
+  row[d + 65] = q3;
+  srow[d] = q0;
+  srow[d + 1] = q1;
+  srow[d + 64] = q2;
+  srow[d + 65] = q3;
+  if (lane == 0) {
+    *scale_slot = s16;
+    *sscale = s16;
+  }
 }
 
-// Attention of the new token (position pos) over the INT8 cache: work items
-// (KV head, 32-token chunk), one warp each. q of the head's G query heads is
-// rebuilt from the QKV partials; the item holding pos also builds the new K/V
-// row and writes it into the cache. QK^T on the tensor cores (K rows as the A
-// operand, exact int8 -> fp16; q as B with one column per head), softmax
-// partials per head, P.V on the CUDA cores (lane = 4 dims); the KV head's
-// items merge in chunk order in the warp that completes the last one.
+// Attention of the new token (position pos) over the INT8 cache. Work item =
+// (KV head, span of kAttnSpan tokens), one CTA each (the span count depends
+// only on the context length, so the summation structure is the same at every
+// tensor-parallel degree). The CTA rebuilds q of the head's G query heads from
+// the QKV partials; each consumer warp takes one 32-token slice: QK^T on the
+// tensor cores (K rows as the A operand, exact int8 -> fp16; q as B with one
+// column per head), softmax partials, P.V on the CUDA cores (lane = 4 dims).
+// The warps' partials merge in shared memory in token order; spans of one KV
+// head merge, in span order, in the CTA that completes the last span. The warp
+// whose slice holds pos builds the new K/V row and writes it into the cache.
+constexpr int kAttnSpan = kConsumers * kAttnChunk;
+constexpr int kAttnPart = 132;  // floats per (head) partial: acc[128], m, l, pad
+
+// Ring slot layout of one attention slice (32 tokens of one KV head): K rows
+// [32][128] int8, V rows [32][128], K scales [32] fp16, V scales [32] fp16.
+constexpr int kSliceK = 0, kSliceV = 4096, kSliceKs = 8192, kSliceVs = 8192 + 64, kSliceBytes = 8192 + 128;
+
+// Number of 32-token slices of attention item `item` (tokens [span*kAttnSpan, n)).
+__device__ __forceinline__ int attn_slices(int item, int spans, int n) {
+  const int tspan = (item % spans) * kAttnSpan;
+  return min(kConsumers, (n - tspan + kAttnChunk - 1) / kAttnChunk);
+}
+
 template <int G>
-__device__ void attention_step(const Params& p, const Layer& L, int pos, uint8_t* scratch) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, int layer, int pos, uint8_t* scratch,
+                               uint32_t& seq) {
+  Misc* misc = sm.misc;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int g = lane >> 2, c = lane & 3;
   const int n = pos + 1;
-  const int nch = (n + kAttnChunk - 1) / kAttnChunk;
-  const int items = p.kv_heads * nch;
-  const int stride = gridDim.x * kConsumers;
-  __half* qs = reinterpret_cast<__half*>(scratch + warp * kAttnWarpBytes);        // [4][128] fp16
-  float* pw = reinterpret_cast<float*>(scratch + warp * kAttnWarpBytes + 1024);   // [32][4]
+  const int spans = (n + kAttnSpan - 1) / kAttnSpan;
+  const int items = p.kv_heads * spans;
   const size_t cap = static_cast<size_t>(p.capacity);
-  // rotation angles of the lane's two dims (shared by all heads)
+  __half* qs = reinterpret_cast<__half*>(scratch);                                    // [G][128] fp16
+  float* wpart = reinterpret_cast<float*>(scratch + 1024) + warp * G * kAttnPart;      // this warp's partial
+  float* pw = wpart;                                                                   // [32][4] probabilities (before the partial)
+  float* allpart = reinterpret_cast<float*>(scratch + 1024);
   float cs[2], sn[2];
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     const int d = 8 * (lane >> 2) + 2 * (lane & 3) + e;
     sincosf(static_cast<float>(pos) * p.inv_freq[d], &sn[e], &cs[e]);
   }
-  for (int item = blockIdx.x * kConsumers + warp; item < items; item += stride) {
-    const int h = item / nch, ck = item % nch;
-    const int tb = ck * kAttnChunk;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int h = item / spans, span = item % spans;
+    const int tspan = span * kAttnSpan;
+    const int tb = tspan + warp * kAttnChunk;  // this warp's slice
+    const int slices = attn_slices(item, spans, n);
+    const bool has_slice = warp < slices;
+    // this warp's ring slot: K/V rows of the slice below pos (copied by the producer)
+    const uint32_t q_slot = seq + static_cast<uint32_t>(warp);
+    const int slot = static_cast<int>(q_slot % static_cast<uint32_t>(p.slots));
+    uint8_t* tile = sm.ring + static_cast<size_t>(slot) * p.slot_bytes;
+    if (has_slice) wait_bar(sm.full + slot, (q_slot / static_cast<uint32_t>(p.slots)) & 1u, p, misc);
+    const bool span_has_pos = pos >= tspan && pos < tspan + kAttnSpan;
+    const bool newest = pos >= tb && pos < tb + kAttnChunk;
     int8_t* kc = L.k_cache + static_cast<size_t>(h) * cap * 128;
     int8_t* vc = L.v_cache + static_cast<size_t>(h) * cap * 128;
     __half* ksc = L.k_scale + static_cast<size_t>(h) * cap;
     __half* vsc = L.v_scale + static_cast<size_t>(h) * cap;
-    // ---- q of the G query heads (fp16, exact for these bf16 values)
-    const int d0 = 8 * (lane >> 2) + 2 * (lane & 3);
-#pragma unroll
-    for (int j = 0; j < G; ++j) {
-      float lo[2], hi[2];
-      head_rows(p, L, G * h + j, true, cs, sn, lane, lo, hi);
-      *reinterpret_cast<__half2*>(qs + j * 128 + d0) = __floats2half2_rn(lo[0], lo[1]);
-      *reinterpret_cast<__half2*>(qs + j * 128 + d0 + 64) = __floats2half2_rn(hi[0], hi[1]);
+    // ---- the QKV tiles of the heads this span reads
+    if (tid == 0) {
+      const unsigned need = static_cast<unsigned>((layer + 1) * 8 * p.sq.chunks);
+      bool ok = true;
+      for (int j = 0; j < G && ok; ++j) ok = spin_geq(p, misc, p.hdr + kHdrQkv + G * h + j, need);
+      if (span_has_pos && ok) ok = spin_geq(p, misc, p.hdr + kHdrQkv + p.heads + h, need);
+      if (span_has_pos && ok) spin_geq(p, misc, p.hdr + kHdrQkv + p.heads + p.kv_heads + h, need);
     }
-    const bool newest = pos >= tb && pos < tb + kAttnChunk;
+    named_sync();
+    // (after a failed wait the item still runs through every barrier; its output is invalid and
+    // the status word reports it)
+    // ---- q of the G query heads (warp j builds head j), fp16 (exact for these bf16 values)
+    const int d0 = 8 * (lane >> 2) + 2 * (lane & 3);
+    if (warp < G) {
+      float lo[2], hi[2];
+      head_rows(p, L, G * h + warp, true, cs, sn, lane, lo, hi);
+      *reinterpret_cast<__half2*>(qs + warp * 128 + d0) = __floats2half2_rn(lo[0], lo[1]);
+      *reinterpret_cast<__half2*>(qs + warp * 128 + d0 + 64) = __floats2half2_rn(hi[0], hi[1]);
+    }
     if (newest) {
+      // the new token's K/V row: into the cache and into this warp's slice
+      const int r = pos - tb;
       float lo[2], hi[2];
       head_rows(p, L, p.heads + h, true, cs, sn, lane, lo, hi);
-      quantize_row(lo, hi, lane, kc + static_cast<size_t>(pos) * 128, ksc + pos);
+      quantize_row(lo, hi, lane, kc + static_cast<size_t>(pos) * 128, ksc + pos,
+                   reinterpret_cast<int8_t*>(tile + kSliceK) + r * 128, reinterpret_cast<__half*>(tile + kSliceKs) + r);
       head_rows(p, L, p.heads + p.kv_heads + h, false, cs, sn, lane, lo, hi);
-      quantize_row(lo, hi, lane, vc + static_cast<size_t>(pos) * 128, vsc + pos);
-      __threadfence();
+      quantize_row(lo, hi, lane, vc + static_cast<size_t>(pos) * 128, vsc + pos,
+                   reinterpret_cast<int8_t*>(tile + kSliceV) + r * 128, reinterpret_cast<__half*>(tile + kSliceVs) + r);
     }
-    __syncwarp();
-    // ---- B fragments: column g < G is query head g; dims of MMA s for lane quad c: 32c + 4s + {0..3}
-    uint32_t bq[8][2];
-#pragma unroll
-    for (int s = 0; s < 8; ++s) {
-      if (g < G) {
-        const uint2 v = *reinterpret_cast<const uint2*>(qs + g * 128 + 32 * c + 4 * s);
-        bq[s][0] = v.x;
-        bq[s][1] = v.y;
-      } else {
-        bq[s][0] = bq[s][1] = 0u;
-      }
-    }
-    // ---- scores of the chunk's 32 tokens (two 16-token MMA row blocks)
-    float sc[2][4];
-#pragma unroll
-    for (int rbk = 0; rbk < 2; ++rbk) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const int tg = tb + rbk * 16 + g, th = tg + 8;
-      uint4 kg0 = make_uint4(0u, 0u, 0u, 0u), kg1 = kg0, kh0 = kg0, kh1 = kg0;
-      if (tg < n) {
-        const int8_t* r = kc + static_cast<size_t>(tg) * 128 + 32 * c;
-        kg0 = tg == pos ? ldcg16(r) : *reinterpret_cast<const uint4*>(r);
-        kg1 = tg == pos ? ldcg16(r + 16) : *reinterpret_cast<const uint4*>(r + 16);
-      }
-      if (th < n) {
-        const int8_t* r = kc + static_cast<size_t>(th) * 128 + 32 * c;
-        kh0 = th == pos ? ldcg16(r) : *reinterpret_cast<const uint4*>(r);
-        kh1 = th == pos ? ldcg16(r + 16) : *reinterpret_cast<const uint4*>(r + 16);
-      }
-      const uint32_t wg[8] = {kg0.x, kg0.y, kg0.z, kg0.w, kg1.x, kg1.y, kg1.z, kg1.w};
-      const uint32_t wh[8] = {kh0.x, kh0.y, kh0.z, kh0.w, kh1.x, kh1.y, kh1.z, kh1.w};
-      constexpr uint32_t kMagic = 0x64646464u, kOff = 0x64806480u;
-#pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint32_t ug = wg[s] ^ 0x80808080u, uh = wh[s] ^ 0x80808080u;
-        const uint32_t a[4] = {hsub2_u32(prmt(ug, kMagic, 0x4140u), kOff), hsub2_u32(prmt(uh, kMagic, 0x4140u), kOff),
-                               hsub2_u32(prmt(ug, kMagic, 0x4342u), kOff), hsub2_u32(prmt(uh, kMagic, 0x4342u), kOff)};
-        mma_16816<true>(acc, a, bq[s][0], bq[s][1]);
-      }
-      // lane holds tokens tg (acc 0,1) and th (acc 2,3) for heads 2c, 2c+1
-      const float kgs = tg < n ? __half2float(tg == pos ? __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(ksc + tg))) : ksc[tg]) : 0.f;
-      const float khs = th < n ? __half2float(th == pos ? __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(ksc + th))) : ksc[th]) : 0.f;
-      sc[rbk][0] = tg < n ? acc[0] * kgs * p.attn_scale : -INFINITY;
-      sc[rbk][1] = tg < n ? acc[1] * kgs * p.attn_scale : -INFINITY;
-      sc[rbk][2] = th < n ? acc[2] * khs * p.attn_scale : -INFINITY;
-      sc[rbk][3] = th < n ? acc[3] * khs * p.attn_scale : -INFINITY;
-    }
-    // ---- softmax partials per head (column 2c + e), over the 32 tokens
-    float m2[2], l2[2];
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      float mx = fmaxf(fmaxf(sc[0][e], sc[0][e + 2]), fmaxf(sc[1][e], sc[1][e + 2]));
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-      m2[e] = mx;
-      float sum = 0.f;
-#pragma unroll
-      for (int rbk = 0; rbk < 2; ++rbk)
-#pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const float v = sc[rbk][e + 2 * hh];
-          const float pe = v == -INFINITY ? 0.f : expf(v - mx);
-          sc[rbk][e + 2 * hh] = pe;
-          sum += pe;
-        }
-#pragma unroll
-      for (int o = 4; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-      l2[e] = sum;
-    }
-    // probabilities to shared memory: pw[token][head]
-    if (2 * c < G) {
-#pragma unroll
-      for (int rbk = 0; rbk < 2; ++rbk)
-#pragma unroll
-        for (int e = 0; e < 2; ++e)
-          if (2 * c + e < G) {
-            pw[(rbk * 16 + g) * 4 + 2 * c + e] = sc[rbk][e];
-            pw[(rbk * 16 + g + 8) * 4 + 2 * c + e] = sc[rbk][e + 2];
-          }
-    }
-    __syncwarp();
-    // ---- P.V: lane owns dims 4*lane .. 4*lane+3
+    named_sync();
+    float m2[2] = {-INFINITY, -INFINITY}, l2[2] = {0.f, 0.f};
     float acc[G][4];
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = acc[hh][2] = acc[hh][3] = 0.f;
-    const int tend = min(n - tb, kAttnChunk);
-    for (int tt = 0; tt < tend; ++tt) {
-      const int t = tb + tt;
-      const int8_t* vr = vc + static_cast<size_t>(t) * 128 + lane * 4;
-      const int vw = t == pos ? __ldcg(reinterpret_cast<const int*>(vr)) : *reinterpret_cast<const int*>(vr);
-      const float vs = __half2float(t == pos ? __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(vsc + t))) : vsc[t]);
-      const float4 p4 = *reinterpret_cast<const float4*>(pw + tt * 4);
-      const float pr[4] = {p4.x * vs, p4.y * vs, p4.z * vs, p4.w * vs};
-      const float vf[4] = {static_cast<float>(static_cast<int8_t>(vw & 0xFF)), static_cast<float>(static_cast<int8_t>((vw >> 8) & 0xFF)),
-                           static_cast<float>(static_cast<int8_t>((vw >> 16) & 0xFF)), static_cast<float>(static_cast<int8_t>(vw >> 24))};
+    if (tb < n) {
+      // ---- B fragments: column g < G is query head g; dims of MMA s for lane quad c: 32c + 4s + {0..3}
+      uint32_t bq[8][2];
 #pragma unroll
-      for (int hh = 0; hh < G; ++hh)
+      for (int s2 = 0; s2 < 8; ++s2) {
+        if (g < G) {
+          const uint2 v = *reinterpret_cast<const uint2*>(qs + g * 128 + 32 * c + 4 * s2);
+          bq[s2][0] = v.x;
+          bq[s2][1] = v.y;
+        } else {
+          bq[s2][0] = bq[s2][1] = 0u;
+        }
+      }
+      // ---- scores of the slice's 32 tokens (two 16-token MMA row blocks)
+      float sc[2][4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[hh][e] = fmaf(pr[hh], vf[e], acc[hh][e]);
+      for (int rbk = 0; rbk < 2; ++rbk) {
+        float ac[4] = {0.f, 0.f, 0.f, 0.f};
+        const int rg = rbk * 16 + g, rh = rg + 8;  // rows of the slice
+        const int tg = tb + rg, th = tb + rh;
+        const uint8_t* kr_g = tile + kSliceK + rg * 128 + 32 * c;
+        const uint8_t* kr_h = tile + kSliceK + rh * 128 + 32 * c;
+        const uint4 kg0 = lds128(kr_g), kg1 = lds128(kr_g + 16), kh0 = lds128(kr_h), kh1 = lds128(kr_h + 16);
+        const __half* ks_s = reinterpret_cast<const __half*>(tile + kSliceKs);
+        const float kgs = tg < n ? __half2float(ks_s[rg]) : 0.f;
+        const float khs = th < n ? __half2float(ks_s[rh]) : 0.f;
+        const uint32_t wg[8] = {kg0.x, kg0.y, kg0.z, kg0.w, kg1.x, kg1.y, kg1.z, kg1.w};
+        const uint32_t wh[8] = {kh0.x, kh0.y, kh0.z, kh0.w, kh1.x, kh1.y, kh1.z, kh1.w};
+        constexpr uint32_t kMagic = 0x64646464u, kOff = 0x64806480u;
+#pragma unroll
+        for (int s2 = 0; s2 < 8; ++s2) {
+          const uint32_t ug = wg[s2] ^ 0x80808080u, uh = wh[s2] ^ 0x80808080u;
+          const uint32_t a[4] = {hsub2_u32(prmt(ug, kMagic, 0x4140u), kOff), hsub2_u32(prmt(uh, kMagic, 0x4140u), kOff),
+                                 hsub2_u32(prmt(ug, kMagic, 0x4342u), kOff), hsub2_u32(prmt(uh, kMagic, 0x4342u), kOff)};
+          mma_16816<true>(ac, a, bq[s2][0], bq[s2][1]);
+        }
+        // lane holds tokens tg (ac 0,1) and th (ac 2,3) for heads 2c, 2c+1
+        sc[rbk][0] = tg < n ? ac[0] * kgs * p.attn_scale : -INFINITY;
+        sc[rbk][1] = tg < n ? ac[1] * kgs * p.attn_scale : -INFINITY;
+        sc[rbk][2] = th < n ? ac[2] * khs * p.attn_scale : -INFINITY;
+        sc[rbk][3] = th < n ? ac[3] * khs * p.attn_scale : -INFINITY;
+      }
+      // ---- softmax partials per head (column 2c + e), over the 32 tokens
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        float mx = fmaxf(fmaxf(sc[0][e], sc[0][e + 2]), fmaxf(sc[1][e], sc[1][e + 2]));
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        m2[e] = mx;
+        float sum = 0.f;
+#pragma unroll
+        for (int rbk = 0; rbk < 2; ++rbk)
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const float v = sc[rbk][e + 2 * hh];
+            const float pe = v == -INFINITY ? 0.f : expf(v - mx);
+            sc[rbk][e + 2 * hh] = pe;
+            sum += pe;
+          }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        l2[e] = sum;
+      }
+      if (2 * c < G) {
+#pragma unroll
+        for (int rbk = 0; rbk < 2; ++rbk)
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            if (2 * c + e < G) {
+              pw[(rbk * 16 + g) * 4 + 2 * c + e] = sc[rbk][e];
+              pw[(rbk * 16 + g + 8) * 4 + 2 * c + e] = sc[rbk][e + 2];
+            }
+      }
+      __syncwarp();
+      // ---- P.V: lane owns dims 4*lane .. 4*lane+3; V words and scales 8 tokens at a time
+      const int tend = min(n - tb, kAttnChunk);
+      const __half* vs_s = reinterpret_cast<const __half*>(tile + kSliceVs);
+      for (int t0 = 0; t0 < tend; t0 += 8) {
+        int vw[8];
+        float vs[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int tt = t0 + j;
+          vw[j] = 0;
+          vs[j] = 0.f;
+          if (tt < tend) {
+            vw[j] = *reinterpret_cast<const int*>(tile + kSliceV + tt * 128 + lane * 4);
+            vs[j] = __half2float(vs_s[tt]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (t0 + j >= tend) break;
+          const float4 p4 = *reinterpret_cast<const float4*>(pw + (t0 + j) * 4);
+          const float pr[4] = {p4.x * vs[j], p4.y * vs[j], p4.z * vs[j], p4.w * vs[j]};
+          const int w = vw[j];
+          const float vf[4] = {static_cast<float>(static_cast<int8_t>(w & 0xFF)),
+                               static_cast<float>(static_cast<int8_t>((w >> 8) & 0xFF)),
+                               static_cast<float>(static_cast<int8_t>((w >> 16) & 0xFF)),
+                               static_cast<float>(static_cast<int8_t>(w >> 24))};
+#pragma unroll
+          for (int hh = 0; hh < G; ++hh)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[hh][e] = fmaf(pr[hh], vf[e], acc[hh][e]);
+        }
+      }
+      __syncwarp();  // pw is overwritten by the partial below
     }
-    // ---- this item's partial: per head (m, l) from the lanes of quad 2c+e and the lane's 4 dims
-    float* ap = p.apart + (static_cast<size_t>(h) * p.attn_max_chunks + ck) * G * 132;
+    if (has_slice && lane == 0) mbar_arrive(sm.empty + slot);
+    // ---- this warp's partial into shared memory: [head][acc 128 | m | l]
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) {
-      *reinterpret_cast<float4*>(ap + hh * 132 + lane * 4) = make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
+      *reinterpret_cast<float4*>(wpart + hh * kAttnPart + lane * 4) = make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
       if (lane == hh / 2) {  // lane (g = 0, c = hh/2) holds column hh = 2c + e
-        ap[hh * 132 + 128] = m2[hh & 1];
-        ap[hh * 132 + 129] = l2[hh & 1];
+        wpart[hh * kAttnPart + 128] = m2[hh & 1];
+        wpart[hh * kAttnPart + 129] = l2[hh & 1];
       }
     }
-    __threadfence();
-    __syncwarp();
-    unsigned old = 0;
-    if (lane == 0) old = atomicAdd(p.acount + h, 1u);
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (static_cast<int>(old) + 1 != nch) continue;
-    // ---- last item of KV head h: merge its chunks in order
-    __threadfence();
-    if (lane == 0) p.acount[h] = 0u;
-    const float* base = p.apart + static_cast<size_t>(h) * p.attn_max_chunks * G * 132;
-#pragma unroll
-    for (int hh = 0; hh < G; ++hh) {
+    named_sync();
+    // ---- merge the warps' partials in token order; thread -> (head, dim) outputs
+    float* gbase = p.apart + (static_cast<size_t>(h) * p.attn_max_chunks) * G * kAttnPart;
+    for (int o = tid; o < G * 128; o += kConsumerThreads) {
+      const int hh = o >> 7, d = o & 127;
       float M = -INFINITY;
-      for (int c2 = 0; c2 < nch; ++c2) M = fmaxf(M, ldcg_f(base + (c2 * G + hh) * 132 + 128));
-      float Lsum = 0.f, o[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int c2 = 0; c2 < nch; ++c2) {
-        const float* e = base + (c2 * G + hh) * 132;
-        const float w = expf(ldcg_f(e + 128) - M);
-        Lsum = fmaf(ldcg_f(e + 129), w, Lsum);
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(e + lane * 4));
-        o[0] = fmaf(a.x, w, o[0]);
-        o[1] = fmaf(a.y, w, o[1]);
-        o[2] = fmaf(a.z, w, o[2]);
-        o[3] = fmaf(a.w, w, o[3]);
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, allpart[(w * G + hh) * kAttnPart + 128]);
+      float Lsum = 0.f, A = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) {
+        const float* e = allpart + (w * G + hh) * kAttnPart;
+        const float wt = e[128] == -INFINITY ? 0.f : expf(e[128] - M);
+        Lsum = fmaf(e[129], wt, Lsum);
+        A = fmaf(e[d], wt, A);
       }
-      const float inv = Lsum > 0.f ? 1.0f / Lsum : 0.f;
-      __nv_bfloat16* dst = p.attn + (h * G + hh) * 128 + lane * 4;
-      *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
-      *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
+      if (spans == 1) {
+        p.attn[(h * G + hh) * 128 + d] = __float2bfloat16_rn(Lsum > 0.f ? A / Lsum : 0.f);
+      } else {
+        float* gp = gbase + (span * G + hh) * kAttnPart;
+        gp[d] = A;
+        if (d == 0) {
+          gp[128] = M;
+          gp[129] = Lsum;
+        }
+      }
     }
+    if (spans > 1) {
+      // spans of this KV head: the CTA that finishes the last one merges them in span order
+      named_sync();
+      if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(p.acount + h, 1u);
+        misc->last = (static_cast<int>(old) + 1 == spans) ? 1 : 0;
+        if (misc->last) {
+          __threadfence();
+          p.acount[h] = 0u;
+        }
+      }
+      named_sync();
+      if (misc->last) {
+        for (int o = tid; o < G * 128; o += kConsumerThreads) {
+          const int hh = o >> 7, d = o & 127;
+          float M = -INFINITY;
+          for (int j = 0; j < spans; ++j) M = fmaxf(M, ldcg_f(gbase + (j * G + hh) * kAttnPart + 128));
+          float Lsum = 0.f, A = 0.f;
+          for (int j0 = 0; j0 < spans; j0 += 8) {
+            float mv[8], lv[8], av[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float* e = gbase + ((j0 + j) * G + hh) * kAttnPart;
+              const bool ok = j0 + j < spans;
+              mv[j] = ok ? ldcg_f(e + 128) : -INFINITY;
+              lv[j] = ok ? ldcg_f(e + 129) : 0.f;
+              av[j] = ok ? ldcg_f(e + d) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float wt = mv[j] == -INFINITY ? 0.f : expf(mv[j] - M);
+              Lsum = fmaf(lv[j], wt, Lsum);
+              A = fmaf(av[j], wt, A);
+            }
+          }
+          p.attn[(h * G + hh) * 128 + d] = __float2bfloat16_rn(Lsum > 0.f ? A / Lsum : 0.f);
+        }
+      }
+    }
+    // ---- KV head h's output is complete for this layer (written by this CTA)
+    named_sync();
+    if (tid == 0 && (spans == 1 || misc->last)) {
+      __threadfence();
+      st_volatile_u32(p.hdr + kHdrAttn + h, static_cast<unsigned>(layer + 1));
+    }
+    named_sync();  // the scratch is reused by the next item
+    seq += static_cast<uint32_t>(slices);
   }
 }
 
 // --------------------------------------------------------------- producer
+// Attention slices of this CTA's items: the cache rows below pos (the new row is
+// built by the consumer) are copied into one ring slot per slice, so the
+// attention reads K and V from shared memory. Slots holding no rows complete
+// without a copy.
+__device__ void produce_attention(const Params& p, const Smem& s, const Layer& L, int pos, uint32_t& seq,
+                                  uint64_t pol) {
+  const int n = pos + 1;
+  const int spans = (n + kAttnSpan - 1) / kAttnSpan;
+  const int items = p.kv_heads * spans;
+  const size_t cap = static_cast<size_t>(p.capacity);
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int h = item / spans, tspan = (item % spans) * kAttnSpan;
+    const int slices = attn_slices(item, spans, n);
+    for (int w = 0; w < slices; ++w, ++seq) {
+      if (*reinterpret_cast<volatile int*>(&s.misc->abort)) return;
+      const int slot = static_cast<int>(seq % static_cast<uint32_t>(p.slots));
+      const uint32_t use = seq / static_cast<uint32_t>(p.slots);
+      if (use > 0 && !wait_bar(s.empty + slot, (use - 1) & 1u, p, s.misc)) return;
+      const int tb = tspan + w * kAttnChunk;
+      const int cnt = min(kAttnChunk, pos - tb);  // rows below the new token
+      if (cnt <= 0) {
+        mbar_arrive_expect_tx(s.full + slot, 0u);
+        continue;
+      }
+      const int cnt8 = (cnt + 7) & ~7;  // scale copies in 16-byte units (capacity is a multiple of 16)
+      uint8_t* dst = s.ring + static_cast<size_t>(slot) * p.slot_bytes;
+      mbar_arrive_expect_tx(s.full + slot, static_cast<uint32_t>(2 * cnt * 128 + 2 * cnt8 * 2));
+      const size_t row0 = static_cast<size_t>(h) * cap + tb;
+      (void)pol;  // cache rows are read again next step: no evict-first hint
+      bulk_copy_g2s(dst + kSliceK, L.k_cache + row0 * 128, static_cast<uint32_t>(cnt * 128), s.full + slot);
+      bulk_copy_g2s(dst + kSliceV, L.v_cache + row0 * 128, static_cast<uint32_t>(cnt * 128), s.full + slot);
+      bulk_copy_g2s(dst + kSliceKs, L.k_scale + row0, static_cast<uint32_t>(cnt8 * 2), s.full + slot);
+      bulk_copy_g2s(dst + kSliceVs, L.v_scale + row0, static_cast<uint32_t>(cnt8 * 2), s.full + slot);
+    }
+  }
+}
+
 __device__ void produce_op(const Params& p, const Smem& s, const Stream& st, const uint8_t* stream, uint32_t& seq,
                            uint64_t pol) {
   const int W = gridDim.x, cta = blockIdx.x;
@@ -971,6 +1212,8 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     mbar_fence_init();
     s.misc->abort = 0;
     s.misc->key = 0ull;
+    s.misc->wait_ns = 0ull;
+    s.misc->busy_ns = 0ull;
   }
   for (int i = threadIdx.x; i < kRbSlots; i += blockDim.x) s.rbcnt[i] = 0u;
   for (int i = threadIdx.x; i < 64; i += blockDim.x) reinterpret_cast<uint32_t*>(base + kOffZero)[i] = 0u;
@@ -991,6 +1234,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
       for (int l = 0; l < p.num_layers; ++l) {
         const Layer& L = p.layers[l];
         produce_op(p, s, p.sq, L.qkv, seq, pol);
+        produce_attention(p, s, L, pos, seq, pol);
         produce_op(p, s, p.so, L.o, seq, pol);
         produce_op(p, s, p.sgu, L.gateup, seq, pol);
         produce_op(p, s, p.sdn, L.down, seq, pol);
@@ -1007,19 +1251,21 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
   }
 
   // ---------------- consumer warps
-  const int W = gridDim.x;
   const int tid = threadIdx.x;
   if (p.trace != nullptr && tid == 0)
-    p.trace[(static_cast<size_t>(blockIdx.x) * p.trace_slots + p.trace_slots - 1) * 2] = global_ns();
+    p.trace[(static_cast<size_t>(blockIdx.x) * p.trace_slots + p.trace_slots - 1) * 4] = global_ns();
   const int token = p.tokens[0];
   const __nv_bfloat16* emb = p.embed + static_cast<size_t>(min(max(token, 0), p.vocab_total - 1)) * p.hidden;
   uint32_t seq = 0;
   unsigned joins = 0;
   const int G = p.heads / p.kv_heads;
   const int nwords = p.hidden / 8;
+  const int act_chunk = p.sdn.ck * 64;       // activation values per down K chunk
+  const int gu_rbs_per_chunk = act_chunk / 16;
   load_residual(emb, p.hidden, p.eps, s.xres, s.misc);
   for (int l = 0; l < p.num_layers; ++l) {
     const Layer& L = p.layers[l];
+    const int mk = l * kMarksPerLayer;
     // ---- RMSNorm + QKV projection (per-chunk partials; RoPE happens in the attention items)
     if (l > 0) fold_residual(p.pdn, nullptr, p.hidden, p.eps, s.xres, s.misc);
     for (int v = tid; v < nwords; v += kConsumerThreads) {
@@ -1028,24 +1274,43 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
       put_w8(s.xs, v, f);
     }
     named_sync();
-    run_partials<K_W8>(p, s, p.sq, false, p.pqkv, 8, 0, seq);
-    grid_join(p, s.misc, (++joins) * W);
-    // ---- attention of the new token
+    mark(p, s.misc, mk + 0);
+    run_partials<K_W8>(p, s, p.sq, false, p.pqkv, 8, 0, seq, p.hdr + kHdrQkv, 8);
+    mark(p, s.misc, mk + 1);
+    // ---- attention of the new token (items wait for their heads' QKV tiles)
+    named_sync();  // the attention scratch aliases the staged activations
     uint8_t* scratch = base + kOffPart;
-    if (G == 1) attention_step<1>(p, L, pos, scratch);
-    else if (G == 2) attention_step<2>(p, L, pos, scratch);
-    else attention_step<4>(p, L, pos, scratch);
-    grid_join(p, s.misc, (++joins) * W);
-    // ---- o_proj (partials; the residual add happens in the next prologue)
-    for (int v = tid; v < p.heads * 16; v += kConsumerThreads) {
-      float f[8];
-      plain8(p.attn, v, f);
-      put_w8(s.xs, v, f);
+    if (G == 1) attention_step<1>(p, s, L, l, pos, scratch, seq);
+    else if (G == 2) attention_step<2>(p, s, L, l, pos, scratch, seq);
+    else attention_step<4>(p, s, L, l, pos, scratch, seq);
+    mark(p, s.misc, mk + 2);
+    named_sync();
+    // ---- o_proj: this CTA's tiles (K-chunk-major) need the attention output of their chunks' KV heads
+    {
+      const Stream& st = p.so;
+      int t0, t1;
+      cta_range(st.rbs * st.chunks, t0, t1);
+      if (t1 > t0) {
+        const int c0 = t0 / st.rbs, c1 = (t1 - 1) / st.rbs;
+        if (tid == 0) {
+          // KV heads whose query heads feed K values [c0*ck, (c1+1)*ck)
+          const int h0 = (c0 * st.ck) / (128 * G), h1 = ((c1 + 1) * st.ck - 1) / (128 * G);
+          for (int h = h0; h <= h1; ++h)
+            if (!spin_geq(p, s.misc, p.hdr + kHdrAttn + h, static_cast<unsigned>(l + 1))) break;
+        }
+        named_sync();
+        for (int v = c0 * st.ck / 8 + tid; v < (c1 + 1) * st.ck / 8; v += kConsumerThreads) {
+          float f[8];
+          plain8(p.attn, v, f);
+          put_w8(s.xs, v, f);
+        }
+      }
     }
     named_sync();
-    run_partials<K_W8>(p, s, p.so, false, p.po, 8, 0, seq);
-    grid_join(p, s.misc, (++joins) * W);
-    // ---- residual += o; RMSNorm + gate/up (partials)
+    if (p.trace != nullptr && tid == 0) trace_mark(p, s.misc, mk + 3, global_ns(), global_ns());
+    run_partials<K_W8>(p, s, p.so, true, p.po, 8, 0, seq);
+    grid_join(p, s.misc, ++joins, mk + 4);
+    // ---- residual += o; RMSNorm + gate/up (partials; progress per down K chunk)
     fold_residual(p.po, L.o_scale, p.hidden, p.eps, s.xres, s.misc);
     for (int v0 = 0; v0 < nwords; v0 += kConsumerThreads) {
       const int v = v0 + tid;
@@ -1054,16 +1319,24 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
       put_w4(s.xs, s.om, v, v < nwords, f);
     }
     named_sync();
-    run_partials<K_W4PAIR>(p, s, p.sgu, false, p.pgu, 16, 0, seq);
-    grid_join(p, s.misc, (++joins) * W);
-    // ---- SwiGLU of the K chunks this CTA's down tiles read, then down (partials)
+    mark(p, s.misc, mk + 5);
+    run_partials<K_W4PAIR>(p, s, p.sgu, false, p.pgu, 16, 0, seq, p.hdr + kHdrGu, gu_rbs_per_chunk);
+    mark(p, s.misc, mk + 6);
+    // ---- SwiGLU of the K chunks this CTA's down tiles read (once their gate/up tiles are done), then down
+    named_sync();
     {
       const Stream& st = p.sdn;
       int t0, t1;
       cta_range(st.rbs * st.chunks, t0, t1);
       if (t1 > t0) {
-        const int ck = st.ck * 64;  // activation values per chunk
-        const int w0 = (t0 / st.rbs) * ck / 8, w1 = ((t1 - 1) / st.rbs + 1) * ck / 8;
+        const int c0 = t0 / st.rbs, c1 = (t1 - 1) / st.rbs;
+        if (tid == 0) {
+          const unsigned need = static_cast<unsigned>((l + 1) * gu_rbs_per_chunk * p.sgu.chunks);
+          for (int c = c0; c <= c1; ++c)
+            if (!spin_geq(p, s.misc, p.hdr + kHdrGu + c, need)) break;
+        }
+        named_sync();
+        const int w0 = c0 * act_chunk / 8, w1 = (c1 + 1) * act_chunk / 8;
         for (int v0 = w0 & ~7; v0 < w1; v0 += kConsumerThreads) {
           const int v = v0 + tid;
           const bool valid = v >= w0 && v < w1;
@@ -1082,8 +1355,9 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
       }
     }
     named_sync();
+    if (p.trace != nullptr && tid == 0) trace_mark(p, s.misc, mk + 7, global_ns(), global_ns());
     run_partials<K_W4>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
-    grid_join(p, s.misc, (++joins) * W);
+    grid_join(p, s.misc, ++joins, mk + 8);
   }
   // ---- residual += down; final RMSNorm + lm_head + greedy argmax
   fold_residual(p.pdn, nullptr, p.hidden, p.eps, s.xres, s.misc);
@@ -1097,10 +1371,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
   named_sync();
   if (tid == 0) {
     if (s.misc->key) atomicMax(p.keys, s.misc->key);
-    if (p.trace != nullptr) {
-      const int slot = static_cast<int>(joins);
-      if (slot < p.trace_slots) p.trace[(static_cast<size_t>(blockIdx.x) * p.trace_slots + slot) * 2] = global_ns();
-    }
+    if (p.trace != nullptr) trace_mark(p, s.misc, p.num_layers * kMarksPerLayer, global_ns(), global_ns());
   }
   // the residual stream of this step, for callers that inspect it (CTA 0)
   if (blockIdx.x == 0)
@@ -1123,6 +1394,13 @@ struct Geometry {
   int slot_bytes;
 };
 
+int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
+  return n;
+}
+
 int geometry(const sb_step_desc* d, Geometry* g) {
   SB_REQUIRE(d != nullptr, "null descriptor");
   SB_REQUIRE(d->head_dim == 128, "the decode-step kernel supports head_dim 128");
@@ -1133,6 +1411,8 @@ int geometry(const sb_step_desc* d, Geometry* g) {
   SB_REQUIRE(d->num_heads > 0 && d->num_kv_heads > 0 && d->num_heads % d->num_kv_heads == 0, "heads");
   const int G = d->num_heads / d->num_kv_heads;
   SB_REQUIRE(G == 1 || G == 2 || G == 4, "query heads per KV head must be 1, 2 or 4");
+  SB_REQUIRE(d->num_heads + 2 * d->num_kv_heads <= 64, "at most 64 attention heads (query + key + value) per rank");
+  SB_REQUIRE(sm_count() <= kMaxCtas, "at most 256 SMs");
   const int qk = d->num_heads * 128;  // o_proj K (this rank)
   SB_REQUIRE(qk <= kMaxK && qk % (kChunks * 32 / d->world) == 0, "o_proj K must split into 8 chunks of 32-multiples");
   SB_REQUIRE(d->inter > 0 && d->inter % 16 == 0 && d->inter <= kMaxK, "inter must be a multiple of 16, <= 10240");
@@ -1150,10 +1430,11 @@ int geometry(const sb_step_desc* d, Geometry* g) {
   g->slm = {(d->vocab + 15) / 16, kChunks, 16 * lck * 2, lck};
   int tmax = 0;
   for (const Stream* st : {&g->sq, &g->so, &g->sgu, &g->sdn, &g->slm}) tmax = tmax > st->tile ? tmax : st->tile;
+  tmax = tmax > kSliceBytes ? tmax : kSliceBytes;
   g->slot_bytes = (tmax + 127) / 128 * 128;
-  g->attn_chunks = (d->capacity + kAttnChunk - 1) / kAttnChunk;
+  g->attn_chunks = (d->capacity + kAttnSpan - 1) / kAttnSpan;
   Workspace& w = g->ws;
-  size_t off = 256;  // header words
+  size_t off = kHdrBytes;  // header words and release flags
   auto take = [&](size_t bytes) {
     const size_t at = off;
     off = (off + bytes + 255) / 256 * 256;
@@ -1162,7 +1443,7 @@ int geometry(const sb_step_desc* d, Geometry* g) {
   w.gcount = take(static_cast<size_t>(g->slm.rbs) * 4);
   w.acount = take(64 * 4);
   w.gpart = take(static_cast<size_t>(g->slm.rbs) * kChunks * 32 * 4);
-  w.apart = take(static_cast<size_t>(d->num_kv_heads) * g->attn_chunks * G * 132 * 4);
+  w.apart = take(static_cast<size_t>(d->num_kv_heads) * g->attn_chunks * G * kAttnPart * 4);
   w.pqkv = take(static_cast<size_t>(g->sq.rbs) * 16 * 8 * 4);
   w.po = take(static_cast<size_t>(d->hidden) * 8 * 4);
   w.pgu = take(static_cast<size_t>(d->inter) * 16 * 4);
@@ -1171,12 +1452,7 @@ int geometry(const sb_step_desc* d, Geometry* g) {
   return SB_OK;
 }
 
-int sm_count() {
-  int dev = 0, n = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
-  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) return 148;
-  return n;
-}
+
 
 }  // namespace step
 }  // namespace sb
@@ -1184,7 +1460,7 @@ int sm_count() {
 using namespace sb;
 using namespace sb::step;
 
-extern "C" int sb_step_trace_slots(int num_layers) { return num_layers * 5 + 2; }
+extern "C" int sb_step_trace_slots(int num_layers) { return num_layers * kMarksPerLayer + 2; }
 
 extern "C" size_t sb_step_workspace_size(const sb_step_desc* d) {
   Geometry g;
@@ -1239,6 +1515,8 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   unsigned* ws = static_cast<unsigned*>(d->workspace);
   p.sync = ws;
   p.status = ws + 1;
+  p.hdr = ws;
+  p.release = ws + 256;
   uint8_t* wb = static_cast<uint8_t*>(d->workspace);
   p.gcount = reinterpret_cast<unsigned*>(wb + g.ws.gcount);
   p.acount = reinterpret_cast<unsigned*>(wb + g.ws.acount);
@@ -1256,10 +1534,14 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   p.slm = g.slm;
   p.slot_bytes = g.slot_bytes;
   p.trace = d->trace;
-  p.trace_slots = d->num_layers * 5 + 2;
+  p.trace_slots = d->num_layers * kMarksPerLayer + 2;
   int max_smem = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  {
+    cudaFuncAttributes fa{};
+    if (cudaFuncGetAttributes(&fa, step_kernel) == cudaSuccess) max_smem -= static_cast<int>(fa.sharedSizeBytes);
+  }
   const int fixed = kOffRing + 1024;  // + alignment slack
   p.slots = std::min(kMaxSlots, (max_smem - fixed) / g.slot_bytes);
   SB_REQUIRE(p.slots >= 4, "not enough shared memory for the weight ring");
@@ -1288,7 +1570,7 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
     }
   }
   // the arrival counter starts at zero for every step
-  cudaError_t err = cudaMemsetAsync(d->workspace, 0, 4, as_stream(stream));
+  cudaError_t err = cudaMemsetAsync(d->workspace, 0, kHdrBytes, as_stream(stream));
   if (err != cudaSuccess) return fail(SB_ECUDA, std::string("step counter reset: ") + cudaGetErrorString(err));
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(static_cast<unsigned>(sm_count()));

@@ -37,7 +37,7 @@ def qkv_row_order(num_heads, num_kv_heads, head_dim=128, device=None):
     return (hd * head_dim + hh * (head_dim // 2) + 8 * i + g).reshape(-1)
 
 
-def pack_w8(w_int8, chunk_k, row_order=None):
+def pack_w8(w_int8, chunk_k, row_order=None, chunk_major=False):
     """Per-channel int8 ``[N, K]`` -> W8 tile stream (uint8).
 
     Tile (block b, chunk c) is ``chunk_k/32`` runs of 512 bytes; in run j
@@ -50,7 +50,10 @@ def pack_w8(w_int8, chunk_k, row_order=None):
         raise ValueError("W8 stream: N % 16, K % chunk and chunk % 32 must be 0")
     u = w_int8.contiguous().view(torch.uint8) ^ 0x80
     t = u.view(n // 16, 2, 8, k // chunk_k, chunk_k // 32, 4, 2, 4)  # [rb, hh, g, ch, kb, c, word, byte]
-    return t.permute(0, 3, 4, 2, 5, 6, 1, 7).contiguous().view(-1)
+    t = t.permute(0, 3, 4, 2, 5, 6, 1, 7)  # [rb, ch, kb, g, c, word, hh, byte]
+    if chunk_major:  # tiles ordered by K chunk first (o_proj: a CTA's tiles read few chunks)
+        t = t.transpose(0, 1)
+    return t.contiguous().view(-1)
 
 
 def pack_w4(mats, groups_per_chunk, chunk_major=False):
@@ -130,7 +133,7 @@ class StepStreams:
         for li, layer in enumerate(dec.layers):
             qkv = pack_w8(layer["qkv_w"], 512, order)
             qkv_s = layer["qkv_s"][order].contiguous()
-            o = pack_w8(layer["o_w"], (dec.hq * d) // CHUNKS)
+            o = pack_w8(layer["o_w"], (dec.hq * d) // CHUNKS, chunk_major=True)
             gu = pack_w4([layer["gate"], layer["up"]], 8)
             dn = pack_w4([layer["down"]], down_groups, chunk_major=True)
             self.keep += [qkv, qkv_s, o, gu, dn]
