@@ -214,6 +214,16 @@ __device__ __forceinline__ unsigned long long global_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
+// Release-ordered add (this thread's earlier writes, and those ordered before
+// them by a barrier, are visible to whoever observes the new value).
+__device__ __forceinline__ void red_release_add(unsigned* addr, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* addr) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
 __device__ __forceinline__ void st_volatile_u32(unsigned* addr, unsigned v) {
   asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
@@ -223,9 +233,9 @@ __device__ __forceinline__ void st_volatile_u32(unsigned* addr, unsigned v) {
 // already recorded a failure, records it and raises the CTA's abort flag.
 __device__ bool spin_geq(const Params& p, Misc* misc, const unsigned* addr, unsigned target) {
   if (*reinterpret_cast<volatile int*>(&misc->abort)) return false;
-  if (ld_volatile_u32(addr) < target) {
+  if (ld_acquire_u32(addr) < target) {
     const long long start = clock64();
-    while (ld_volatile_u32(addr) < target) {
+    while (ld_acquire_u32(addr) < target) {
       if (clock64() - start > (1LL << 31) || ld_volatile_u32(p.status) != 0u) {
         atomicOr(p.status, kStatusTimeout);
         *reinterpret_cast<volatile int*>(&misc->abort) = 1;
@@ -261,30 +271,15 @@ __device__ void mark(const Params& p, Misc* misc, int slot) {
 
 // Grid-wide join between operators (join `idx`, 1-based, monotonic within a
 // launch): the CTA's consumer threads finish the operator; thread 0 adds the
-// CTA's arrival; the CTA whose arrival completes the join writes every CTA's
-// release flag (one line each, so the waiters do not poll a shared line);
-// then the CTA waits (bounded) for its own flag and releases its consumers.
+// CTA's arrival (release) and waits (bounded, acquire) until every CTA has
+// arrived idx times, then releases its consumers.
 __device__ void grid_join(const Params& p, Misc* misc, unsigned idx, int slot) {
   named_sync();
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    unsigned long long t0 = 0;
-    unsigned old = 0;
-    if (lane == 0) {
-      if (p.trace != nullptr) t0 = global_ns();
-      __threadfence();
-      old = atomicAdd(p.sync, 1u);
-    }
-    old = __shfl_sync(0xffffffffu, old, 0);
-    if (old + 1u == idx * gridDim.x) {
-      __threadfence();
-      for (int c = lane; c < static_cast<int>(gridDim.x); c += 32) st_volatile_u32(p.release + c * 32, idx);
-    }
-    if (lane == 0) {
-      spin_geq(p, misc, p.release + blockIdx.x * 32, idx);
-      if (p.trace != nullptr) trace_mark(p, misc, slot, t0, global_ns());
-    }
-    __syncwarp();
+  if (threadIdx.x == 0) {
+    const unsigned long long t0 = p.trace != nullptr ? global_ns() : 0ull;
+    red_release_add(p.sync, 1u);
+    spin_geq(p, misc, p.sync, idx * gridDim.x);
+    if (p.trace != nullptr) trace_mark(p, misc, slot, t0, global_ns());
   }
   named_sync();
 }
@@ -352,6 +347,45 @@ __device__ __forceinline__ void w4_convert(uint32_t w, uint32_t (&t)[4]) {
   t[3] = lop_and_or(s, 0x00F000F0u, 0x54005400u);
 }
 
+// The MMAs of one round (up to 8 groups) of a W4 tile; FULL rounds have no
+// per-group predicate, so loads of later groups can be scheduled early.
+template <int MATS, bool FULL>
+__device__ __forceinline__ void w4_round(const uint8_t* a_ptr, const uint8_t* xs, const uint8_t* zero, int gi0, int jn,
+                                         int g, int c, float (&acc)[MATS][4], float (&acc2)[MATS][4]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (FULL || j < jn) {
+      const int gi = gi0 + j;
+      const uint8_t* bp = (g == j) ? xs + gi * 128 : zero;
+      const uint4 b0 = lds128(bp + c * 16);
+      const uint4 b1 = lds128(bp + 64 + c * 16);
+      uint4 a[MATS];
+#pragma unroll
+      for (int m = 0; m < MATS; ++m) a[m] = lds128(a_ptr + (gi * MATS + m) * 512);
+#pragma unroll
+      for (int m = 0; m < MATS; ++m) {
+        uint32_t tg[4], th[4];
+        w4_convert(a[m].x, tg);
+        w4_convert(a[m].y, th);
+        {
+          const uint32_t fa[4] = {tg[0], th[0], tg[2], th[2]};
+          const uint32_t fb[4] = {tg[1], th[1], tg[3], th[3]};
+          mma_16816<false>(acc[m], fa, b0.x, b0.y);
+          mma_16816<true>(acc2[m], fb, b0.z, b0.w);
+        }
+        w4_convert(a[m].z, tg);
+        w4_convert(a[m].w, th);
+        {
+          const uint32_t fa[4] = {tg[0], th[0], tg[2], th[2]};
+          const uint32_t fb[4] = {tg[1], th[1], tg[3], th[3]};
+          mma_16816<false>(acc[m], fa, b1.x, b1.y);
+          mma_16816<true>(acc2[m], fb, b1.z, b1.w);
+        }
+      }
+    }
+  }
+}
+
 // W4 tile of MATS matrices (1 = down, 2 = gate+up) over `ngroups` groups of
 // 64. xs points at the chunk's first staged group, om at its (O, X) pairs.
 template <int MATS>
@@ -373,38 +407,8 @@ __device__ __forceinline__ void w4_tile(const uint8_t* tile, int ngroups, const 
 #pragma unroll
       for (int e = 0; e < 4; ++e) acc[m][e] = acc2[m][e] = 0.f;
     const int jn = min(8, ngroups - 8 * r);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      if (j < jn) {
-        const int gi = 8 * r + j;
-        const uint8_t* bp = (g == j) ? xs + gi * 128 : zero;
-        const uint4 b0 = lds128(bp + c * 16);
-        const uint4 b1 = lds128(bp + 64 + c * 16);
-        uint4 a[MATS];
-#pragma unroll
-        for (int m = 0; m < MATS; ++m) a[m] = lds128(a_ptr + (gi * MATS + m) * 512);
-#pragma unroll
-        for (int m = 0; m < MATS; ++m) {
-          uint32_t tg[4], th[4];
-          w4_convert(a[m].x, tg);
-          w4_convert(a[m].y, th);
-          {
-            const uint32_t fa[4] = {tg[0], th[0], tg[2], th[2]};
-            const uint32_t fb[4] = {tg[1], th[1], tg[3], th[3]};
-            mma_16816<false>(acc[m], fa, b0.x, b0.y);
-            mma_16816<true>(acc2[m], fb, b0.z, b0.w);
-          }
-          w4_convert(a[m].z, tg);
-          w4_convert(a[m].w, th);
-          {
-            const uint32_t fa[4] = {tg[0], th[0], tg[2], th[2]};
-            const uint32_t fb[4] = {tg[1], th[1], tg[3], th[3]};
-            mma_16816<false>(acc[m], fa, b1.x, b1.y);
-            mma_16816<true>(acc2[m], fb, b1.z, b1.w);
-          }
-        }
-      }
-    }
+    if (jn == 8) w4_round<MATS, true>(a_ptr, xs, zero, 8 * r, 8, g, c, acc, acc2);
+    else w4_round<MATS, false>(a_ptr, xs, zero, 8 * r, jn, g, c, acc, acc2);
 #pragma unroll
     for (int m = 0; m < MATS; ++m)
 #pragma unroll
@@ -615,6 +619,16 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
   int t0, t1;
   cta_range(T, t0, t1);
   const int g = lane >> 2;
+  // progress of this warp's tiles not yet published: counter index and count
+  int pend_idx = -1;
+  unsigned pend_cnt = 0;
+  auto publish = [&]() {
+    if (cnt != nullptr && pend_cnt != 0u) {
+      __syncwarp();
+      if (lane == 0) red_release_add(cnt + pend_idx, pend_cnt);
+      pend_cnt = 0;
+    }
+  };
   for (int t = t0; t < t1; ++t) {
     const uint32_t q = seq + static_cast<uint32_t>(t - t0);
     if (static_cast<int>(q % kConsumers) != warp) continue;
@@ -653,13 +667,15 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
       }
     }
     if (cnt != nullptr) {
-      __syncwarp();
-      if (lane == 0) {
-        __threadfence();
-        atomicAdd(cnt + rb / cnt_rbs, 1u);
+      const int idx = rb / cnt_rbs;
+      if (idx != pend_idx) {
+        publish();
+        pend_idx = idx;
       }
+      ++pend_cnt;
     }
   }
+  publish();
   seq += static_cast<uint32_t>(t1 - t0);
 }
 
@@ -866,7 +882,7 @@ __device__ __forceinline__ int attn_slices(int item, int spans, int n) {
 
 template <int G>
 __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, int layer, int pos, uint8_t* scratch,
-                               uint32_t& seq) {
+                               uint32_t& seq, const float (&cs)[2], const float (&sn)[2]) {
   Misc* misc = sm.misc;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int g = lane >> 2, c = lane & 3;
@@ -878,12 +894,6 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
   float* wpart = reinterpret_cast<float*>(scratch + 1024) + warp * G * kAttnPart;      // this warp's partial
   float* pw = wpart;                                                                   // [32][4] probabilities (before the partial)
   float* allpart = reinterpret_cast<float*>(scratch + 1024);
-  float cs[2], sn[2];
-#pragma unroll
-  for (int e = 0; e < 2; ++e) {
-    const int d = 8 * (lane >> 2) + 2 * (lane & 3) + e;
-    sincosf(static_cast<float>(pos) * p.inv_freq[d], &sn[e], &cs[e]);
-  }
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
     const int h = item / spans, span = item % spans;
     const int tspan = span * kAttnSpan;
@@ -896,7 +906,6 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
     uint8_t* tile = sm.ring + static_cast<size_t>(slot) * p.slot_bytes;
     if (has_slice) wait_bar(sm.full + slot, (q_slot / static_cast<uint32_t>(p.slots)) & 1u, p, misc);
     const bool span_has_pos = pos >= tspan && pos < tspan + kAttnSpan;
-    const bool newest = pos >= tb && pos < tb + kAttnChunk;
     int8_t* kc = L.k_cache + static_cast<size_t>(h) * cap * 128;
     int8_t* vc = L.v_cache + static_cast<size_t>(h) * cap * 128;
     __half* ksc = L.k_scale + static_cast<size_t>(h) * cap;
@@ -920,16 +929,27 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
       *reinterpret_cast<__half2*>(qs + warp * 128 + d0) = __floats2half2_rn(lo[0], lo[1]);
       *reinterpret_cast<__half2*>(qs + warp * 128 + d0 + 64) = __floats2half2_rn(hi[0], hi[1]);
     }
-    if (newest) {
-      // the new token's K/V row: into the cache and into this warp's slice
-      const int r = pos - tb;
-      float lo[2], hi[2];
-      head_rows(p, L, p.heads + h, true, cs, sn, lane, lo, hi);
-      quantize_row(lo, hi, lane, kc + static_cast<size_t>(pos) * 128, ksc + pos,
-                   reinterpret_cast<int8_t*>(tile + kSliceK) + r * 128, reinterpret_cast<__half*>(tile + kSliceKs) + r);
-      head_rows(p, L, p.heads + p.kv_heads + h, false, cs, sn, lane, lo, hi);
-      quantize_row(lo, hi, lane, vc + static_cast<size_t>(pos) * 128, vsc + pos,
-                   reinterpret_cast<int8_t*>(tile + kSliceV) + r * 128, reinterpret_cast<__half*>(tile + kSliceVs) + r);
+    if (span_has_pos) {
+      // the new token's K row (its slice's warp) and V row (the next warp): into the cache and
+      // into the slice, after the slice's copies have landed
+      const int wn = (pos - tspan) / kAttnChunk;
+      const int wv = wn + 1 < kConsumers ? wn + 1 : 0;
+      if (warp == wn || warp == wv) {
+        const bool is_k = warp == wn;
+        const uint32_t qn = seq + static_cast<uint32_t>(wn);
+        const int sn2 = static_cast<int>(qn % static_cast<uint32_t>(p.slots));
+        uint8_t* tn = sm.ring + static_cast<size_t>(sn2) * p.slot_bytes;
+        if (!is_k) wait_bar(sm.full + sn2, (qn / static_cast<uint32_t>(p.slots)) & 1u, p, misc);
+        const int r = pos - (tspan + wn * kAttnChunk);
+        float lo[2], hi[2];
+        head_rows(p, L, is_k ? p.heads + h : p.heads + p.kv_heads + h, is_k, cs, sn, lane, lo, hi);
+        if (is_k)
+          quantize_row(lo, hi, lane, kc + static_cast<size_t>(pos) * 128, ksc + pos,
+                       reinterpret_cast<int8_t*>(tn + kSliceK) + r * 128, reinterpret_cast<__half*>(tn + kSliceKs) + r);
+        else
+          quantize_row(lo, hi, lane, vc + static_cast<size_t>(pos) * 128, vsc + pos,
+                       reinterpret_cast<int8_t*>(tn + kSliceV) + r * 128, reinterpret_cast<__half*>(tn + kSliceVs) + r);
+      }
     }
     named_sync();
     float m2[2] = {-INFINITY, -INFINITY}, l2[2] = {0.f, 0.f};
@@ -1055,8 +1075,8 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
       }
     }
     named_sync();
-    // ---- merge the warps' partials in token order; thread -> (head, dim) outputs
-    float* gbase = p.apart + (static_cast<size_t>(h) * p.attn_max_chunks) * G * kAttnPart;
+    // ---- merge the warps' partials in token order into this span's partial (L2); thread -> (head, dim)
+    float* gp0 = p.apart + ((static_cast<size_t>(h) * p.attn_max_chunks + span) * G) * kAttnPart;
     for (int o = tid; o < G * 128; o += kConsumerThreads) {
       const int hh = o >> 7, d = o & 127;
       float M = -INFINITY;
@@ -1070,63 +1090,16 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
         Lsum = fmaf(e[129], wt, Lsum);
         A = fmaf(e[d], wt, A);
       }
-      if (spans == 1) {
-        p.attn[(h * G + hh) * 128 + d] = __float2bfloat16_rn(Lsum > 0.f ? A / Lsum : 0.f);
-      } else {
-        float* gp = gbase + (span * G + hh) * kAttnPart;
-        gp[d] = A;
-        if (d == 0) {
-          gp[128] = M;
-          gp[129] = Lsum;
-        }
+      float* gp = gp0 + hh * kAttnPart;
+      gp[d] = A;
+      if (d == 0) {
+        gp[128] = M;
+        gp[129] = Lsum;
       }
     }
-    if (spans > 1) {
-      // spans of this KV head: the CTA that finishes the last one merges them in span order
-      named_sync();
-      if (tid == 0) {
-        __threadfence();
-        const unsigned old = atomicAdd(p.acount + h, 1u);
-        misc->last = (static_cast<int>(old) + 1 == spans) ? 1 : 0;
-        if (misc->last) {
-          __threadfence();
-          p.acount[h] = 0u;
-        }
-      }
-      named_sync();
-      if (misc->last) {
-        for (int o = tid; o < G * 128; o += kConsumerThreads) {
-          const int hh = o >> 7, d = o & 127;
-          float M = -INFINITY;
-          for (int j = 0; j < spans; ++j) M = fmaxf(M, ldcg_f(gbase + (j * G + hh) * kAttnPart + 128));
-          float Lsum = 0.f, A = 0.f;
-          for (int j0 = 0; j0 < spans; j0 += 8) {
-            float mv[8], lv[8], av[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float* e = gbase + ((j0 + j) * G + hh) * kAttnPart;
-              const bool ok = j0 + j < spans;
-              mv[j] = ok ? ldcg_f(e + 128) : -INFINITY;
-              lv[j] = ok ? ldcg_f(e + 129) : 0.f;
-              av[j] = ok ? ldcg_f(e + d) : 0.f;
-            }
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const float wt = mv[j] == -INFINITY ? 0.f : expf(mv[j] - M);
-              Lsum = fmaf(lv[j], wt, Lsum);
-              A = fmaf(av[j], wt, A);
-            }
-          }
-          p.attn[(h * G + hh) * 128 + d] = __float2bfloat16_rn(Lsum > 0.f ? A / Lsum : 0.f);
-        }
-      }
-    }
-    // ---- KV head h's output is complete for this layer (written by this CTA)
+    // ---- one more span of KV head h is published (the o_proj prologue merges the spans)
     named_sync();
-    if (tid == 0 && (spans == 1 || misc->last)) {
-      __threadfence();
-      st_volatile_u32(p.hdr + kHdrAttn + h, static_cast<unsigned>(layer + 1));
-    }
+    if (tid == 0) red_release_add(p.hdr + kHdrAttn + h, 1u);
     named_sync();  // the scratch is reused by the next item
     seq += static_cast<uint32_t>(slices);
   }
@@ -1263,6 +1236,13 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
   const int act_chunk = p.sdn.ck * 64;       // activation values per down K chunk
   const int gu_rbs_per_chunk = act_chunk / 16;
   load_residual(emb, p.hidden, p.eps, s.xres, s.misc);
+  // RoPE angles of this position for the lane's two dims (the same in every layer)
+  float rope_cs[2], rope_sn[2];
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int d = 8 * ((tid & 31) >> 2) + 2 * (tid & 3) + e;
+    sincosf(static_cast<float>(pos) * p.inv_freq[d], &rope_sn[e], &rope_cs[e]);
+  }
   for (int l = 0; l < p.num_layers; ++l) {
     const Layer& L = p.layers[l];
     const int mk = l * kMarksPerLayer;
@@ -1280,9 +1260,9 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     // ---- attention of the new token (items wait for their heads' QKV tiles)
     named_sync();  // the attention scratch aliases the staged activations
     uint8_t* scratch = base + kOffPart;
-    if (G == 1) attention_step<1>(p, s, L, l, pos, scratch, seq);
-    else if (G == 2) attention_step<2>(p, s, L, l, pos, scratch, seq);
-    else attention_step<4>(p, s, L, l, pos, scratch, seq);
+    if (G == 1) attention_step<1>(p, s, L, l, pos, scratch, seq, rope_cs, rope_sn);
+    else if (G == 2) attention_step<2>(p, s, L, l, pos, scratch, seq, rope_cs, rope_sn);
+    else attention_step<4>(p, s, L, l, pos, scratch, seq, rope_cs, rope_sn);
     mark(p, s.misc, mk + 2);
     named_sync();
     // ---- o_proj: this CTA's tiles (K-chunk-major) need the attention output of their chunks' KV heads
@@ -1292,16 +1272,55 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
       cta_range(st.rbs * st.chunks, t0, t1);
       if (t1 > t0) {
         const int c0 = t0 / st.rbs, c1 = (t1 - 1) / st.rbs;
+        const int spans = (pos + kAttnSpan) / kAttnSpan;  // ceil((pos + 1) / kAttnSpan)
         if (tid == 0) {
-          // KV heads whose query heads feed K values [c0*ck, (c1+1)*ck)
+          // every span of the KV heads whose query heads feed K values [c0*ck, (c1+1)*ck)
           const int h0 = (c0 * st.ck) / (128 * G), h1 = ((c1 + 1) * st.ck - 1) / (128 * G);
           for (int h = h0; h <= h1; ++h)
-            if (!spin_geq(p, s.misc, p.hdr + kHdrAttn + h, static_cast<unsigned>(l + 1))) break;
+            if (!spin_geq(p, s.misc, p.hdr + kHdrAttn + h, static_cast<unsigned>((l + 1) * spans))) break;
         }
         named_sync();
+        // attention output: the spans' partials merged in span order, rounded to bf16
         for (int v = c0 * st.ck / 8 + tid; v < (c1 + 1) * st.ck / 8; v += kConsumerThreads) {
+          const int qh = (v * 8) >> 7, d0 = (v * 8) & 127;
+          const int h = qh / G, hh = qh % G;
+          const float* e0 = p.apart + (static_cast<size_t>(h) * p.attn_max_chunks * G + hh) * kAttnPart;
+          const size_t jstride = static_cast<size_t>(G) * kAttnPart;
+          // spans in batches of 4: all of a batch's loads are issued before any is used
+          float M = -INFINITY;
+          for (int j0 = 0; j0 < spans; j0 += 4) {
+            float mv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mv[j] = j0 + j < spans ? ldcg_f(e0 + (j0 + j) * jstride + 128) : -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) M = fmaxf(M, mv[j]);
+          }
+          float Lsum = 0.f, A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int j0 = 0; j0 < spans; j0 += 4) {
+            float4 a0[4], a1[4];
+            float mj[4], lj[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float* e = e0 + (j0 + j) * jstride;
+              const bool ok = j0 + j < spans;
+              a0[j] = ok ? __ldcg(reinterpret_cast<const float4*>(e + d0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+              a1[j] = ok ? __ldcg(reinterpret_cast<const float4*>(e + d0 + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+              mj[j] = ok ? ldcg_f(e + 128) : -INFINITY;
+              lj[j] = ok ? ldcg_f(e + 129) : 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float wt = mj[j] == -INFINITY ? 0.f : expf(mj[j] - M);
+              Lsum = fmaf(lj[j], wt, Lsum);
+              const float av[8] = {a0[j].x, a0[j].y, a0[j].z, a0[j].w, a1[j].x, a1[j].y, a1[j].z, a1[j].w};
+#pragma unroll
+              for (int i = 0; i < 8; ++i) A[i] = fmaf(av[i], wt, A[i]);
+            }
+          }
+          const float inv = Lsum > 0.f ? 1.0f / Lsum : 0.f;
           float f[8];
-          plain8(p.attn, v, f);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = bfr(A[i] * inv);
           put_w8(s.xs, v, f);
         }
       }
