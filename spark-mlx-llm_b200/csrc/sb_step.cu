@@ -53,7 +53,8 @@ constexpr int kMaxK = 10240;                 // staged activation values
 constexpr int kMaxHidden = 4096;             // residual stream kept in shared memory
 constexpr int kMaxGroups = kMaxK / 64;
 constexpr int kChunks = 8;                   // K chunks of o/down/lm_head (tensor-parallel unit)
-constexpr int kAttnChunk = 32;               // tokens per attention work item (one warp)
+constexpr int kAttnChunk = 16;               // tokens of an attention slice (one warp)
+constexpr int kAttnRbk = kAttnChunk / 16;    // 16-token MMA row blocks per slice
 constexpr int kMaxLayers = 128;
 constexpr unsigned kStatusRange = 2u;        // status bit: position outside the KV cache
 // Workspace header (zeroed before every launch): word 0 the grid arrival
@@ -65,6 +66,9 @@ constexpr int kHdrQkv = 64, kHdrAttn = 128, kHdrGu = 192;
 constexpr int kMaxCtas = 256;
 constexpr size_t kHdrBytes = 1024 + static_cast<size_t>(kMaxCtas) * 128;
 constexpr int kMarksPerLayer = 9;  // trace marks per layer
+constexpr int kAttnMarks = 4;      // extra trace marks per layer inside an attention item
+constexpr int kTlEvents = 96;      // timeline events per consumer warp (one traced layer)
+constexpr int kTlSlots = kConsumers * kTlEvents / 2;  // trace slots (4 x u64) holding the timeline
 
 // shared-memory layout (offsets from a 1024-byte aligned base)
 constexpr int kOffBars = 0;            // full[16], empty[16]
@@ -80,7 +84,7 @@ constexpr int kOffRing = ((kOffXs + kMaxK * 2 + 1023) / 1024) * 1024;
 // attention scratch (aliases part + xs, unused during attention): q of the
 // G heads as fp16 [4][128], then per warp its partial [4 heads][132] floats
 // (the warp's probabilities [32][4] live there until the partial is written)
-static_assert(kOffPart + 1024 + kConsumers * 4 * 132 * 4 <= kOffRing, "attention scratch");
+static_assert(kOffPart + 1024 + kConsumers * 4 * 132 * 4 + (kConsumers + 2) * 4 * 4 <= kOffRing, "attention scratch");
 
 struct Misc {
   int abort;
@@ -90,7 +94,10 @@ struct Misc {
   int last;                    // attention: this CTA merges the KV head's spans
   unsigned long long wait_ns;  // tracing: consumer time waiting for tiles (sum over warps)
   unsigned long long busy_ns;  // tracing: consumer time computing tiles
+  int tl_on;                   // tracing: this layer's events go to the per-warp timeline
+  unsigned tl_n[kConsumers];   // tracing: timeline events recorded per consumer warp
 };
+static_assert(sizeof(Misc) <= 768, "misc block");
 
 struct Layer {
   const uint8_t* qkv;
@@ -259,6 +266,20 @@ __device__ void trace_mark(const Params& p, Misc* misc, int slot, unsigned long 
   misc->wait_ns = 0;
   misc->busy_ns = 0;
 }
+// Timeline event (tracing, layer num_layers / 2 only): lane 0 of a consumer warp
+// records (code, aux) with the SM clock; the analysis reads it per CTA and warp.
+__device__ __forceinline__ void tl_event(const Params& p, const Misc* misc, int code, int aux = 0) {
+  if (p.trace == nullptr) return;
+  if ((threadIdx.x & 31) != 0 || !misc->tl_on) return;
+  const int warp = threadIdx.x >> 5;
+  Misc* m = const_cast<Misc*>(misc);
+  const unsigned i = m->tl_n[warp]++;
+  if (i >= static_cast<unsigned>(kTlEvents)) return;
+  unsigned long long* ev = p.trace + (static_cast<size_t>(blockIdx.x) * p.trace_slots + p.trace_slots - kTlSlots) * 4 +
+                           (static_cast<size_t>(warp) * kTlEvents + i) * 2;
+  ev[0] = static_cast<unsigned long long>(code) | (static_cast<unsigned long long>(static_cast<unsigned>(aux)) << 32);
+  ev[1] = static_cast<unsigned long long>(clock64());
+}
 // A trace mark at a point where the CTA's warps are not otherwise joined.
 __device__ void mark(const Params& p, Misc* misc, int slot) {
   if (p.trace == nullptr) return;
@@ -274,14 +295,19 @@ __device__ void mark(const Params& p, Misc* misc, int slot) {
 // CTA's arrival (release) and waits (bounded, acquire) until every CTA has
 // arrived idx times, then releases its consumers.
 __device__ void grid_join(const Params& p, Misc* misc, unsigned idx, int slot) {
+  tl_event(p, misc, 40);
   named_sync();
   if (threadIdx.x == 0) {
     const unsigned long long t0 = p.trace != nullptr ? global_ns() : 0ull;
+    tl_event(p, misc, 41);
     red_release_add(p.sync, 1u);
+    tl_event(p, misc, 42);
     spin_geq(p, misc, p.sync, idx * gridDim.x);
+    tl_event(p, misc, 43);
     if (p.trace != nullptr) trace_mark(p, misc, slot, t0, global_ns());
   }
   named_sync();
+  tl_event(p, misc, 44);
 }
 
 // ------------------------------------------------------------------ tiles
@@ -605,6 +631,23 @@ __device__ __forceinline__ void cta_range(int T, int& t0, int& t1) {
   t1 = static_cast<int>((static_cast<long long>(T) * (blockIdx.x + 1)) / gridDim.x);
 }
 
+// Tile range of this CTA in a weight stream. Row-block-major streams split their
+// tiles evenly. K-chunk-major streams (o_proj, down_proj) give every K chunk its
+// own CTAs - chunk c: CTAs [ceil(c W / C), ceil((c + 1) W / C)) - which split the
+// chunk's row blocks evenly, so that no CTA needs the activations of two chunks.
+__device__ __forceinline__ void stream_range(const Stream& st, bool chunk_major, int& t0, int& t1) {
+  const int C = st.chunks, W = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
+  if (!chunk_major || W < C) {
+    cta_range(st.rbs * C, t0, t1);
+    return;
+  }
+  const int c = (b * C) / W;
+  const int first = (c * W + C - 1) / C, count = ((c + 1) * W + C - 1) / C - first;
+  const int i = b - first;
+  t0 = c * st.rbs + (i * st.rbs) / count;
+  t1 = c * st.rbs + ((i + 1) * st.rbs) / count;
+}
+
 // One projection over this CTA's share of its weight stream: every tile's
 // per-row partial sums go to P[row * pstride + matrix * 8 + chunk] in L2 (the
 // consumer of the projection sums the chunks in order). Tiles are taken
@@ -615,18 +658,20 @@ template <int KIND>
 __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, bool chunk_major, float* P,
                              int pstride, int chunk0, uint32_t& seq, unsigned* cnt = nullptr, int cnt_rbs = 1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int T = st.rbs * st.chunks;
   int t0, t1;
-  cta_range(T, t0, t1);
+  stream_range(st, chunk_major, t0, t1);
   const int g = lane >> 2;
+  const int tl_op = KIND * 2 + (chunk_major ? 1 : 0);
   // progress of this warp's tiles not yet published: counter index and count
   int pend_idx = -1;
   unsigned pend_cnt = 0;
   auto publish = [&]() {
     if (cnt != nullptr && pend_cnt != 0u) {
+      tl_event(p, s.misc, 13);
       __syncwarp();
       if (lane == 0) red_release_add(cnt + pend_idx, pend_cnt);
       pend_cnt = 0;
+      tl_event(p, s.misc, 14);
     }
   };
   for (int t = t0; t < t1; ++t) {
@@ -635,7 +680,9 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
     if (*reinterpret_cast<volatile int*>(&s.misc->abort)) break;
     const int slot = static_cast<int>(q % static_cast<uint32_t>(p.slots));
     const unsigned long long tw0 = p.trace != nullptr ? global_ns() : 0ull;
+    tl_event(p, s.misc, 10, tl_op * 65536 + (t - t0));
     if (!wait_bar(s.full + slot, (q / static_cast<uint32_t>(p.slots)) & 1u, p, s.misc)) break;
+    tl_event(p, s.misc, 11);
     const unsigned long long tw1 = p.trace != nullptr ? global_ns() : 0ull;
     const uint8_t* tile = s.ring + static_cast<size_t>(slot) * p.slot_bytes;
     const int rb = chunk_major ? t % st.rbs : t / st.chunks;
@@ -653,6 +700,7 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(s.empty + slot);
+    tl_event(p, s.misc, 12);
     if (p.trace != nullptr && lane == 0) {
       atomicAdd(&s.misc->wait_ns, tw1 - tw0);
       atomicAdd(&s.misc->busy_ns, global_ns() - tw1);
@@ -676,6 +724,7 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
     }
   }
   publish();
+  tl_event(p, s.misc, 15);
   seq += static_cast<uint32_t>(t1 - t0);
 }
 
@@ -785,6 +834,15 @@ __device__ void run_lm(const Params& p, const Smem& s, uint32_t& seq) {
 
 // Sum, in chunk order, of the first n (<= 8) per-chunk partials of a row
 // stored as 8 floats (written by other CTAs: read through L2).
+// Sum of the first n (<= 8) chunk partials a.x .. b.w, in chunk order.
+__device__ __forceinline__ float sum_loaded(const float4& a, const float4& b, int n) {
+  const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  float acc = v[0];
+#pragma unroll
+  for (int i = 1; i < 8; ++i)
+    if (i < n) acc += v[i];
+  return acc;
+}
 __device__ __forceinline__ float sum_chunks(const float* row, int n) {
   const float4 a = __ldcg(reinterpret_cast<const float4*>(row));
   float v[8] = {a.x, a.y, a.z, a.w, 0.f, 0.f, 0.f, 0.f};
@@ -812,11 +870,20 @@ __device__ __forceinline__ void head_rows(const Params& p, const Layer& L, int h
                                           const float (&sn)[2], int lane, float (&lo)[2], float (&hi)[2]) {
   const int i = lane >> 2, gg = (lane & 3) * 2;
   const int base = (hd * 8 + i) * 16;
+  // the four rows' chunk partials and scales, all loads issued before any is used
+  float4 pa[4], pb[4];
+  float sc[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int r = base + gg + (k >> 1) + 8 * (k & 1);
+    pa[k] = __ldcg(reinterpret_cast<const float4*>(p.pqkv + r * 8));
+    pb[k] = __ldcg(reinterpret_cast<const float4*>(p.pqkv + r * 8 + 4));
+    sc[k] = L.qkv_scale[r];
+  }
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
-    const int r0 = base + gg + e, r1 = r0 + 8;
-    float x0 = bfr(sum_chunks(p.pqkv + r0 * 8, p.sq.chunks) * L.qkv_scale[r0]);
-    float x1 = bfr(sum_chunks(p.pqkv + r1 * 8, p.sq.chunks) * L.qkv_scale[r1]);
+    float x0 = bfr(sum_loaded(pa[2 * e], pb[2 * e], p.sq.chunks) * sc[2 * e]);
+    float x1 = bfr(sum_loaded(pa[2 * e + 1], pb[2 * e + 1], p.sq.chunks) * sc[2 * e + 1]);
     if (rope) {
       const float ra = x0 * cs[e] - x1 * sn[e];
       const float rb2 = x1 * cs[e] + x0 * sn[e];
@@ -861,7 +928,7 @@ __device__ __forceinline__ void quantize_row(const float (&lo)[2], const float (
 // (KV head, span of kAttnSpan tokens), one CTA each (the span count depends
 // only on the context length, so the summation structure is the same at every
 // tensor-parallel degree). The CTA rebuilds q of the head's G query heads from
-// the QKV partials; each consumer warp takes one 32-token slice: QK^T on the
+// the QKV partials; each consumer warp takes one kAttnChunk-token slice: QK^T on the
 // tensor cores (K rows as the A operand, exact int8 -> fp16; q as B with one
 // column per head), softmax partials, P.V on the CUDA cores (lane = 4 dims).
 // The warps' partials merge in shared memory in token order; spans of one KV
@@ -870,11 +937,14 @@ __device__ __forceinline__ void quantize_row(const float (&lo)[2], const float (
 constexpr int kAttnSpan = kConsumers * kAttnChunk;
 constexpr int kAttnPart = 132;  // floats per (head) partial: acc[128], m, l, pad
 
-// Ring slot layout of one attention slice (32 tokens of one KV head): K rows
-// [32][128] int8, V rows [32][128], K scales [32] fp16, V scales [32] fp16.
-constexpr int kSliceK = 0, kSliceV = 4096, kSliceKs = 8192, kSliceVs = 8192 + 64, kSliceBytes = 8192 + 128;
+// Ring slot layout of one attention slice (kAttnChunk tokens of one KV head): K
+// rows [kAttnChunk][128] int8, V rows likewise, K scales [kAttnChunk] fp16, V
+// scales likewise (every part starts on a 16-byte boundary).
+constexpr int kSliceK = 0, kSliceV = kAttnChunk * 128, kSliceKs = 2 * kAttnChunk * 128,
+              kSliceVs = kSliceKs + kAttnChunk * 2, kSliceBytes = kSliceVs + kAttnChunk * 2;
+static_assert(kAttnChunk % 16 == 0 && (kAttnChunk * 2) % 16 == 0, "slice layout");
 
-// Number of 32-token slices of attention item `item` (tokens [span*kAttnSpan, n)).
+// Number of slices of attention item `item` (tokens [span*kAttnSpan, n)).
 __device__ __forceinline__ int attn_slices(int item, int spans, int n) {
   const int tspan = (item % spans) * kAttnSpan;
   return min(kConsumers, (n - tspan + kAttnChunk - 1) / kAttnChunk);
@@ -884,6 +954,11 @@ template <int G>
 __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, int layer, int pos, uint8_t* scratch,
                                uint32_t& seq, const float (&cs)[2], const float (&sn)[2]) {
   Misc* misc = sm.misc;
+  // tracing: thread 0 stamps item milestones (heads ready, q built, computed, published)
+  unsigned long long* astamp = (p.trace != nullptr && threadIdx.x == 0)
+                                   ? p.trace + (static_cast<size_t>(blockIdx.x) * p.trace_slots +
+                                                p.num_layers * kMarksPerLayer + 2 + layer * kAttnMarks) * 4
+                                   : nullptr;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int g = lane >> 2, c = lane & 3;
   const int n = pos + 1;
@@ -892,7 +967,7 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
   const size_t cap = static_cast<size_t>(p.capacity);
   __half* qs = reinterpret_cast<__half*>(scratch);                                    // [G][128] fp16
   float* wpart = reinterpret_cast<float*>(scratch + 1024) + warp * G * kAttnPart;      // this warp's partial
-  float* pw = wpart;                                                                   // [32][4] probabilities (before the partial)
+  float* pw = wpart;  // [kAttnChunk][4] probabilities (before the partial)
   float* allpart = reinterpret_cast<float*>(scratch + 1024);
   for (int item = blockIdx.x; item < items; item += gridDim.x) {
     const int h = item / spans, span = item % spans;
@@ -905,6 +980,7 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
     const int slot = static_cast<int>(q_slot % static_cast<uint32_t>(p.slots));
     uint8_t* tile = sm.ring + static_cast<size_t>(slot) * p.slot_bytes;
     if (has_slice) wait_bar(sm.full + slot, (q_slot / static_cast<uint32_t>(p.slots)) & 1u, p, misc);
+    tl_event(p, misc, 20, item);
     const bool span_has_pos = pos >= tspan && pos < tspan + kAttnSpan;
     int8_t* kc = L.k_cache + static_cast<size_t>(h) * cap * 128;
     int8_t* vc = L.v_cache + static_cast<size_t>(h) * cap * 128;
@@ -917,6 +993,8 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
       for (int j = 0; j < G && ok; ++j) ok = spin_geq(p, misc, p.hdr + kHdrQkv + G * h + j, need);
       if (span_has_pos && ok) ok = spin_geq(p, misc, p.hdr + kHdrQkv + p.heads + h, need);
       if (span_has_pos && ok) spin_geq(p, misc, p.hdr + kHdrQkv + p.heads + p.kv_heads + h, need);
+      if (astamp) astamp[0] = global_ns();
+      tl_event(p, misc, 21);
     }
     named_sync();
     // (after a failed wait the item still runs through every barrier; its output is invalid and
@@ -952,11 +1030,14 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
       }
     }
     named_sync();
+    tl_event(p, misc, 22);
+    if (astamp) astamp[4] = global_ns();
     float m2[2] = {-INFINITY, -INFINITY}, l2[2] = {0.f, 0.f};
-    float acc[G][4];
+    float2 acc[G][2];  // dims (4 lane, +1), (4 lane + 2, +3)
 #pragma unroll
-    for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = acc[hh][2] = acc[hh][3] = 0.f;
+    for (int hh = 0; hh < G; ++hh) acc[hh][0] = acc[hh][1] = make_float2(0.f, 0.f);
     if (tb < n) {
+      tl_event(p, misc, 26);
       // ---- B fragments: column g < G is query head g; dims of MMA s for lane quad c: 32c + 4s + {0..3}
       uint32_t bq[8][2];
 #pragma unroll
@@ -969,10 +1050,10 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
           bq[s2][0] = bq[s2][1] = 0u;
         }
       }
-      // ---- scores of the slice's 32 tokens (two 16-token MMA row blocks)
-      float sc[2][4];
+      // ---- scores of the slice's tokens (16-token MMA row blocks)
+      float sc[kAttnRbk][4];
 #pragma unroll
-      for (int rbk = 0; rbk < 2; ++rbk) {
+      for (int rbk = 0; rbk < kAttnRbk; ++rbk) {
         float ac[4] = {0.f, 0.f, 0.f, 0.f};
         const int rg = rbk * 16 + g, rh = rg + 8;  // rows of the slice
         const int tg = tb + rg, th = tb + rh;
@@ -998,16 +1079,19 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
         sc[rbk][2] = th < n ? ac[2] * khs * p.attn_scale : -INFINITY;
         sc[rbk][3] = th < n ? ac[3] * khs * p.attn_scale : -INFINITY;
       }
-      // ---- softmax partials per head (column 2c + e), over the 32 tokens
+      tl_event(p, misc, 27);
+      // ---- softmax partials per head (column 2c + e), over the slice's tokens
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
-        float mx = fmaxf(fmaxf(sc[0][e], sc[0][e + 2]), fmaxf(sc[1][e], sc[1][e + 2]));
+        float mx = fmaxf(sc[0][e], sc[0][e + 2]);
+#pragma unroll
+        for (int rbk = 1; rbk < kAttnRbk; ++rbk) mx = fmaxf(mx, fmaxf(sc[rbk][e], sc[rbk][e + 2]));
 #pragma unroll
         for (int o = 4; o < 32; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
         m2[e] = mx;
         float sum = 0.f;
 #pragma unroll
-        for (int rbk = 0; rbk < 2; ++rbk)
+        for (int rbk = 0; rbk < kAttnRbk; ++rbk)
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
             const float v = sc[rbk][e + 2 * hh];
@@ -1021,7 +1105,7 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
       }
       if (2 * c < G) {
 #pragma unroll
-        for (int rbk = 0; rbk < 2; ++rbk)
+        for (int rbk = 0; rbk < kAttnRbk; ++rbk)
 #pragma unroll
           for (int e = 0; e < 2; ++e)
             if (2 * c + e < G) {
@@ -1030,6 +1114,7 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
             }
       }
       __syncwarp();
+      tl_event(p, misc, 28);
       // ---- P.V: lane owns dims 4*lane .. 4*lane+3; V words and scales 8 tokens at a time
       const int tend = min(n - tb, kAttnChunk);
       const __half* vs_s = reinterpret_cast<const __half*>(tile + kSliceVs);
@@ -1051,55 +1136,76 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
           if (t0 + j >= tend) break;
           const float4 p4 = *reinterpret_cast<const float4*>(pw + (t0 + j) * 4);
           const float pr[4] = {p4.x * vs[j], p4.y * vs[j], p4.z * vs[j], p4.w * vs[j]};
-          const int w = vw[j];
-          const float vf[4] = {static_cast<float>(static_cast<int8_t>(w & 0xFF)),
-                               static_cast<float>(static_cast<int8_t>((w >> 8) & 0xFF)),
-                               static_cast<float>(static_cast<int8_t>((w >> 16) & 0xFF)),
-                               static_cast<float>(static_cast<int8_t>(w >> 24))};
+          // codes -> fp32 exactly: the biased byte b = code + 128 under exponent 2^23 is 2^23 + b,
+          // minus 2^23 + 128 (both exact), two lanes of a packed fp32 pair at a time
+          const uint32_t u = static_cast<uint32_t>(vw[j]) ^ 0x80808080u;
+          const float2 kBias = make_float2(-8388736.0f, -8388736.0f);
+          const float2 v01 = __fadd2_rn(make_float2(__uint_as_float(prmt(u, 0x4B000000u, 0x7540u)),
+                                                    __uint_as_float(prmt(u, 0x4B000000u, 0x7541u))), kBias);
+          const float2 v23 = __fadd2_rn(make_float2(__uint_as_float(prmt(u, 0x4B000000u, 0x7542u)),
+                                                    __uint_as_float(prmt(u, 0x4B000000u, 0x7543u))), kBias);
 #pragma unroll
-          for (int hh = 0; hh < G; ++hh)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) acc[hh][e] = fmaf(pr[hh], vf[e], acc[hh][e]);
+          for (int hh = 0; hh < G; ++hh) {
+            const float2 ph = make_float2(pr[hh], pr[hh]);
+            acc[hh][0] = __ffma2_rn(ph, v01, acc[hh][0]);
+            acc[hh][1] = __ffma2_rn(ph, v23, acc[hh][1]);
+          }
         }
       }
       __syncwarp();  // pw is overwritten by the partial below
     }
     if (has_slice && lane == 0) mbar_arrive(sm.empty + slot);
+    tl_event(p, misc, 23);
     // ---- this warp's partial into shared memory: [head][acc 128 | m | l]
 #pragma unroll
     for (int hh = 0; hh < G; ++hh) {
-      *reinterpret_cast<float4*>(wpart + hh * kAttnPart + lane * 4) = make_float4(acc[hh][0], acc[hh][1], acc[hh][2], acc[hh][3]);
+      *reinterpret_cast<float4*>(wpart + hh * kAttnPart + lane * 4) =
+          make_float4(acc[hh][0].x, acc[hh][0].y, acc[hh][1].x, acc[hh][1].y);
       if (lane == hh / 2) {  // lane (g = 0, c = hh/2) holds column hh = 2c + e
         wpart[hh * kAttnPart + 128] = m2[hh & 1];
         wpart[hh * kAttnPart + 129] = l2[hh & 1];
       }
     }
     named_sync();
+    if (astamp) astamp[8] = global_ns();
     // ---- merge the warps' partials in token order into this span's partial (L2); thread -> (head, dim)
     float* gp0 = p.apart + ((static_cast<size_t>(h) * p.attn_max_chunks + span) * G) * kAttnPart;
-    for (int o = tid; o < G * 128; o += kConsumerThreads) {
-      const int hh = o >> 7, d = o & 127;
+    float* wts = allpart + kConsumers * G * kAttnPart;  // [kConsumers][G] weights, then [G] max, [G] sum
+    if (tid < G) {
+      const int hh = tid;
       float M = -INFINITY;
 #pragma unroll
       for (int w = 0; w < kConsumers; ++w) M = fmaxf(M, allpart[(w * G + hh) * kAttnPart + 128]);
-      float Lsum = 0.f, A = 0.f;
+      float Lsum = 0.f;
 #pragma unroll
       for (int w = 0; w < kConsumers; ++w) {
         const float* e = allpart + (w * G + hh) * kAttnPart;
         const float wt = e[128] == -INFINITY ? 0.f : expf(e[128] - M);
         Lsum = fmaf(e[129], wt, Lsum);
-        A = fmaf(e[d], wt, A);
+        wts[w * G + hh] = wt;
       }
+      wts[kConsumers * G + hh] = M;
+      wts[kConsumers * G + G + hh] = Lsum;
+    }
+    named_sync();
+    for (int o = tid; o < G * 128; o += kConsumerThreads) {
+      const int hh = o >> 7, d = o & 127;
+      float A = 0.f;
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) A = fmaf(allpart[(w * G + hh) * kAttnPart + d], wts[w * G + hh], A);
       float* gp = gp0 + hh * kAttnPart;
       gp[d] = A;
       if (d == 0) {
-        gp[128] = M;
-        gp[129] = Lsum;
+        gp[128] = wts[kConsumers * G + hh];
+        gp[129] = wts[kConsumers * G + G + hh];
       }
     }
     // ---- one more span of KV head h is published (the o_proj prologue merges the spans)
+    tl_event(p, misc, 24);
     named_sync();
     if (tid == 0) red_release_add(p.hdr + kHdrAttn + h, 1u);
+    tl_event(p, misc, 25);
+    if (astamp) astamp[12] = global_ns();
     named_sync();  // the scratch is reused by the next item
     seq += static_cast<uint32_t>(slices);
   }
@@ -1143,12 +1249,10 @@ __device__ void produce_attention(const Params& p, const Smem& s, const Layer& L
   }
 }
 
-__device__ void produce_op(const Params& p, const Smem& s, const Stream& st, const uint8_t* stream, uint32_t& seq,
-                           uint64_t pol) {
-  const int W = gridDim.x, cta = blockIdx.x;
-  const int T = st.rbs * st.chunks;
-  const int t0 = static_cast<int>((static_cast<long long>(T) * cta) / W);
-  const int t1 = static_cast<int>((static_cast<long long>(T) * (cta + 1)) / W);
+__device__ void produce_op(const Params& p, const Smem& s, const Stream& st, bool chunk_major, const uint8_t* stream,
+                           uint32_t& seq, uint64_t pol) {
+  int t0, t1;
+  stream_range(st, chunk_major, t0, t1);
   for (int t = t0; t < t1; ++t, ++seq) {
     if (*reinterpret_cast<volatile int*>(&s.misc->abort)) return;
     const int slot = static_cast<int>(seq % static_cast<uint32_t>(p.slots));
@@ -1187,6 +1291,8 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     s.misc->key = 0ull;
     s.misc->wait_ns = 0ull;
     s.misc->busy_ns = 0ull;
+    s.misc->tl_on = 0;
+    for (int w = 0; w < kConsumers; ++w) s.misc->tl_n[w] = 0u;
   }
   for (int i = threadIdx.x; i < kRbSlots; i += blockDim.x) s.rbcnt[i] = 0u;
   for (int i = threadIdx.x; i < 64; i += blockDim.x) reinterpret_cast<uint32_t*>(base + kOffZero)[i] = 0u;
@@ -1206,13 +1312,13 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
       uint32_t seq = 0;
       for (int l = 0; l < p.num_layers; ++l) {
         const Layer& L = p.layers[l];
-        produce_op(p, s, p.sq, L.qkv, seq, pol);
+        produce_op(p, s, p.sq, false, L.qkv, seq, pol);
         produce_attention(p, s, L, pos, seq, pol);
-        produce_op(p, s, p.so, L.o, seq, pol);
-        produce_op(p, s, p.sgu, L.gateup, seq, pol);
-        produce_op(p, s, p.sdn, L.down, seq, pol);
+        produce_op(p, s, p.so, true, L.o, seq, pol);
+        produce_op(p, s, p.sgu, false, L.gateup, seq, pol);
+        produce_op(p, s, p.sdn, true, L.down, seq, pol);
       }
-      produce_op(p, s, p.slm, p.head, seq, pol);
+      produce_op(p, s, p.slm, false, p.head, seq, pol);
       // no copy may be in flight when the CTA exits: wait for the last issued ones
       const uint32_t nslots = static_cast<uint32_t>(p.slots);
       for (uint32_t q = seq > nslots ? seq - nslots : 0u; q < seq; ++q) {
@@ -1226,7 +1332,11 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
   // ---------------- consumer warps
   const int tid = threadIdx.x;
   if (p.trace != nullptr && tid == 0)
-    p.trace[(static_cast<size_t>(blockIdx.x) * p.trace_slots + p.trace_slots - 1) * 4] = global_ns();
+  {
+    unsigned long long* st0 = p.trace + (static_cast<size_t>(blockIdx.x) * p.trace_slots + p.num_layers * kMarksPerLayer + 1) * 4;
+    st0[0] = global_ns();
+    st0[1] = static_cast<unsigned long long>(clock64());
+  }
   const int token = p.tokens[0];
   const __nv_bfloat16* emb = p.embed + static_cast<size_t>(min(max(token, 0), p.vocab_total - 1)) * p.hidden;
   uint32_t seq = 0;
@@ -1246,14 +1356,21 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
   for (int l = 0; l < p.num_layers; ++l) {
     const Layer& L = p.layers[l];
     const int mk = l * kMarksPerLayer;
+    if (p.trace != nullptr) {
+      if (tid == 0) s.misc->tl_on = l == p.num_layers / 2;
+      named_sync();
+      tl_event(p, s.misc, 1);
+    }
     // ---- RMSNorm + QKV projection (per-chunk partials; RoPE happens in the attention items)
     if (l > 0) fold_residual(p.pdn, nullptr, p.hidden, p.eps, s.xres, s.misc);
+    tl_event(p, s.misc, 2);
     for (int v = tid; v < nwords; v += kConsumerThreads) {
       float f[8];
       norm8(s.xres, L.in_norm, s.misc->rms, v, f);
       put_w8(s.xs, v, f);
     }
     named_sync();
+    tl_event(p, s.misc, 3);
     mark(p, s.misc, mk + 0);
     run_partials<K_W8>(p, s, p.sq, false, p.pqkv, 8, 0, seq, p.hdr + kHdrQkv, 8);
     mark(p, s.misc, mk + 1);
@@ -1269,15 +1386,17 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     {
       const Stream& st = p.so;
       int t0, t1;
-      cta_range(st.rbs * st.chunks, t0, t1);
+      stream_range(st, true, t0, t1);
       if (t1 > t0) {
         const int c0 = t0 / st.rbs, c1 = (t1 - 1) / st.rbs;
         const int spans = (pos + kAttnSpan) / kAttnSpan;  // ceil((pos + 1) / kAttnSpan)
         if (tid == 0) {
           // every span of the KV heads whose query heads feed K values [c0*ck, (c1+1)*ck)
           const int h0 = (c0 * st.ck) / (128 * G), h1 = ((c1 + 1) * st.ck - 1) / (128 * G);
+          tl_event(p, s.misc, 30);
           for (int h = h0; h <= h1; ++h)
             if (!spin_geq(p, s.misc, p.hdr + kHdrAttn + h, static_cast<unsigned>((l + 1) * spans))) break;
+          tl_event(p, s.misc, 31);
         }
         named_sync();
         // attention output: the spans' partials merged in span order, rounded to bf16
@@ -1286,19 +1405,11 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
           const int h = qh / G, hh = qh % G;
           const float* e0 = p.apart + (static_cast<size_t>(h) * p.attn_max_chunks * G + hh) * kAttnPart;
           const size_t jstride = static_cast<size_t>(G) * kAttnPart;
-          // spans in batches of 4: all of a batch's loads are issued before any is used
-          float M = -INFINITY;
-          for (int j0 = 0; j0 < spans; j0 += 4) {
-            float mv[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) mv[j] = j0 + j < spans ? ldcg_f(e0 + (j0 + j) * jstride + 128) : -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) M = fmaxf(M, mv[j]);
-          }
-          float Lsum = 0.f, A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-          for (int j0 = 0; j0 < spans; j0 += 4) {
-            float4 a0[4], a1[4];
-            float mj[4], lj[4];
+          // spans in batches of 4, every load of a batch issued before any is used; the first
+          // batch is loaded together with the maxima of the rest (one round of loads up to 4 spans)
+          float4 a0[4], a1[4];
+          float mj[4], lj[4];
+          auto load_batch = [&](int j0) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const float* e = e0 + (j0 + j) * jstride;
@@ -1308,6 +1419,19 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
               mj[j] = ok ? ldcg_f(e + 128) : -INFINITY;
               lj[j] = ok ? ldcg_f(e + 129) : 0.f;
             }
+          };
+          load_batch(0);
+          float M = fmaxf(fmaxf(mj[0], mj[1]), fmaxf(mj[2], mj[3]));
+          for (int j0 = 4; j0 < spans; j0 += 4) {
+            float mv[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) mv[j] = j0 + j < spans ? ldcg_f(e0 + (j0 + j) * jstride + 128) : -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) M = fmaxf(M, mv[j]);
+          }
+          float Lsum = 0.f, A[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int j0 = 0; j0 < spans; j0 += 4) {
+            if (j0 > 0) load_batch(j0);
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const float wt = mj[j] == -INFINITY ? 0.f : expf(mj[j] - M);
@@ -1325,12 +1449,16 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
         }
       }
     }
+    tl_event(p, s.misc, 32);
     named_sync();
+    tl_event(p, s.misc, 33);
     if (p.trace != nullptr && tid == 0) trace_mark(p, s.misc, mk + 3, global_ns(), global_ns());
     run_partials<K_W8>(p, s, p.so, true, p.po, 8, 0, seq);
     grid_join(p, s.misc, ++joins, mk + 4);
     // ---- residual += o; RMSNorm + gate/up (partials; progress per down K chunk)
+    tl_event(p, s.misc, 50);
     fold_residual(p.po, L.o_scale, p.hidden, p.eps, s.xres, s.misc);
+    tl_event(p, s.misc, 51);
     for (int v0 = 0; v0 < nwords; v0 += kConsumerThreads) {
       const int v = v0 + tid;
       float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -1338,6 +1466,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
       put_w4(s.xs, s.om, v, v < nwords, f);
     }
     named_sync();
+    tl_event(p, s.misc, 52);
     mark(p, s.misc, mk + 5);
     run_partials<K_W4PAIR>(p, s, p.sgu, false, p.pgu, 16, 0, seq, p.hdr + kHdrGu, gu_rbs_per_chunk);
     mark(p, s.misc, mk + 6);
@@ -1346,27 +1475,46 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     {
       const Stream& st = p.sdn;
       int t0, t1;
-      cta_range(st.rbs * st.chunks, t0, t1);
+      stream_range(st, true, t0, t1);
       if (t1 > t0) {
         const int c0 = t0 / st.rbs, c1 = (t1 - 1) / st.rbs;
         if (tid == 0) {
           const unsigned need = static_cast<unsigned>((l + 1) * gu_rbs_per_chunk * p.sgu.chunks);
+          tl_event(p, s.misc, 60);
           for (int c = c0; c <= c1; ++c)
             if (!spin_geq(p, s.misc, p.hdr + kHdrGu + c, need)) break;
+          tl_event(p, s.misc, 61);
         }
         named_sync();
-        const int w0 = c0 * act_chunk / 8, w1 = (c1 + 1) * act_chunk / 8;
+        // SwiGLU values of the chunks into shared memory (thread per value: its gate and up
+        // chunk partials are 64 contiguous bytes, loaded in one round) ...
+        const int a0 = c0 * act_chunk, a1 = (c1 + 1) * act_chunk;
+        __nv_bfloat16* actv = reinterpret_cast<__nv_bfloat16*>(base + kOffPart);
+        for (int r = a0 + tid; r < a1; r += kConsumerThreads) {
+          const float* pr = p.pgu + static_cast<size_t>(r) * 16;
+          const float4 g0 = __ldcg(reinterpret_cast<const float4*>(pr));
+          const float4 g1 = __ldcg(reinterpret_cast<const float4*>(pr + 4));
+          const float4 u0 = __ldcg(reinterpret_cast<const float4*>(pr + 8));
+          const float4 u1 = __ldcg(reinterpret_cast<const float4*>(pr + 12));
+          const float gt = bfr(sum_loaded(g0, g1, p.sgu.chunks));
+          const float up = bfr(sum_loaded(u0, u1, p.sgu.chunks));
+          actv[r - a0] = __float2bfloat16_rn(gt / (1.0f + expf(-gt)) * up);
+        }
+        named_sync();
+        // ... then staged for the W4 tiles, 8 values per thread
+        const int w0 = a0 / 8, w1 = a1 / 8;
         for (int v0 = w0 & ~7; v0 < w1; v0 += kConsumerThreads) {
           const int v = v0 + tid;
           const bool valid = v >= w0 && v < w1;
           float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
           if (valid) {
+            const uint4 w = *reinterpret_cast<const uint4*>(actv + (v * 8 - a0));
+            const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float* pr = p.pgu + static_cast<size_t>(v * 8 + i) * 16;
-              const float gt = bfr(sum_chunks(pr, p.sgu.chunks));
-              const float up = bfr(sum_chunks(pr + 8, p.sgu.chunks));
-              f[i] = bfr(gt / (1.0f + expf(-gt)) * up);
+            for (int i = 0; i < 4; ++i) {
+              const float2 t = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ws[i]));
+              f[2 * i] = t.x;
+              f[2 * i + 1] = t.y;
             }
           }
           put_w4(s.xs, s.om, v, valid, f);
@@ -1374,6 +1522,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
       }
     }
     named_sync();
+    tl_event(p, s.misc, 62);
     if (p.trace != nullptr && tid == 0) trace_mark(p, s.misc, mk + 7, global_ns(), global_ns());
     run_partials<K_W4>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
     grid_join(p, s.misc, ++joins, mk + 8);
@@ -1436,6 +1585,8 @@ int geometry(const sb_step_desc* d, Geometry* g) {
   SB_REQUIRE(qk <= kMaxK && qk % (kChunks * 32 / d->world) == 0, "o_proj K must split into 8 chunks of 32-multiples");
   SB_REQUIRE(d->inter > 0 && d->inter % 16 == 0 && d->inter <= kMaxK, "inter must be a multiple of 16, <= 10240");
   SB_REQUIRE(d->inter_total % (kChunks * 64) == 0, "intermediate size must be a multiple of 512");
+  SB_REQUIRE(2 * (d->inter_total / kChunks) * 2 <= kPartSlots * 32 * 4,
+             "two K chunks of down_proj activations must fit the shared staging area");
   SB_REQUIRE(d->vocab > 0 && d->capacity > 0 && d->capacity % 16 == 0, "vocab and capacity");
   SB_REQUIRE(d->hidden % (kChunks * 16) == 0, "hidden must split into 8 chunks of 16-multiples");
   g->sq = {(d->num_heads + 2 * d->num_kv_heads) * 128 / 16, d->hidden / 512, 16 * 512, 512};
@@ -1479,7 +1630,9 @@ int geometry(const sb_step_desc* d, Geometry* g) {
 using namespace sb;
 using namespace sb::step;
 
-extern "C" int sb_step_trace_slots(int num_layers) { return num_layers * kMarksPerLayer + 2; }
+extern "C" int sb_step_trace_slots(int num_layers) {
+  return num_layers * (kMarksPerLayer + kAttnMarks) + 2 + kTlSlots;
+}
 
 extern "C" size_t sb_step_workspace_size(const sb_step_desc* d) {
   Geometry g;
@@ -1553,7 +1706,7 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   p.slm = g.slm;
   p.slot_bytes = g.slot_bytes;
   p.trace = d->trace;
-  p.trace_slots = d->num_layers * kMarksPerLayer + 2;
+  p.trace_slots = sb_step_trace_slots(d->num_layers);
   int max_smem = 0, dev = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
