@@ -235,9 +235,12 @@ __device__ __forceinline__ void st_volatile_u32(unsigned* addr, unsigned v) {
   asm volatile("st.volatile.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
 }
 
-// Bounded wait until *addr >= target (another CTA's progress), then acquire
-// ordering for the loads that follow. On timeout, or when another CTA has
-// already recorded a failure, records it and raises the CTA's abort flag.
+// Bounded wait until *addr >= target (another CTA's progress). The load that
+// observes the target is an acquire at GPU scope: the waiting thread's later
+// loads, and those of the threads it releases through a CTA barrier, see the
+// writes ordered before the matching release (the other CTA's red.release).
+// On timeout, or when another CTA has already recorded a failure, records it
+// and raises the CTA's abort flag.
 __device__ bool spin_geq(const Params& p, Misc* misc, const unsigned* addr, unsigned target) {
   if (*reinterpret_cast<volatile int*>(&misc->abort)) return false;
   if (ld_acquire_u32(addr) < target) {
@@ -250,8 +253,35 @@ __device__ bool spin_geq(const Params& p, Misc* misc, const unsigned* addr, unsi
       }
     }
   }
-  __threadfence();
   return true;
+}
+
+// Bounded wait until the QKV progress counters of KV head h's G query heads -
+// and, when `with_kv`, of its new K and V rows - are all >= target, polling
+// them together (acquire loads); same failure handling as spin_geq.
+template <int G>
+__device__ bool spin_heads(const Params& p, Misc* misc, int h, bool with_kv, unsigned target) {
+  if (*reinterpret_cast<volatile int*>(&misc->abort)) return false;
+  const unsigned* q0 = p.hdr + kHdrQkv + G * h;
+  const unsigned* kq = p.hdr + kHdrQkv + p.heads + h;
+  const unsigned* vq = kq + p.kv_heads;
+  const long long start = clock64();
+  while (true) {
+    unsigned v[G + 2];
+#pragma unroll
+    for (int i = 0; i < G; ++i) v[i] = ld_acquire_u32(q0 + i);
+    v[G] = with_kv ? ld_acquire_u32(kq) : target;
+    v[G + 1] = with_kv ? ld_acquire_u32(vq) : target;
+    bool ok = true;
+#pragma unroll
+    for (int i = 0; i < G + 2; ++i) ok = ok && v[i] >= target;
+    if (ok) return true;
+    if (clock64() - start > (1LL << 31) || ld_volatile_u32(p.status) != 0u) {
+      atomicOr(p.status, kStatusTimeout);
+      *reinterpret_cast<volatile int*>(&misc->abort) = 1;
+      return false;
+    }
+  }
 }
 
 // Tracing (thread 0): mark `slot` of this CTA with (t0, t1) and the tile
@@ -312,15 +342,20 @@ __device__ void grid_join(const Params& p, Misc* misc, unsigned idx, int slot) {
 
 // ------------------------------------------------------------------ tiles
 // W8 tile: `kb` blocks of 32 columns. Returns the rows' partial sums.
+// NKB > 0: the block count is a compile-time constant (loop fully unrolled, every
+// load hoisted); 0: kb_count at run time.
+template <int NKB>
 __device__ __forceinline__ void w8_tile(const uint8_t* tile, const uint8_t* xs, int kb_count, int lane, float& og,
                                         float& oh) {
+  constexpr int kUnroll = NKB > 0 ? NKB : 4;
+  if (NKB > 0) kb_count = NKB;
   const int c = lane & 3;
   float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
   const uint8_t* a_ptr = tile + lane * 16;
   const uint8_t* x_ptr = xs + c * 16;
   constexpr uint32_t kMagic = 0x64646464u;
   constexpr uint32_t kOff = 0x64806480u;  // fp16 1152 in both halves
-#pragma unroll 4
+#pragma unroll kUnroll
   for (int kb = 0; kb < kb_count; ++kb) {
     const uint4 a = lds128(a_ptr + kb * 512);
     const uint4 b = lds128(x_ptr + kb * 64);
@@ -414,9 +449,11 @@ __device__ __forceinline__ void w4_round(const uint8_t* a_ptr, const uint8_t* xs
 
 // W4 tile of MATS matrices (1 = down, 2 = gate+up) over `ngroups` groups of
 // 64. xs points at the chunk's first staged group, om at its (O, X) pairs.
-template <int MATS>
+template <int MATS, int NG>
 __device__ __forceinline__ void w4_tile(const uint8_t* tile, int ngroups, const uint8_t* xs, const float2* om,
                                         const uint8_t* zero, int lane, float (&out)[MATS][2]) {
+  constexpr int kRoundUnroll = NG > 0 ? (NG + 7) / 8 : 1;
+  if (NG > 0) ngroups = NG;
   const int g = lane >> 2, c = lane & 3;
   const uint8_t* a_ptr = tile + lane * 16;
   const int rounds = (ngroups + 7) >> 3;
@@ -425,6 +462,7 @@ __device__ __forceinline__ void w4_tile(const uint8_t* tile, int ngroups, const 
   float res[MATS][2];
 #pragma unroll
   for (int m = 0; m < MATS; ++m) res[m][0] = res[m][1] = 0.f;
+#pragma unroll kRoundUnroll
   for (int r = 0; r < rounds; ++r) {
     // two accumulator chains per matrix (bf16 and fp16 MMAs), summed in the epilogue
     float acc[MATS][4], acc2[MATS][4];
@@ -626,6 +664,13 @@ struct Smem {
 };
 
 // Tile range [t0, t1) of this CTA in a stream of T tiles (balanced, contiguous).
+// First tile index >= t0 of consumer warp `warp` when tiles t0, t0 + 1, ... are
+// dealt round-robin from ring sequence number seq (tile t has sequence number
+// seq + t - t0 and goes to warp (seq + t - t0) % kConsumers).
+__device__ __forceinline__ int first_tile(int t0, uint32_t seq, int warp) {
+  return t0 + (warp + kConsumers - static_cast<int>(seq % kConsumers)) % kConsumers;
+}
+
 __device__ __forceinline__ void cta_range(int T, int& t0, int& t1) {
   t0 = static_cast<int>((static_cast<long long>(T) * blockIdx.x) / gridDim.x);
   t1 = static_cast<int>((static_cast<long long>(T) * (blockIdx.x + 1)) / gridDim.x);
@@ -654,7 +699,9 @@ __device__ __forceinline__ void stream_range(const Stream& st, bool chunk_major,
 // round-robin by the consumer warps in stream order (the ring order).
 // When `cnt` is set, each finished tile also adds one to cnt[rb / cnt_rbs]
 // (progress that the next operator's consumers wait for).
-template <int KIND>
+// NK > 0: the stream's chunk size (W8: K blocks of 32; W4: groups) as a
+// compile-time constant for the tile loops; 0: st.ck at run time.
+template <int KIND, int NK>
 __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, bool chunk_major, float* P,
                              int pstride, int chunk0, uint32_t& seq, unsigned* cnt = nullptr, int cnt_rbs = 1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -674,37 +721,30 @@ __device__ void run_partials(const Params& p, const Smem& s, const Stream& st, b
       tl_event(p, s.misc, 14);
     }
   };
-  for (int t = t0; t < t1; ++t) {
+  for (int t = first_tile(t0, seq, warp); t < t1; t += kConsumers) {
     const uint32_t q = seq + static_cast<uint32_t>(t - t0);
-    if (static_cast<int>(q % kConsumers) != warp) continue;
     if (*reinterpret_cast<volatile int*>(&s.misc->abort)) break;
     const int slot = static_cast<int>(q % static_cast<uint32_t>(p.slots));
-    const unsigned long long tw0 = p.trace != nullptr ? global_ns() : 0ull;
     tl_event(p, s.misc, 10, tl_op * 65536 + (t - t0));
     if (!wait_bar(s.full + slot, (q / static_cast<uint32_t>(p.slots)) & 1u, p, s.misc)) break;
     tl_event(p, s.misc, 11);
-    const unsigned long long tw1 = p.trace != nullptr ? global_ns() : 0ull;
     const uint8_t* tile = s.ring + static_cast<size_t>(slot) * p.slot_bytes;
     const int rb = chunk_major ? t % st.rbs : t / st.chunks;
     const int ch = chunk_major ? t / st.rbs : t % st.chunks;
     float vals[2][2];
     if constexpr (KIND == K_W8) {
-      w8_tile(tile, s.xs + ch * st.ck * 2, st.ck / 32, lane, vals[0][0], vals[0][1]);
+      w8_tile<NK>(tile, s.xs + ch * st.ck * 2, st.ck / 32, lane, vals[0][0], vals[0][1]);
     } else if constexpr (KIND == K_W4) {
       float o[1][2];
-      w4_tile<1>(tile, st.ck, s.xs + ch * st.ck * 128, s.om + ch * st.ck, s.zero, lane, o);
+      w4_tile<1, NK>(tile, st.ck, s.xs + ch * st.ck * 128, s.om + ch * st.ck, s.zero, lane, o);
       vals[0][0] = o[0][0];
       vals[0][1] = o[0][1];
     } else {
-      w4_tile<2>(tile, st.ck, s.xs + ch * st.ck * 128, s.om + ch * st.ck, s.zero, lane, vals);
+      w4_tile<2, NK>(tile, st.ck, s.xs + ch * st.ck * 128, s.om + ch * st.ck, s.zero, lane, vals);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(s.empty + slot);
     tl_event(p, s.misc, 12);
-    if (p.trace != nullptr && lane == 0) {
-      atomicAdd(&s.misc->wait_ns, tw1 - tw0);
-      atomicAdd(&s.misc->busy_ns, global_ns() - tw1);
-    }
     if ((lane & 3) == 0) {
       float* out = P + static_cast<size_t>(rb * 16 + g) * pstride + chunk0 + ch;
       out[0] = vals[0][0];
@@ -740,9 +780,8 @@ __device__ void run_lm(const Params& p, const Smem& s, uint32_t& seq) {
   for (int i = threadIdx.x; i < kPartSlots; i += kConsumerThreads) s.ready[i] = i;
   named_sync();
   const int rb_first = t0 / st.chunks;
-  for (int t = t0; t < t1; ++t) {
+  for (int t = first_tile(t0, seq, warp); t < t1; t += kConsumers) {
     const uint32_t q = seq + static_cast<uint32_t>(t - t0);
-    if (static_cast<int>(q % kConsumers) != warp) continue;
     if (*reinterpret_cast<volatile int*>(&s.misc->abort)) break;
     const int slot = static_cast<int>(q % static_cast<uint32_t>(p.slots));
     if (!wait_bar(s.full + slot, (q / static_cast<uint32_t>(p.slots)) & 1u, p, s.misc)) break;
@@ -989,10 +1028,8 @@ __device__ void attention_step(const Params& p, const Smem& sm, const Layer& L, 
     // ---- the QKV tiles of the heads this span reads
     if (tid == 0) {
       const unsigned need = static_cast<unsigned>((layer + 1) * 8 * p.sq.chunks);
-      bool ok = true;
-      for (int j = 0; j < G && ok; ++j) ok = spin_geq(p, misc, p.hdr + kHdrQkv + G * h + j, need);
-      if (span_has_pos && ok) ok = spin_geq(p, misc, p.hdr + kHdrQkv + p.heads + h, need);
-      if (span_has_pos && ok) spin_geq(p, misc, p.hdr + kHdrQkv + p.heads + p.kv_heads + h, need);
+      // the G query heads' rows, and the new K and V rows when this span holds pos
+      spin_heads<G>(p, misc, h, span_has_pos, need);
       if (astamp) astamp[0] = global_ns();
       tl_event(p, misc, 21);
     }
@@ -1372,7 +1409,8 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     named_sync();
     tl_event(p, s.misc, 3);
     mark(p, s.misc, mk + 0);
-    run_partials<K_W8>(p, s, p.sq, false, p.pqkv, 8, 0, seq, p.hdr + kHdrQkv, 8);
+    if (p.sq.ck == 320) run_partials<K_W8, 10>(p, s, p.sq, false, p.pqkv, 8, 0, seq, p.hdr + kHdrQkv, 8);
+    else run_partials<K_W8, 0>(p, s, p.sq, false, p.pqkv, 8, 0, seq, p.hdr + kHdrQkv, 8);
     mark(p, s.misc, mk + 1);
     // ---- attention of the new token (items wait for their heads' QKV tiles)
     named_sync();  // the attention scratch aliases the staged activations
@@ -1453,7 +1491,8 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     named_sync();
     tl_event(p, s.misc, 33);
     if (p.trace != nullptr && tid == 0) trace_mark(p, s.misc, mk + 3, global_ns(), global_ns());
-    run_partials<K_W8>(p, s, p.so, true, p.po, 8, 0, seq);
+    if (p.so.ck == 512) run_partials<K_W8, 16>(p, s, p.so, true, p.po, 8, 0, seq);
+    else run_partials<K_W8, 0>(p, s, p.so, true, p.po, 8, 0, seq);
     grid_join(p, s.misc, ++joins, mk + 4);
     // ---- residual += o; RMSNorm + gate/up (partials; progress per down K chunk)
     tl_event(p, s.misc, 50);
@@ -1468,7 +1507,8 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     named_sync();
     tl_event(p, s.misc, 52);
     mark(p, s.misc, mk + 5);
-    run_partials<K_W4PAIR>(p, s, p.sgu, false, p.pgu, 16, 0, seq, p.hdr + kHdrGu, gu_rbs_per_chunk);
+    if (p.sgu.ck == 5) run_partials<K_W4PAIR, 5>(p, s, p.sgu, false, p.pgu, 16, 0, seq, p.hdr + kHdrGu, gu_rbs_per_chunk);
+    else run_partials<K_W4PAIR, 0>(p, s, p.sgu, false, p.pgu, 16, 0, seq, p.hdr + kHdrGu, gu_rbs_per_chunk);
     mark(p, s.misc, mk + 6);
     // ---- SwiGLU of the K chunks this CTA's down tiles read (once their gate/up tiles are done), then down
     named_sync();
@@ -1524,7 +1564,8 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     named_sync();
     tl_event(p, s.misc, 62);
     if (p.trace != nullptr && tid == 0) trace_mark(p, s.misc, mk + 7, global_ns(), global_ns());
-    run_partials<K_W4>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
+    if (p.sdn.ck == 19) run_partials<K_W4, 19>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
+    else run_partials<K_W4, 0>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
     grid_join(p, s.misc, ++joins, mk + 8);
   }
   // ---- residual += down; final RMSNorm + lm_head + greedy argmax
