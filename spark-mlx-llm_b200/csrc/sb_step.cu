@@ -1409,8 +1409,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     named_sync();
     tl_event(p, s.misc, 3);
     mark(p, s.misc, mk + 0);
-    if (p.sq.ck == 320) run_partials<K_W8, 10>(p, s, p.sq, false, p.pqkv, 8, 0, seq, p.hdr + kHdrQkv, 8);
-    else run_partials<K_W8, 0>(p, s, p.sq, false, p.pqkv, 8, 0, seq, p.hdr + kHdrQkv, 8);
+    run_partials<K_W8, 0>(p, s, p.sq, false, p.pqkv, 8, 0, seq, p.hdr + kHdrQkv, 8);
     mark(p, s.misc, mk + 1);
     // ---- attention of the new token (items wait for their heads' QKV tiles)
     named_sync();  // the attention scratch aliases the staged activations
@@ -1491,8 +1490,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     named_sync();
     tl_event(p, s.misc, 33);
     if (p.trace != nullptr && tid == 0) trace_mark(p, s.misc, mk + 3, global_ns(), global_ns());
-    if (p.so.ck == 512) run_partials<K_W8, 16>(p, s, p.so, true, p.po, 8, 0, seq);
-    else run_partials<K_W8, 0>(p, s, p.so, true, p.po, 8, 0, seq);
+    run_partials<K_W8, 0>(p, s, p.so, true, p.po, 8, 0, seq);
     grid_join(p, s.misc, ++joins, mk + 4);
     // ---- residual += o; RMSNorm + gate/up (partials; progress per down K chunk)
     tl_event(p, s.misc, 50);
@@ -1507,8 +1505,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     named_sync();
     tl_event(p, s.misc, 52);
     mark(p, s.misc, mk + 5);
-    if (p.sgu.ck == 5) run_partials<K_W4PAIR, 5>(p, s, p.sgu, false, p.pgu, 16, 0, seq, p.hdr + kHdrGu, gu_rbs_per_chunk);
-    else run_partials<K_W4PAIR, 0>(p, s, p.sgu, false, p.pgu, 16, 0, seq, p.hdr + kHdrGu, gu_rbs_per_chunk);
+    run_partials<K_W4PAIR, 0>(p, s, p.sgu, false, p.pgu, 16, 0, seq, p.hdr + kHdrGu, gu_rbs_per_chunk);
     mark(p, s.misc, mk + 6);
     // ---- SwiGLU of the K chunks this CTA's down tiles read (once their gate/up tiles are done), then down
     named_sync();
@@ -1564,8 +1561,7 @@ __global__ void __maxnreg__(160) step_kernel(const __grid_constant__ Params p) {
     named_sync();
     tl_event(p, s.misc, 62);
     if (p.trace != nullptr && tid == 0) trace_mark(p, s.misc, mk + 7, global_ns(), global_ns());
-    if (p.sdn.ck == 19) run_partials<K_W4, 19>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
-    else run_partials<K_W4, 0>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
+    run_partials<K_W4, 0>(p, s, p.sdn, true, p.pdn, 8, 0, seq);
     grid_join(p, s.misc, ++joins, mk + 8);
   }
   // ---- residual += down; final RMSNorm + lm_head + greedy argmax
