@@ -44,10 +44,12 @@
  * Conventions as spark_b200.h: device pointers, caller-owned buffers, a status
  * code, no allocation, no synchronization. The workspace (sb_step_workspace_size
  * bytes) must be zero-filled before the first launch; launches leave it ready
- * for the next one. Status word (uint32 index 1 of the workspace, sticky until
- * the caller clears it): bit 0 - a bounded device-side wait gave up and the
- * kernel returned early; bit 1 - positions[0] was outside [0, capacity), so
- * the step did nothing (no cache row is ever written out of bounds).
+ * for the next one (each launch zeroes only its first SB_STEP_STATUS_OFFSET
+ * bytes). Status word (uint32 at byte SB_STEP_STATUS_OFFSET of the workspace,
+ * sticky across launches until the caller clears it): bit 0 - a bounded
+ * device-side wait gave up and the kernel returned early; bit 1 -
+ * positions[0] was outside [0, capacity), so the step did nothing (no cache
+ * row is ever written out of bounds).
  */
 #ifndef SPARK_B200_STEP_H
 #define SPARK_B200_STEP_H
@@ -107,15 +109,20 @@ typedef struct sb_step_desc {
   size_t workspace_bytes;
   int world;   /* tensor-parallel degree (1 in this build) */
   int rank;
-  /* Optional (NULL = off): per-CTA timing of every join between operators,
-   * [grid CTAs][sb_step_trace_slots][4] uint64: arrival (this CTA's operator
-   * done) and release (all CTAs arrived) as globaltimer ns, then the time the
-   * CTA's consumer warps spent waiting for weight tiles and computing them
-   * during the operator (ns, summed over warps). */
+  /* Optional (NULL = off): per-CTA timing, [grid CTAs][sb_step_trace_slots][4]
+   * uint64: for every operator boundary the arrival (this CTA's operator done)
+   * and release (all CTAs arrived) as globaltimer ns; then, for the middle
+   * layer, a per-warp list of (event code, SM clock) pairs. */
   unsigned long long* trace;
 } sb_step_desc;
 
-/* Join slots per CTA in sb_step_desc.trace (5 per layer + the lm_head + 1). */
+/* Byte offset of the status word in the workspace. */
+#define SB_STEP_STATUS_OFFSET 1024
+size_t sb_step_status_offset(void);
+
+/* Trace slots per CTA in sb_step_desc.trace (the layers' operator marks, the
+ * lm_head, the kernel start, the attention items' marks and a per-warp event
+ * timeline of the middle layer). */
 int sb_step_trace_slots(int num_layers);
 
 /* Bytes of the workspace for `desc` (0 if the shape is unsupported). */

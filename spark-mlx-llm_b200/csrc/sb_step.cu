@@ -58,13 +58,15 @@ constexpr int kAttnRbk = kAttnChunk / 16;    // 16-token MMA row blocks per slic
 constexpr int kMaxLayers = 128;
 constexpr unsigned kStatusRange = 2u;        // status bit: position outside the KV cache
 // Workspace header (zeroed before every launch): word 0 the grid arrival
-// counter, word 1 the status; words [64, 128) QKV tiles finished per head
-// (stream order), [128, 192) attention finished per KV head (layer + 1),
-// [192, 256) gate/up tiles finished per down K chunk; then one 128-byte
-// release flag per CTA (written by the last CTA to arrive at a join).
+// counter; words [64, 128) QKV tiles finished per head (stream order),
+// [128, 192) attention finished per KV head (layer + 1), [192, 256) gate/up
+// tiles finished per down K chunk. After the header, a persistent block that
+// launches do not zero: word 0 the status (sticky until the caller clears it).
 constexpr int kHdrQkv = 64, kHdrAttn = 128, kHdrGu = 192;
 constexpr int kMaxCtas = 256;
-constexpr size_t kHdrBytes = 1024 + static_cast<size_t>(kMaxCtas) * 128;
+constexpr size_t kHdrBytes = 1024;
+constexpr size_t kPersistBytes = 256;
+static_assert(kHdrBytes == SB_STEP_STATUS_OFFSET, "status word offset");
 constexpr int kMarksPerLayer = 9;  // trace marks per layer
 constexpr int kAttnMarks = 4;      // extra trace marks per layer inside an attention item
 constexpr int kTlEvents = 96;      // timeline events per consumer warp (one traced layer)
@@ -140,9 +142,8 @@ struct Params {
   __nv_bfloat16* act;
   unsigned long long* keys;
   unsigned* sync;     // workspace word 0: grid arrival counter
-  unsigned* status;   // workspace word 1
+  unsigned* status;   // persistent word 0 (after the header)
   unsigned* hdr;      // workspace header words (per-head / per-chunk progress counters)
-  unsigned* release;  // per-CTA release flags (stride 32 words)
   unsigned* gcount;   // lm_head: counters of row blocks split between CTAs
   unsigned* acount;   // attention per-KV-head counters
   float* gpart;       // lm_head: split row-block partials [rb][kChunks][32]
@@ -1641,7 +1642,7 @@ int geometry(const sb_step_desc* d, Geometry* g) {
   g->slot_bytes = (tmax + 127) / 128 * 128;
   g->attn_chunks = (d->capacity + kAttnSpan - 1) / kAttnSpan;
   Workspace& w = g->ws;
-  size_t off = kHdrBytes;  // header words and release flags
+  size_t off = kHdrBytes + kPersistBytes;  // header words, persistent words
   auto take = [&](size_t bytes) {
     const size_t at = off;
     off = (off + bytes + 255) / 256 * 256;
@@ -1666,6 +1667,8 @@ int geometry(const sb_step_desc* d, Geometry* g) {
 
 using namespace sb;
 using namespace sb::step;
+
+extern "C" size_t sb_step_status_offset(void) { return kHdrBytes; }
 
 extern "C" int sb_step_trace_slots(int num_layers) {
   return num_layers * (kMarksPerLayer + kAttnMarks) + 2 + kTlSlots;
@@ -1723,9 +1726,8 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   p.keys = d->argmax_key;
   unsigned* ws = static_cast<unsigned*>(d->workspace);
   p.sync = ws;
-  p.status = ws + 1;
+  p.status = reinterpret_cast<unsigned*>(static_cast<uint8_t*>(d->workspace) + kHdrBytes);
   p.hdr = ws;
-  p.release = ws + 256;
   uint8_t* wb = static_cast<uint8_t*>(d->workspace);
   p.gcount = reinterpret_cast<unsigned*>(wb + g.ws.gcount);
   p.acount = reinterpret_cast<unsigned*>(wb + g.ws.acount);
@@ -1778,7 +1780,7 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
                                 " B dynamic + " + std::to_string(fa.sharedSizeBytes) + " B static shared memory)");
     }
   }
-  // the arrival counter starts at zero for every step
+  // the header counters start at zero for every step (the status word after the header persists)
   cudaError_t err = cudaMemsetAsync(d->workspace, 0, kHdrBytes, as_stream(stream));
   if (err != cudaSuccess) return fail(SB_ECUDA, std::string("step counter reset: ") + cudaGetErrorString(err));
   cudaLaunchConfig_t config = {};

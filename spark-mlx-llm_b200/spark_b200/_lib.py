@@ -178,6 +178,7 @@ SIGNATURES = {
     "sb_step_tile_bytes": (_int, [ctypes.POINTER(sb_step_desc), ctypes.POINTER(_i64)]),
     "sb_step_run": (_int, [ctypes.POINTER(sb_step_desc), _c_void_p]),
     "sb_step_trace_slots": (_int, [_int]),
+    "sb_step_status_offset": (_size, []),
 }
 
 _lock = threading.Lock()

@@ -188,8 +188,11 @@ class StepStreams:
             self.desc.num_layers = full
 
     def status(self):
-        """Device status word of the step kernel (nonzero: a bounded wait gave up)."""
-        return int(self.workspace[:8].view(torch.int32)[1].item())
+        """Device status word of the step kernel (nonzero: a bounded wait gave up,
+        or a position outside the cache); sticky across launches until cleared."""
+        at = lib().sb_step_status_offset()
+        return int(self.workspace[at:at + 4].view(torch.int32).item())
 
     def clear_status(self):
-        self.workspace[4:8].zero_()
+        at = lib().sb_step_status_offset()
+        self.workspace[at:at + 4].zero_()

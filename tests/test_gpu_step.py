@@ -135,3 +135,22 @@ def test_step_kernel_rejects_positions_beyond_the_cache():
     for a, b in zip(before, (dec.k_cache[0], dec.v_cache[0], dec.k_scale[0])):
         assert torch.equal(a, b)
     dec.check_status()  # cleared
+
+
+def test_step_kernel_status_is_sticky_across_launches():
+    """A status raised by one launch survives the launches after it until it is read."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from spark_b200._lib import SBError
+
+    dec = _decoder("step", layers=1, capacity=16)
+    dec.reset(torch.tensor([5], dtype=torch.int32))
+    dec.positions.fill_(dec.capacity)
+    dec.step()  # outside the cache: reports and does nothing
+    dec.positions.fill_(1)
+    for _ in range(3):
+        dec.step()  # good steps after it
+    torch.cuda.synchronize()
+    with pytest.raises(SBError, match="outside the KV cache"):
+        dec.check_status()
+    dec.check_status()  # cleared
