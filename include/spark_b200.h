@@ -191,6 +191,27 @@ int sb_int8_sdpa_decode_static(const void* q, const int8_t* k, const void* k_sca
                                float scale, void* stream);
 
 /*
+ * INT8-KV multi-query attention (prefill / chunked prompt), the BASELINE KV
+ * format of sb_int8_sdpa_decode with L >= 1 queries per sequence. Replaces the
+ * prefill route of int8_quantized_sdpa (spark_mlx_ext/int8_quantized_sdpa_prefill.py:44-57,
+ * kernel _int8_prefill_sources.py:7-154) and its staged recipe
+ * (int8_quantized_sdpa.py:122-153) for this format:
+ *   q    [B, H, q_len, D] BF16 (layout 0) or [B, q_len, H, D] (layout 1)
+ *   k, v [B, KH, capacity, D] int8; k_scale, v_scale [B, KH, capacity] fp16
+ *   out  same layout as q, BF16
+ * The queries are the last q_len of `length` positions; causal != 0 applies
+ * the bottom-right mask (query l sees keys [0, length - q_len + l]), else every
+ * query sees keys [0, length). Scores, softmax and accumulation in fp32; the
+ * probabilities times the V scale are rounded to fp16 for P.V. D = 128, H/KH
+ * in {1, 2, 4, 8}, q_len <= length <= capacity, K/V caches 16-byte aligned.
+ * No workspace.
+ */
+int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                         const void* v_scale, void* out, int64_t batch, int num_heads,
+                         int num_kv_heads, int64_t q_len, int64_t length, int64_t capacity,
+                         int head_dim, float scale, int causal, int layout, void* stream);
+
+/*
  * Attention over MLX affine-quantized KV tuples: the int8_quantized_sdpa input
  * format (spark_mlx_ext/int8_quantized_sdpa.py:156-287, staged recipe
  * _fallback :122-153). Replaces int8_quantized_sdpa for its affine tuples.

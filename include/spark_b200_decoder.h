@@ -114,6 +114,26 @@ int sb_kv_append_int8(const void* k_new, const void* v_new, int8_t* k_cache, voi
                       void* v_scale, int64_t batch, int num_kv_heads, int64_t seq_len, int head_dim,
                       int64_t capacity, const int32_t* start, void* stream);
 
+/*
+ * Batched-prompt split of a QKV projection: rows qkv[m, :] (stride ld,
+ * [H + 2 KH heads x D] bf16, m = b * seq_len + l) -> query heads RoPE-rotated
+ * (non-traditional half split, rope_dims = head_dim = 128, angle
+ * positions[m] * rope_base^(-2i/rope_dims)) into q_out [B, seq_len, H, D];
+ * key heads rotated and value heads as they are, quantized into the INT8 cache
+ * at positions[m] (the arithmetic of sb_kv_append_int8). Replaces the split,
+ * RoPE and cache update of Attention.__call__ (spark_mlx_llm/model.py:172-193,
+ * ops/qkv.py:140-177) for a prompt chunk. Rows whose position is outside
+ * [0, capacity) write nothing to the cache.
+ */
+int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, void* q_out, int8_t* k_cache,
+                      void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch, int64_t seq_len,
+                      int num_heads, int num_kv_heads, int head_dim, int64_t capacity, int rope_dims,
+                      float rope_base, void* stream);
+
+/* out = bf16(silu(gate) * up) elementwise over `count` bf16 values (the gated MLP
+ * of spark_mlx_llm/ops/ffn.py:98-103 with SiLU); 16-byte aligned buffers. */
+int sb_swiglu(const void* gate, const void* up, void* out, int64_t count, void* stream);
+
 /* INT8-KV decode attention with per-batch lengths lengths[b] + length_offset read on
  * the device; max_length bounds them (it sizes the split-K workspace).
  * prefix_constant = 1 promises that `lengths` and every cache row except the

@@ -1,0 +1,509 @@
+// INT8-KV multi-query (prefill) attention and the batched-prompt helpers for sm_100a.
+//
+// Reference: the prefill route of int8_quantized_sdpa
+// (extensions/spark-mlx-ext/spark_mlx_ext/int8_quantized_sdpa_prefill.py:44-57,
+// kernel _int8_prefill_sources.py:7-154: query rows interleaved across the GQA
+// heads share each KV tile; QK, online softmax and PV in one dispatch; fp32
+// scores, normalizers and accumulators) and its staged recipe
+// int8_quantized_sdpa.py:122-153 (bottom-right causal mask: query l of L sees
+// keys [0, N - L + l]). KV format here: the BASELINE int8 codes [B, KH, cap, D]
+// with one fp16 scale per token per head (K = code * scale), D = 128.
+//
+// Design (B200): one CTA = 64 query rows (position-major, the G heads of a KV
+// head interleaved) x one KV head; four warps of 16 rows. KV tiles of 64
+// tokens stream through a double-buffered shared-memory stage (cp.async), are
+// converted once per CTA to fp16 codes (exact: |code| <= 127) and read by the
+// tensor cores (mma.sync m16n8k16, fp16 operands, fp32 accumulators) through
+// ldmatrix (K as the column-major B of QK^T, V transposed by ldmatrix.trans
+// for PV). The K scale multiplies each score column, the V scale each
+// probability before it is rounded to fp16 for PV; softmax is online in fp32
+// (exp2 with log2 e folded into the score scale). Tiles past a CTA's last
+// query position are skipped (causal), the diagonal tile is masked per row.
+#include <algorithm>
+#include <cmath>
+#include <string>
+
+#include "sb_common.cuh"
+#include "spark_b200_decoder.h"
+
+namespace sb {
+namespace prefill {
+
+constexpr int kD = 128;
+constexpr int kRows = 64;        // query rows per CTA
+constexpr int kKeys = 64;        // keys per tile
+constexpr int kWarps = 4;        // 16 query rows each
+constexpr int kThreads = kWarps * 32;
+constexpr int kHStride = kD * 2 + 16;                // fp16 tile row stride (bytes): ldmatrix without bank conflicts
+constexpr int kHTile = kKeys * kHStride;             // one fp16 tile (K or V)
+constexpr int kRawTile = kKeys * kD;                 // one int8 tile (K or V)
+constexpr int kOffKh = 0;
+constexpr int kOffVh = kHTile;
+constexpr int kOffRaw = 2 * kHTile;                  // [2 buffers][K | V] int8
+constexpr int kOffScale = kOffRaw + 2 * 2 * kRawTile;  // float K scales [64], V scales [64]
+constexpr int kSmem = kOffScale + 2 * kKeys * 4;
+
+struct Params {
+  const __nv_bfloat16* q;
+  const int8_t* k;
+  const __half* ks;
+  const int8_t* v;
+  const __half* vs;
+  __nv_bfloat16* out;
+  int heads, kv_heads, q_len, length, capacity;
+  int causal, layout;  // layout 0: q/out [B, H, L, D]; 1: [B, L, H, D]
+  float scale_log2;    // softmax scale * log2(e)
+  int tiles;           // query tiles per (batch, kv head)
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// Four int8 codes (one 32-bit word) -> two fp16x2 words of the same values, exactly:
+// byte b = code + 128 under the fp16 exponent of 1024 is 1024 + b; minus 1152.
+__device__ __forceinline__ void codes_to_half(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const __half2 off = __floats2half2_rn(1152.f, 1152.f);
+  const uint32_t a = prmt(u, 0x64646464u, 0x4140u), b = prmt(u, 0x64646464u, 0x4342u);
+  const __half2 ha = __hsub2(*reinterpret_cast<const __half2*>(&a), off);
+  const __half2 hb = __hsub2(*reinterpret_cast<const __half2*>(&b), off);
+  lo = *reinterpret_cast<const uint32_t*>(&ha);
+  hi = *reinterpret_cast<const uint32_t*>(&hb);
+}
+
+template <int G>
+__global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant__ Params p) {
+  extern __shared__ __align__(128) uint8_t sm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int g = lane >> 2, c = lane & 3;
+  const int tile = p.tiles - 1 - static_cast<int>(blockIdx.x);  // latest (longest) query tiles first
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int nrows = p.q_len * G;  // query row r = l * G + (head in group)
+  const int row0 = tile * kRows;
+  const int qoff = p.length - p.q_len;  // position of query l is qoff + l (bottom-right)
+  const int last_row = min(row0 + kRows, nrows) - 1;
+  // keys this CTA reads: [0, kend)
+  const int kend = p.causal ? min(p.length, qoff + last_row / G + 1) : p.length;
+  const int ntiles = (kend + kKeys - 1) / kKeys;
+  const size_t head_base = (static_cast<size_t>(b) * p.kv_heads + kvh) * p.capacity;
+  const int8_t* kbase = p.k + head_base * kD;
+  const int8_t* vbase = p.v + head_base * kD;
+  float* sks = reinterpret_cast<float*>(sm + kOffScale);
+  float* svs = sks + kKeys;
+
+  // this warp's two rows per lane (g, g + 8) and their positions / pointers
+  const int wr0 = row0 + warp * 16;
+  const int ra = wr0 + g, rb = ra + 8;
+  auto qkv_offset = [&](int r) -> size_t {
+    const int l = r / G, head = kvh * G + r % G;
+    return p.layout == 0 ? ((static_cast<size_t>(b) * p.heads + head) * p.q_len + l) * kD
+                         : ((static_cast<size_t>(b) * p.q_len + l) * p.heads + head) * kD;
+  };
+  const int pos_a = qoff + ra / G, pos_b = qoff + rb / G;
+  const int kend_a = p.causal ? min(p.length, pos_a + 1) : p.length;
+  const int kend_b = p.causal ? min(p.length, pos_b + 1) : p.length;
+  const int warp_last = qoff + min(wr0 + 15, nrows - 1) / G;  // latest position among the warp's rows
+  const bool warp_live = wr0 < nrows;
+
+  grid_dependency_wait();
+
+  auto load_tile = [&](int kt, int buf) {
+    int8_t* rk = reinterpret_cast<int8_t*>(sm + kOffRaw + buf * 2 * kRawTile);
+    const int key0 = kt * kKeys;
+    for (int i = tid; i < 2 * kKeys * (kD / 16); i += kThreads) {
+      const int mat = i / (kKeys * (kD / 16)), rem = i % (kKeys * (kD / 16));
+      const int key = rem / (kD / 16), ch = rem % (kD / 16);
+      int8_t* dst = rk + mat * kRawTile + key * kD + ch * 16;
+      if (key0 + key < kend)
+        cp_async16(dst, (mat ? vbase : kbase) + static_cast<size_t>(key0 + key) * kD + ch * 16);
+      else
+        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    cp_async_commit_group();
+  };
+
+  // q rows of the warp as fp16 A fragments (rows beyond the query count are zero)
+  uint32_t qa[8][4];
+  {
+    const __nv_bfloat16* qra = ra < nrows ? p.q + qkv_offset(ra) : nullptr;
+    const __nv_bfloat16* qrb = rb < nrows ? p.q + qkv_offset(rb) : nullptr;
+#pragma unroll
+    for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int d = ks * 16 + h * 8 + 2 * c;
+        const uint32_t wa = qra ? *reinterpret_cast<const uint32_t*>(qra + d) : 0u;
+        const uint32_t wb = qrb ? *reinterpret_cast<const uint32_t*>(qrb + d) : 0u;
+        qa[ks][2 * h] = pack_half2(bf16_lo(wa), bf16_hi(wa));
+        qa[ks][2 * h + 1] = pack_half2(bf16_lo(wb), bf16_hi(wb));
+      }
+  }
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const uint32_t kh_base = smem_u32(sm + kOffKh), vh_base = smem_u32(sm + kOffVh);
+
+  if (ntiles > 0) load_tile(0, 0);
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int key0 = kt * kKeys;
+    if (kt + 1 < ntiles) load_tile(kt + 1, (kt + 1) & 1);
+    else cp_async_commit_group();  // an empty group keeps the wait count uniform
+    cp_async_wait_group<1>();
+    __syncthreads();
+    // ---- int8 tile -> fp16 codes (exact), and the tile's scales
+    {
+      const int8_t* rk = reinterpret_cast<const int8_t*>(sm + kOffRaw + (kt & 1) * 2 * kRawTile);
+      for (int i = tid; i < 2 * kKeys * (kD / 16); i += kThreads) {
+        const int mat = i / (kKeys * (kD / 16)), rem = i % (kKeys * (kD / 16));
+        const int key = rem / (kD / 16), ch = rem % (kD / 16);
+        const uint4 w = *reinterpret_cast<const uint4*>(rk + mat * kRawTile + key * kD + ch * 16);
+        uint32_t h[8];
+        codes_to_half(w.x, h[0], h[1]);
+        codes_to_half(w.y, h[2], h[3]);
+        codes_to_half(w.z, h[4], h[5]);
+        codes_to_half(w.w, h[6], h[7]);
+        uint8_t* dst = sm + (mat ? kOffVh : kOffKh) + key * kHStride + ch * 32;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(dst + 16) = make_uint4(h[4], h[5], h[6], h[7]);
+      }
+      if (tid < 2 * kKeys) {
+        const int key = key0 + (tid & (kKeys - 1));
+        const __half* src = tid < kKeys ? p.ks : p.vs;
+        const float sc = key < kend ? __half2float(src[head_base + key]) : 0.f;
+        (tid < kKeys ? sks : svs)[tid & (kKeys - 1)] = sc;
+      }
+    }
+    __syncthreads();
+    if (warp_live && key0 <= warp_last) {
+      // ---- scores S = q . K^T for the warp's 16 rows x 64 keys
+      float s[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+#pragma unroll
+      for (int ks2 = 0; ks2 < 4; ++ks2)
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          uint32_t bk[4];
+          ldsm_x4(bk, kh_base + (nt * 8 + (lane & 7)) * kHStride + (ks2 * 32 + (lane >> 3) * 8) * 2);
+          mma_16816<true>(s[nt], qa[2 * ks2], bk[0], bk[1]);
+          mma_16816<true>(s[nt], qa[2 * ks2 + 1], bk[2], bk[3]);
+        }
+      // ---- scale, mask, online softmax (log2 domain)
+      float mx[2] = {m_run[0], m_run[1]};
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int kk = nt * 8 + 2 * c + (e & 1);
+          const int key = key0 + kk;
+          const bool ok = key < ((e < 2) ? kend_a : kend_b);
+          const float v = s[nt][e] * sks[kk] * p.scale_log2;
+          s[nt][e] = ok ? v : -INFINITY;
+          mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
+        }
+      float corr[2];
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+        mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 1));
+        mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], 2));
+        corr[i] = mx[i] == -INFINITY ? 1.f : exp2f(m_run[i] - mx[i]);
+        m_run[i] = mx[i];
+        l_run[i] *= corr[i];
+      }
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= corr[0];
+        o[n][1] *= corr[0];
+        o[n][2] *= corr[1];
+        o[n][3] *= corr[1];
+      }
+      // probabilities; P' = P * V scale rounded to fp16 as the A operand of P.V
+      uint32_t pa[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        float pr[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float mrow = m_run[e >> 1];
+          const float pe = s[nt][e] == -INFINITY ? 0.f : exp2f(s[nt][e] - mrow);
+          l_run[e >> 1] += pe;
+          pr[e] = pe * svs[nt * 8 + 2 * c + (e & 1)];
+        }
+        pa[nt >> 1][(nt & 1) * 2] = pack_half2(pr[0], pr[1]);
+        pa[nt >> 1][(nt & 1) * 2 + 1] = pack_half2(pr[2], pr[3]);
+      }
+      // ---- O += P' . V (V transposed by ldmatrix.trans)
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int np = 0; np < 8; ++np) {
+          uint32_t bv[4];
+          ldsm_x4_trans(bv, vh_base + (j * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kHStride +
+                                (np * 16 + (lane >> 4) * 8) * 2);
+          mma_16816<true>(o[2 * np], pa[j], bv[0], bv[1]);
+          mma_16816<true>(o[2 * np + 1], pa[j], bv[2], bv[3]);
+        }
+    }
+    __syncthreads();  // the fp16 tiles and scales are rewritten by the next tile
+  }
+  cp_async_wait_group<0>();
+  // ---- normalize and store (rows past the query count are not stored)
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 1);
+    l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 2);
+  }
+  if (!warp_live) return;
+  const float inv_a = l_run[0] > 0.f ? 1.0f / l_run[0] : 0.f;
+  const float inv_b = l_run[1] > 0.f ? 1.0f / l_run[1] : 0.f;
+  __nv_bfloat16* oa = ra < nrows ? p.out + qkv_offset(ra) : nullptr;
+  __nv_bfloat16* ob = rb < nrows ? p.out + qkv_offset(rb) : nullptr;
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const int d = n * 8 + 2 * c;
+    if (oa) *reinterpret_cast<__nv_bfloat162*>(oa + d) = __floats2bfloat162_rn(o[n][0] * inv_a, o[n][1] * inv_a);
+    if (ob) *reinterpret_cast<__nv_bfloat162*>(ob + d) = __floats2bfloat162_rn(o[n][2] * inv_b, o[n][3] * inv_b);
+  }
+}
+
+// ------------------------------------------- batched prompt: RoPE + split + KV append
+// One warp per (token m, head j of the H + 2 KH heads of a QKV projection row):
+// query heads rotate into q_out [M, H, D]; key heads rotate and, like value
+// heads, are quantized into the INT8 cache at the token's position. The
+// arithmetic is the single-token path's (the QKV projection's bf16 outputs are
+// rotated in fp32 with sincosf(pos * inv_freq[i]) and stored as bf16; K/V rows
+// are quantized from those bf16 values with fp16 scale = absmax / 127, 1 for a
+// zero row, code = clamp(rint(x / scale), -127, 127)).
+struct RopeParams {
+  const __nv_bfloat16* qkv;
+  int64_t ld;  // qkv row stride (elements)
+  const int32_t* positions;
+  __nv_bfloat16* q_out;
+  int8_t* k_cache;
+  __half* k_scale;
+  int8_t* v_cache;
+  __half* v_scale;
+  int rows, seq_len, heads, kv_heads, capacity, rope_pairs;
+  float inv_freq[kD / 2];
+};
+
+__global__ void rope_append_kernel(const __grid_constant__ RopeParams p) {
+  grid_dependency_wait();
+  const int lane = threadIdx.x & 31;
+  const int nh = p.heads + 2 * p.kv_heads;
+  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (item >= p.rows * nh) return;
+  const int m = item / nh, j = item % nh;
+  const int bi = m / p.seq_len;
+  const int pos = p.positions[m];
+  const __nv_bfloat16* src = p.qkv + static_cast<size_t>(m) * p.ld + static_cast<size_t>(j) * kD;
+  float a[2], bb[2];
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const int i = lane + 32 * t;  // rotation pair (i, i + 64)
+    a[t] = __bfloat162float(src[i]);
+    bb[t] = __bfloat162float(src[i + kD / 2]);
+    if (j < p.heads + p.kv_heads && i < p.rope_pairs) {
+      float sn, cs;
+      sincosf(static_cast<float>(pos) * p.inv_freq[i], &sn, &cs);
+      const float ra = a[t] * cs - bb[t] * sn, rb = bb[t] * cs + a[t] * sn;
+      a[t] = __bfloat162float(__float2bfloat16_rn(ra));
+      bb[t] = __bfloat162float(__float2bfloat16_rn(rb));
+    }
+  }
+  if (j < p.heads) {
+    __nv_bfloat16* dst = p.q_out + (static_cast<size_t>(m) * p.heads + j) * kD;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      dst[lane + 32 * t] = __float2bfloat16_rn(a[t]);
+      dst[lane + 32 * t + kD / 2] = __float2bfloat16_rn(bb[t]);
+    }
+    return;
+  }
+  const bool is_k = j < p.heads + p.kv_heads;
+  const int h = is_k ? j - p.heads : j - p.heads - p.kv_heads;
+  if (pos < 0 || pos >= p.capacity) return;  // the host checks positions; never write outside the cache
+  float amax = fmaxf(fmaxf(fabsf(a[0]), fabsf(a[1])), fmaxf(fabsf(bb[0]), fabsf(bb[1])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
+  if (__half2float(s16) == 0.f) s16 = __float2half_rn(1.0f);
+  const float sc = __half2float(s16);
+  const size_t row = (static_cast<size_t>(bi) * p.kv_heads + h) * p.capacity + pos;
+  int8_t* dst = (is_k ? p.k_cache : p.v_cache) + row * kD;
+  auto code = [&](float x) {
+    return static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(x, sc)), -127.f), 127.f)));
+  };
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    dst[lane + 32 * t] = code(a[t]);
+    dst[lane + 32 * t + kD / 2] = code(bb[t]);
+  }
+  if (lane == 0) (is_k ? p.k_scale : p.v_scale)[row] = s16;
+}
+
+// ------------------------------------------------------------- SwiGLU (elementwise)
+// out = bf16(silu(g) * u) with g, u the bf16 gate / up projections (the
+// single-token path's fused gate/up epilogue, sb_gemv.cu EPI_SWIGLU).
+__global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ gate, const __nv_bfloat16* __restrict__ up,
+                              __nv_bfloat16* __restrict__ out, int64_t count) {
+  grid_dependency_wait();
+  const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
+  if (i >= count) return;
+  if (i + 8 <= count) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(gate + i), uv = *reinterpret_cast<const uint4*>(up + i);
+    const uint32_t gw[4] = {gv.x, gv.y, gv.z, gv.w}, uw[4] = {uv.x, uv.y, uv.z, uv.w};
+    uint32_t r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float o2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float g = e ? bf16_hi(gw[k]) : bf16_lo(gw[k]);
+        const float u = e ? bf16_hi(uw[k]) : bf16_lo(uw[k]);
+        o2[e] = g / (1.0f + expf(-g)) * u;
+      }
+      const __nv_bfloat162 h = __floats2bfloat162_rn(o2[0], o2[1]);
+      r[k] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    *reinterpret_cast<uint4*>(out + i) = make_uint4(r[0], r[1], r[2], r[3]);
+  } else {
+    for (int64_t k = i; k < count; ++k) {
+      const float g = __bfloat162float(gate[k]), u = __bfloat162float(up[k]);
+      out[k] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+    }
+  }
+}
+
+}  // namespace prefill
+}  // namespace sb
+
+using namespace sb;
+using namespace sb::prefill;
+
+namespace {
+
+template <int G>
+int launch_prefill(const Params& p, int batch, int kv_heads, cudaStream_t stream) {
+  static bool attr_done = false;  // per template instance; the attribute is per function
+  if (!attr_done) {
+    const cudaError_t e = cudaFuncSetAttribute(prefill_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    if (e != cudaSuccess) return fail(SB_ECUDA, std::string("prefill attention attribute: ") + cudaGetErrorString(e));
+    attr_done = true;
+  }
+  return launch("int8_sdpa_prefill", prefill_kernel<G>, dim3(p.tiles, kv_heads, batch), dim3(kThreads), kSmem,
+                stream, p);
+}
+
+}  // namespace
+
+extern "C" int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                                    const void* v_scale, void* out, int64_t batch, int num_heads, int num_kv_heads,
+                                    int64_t q_len, int64_t length, int64_t capacity, int head_dim, float scale,
+                                    int causal, int layout, void* stream) {
+  SB_REQUIRE(q && k && k_scale && v && v_scale && out, "null pointer");
+  SB_REQUIRE(head_dim == kD, "the prefill attention supports head_dim 128");
+  SB_REQUIRE(batch >= 1 && batch <= 65535, "batch must be in [1, 65535]");
+  SB_REQUIRE(num_kv_heads >= 1 && num_kv_heads <= 65535 && num_heads % num_kv_heads == 0, "heads");
+  const int G = num_heads / num_kv_heads;
+  SB_REQUIRE(G == 1 || G == 2 || G == 4 || G == 8, "query heads per KV head must be 1, 2, 4 or 8");
+  SB_REQUIRE(q_len >= 1 && q_len <= length && length <= capacity && capacity <= (1LL << 30),
+             "need 1 <= q_len <= length <= capacity");
+  SB_REQUIRE(layout == 0 || layout == 1, "layout must be 0 ([B,H,L,D]) or 1 ([B,L,H,D])");
+  SB_REQUIRE(reinterpret_cast<uintptr_t>(k) % 16 == 0 && reinterpret_cast<uintptr_t>(v) % 16 == 0,
+             "the K/V caches must be 16-byte aligned");
+  SB_REQUIRE(reinterpret_cast<uintptr_t>(q) % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 4 == 0,
+             "q and out must be 4-byte aligned");
+  Params p;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = k;
+  p.ks = static_cast<const __half*>(k_scale);
+  p.v = v;
+  p.vs = static_cast<const __half*>(v_scale);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.heads = num_heads;
+  p.kv_heads = num_kv_heads;
+  p.q_len = static_cast<int>(q_len);
+  p.length = static_cast<int>(length);
+  p.capacity = static_cast<int>(capacity);
+  p.causal = causal != 0;
+  p.layout = layout;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  const int64_t tiles = (q_len * G + kRows - 1) / kRows;
+  SB_REQUIRE(tiles <= 0x7fffffff, "too many query rows");
+  p.tiles = static_cast<int>(tiles);
+  cudaStream_t s = as_stream(stream);
+  switch (G) {
+    case 1: return launch_prefill<1>(p, static_cast<int>(batch), num_kv_heads, s);
+    case 2: return launch_prefill<2>(p, static_cast<int>(batch), num_kv_heads, s);
+    case 4: return launch_prefill<4>(p, static_cast<int>(batch), num_kv_heads, s);
+    default: return launch_prefill<8>(p, static_cast<int>(batch), num_kv_heads, s);
+  }
+}
+
+extern "C" int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, void* q_out,
+                                 int8_t* k_cache, void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch,
+                                 int64_t seq_len, int num_heads, int num_kv_heads, int head_dim, int64_t capacity,
+                                 int rope_dims, float rope_base, void* stream) {
+  SB_REQUIRE(qkv && positions && q_out && k_cache && k_scale && v_cache && v_scale, "null pointer");
+  SB_REQUIRE(head_dim == kD && rope_dims == kD, "head_dim and rope_dims must be 128");
+  SB_REQUIRE(batch >= 1 && seq_len >= 1 && num_heads >= 1 && num_kv_heads >= 1, "shape");
+  SB_REQUIRE(ld >= static_cast<int64_t>(num_heads + 2 * num_kv_heads) * head_dim, "qkv row stride too small");
+  SB_REQUIRE(capacity >= 1 && capacity <= (1LL << 30), "capacity");
+  const int64_t rows = batch * seq_len;
+  const int64_t items = rows * (num_heads + 2 * num_kv_heads);
+  SB_REQUIRE(items <= (1LL << 31) - 1, "too many rows");
+  RopeParams p;
+  p.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  p.ld = ld;
+  p.positions = positions;
+  p.q_out = static_cast<__nv_bfloat16*>(q_out);
+  p.k_cache = k_cache;
+  p.k_scale = static_cast<__half*>(k_scale);
+  p.v_cache = v_cache;
+  p.v_scale = static_cast<__half*>(v_scale);
+  p.rows = static_cast<int>(rows);
+  p.seq_len = static_cast<int>(seq_len);
+  p.heads = num_heads;
+  p.kv_heads = num_kv_heads;
+  p.capacity = static_cast<int>(capacity);
+  p.rope_pairs = rope_dims / 2;
+  for (int i = 0; i < kD / 2; ++i)
+    p.inv_freq[i] = static_cast<float>(std::pow(static_cast<double>(rope_base), -2.0 * i / rope_dims));
+  constexpr int kWarpsPerBlock = 8;
+  return launch("rope_kv_append", rope_append_kernel, dim3(static_cast<unsigned>((items + kWarpsPerBlock - 1) / kWarpsPerBlock)),
+                dim3(32 * kWarpsPerBlock), 0, as_stream(stream), p);
+}
+
+extern "C" int sb_swiglu(const void* gate, const void* up, void* out, int64_t count, void* stream) {
+  SB_REQUIRE(gate && up && out, "null pointer");
+  SB_REQUIRE(count >= 0, "count");
+  if (count == 0) return SB_OK;
+  SB_REQUIRE(reinterpret_cast<uintptr_t>(gate) % 16 == 0 && reinterpret_cast<uintptr_t>(up) % 16 == 0 &&
+                 reinterpret_cast<uintptr_t>(out) % 16 == 0,
+             "gate, up and out must be 16-byte aligned");
+  const int64_t threads = (count + 7) / 8;
+  return launch("swiglu", swiglu_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0,
+                as_stream(stream), static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up),
+                static_cast<__nv_bfloat16*>(out), count);
+}

@@ -140,6 +140,17 @@ SIGNATURES = {
          _int, _float, _c_void_p, _size, _c_void_p],
     ),
     "sb_int8_sdpa_workspace_size": (_size, [_i64, _int, _int, _i64, _int]),
+    "sb_int8_sdpa_prefill": (
+        _int,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _i64, _i64, _i64,
+         _int, _float, _int, _int, _c_void_p],
+    ),
+    "sb_rope_kv_append": (
+        _int,
+        [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _int,
+         _int, _int, _i64, _int, _float, _c_void_p],
+    ),
+    "sb_swiglu": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "sb_int8_sdpa_decode_static": (
         _int,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _i64, _i64, _int,

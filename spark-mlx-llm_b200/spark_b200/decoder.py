@@ -42,6 +42,8 @@ BF16 = 0
 # device status word: the last 32-bit word of a workspace's 128 KiB counter
 # region (nonzero when a bounded device-side wait gave up)
 STATUS_WORD = 128 * 1024 // 4 - 1
+# prompt tokens per batched prefill chunk (the reference's prompt chunk, generation.py:78)
+PREFILL_CHUNK = 512
 
 
 @dataclass(frozen=True)
@@ -390,12 +392,26 @@ class SyntheticDecoder:
         self.keys.zero_()
         self.tokens.copy_(torch.as_tensor(first_tokens, dtype=torch.int32, device=self.device).reshape(-1))
 
-    def prefill(self, prompt):
-        """Feed prompt[:, 0..P-1] token by token; leaves the greedy next token in ``tokens``.
+    def prefill(self, prompt, *, chunk=PREFILL_CHUNK):
+        """Feed prompt[:, 0..P-1]; leaves the greedy next token in ``tokens``.
 
-        ``prompt`` is an int32 device tensor [batch, P]. Runs decode steps (the
-        lm_head only on the last one); positions end at P.
+        ``prompt`` is an int32 device tensor [batch, P]; positions end at P.
+        One GPU: the prompt runs in chunks of ``chunk`` tokens (the reference's
+        prompt chunk, ``generation.py:78``) through the batched path - tensor-core
+        linears at M = batch x chunk, RoPE and the INT8 cache append per chunk,
+        and the INT8-KV prefill attention (bottom-right causal over the cache).
+        Tensor-parallel ranks, or ``chunk=0``, feed it token by token
+        (``prefill_stepwise``).
         """
+        prompt = prompt.to(device=self.device, dtype=torch.int32)
+        if self.world > 1 or not chunk:
+            self.prefill_stepwise(prompt)
+            return
+        self._prefill_chunked(prompt, int(chunk))
+
+    def prefill_stepwise(self, prompt):
+        """Feed the prompt through single-token decode steps (the lm_head only on
+        the last one); positions end at P."""
         prompt = prompt.to(device=self.device, dtype=torch.int32)
         self.reset(prompt[:, 0])
         for t in range(prompt.shape[1]):
@@ -404,6 +420,82 @@ class SyntheticDecoder:
             if not last:
                 self.tokens.copy_(prompt[:, t + 1])
         # positions[b] == P now; tokens holds the first generated token
+
+    def _prefill_buffers(self, rows):
+        """Activation buffers for `rows` prompt tokens (grown on demand, kept)."""
+        cfg, dev = self.cfg, self.device
+        have = getattr(self, "_pf", None)
+        if have is not None and have["rows"] >= rows:
+            return have
+        d, hq, hkv = cfg.head_dim, self.hq, self.hkv
+        nqkv = (hq + 2 * hkv) * d
+
+        def buf(*shape):
+            return torch.empty(shape, dtype=torch.bfloat16, device=dev)
+
+        L = lib()
+        ws = max(L.sb_w8a16_per_channel_workspace_size(rows, nqkv, cfg.hidden),
+                 L.sb_w8a16_per_channel_workspace_size(rows, cfg.hidden, hq * d),
+                 L.sb_affine_linear_workspace_size(rows, self.inter, cfg.hidden, cfg.mlp_group, 4),
+                 L.sb_affine_linear_workspace_size(rows, cfg.hidden, self.inter, cfg.mlp_group, 4))
+        self._pf = dict(rows=rows, x=buf(rows, cfg.hidden), xn=buf(rows, cfg.hidden), qkv=buf(rows, nqkv),
+                        q=buf(rows, hq * d), attn=buf(rows, hq * d), o=buf(rows, cfg.hidden),
+                        g=buf(rows, self.inter), u=buf(rows, self.inter), act=buf(rows, self.inter),
+                        ws=torch.zeros(max(ws, 256), dtype=torch.uint8, device=dev))
+        return self._pf
+
+    def _prefill_chunked(self, prompt, chunk):
+        cfg, b = self.cfg, self.batch
+        d, hq, hkv, cap = cfg.head_dim, self.hq, self.hkv, self.capacity
+        total = prompt.shape[1]
+        if total < 1 or total > cap:
+            raise ValueError(f"prompt length {total} must be in [1, capacity {cap}]")
+        if chunk < 1:
+            raise ValueError("chunk must be positive")
+        L = lib()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        nqkv = (hq + 2 * hkv) * d
+        hidden, inter, group = cfg.hidden, self.inter, cfg.mlp_group
+        scale = 1.0 / math.sqrt(d)
+        t = self._prefill_buffers(b * min(chunk, total))
+        ws, wsb = t["ws"].data_ptr(), t["ws"].numel()
+        self.reset(prompt[:, 0])
+        for c0 in range(0, total, chunk):
+            lc = min(chunk, total - c0)
+            m = b * lc
+            ids = prompt[:, c0:c0 + lc].reshape(-1).contiguous()
+            pos = torch.arange(c0, c0 + lc, device=self.device, dtype=torch.int32).repeat(b)
+            x, xn, qkv, q, attn, o = (t[k][:m] for k in ("x", "xn", "qkv", "q", "attn", "o"))
+            g, u, act = (t[k][:m] for k in ("g", "u", "act"))
+            check(L.sb_embed_rows(_ptr(self.embed), _ptr(ids), _ptr(x), m, hidden, cfg.vocab, stream), "embed")
+            for li, layer in enumerate(self.layers):
+                kc, ks, vc, vs = self.k_cache[li], self.k_scale[li], self.v_cache[li], self.v_scale[li]
+                check(L.sb_rms_norm(_ptr(x), _ptr(layer["in_norm"]), _ptr(xn), BF16, m, hidden, cfg.rms_eps, stream),
+                      "rms_norm")
+                check(L.sb_w8a16_per_channel(_ptr(xn), BF16, _ptr(layer["qkv_w"]), _ptr(layer["qkv_s"]), _ptr(qkv),
+                                             m, nqkv, hidden, ws, wsb, stream), "qkv")
+                check(L.sb_rope_kv_append(_ptr(qkv), nqkv, _ptr(pos), _ptr(q), _ptr(kc), _ptr(ks), _ptr(vc),
+                                          _ptr(vs), b, lc, hq, hkv, d, cap, d, cfg.rope_theta, stream), "rope")
+                check(L.sb_int8_sdpa_prefill(_ptr(q), _ptr(kc), _ptr(ks), _ptr(vc), _ptr(vs), _ptr(attn), b, hq, hkv,
+                                             lc, c0 + lc, cap, d, scale, 1, 1, stream), "prefill attention")
+                check(L.sb_w8a16_per_channel(_ptr(attn), BF16, _ptr(layer["o_w"]), _ptr(layer["o_s"]), _ptr(o), m,
+                                             hidden, hq * d, ws, wsb, stream), "o_proj")
+                check(L.sb_residual_add(_ptr(x), _ptr(o), m * hidden, stream), "residual")
+                check(L.sb_rms_norm(_ptr(x), _ptr(layer["post_norm"]), _ptr(xn), BF16, m, hidden, cfg.rms_eps,
+                                    stream), "rms_norm")
+                for (w, sc, bi), out in ((layer["gate"], g), (layer["up"], u)):
+                    check(L.sb_affine_linear(_ptr(xn), BF16, _ptr(w), _ptr(sc), _ptr(bi), _ptr(out), m, inter, hidden,
+                                             group, 4, ws, wsb, stream), "gate/up")
+                check(L.sb_swiglu(_ptr(g), _ptr(u), _ptr(act), m * inter, stream), "swiglu")
+                dw, ds, db = layer["down"]
+                check(L.sb_affine_linear(_ptr(act), BF16, _ptr(dw), _ptr(ds), _ptr(db), _ptr(o), m, hidden, inter,
+                                         group, 4, ws, wsb, stream), "down")
+                check(L.sb_residual_add(_ptr(x), _ptr(o), m * hidden, stream), "residual")
+            if c0 + lc == total:
+                self.x.copy_(x.view(b, lc, hidden)[:, lc - 1])
+        self.positions.fill_(total)
+        check(L.sb_linear_ex(ctypes.byref(self.head_desc), stream), "lm_head")
+        check(L.sb_decode_advance(_ptr(self.keys), _ptr(self.tokens), _ptr(self.positions), b, 0, stream), "advance")
 
     def capture(self):
         """Capture one decode step (lm_head, argmax and position advance included)."""

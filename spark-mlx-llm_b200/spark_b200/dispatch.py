@@ -242,9 +242,11 @@ def dispatch_qkv(x, projection, rope, *, q_size, kv_size, n_heads, n_kv_heads, h
 def dispatch_sdpa(queries, keys, values, *, cache, scale, mask, config=None, is_sliding=False):
     """Decode attention over a quantized KV cache (ops/sdpa.py:39-78).
 
-    * INT8 pair ``(codes [B,KH,N,D] int8, scales [B,KH,N] fp16)``, one query
-      token (``L == 1``, the last position attends to all N keys): the B200
-      INT8-KV kernel.
+    * INT8 pair ``(codes [B,KH,N,D] int8, scales [B,KH,N] fp16)``: one query
+      token (``L == 1``, the last position attends to all N keys) runs the
+      B200 INT8-KV decode kernel; ``L > 1`` queries (the last L of the N
+      positions) run the INT8-KV prefill kernel, with the bottom-right causal
+      mask for ``mask="causal"``.
     * Affine tuple ``(packed, scales, biases)`` with ``cache.bits`` /
       ``cache.group_size``: ``int8_quantized_sdpa`` (decode or causal prefill).
     """
@@ -252,10 +254,13 @@ def dispatch_sdpa(queries, keys, values, *, cache, scale, mask, config=None, is_
     if not isinstance(config, SDPAConfig):
         raise TypeError("config must be an SDPAConfig")
     if isinstance(keys, (tuple, list)) and len(keys) == 2 and len(values) == 2:
-        if queries.shape[2] != 1 or mask not in (None, "causal"):
-            raise ValueError("the INT8 KV pair path serves single-token decode with no mask or 'causal'")
+        if mask not in (None, "causal"):
+            raise ValueError("the INT8 KV pair path takes no mask or 'causal'")
         n = keys[0].shape[2]
-        return ops.int8_sdpa_decode(queries, keys[0], keys[1], values[0], values[1], n, float(scale))
+        if queries.shape[2] == 1:
+            return ops.int8_sdpa_decode(queries, keys[0], keys[1], values[0], values[1], n, float(scale))
+        return ops.int8_sdpa_prefill(queries, keys[0], keys[1], values[0], values[1], n, float(scale),
+                                     mask == "causal")
     if isinstance(keys, (tuple, list)) and len(keys) == 3 and len(values) == 3:
         return ext.int8_quantized_sdpa(queries, keys, values, scale=scale,
                                        group_size=getattr(cache, "group_size", 32), bits=getattr(cache, "bits", 8),

@@ -21,6 +21,7 @@ __all__ = [
     "w8a8_linear",
     "qkv_rope",
     "int8_sdpa_decode",
+    "int8_sdpa_prefill",
     "rms_norm",
     "workspace",
 ]
@@ -296,6 +297,41 @@ def int8_sdpa_decode(q: torch.Tensor, k: torch.Tensor, k_scale: torch.Tensor, v:
 
 @int8_sdpa_decode.register_fake
 def _(q, k, k_scale, v, v_scale, length, scale):
+    return torch.empty_like(q)
+
+
+@torch.library.custom_op("spark_b200::int8_sdpa_prefill", mutates_args=())
+def int8_sdpa_prefill(q: torch.Tensor, k: torch.Tensor, k_scale: torch.Tensor, v: torch.Tensor,
+                      v_scale: torch.Tensor, length: int, scale: float, causal: bool) -> torch.Tensor:
+    """Multi-query attention over INT8 K/V with fp16 per-token/per-head scales
+    (the prefill route of int8_quantized_sdpa, int8_quantized_sdpa_prefill.py:44-57,
+    for the BASELINE KV format). ``q[B,H,L,D]`` bf16 holds the last L of
+    ``length`` positions; ``k/v[B,KH,capacity,D]`` int8, scales ``[B,KH,capacity]``
+    fp16. ``causal``: query l sees keys ``[0, length - L + l]`` (bottom-right),
+    else all ``length`` keys."""
+    _require_cuda(q, k, k_scale, v, v_scale)
+    if q.ndim != 4 or q.dtype != torch.bfloat16:
+        raise ValueError("q must be bfloat16 [B, H, L, D]")
+    if k.dtype != torch.int8 or v.dtype != torch.int8 or k.shape != v.shape or k.ndim != 4:
+        raise ValueError("k and v must be int8 [B, KH, capacity, D] of equal shape")
+    if k_scale.dtype != torch.float16 or v_scale.dtype != torch.float16 or k_scale.shape != k.shape[:3]:
+        raise ValueError("k_scale and v_scale must be float16 [B, KH, capacity]")
+    bsz, heads, q_len, dim = q.shape
+    kv_heads, capacity = k.shape[1], k.shape[2]
+    out = torch.empty_like(q)
+    qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+    ksc, vsc = k_scale.contiguous(), v_scale.contiguous()
+    check(
+        lib().sb_int8_sdpa_prefill(qc.data_ptr(), kc.data_ptr(), ksc.data_ptr(), vc.data_ptr(), vsc.data_ptr(),
+                                   out.data_ptr(), bsz, heads, kv_heads, q_len, length, capacity, dim, float(scale),
+                                   int(bool(causal)), 0, _stream(q)),
+        "int8_quantized_sdpa",
+    )
+    return out
+
+
+@int8_sdpa_prefill.register_fake
+def _(q, k, k_scale, v, v_scale, length, scale, causal):
     return torch.empty_like(q)
 
 
