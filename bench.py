@@ -532,6 +532,29 @@ def measure_ops(dev, peak_gbs, peak_tflops, peak_kind):
         rec(f"cfg3_int8_sdpa_b{bsz}_32k", cache + bsz * 32 * 128 * 4, us, 4.0 * bsz * 32 * ctx * 128,
             bound="hbm", batch=bsz, context=ctx, l2_copies=len(copies))
         del copies
+    # ---- INT8-KV prefill attention (chunked prompt): 32/8 heads x 128, causal over the int8 cache
+    for q_len, length in ((1024, 1024), (512, 4096)):
+        cap = length
+        kc = torch.randint(-127, 128, (1, 8, cap, 128), generator=g, device=dev, dtype=torch.int8)
+        vc = torch.randint(-127, 128, (1, 8, cap, 128), generator=g, device=dev, dtype=torch.int8)
+        ks = (torch.rand(1, 8, cap, generator=g, device=dev) * 0.02 + 0.005).half()
+        vs = (torch.rand(1, 8, cap, generator=g, device=dev) * 0.02 + 0.005).half()
+        qv = torch.randn(1, 32, q_len, 128, generator=g, device=dev).bfloat16()
+        o = torch.empty_like(qv)
+
+        def launch(c, st, qv=qv, o=o, q_len=q_len, length=length, cap=cap):
+            kc, ks, vc, vs = c
+            check(L.sb_int8_sdpa_prefill(qv.data_ptr(), kc.data_ptr(), ks.data_ptr(), vc.data_ptr(), vs.data_ptr(),
+                                         o.data_ptr(), 1, 32, 8, q_len, length, cap, 128, 128 ** -0.5, 1, 0, st),
+                  "int8 prefill")
+
+        us = _graph_us(dev, launch, [(kc, ks, vc, vs)])
+        first = length - q_len  # keys seen by query l: first + l + 1
+        pairs = q_len * first + q_len * (q_len + 1) // 2
+        rec(f"prefill_int8_attn_{q_len}x{length}", 8 * length * 260 + 2 * 32 * q_len * 128 * 2, us,
+            4.0 * 32 * 128 * pairs, bound="tensor", q_len=q_len, length=length, causal=True,
+            kernel="mma.sync m16n8k16 flash attention over int8 K/V (fp16 operands)")
+        del kc, vc, ks, vs
     torch.cuda.synchronize(dev)
     out["_method"] = (f"CUDA-graph replays, device time per launch from CUDA events; inputs rotate over buffer sets "
                       f"> 2 x L2 (252 MB); frac against {peak_kind} HBM {peak_gbs:.1f} GB/s or bf16 "
@@ -575,7 +598,25 @@ def main():
     args.engine_used = dec.engine
     gen = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (args.batch, args.prompt), generator=gen, dtype=torch.int32)
-    dec.prefill(prompt.to(device))
+    prefill = None
+    if world == 1:
+        # the chunked prompt path (tensor-core linears + INT8-KV prefill attention): one untimed
+        # call, then one timed with CUDA events
+        dec.prefill(prompt.to(device))
+        torch.cuda.synchronize(device)
+        pe0, pe1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        pe0.record()
+        dec.prefill(prompt.to(device))
+        pe1.record()
+        torch.cuda.synchronize(device)
+        pms = pe0.elapsed_time(pe1)
+        prefill = {"tokens_per_s": args.batch * args.prompt / (pms * 1e-3), "ms": pms, "batch": args.batch,
+                   "prompt_tokens": args.prompt, "chunk": dec_mod.PREFILL_CHUNK,
+                   "path": "chunked: tcgen05 linears at M = batch x chunk, RoPE + INT8 cache append, "
+                           "INT8-KV prefill attention"}
+    # the decode state after the prompt comes from single-token steps at every N, so that the token
+    # digests of different tensor-parallel degrees start from the same cache
+    dec.prefill_stepwise(prompt.to(device))
     dec.capture()
     # greedy tokens from the state after the prompt, hashed: identical digests
     # across --gpus N mean the tensor-parallel runs generate the TP1 tokens
@@ -698,6 +739,8 @@ def main():
             "tokens_head": digest_tokens[0, :16].tolist(),
             "ops": ops,
         }
+        if prefill is not None:
+            out["prefill"] = prefill
         print(json.dumps(out), flush=True)
     if world > 1:
         del dec.graph

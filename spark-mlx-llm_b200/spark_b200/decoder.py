@@ -122,9 +122,14 @@ class SyntheticDecoder:
         self._alloc_state()
         self.graph = None
         # "step": the whole decode step is one persistent kernel (batch 1, one
-        # rank, spark_b200_step.h); "launches": one fused kernel per operator
+        # rank, head_dim 128; spark_b200_step.h); "launches": one fused kernel
+        # per operator with programmatic dependent launch. "auto" takes the
+        # launch sequence, measured the faster of the two at the 4B shape
+        # (1.80 vs 1.86 ms per batch-1 step on B200)
         if engine == "auto":
-            engine = "step" if (batch == 1 and world == 1 and cfg.head_dim == 128) else "launches"
+            engine = "launches"
+        if engine == "step" and not (batch == 1 and world == 1 and cfg.head_dim == 128):
+            raise ValueError("the decode-step kernel serves batch 1 on one GPU with head_dim 128")
         self.engine = engine
         self.stepper = None
         if engine == "step":
@@ -328,8 +333,23 @@ class SyntheticDecoder:
 
         dist.all_reduce(t, op=op or dist.ReduceOp.SUM, group=self.group)
 
-    def step(self, *, lm_head=True, advance=True):
-        """Enqueue one decode step on the current stream (token in ``tokens``)."""
+    def residual(self):
+        """The residual stream after the last step's layers, [batch, hidden] bf16 (device)."""
+        return self.stepper.x.view(1, -1) if self.engine == "step" else self.x
+
+    def run_layers(self, n):
+        """Enqueue the embedding and the first ``n`` layers of a step on the current
+        stream (no lm_head, no cache-position advance); ``residual()`` then holds
+        layer n's output. Used to compare layer outputs with the oracle."""
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if self.engine == "step":
+            self.stepper.run_layers(n, stream)
+            return
+        self.step(lm_head=False, advance=False, layers=n)
+
+    def step(self, *, lm_head=True, advance=True, layers=None):
+        """Enqueue one decode step on the current stream (token in ``tokens``);
+        ``layers`` (launch engine) stops after that many layers."""
         cfg, b = self.cfg, self.batch
         L = lib()
         stream = torch.cuda.current_stream(self.device).cuda_stream
@@ -345,7 +365,7 @@ class SyntheticDecoder:
         check(L.sb_embed_rows(_ptr(self.embed), _ptr(self.tokens), _ptr(self.x), b, cfg.hidden, cfg.vocab, stream),
               "embed")
         scale = 1.0 / math.sqrt(d)
-        for li, (qkv, o, gateup, down) in enumerate(self.descs):
+        for li, (qkv, o, gateup, down) in enumerate(self.descs[:layers]):
             check(L.sb_linear_ex(ctypes.byref(qkv), stream), "qkv_rope")
             if not self.fused_append:
                 check(L.sb_kv_append_int8(_ptr(self.k_new), _ptr(self.v_new), _ptr(self.k_cache[li]),
