@@ -212,6 +212,25 @@ int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* k_scale, co
                          int head_dim, float scale, int causal, int layout, void* stream);
 
 /*
+ * BF16 multi-query attention (speculative verification, sliding-window layers).
+ * Replaces bf16_sdpa_multiquery (spark_mlx_ext/bf16_sdpa_multiquery.py:155-189)
+ * and the BF16 scaled_dot_product_attention it falls back to:
+ *   q    [B, H, q_len, D] BF16 (layout 0) or [B, q_len, H, D] (layout 1)
+ *   k, v [B, KH, capacity, D] BF16; out: the layout of q, BF16
+ * The queries are the last q_len of `length` positions. Masks combine: causal
+ * != 0 - bottom-right causal (query l sees keys [0, length - q_len + l]);
+ * window > 0 (with causal) - also only the last `window` keys up to the query's
+ * position; mask != NULL - bytes [q_len, mask_ld] (nonzero = visible, shared by
+ * every batch row and head). Scores, softmax and accumulation in fp32; the
+ * probabilities enter P.V as a bf16 hi + lo pair. A query with no visible key
+ * gets zeros. D = 128, H/KH in {1, 2, 4, 8}, 16-byte aligned K/V. No workspace.
+ */
+int sb_bf16_sdpa_multiquery(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                            int num_heads, int num_kv_heads, int64_t q_len, int64_t length,
+                            int64_t capacity, int head_dim, float scale, int causal, int window,
+                            const uint8_t* mask, int64_t mask_ld, int layout, void* stream);
+
+/*
  * Attention over MLX affine-quantized KV tuples: the int8_quantized_sdpa input
  * format (spark_mlx_ext/int8_quantized_sdpa.py:156-287, staged recipe
  * _fallback :122-153). Replaces int8_quantized_sdpa for its affine tuples.

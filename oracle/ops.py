@@ -165,6 +165,38 @@ def _attend(q, k, v, scale, causal):
     return np.einsum("bhln,bhnd->bhld", p, v)
 
 
+def sdpa_masked(q, k, v, scale, causal=False, window=0, mask=None):
+    """Softmax attention in float64 with the masks of ``mx.fast.scaled_dot_product_attention``
+    as ``bf16_sdpa_multiquery`` uses them (``bf16_sdpa_multiquery.py:155-189``):
+    bottom-right causal, a sliding window of the last ``window`` keys up to the
+    query's position, and a boolean ``mask[L, N]`` (True = visible). A query
+    with no visible key returns zeros. ``q[B,H,L,D]``, ``k/v[B,KH,N,D]``."""
+    q = np.asarray(q, np.float64)
+    k = np.asarray(k, np.float64)
+    v = np.asarray(v, np.float64)
+    bsz, heads, length, dim = q.shape
+    kv_heads, n = k.shape[1], k.shape[2]
+    rep = heads // kv_heads
+    k = np.repeat(k, rep, axis=1)
+    v = np.repeat(v, rep, axis=1)
+    scores = np.einsum("bhld,bhnd->bhln", q * scale, k)
+    pos = np.arange(n - length, n)[:, None]
+    keys = np.arange(n)[None, :]
+    visible = np.ones((length, n), bool)
+    if causal:
+        visible &= keys <= pos
+    if window > 0:
+        visible &= keys > pos - window
+    if mask is not None:
+        visible &= np.asarray(mask, bool)
+    scores = np.where(visible, scores, -np.inf)
+    m = scores.max(axis=-1, keepdims=True)
+    m = np.where(np.isfinite(m), m, 0.0)
+    p = np.exp(scores - m)
+    s = p.sum(axis=-1, keepdims=True)
+    return np.einsum("bhln,bhnd->bhld", p / np.where(s > 0, s, 1.0), v)
+
+
 def sdpa_int8(q, k_int8, k_scale, v_int8, v_scale, scale, causal=False):
     """INT8-KV attention (symmetric per token per head, fp16 scales).
 

@@ -34,26 +34,31 @@ constexpr int kRows = 64;        // query rows per CTA
 constexpr int kKeys = 64;        // keys per tile
 constexpr int kWarps = 4;        // 16 query rows each
 constexpr int kThreads = kWarps * 32;
-constexpr int kHStride = kD * 2 + 16;                // fp16 tile row stride (bytes): ldmatrix without bank conflicts
-constexpr int kHTile = kKeys * kHStride;             // one fp16 tile (K or V)
+constexpr int kHStride = kD * 2 + 16;                // 16-bit tile row stride (bytes): ldmatrix without bank conflicts
+constexpr int kHTile = kKeys * kHStride;             // one 16-bit tile (K or V)
 constexpr int kRawTile = kKeys * kD;                 // one int8 tile (K or V)
+// INT8 KV: [K | V] 16-bit code tiles, [2 buffers][K | V] int8 tiles, the tile's K and V scales (fp32)
 constexpr int kOffKh = 0;
 constexpr int kOffVh = kHTile;
-constexpr int kOffRaw = 2 * kHTile;                  // [2 buffers][K | V] int8
-constexpr int kOffScale = kOffRaw + 2 * 2 * kRawTile;  // float K scales [64], V scales [64]
-constexpr int kSmem = kOffScale + 2 * kKeys * 4;
+constexpr int kOffRaw = 2 * kHTile;
+constexpr int kOffScale = kOffRaw + 2 * 2 * kRawTile;
+constexpr int kSmemI8 = kOffScale + 2 * kKeys * 4;
+// bf16 KV: [2 buffers][K | V] bf16 tiles, loaded straight into the padded layout
+constexpr int kSmemBf = 2 * 2 * kHTile;
 
 struct Params {
   const __nv_bfloat16* q;
-  const int8_t* k;
+  const void* k;  // int8 codes or bf16 values [B, KH, cap, D]
   const __half* ks;
-  const int8_t* v;
+  const void* v;
   const __half* vs;
   __nv_bfloat16* out;
+  const uint8_t* mask;  // optional [q_len, mask_ld] bytes, nonzero = visible (broadcast over batch and heads)
+  int mask_ld;
   int heads, kv_heads, q_len, length, capacity;
-  int causal, layout;  // layout 0: q/out [B, H, L, D]; 1: [B, L, H, D]
-  float scale_log2;    // softmax scale * log2(e)
-  int tiles;           // query tiles per (batch, kv head)
+  int causal, window, layout;  // window > 0: keys (pos - window, pos] (with causal); layout 0: [B, H, L, D], 1: [B, L, H, D]
+  float scale_log2;            // softmax scale * log2(e)
+  int tiles;                   // query tiles per (batch, kv head)
 };
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -90,7 +95,9 @@ __device__ __forceinline__ void codes_to_half(uint32_t w, uint32_t& lo, uint32_t
   hi = *reinterpret_cast<const uint32_t*>(&hb);
 }
 
-template <int G>
+// KVB: bf16 K/V (no scales; bf16 operands, probabilities as a bf16 hi + lo pair for P.V);
+// else INT8 codes + fp16 scales (fp16 code tiles, probabilities times the V scale in fp16).
+template <int G, bool KVB>
 __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
@@ -101,12 +108,14 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
   const int row0 = tile * kRows;
   const int qoff = p.length - p.q_len;  // position of query l is qoff + l (bottom-right)
   const int last_row = min(row0 + kRows, nrows) - 1;
-  // keys this CTA reads: [0, kend)
+  // keys this CTA reads: [kbeg, kend)
   const int kend = p.causal ? min(p.length, qoff + last_row / G + 1) : p.length;
+  const int kbeg = p.window > 0 ? max(0, qoff + row0 / G - p.window + 1) : 0;
+  const int kt0 = kbeg / kKeys;
   const int ntiles = (kend + kKeys - 1) / kKeys;
   const size_t head_base = (static_cast<size_t>(b) * p.kv_heads + kvh) * p.capacity;
-  const int8_t* kbase = p.k + head_base * kD;
-  const int8_t* vbase = p.v + head_base * kD;
+  const uint8_t* kbase = static_cast<const uint8_t*>(p.k) + head_base * kD * (KVB ? 2 : 1);
+  const uint8_t* vbase = static_cast<const uint8_t*>(p.v) + head_base * kD * (KVB ? 2 : 1);
   float* sks = reinterpret_cast<float*>(sm + kOffScale);
   float* svs = sks + kKeys;
 
@@ -118,30 +127,50 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
     return p.layout == 0 ? ((static_cast<size_t>(b) * p.heads + head) * p.q_len + l) * kD
                          : ((static_cast<size_t>(b) * p.q_len + l) * p.heads + head) * kD;
   };
-  const int pos_a = qoff + ra / G, pos_b = qoff + rb / G;
+  const int la = ra / G, lb = rb / G;
+  const int pos_a = qoff + la, pos_b = qoff + lb;
   const int kend_a = p.causal ? min(p.length, pos_a + 1) : p.length;
   const int kend_b = p.causal ? min(p.length, pos_b + 1) : p.length;
+  const int kbeg_a = p.window > 0 ? pos_a - p.window + 1 : 0;
+  const int kbeg_b = p.window > 0 ? pos_b - p.window + 1 : 0;
+  const uint8_t* mrow_a = (p.mask && la < p.q_len) ? p.mask + static_cast<size_t>(la) * p.mask_ld : nullptr;
+  const uint8_t* mrow_b = (p.mask && lb < p.q_len) ? p.mask + static_cast<size_t>(lb) * p.mask_ld : nullptr;
   const int warp_last = qoff + min(wr0 + 15, nrows - 1) / G;  // latest position among the warp's rows
+  const int warp_first = qoff + wr0 / G;
   const bool warp_live = wr0 < nrows;
 
   grid_dependency_wait();
 
   auto load_tile = [&](int kt, int buf) {
-    int8_t* rk = reinterpret_cast<int8_t*>(sm + kOffRaw + buf * 2 * kRawTile);
     const int key0 = kt * kKeys;
-    for (int i = tid; i < 2 * kKeys * (kD / 16); i += kThreads) {
-      const int mat = i / (kKeys * (kD / 16)), rem = i % (kKeys * (kD / 16));
-      const int key = rem / (kD / 16), ch = rem % (kD / 16);
-      int8_t* dst = rk + mat * kRawTile + key * kD + ch * 16;
-      if (key0 + key < kend)
-        cp_async16(dst, (mat ? vbase : kbase) + static_cast<size_t>(key0 + key) * kD + ch * 16);
-      else
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+    if constexpr (KVB) {
+      uint8_t* dst0 = sm + buf * 2 * kHTile;
+      for (int i = tid; i < 2 * kKeys * (kD * 2 / 16); i += kThreads) {
+        const int mat = i / (kKeys * (kD * 2 / 16)), rem = i % (kKeys * (kD * 2 / 16));
+        const int key = rem / (kD * 2 / 16), ch = rem % (kD * 2 / 16);
+        uint8_t* dst = dst0 + mat * kHTile + key * kHStride + ch * 16;
+        if (key0 + key < kend && key0 + key >= kbeg)
+          cp_async16(dst, (mat ? vbase : kbase) + static_cast<size_t>(key0 + key) * kD * 2 + ch * 16);
+        else
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
+    } else {
+      int8_t* rk = reinterpret_cast<int8_t*>(sm + kOffRaw + buf * 2 * kRawTile);
+      for (int i = tid; i < 2 * kKeys * (kD / 16); i += kThreads) {
+        const int mat = i / (kKeys * (kD / 16)), rem = i % (kKeys * (kD / 16));
+        const int key = rem / (kD / 16), ch = rem % (kD / 16);
+        int8_t* dst = rk + mat * kRawTile + key * kD + ch * 16;
+        if (key0 + key < kend && key0 + key >= kbeg)
+          cp_async16(dst, (mat ? vbase : kbase) + static_cast<size_t>(key0 + key) * kD + ch * 16);
+        else
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+      }
     }
     cp_async_commit_group();
   };
 
-  // q rows of the warp as fp16 A fragments (rows beyond the query count are zero)
+  // q rows of the warp as A fragments (fp16 for INT8 KV, bf16 as stored for bf16 KV;
+  // rows beyond the query count are zero)
   uint32_t qa[8][4];
   {
     const __nv_bfloat16* qra = ra < nrows ? p.q + qkv_offset(ra) : nullptr;
@@ -153,25 +182,28 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
         const int d = ks * 16 + h * 8 + 2 * c;
         const uint32_t wa = qra ? *reinterpret_cast<const uint32_t*>(qra + d) : 0u;
         const uint32_t wb = qrb ? *reinterpret_cast<const uint32_t*>(qrb + d) : 0u;
-        qa[ks][2 * h] = pack_half2(bf16_lo(wa), bf16_hi(wa));
-        qa[ks][2 * h + 1] = pack_half2(bf16_lo(wb), bf16_hi(wb));
+        qa[ks][2 * h] = KVB ? wa : pack_half2(bf16_lo(wa), bf16_hi(wa));
+        qa[ks][2 * h + 1] = KVB ? wb : pack_half2(bf16_lo(wb), bf16_hi(wb));
       }
   }
   float o[16][4];
 #pragma unroll
   for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  const uint32_t kh_base = smem_u32(sm + kOffKh), vh_base = smem_u32(sm + kOffVh);
 
-  if (ntiles > 0) load_tile(0, 0);
-  for (int kt = 0; kt < ntiles; ++kt) {
+  if (kt0 < ntiles) load_tile(kt0, kt0 & 1);
+  for (int kt = kt0; kt < ntiles; ++kt) {
     const int key0 = kt * kKeys;
     if (kt + 1 < ntiles) load_tile(kt + 1, (kt + 1) & 1);
     else cp_async_commit_group();  // an empty group keeps the wait count uniform
     cp_async_wait_group<1>();
     __syncthreads();
-    // ---- int8 tile -> fp16 codes (exact), and the tile's scales
-    {
+    uint32_t kh_base, vh_base;
+    if constexpr (KVB) {
+      kh_base = smem_u32(sm + (kt & 1) * 2 * kHTile);
+      vh_base = kh_base + kHTile;
+    } else {
+      // ---- int8 tile -> fp16 codes (exact), and the tile's scales
       const int8_t* rk = reinterpret_cast<const int8_t*>(sm + kOffRaw + (kt & 1) * 2 * kRawTile);
       for (int i = tid; i < 2 * kKeys * (kD / 16); i += kThreads) {
         const int mat = i / (kKeys * (kD / 16)), rem = i % (kKeys * (kD / 16));
@@ -189,12 +221,14 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
       if (tid < 2 * kKeys) {
         const int key = key0 + (tid & (kKeys - 1));
         const __half* src = tid < kKeys ? p.ks : p.vs;
-        const float sc = key < kend ? __half2float(src[head_base + key]) : 0.f;
+        const float sc = (key < kend && key >= kbeg) ? __half2float(src[head_base + key]) : 0.f;
         (tid < kKeys ? sks : svs)[tid & (kKeys - 1)] = sc;
       }
+      __syncthreads();
+      kh_base = smem_u32(sm + kOffKh);
+      vh_base = smem_u32(sm + kOffVh);
     }
-    __syncthreads();
-    if (warp_live && key0 <= warp_last) {
+    if (warp_live && key0 <= warp_last && (p.window <= 0 || key0 + kKeys > warp_first - p.window + 1)) {
       // ---- scores S = q . K^T for the warp's 16 rows x 64 keys
       float s[8][4];
 #pragma unroll
@@ -205,8 +239,8 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
         for (int nt = 0; nt < 8; ++nt) {
           uint32_t bk[4];
           ldsm_x4(bk, kh_base + (nt * 8 + (lane & 7)) * kHStride + (ks2 * 32 + (lane >> 3) * 8) * 2);
-          mma_16816<true>(s[nt], qa[2 * ks2], bk[0], bk[1]);
-          mma_16816<true>(s[nt], qa[2 * ks2 + 1], bk[2], bk[3]);
+          mma_16816<!KVB>(s[nt], qa[2 * ks2], bk[0], bk[1]);
+          mma_16816<!KVB>(s[nt], qa[2 * ks2 + 1], bk[2], bk[3]);
         }
       // ---- scale, mask, online softmax (log2 domain)
       float mx[2] = {m_run[0], m_run[1]};
@@ -216,8 +250,11 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
         for (int e = 0; e < 4; ++e) {
           const int kk = nt * 8 + 2 * c + (e & 1);
           const int key = key0 + kk;
-          const bool ok = key < ((e < 2) ? kend_a : kend_b);
-          const float v = s[nt][e] * sks[kk] * p.scale_log2;
+          const bool row_a = e < 2;
+          const uint8_t* mrow = row_a ? mrow_a : mrow_b;
+          const bool ok = key < (row_a ? kend_a : kend_b) && key >= (row_a ? kbeg_a : kbeg_b) &&
+                          (mrow == nullptr || mrow[key] != 0);
+          const float v = KVB ? s[nt][e] * p.scale_log2 : s[nt][e] * sks[kk] * p.scale_log2;
           s[nt][e] = ok ? v : -INFINITY;
           mx[e >> 1] = fmaxf(mx[e >> 1], s[nt][e]);
         }
@@ -237,8 +274,8 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
         o[n][2] *= corr[1];
         o[n][3] *= corr[1];
       }
-      // probabilities; P' = P * V scale rounded to fp16 as the A operand of P.V
-      uint32_t pa[4][4];
+      // probabilities as the A operand of P.V
+      uint32_t pa[4][4], pl[4][4];
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         float pr[4];
@@ -247,12 +284,23 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
           const float mrow = m_run[e >> 1];
           const float pe = s[nt][e] == -INFINITY ? 0.f : exp2f(s[nt][e] - mrow);
           l_run[e >> 1] += pe;
-          pr[e] = pe * svs[nt * 8 + 2 * c + (e & 1)];
+          pr[e] = KVB ? pe : pe * svs[nt * 8 + 2 * c + (e & 1)];
         }
-        pa[nt >> 1][(nt & 1) * 2] = pack_half2(pr[0], pr[1]);
-        pa[nt >> 1][(nt & 1) * 2 + 1] = pack_half2(pr[2], pr[3]);
+        if constexpr (KVB) {
+          // P = hi + lo in bf16 (about 16 significant bits)
+          const __nv_bfloat162 h01 = __floats2bfloat162_rn(pr[0], pr[1]), h23 = __floats2bfloat162_rn(pr[2], pr[3]);
+          const __nv_bfloat162 l01 = __floats2bfloat162_rn(pr[0] - __low2float(h01), pr[1] - __high2float(h01));
+          const __nv_bfloat162 l23 = __floats2bfloat162_rn(pr[2] - __low2float(h23), pr[3] - __high2float(h23));
+          pa[nt >> 1][(nt & 1) * 2] = *reinterpret_cast<const uint32_t*>(&h01);
+          pa[nt >> 1][(nt & 1) * 2 + 1] = *reinterpret_cast<const uint32_t*>(&h23);
+          pl[nt >> 1][(nt & 1) * 2] = *reinterpret_cast<const uint32_t*>(&l01);
+          pl[nt >> 1][(nt & 1) * 2 + 1] = *reinterpret_cast<const uint32_t*>(&l23);
+        } else {
+          pa[nt >> 1][(nt & 1) * 2] = pack_half2(pr[0], pr[1]);
+          pa[nt >> 1][(nt & 1) * 2 + 1] = pack_half2(pr[2], pr[3]);
+        }
       }
-      // ---- O += P' . V (V transposed by ldmatrix.trans)
+      // ---- O += P . V (V transposed by ldmatrix.trans)
 #pragma unroll
       for (int j = 0; j < 4; ++j)
 #pragma unroll
@@ -260,14 +308,18 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
           uint32_t bv[4];
           ldsm_x4_trans(bv, vh_base + (j * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kHStride +
                                 (np * 16 + (lane >> 4) * 8) * 2);
-          mma_16816<true>(o[2 * np], pa[j], bv[0], bv[1]);
-          mma_16816<true>(o[2 * np + 1], pa[j], bv[2], bv[3]);
+          mma_16816<!KVB>(o[2 * np], pa[j], bv[0], bv[1]);
+          mma_16816<!KVB>(o[2 * np + 1], pa[j], bv[2], bv[3]);
+          if constexpr (KVB) {
+            mma_16816<false>(o[2 * np], pl[j], bv[0], bv[1]);
+            mma_16816<false>(o[2 * np + 1], pl[j], bv[2], bv[3]);
+          }
         }
     }
-    __syncthreads();  // the fp16 tiles and scales are rewritten by the next tile
+    __syncthreads();  // the tiles and scales are rewritten by the next tile
   }
   cp_async_wait_group<0>();
-  // ---- normalize and store (rows past the query count are not stored)
+  // ---- normalize and store (rows past the query count are not stored; fully masked rows are 0)
 #pragma unroll
   for (int i = 0; i < 2; ++i) {
     l_run[i] += __shfl_xor_sync(0xffffffffu, l_run[i], 1);
@@ -403,26 +455,38 @@ using namespace sb::prefill;
 
 namespace {
 
-template <int G>
+template <int G, bool KVB>
 int launch_prefill(const Params& p, int batch, int kv_heads, cudaStream_t stream) {
+  constexpr int smem = KVB ? kSmemBf : kSmemI8;
   static bool attr_done = false;  // per template instance; the attribute is per function
   if (!attr_done) {
-    const cudaError_t e = cudaFuncSetAttribute(prefill_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
+    const cudaError_t e = cudaFuncSetAttribute(prefill_kernel<G, KVB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return fail(SB_ECUDA, std::string("prefill attention attribute: ") + cudaGetErrorString(e));
     attr_done = true;
   }
-  return launch("int8_sdpa_prefill", prefill_kernel<G>, dim3(p.tiles, kv_heads, batch), dim3(kThreads), kSmem,
-                stream, p);
+  return launch(KVB ? "bf16_sdpa_multiquery" : "int8_sdpa_prefill", prefill_kernel<G, KVB>,
+                dim3(p.tiles, kv_heads, batch), dim3(kThreads), smem, stream, p);
 }
 
-}  // namespace
+template <bool KVB>
+int launch_any(Params& p, int64_t batch, int num_kv_heads, int G, int64_t q_len, cudaStream_t s) {
+  const int64_t tiles = (q_len * G + kRows - 1) / kRows;
+  SB_REQUIRE(tiles <= 0x7fffffff, "too many query rows");
+  p.tiles = static_cast<int>(tiles);
+  switch (G) {
+    case 1: return launch_prefill<1, KVB>(p, static_cast<int>(batch), num_kv_heads, s);
+    case 2: return launch_prefill<2, KVB>(p, static_cast<int>(batch), num_kv_heads, s);
+    case 4: return launch_prefill<4, KVB>(p, static_cast<int>(batch), num_kv_heads, s);
+    default: return launch_prefill<8, KVB>(p, static_cast<int>(batch), num_kv_heads, s);
+  }
+}
 
-extern "C" int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
-                                    const void* v_scale, void* out, int64_t batch, int num_heads, int num_kv_heads,
-                                    int64_t q_len, int64_t length, int64_t capacity, int head_dim, float scale,
-                                    int causal, int layout, void* stream) {
-  SB_REQUIRE(q && k && k_scale && v && v_scale && out, "null pointer");
-  SB_REQUIRE(head_dim == kD, "the prefill attention supports head_dim 128");
+// Checks shared by both entry points; fills the common fields.
+int common_params(Params& p, const void* q, const void* k, const void* v, void* out, int64_t batch, int num_heads,
+                  int num_kv_heads, int64_t q_len, int64_t length, int64_t capacity, int head_dim, float scale,
+                  int causal, int layout) {
+  SB_REQUIRE(q && k && v && out, "null pointer");
+  SB_REQUIRE(head_dim == kD, "head_dim must be 128");
   SB_REQUIRE(batch >= 1 && batch <= 65535, "batch must be in [1, 65535]");
   SB_REQUIRE(num_kv_heads >= 1 && num_kv_heads <= 65535 && num_heads % num_kv_heads == 0, "heads");
   const int G = num_heads / num_kv_heads;
@@ -434,12 +498,10 @@ extern "C" int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* 
              "the K/V caches must be 16-byte aligned");
   SB_REQUIRE(reinterpret_cast<uintptr_t>(q) % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 4 == 0,
              "q and out must be 4-byte aligned");
-  Params p;
+  p = Params{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = k;
-  p.ks = static_cast<const __half*>(k_scale);
   p.v = v;
-  p.vs = static_cast<const __half*>(v_scale);
   p.out = static_cast<__nv_bfloat16*>(out);
   p.heads = num_heads;
   p.kv_heads = num_kv_heads;
@@ -449,16 +511,40 @@ extern "C" int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* 
   p.causal = causal != 0;
   p.layout = layout;
   p.scale_log2 = scale * 1.4426950408889634f;
-  const int64_t tiles = (q_len * G + kRows - 1) / kRows;
-  SB_REQUIRE(tiles <= 0x7fffffff, "too many query rows");
-  p.tiles = static_cast<int>(tiles);
-  cudaStream_t s = as_stream(stream);
-  switch (G) {
-    case 1: return launch_prefill<1>(p, static_cast<int>(batch), num_kv_heads, s);
-    case 2: return launch_prefill<2>(p, static_cast<int>(batch), num_kv_heads, s);
-    case 4: return launch_prefill<4>(p, static_cast<int>(batch), num_kv_heads, s);
-    default: return launch_prefill<8>(p, static_cast<int>(batch), num_kv_heads, s);
-  }
+  return SB_OK;
+}
+
+}  // namespace
+
+extern "C" int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                                    const void* v_scale, void* out, int64_t batch, int num_heads, int num_kv_heads,
+                                    int64_t q_len, int64_t length, int64_t capacity, int head_dim, float scale,
+                                    int causal, int layout, void* stream) {
+  SB_REQUIRE(k_scale && v_scale, "null pointer");
+  Params p;
+  if (int st = common_params(p, q, k, v, out, batch, num_heads, num_kv_heads, q_len, length, capacity, head_dim,
+                             scale, causal, layout))
+    return st;
+  p.ks = static_cast<const __half*>(k_scale);
+  p.vs = static_cast<const __half*>(v_scale);
+  return launch_any<false>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, as_stream(stream));
+}
+
+extern "C" int sb_bf16_sdpa_multiquery(const void* q, const void* k, const void* v, void* out, int64_t batch,
+                                       int num_heads, int num_kv_heads, int64_t q_len, int64_t length,
+                                       int64_t capacity, int head_dim, float scale, int causal, int window,
+                                       const uint8_t* mask, int64_t mask_ld, int layout, void* stream) {
+  Params p;
+  if (int st = common_params(p, q, k, v, out, batch, num_heads, num_kv_heads, q_len, length, capacity, head_dim,
+                             scale, causal, layout))
+    return st;
+  SB_REQUIRE(window >= 0, "window must be >= 0");
+  SB_REQUIRE(window == 0 || causal, "a sliding window applies with the causal mask");
+  SB_REQUIRE(mask == nullptr || (mask_ld >= length && mask_ld <= (1LL << 30)), "mask row stride must be >= length");
+  p.window = window;
+  p.mask = mask;
+  p.mask_ld = static_cast<int>(mask ? mask_ld : 0);
+  return launch_any<true>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, as_stream(stream));
 }
 
 extern "C" int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, void* q_out,

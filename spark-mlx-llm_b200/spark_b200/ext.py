@@ -26,6 +26,7 @@ from ._lib import DTYPE_CODES, check, lib
 
 __all__ = [
     "W8A8Linear",
+    "bf16_sdpa_multiquery",
     "int8_matmul_int32",
     "int8_quantized_sdpa",
     "is_w8a8_available",
@@ -253,6 +254,43 @@ def int8_quantized_sdpa(queries, keys, values, *, scale, group_size=32, bits=8, 
             "int8_quantized_sdpa",
         )
     return out
+
+
+def bf16_sdpa_multiquery(queries, keys, values, *, scale, mask=None, stream=None):
+    """BF16 SDPA for a few queries (speculative verification) and the sliding
+    layers (bf16_sdpa_multiquery.py:155-189): Q ``[B,H,M,D]``, K/V ``[B,KH,N,D]``
+    BF16; ``mask`` None, ``"causal"`` (bottom-right) or a boolean array
+    broadcast to ``[B,Hq,M,N]`` that is the same for every batch row and head
+    (shape ``[M,N]``, ``[1,M,N]`` or ``[1,1,M,N]``). fp32 scores and softmax,
+    BF16 output of Q's first three dimensions."""
+    if not all(isinstance(t, torch.Tensor) for t in (queries, keys, values)):
+        raise TypeError("queries, keys and values must be torch tensors")
+    if queries.ndim != 4 or keys.ndim != 4 or values.shape != keys.shape:
+        raise ValueError("Expected Q[B,H,M,D] and K/V[B,KH,N,D] of equal shape")
+    if any(t.dtype != torch.bfloat16 for t in (queries, keys, values)):
+        raise ValueError("Q, K and V must be bfloat16")
+    batch, heads, m, dim = queries.shape
+    kv_heads, n = keys.shape[1], keys.shape[2]
+    if keys.shape[0] != batch or keys.shape[3] != dim or heads % kv_heads or min(batch, heads, m, n) <= 0:
+        raise ValueError("Incompatible Q/K/V geometry")
+    if not isinstance(scale, (float, int)) or not math.isfinite(scale):
+        raise ValueError("scale must be a finite Python number")
+    causal, bool_mask = False, None
+    if isinstance(mask, str):
+        if mask != "causal":
+            raise ValueError("mask string must be 'causal'")
+        causal = True
+    elif mask is not None:
+        if not isinstance(mask, torch.Tensor) or mask.dtype != torch.bool:
+            raise ValueError("array masks must be boolean")
+        lead = tuple(mask.shape[:-2])
+        if mask.ndim < 2 or tuple(mask.shape[-2:]) != (m, n) or any(d != 1 for d in lead) or len(lead) > 2:
+            raise ValueError("boolean masks must be [M,N] (shared by every batch row and head)")
+        bool_mask = mask.reshape(m, n)
+    if m > n:
+        raise ValueError("more queries than keys")
+    with _on(stream, "bf16_sdpa_multiquery", queries, keys, values):
+        return ops.bf16_sdpa_multiquery(queries, keys, values, float(scale), causal, 0, bool_mask)
 
 
 class W8A8Linear(torch.nn.Module):

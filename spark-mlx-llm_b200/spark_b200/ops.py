@@ -8,6 +8,7 @@ GPU-only primitives (``src/spark_w8a8.cpp:156-158``).
 """
 
 import threading
+from typing import Optional
 
 import torch
 
@@ -22,6 +23,7 @@ __all__ = [
     "qkv_rope",
     "int8_sdpa_decode",
     "int8_sdpa_prefill",
+    "bf16_sdpa_multiquery",
     "rms_norm",
     "workspace",
 ]
@@ -332,6 +334,42 @@ def int8_sdpa_prefill(q: torch.Tensor, k: torch.Tensor, k_scale: torch.Tensor, v
 
 @int8_sdpa_prefill.register_fake
 def _(q, k, k_scale, v, v_scale, length, scale, causal):
+    return torch.empty_like(q)
+
+
+@torch.library.custom_op("spark_b200::bf16_sdpa_multiquery", mutates_args=())
+def bf16_sdpa_multiquery(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal: bool,
+                         window: int, mask: Optional[torch.Tensor]) -> torch.Tensor:
+    """BF16 multi-query attention (bf16_sdpa_multiquery.py:155-189). ``q[B,H,L,D]``
+    holds the last L of N positions, ``k/v[B,KH,N,D]``; ``causal`` is the
+    bottom-right mask, ``window > 0`` also limits each query to its last
+    ``window`` keys, ``mask`` an optional bool/uint8 ``[L, N]`` (True = visible)
+    shared by every batch row and head."""
+    _require_cuda(q, k, v)
+    if q.ndim != 4 or k.ndim != 4 or v.shape != k.shape:
+        raise ValueError("q must be [B, H, L, D], k and v [B, KH, N, D] of equal shape")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise ValueError("q, k and v must be bfloat16")
+    bsz, heads, q_len, dim = q.shape
+    kv_heads, n = k.shape[1], k.shape[2]
+    m = None
+    if mask is not None:
+        if tuple(mask.shape) != (q_len, n) or mask.dtype not in (torch.bool, torch.uint8):
+            raise ValueError("mask must be bool or uint8 [L, N]")
+        m = mask.to(device=q.device, dtype=torch.uint8).contiguous()
+    out = torch.empty_like(q)
+    qc, kc, vc = q.contiguous(), k.contiguous(), v.contiguous()
+    check(
+        lib().sb_bf16_sdpa_multiquery(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), out.data_ptr(), bsz, heads,
+                                      kv_heads, q_len, n, n, dim, float(scale), int(bool(causal)), int(window),
+                                      m.data_ptr() if m is not None else None, n, 0, _stream(q)),
+        "bf16_sdpa_multiquery",
+    )
+    return out
+
+
+@bf16_sdpa_multiquery.register_fake
+def _(q, k, v, scale, causal, window, mask):
     return torch.empty_like(q)
 
 

@@ -178,3 +178,65 @@ def test_chunked_prompt_matches_oracle():
     top2 = np.sort(logits, axis=-1)[0, -2:]
     if top2[1] - top2[0] > 1e-2 * abs(top2[1]) + 1e-3:
         assert int(dec.tokens[0]) == int(orc.greedy(logits)[0])
+
+
+# ------------------------------------------------------------ bf16 multi-query attention
+BF16_CASES = [
+    # batch, heads, kv_heads, q_len, length, causal, window, sliding mask (window of a boolean mask), layout
+    (1, 16, 4, 8, 519, False, 0, 128, 0),  # the reference's verification geometry at D = 128, boolean sliding mask
+    (2, 8, 8, 33, 200, True, 64, 0, 1),
+    (1, 32, 8, 1, 77, False, 0, 0, 0),
+    (1, 8, 1, 70, 300, True, 0, 0, 0),
+]
+
+
+@pytest.mark.parametrize("case", BF16_CASES)
+def test_bf16_multiquery_matches_oracle(case):
+    _need_cuda()
+    from spark_b200._lib import check, lib
+
+    b, h, kh, ql, n, causal, window, mwin, layout = case
+    d = 128
+    gen = torch.Generator().manual_seed(sum(case[:5]))
+    q = torch.randn(b, h, ql, d, generator=gen).to(torch.bfloat16)
+    k = torch.randn(b, kh, n, d, generator=gen).to(torch.bfloat16)
+    v = torch.randn(b, kh, n, d, generator=gen).to(torch.bfloat16)
+    mask = None
+    if mwin:
+        pos = np.arange(n - ql, n)[:, None]
+        keys = np.arange(n)[None, :]
+        mask = (keys <= pos) & (keys > pos - mwin)
+        mask[3] = False  # one query sees nothing: zeros
+    q_dev = (q if layout == 0 else q.permute(0, 2, 1, 3)).contiguous().cuda()
+    out = torch.empty_like(q_dev)
+    m_dev = torch.from_numpy(mask.astype(np.uint8)).cuda() if mask is not None else None
+    scale = 1.0 / math.sqrt(d)
+    k_dev, v_dev = k.cuda(), v.cuda()  # kept alive until the kernel has run
+    check(lib().sb_bf16_sdpa_multiquery(q_dev.data_ptr(), k_dev.data_ptr(), v_dev.data_ptr(), out.data_ptr(),
+                                        b, h, kh, ql, n, n, d, scale, int(causal), window,
+                                        m_dev.data_ptr() if m_dev is not None else None, n, layout,
+                                        torch.cuda.current_stream().cuda_stream), "bf16 multiquery")
+    torch.cuda.synchronize()
+    got = _f32(out if layout == 0 else out.permute(0, 2, 1, 3))
+    ref = oracle_ops.sdpa_masked(_f32(q), _f32(k), _f32(v), scale, causal=causal, window=window, mask=mask)
+    np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
+
+
+def test_ext_bf16_multiquery_masks():
+    _need_cuda()
+    from spark_b200 import ext
+
+    gen = torch.Generator().manual_seed(9)
+    q = torch.randn(1, 8, 8, 128, generator=gen).to(torch.bfloat16).cuda()
+    k = torch.randn(1, 2, 100, 128, generator=gen).to(torch.bfloat16).cuda()
+    v = torch.randn(1, 2, 100, 128, generator=gen).to(torch.bfloat16).cuda()
+    causal = ext.bf16_sdpa_multiquery(q, k, v, scale=0.08, mask="causal")
+    ref = oracle_ops.sdpa_masked(_f32(q), _f32(k), _f32(v), 0.08, causal=True)
+    np.testing.assert_allclose(_f32(causal), ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
+    band = np.zeros((8, 100), bool)
+    band[:, 40:60] = True
+    masked = ext.bf16_sdpa_multiquery(q, k, v, scale=0.08, mask=torch.from_numpy(band)[None, None].cuda())
+    ref = oracle_ops.sdpa_masked(_f32(q), _f32(k), _f32(v), 0.08, mask=band)
+    np.testing.assert_allclose(_f32(masked), ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
+    with pytest.raises(ValueError):
+        ext.bf16_sdpa_multiquery(q, k, v, scale=0.08, mask=torch.ones(2, 8, 100, dtype=torch.bool).cuda())
