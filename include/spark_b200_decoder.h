@@ -34,7 +34,8 @@ extern "C" {
 /* Epilogues of sb_linear_ex. */
 #define SB_EPI_STORE 0  /* y[m, n] = T(acc)                                              */
 #define SB_EPI_RESID 1  /* y[m, n] = T(residual[m, n] + T(acc))                          */
-#define SB_EPI_SWIGLU 2 /* y[m, n] = T(silu(T(gate)) * T(up)); weight = gate, weight2 = up */
+#define SB_EPI_SWIGLU 2 /* y[m, n] = T(act(T(gate)) * T(up)); weight = gate, weight2 = up;
+                         act = SiLU or exact GELU (sb_linear_ex_desc.activation)      */
 #define SB_EPI_ROPE 3   /* QKV rows -> q/k/v [B, heads, L, head_dim], RoPE on q and k    */
 #define SB_EPI_ARGMAX 4 /* argmax_keys[m] = max over n of (fp32 logit, lowest index)     */
 
@@ -98,6 +99,10 @@ typedef struct sb_linear_ex_desc {
   int ar_rank;
   int ar_channel;
   void* ar_buffers[8];
+  /* SB_EPI_SWIGLU activation of the gate: 0 SiLU (SwiGLU, the synthetic model),
+   * 1 exact GELU 0.5 x (1 + erf(x / sqrt 2)) (the GELU-gated FFN of the
+   * reference's Spark2_5 block, spark_mlx_llm/ops/ffn.py:98-103). */
+  int activation;
 } sb_linear_ex_desc;
 
 /* Fused weight-streaming linear (1 <= M <= 8). */
@@ -133,6 +138,21 @@ int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, voi
 /* out = bf16(silu(gate) * up) elementwise over `count` bf16 values (the gated MLP
  * of spark_mlx_llm/ops/ffn.py:98-103 with SiLU); 16-byte aligned buffers. */
 int sb_swiglu(const void* gate, const void* up, void* out, int64_t count, void* stream);
+
+/* out = bf16(act(gate) * up): activation 0 SiLU, 1 exact GELU 0.5 x (1 + erf(x / sqrt 2))
+ * (nn.gelu in the reference's Spark2_5 FFN, spark_mlx_llm/ops/ffn.py:98-103). */
+int sb_gated_activation(const void* gate, const void* up, void* out, int64_t count, int activation,
+                        void* stream);
+
+/*
+ * Attention-output head gate of the Spark2_5 block (spark_mlx_llm/ops/attention_output.py:91-95):
+ * per row m and head h, d = bf16(x[m, :] . gate_weight[h, :]) (fp32 accumulation),
+ * gate = bf16(sigmoid(d)) in fp32, out[m, h, :] = bf16(attn[m, h, :] * gate).
+ *   x [rows, hidden] bf16 (hidden a multiple of 8), gate_weight [heads, hidden] bf16,
+ *   attn / out [rows, heads, head_dim] bf16 (out may alias attn); x, gate_weight 16-byte aligned.
+ */
+int sb_head_gate(const void* x, const void* gate_weight, const void* attn, void* out, int64_t rows,
+                 int64_t hidden, int num_heads, int head_dim, void* stream);
 
 /* INT8-KV decode attention with per-batch lengths lengths[b] + length_offset read on
  * the device; max_length bounds them (it sizes the split-K workspace).

@@ -5,6 +5,8 @@ Floating-point results are computed in float64 from the exact quantized inputs
 bf16 only where the reference stores a bf16 tensor. Integer results are exact.
 """
 
+import math
+
 import numpy as np
 
 from .formats import round_bf16, unpack_codes
@@ -233,6 +235,28 @@ def rms_norm(x, weight, eps):
     x = np.asarray(x, dtype=np.float64)
     r = 1.0 / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
     return x * r * np.asarray(weight, dtype=np.float64)
+
+
+def gelu(x):
+    """Exact GELU ``0.5 x (1 + erf(x / sqrt 2))`` (``nn.gelu`` of the reference's
+    Spark2_5 FFN, ``spark_mlx_llm/ops/ffn.py:102``), float64."""
+    x = np.asarray(x, dtype=np.float64)
+    return 0.5 * x * (1.0 + np.vectorize(math.erf)(x / math.sqrt(2.0)))
+
+
+def gelu_glu(gate, up):
+    """``gelu(gate) * up`` in float64 from bf16 gate/up (``ops/ffn.py:98-103``)."""
+    return gelu(gate) * np.asarray(up, dtype=np.float64)
+
+
+def head_gate(x, gate_weight, attn):
+    """Attention-output head gate (``spark_mlx_llm/ops/attention_output.py:91-95``):
+    ``gate = bf16(sigmoid(float32(bf16(x @ gate_weight.T))))`` per row and head,
+    ``attn[m, h, :] * gate`` in float64. ``x[M, hidden]``, ``gate_weight[H, hidden]``,
+    ``attn[M, H, D]``."""
+    d = round_bf16((np.asarray(x, np.float64) @ np.asarray(gate_weight, np.float64).T).astype(np.float32))
+    g = round_bf16((1.0 / (1.0 + np.exp(-d.astype(np.float64)))).astype(np.float32))
+    return np.asarray(attn, np.float64) * g.astype(np.float64)[:, :, None]
 
 
 def swiglu(gate, up):

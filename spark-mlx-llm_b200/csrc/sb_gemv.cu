@@ -799,8 +799,8 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
       const int n = row_lo;  // gate row n (set 0) pairs with up row n (set 1)
       if (n < p.N) {
         const float gt = round_act<TA>(v_lo), up = round_act<TA>(v_hi);
-        const float silu = gt / (1.0f + expf(-gt));
-        store_act<TA>(p.y, static_cast<size_t>(m + p.m0) * p.ldy + n, silu * up);
+        const float act = p.act ? 0.5f * gt * (1.0f + erff(gt * 0.70710678118654752f)) : gt / (1.0f + expf(-gt));
+        store_act<TA>(p.y, static_cast<size_t>(m + p.m0) * p.ldy + n, act * up);
       }
     } else if constexpr (EPI == EPI_ROPE) {
       const int wph = p.head_dim / 32;
@@ -1260,6 +1260,7 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   p.argmax_keys = r.argmax_keys;
   p.argmax_offset = r.argmax_offset;
   p.early_prefetch = r.weights_constant ? 1 : 0;
+  p.act = r.activation;
   if (r.epi == EPI_ROPE) {
     for (int i = 0; i < r.rope_dims / 2; ++i)
       p.inv_freq[i] = static_cast<float>(std::pow(static_cast<double>(r.rope_base), -2.0 * i / r.rope_dims));

@@ -117,6 +117,7 @@ struct GemvParams {
   // 1: the weights are constant across the stream (model weights), so the
   // kernel may start streaming them before the previous kernel finishes.
   int early_prefetch;
+  int act;  // EPI_SWIGLU: 0 SiLU, 1 exact GELU
 };
 
 // Common request for every linear entry point.
@@ -148,6 +149,7 @@ struct LinearRequest {
   int64_t kv_capacity;
   int ar_world, ar_rank, ar_channel;
   void* ar_buffers[8];
+  int activation;  // EPI_SWIGLU: 0 SiLU, 1 exact GELU
   unsigned long long* argmax_keys;
   int argmax_offset;
   void* workspace;

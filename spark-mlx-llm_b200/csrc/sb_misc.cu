@@ -498,6 +498,8 @@ extern "C" int sb_linear_ex(const sb_linear_ex_desc* d, void* stream) {
   r.workspace = d->workspace;
   r.workspace_bytes = d->workspace_bytes;
   r.weights_constant = d->weights_constant != 0;
+  SB_REQUIRE(d->activation == 0 || d->activation == 1, "activation must be 0 (SiLU) or 1 (GELU)");
+  r.activation = d->activation;
   return run_linear(r, as_stream(stream));
 }
 

@@ -414,11 +414,16 @@ __global__ void rope_append_kernel(const __grid_constant__ RopeParams p) {
   if (lane == 0) (is_k ? p.k_scale : p.v_scale)[row] = s16;
 }
 
-// ------------------------------------------------------------- SwiGLU (elementwise)
-// out = bf16(silu(g) * u) with g, u the bf16 gate / up projections (the
-// single-token path's fused gate/up epilogue, sb_gemv.cu EPI_SWIGLU).
+// ------------------------------------------------- gated activations (elementwise)
+// out = bf16(act(g) * u) with g, u the bf16 gate / up projections and act SiLU
+// (act 0) or the exact GELU (act 1) - the single-token path's fused gate/up
+// epilogue (sb_gemv.cu EPI_SWIGLU).
+__device__ __forceinline__ float gate_act(float g, int act) {
+  return act ? 0.5f * g * (1.0f + erff(g * 0.70710678118654752f)) : g / (1.0f + expf(-g));
+}
+
 __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ gate, const __nv_bfloat16* __restrict__ up,
-                              __nv_bfloat16* __restrict__ out, int64_t count) {
+                              __nv_bfloat16* __restrict__ out, int64_t count, int act) {
   grid_dependency_wait();
   const int64_t i = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8;
   if (i >= count) return;
@@ -433,7 +438,7 @@ __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ gate, const __nv
       for (int e = 0; e < 2; ++e) {
         const float g = e ? bf16_hi(gw[k]) : bf16_lo(gw[k]);
         const float u = e ? bf16_hi(uw[k]) : bf16_lo(uw[k]);
-        o2[e] = g / (1.0f + expf(-g)) * u;
+        o2[e] = gate_act(g, act) * u;
       }
       const __nv_bfloat162 h = __floats2bfloat162_rn(o2[0], o2[1]);
       r[k] = *reinterpret_cast<const uint32_t*>(&h);
@@ -442,9 +447,41 @@ __global__ void swiglu_kernel(const __nv_bfloat16* __restrict__ gate, const __nv
   } else {
     for (int64_t k = i; k < count; ++k) {
       const float g = __bfloat162float(gate[k]), u = __bfloat162float(up[k]);
-      out[k] = __float2bfloat16_rn(g / (1.0f + expf(-g)) * u);
+      out[k] = __float2bfloat16_rn(gate_act(g, act) * u);
     }
   }
+}
+
+// --------------------------------------------------------- attention-output head gate
+// One warp per (row m, head h): the reference's sigmoid head gate
+// (spark_mlx_llm/ops/attention_output.py:91-95): d = bf16(x[m] . gate_w[h]) (fp32
+// accumulation), gate = bf16(sigmoid(d)) in fp32, out[m, h, :] = bf16(attn[m, h, :] * gate).
+__global__ void head_gate_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                                 const __nv_bfloat16* attn, __nv_bfloat16* out, int rows, int hidden, int heads,
+                                 int head_dim) {
+  grid_dependency_wait();
+  const int lane = threadIdx.x & 31;
+  const int item = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (item >= rows * heads) return;
+  const int m = item / heads, h = item % heads;
+  const __nv_bfloat16* xr = x + static_cast<size_t>(m) * hidden;
+  const __nv_bfloat16* wr = w + static_cast<size_t>(h) * hidden;
+  float acc = 0.f;
+  for (int k = lane * 8; k < hidden; k += 256) {
+    const uint4 xa = *reinterpret_cast<const uint4*>(xr + k), wa = *reinterpret_cast<const uint4*>(wr + k);
+    const uint32_t xs[4] = {xa.x, xa.y, xa.z, xa.w}, ws[4] = {wa.x, wa.y, wa.z, wa.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc = fmaf(bf16_lo(xs[i]), bf16_lo(ws[i]), acc);
+      acc = fmaf(bf16_hi(xs[i]), bf16_hi(ws[i]), acc);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  const float d = __bfloat162float(__float2bfloat16_rn(acc));
+  const float gate = __bfloat162float(__float2bfloat16_rn(1.0f / (1.0f + expf(-d))));
+  const size_t base = (static_cast<size_t>(m) * heads + h) * head_dim;
+  for (int i = lane; i < head_dim; i += 32) out[base + i] = __float2bfloat16_rn(__bfloat162float(attn[base + i]) * gate);
 }
 
 }  // namespace prefill
@@ -591,5 +628,35 @@ extern "C" int sb_swiglu(const void* gate, const void* up, void* out, int64_t co
   const int64_t threads = (count + 7) / 8;
   return launch("swiglu", swiglu_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0,
                 as_stream(stream), static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up),
-                static_cast<__nv_bfloat16*>(out), count);
+                static_cast<__nv_bfloat16*>(out), count, 0);
+}
+
+extern "C" int sb_gated_activation(const void* gate, const void* up, void* out, int64_t count, int activation,
+                                   void* stream) {
+  SB_REQUIRE(gate && up && out, "null pointer");
+  SB_REQUIRE(count >= 0, "count");
+  SB_REQUIRE(activation == 0 || activation == 1, "activation must be 0 (SiLU) or 1 (GELU)");
+  if (count == 0) return SB_OK;
+  SB_REQUIRE(reinterpret_cast<uintptr_t>(gate) % 16 == 0 && reinterpret_cast<uintptr_t>(up) % 16 == 0 &&
+                 reinterpret_cast<uintptr_t>(out) % 16 == 0,
+             "gate, up and out must be 16-byte aligned");
+  const int64_t threads = (count + 7) / 8;
+  return launch("gated_activation", swiglu_kernel, dim3(static_cast<unsigned>((threads + 255) / 256)), dim3(256), 0,
+                as_stream(stream), static_cast<const __nv_bfloat16*>(gate), static_cast<const __nv_bfloat16*>(up),
+                static_cast<__nv_bfloat16*>(out), count, activation);
+}
+
+extern "C" int sb_head_gate(const void* x, const void* gate_weight, const void* attn, void* out, int64_t rows,
+                            int64_t hidden, int num_heads, int head_dim, void* stream) {
+  SB_REQUIRE(x && gate_weight && attn && out, "null pointer");
+  SB_REQUIRE(rows >= 1 && num_heads >= 1 && head_dim >= 1 && hidden >= 8 && hidden % 8 == 0, "shape");
+  SB_REQUIRE(rows * num_heads <= (1LL << 31) - 1 && hidden <= (1LL << 30), "too large");
+  SB_REQUIRE(reinterpret_cast<uintptr_t>(x) % 16 == 0 && reinterpret_cast<uintptr_t>(gate_weight) % 16 == 0,
+             "x and gate_weight must be 16-byte aligned");
+  const int64_t items = rows * num_heads;
+  return launch("head_gate", head_gate_kernel, dim3(static_cast<unsigned>((items + 7) / 8)), dim3(256), 0,
+                as_stream(stream), static_cast<const __nv_bfloat16*>(x),
+                static_cast<const __nv_bfloat16*>(gate_weight), static_cast<const __nv_bfloat16*>(attn),
+                static_cast<__nv_bfloat16*>(out), static_cast<int>(rows), static_cast<int>(hidden), num_heads,
+                head_dim);
 }

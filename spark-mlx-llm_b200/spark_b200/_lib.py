@@ -75,6 +75,7 @@ class sb_linear_ex_desc(ctypes.Structure):
         ("ar_rank", _int),
         ("ar_channel", _int),
         ("ar_buffers", _c_void_p * 8),
+        ("activation", _int),
     ]
 
 
@@ -156,6 +157,8 @@ SIGNATURES = {
          _int, _int, _i64, _int, _float, _c_void_p],
     ),
     "sb_swiglu": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
+    "sb_gated_activation": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _int, _c_void_p]),
+    "sb_head_gate": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _int, _int, _c_void_p]),
     "sb_int8_sdpa_decode_static": (
         _int,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _i64, _i64, _int,

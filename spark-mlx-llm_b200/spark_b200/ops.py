@@ -24,6 +24,8 @@ __all__ = [
     "int8_sdpa_decode",
     "int8_sdpa_prefill",
     "bf16_sdpa_multiquery",
+    "gated_activation",
+    "head_gate",
     "rms_norm",
     "workspace",
 ]
@@ -371,6 +373,50 @@ def bf16_sdpa_multiquery(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scal
 @bf16_sdpa_multiquery.register_fake
 def _(q, k, v, scale, causal, window, mask):
     return torch.empty_like(q)
+
+
+@torch.library.custom_op("spark_b200::gated_activation", mutates_args=())
+def gated_activation(gate: torch.Tensor, up: torch.Tensor, activation: int) -> torch.Tensor:
+    """``bf16(act(gate) * up)``: activation 0 SiLU (SwiGLU), 1 exact GELU (the
+    Spark2_5 FFN, ``spark_mlx_llm/ops/ffn.py:98-103``). bf16 tensors of one shape."""
+    _require_cuda(gate, up)
+    if gate.dtype != torch.bfloat16 or up.dtype != torch.bfloat16 or gate.shape != up.shape:
+        raise ValueError("gate and up must be bfloat16 tensors of one shape")
+    if activation not in (0, 1):
+        raise ValueError("activation must be 0 (SiLU) or 1 (GELU)")
+    g, u = gate.contiguous(), up.contiguous()
+    out = torch.empty_like(g)
+    check(lib().sb_gated_activation(g.data_ptr(), u.data_ptr(), out.data_ptr(), g.numel(), int(activation),
+                                    _stream(g)), "gated activation")
+    return out
+
+
+@gated_activation.register_fake
+def _(gate, up, activation):
+    return torch.empty_like(gate)
+
+
+@torch.library.custom_op("spark_b200::head_gate", mutates_args=())
+def head_gate(x: torch.Tensor, gate_weight: torch.Tensor, attn: torch.Tensor) -> torch.Tensor:
+    """Attention-output head gate (``ops/attention_output.py:91-95``): ``x[M, hidden]``,
+    ``gate_weight[H, hidden]``, ``attn[M, H, D]`` bf16; returns ``attn * gate`` with
+    ``gate = bf16(sigmoid(bf16(x . gate_weight[h])))``."""
+    _require_cuda(x, gate_weight, attn)
+    if any(t.dtype != torch.bfloat16 for t in (x, gate_weight, attn)):
+        raise ValueError("x, gate_weight and attn must be bfloat16")
+    if x.ndim != 2 or gate_weight.ndim != 2 or attn.ndim != 3 or gate_weight.shape[1] != x.shape[1] \
+            or attn.shape[:2] != (x.shape[0], gate_weight.shape[0]):
+        raise ValueError("expected x [M, hidden], gate_weight [H, hidden], attn [M, H, D]")
+    xc, wc, ac = x.contiguous(), gate_weight.contiguous(), attn.contiguous()
+    out = torch.empty_like(ac)
+    check(lib().sb_head_gate(xc.data_ptr(), wc.data_ptr(), ac.data_ptr(), out.data_ptr(), x.shape[0], x.shape[1],
+                             gate_weight.shape[0], attn.shape[2], _stream(x)), "head gate")
+    return out
+
+
+@head_gate.register_fake
+def _(x, gate_weight, attn):
+    return torch.empty_like(attn)
 
 
 # ---------------------------------------------------------------------- RMSNorm
