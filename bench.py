@@ -55,7 +55,10 @@ def parse_args():
     p.add_argument("--no-ops", action="store_true", help="skip the per-operator roofline section")
     p.add_argument("--engine", choices=["auto", "step", "launches"], default="auto",
                    help="decode engine: the persistent decode-step kernel (batch 1, one GPU) or the per-operator "
-                        "launch sequence; auto picks the step kernel where it applies")
+                        "launch sequence; auto picks the launch sequence (measured faster)")
+    p.add_argument("--no-invariant", action="store_true",
+                   help="let each tensor-parallel degree pick its own K splits (faster shards, greedy tokens "
+                        "no longer bit-identical across degrees)")
     p.add_argument("--digest-steps", type=int, default=256,
                    help="greedy tokens hashed into tokens_sha256 (decoded from the state after the prompt)")
     p.add_argument("--kernel-only", choices=["gateup", "sdpa", "tc"], default=None,
@@ -250,6 +253,7 @@ def workload_config(args, parallel):
                     f"decode batch {args.batch} after a {args.prompt}-token prompt",
         "batch": args.batch, "prompt_tokens": args.prompt, "layers": args.layers, "parallelism": parallel,
         "engine": getattr(args, "engine_used", getattr(args, "engine", "auto")),
+        "summation": "fast" if getattr(args, "no_invariant", False) else "tp-invariant",
         "l2": "inputs larger than L2: every step streams ~3.2 GB of weights (126 MB L2)",
     }
 
@@ -594,7 +598,7 @@ def main():
     # post-prompt state) or warm-up + timed + end-to-end steps, whichever is longer
     capacity = args.prompt + max(args.digest_steps, args.warmup + 2 * args.steps) + 16
     dec = SyntheticDecoder(cfg, batch=args.batch, capacity=capacity, device=device, seed=0, rank=rank, world=world,
-                           group=group, engine=args.engine)
+                           group=group, engine=args.engine, invariant=not args.no_invariant)
     args.engine_used = dec.engine
     gen = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, cfg.vocab, (args.batch, args.prompt), generator=gen, dtype=torch.int32)

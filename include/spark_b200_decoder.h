@@ -89,8 +89,9 @@ typedef struct sb_linear_ex_desc {
   /* RESID, optional fused tensor-parallel all-reduce (ar_world 2..8): y is
    * T(residual + T(sum over ranks of the fp32 partial products)). Each rank
    * stores its partial rows into every rank's exchange buffer over NVLink,
-   * signals per CTA, waits (bounded) for the other ranks' same CTA and sums in
-   * rank order - this replaces all-reduce + residual-add after the row-split
+   * signals per CTA, waits (bounded) for the other ranks' same CTA and adds
+   * the ranks' partials in a balanced binary tree (pairs (0,1) (2,3) ..., then
+   * pairs of pairs; the order of k_chunks below) - this replaces all-reduce + residual-add after the row-split
    * o/down projections. ar_buffers[r] is rank r's exchange buffer as mapped in
    * this process (sb_peer_buffer_alloc / _open), sb_tp_exchange_bytes(ar_world,
    * N) bytes, zeroed at creation; consecutive exchanges alternate ar_channel
@@ -103,10 +104,43 @@ typedef struct sb_linear_ex_desc {
    * 1 exact GELU 0.5 x (1 + erf(x / sqrt 2)) (the GELU-gated FFN of the
    * reference's Spark2_5 block, spark_mlx_llm/ops/ffn.py:98-103). */
   int activation;
+  /* Summation order fixed across tensor-parallel degrees (greedy tokens that are
+   * bit-identical at TP 1/2/4/8):
+   * k_chunks 2..8 (STORE/RESID, no norm_weight): K is k_chunks equal chunks of
+   *   whole groups (16-byte multiples of weight bytes). Each chunk's fp32 partial
+   *   is computed exactly as a launch over that chunk's K alone computes it (the
+   *   chunks are CTA groups of one thread-block cluster), and the partials are
+   *   added in a balanced binary tree in chunk order before the epilogue. A
+   *   row-split projection whose unsharded K has c chunks then rounds
+   *   identically when rank r of a TP-n group holds chunks [r c/n, (r+1) c/n)
+   *   with k_chunks = c/n, plan_k_chunks = c, and the fused all-reduce adds the
+   *   ranks' partials.
+   * plan_rows > 0: choose the K split as for plan_rows output rows (a
+   *   column-split shard names the unsharded row count, so each of its rows sums
+   *   exactly as in the whole matrix); plan_k_chunks > 0 likewise plans for that
+   *   many K chunks resident at once (the unsharded chunk count). 0 = this
+   *   launch's own shape. */
+  int k_chunks;
+  int64_t plan_rows;
+  int plan_k_chunks;
+  /* SB_EPI_STORE: 1 stores y as fp32 (the unrounded sum, e.g. a partial for an
+   * external all-reduce), 0 in the activation dtype. */
+  int y_fp32;
+  /* Affine formats: scale/bias groups per weight row in scales/biases (and
+   * scales2/biases2), >= K / group_size; 0 = K / group_size. Rows padded to a
+   * multiple of 8 groups (16 bytes) let the tables stream by TMA. */
+  int64_t scales_ld;
 } sb_linear_ex_desc;
 
 /* Fused weight-streaming linear (1 <= M <= 8). */
 int sb_linear_ex(const sb_linear_ex_desc* desc, void* stream);
+/* The launch plan sb_linear_ex would use for `desc`, without launching (needs
+ * the device for its occupancy queries): plan[0..7] = CTAs per cluster,
+ * clusters (row groups), threads per CTA, dynamic shared memory bytes, CTAs
+ * per K chunk, K sub-parts per CTA, TMA ring depth per warp, 128-byte weight
+ * stages per row (of one K chunk). For M > 4 with group 32 (two launches) the
+ * first launch's plan. */
+int sb_linear_ex_plan(const sb_linear_ex_desc* desc, int* plan);
 size_t sb_linear_ex_workspace_size(const sb_linear_ex_desc* desc);
 
 /*
@@ -160,11 +194,15 @@ int sb_head_gate(const void* x, const void* gate_weight, const void* attn, void*
  * newest one (position lengths[b] + length_offset - 1) were written before the
  * kernel that precedes this launch in the stream; the kernel then streams those
  * rows while that kernel still runs (programmatic dependent launch). 0 waits
- * for the previous kernel before reading anything. */
+ * for the previous kernel before reading anything. plan_kv_heads > 0 splits
+ * the tokens as a launch over that many KV heads would (a tensor-parallel shard
+ * naming the unsharded KV head count computes its heads bit-identically to the
+ * unsharded launch); the workspace must then hold that plan's splits
+ * (sb_int8_sdpa_workspace_size with the unsharded head counts suffices). */
 int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
                             const void* v_scale, void* out, int64_t batch, int num_heads, int num_kv_heads,
                             const int32_t* lengths, int length_offset, int64_t max_length, int64_t capacity,
-                            int head_dim, float scale, int prefix_constant, void* workspace,
+                            int head_dim, float scale, int prefix_constant, int plan_kv_heads, void* workspace,
                             size_t workspace_bytes, void* stream);
 
 /* Exchange buffers of the fused tensor-parallel all-reduce (sb_linear_ex

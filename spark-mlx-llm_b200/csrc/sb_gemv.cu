@@ -208,11 +208,15 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
   const bool active = rb < rowblocks;
   const int rbc = min(rb, rowblocks - 1);
   const int M = p.M;
-  const int gpr = p.K / C::kGroupK;  // groups per row
+  const int gpr = p.K / C::kGroupK;  // groups per row (of this K chunk)
+  const int cparts = p.chunk_parts;  // CTAs per K chunk (chunk-major cluster ranks)
+  const int zc = part / cparts;      // K chunk of this CTA
+  const int cq = part - zc * cparts; // part inside the chunk
+  const TA* xz = static_cast<const TA*>(p.x) + static_cast<size_t>(zc) * p.K;
 
-  // stages [st0, st1) of this CTA
-  const int st0 = static_cast<int>((static_cast<long long>(p.stages_total) * part) / nparts);
-  const int st1 = static_cast<int>((static_cast<long long>(p.stages_total) * (part + 1)) / nparts);
+  // stages [st0, st1) of this CTA (of its chunk)
+  const int st0 = static_cast<int>((static_cast<long long>(p.stages_total) * cq) / cparts);
+  const int st1 = static_cast<int>((static_cast<long long>(p.stages_total) * (cq + 1)) / cparts);
   const int nst = st1 - st0;
 
   // ---- shared memory: barriers + zero block, per-warp rings, staged x, group meta, reduction buffer
@@ -234,7 +238,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
   auto issue_stage = [&](int slot, int st) {
     uint8_t* dst = ring + slot * kStageBytes;
     mbar_arrive_expect_tx(bars + slot, kStageBytes);
-    const int x = (st0 + st) * 128;
+    const int x = zc * p.chunk_wbytes + (st0 + st) * 128;
     tma_load_2d(dst, &p.tmap0, x, rowA, bars + slot);
     tma_load_2d(dst + 16 * 128, &p.tmap1, x, rowB, bars + slot);
   };
@@ -250,7 +254,8 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
     if constexpr (C::kAffine) {
       const int G0 = (st0 + sb) * C::kGPS;
       if (p.sc_tma) {
-        sc_off = G0 & 7;
+        const int Ga = zc * gpr + G0;  // group in the table row
+        sc_off = Ga & 7;
         if (threadIdx.x == 0) {
           fence_proxy_async_smem();
           mbar_arrive_expect_tx(scbar, static_cast<uint32_t>(2 * kGemvWarps * 32 * p.sc_ld * 2));
@@ -260,8 +265,8 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
             for (int h = 0; h < 2; ++h) {
               const int row0 = box_row0<EPI>(p, rbw, h);
               const int o = (w * 32 + h * 16) * p.sc_ld;
-              tma_load_2d(scs + o, set_of(h) ? &p.smap1 : &p.smap0, G0 - sc_off, row0, scbar);
-              tma_load_2d(scb + o, set_of(h) ? &p.bmap1 : &p.bmap0, G0 - sc_off, row0, scbar);
+              tma_load_2d(scs + o, set_of(h) ? &p.smap1 : &p.smap0, Ga - sc_off, row0, scbar);
+              tma_load_2d(scb + o, set_of(h) ? &p.bmap1 : &p.bmap0, Ga - sc_off, row0, scbar);
             }
           }
         }
@@ -280,7 +285,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
         const int rbw = min(static_cast<int>(blockIdx.y) * kGemvWarps + w, rowblocks - 1);
         const int grow = min(box_row0<EPI>(p, rbw, h) + (row & 15), p.N - 1);
         const uint16_t* src = static_cast<const uint16_t*>(which ? (set_of(h) ? p.b1 : p.b0) : (set_of(h) ? p.s1 : p.s0)) +
-                              static_cast<size_t>(grow) * gpr + G0;
+                              static_cast<size_t>(grow) * p.sc_stride + zc * gpr + G0;
         uint16_t* dst = (which ? scb : scs) + wr * p.sc_ld;
         if (async) cp_async4(dst + 2 * c, src + 2 * c);
         else dst[c] = src[c];
@@ -360,7 +365,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
     const int idx = it * kNT + static_cast<int>(threadIdx.x);
     if (idx < M * nvec) {
       const int m = idx / nvec, k = k0 + 8 * (idx - m * nvec);
-      pre_x[it] = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + k);
+      pre_x[it] = *reinterpret_cast<const uint4*>(xz + static_cast<size_t>(m) * p.ldx + k);
       if constexpr (NORM) pre_w[it] = *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.norm_w) + k);
     }
   }
@@ -430,7 +435,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
       if (ok) {
         const bool pre = sb == 0 && b0 < 2 * kNT;
         const uint4 xv = pre ? (b0 == 0 ? pre_x[0] : pre_x[1])
-                             : *reinterpret_cast<const uint4*>(static_cast<const TA*>(p.x) + static_cast<size_t>(m) * p.ldx + k);
+                             : *reinterpret_cast<const uint4*>(xz + static_cast<size_t>(m) * p.ldx + k);
         const TA* xe = reinterpret_cast<const TA*>(&xv);
         if constexpr (NORM) {
           const uint4 wv = pre ? (b0 == 0 ? pre_w[0] : pre_w[1])
@@ -652,8 +657,13 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
             for (int h = 0; h < 2; ++h) {
               const int o = (rbi * 32 + h * 16 + 8 * r + sg) * p.sc_ld + gseg + ss0 + sc_off;
               if constexpr (kPairCols) {
-                sv[r][h] = *reinterpret_cast<const uint32_t*>(scs + o);
-                bv[r][h] = *reinterpret_cast<const uint32_t*>(scb + o);
+                if ((sc_off & 1) == 0) {
+                  sv[r][h] = *reinterpret_cast<const uint32_t*>(scs + o);
+                  bv[r][h] = *reinterpret_cast<const uint32_t*>(scb + o);
+                } else {  // a K chunk starting at an odd group: the pair straddles 4 bytes
+                  sv[r][h] = static_cast<uint32_t>(scs[o]) | (static_cast<uint32_t>(scs[o + 1]) << 16);
+                  bv[r][h] = static_cast<uint32_t>(scb[o]) | (static_cast<uint32_t>(scb[o + 1]) << 16);
+                }
               } else {
                 sv[r][h] = scs[o];
                 bv[r][h] = scb[o];
@@ -768,6 +778,54 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
     if (threadIdx.x == 0) s_epoch = *ar_seen + 1u;
     __syncthreads();
   }
+  // value of pair pl (box h) for activation row m: per K chunk the chunk's
+  // parts added in rank order from zero, times the per-channel scale (a
+  // rounded product, never fused into a later add: the value a launch over
+  // that chunk alone produces); the chunks' values then meet in the balanced
+  // tree of tree_sum8
+  const int nchunks = p.chunks;
+  const int sstride = ppc * 2 * M;  // floats between sources in `red`
+  auto pair_row = [&](int pl, int h) {
+    const int P = part * ppc + pl;
+    const int rbx = blockIdx.y * kGemvWarps + (P >> 4);
+    return rbx < rowblocks ? box_row0<EPI>(p, rbx, h) + 8 * ((P >> 3) & 1) + sigma_row<C::kLaneB>(P & 7) : p.N;
+  };
+  if (nchunks > 1) {
+    // chunk values in parallel, each into its chunk's first source slot
+    const int per = cparts * nsub;
+    const int items = own_pairs * M * 2 * nchunks;
+    for (int idx = threadIdx.x; idx < items; idx += kNT) {
+      const int z = idx % nchunks;
+      const int rest = idx / nchunks;
+      const int h = rest & 1, m = (rest >> 1) % M, pl = (rest >> 1) / M;
+      float* rd = red + pl * 2 * M + h * M + m;
+      float v = 0.f;
+      for (int src = z * per; src < (z + 1) * per; ++src) v += rd[src * sstride];
+      if constexpr (WF == W_I8PC) {
+        const int row = pair_row(pl, h);
+        if (row < p.N) v = __fmul_rn(v, static_cast<const float*>(p.s0)[row]);
+      }
+      rd[z * per * sstride] = v;
+    }
+    __syncthreads();
+  }
+  auto part_sum = [&](int pl, int m, int h, int row) {
+    const float* rd = red + pl * 2 * M + h * M + m;  // source src at rd[src * sstride]
+    if (nchunks == 1) {
+      float v = 0.f;
+      for (int src = 0; src < nparts * nsub; ++src) v += rd[src * sstride];
+      if constexpr (WF == W_I8PC) {
+        if (row < p.N) v = __fmul_rn(v, static_cast<const float*>(p.s0)[row]);
+      }
+      return v;
+    }
+    const int per = cparts * nsub;
+    float c[8];
+#pragma unroll
+    for (int z = 0; z < 8; ++z) c[z] = z < nchunks ? rd[z * per * sstride] : 0.f;
+    return tree_sum8(c, nchunks);
+  };
+
   bool gave_up = false;  // fused all-reduce: a wait of this thread ran out
   for (int idx = threadIdx.x; idx < own_pairs * M; idx += kNT) {
     const int pl = idx / M, m = idx - (idx / M) * M;
@@ -775,18 +833,11 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
     const int w = P >> 4, r = (P >> 3) & 1, gg = P & 7;
     const int rbx = blockIdx.y * kGemvWarps + w;
     if (rbx >= rowblocks) continue;
-    float v_lo = 0.f, v_hi = 0.f;
-    for (int src = 0; src < nparts * nsub; ++src) {
-      v_lo += red[((src * ppc + pl) * 2 + 0) * M + m];
-      v_hi += red[((src * ppc + pl) * 2 + 1) * M + m];
-    }
     const int sgg = sigma_row<C::kLaneB>(gg);
     const int row_lo = box_row0<EPI>(p, rbx, 0) + 8 * r + sgg;
     const int row_hi = box_row0<EPI>(p, rbx, 1) + 8 * r + sgg;
-    if constexpr (WF == W_I8PC) {
-      if (row_lo < p.N) v_lo *= static_cast<const float*>(p.s0)[row_lo];
-      if (row_hi < p.N) v_hi *= static_cast<const float*>(p.s0)[row_hi];
-    }
+    float v_lo = part_sum(pl, m, 0, row_lo);
+    float v_hi = part_sum(pl, m, 1, row_hi);
     if constexpr (EPI == EPI_ARGMAX) {
       unsigned long long best = 0ull;
       if (row_lo < p.N) best = argmax_key(v_lo, row_lo + p.argmax_offset);
@@ -856,17 +907,20 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
           if (p.ar_world > 1) {
             // fused all-reduce: post this rank's fp32 partial with the epoch in
             // slot [ar_rank] of every other rank, wait for the other ranks'
-            // partials of the same output element here, sum in rank order
+            // partials of the same output element here, add them in tree order
             const unsigned epoch = s_epoch;
             const size_t col = (static_cast<size_t>(row) * 8 + m + p.m0) * 8;
             const size_t chan = p.ar_channel * ar_chan_bytes;
             for (int q = 0; q < p.ar_world; ++q)
               if (q != p.ar_rank)
                 st_slot(p.ar_buf[q] + chan + static_cast<size_t>(p.ar_rank) * p.ar_np * 64 + col, v, epoch);
-            float sum = 0.f;
+            // the ranks' partials, added in the balanced tree of the K chunks
+            // (rank r holds chunks [r*c, (r+1)*c)), so every degree rounds alike
+            float pv[8];
+            for (int q = 0; q < 8; ++q) pv[q] = 0.f;
             for (int q = 0; q < p.ar_world; ++q) {
               if (q == p.ar_rank) {
-                sum += v;
+                pv[q] = v;
                 continue;
               }
               const uint8_t* slot = p.ar_buf[p.ar_rank] + chan + static_cast<size_t>(q) * p.ar_np * 64 + col;
@@ -892,8 +946,9 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
                   }
                 }
               }
-              sum += __uint_as_float(static_cast<unsigned>(w));
+              pv[q] = __uint_as_float(static_cast<unsigned>(w));
             }
+            const float sum = tree_sum8(pv, p.ar_world);
             const float res_v = load_act<TA>(p.residual, static_cast<size_t>(m + p.m0) * p.ldr + row);
             store_act<TA>(p.y, o, res_v + round_act<TA>(sum));
             continue;
@@ -901,7 +956,8 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const __gri
           const float res_v = load_act<TA>(p.residual, static_cast<size_t>(m + p.m0) * p.ldr + row);
           store_act<TA>(p.y, o, res_v + round_act<TA>(v));
         } else {
-          store_act<TA>(p.y, o, v);
+          if (p.y_f32) static_cast<float*>(p.y)[o] = v;
+          else store_act<TA>(p.y, o, v);
         }
       }
     }
@@ -1021,6 +1077,10 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
   if (!prepare_kernel(reinterpret_cast<const void*>(kernel), &large_clusters))
     return fail(SB_ECUDA, "gemv: shared memory opt-in failed");
   const int row_groups = (rowblocks_of(EPI, p.N) + kGemvWarps - 1) / kGemvWarps;
+  // the K split is chosen for the planned shape (the rows and K chunks of the
+  // unsharded matrix, its clusters all resident at once), so shards of it sum alike
+  const int plan_groups = (rowblocks_of(EPI, p.plan_rows > 0 ? p.plan_rows : p.N) + kGemvWarps - 1) / kGemvWarps;
+  const int pchunks = std::max(1, p.plan_chunks > 0 ? p.plan_chunks : p.chunks);
   const int row_bytes = static_cast<int>(static_cast<int64_t>(p.K) * C::kBits / 8);
   p.stages_total = (row_bytes + 127) / 128;
 
@@ -1028,7 +1088,12 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
   // the tables are 16-byte aligned.
   const int gpr = C::kAffine ? p.K / C::kGroupK : 0;
   auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  const bool tma_ok = C::kAffine && gpr % 8 == 0 && al16(p.s0) && al16(p.b0) && al16(p.s1) && al16(p.b1);
+  // (a K chunk may start at any group: the box then starts at the group rounded
+  // down to 8, and a planned launch reserves the 7 columns that can cost
+  // whether or not its tables allow TMA, so its plan does not depend on them)
+  const bool planned = pchunks > 1;
+  const bool tma_ok = C::kAffine && (gpr % 8 == 0 || planned) && p.sc_stride % 8 == 0 && al16(p.s0) && al16(p.b0) &&
+                      al16(p.s1) && al16(p.b1);
   // Per candidate (cluster size, K sub-parts per CTA, ring depth): activation
   // segment and shared memory; 0 when the sub-parts cannot share one segment.
   auto configure = [&](int parts, int nsub, int ring) -> size_t {
@@ -1049,7 +1114,7 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
     p.sc_ld = 0;
     if (C::kAffine) {
       // TMA boxes start at the group rounded down to 8 (up to 6 more columns)
-      const int need = seg_groups + (MC == 1 ? std::max(0, 8 - C::kSlots) : 0) + (tma_ok ? 6 : 0);
+      const int need = seg_groups + (MC == 1 ? std::max(0, 8 - C::kSlots) : 0) + (planned ? 7 : (tma_ok ? 6 : 0));
       int q = (need + 7) / 8;
       if ((q & 1) == 0) ++q;
       p.sc_ld = 8 * q;
@@ -1062,18 +1127,21 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
   // Largest cluster (K split across CTAs) whose clusters are all co-resident,
   // each CTA with at least two stages; within it, two K sub-parts per CTA (8
   // warps) when they fit, and the deepest ring (4..2) that fits. One CTA of 4
-  // warps per row group when the row groups alone fill the GPU.
+  // warps per row group when the row groups alone fill the GPU. With K chunks
+  // the cluster is chunks x (CTAs per chunk), planned for the unsharded chunk
+  // count; `parts` below counts the CTAs of one chunk.
   int parts = 1, nsub = 1;
   size_t smem = 0;
   bool chosen = false;
-  for (int cand = kMaxParts; cand >= 2 && !chosen; cand >>= 1) {
-    if (p.stages_total < 2 * cand || (cand > 8 && !large_clusters)) continue;
+  for (int cand = kMaxParts / pchunks; cand >= (pchunks > 1 ? 1 : 2) && !chosen; cand >>= 1) {
+    const int cl = cand * pchunks;
+    if (p.stages_total < 2 * cand || (cl > 8 && !large_clusters)) continue;
     for (int ns = 2; ns >= 1 && !chosen; --ns)
       for (int ring = 4; ring >= 2 && !chosen; --ring) {
         smem = configure(cand, ns, ring);
         if (smem == 0) continue;
-        if (max_active_clusters(reinterpret_cast<const void*>(kernel), cand, 32 * kGemvWarps * ns, smem, row_groups) >=
-            row_groups) {
+        if (max_active_clusters(reinterpret_cast<const void*>(kernel), cl, 32 * kGemvWarps * ns, smem, plan_groups) >=
+            plan_groups) {
           parts = cand;
           nsub = ns;
           chosen = true;
@@ -1081,19 +1149,28 @@ int launch_gemv_mc(GemvParams& p, cudaStream_t stream) {
       }
   }
   if (!chosen) smem = configure(1, 1, 4);
+  p.chunk_parts = parts;
+  const int cluster = parts * std::max(1, p.chunks);
   p.sc_tma = 0;
   if (tma_ok && p.sc_ld <= 256) {
     p.sc_tma = 1;
     const uint64_t n = static_cast<uint64_t>(p.N);
-    if (int st = make_tmap_u16(&p.smap0, p.s0, n, gpr, p.sc_ld, 16)) return st;
-    if (int st = make_tmap_u16(&p.bmap0, p.b0, n, gpr, p.sc_ld, 16)) return st;
-    if (int st = make_tmap_u16(&p.smap1, p.s1, n, gpr, p.sc_ld, 16)) return st;
-    if (int st = make_tmap_u16(&p.bmap1, p.b1, n, gpr, p.sc_ld, 16)) return st;
+    if (int st = make_tmap_u16(&p.smap0, p.s0, n, p.sc_stride, p.sc_ld, 16)) return st;
+    if (int st = make_tmap_u16(&p.bmap0, p.b0, n, p.sc_stride, p.sc_ld, 16)) return st;
+    if (int st = make_tmap_u16(&p.smap1, p.s1, n, p.sc_stride, p.sc_ld, 16)) return st;
+    if (int st = make_tmap_u16(&p.bmap1, p.b1, n, p.sc_stride, p.sc_ld, 16)) return st;
   }
-  if (p.ar_world > 1 && parts * row_groups > kArCtas)
+  if (p.ar_world > 1 && cluster * row_groups > kArCtas)
     return fail(SB_EUNSUPPORTED, "fused all-reduce: too many CTAs for the exchange counters");
-  dim3 grid(parts, row_groups);
-  return launch_cluster("gemv", kernel, grid, dim3(kGemvWarps * 32 * nsub), smem, parts, stream, p);
+  if (cluster > 8 && !large_clusters) return fail(SB_EUNSUPPORTED, "K chunks: cluster larger than 8 CTAs unavailable");
+  dim3 grid(cluster, row_groups);
+  if (p.plan_out) {
+    const int plan[8] = {cluster, row_groups, kGemvWarps * 32 * nsub, static_cast<int>(smem), parts, nsub, p.ring,
+                         p.stages_total};
+    for (int i = 0; i < 8; ++i) p.plan_out[i] = plan[i];
+    return SB_OK;
+  }
+  return launch_cluster("gemv", kernel, grid, dim3(kGemvWarps * 32 * nsub), smem, cluster, stream, p);
 }
 
 template <typename TA, int WF, int G, int EPI, bool NORM>
@@ -1207,12 +1284,34 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
     SB_REQUIRE(r.positions != nullptr, "fused cache append needs positions");
   }
 
+  const int bits = r.wf == W_AFF4 ? 4 : (r.wf == W_BF16 ? 16 : 8);
+  const int chunks = r.k_chunks > 1 ? r.k_chunks : 1;
+  if (chunks > 1) {
+    SB_REQUIRE(chunks <= 8, "k_chunks must be 1..8");
+    SB_REQUIRE(r.epi == EPI_RESID || r.epi == EPI_STORE, "K chunks belong to the STORE and RESID epilogues");
+    SB_REQUIRE(!r.norm, "K chunks do not combine with the fused RMSNorm");
+    SB_REQUIRE(r.plan_chunks == 0 || r.plan_chunks >= chunks, "plan_k_chunks must cover k_chunks");
+    SB_REQUIRE(r.K % (chunks * gk) == 0, "K must split into k_chunks chunks of whole groups");
+    SB_REQUIRE((static_cast<int64_t>(r.K / chunks) * bits / 8) % 16 == 0,
+               "each K chunk must hold a multiple of 16 weight bytes per row");
+  }
+
   GemvParams p{};
   p.x = r.x;
   p.ldx = r.ldx;
   p.M = r.M;
   p.N = r.N;
-  p.K = r.K;
+  p.K = r.K / chunks;
+  p.chunks = chunks;
+  p.chunk_wbytes = static_cast<int>(static_cast<int64_t>(p.K) * bits / 8);
+  SB_REQUIRE(r.scales_ld == 0 || r.scales_ld >= r.K / gk, "scales_ld must cover K / group_size groups");
+  p.sc_stride = r.scales_ld > 0 ? r.scales_ld : r.K / gk;
+  p.plan_rows = r.plan_rows;
+  p.plan_chunks = r.plan_chunks;
+  SB_REQUIRE(!r.y_f32 || r.epi == EPI_STORE, "fp32 outputs belong to the STORE epilogue");
+  p.y_f32 = r.y_f32 ? 1 : 0;
+  p.plan_out = r.plan_out;
+
   p.w0 = r.w0;
   p.s0 = r.s0;
   p.b0 = r.b0;
@@ -1221,12 +1320,11 @@ int run_linear(const LinearRequest& r, cudaStream_t stream) {
   p.b1 = r.b1 ? r.b1 : r.b0;
   p.group_size = r.group_size;
   {
-    const int gpr = r.K / gk;
+    const int gpr = p.K / gk;
     auto al4 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 3) == 0; };
-    p.pair_scales = (gpr % 2 == 0) && al4(p.s0) && al4(p.b0) && al4(p.s1) && al4(p.b1) ? 1 : 0;
+    p.pair_scales = (gpr % 2 == 0) && (p.sc_stride % 2 == 0) && al4(p.s0) && al4(p.b0) && al4(p.s1) && al4(p.b1) ? 1 : 0;
   }
   {
-    const int bits = r.wf == W_AFF4 ? 4 : (r.wf == W_BF16 ? 16 : 8);
     const uint64_t row_bytes = static_cast<uint64_t>(r.K) * bits / 8;
     if (int st = make_tmap_rows(&p.tmap0, r.w0, static_cast<uint64_t>(r.N), row_bytes, 16)) return st;
     if (int st = make_tmap_rows(&p.tmap1, r.w1 ? r.w1 : r.w0, static_cast<uint64_t>(r.N), row_bytes, 16)) return st;

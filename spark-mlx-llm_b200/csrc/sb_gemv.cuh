@@ -118,6 +118,23 @@ struct GemvParams {
   // kernel may start streaming them before the previous kernel finishes.
   int early_prefetch;
   int act;  // EPI_SWIGLU: 0 SiLU, 1 exact GELU
+  // K chunks (RESID/STORE): chunk z is K values [z*K, (z+1)*K) of rows that
+  // hold chunk_wbytes * chunks weight bytes and sc_stride scale/bias groups.
+  // The cluster's CTAs are chunk-major: CTA rank c = z * chunk_parts + q, and
+  // the chunk's chunk_parts CTAs split its stages as a launch over that chunk
+  // alone would. Each chunk's fp32 partial (its K parts added in rank order,
+  // times the per-channel scale) is computed exactly as such a launch computes
+  // it; the chunks' partials are then added in a balanced binary tree.
+  int chunks;
+  int chunk_parts;
+  int chunk_wbytes;
+  int sc_stride;  // scale/bias groups per weight row in the tables
+  int y_f32;  // EPI_STORE: y is fp32 (the sum before any rounding)
+  int* plan_out;  // host only: report the plan instead of launching
+  // launch planning only: the K split is chosen as for plan_rows output rows in
+  // plan_chunks chunks (the unsharded matrix), so that every tensor-parallel
+  // shard sums its rows exactly as the whole matrix does
+  int plan_rows, plan_chunks;
 };
 
 // Common request for every linear entry point.
@@ -155,6 +172,11 @@ struct LinearRequest {
   void* workspace;
   size_t workspace_bytes;
   bool weights_constant;
+  int k_chunks;  // > 1: fixed K chunks summed in a balanced tree (GemvParams)
+  int plan_rows, plan_chunks;
+  bool y_f32;
+  int* plan_out;  // non-null: report the launch plan (sb_linear_ex_plan) instead of launching
+  int scales_ld;  // affine: scale/bias groups per weight row in the tables (0: K / group)
 };
 
 int run_linear(const LinearRequest& r, cudaStream_t stream);
@@ -168,5 +190,17 @@ inline size_t ar_channel_bytes(int world, int64_t n) {
   return static_cast<size_t>(world) * ar_np(n) * 8 * 8 + static_cast<size_t>(kArCtas) * 4;
 }
 size_t linear_workspace_size(int epi, int N, int K, int group_k);
+// Balanced binary tree over v[0..n) (n <= 8) in index order: pairs (0,1) (2,3)
+// ..., then pairs of pairs: how the fused all-reduce adds the ranks' partials.
+// The K chunks of one launch meet in the same tree (built incrementally there),
+// so a sum split over 1, 2, 4 or 8 ranks rounds identically.
+__device__ __forceinline__ float tree_sum8(float (&v)[8], int n) {
+#pragma unroll
+  for (int s = 1; s < 8; s <<= 1)
+#pragma unroll
+    for (int i = 0; i + s < 8; i += 2 * s)
+      if (i + s < n) v[i] += v[i + s];
+  return v[0];
+}
 
 }  // namespace sb

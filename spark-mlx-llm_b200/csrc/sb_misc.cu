@@ -451,7 +451,8 @@ extern "C" size_t sb_linear_ex_workspace_size(const sb_linear_ex_desc* d) {
   return linear_workspace_size(d->epilogue, static_cast<int>(d->N), static_cast<int>(d->K), gk);
 }
 
-extern "C" int sb_linear_ex(const sb_linear_ex_desc* d, void* stream) {
+namespace {
+int linear_ex(const sb_linear_ex_desc* d, void* stream, int* plan_out) {
   SB_REQUIRE(d != nullptr, "null descriptor");
   if (int st = check_sizes(d->M, d->N, d->K)) return st;
   SB_REQUIRE(d->epilogue >= SB_EPI_STORE && d->epilogue <= SB_EPI_ARGMAX, "unknown epilogue");
@@ -500,7 +501,26 @@ extern "C" int sb_linear_ex(const sb_linear_ex_desc* d, void* stream) {
   r.weights_constant = d->weights_constant != 0;
   SB_REQUIRE(d->activation == 0 || d->activation == 1, "activation must be 0 (SiLU) or 1 (GELU)");
   r.activation = d->activation;
+  SB_REQUIRE(d->k_chunks >= 0 && d->k_chunks <= 8, "k_chunks must be 0..8");
+  SB_REQUIRE(d->plan_rows >= 0 && d->plan_rows < (1LL << 31) && d->plan_k_chunks >= 0 && d->plan_k_chunks <= 8,
+             "plan_rows must be >= 0 and plan_k_chunks 0..8");
+  r.k_chunks = d->k_chunks;
+  r.plan_rows = static_cast<int>(d->plan_rows);
+  r.plan_chunks = d->plan_k_chunks;
+  SB_REQUIRE(d->y_fp32 == 0 || d->y_fp32 == 1, "y_fp32 must be 0 or 1");
+  r.y_f32 = d->y_fp32 != 0;
+  SB_REQUIRE(d->scales_ld >= 0 && d->scales_ld < (1LL << 31), "scales_ld must be >= 0");
+  r.scales_ld = static_cast<int>(d->scales_ld);
+  r.plan_out = plan_out;
   return run_linear(r, as_stream(stream));
+}
+}  // namespace
+
+extern "C" int sb_linear_ex(const sb_linear_ex_desc* d, void* stream) { return linear_ex(d, stream, nullptr); }
+
+extern "C" int sb_linear_ex_plan(const sb_linear_ex_desc* d, int* plan) {
+  SB_REQUIRE(plan != nullptr, "null plan array");
+  return linear_ex(d, nullptr, plan);
 }
 
 extern "C" int sb_kv_append_int8(const void* k_new, const void* v_new, int8_t* k_cache, void* k_scale,

@@ -581,7 +581,8 @@ size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int6
 int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int8_t* v, const void* v_scale,
                   void* out, int64_t batch, int num_heads, int num_kv_heads, int64_t length, int64_t capacity,
                   int head_dim, float scale, void* workspace, size_t workspace_bytes, cudaStream_t stream,
-                  int force_splits, const int* length_dev, int length_offset, int early = 0) {
+                  int force_splits, const int* length_dev, int length_offset, int early = 0,
+                  int plan_kv_heads = 0) {
   SB_REQUIRE(head_dim == kSdpaD, "this build supports head_dim 128");
   SB_REQUIRE(batch > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
              "Nonempty inputs and query heads divisible by KV heads required");
@@ -594,7 +595,9 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
              "q, k and v must be 16-byte aligned");
   const bool bulk = capacity % 16 == 0 &&
                     ((reinterpret_cast<uintptr_t>(k_scale) | reinterpret_cast<uintptr_t>(v_scale)) & 15) == 0;
-  const SdpaPlan plan = sdpa_plan(batch, num_kv_heads, length, kSdpaWarpsUsed);
+  // plan_kv_heads > 0: split the tokens as for that many KV heads (a tensor-
+  // parallel shard planning like the unsharded model, so its heads merge alike)
+  const SdpaPlan plan = sdpa_plan(batch, plan_kv_heads > 0 ? plan_kv_heads : num_kv_heads, length, kSdpaWarpsUsed);
   int splits = force_splits > 0 ? force_splits : plan.splits;
   SB_REQUIRE(splits <= kMaxSplits, "at most 64 token splits");
   const int64_t bkv = batch * num_kv_heads;
@@ -752,9 +755,11 @@ extern "C" int sb_int8_sdpa_decode_dev(const void* q, const int8_t* k, const voi
                                        const void* v_scale, void* out, int64_t batch, int num_heads,
                                        int num_kv_heads, const int32_t* lengths, int length_offset,
                                        int64_t max_length, int64_t capacity, int head_dim, float scale,
-                                       int prefix_constant, void* workspace, size_t workspace_bytes, void* stream) {
+                                       int prefix_constant, int plan_kv_heads, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
   SB_REQUIRE(lengths != nullptr, "lengths must be a device pointer");
+  SB_REQUIRE(plan_kv_heads >= 0, "plan_kv_heads must be >= 0");
   return sb::run_sdpa_int8(q, k, k_scale, v, v_scale, out, batch, num_heads, num_kv_heads, max_length, capacity,
                            head_dim, scale, workspace, workspace_bytes, sb::as_stream(stream), 0, lengths,
-                           length_offset, prefix_constant);
+                           length_offset, prefix_constant, plan_kv_heads);
 }

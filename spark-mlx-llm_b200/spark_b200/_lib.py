@@ -76,6 +76,11 @@ class sb_linear_ex_desc(ctypes.Structure):
         ("ar_channel", _int),
         ("ar_buffers", _c_void_p * 8),
         ("activation", _int),
+        ("k_chunks", _int),
+        ("plan_rows", _i64),
+        ("plan_k_chunks", _int),
+        ("y_fp32", _int),
+        ("scales_ld", _i64),
     ]
 
 
@@ -174,6 +179,7 @@ SIGNATURES = {
     # decoder header
     "sb_linear_ex": (_int, [ctypes.POINTER(sb_linear_ex_desc), _c_void_p]),
     "sb_linear_ex_workspace_size": (_size, [ctypes.POINTER(sb_linear_ex_desc)]),
+    "sb_linear_ex_plan": (_int, [ctypes.POINTER(sb_linear_ex_desc), ctypes.POINTER(ctypes.c_int)]),
     "sb_kv_append_int8": (
         _int,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _i64, _int, _i64,
@@ -182,7 +188,7 @@ SIGNATURES = {
     "sb_int8_sdpa_decode_dev": (
         _int,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _c_void_p, _int,
-         _i64, _i64, _int, _float, _int, _c_void_p, _size, _c_void_p],
+         _i64, _i64, _int, _float, _int, _int, _c_void_p, _size, _c_void_p],
     ),
     "sb_embed_rows": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _c_void_p]),
     "sb_decode_advance": (_int, [_c_void_p, _c_void_p, _c_void_p, _int, _int, _c_void_p]),

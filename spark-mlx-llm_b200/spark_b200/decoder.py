@@ -44,6 +44,8 @@ BF16 = 0
 STATUS_WORD = 128 * 1024 // 4 - 1
 # prompt tokens per batched prefill chunk (the reference's prompt chunk, generation.py:78)
 PREFILL_CHUNK = 512
+# fixed K chunks of the row-split projections: the largest tensor-parallel degree
+TP_CHUNKS = 8
 
 
 @dataclass(frozen=True)
@@ -94,10 +96,18 @@ class SyntheticDecoder:
 
     ``rank``/``world`` select the tensor-parallel shard; ``group`` is the
     ``torch.distributed`` process group used for the all-reduces (None for 1 GPU).
+
+    ``invariant`` (launch engine) fixes every floating-point summation order
+    independently of ``world``, so greedy tokens are bit-identical at TP
+    1/2/4/8: the column-split GEMVs (QKV, gate/up, lm_head) split K as for the
+    unsharded matrix, the row-split o/down projections sum K in 8 fixed chunks
+    added in a balanced tree (a rank holds 8/world of them; the fused exchange
+    adds the ranks' partials in the same tree), and attention splits its tokens
+    as for all KV heads.
     """
 
     def __init__(self, config, *, batch, capacity, device="cuda", seed=0, rank=0, world=1, group=None,
-                 engine="auto"):
+                 engine="auto", invariant=True):
         cfg = config
         self.cfg = cfg
         self.batch = batch
@@ -116,6 +126,14 @@ class SyntheticDecoder:
         # TP: o/down partial sums meet inside the GEMV epilogue (NVLink peer
         # stores) instead of an NCCL all-reduce and a residual-add launch
         self.fused_allreduce = world > 1 and world <= 8
+        # K chunks of the unsharded o/down projections (1: no fixed chunking)
+        self.k_chunks = 1
+        if invariant and TP_CHUNKS % world == 0:
+            o_k, down_k = cfg.num_heads * cfg.head_dim, cfg.intermediate
+            if (o_k % (TP_CHUNKS * 64) == 0 and (o_k // TP_CHUNKS) % 16 == 0
+                    and down_k % (TP_CHUNKS * cfg.mlp_group) == 0 and (down_k // TP_CHUNKS) % 32 == 0):
+                self.k_chunks = TP_CHUNKS
+        self.invariant = invariant
         if engine not in ("auto", "step", "launches"):
             raise ValueError("engine must be 'auto', 'step' or 'launches'")
         self._build_weights(seed)
@@ -177,6 +195,16 @@ class SyntheticDecoder:
             wd = randn(cfg.hidden, cfg.intermediate, std=cfg.weight_std, key=base + 7)
             wd = wd[:, sp.down_cols[0]:sp.down_cols[0] + sp.down_cols[1]].contiguous()
             layer["down"] = quantize.quantize_affine_minmax(wd, cfg.mlp_group, 4)
+            # the decode GEMV's copy of the scale/bias tables, rows padded to a
+            # multiple of 8 groups (16 bytes) so a shard's tables stream by TMA
+            groups = layer["down"][1].shape[1]
+            ld = -(-groups // 8) * 8
+            pads = []
+            for t in layer["down"][1:]:
+                pad = torch.zeros(t.shape[0], ld, dtype=t.dtype, device=dev)
+                pad[:, :groups] = t
+                pads.append(pad)
+            layer["down_tables"], layer["down_ld"] = pads, ld
             del wd
             layer["in_norm"] = (1.0 + 0.1 * randn(cfg.hidden, std=1.0, key=base + 8)).to(torch.bfloat16)
             layer["post_norm"] = (1.0 + 0.1 * randn(cfg.hidden, std=1.0, key=base + 9)).to(torch.bfloat16)
@@ -211,7 +239,8 @@ class SyntheticDecoder:
         self._setup_exchange()
         self._build_descs()
         sizes = [lib().sb_linear_ex_workspace_size(ctypes.byref(desc)) for desc in self._descs_all()]
-        sizes.append(lib().sb_int8_sdpa_workspace_size(b, self.hq, self.hkv, self.capacity, d))
+        # attention plans its token splits as for the unsharded heads (invariant)
+        sizes.append(lib().sb_int8_sdpa_workspace_size(b, cfg.num_heads, cfg.num_kv_heads, self.capacity, d))
         self.workspace = torch.zeros(max(sizes) + 256, dtype=torch.uint8, device=dev)
         for desc in self._descs_all():
             desc.workspace = self.workspace.data_ptr()
@@ -281,6 +310,12 @@ class SyntheticDecoder:
         cfg, b = self.cfg, self.batch
         d = cfg.head_dim
         tp = self.world > 1
+        chunks = self.k_chunks // self.world
+        plan_chunks = self.k_chunks if self.k_chunks > 1 else 0
+
+        def plan(rows):  # column-split shards plan their K split as the whole matrix
+            return rows if self.invariant else 0
+
         self.descs = []
         for layer in self.layers:
             qkv = self._desc(x=_ptr(self.x), M=b, N=(self.hq + 2 * self.hkv) * d, K=cfg.hidden,
@@ -288,7 +323,7 @@ class SyntheticDecoder:
                              norm_weight=_ptr(layer["in_norm"]), epilogue=SB_EPI_ROPE,
                              positions=_ptr(self.positions), num_heads=self.hq, num_kv_heads=self.hkv, head_dim=d,
                              seq_len=1, rope_base=cfg.rope_theta, q_out=_ptr(self.q), k_out=_ptr(self.k_new),
-                             v_out=_ptr(self.v_new))
+                             v_out=_ptr(self.v_new), plan_rows=plan((cfg.num_heads + 2 * cfg.num_kv_heads) * d))
             if self.fused_append:
                 # the QKV kernel quantizes K/V straight into this layer's INT8 cache
                 li = len(self.descs)
@@ -300,18 +335,22 @@ class SyntheticDecoder:
             o = self._desc(x=_ptr(self.attn), M=b, N=cfg.hidden, K=self.hq * d, weight_format=SB_WEIGHT_INT8_PC,
                            weight=_ptr(layer["o_w"]), scales=_ptr(layer["o_s"]),
                            epilogue=SB_EPI_STORE if tp else SB_EPI_RESID,
-                           y=_ptr(self.part if tp else self.x), residual=_ptr(self.x))
+                           y=_ptr(self.part if tp else self.x), residual=_ptr(self.x), k_chunks=chunks,
+                           plan_k_chunks=plan_chunks)
             gw, gs, gb = layer["gate"]
             uw, us, ub = layer["up"]
             gateup = self._desc(x=_ptr(self.x), M=b, N=self.inter, K=cfg.hidden, weight_format=SB_WEIGHT_AFFINE4,
                                 weight=_ptr(gw), scales=_ptr(gs), biases=_ptr(gb), weight2=_ptr(uw),
                                 scales2=_ptr(us), biases2=_ptr(ub), group_size=cfg.mlp_group,
-                                norm_weight=_ptr(layer["post_norm"]), epilogue=SB_EPI_SWIGLU, y=_ptr(self.act))
-            dw, ds, db = layer["down"]
+                                norm_weight=_ptr(layer["post_norm"]), epilogue=SB_EPI_SWIGLU, y=_ptr(self.act),
+                                plan_rows=plan(cfg.intermediate))
+            dw = layer["down"][0]
+            ds, db = layer["down_tables"]
             down = self._desc(x=_ptr(self.act), M=b, N=cfg.hidden, K=self.inter, weight_format=SB_WEIGHT_AFFINE4,
                               weight=_ptr(dw), scales=_ptr(ds), biases=_ptr(db), group_size=cfg.mlp_group,
                               epilogue=SB_EPI_STORE if tp else SB_EPI_RESID,
-                              y=_ptr(self.part if tp else self.x), residual=_ptr(self.x))
+                              y=_ptr(self.part if tp else self.x), residual=_ptr(self.x), k_chunks=chunks,
+                              plan_k_chunks=plan_chunks, scales_ld=layer["down_ld"])
             if self.fused_allreduce:
                 self._allreduce_desc(o, 0)
                 self._allreduce_desc(down, 1)
@@ -319,7 +358,8 @@ class SyntheticDecoder:
         self.head_desc = self._desc(x=_ptr(self.x), M=b, N=self.vocab_shard, K=cfg.hidden,
                                     weight_format=SB_WEIGHT_BF16, weight=_ptr(self.head),
                                     norm_weight=_ptr(self.final_norm), epilogue=SB_EPI_ARGMAX,
-                                    argmax_keys=_ptr(self.keys), argmax_offset=self.plan.vocab_rows[0])
+                                    argmax_keys=_ptr(self.keys), argmax_offset=self.plan.vocab_rows[0],
+                                    plan_rows=plan(cfg.vocab))
 
     def _descs_all(self):
         out = [self.head_desc]
@@ -374,7 +414,8 @@ class SyntheticDecoder:
             check(L.sb_int8_sdpa_decode_dev(_ptr(self.q), _ptr(self.k_cache[li]), _ptr(self.k_scale[li]),
                                             _ptr(self.v_cache[li]), _ptr(self.v_scale[li]), _ptr(self.attn), b,
                                             self.hq, self.hkv, _ptr(self.positions), 1, self.capacity,
-                                            self.capacity, d, scale, 1, self.workspace.data_ptr(),
+                                            self.capacity, d, scale, 1,
+                                            cfg.num_kv_heads if self.invariant else 0, self.workspace.data_ptr(),
                                             self.workspace.numel(), stream), "int8_sdpa")
             check(L.sb_linear_ex(ctypes.byref(o), stream), "o_proj")
             if tp and not self.fused_allreduce:

@@ -22,7 +22,7 @@ def predictions(world, rank, group, device, steps=24, prompt_len=8, batch=2):
     gen = torch.Generator().manual_seed(11)
     prompt = torch.randint(0, cfg.vocab, (batch, prompt_len), generator=gen, dtype=torch.int32)
     forced = torch.randint(0, cfg.vocab, (steps, batch), generator=gen, dtype=torch.int32)
-    dec.prefill(prompt.to(device))
+    dec.prefill_stepwise(prompt.to(device))  # the same prompt path at every degree
     out = []
     for s in range(steps):
         dec.tokens.copy_(forced[s].to(device))
