@@ -536,6 +536,31 @@ def measure_ops(dev, peak_gbs, peak_tflops, peak_kind):
         rec(f"cfg3_int8_sdpa_b{bsz}_32k", cache + bsz * 32 * 128 * 4, us, 4.0 * bsz * 32 * ctx * 128,
             bound="hbm", batch=bsz, context=ctx, l2_copies=len(copies))
         del copies
+    # ---- the same decode attention at the reference model's head shape: 16/4 heads x 256, 32K tokens
+    for bsz in (1, 8):
+        cache = bsz * 4 * ctx * 516
+        copies = []
+        for _ in range(ncopies(cache) if cache < L2_ROTATE_BYTES else 1):
+            kc = torch.randint(-127, 128, (bsz, 4, ctx, 256), generator=g, device=dev, dtype=torch.int8)
+            vc = torch.randint(-127, 128, (bsz, 4, ctx, 256), generator=g, device=dev, dtype=torch.int8)
+            ks = (torch.rand(bsz, 4, ctx, generator=g, device=dev) * 0.02 + 0.005).half()
+            vs = (torch.rand(bsz, 4, ctx, generator=g, device=dev) * 0.02 + 0.005).half()
+            copies.append((kc, ks, vc, vs))
+        qv = torch.randn(bsz, 16, 1, 256, generator=g, device=dev).bfloat16()
+        o = torch.empty_like(qv)
+        wsb = L.sb_int8_sdpa_workspace_size(bsz, 16, 4, ctx, 256)
+        ws = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+        def launch(c, st, qv=qv, o=o, ws=ws, wsb=wsb, bsz=bsz):
+            kc, ks, vc, vs = c
+            check(L.sb_int8_sdpa_decode(qv.data_ptr(), kc.data_ptr(), ks.data_ptr(), vc.data_ptr(), vs.data_ptr(),
+                                        o.data_ptr(), bsz, 16, 4, ctx, ctx, 256, 256 ** -0.5, ws.data_ptr(), wsb,
+                                        st), "int8 sdpa d256")
+
+        us = _graph_us(dev, launch, copies)
+        rec(f"int8_sdpa_d256_b{bsz}_32k", cache + bsz * 16 * 256 * 4, us, 4.0 * bsz * 16 * ctx * 256,
+            bound="hbm", batch=bsz, context=ctx, heads="16/4 x 256", l2_copies=len(copies))
+        del copies
     # ---- INT8-KV prefill attention (chunked prompt): 32/8 heads x 128, causal over the int8 cache
     for q_len, length in ((1024, 1024), (512, 4096)):
         cap = length

@@ -152,7 +152,8 @@ size_t sb_qkv_rope_workspace_size(int64_t batch, int64_t seq_len, int64_t hidden
  *   k_scale, v_scale [B, KH, capacity] fp16; K[t] = k[t] * k_scale[t]
  *   out     [B, H, 1, D] BF16; attends to tokens 0..length-1 (the query is the last
  *   position, so the bottom-right causal mask keeps them all).
- *   D = 128; H % KH == 0 with H/KH in {1, 2, 4, 8}; softmax in fp32.
+ *   D = 128 or 256 (the reference model's 256: int8_quantized_sdpa.py:226-230);
+ *   H % KH == 0 with H/KH in {1, 2, 4, 8}; softmax in fp32.
  */
 int sb_int8_sdpa_decode(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
                         const void* v_scale, void* out, int64_t batch, int num_heads,

@@ -23,7 +23,7 @@ int fail(int status, const std::string& message) {
   return status;
 }
 
-size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int64_t length);
+size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int64_t length, int D);
 
 // ------------------------------------------------------------ TMA descriptors
 namespace {

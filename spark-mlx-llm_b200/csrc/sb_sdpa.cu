@@ -36,14 +36,14 @@ namespace sb {
 // 32K-token case (16 warps: fewer CTAs and one 200 KB ring per SM), so the
 // launch plan uses 8.
 constexpr int kSdpaWarpsUsed = 8;
-constexpr int kSdpaD = 128;
-constexpr int kPartStride = kSdpaD + 4;  // O[D], then m, l
+// head dims 128 and 256 (a K/V row is one or two 128-byte TMA boxes)
+constexpr int part_stride(int D) { return D + 4; }  // O[D], then m, l
 constexpr int kSdpaStages = 3;           // 16-token blocks in flight per warp
 constexpr int kMaxSplits = 64;           // token splits per (batch, kv head)
-constexpr int kSdpaStageBytes = 2 * 16 * kSdpaD;  // swizzled K box + V box
+constexpr int stage_bytes(int D) { return 2 * 16 * D; }  // swizzled K boxes + V boxes of 16 tokens
 constexpr int kSdpaScaleBytes = 64;                 // the block's 16 K scales + 16 V scales (fp16)
-constexpr size_t sdpa_smem(int warps, int stages) {
-  return 2048 + static_cast<size_t>(warps) * stages * (kSdpaStageBytes + kSdpaScaleBytes);
+constexpr size_t sdpa_smem(int warps, int stages, int D) {
+  return 2048 + static_cast<size_t>(warps) * stages * (stage_bytes(D) + kSdpaScaleBytes);
 }
 
 struct SdpaParams {
@@ -59,7 +59,7 @@ struct SdpaParams {
   const int* length_dev;  // optional per-batch lengths in device memory (+ length_offset)
   int length_offset;
   float scale_log2e;
-  float* partial;      // [B*KH][splits][G][kPartStride] (global merge)
+  float* partial;      // [B*KH][splits][G][D + 4] (global merge)
   unsigned* counters;  // [B*KH]
   unsigned* status;    // device status word or null
   int cluster;         // 1: the splits of a (b, kv head) form a cluster and merge in shared memory
@@ -69,8 +69,8 @@ struct SdpaParams {
 };
 
 constexpr int kSdpaMaxClusterSplits = 16;
-// cluster merge buffer: [split][G][slice + 2] floats, slice = ceil(128 / splits)
-constexpr int kSdpaClusterBuf = 8 * kSdpaD + 3 * 8 * kSdpaMaxClusterSplits;
+// cluster merge buffer: [split][G][slice + 2] floats, slice = ceil(D / splits)
+constexpr int cluster_buf(int D) { return 8 * D + 3 * 8 * kSdpaMaxClusterSplits; }
 
 // m16n8k16 fp16 MMA keeping only rows 0-7 of the accumulator tile: rows 8-15
 // (zero A rows here) start from zero and are discarded, so they hold no
@@ -88,8 +88,12 @@ __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-template <int G, bool kBulk, int kSdpaWarps>
-__global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_decode_kernel(const __grid_constant__ SdpaParams p) {
+template <int G, bool kBulk, int kSdpaWarps, int D>
+__global__ void __launch_bounds__(kSdpaWarps * 32, D == 128 ? 16 / kSdpaWarps : 1)
+    sdpa_int8_decode_kernel(const __grid_constant__ SdpaParams p) {
+  constexpr int kBoxes = D / 128;           // 128-byte TMA boxes per K/V row
+  constexpr int kStageBytes = stage_bytes(D);
+  constexpr int kPartStride = part_stride(D);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
   const int split = blockIdx.x;
   const int bkv = blockIdx.y;
@@ -111,10 +115,10 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
 
   // ---- running state (row g of the MMA tiles; rows g+8 are unused padding)
   float m_run = -INFINITY, l_run = 0.f;
-  float acc[16][2];  // rows g (the heads) of each 16 x 8 tile; rows g + 8 are padding
+  float acc[16 * kBoxes][2];  // rows g (the heads) of each 16 x 8 tile; rows g + 8 are padding
   float psum[2] = {0.f, 0.f};
 #pragma unroll
-  for (int j = 0; j < 16; ++j)
+  for (int j = 0; j < 16 * kBoxes; ++j)
 #pragma unroll
     for (int e = 0; e < 2; ++e) acc[j][e] = 0.f;
   constexpr uint32_t kOnes = 0x3C003C00u;
@@ -125,18 +129,22 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   uint8_t* sbase = smem_dyn + ((1024u - (smem_u32(smem_dyn) & 1023u)) & 1023u);
   const int NS = p.stages;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sbase) + warp * NS;
-  uint8_t* ring = sbase + 1024 + warp * NS * kSdpaStageBytes;
+  uint8_t* ring = sbase + 1024 + warp * NS * kStageBytes;
   // per-warp ring of the blocks' scales: [stage][k 16 x fp16 | v 16 x fp16]
-  uint8_t* sring = sbase + 1024 + kSdpaWarps * NS * kSdpaStageBytes + warp * NS * kSdpaScaleBytes;
+  uint8_t* sring = sbase + 1024 + kSdpaWarps * NS * kStageBytes + warp * NS * kSdpaScaleBytes;
   const int nb = blk_end - blk_begin;
   const int my_blocks = nb > warp ? (nb - warp + kSdpaWarps - 1) / kSdpaWarps : 0;
   auto block_of = [&](int i) { return blk_begin + warp + i * kSdpaWarps; };
   auto issue = [&](int i, int slot) {
     const int row = static_cast<int>(kv_base) + block_of(i) * 16;
-    uint8_t* dst = ring + slot * kSdpaStageBytes;
-    mbar_arrive_expect_tx(bars + slot, kSdpaStageBytes + (kBulk ? kSdpaScaleBytes : 0));
-    tma_load_2d(dst, &p.kmap, 0, row, bars + slot);
-    tma_load_2d(dst + 16 * kSdpaD, &p.vmap, 0, row, bars + slot);
+    uint8_t* dst = ring + slot * kStageBytes;
+    mbar_arrive_expect_tx(bars + slot, kStageBytes + (kBulk ? kSdpaScaleBytes : 0));
+    // [K box 0 | K box 1 ..][V box 0 | V box 1 ..], 16 rows x 128 B each
+#pragma unroll
+    for (int x = 0; x < kBoxes; ++x) {
+      tma_load_2d(dst + x * 2048, &p.kmap, 128 * x, row, bars + slot);
+      tma_load_2d(dst + 16 * D + x * 2048, &p.vmap, 128 * x, row, bars + slot);
+    }
     if constexpr (kBulk) {
       uint8_t* sdst = sring + slot * kSdpaScaleBytes;
       bulk_copy_g2s(sdst, p.ks + row, 32, bars + slot);
@@ -162,12 +170,13 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   // ---- q fragments: row g = query head kvh*G + g, k-slot d = 32t + 4s + {0..3}
   const bool head_ok = g < G;
   const int head = kvh * G + (head_ok ? g : 0);
-  const __nv_bfloat16* qrow = p.q + (static_cast<size_t>(b) * p.kv_heads * G + head) * kSdpaD + 32 * t;
-  float qv[32];
+  // (box x: d = 128x + 32t + 4s + {0..3}; qv[32x + ...])
+  const __nv_bfloat16* qrow = p.q + (static_cast<size_t>(b) * p.kv_heads * G + head) * D + 32 * t;
+  float qv[32 * kBoxes];
   {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 w = *reinterpret_cast<const uint4*>(qrow + 8 * i);
+    for (int i = 0; i < 4 * kBoxes; ++i) {
+      const uint4 w = *reinterpret_cast<const uint4*>(qrow + 128 * (i >> 2) + 8 * (i & 3));
       const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -178,7 +187,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   }
   float qmax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; ++i) qmax = fmaxf(qmax, fabsf(qv[i]));
+  for (int i = 0; i < 32 * kBoxes; ++i) qmax = fmaxf(qmax, fabsf(qv[i]));
   qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 1));
   qmax = fmaxf(qmax, __shfl_xor_sync(0xffffffffu, qmax, 2));
   int qexp = 0;
@@ -186,10 +195,10 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   const float up = qmax > 0.f ? ldexpf(1.0f, 15 - qexp) : 1.0f;     // |q*up| < 2^15
   const float down = qmax > 0.f ? ldexpf(1.0f, qexp - 15) : 1.0f;
   // A operand: a0 = slots (2t, 2t+1) -> d = 32t+4s+{0,1}; a2 = slots (2t+8, 2t+9) -> d = 32t+4s+{2,3}
-  uint32_t aq[8], aq2[8];
+  uint32_t aq[8 * kBoxes], aq2[8 * kBoxes];
   float qsum = 0.f;
 #pragma unroll
-  for (int s = 0; s < 8; ++s) {
+  for (int s = 0; s < 8 * kBoxes; ++s) {
     const __half2 lo = __floats2half2_rn(qv[4 * s] * up, qv[4 * s + 1] * up);
     const __half2 hi = __floats2half2_rn(qv[4 * s + 2] * up, qv[4 * s + 3] * up);
     aq[s] = head_ok ? *reinterpret_cast<const uint32_t*>(&lo) : 0u;
@@ -248,26 +257,29 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
       for (int j = 0; j < 4; ++j)
         if (tb + (j < 2 ? 2 * t + j : 2 * t + 6 + j) >= N) sv[j] = 0.f;  // rows past the length: any bits
     }
-    const uint8_t* kst = ring + slot * kSdpaStageBytes;
-    const uint8_t* vst = kst + 16 * kSdpaD;
+    const uint8_t* kst = ring + slot * kStageBytes;
+    const uint8_t* vst = kst + 16 * D;
     const int vt[4] = {tb + 2 * t, tb + 2 * t + 1, tb + 2 * t + 8, tb + 2 * t + 9};
 
     // QK^T: C[u] rows = heads, cols = tokens 8u + (2t, 2t+1); K row (8u + g), bytes 32t..32t+31
     float cqk[2][2];
 #pragma unroll
     for (int u = 0; u < 2; ++u) {
-      const uint4 ka = *reinterpret_cast<const uint4*>(swz128(kst, 8 * u + g, 32 * t));
-      const uint4 kb = *reinterpret_cast<const uint4*>(swz128(kst, 8 * u + g, 32 * t + 16));
-      const uint32_t kw[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
 #pragma unroll
       for (int e = 0; e < 2; ++e) cqk[u][e] = 0.f;
 #pragma unroll
-      for (int s = 0; s < 8; ++s) {
-        const uint32_t w = kw[s] ^ 0x80808080u;
-        const uint32_t b0 = prmt(w, 0x64646464u, 0x4140u);
-        const uint32_t b1 = prmt(w, 0x64646464u, 0x4342u);
-        const uint32_t a[4] = {aq[s], 0u, aq2[s], 0u};
-        mma_16816_top(cqk[u], a, b0, b1);
+      for (int x = 0; x < kBoxes; ++x) {
+        const uint4 ka = *reinterpret_cast<const uint4*>(swz128(kst + x * 2048, 8 * u + g, 32 * t));
+        const uint4 kb = *reinterpret_cast<const uint4*>(swz128(kst + x * 2048, 8 * u + g, 32 * t + 16));
+        const uint32_t kw[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
+#pragma unroll
+        for (int s = 0; s < 8; ++s) {
+          const uint32_t w = kw[s] ^ 0x80808080u;
+          const uint32_t b0 = prmt(w, 0x64646464u, 0x4140u);
+          const uint32_t b1 = prmt(w, 0x64646464u, 0x4342u);
+          const uint32_t a[4] = {aq[8 * x + s], 0u, aq2[8 * x + s], 0u};
+          mma_16816_top(cqk[u], a, b0, b1);
+        }
       }
     }
     // scores (log2 domain) for tokens vt[0..3] = (u0: 2t, 2t+1), (u1: 2t+8, 2t+9)
@@ -292,7 +304,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
     // rescale only when some row's running maximum moved (alpha == 1 exactly otherwise)
     if (__any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
+      for (int j = 0; j < 16 * kBoxes; ++j)
 #pragma unroll
         for (int e = 0; e < 2; ++e) acc[j][e] *= alpha;
 #pragma unroll
@@ -306,20 +318,24 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
     ap[3] = 0u;
     mma_16816_top(psum, ap, kOnes, kOnes);
     // P'V: n-tile j covers d = 16n + j; the lane's B column n = g reads bytes 16g..16g+15
-    const uint4 vr0 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t, 16 * g));
-    const uint4 vr1 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t + 1, 16 * g));
-    const uint4 vr2 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t + 8, 16 * g));
-    const uint4 vr3 = *reinterpret_cast<const uint4*>(swz128(vst, 2 * t + 9, 16 * g));
-    const uint32_t va[4] = {vr0.x, vr0.y, vr0.z, vr0.w}, vb[4] = {vr1.x, vr1.y, vr1.z, vr1.w};
-    const uint32_t vc[4] = {vr2.x, vr2.y, vr2.z, vr2.w}, vd[4] = {vr3.x, vr3.y, vr3.z, vr3.w};
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t sel = static_cast<uint32_t>(j & 3) | (static_cast<uint32_t>(4 + (j & 3)) << 8);
-      uint32_t b0 = prmt(va[j >> 2], vb[j >> 2], sel);
-      uint32_t b1 = prmt(vc[j >> 2], vd[j >> 2], sel);
-      b0 = (b0 & 0x00FF00FFu) ^ 0x64806480u;
-      b1 = (b1 & 0x00FF00FFu) ^ 0x64806480u;
-      mma_16816_top(acc[j], ap, b0, b1);
+    for (int x = 0; x < kBoxes; ++x) {
+      const uint8_t* vbx = vst + x * 2048;  // d = 128x + 16n + j
+      const uint4 vr0 = *reinterpret_cast<const uint4*>(swz128(vbx, 2 * t, 16 * g));
+      const uint4 vr1 = *reinterpret_cast<const uint4*>(swz128(vbx, 2 * t + 1, 16 * g));
+      const uint4 vr2 = *reinterpret_cast<const uint4*>(swz128(vbx, 2 * t + 8, 16 * g));
+      const uint4 vr3 = *reinterpret_cast<const uint4*>(swz128(vbx, 2 * t + 9, 16 * g));
+      const uint32_t va[4] = {vr0.x, vr0.y, vr0.z, vr0.w}, vb[4] = {vr1.x, vr1.y, vr1.z, vr1.w};
+      const uint32_t vc[4] = {vr2.x, vr2.y, vr2.z, vr2.w}, vd[4] = {vr3.x, vr3.y, vr3.z, vr3.w};
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const uint32_t sel = static_cast<uint32_t>(j & 3) | (static_cast<uint32_t>(4 + (j & 3)) << 8);
+        uint32_t b0 = prmt(va[j >> 2], vb[j >> 2], sel);
+        uint32_t b1 = prmt(vc[j >> 2], vd[j >> 2], sel);
+        b0 = (b0 & 0x00FF00FFu) ^ 0x64806480u;
+        b1 = (b1 & 0x00FF00FFu) ^ 0x64806480u;
+        mma_16816_top(acc[16 * x + j], ap, b0, b1);
+      }
     }
     if constexpr (!kBulk) {
 #pragma unroll
@@ -351,16 +367,18 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   __shared__ float s_m[kSdpaWarps][8], s_l[kSdpaWarps][8];
   // the warp's partial O [8][D] goes to its own (drained) ring: warp w at ring_of(w)
   auto o_of = [&](int w) {
-    return reinterpret_cast<float*>(sbase + 1024 + w * NS * kSdpaStageBytes);
+    return reinterpret_cast<float*>(sbase + 1024 + w * NS * kStageBytes);
   };
   __syncwarp();
   if (head_ok) {
-    float* ow = o_of(warp) + g * kSdpaD;
+    float* ow = o_of(warp) + g * D;
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      ow[32 * t + j] = acc[j][0] - 1152.0f * psum[0];
-      ow[32 * t + 16 + j] = acc[j][1] - 1152.0f * psum[1];
-    }
+    for (int x = 0; x < kBoxes; ++x)
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        ow[128 * x + 32 * t + j] = acc[16 * x + j][0] - 1152.0f * psum[0];
+        ow[128 * x + 32 * t + 16 + j] = acc[16 * x + j][1] - 1152.0f * psum[1];
+      }
     if (t == 0) {
       s_m[warp][g] = m_run;
       s_l[warp][g] = l_run;
@@ -373,11 +391,11 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   // (m, l, o) over the head dimension in distributed shared memory; rank r
   // merges dims [r*SL, (r+1)*SL) of every head in split order
   if (p.cluster) {
-    __shared__ float s_cred[kSdpaClusterBuf];
-    const int S = p.splits, SL = (kSdpaD + S - 1) / S, stride = SL + 2;
+    __shared__ float s_cred[cluster_buf(D)];
+    const int S = p.splits, SL = (D + S - 1) / S, stride = SL + 2;
     const uint32_t cred = smem_u32(s_cred);
-    for (int idx = threadIdx.x; idx < G * kSdpaD; idx += kSdpaWarps * 32) {
-      const int hh = idx / kSdpaD, d = idx % kSdpaD;
+    for (int idx = threadIdx.x; idx < G * D; idx += kSdpaWarps * 32) {
+      const int hh = idx / D, d = idx % D;
       float mm = -INFINITY;
 #pragma unroll
       for (int w = 0; w < kSdpaWarps; ++w) mm = fmaxf(mm, s_m[w][hh]);
@@ -387,7 +405,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
         for (int w = 0; w < kSdpaWarps; ++w) {
           const float f = s_m[w][hh] == -INFINITY ? 0.f : exp2f(s_m[w][hh] - mm);
           ll += s_l[w][hh] * f;
-          oo += o_of(w)[hh * kSdpaD + d] * f;
+          oo += o_of(w)[hh * D + d] * f;
         }
       }
       const int r = d / SL;
@@ -403,7 +421,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
     cluster_sync_all();
     for (int idx = threadIdx.x; idx < G * SL; idx += kSdpaWarps * 32) {
       const int hh = idx / SL, dl = idx % SL, d = split * SL + dl;
-      if (d >= kSdpaD) continue;
+      if (d >= D) continue;
       float mm = -INFINITY;
       for (int src = 0; src < S; ++src) mm = fmaxf(mm, s_cred[(src * G + hh) * stride + SL]);
       float ll = 0.f, oo = 0.f;
@@ -415,7 +433,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
           oo += s_cred[(src * G + hh) * stride + dl] * w;
         }
       }
-      p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] =
+      p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * D + d] =
           __float2bfloat16_rn(ll > 0.f ? oo / ll : 0.f);
     }
     return;
@@ -424,8 +442,8 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   // ---- CTA merge (fixed warp order) -> partial or final output
   const bool single = p.splits == 1;
   float* part = p.partial + (static_cast<size_t>(bkv) * p.splits + split) * G * kPartStride;
-  for (int idx = threadIdx.x; idx < G * kSdpaD; idx += kSdpaWarps * 32) {
-    const int hh = idx / kSdpaD, d = idx % kSdpaD;
+  for (int idx = threadIdx.x; idx < G * D; idx += kSdpaWarps * 32) {
+    const int hh = idx / D, d = idx % D;
     float mm = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kSdpaWarps; ++w) mm = fmaxf(mm, s_m[w][hh]);
@@ -435,17 +453,17 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
       for (int w = 0; w < kSdpaWarps; ++w) {
         const float f = s_m[w][hh] == -INFINITY ? 0.f : exp2f(s_m[w][hh] - mm);
         ll += s_l[w][hh] * f;
-        oo += o_of(w)[hh * kSdpaD + d] * f;
+        oo += o_of(w)[hh * D + d] * f;
       }
     }
     if (single) {
       const float o = ll > 0.f ? oo / ll : 0.f;
-      p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] = __float2bfloat16_rn(o);
+      p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * D + d] = __float2bfloat16_rn(o);
     } else {
       part[hh * kPartStride + d] = oo;
       if (d == 0) {
-        part[hh * kPartStride + kSdpaD] = mm;
-        part[hh * kPartStride + kSdpaD + 1] = ll;
+        part[hh * kPartStride + D] = mm;
+        part[hh * kPartStride + D + 1] = ll;
       }
     }
   }
@@ -464,8 +482,8 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   __shared__ float s_mw[kMaxSplits][8], s_ls[kMaxSplits][8], s_norm[8];
   for (int idx = threadIdx.x; idx < p.splits * G; idx += kSdpaWarps * 32) {
     const int s = idx / G, hh = idx % G;
-    s_mw[s][hh] = __ldcg(all + (s * G + hh) * kPartStride + kSdpaD);
-    s_ls[s][hh] = __ldcg(all + (s * G + hh) * kPartStride + kSdpaD + 1);
+    s_mw[s][hh] = __ldcg(all + (s * G + hh) * kPartStride + D);
+    s_ls[s][hh] = __ldcg(all + (s * G + hh) * kPartStride + D + 1);
   }
   __syncthreads();
   if (threadIdx.x < G) {
@@ -483,7 +501,7 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
   __syncthreads();
   // every output of this thread loads its next kBatch splits together: one
   // round trip per kBatch splits, not per split and output
-  constexpr int kOut = (G * kSdpaD + kSdpaWarps * 32 - 1) / (kSdpaWarps * 32);
+  constexpr int kOut = (G * D + kSdpaWarps * 32 - 1) / (kSdpaWarps * 32);
   constexpr int kBatch = 32 / kOut;
   float oo[kOut];
 #pragma unroll
@@ -493,14 +511,14 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
 #pragma unroll
     for (int o = 0; o < kOut; ++o) {
       const int idx = threadIdx.x + o * kSdpaWarps * 32;
-      const int hh = idx / kSdpaD, d = idx % kSdpaD;
+      const int hh = idx / D, d = idx % D;
 #pragma unroll
       for (int j = 0; j < kBatch; ++j)
-        v[o][j] = (idx < G * kSdpaD && s0 + j < p.splits) ? __ldcg(all + ((s0 + j) * G + hh) * kPartStride + d) : 0.f;
+        v[o][j] = (idx < G * D && s0 + j < p.splits) ? __ldcg(all + ((s0 + j) * G + hh) * kPartStride + d) : 0.f;
     }
 #pragma unroll
     for (int o = 0; o < kOut; ++o) {
-      const int hh = min((threadIdx.x + o * kSdpaWarps * 32) / kSdpaD, G - 1);
+      const int hh = min((threadIdx.x + o * kSdpaWarps * 32) / D, G - 1);
 #pragma unroll
       for (int j = 0; j < kBatch; ++j)
         if (s0 + j < p.splits) oo[o] += v[o][j] * s_mw[s0 + j][hh];
@@ -509,9 +527,9 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, 16 / kSdpaWarps) sdpa_int8_de
 #pragma unroll
   for (int o = 0; o < kOut; ++o) {
     const int idx = threadIdx.x + o * kSdpaWarps * 32;
-    if (idx >= G * kSdpaD) continue;
-    const int hh = idx / kSdpaD, d = idx % kSdpaD;
-    p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * kSdpaD + d] =
+    if (idx >= G * D) continue;
+    const int hh = idx / D, d = idx % D;
+    p.out[(static_cast<size_t>(b) * p.kv_heads * G + kvh * G + hh) * D + d] =
         __float2bfloat16_rn(oo[o] * s_norm[hh]);
   }
   if (threadIdx.x == 0) p.counters[bkv] = 0u;
@@ -544,12 +562,13 @@ int sdpa_sms() {
 struct SdpaPlan {
   int warps, splits;
 };
-SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int max_warps) {
+SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int max_warps, int D) {
   const int64_t bkv = batch * kv_heads;
   const int64_t nblk = (length + 15) / 16;
-  SdpaPlan pl{nblk >= 512 && max_warps >= 16 ? 16 : 8, 1};
+  SdpaPlan pl{nblk >= 512 && max_warps >= 16 && D == 128 ? 16 : 8, 1};
   const int64_t sms = sdpa_sms();
-  const int64_t slots = sms * (16 / pl.warps);
+  // head_dim 256: the ring of 16-token blocks fills one SM (one CTA each)
+  const int64_t slots = sms * (D == 128 ? 16 / pl.warps : 1);
   int64_t s = (slots + bkv - 1) / bkv;
   // a second wave of a few CTAs costs a whole CTA time: drop to one split less
   // when that still fills three quarters of the slots
@@ -564,18 +583,18 @@ SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int max_warps) {
   return pl;
 }
 // splits of the plan the launch uses (workspace sizing)
-int sdpa_splits(int64_t batch, int kv_heads, int64_t length) {
-  return sdpa_plan(batch, kv_heads, length, kSdpaWarpsUsed).splits;
+int sdpa_splits(int64_t batch, int kv_heads, int64_t length, int D) {
+  return sdpa_plan(batch, kv_heads, length, kSdpaWarpsUsed, D).splits;
 }
 
 }  // namespace
 
-size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int64_t length) {
-  const int splits = sdpa_splits(batch, num_kv_heads, length);
+size_t sdpa_workspace_bytes(int64_t batch, int num_heads, int num_kv_heads, int64_t length, int D) {
+  const int splits = sdpa_splits(batch, num_kv_heads, length, D);
   const int64_t bkv = batch * num_kv_heads;
   const int G = num_heads / num_kv_heads;
   const size_t counters = kCounterBytes;
-  return counters + static_cast<size_t>(bkv) * splits * G * kPartStride * sizeof(float);
+  return counters + static_cast<size_t>(bkv) * splits * G * part_stride(D) * sizeof(float);
 }
 
 int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int8_t* v, const void* v_scale,
@@ -583,7 +602,7 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
                   int head_dim, float scale, void* workspace, size_t workspace_bytes, cudaStream_t stream,
                   int force_splits, const int* length_dev, int length_offset, int early = 0,
                   int plan_kv_heads = 0) {
-  SB_REQUIRE(head_dim == kSdpaD, "this build supports head_dim 128");
+  SB_REQUIRE(head_dim == 128 || head_dim == 256, "head_dim must be 128 or 256");
   SB_REQUIRE(batch > 0 && num_heads > 0 && num_kv_heads > 0 && num_heads % num_kv_heads == 0,
              "Nonempty inputs and query heads divisible by KV heads required");
   const int G = num_heads / num_kv_heads;
@@ -597,7 +616,8 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
                     ((reinterpret_cast<uintptr_t>(k_scale) | reinterpret_cast<uintptr_t>(v_scale)) & 15) == 0;
   // plan_kv_heads > 0: split the tokens as for that many KV heads (a tensor-
   // parallel shard planning like the unsharded model, so its heads merge alike)
-  const SdpaPlan plan = sdpa_plan(batch, plan_kv_heads > 0 ? plan_kv_heads : num_kv_heads, length, kSdpaWarpsUsed);
+  const SdpaPlan plan =
+      sdpa_plan(batch, plan_kv_heads > 0 ? plan_kv_heads : num_kv_heads, length, kSdpaWarpsUsed, head_dim);
   int splits = force_splits > 0 ? force_splits : plan.splits;
   SB_REQUIRE(splits <= kMaxSplits, "at most 64 token splits");
   const int64_t bkv = batch * num_kv_heads;
@@ -608,7 +628,7 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
     SB_REQUIRE(force_splits <= 1, "a forced split count needs at most 32752 (batch x kv head) rows");
     splits = 1;
   }
-  const size_t need = counters + static_cast<size_t>(bkv) * splits * G * kPartStride * sizeof(float);
+  const size_t need = counters + static_cast<size_t>(bkv) * splits * G * part_stride(head_dim) * sizeof(float);
   if (splits > 1 && (workspace == nullptr || workspace_bytes < need)) {
     SB_REQUIRE(force_splits <= 0, "workspace too small for the requested split count");
     splits = 1;
@@ -628,8 +648,8 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   {
     const uint64_t rows = static_cast<uint64_t>(bkv) * static_cast<uint64_t>(capacity);
     if (rows >= (1ULL << 31)) return fail(SB_EINVAL, "KV cache too large for 32-bit TMA row coordinates");
-    if (int st = make_tmap_rows(&p.kmap, k, rows, kSdpaD, 16)) return st;
-    if (int st = make_tmap_rows(&p.vmap, v, rows, kSdpaD, 16)) return st;
+    if (int st = make_tmap_rows(&p.kmap, k, rows, head_dim, 16)) return st;
+    if (int st = make_tmap_rows(&p.vmap, v, rows, head_dim, 16)) return st;
   }
   p.length_offset = length_offset;
   p.scale_bulk = bulk ? 1 : 0;
@@ -646,7 +666,7 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   // Ring depth: 3 blocks per warp. (A 6-deep ring when the grid leaves one CTA
   // per SM measured slower on B200 at batch 1 / 32K tokens: 52 vs 40 us.)
   p.stages = kSdpaStages;
-  const size_t smem = sdpa_smem(plan.warps, p.stages);
+  const size_t smem = sdpa_smem(plan.warps, p.stages, head_dim);
   auto go = [&](auto kernel) -> int {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
         cudaSuccess)
@@ -664,14 +684,21 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
     if (p.cluster) return launch_cluster("int8 sdpa", kernel, grid, block, smem, splits, stream, p);
     return launch("int8 sdpa", kernel, grid, block, smem, stream, p);
   };
-  switch (G) {
-#define SB_SDPA_GO(GG) \
-  return bulk ? go(sdpa_int8_decode_kernel<GG, true, 8>) : go(sdpa_int8_decode_kernel<GG, false, 8>);
-    case 1: SB_SDPA_GO(1)
-    case 2: SB_SDPA_GO(2)
-    case 4: SB_SDPA_GO(4)
-    default: SB_SDPA_GO(8)
+  switch (G * 1000 + head_dim) {
+#define SB_SDPA_GO(GG, DD)                                                                                  \
+  case GG * 1000 + DD:                                                                                     \
+    return bulk ? go(sdpa_int8_decode_kernel<GG, true, 8, DD>) : go(sdpa_int8_decode_kernel<GG, false, 8, DD>);
+    SB_SDPA_GO(1, 128)
+    SB_SDPA_GO(2, 128)
+    SB_SDPA_GO(4, 128)
+    SB_SDPA_GO(8, 128)
+    SB_SDPA_GO(1, 256)
+    SB_SDPA_GO(2, 256)
+    SB_SDPA_GO(4, 256)
+    SB_SDPA_GO(8, 256)
 #undef SB_SDPA_GO
+    default:
+      return fail(SB_EINVAL, "unsupported head_dim / GQA combination");
   }
 }
 
@@ -679,9 +706,10 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
 
 extern "C" size_t sb_int8_sdpa_workspace_size(int64_t batch, int num_heads, int num_kv_heads, int64_t length,
                                               int head_dim) {
-  if (batch <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || length <= 0 || head_dim != sb::kSdpaD)
+  if (batch <= 0 || num_kv_heads <= 0 || num_heads % num_kv_heads || length <= 0 ||
+      (head_dim != 128 && head_dim != 256))
     return 0;
-  return sb::sdpa_workspace_bytes(batch, num_heads, num_kv_heads, length);
+  return sb::sdpa_workspace_bytes(batch, num_heads, num_kv_heads, length, head_dim);
 }
 
 extern "C" int sb_int8_sdpa_decode(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
@@ -734,8 +762,8 @@ extern "C" int sb_int8_sdpa_decode_static(const void* q, const int8_t* k, const 
                                           float scale, void* stream) {
   SB_REQUIRE(batch > 0 && num_kv_heads > 0 && num_heads > 0 && num_heads % num_kv_heads == 0 && length > 0,
              "Nonempty inputs and query heads divisible by KV heads required");
-  SB_REQUIRE(head_dim == sb::kSdpaD, "this build supports head_dim 128");
-  const size_t need = sb::sdpa_workspace_bytes(batch, num_heads, num_kv_heads, length);
+  SB_REQUIRE(head_dim == 128 || head_dim == 256, "head_dim must be 128 or 256");
+  const size_t need = sb::sdpa_workspace_bytes(batch, num_heads, num_kv_heads, length, head_dim);
   if (need > kStaticScratchBytes)
     return sb::fail(SB_EINVAL, "sb_int8_sdpa_decode_static: this shape needs " + std::to_string(need) +
                                    " bytes of scratch but the static scratch holds " +

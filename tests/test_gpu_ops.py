@@ -245,6 +245,22 @@ def test_int8_sdpa_gqa_ratios(sb, g):
     assert_close(to_f32(out), expected, what="gqa")
 
 
+@pytest.mark.parametrize("bsz,n,capacity,g", [(1, 1000, 1008, 4), (4, 4096, 4096, 4), (2, 300, 304, 1),
+                                             (1, 33, 48, 2), (3, 2048, 2048, 8), (1, 32768, 32768, 4)])
+def test_int8_sdpa_decode_head_dim_256(sb, bsz, n, capacity, g):
+    """head_dim 256 (the reference model's attention: 16 q / 4 kv heads x 256,
+    ``int8_quantized_sdpa.py:226-230``): K/V rows as two 128-byte boxes."""
+    rng = np.random.default_rng(256 + bsz * 7 + n + g)
+    hkv, d = 4, 256
+    q = formats.round_bf16(rng.standard_normal((bsz, hkv * g, 1, d)).astype(np.float32))
+    kq, ks, vq, vs, kc, ksc, vc, vsc = make_kv(rng, bsz, hkv, n, d, capacity)
+    scale = 1.0 / np.sqrt(d)
+    expected = ref.sdpa_int8(q, kq, ks, vq, vs, scale, causal=True)
+    out = sb.int8_sdpa_decode(bf16_tensor(q), torch.from_numpy(kc).cuda(), torch.from_numpy(ksc).cuda(),
+                              torch.from_numpy(vc).cuda(), torch.from_numpy(vsc).cuda(), n, float(scale))
+    assert_close(to_f32(out), expected, what="int8 sdpa d256")
+
+
 def test_rms_norm(sb):
     rng = np.random.default_rng(5)
     x = formats.round_bf16(rng.standard_normal((3, 2560)).astype(np.float32))
