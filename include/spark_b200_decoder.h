@@ -156,13 +156,16 @@ int sb_kv_append_int8(const void* k_new, const void* v_new, int8_t* k_cache, voi
 /*
  * Batched-prompt split of a QKV projection: rows qkv[m, :] (stride ld,
  * [H + 2 KH heads x D] bf16, m = b * seq_len + l) -> query heads RoPE-rotated
- * (non-traditional half split, rope_dims = head_dim = 128, angle
- * positions[m] * rope_base^(-2i/rope_dims)) into q_out [B, seq_len, H, D];
+ * (non-traditional: feature i < rope_dims/2 pairs with i + rope_dims/2, angle
+ * positions[m] * rope_base^(-2i/rope_dims); features from rope_dims on are left
+ * as they are - partial rotary) into q_out [B, seq_len, H, D];
  * key heads rotated and value heads as they are, quantized into the INT8 cache
  * at positions[m] (the arithmetic of sb_kv_append_int8). Replaces the split,
  * RoPE and cache update of Attention.__call__ (spark_mlx_llm/model.py:172-193,
  * ops/qkv.py:140-177) for a prompt chunk. Rows whose position is outside
- * [0, capacity) write nothing to the cache.
+ * [0, capacity) write nothing to the cache. D = 64, 128 or 256; rope_dims even,
+ * 2..D. With seq_len = 1 it is the decode step's split + RoPE + cache append
+ * for shapes the fused QKV epilogue does not take (partial rotary, D = 256).
  */
 int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, void* q_out, int8_t* k_cache,
                       void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch, int64_t seq_len,
@@ -217,6 +220,17 @@ int sb_peer_buffer_free(void* ptr);
 
 /* out[r, :] = table[ids[r], :] (bf16 embedding rows). Replaces nn.Embedding
  * (spark_mlx_llm/model.py:296-305). */
+/*
+ * Rows of an MLX-affine quantized embedding table (nn.QuantizedEmbedding, the
+ * reference's quantized checkpoints; tied to the lm_head): out[r, :] =
+ * bf16(scale * q + bias) of table row ids[r] (ids clamped to [0, vocab)).
+ *   weight uint32 [vocab, hidden * bits / 32], scales / biases bf16
+ *   [vocab, hidden / group_size]; bits 4 or 8, group_size 32, 64 or 128,
+ *   hidden a multiple of 8; out bf16 [rows, hidden].
+ */
+int sb_embed_rows_affine(const void* weight, const void* scales, const void* biases, const int32_t* ids, void* out,
+                         int64_t rows, int64_t hidden, int64_t vocab, int group_size, int bits, void* stream);
+
 int sb_embed_rows(const void* table, const int32_t* ids, void* out, int64_t rows, int64_t hidden, int64_t vocab,
                   void* stream);
 

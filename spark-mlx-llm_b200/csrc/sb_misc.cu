@@ -172,6 +172,43 @@ __global__ void embed_kernel(const __nv_bfloat16* __restrict__ table, const int*
   for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) dst[i] = src[i];
 }
 
+// One CTA per row of an MLX-affine quantized table: each thread dequantizes
+// 8 consecutive values (one 32-bit word of 4-bit codes, two of 8-bit codes;
+// element j of a word at bits [j*bits, (j+1)*bits)) as bf16(scale * q + bias).
+__global__ void embed_affine_kernel(const uint32_t* __restrict__ w, const __nv_bfloat16* __restrict__ scales,
+                                    const __nv_bfloat16* __restrict__ biases, const int* __restrict__ ids,
+                                    __nv_bfloat16* __restrict__ out, int hidden, int vocab, int group, int bits) {
+  grid_dependency_wait();
+  const int row = blockIdx.x;
+  int id = ids[row];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);
+  const int words = hidden * bits / 32, groups = hidden / group;
+  const uint32_t* wr = w + static_cast<size_t>(id) * words;
+  const __nv_bfloat16* sr = scales + static_cast<size_t>(id) * groups;
+  const __nv_bfloat16* br = biases + static_cast<size_t>(id) * groups;
+  for (int i = threadIdx.x; i < hidden / 8; i += blockDim.x) {
+    const int g = (8 * i) / group;
+    const float sc = __bfloat162float(sr[g]), bi = __bfloat162float(br[g]);
+    uint32_t q[8];
+    if (bits == 4) {
+      const uint32_t word = wr[i];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = (word >> (4 * j)) & 15u;
+    } else {
+      const uint32_t w0 = wr[2 * i], w1 = wr[2 * i + 1];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        q[j] = (w0 >> (8 * j)) & 255u;
+        q[4 + j] = (w1 >> (8 * j)) & 255u;
+      }
+    }
+    __align__(16) __nv_bfloat16 o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __float2bfloat16_rn(__fmaf_rn(sc, static_cast<float>(q[j]), bi));
+    *reinterpret_cast<uint4*>(out + static_cast<size_t>(row) * hidden + 8 * i) = *reinterpret_cast<const uint4*>(o);
+  }
+}
+
 // ------------------------------------------------------------ residual add
 __global__ void residual_add_kernel(__nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ y, int n) {
   grid_dependency_wait();
@@ -541,6 +578,23 @@ extern "C" int sb_embed_rows(const void* table, const int32_t* ids, void* out, i
   return launch("embed", embed_kernel, dim3(static_cast<unsigned>(rows)), dim3(128), 0, as_stream(stream),
                 static_cast<const __nv_bfloat16*>(table), ids, static_cast<__nv_bfloat16*>(out),
                 static_cast<int>(hidden), static_cast<int>(vocab));
+}
+
+extern "C" int sb_embed_rows_affine(const void* weight, const void* scales, const void* biases, const int32_t* ids,
+                                    void* out, int64_t rows, int64_t hidden, int64_t vocab, int group_size, int bits,
+                                    void* stream) {
+  SB_REQUIRE(weight && scales && biases && ids && out, "null pointer");
+  SB_REQUIRE(bits == 4 || bits == 8, "bits must be 4 or 8");
+  SB_REQUIRE(group_size == 32 || group_size == 64 || group_size == 128, "group_size must be 32, 64 or 128");
+  SB_REQUIRE(rows > 0 && rows < (1LL << 31) && vocab > 0 && vocab < (1LL << 31) && hidden > 0 &&
+                 hidden % group_size == 0 && hidden < (1LL << 24),
+             "bad embedding shape (hidden a multiple of group_size)");
+  SB_REQUIRE((reinterpret_cast<uintptr_t>(out) & 15) == 0 && (reinterpret_cast<uintptr_t>(weight) & 3) == 0,
+             "out must be 16-byte and weight 4-byte aligned");
+  return launch("embed_affine", embed_affine_kernel, dim3(static_cast<unsigned>(rows)), dim3(128), 0,
+                as_stream(stream), static_cast<const uint32_t*>(weight), static_cast<const __nv_bfloat16*>(scales),
+                static_cast<const __nv_bfloat16*>(biases), ids, static_cast<__nv_bfloat16*>(out),
+                static_cast<int>(hidden), static_cast<int>(vocab), group_size, bits);
 }
 
 extern "C" int sb_decode_advance(unsigned long long* argmax_keys, int32_t* tokens, int32_t* positions, int batch,

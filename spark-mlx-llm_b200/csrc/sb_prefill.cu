@@ -356,10 +356,16 @@ struct RopeParams {
   int8_t* v_cache;
   __half* v_scale;
   int rows, seq_len, heads, kv_heads, capacity, rope_pairs;
-  float inv_freq[kD / 2];
+  float inv_freq[128];  // theta^(-2i / rope_dims), i < rope_pairs
 };
 
+// One warp per (row, head) of the projected qkv: RoPE on the first 2 * rope_pairs
+// features of q and k heads (non-traditional: feature e < rope_pairs pairs with
+// e + rope_pairs), the rest unchanged; q heads to q_out, k/v heads quantized into
+// the INT8 cache (symmetric per token and head, fp16 scale = absmax / 127).
+template <int D>
 __global__ void rope_append_kernel(const __grid_constant__ RopeParams p) {
+  constexpr int E = D / 32;  // features per lane: e = lane + 32 t
   grid_dependency_wait();
   const int lane = threadIdx.x & 31;
   const int nh = p.heads + 2 * p.kv_heads;
@@ -368,49 +374,47 @@ __global__ void rope_append_kernel(const __grid_constant__ RopeParams p) {
   const int m = item / nh, j = item % nh;
   const int bi = m / p.seq_len;
   const int pos = p.positions[m];
-  const __nv_bfloat16* src = p.qkv + static_cast<size_t>(m) * p.ld + static_cast<size_t>(j) * kD;
-  float a[2], bb[2];
+  const __nv_bfloat16* src = p.qkv + static_cast<size_t>(m) * p.ld + static_cast<size_t>(j) * D;
+  const int half = p.rope_pairs;
+  float v[E];
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    const int i = lane + 32 * t;  // rotation pair (i, i + 64)
-    a[t] = __bfloat162float(src[i]);
-    bb[t] = __bfloat162float(src[i + kD / 2]);
-    if (j < p.heads + p.kv_heads && i < p.rope_pairs) {
+  for (int t = 0; t < E; ++t) v[t] = __bfloat162float(src[lane + 32 * t]);
+  if (j < p.heads + p.kv_heads) {
+#pragma unroll
+    for (int t = 0; t < E; ++t) {
+      const int e = lane + 32 * t;
+      if (e >= 2 * half) continue;
+      const bool lo = e < half;
+      const int i = lo ? e : e - half;  // rotation pair (i, i + half)
+      const float o = __bfloat162float(src[lo ? e + half : e - half]);
       float sn, cs;
       sincosf(static_cast<float>(pos) * p.inv_freq[i], &sn, &cs);
-      const float ra = a[t] * cs - bb[t] * sn, rb = bb[t] * cs + a[t] * sn;
-      a[t] = __bfloat162float(__float2bfloat16_rn(ra));
-      bb[t] = __bfloat162float(__float2bfloat16_rn(rb));
+      const float r = lo ? v[t] * cs - o * sn : v[t] * cs + o * sn;
+      v[t] = __bfloat162float(__float2bfloat16_rn(r));
     }
   }
   if (j < p.heads) {
-    __nv_bfloat16* dst = p.q_out + (static_cast<size_t>(m) * p.heads + j) * kD;
+    __nv_bfloat16* dst = p.q_out + (static_cast<size_t>(m) * p.heads + j) * D;
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      dst[lane + 32 * t] = __float2bfloat16_rn(a[t]);
-      dst[lane + 32 * t + kD / 2] = __float2bfloat16_rn(bb[t]);
-    }
+    for (int t = 0; t < E; ++t) dst[lane + 32 * t] = __float2bfloat16_rn(v[t]);
     return;
   }
   const bool is_k = j < p.heads + p.kv_heads;
   const int h = is_k ? j - p.heads : j - p.heads - p.kv_heads;
   if (pos < 0 || pos >= p.capacity) return;  // the host checks positions; never write outside the cache
-  float amax = fmaxf(fmaxf(fabsf(a[0]), fabsf(a[1])), fmaxf(fabsf(bb[0]), fabsf(bb[1])));
+  float amax = 0.f;
+#pragma unroll
+  for (int t = 0; t < E; ++t) amax = fmaxf(amax, fabsf(v[t]));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
   __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
   if (__half2float(s16) == 0.f) s16 = __float2half_rn(1.0f);
   const float sc = __half2float(s16);
   const size_t row = (static_cast<size_t>(bi) * p.kv_heads + h) * p.capacity + pos;
-  int8_t* dst = (is_k ? p.k_cache : p.v_cache) + row * kD;
-  auto code = [&](float x) {
-    return static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(x, sc)), -127.f), 127.f)));
-  };
+  int8_t* dst = (is_k ? p.k_cache : p.v_cache) + row * D;
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    dst[lane + 32 * t] = code(a[t]);
-    dst[lane + 32 * t + kD / 2] = code(bb[t]);
-  }
+  for (int t = 0; t < E; ++t)
+    dst[lane + 32 * t] = static_cast<int8_t>(static_cast<int>(fminf(fmaxf(rintf(__fdiv_rn(v[t], sc)), -127.f), 127.f)));
   if (lane == 0) (is_k ? p.k_scale : p.v_scale)[row] = s16;
 }
 
@@ -589,7 +593,8 @@ extern "C" int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* pos
                                  int64_t seq_len, int num_heads, int num_kv_heads, int head_dim, int64_t capacity,
                                  int rope_dims, float rope_base, void* stream) {
   SB_REQUIRE(qkv && positions && q_out && k_cache && k_scale && v_cache && v_scale, "null pointer");
-  SB_REQUIRE(head_dim == kD && rope_dims == kD, "head_dim and rope_dims must be 128");
+  SB_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, "head_dim must be 64, 128 or 256");
+  SB_REQUIRE(rope_dims >= 2 && rope_dims <= head_dim && rope_dims % 2 == 0, "rope_dims must be even, 2..head_dim");
   SB_REQUIRE(batch >= 1 && seq_len >= 1 && num_heads >= 1 && num_kv_heads >= 1, "shape");
   SB_REQUIRE(ld >= static_cast<int64_t>(num_heads + 2 * num_kv_heads) * head_dim, "qkv row stride too small");
   SB_REQUIRE(capacity >= 1 && capacity <= (1LL << 30), "capacity");
@@ -611,11 +616,14 @@ extern "C" int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* pos
   p.kv_heads = num_kv_heads;
   p.capacity = static_cast<int>(capacity);
   p.rope_pairs = rope_dims / 2;
-  for (int i = 0; i < kD / 2; ++i)
-    p.inv_freq[i] = static_cast<float>(std::pow(static_cast<double>(rope_base), -2.0 * i / rope_dims));
+  for (int i = 0; i < 128; ++i)
+    p.inv_freq[i] = i < rope_dims / 2 ? static_cast<float>(std::pow(static_cast<double>(rope_base), -2.0 * i / rope_dims))
+                                      : 0.f;
   constexpr int kWarpsPerBlock = 8;
-  return launch("rope_kv_append", rope_append_kernel, dim3(static_cast<unsigned>((items + kWarpsPerBlock - 1) / kWarpsPerBlock)),
-                dim3(32 * kWarpsPerBlock), 0, as_stream(stream), p);
+  const dim3 grid(static_cast<unsigned>((items + kWarpsPerBlock - 1) / kWarpsPerBlock)), block(32 * kWarpsPerBlock);
+  if (head_dim == 64) return launch("rope_kv_append", rope_append_kernel<64>, grid, block, 0, as_stream(stream), p);
+  if (head_dim == 128) return launch("rope_kv_append", rope_append_kernel<128>, grid, block, 0, as_stream(stream), p);
+  return launch("rope_kv_append", rope_append_kernel<256>, grid, block, 0, as_stream(stream), p);
 }
 
 extern "C" int sb_swiglu(const void* gate, const void* up, void* out, int64_t count, void* stream) {

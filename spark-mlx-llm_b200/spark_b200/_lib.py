@@ -179,6 +179,8 @@ SIGNATURES = {
     # decoder header
     "sb_linear_ex": (_int, [ctypes.POINTER(sb_linear_ex_desc), _c_void_p]),
     "sb_linear_ex_workspace_size": (_size, [ctypes.POINTER(sb_linear_ex_desc)]),
+    "sb_embed_rows_affine": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _i64, _int,
+                                    _int, _c_void_p]),
     "sb_linear_ex_plan": (_int, [ctypes.POINTER(sb_linear_ex_desc), ctypes.POINTER(ctypes.c_int)]),
     "sb_kv_append_int8": (
         _int,

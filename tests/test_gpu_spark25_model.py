@@ -1,0 +1,88 @@
+"""A Spark2_5 checkpoint (MLX-affine safetensors, head_dim 256, G32 4-bit and
+8-bit projections, head gate, GELU FFN, sliding and full layers, tied 4-bit
+embedding) loaded with ``spark_b200.spark25.load`` and decoded on the GPU,
+against the NumPy restatement of the reference block (``oracle/spark25.py``)
+fed the same tokens.
+
+Criteria (as for the config-4 decoder): the final hidden state after 4 layers
+is within the north-star per-op tolerance (|d| <= 2e-2 + 1e-2 |ref|) for all
+but 0.1 % of the elements and within 1.5x of it everywhere (a layer chains
+about ten bf16 rounding points and an INT8 KV quantizer); the logits equal the
+oracle's head (final RMSNorm + tied 4-bit lm_head) applied to the GPU's own
+hidden state within the tolerance, and the greedy token equals that head's
+argmax on every step whose top-1/top-2 gap is decisive (> 1e-3). The logits
+against the fully independent oracle run are not bounded: the tied head
+(unit-scale embedding rows over K = 512) multiplies bf16-ulp differences of
+the hidden state by about 20.
+"""
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from _spark25_ckpt import write_checkpoint  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+PROMPT, STEPS, BATCH = 14, 6, 2  # the prompt outruns the sliding window (12)
+
+
+def _err(got, want):
+    return np.abs(got - want) / (2e-2 + 1e-2 * np.abs(want))
+
+
+def test_spark25_checkpoint_decodes_like_the_oracle(tmp_path):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from oracle.spark25 import Spark25Oracle
+    from spark_b200 import spark25
+    from spark_b200.checkpoint import load_checkpoint_dir
+
+    write_checkpoint(tmp_path, seed=5)
+    model = spark25.load(tmp_path, batch=BATCH, capacity=64)
+    config, weights = load_checkpoint_dir(tmp_path)
+    orc = Spark25Oracle(model.cfg, spark25.sanitize(weights), BATCH)
+    rng = np.random.default_rng(7)
+    tokens = rng.integers(0, model.cfg.vocab_size, (BATCH, PROMPT))
+    worst, beyond, total, head_worst, checked = 0.0, 0, 0, 0.0, 0
+    for i in range(PROMPT + STEPS):
+        tok = tokens[:, i] if i < PROMPT else next_tok
+        got = model.step(torch.from_numpy(tok.astype(np.int32))).float().cpu().numpy()
+        orc.step(tok)
+        hidden = model.x.float().cpu().numpy()
+        e = _err(hidden, orc.last_hidden)
+        worst = max(worst, float(e.max()))
+        beyond += int((e > 1).sum())
+        total += e.size
+        want = orc.head(hidden)  # the head on the GPU's own hidden state
+        head_worst = max(head_worst, float(_err(got, want).max()))
+        next_tok = got.argmax(axis=-1)
+        top2 = np.sort(want, axis=-1)[:, -2:]
+        for bi in range(BATCH):
+            if top2[bi, 1] - top2[bi, 0] > 1e-3:
+                assert next_tok[bi] == want[bi].argmax(), (i, bi)
+                checked += 1
+    print({"hidden_worst_error_over_tolerance": worst, "hidden_beyond": beyond, "elements": total,
+           "head_worst_error_over_tolerance": head_worst, "decisive_tokens": checked})
+    assert worst <= 1.5
+    assert beyond <= 0.001 * total
+    assert head_worst <= 1.0
+    assert checked >= BATCH * (PROMPT + STEPS) - 2
+
+
+def test_spark25_rejects_incomplete_checkpoint(tmp_path):
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    import os
+
+    from spark_b200 import spark25
+    from spark_b200.checkpoint import read_safetensors, write_safetensors
+
+    write_checkpoint(tmp_path, shards=1)
+    shard = os.path.join(tmp_path, "model-00001-of-00001.safetensors")
+    t = {k: v for k, v in read_safetensors(shard).items() if k != "model.layers.2.mlp.up_proj.scales"}
+    t = {k: (dt, np.array(a)) for k, (dt, a) in t.items()}
+    write_safetensors(shard, t)
+    with pytest.raises((ValueError, KeyError)):
+        spark25.load(tmp_path, batch=1, capacity=32)
