@@ -167,6 +167,20 @@ int sb_kv_append_int8(const void* k_new, const void* v_new, int8_t* k_cache, voi
  * 2..D. With seq_len = 1 it is the decode step's split + RoPE + cache append
  * for shapes the fused QKV epilogue does not take (partial rotary, D = 256).
  */
+/*
+ * sb_rope_kv_append into a rotating cache (the sliding-window layers'
+ * RotatingKVCache, spark_mlx_llm/model.py:362-370, with keep = 0): position p
+ * is written to slot p % ring of each [capacity]-row head (ring <= capacity;
+ * RoPE still uses p; seq_len <= ring). Once p >= ring - 1 the slots [0, ring)
+ * hold exactly the last `ring` positions, so a decode query attends to slots
+ * [0, min(p + 1, ring)) - in slot order, which attention does not depend on
+ * beyond its fp32 summation order.
+ */
+int sb_rope_kv_append_ring(const void* qkv, int64_t ld, const int32_t* positions, void* q_out, int8_t* k_cache,
+                           void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch, int64_t seq_len,
+                           int num_heads, int num_kv_heads, int head_dim, int64_t capacity, int rope_dims,
+                           float rope_base, int64_t ring, void* stream);
+
 int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, void* q_out, int8_t* k_cache,
                       void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch, int64_t seq_len,
                       int num_heads, int num_kv_heads, int head_dim, int64_t capacity, int rope_dims,

@@ -356,6 +356,7 @@ struct RopeParams {
   int8_t* v_cache;
   __half* v_scale;
   int rows, seq_len, heads, kv_heads, capacity, rope_pairs;
+  int ring;  // > 0: the cache rows are a ring of `ring` slots (position p -> slot p % ring)
   float inv_freq[128];  // theta^(-2i / rope_dims), i < rope_pairs
 };
 
@@ -401,7 +402,8 @@ __global__ void rope_append_kernel(const __grid_constant__ RopeParams p) {
   }
   const bool is_k = j < p.heads + p.kv_heads;
   const int h = is_k ? j - p.heads : j - p.heads - p.kv_heads;
-  if (pos < 0 || pos >= p.capacity) return;  // the host checks positions; never write outside the cache
+  if (pos < 0 || (p.ring == 0 && pos >= p.capacity)) return;  // never write outside the cache
+  const int slot = p.ring > 0 ? pos % p.ring : pos;
   float amax = 0.f;
 #pragma unroll
   for (int t = 0; t < E; ++t) amax = fmaxf(amax, fabsf(v[t]));
@@ -410,7 +412,7 @@ __global__ void rope_append_kernel(const __grid_constant__ RopeParams p) {
   __half s16 = __float2half_rn(__fdiv_rn(amax, 127.0f));
   if (__half2float(s16) == 0.f) s16 = __float2half_rn(1.0f);
   const float sc = __half2float(s16);
-  const size_t row = (static_cast<size_t>(bi) * p.kv_heads + h) * p.capacity + pos;
+  const size_t row = (static_cast<size_t>(bi) * p.kv_heads + h) * p.capacity + slot;
   int8_t* dst = (is_k ? p.k_cache : p.v_cache) + row * D;
 #pragma unroll
   for (int t = 0; t < E; ++t)
@@ -588,10 +590,11 @@ extern "C" int sb_bf16_sdpa_multiquery(const void* q, const void* k, const void*
   return launch_any<true>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, as_stream(stream));
 }
 
-extern "C" int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, void* q_out,
-                                 int8_t* k_cache, void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch,
-                                 int64_t seq_len, int num_heads, int num_kv_heads, int head_dim, int64_t capacity,
-                                 int rope_dims, float rope_base, void* stream) {
+namespace {
+int rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, void* q_out, int8_t* k_cache,
+                   void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch, int64_t seq_len, int num_heads,
+                   int num_kv_heads, int head_dim, int64_t capacity, int rope_dims, float rope_base, int64_t ring,
+                   void* stream) {
   SB_REQUIRE(qkv && positions && q_out && k_cache && k_scale && v_cache && v_scale, "null pointer");
   SB_REQUIRE(head_dim == 64 || head_dim == 128 || head_dim == 256, "head_dim must be 64, 128 or 256");
   SB_REQUIRE(rope_dims >= 2 && rope_dims <= head_dim && rope_dims % 2 == 0, "rope_dims must be even, 2..head_dim");
@@ -616,6 +619,9 @@ extern "C" int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* pos
   p.kv_heads = num_kv_heads;
   p.capacity = static_cast<int>(capacity);
   p.rope_pairs = rope_dims / 2;
+  SB_REQUIRE(ring >= 0 && ring <= capacity, "ring must be 0 (linear cache) or 1..capacity slots");
+  SB_REQUIRE(ring == 0 || seq_len <= ring, "a chunk's positions must map to distinct ring slots (seq_len <= ring)");
+  p.ring = static_cast<int>(ring);
   for (int i = 0; i < 128; ++i)
     p.inv_freq[i] = i < rope_dims / 2 ? static_cast<float>(std::pow(static_cast<double>(rope_base), -2.0 * i / rope_dims))
                                       : 0.f;
@@ -624,6 +630,24 @@ extern "C" int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* pos
   if (head_dim == 64) return launch("rope_kv_append", rope_append_kernel<64>, grid, block, 0, as_stream(stream), p);
   if (head_dim == 128) return launch("rope_kv_append", rope_append_kernel<128>, grid, block, 0, as_stream(stream), p);
   return launch("rope_kv_append", rope_append_kernel<256>, grid, block, 0, as_stream(stream), p);
+}
+}  // namespace
+
+extern "C" int sb_rope_kv_append(const void* qkv, int64_t ld, const int32_t* positions, void* q_out,
+                                 int8_t* k_cache, void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch,
+                                 int64_t seq_len, int num_heads, int num_kv_heads, int head_dim, int64_t capacity,
+                                 int rope_dims, float rope_base, void* stream) {
+  return rope_kv_append(qkv, ld, positions, q_out, k_cache, k_scale, v_cache, v_scale, batch, seq_len, num_heads,
+                        num_kv_heads, head_dim, capacity, rope_dims, rope_base, 0, stream);
+}
+
+extern "C" int sb_rope_kv_append_ring(const void* qkv, int64_t ld, const int32_t* positions, void* q_out,
+                                      int8_t* k_cache, void* k_scale, int8_t* v_cache, void* v_scale, int64_t batch,
+                                      int64_t seq_len, int num_heads, int num_kv_heads, int head_dim,
+                                      int64_t capacity, int rope_dims, float rope_base, int64_t ring, void* stream) {
+  SB_REQUIRE(ring >= 1, "ring must be at least 1 slot");
+  return rope_kv_append(qkv, ld, positions, q_out, k_cache, k_scale, v_cache, v_scale, batch, seq_len, num_heads,
+                        num_kv_heads, head_dim, capacity, rope_dims, rope_base, ring, stream);
 }
 
 extern "C" int sb_swiglu(const void* gate, const void* up, void* out, int64_t count, void* stream) {

@@ -31,11 +31,12 @@
 
 namespace sb {
 
-// Warps per CTA. The kernel is written for 8 (two CTAs per SM) or 16 (one CTA
-// per SM); on B200 the 8-warp form measured faster at every batch size of the
-// 32K-token case (16 warps: fewer CTAs and one 200 KB ring per SM), so the
-// launch plan uses 8.
-constexpr int kSdpaWarpsUsed = 8;
+// Warps per CTA: head_dim 128 runs 6 (two CTAs per SM, up to 170 registers per
+// thread: no spills), head_dim 256 runs 8 (one CTA per SM: its ring of 8 KB
+// blocks fills the SM). Measured on B200 at head_dim 128 against 8 warps x 2
+// CTAs (128 registers, 150 bytes of spills): 32K tokens 0.61 -> 0.63 of HBM at
+// batch 8, 0.65 -> 0.66 at batch 32; 4K tokens at batch 8 0.40 -> 0.45.
+constexpr int sdpa_warps(int D) { return D == 128 ? 6 : 8; }
 // head dims 128 and 256 (a K/V row is one or two 128-byte TMA boxes)
 constexpr int part_stride(int D) { return D + 4; }  // O[D], then m, l
 constexpr int kSdpaStages = 3;           // 16-token blocks in flight per warp
@@ -552,9 +553,8 @@ int sdpa_sms() {
   return count;
 }
 
-// Launch plan: warps per CTA (16 allowed for long contexts when max_warps is
-// 16, one CTA per SM; else 8, two CTAs per SM) and token splits per (batch,
-// kv head): one wave of CTAs, raised to 16 splits (one thread-block cluster,
+// Launch plan: warps per CTA (sdpa_warps) and token splits per (batch, kv
+// head): one wave of CTAs (two per SM at head_dim 128, one at 256), raised to 16 splits (one thread-block cluster,
 // merged in distributed shared memory) when that still puts a CTA on most SMs,
 // at least two 16-token blocks per warp. (Measured on B200 at 32K tokens:
 // minimising waves per unit of work instead picked 9-15 splits for batch 8-32
@@ -562,13 +562,12 @@ int sdpa_sms() {
 struct SdpaPlan {
   int warps, splits;
 };
-SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int max_warps, int D) {
+SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int D) {
   const int64_t bkv = batch * kv_heads;
   const int64_t nblk = (length + 15) / 16;
-  SdpaPlan pl{nblk >= 512 && max_warps >= 16 && D == 128 ? 16 : 8, 1};
+  SdpaPlan pl{sdpa_warps(D), 1};
   const int64_t sms = sdpa_sms();
-  // head_dim 256: the ring of 16-token blocks fills one SM (one CTA each)
-  const int64_t slots = sms * (D == 128 ? 16 / pl.warps : 1);
+  const int64_t slots = sms * (D == 128 ? 2 : 1);
   int64_t s = (slots + bkv - 1) / bkv;
   // a second wave of a few CTAs costs a whole CTA time: drop to one split less
   // when that still fills three quarters of the slots
@@ -584,7 +583,7 @@ SdpaPlan sdpa_plan(int64_t batch, int kv_heads, int64_t length, int max_warps, i
 }
 // splits of the plan the launch uses (workspace sizing)
 int sdpa_splits(int64_t batch, int kv_heads, int64_t length, int D) {
-  return sdpa_plan(batch, kv_heads, length, kSdpaWarpsUsed, D).splits;
+  return sdpa_plan(batch, kv_heads, length, D).splits;
 }
 
 }  // namespace
@@ -617,7 +616,7 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   // plan_kv_heads > 0: split the tokens as for that many KV heads (a tensor-
   // parallel shard planning like the unsharded model, so its heads merge alike)
   const SdpaPlan plan =
-      sdpa_plan(batch, plan_kv_heads > 0 ? plan_kv_heads : num_kv_heads, length, kSdpaWarpsUsed, head_dim);
+      sdpa_plan(batch, plan_kv_heads > 0 ? plan_kv_heads : num_kv_heads, length, head_dim);
   int splits = force_splits > 0 ? force_splits : plan.splits;
   SB_REQUIRE(splits <= kMaxSplits, "at most 64 token splits");
   const int64_t bkv = batch * num_kv_heads;
@@ -687,7 +686,8 @@ int run_sdpa_int8(const void* q, const int8_t* k, const void* k_scale, const int
   switch (G * 1000 + head_dim) {
 #define SB_SDPA_GO(GG, DD)                                                                                  \
   case GG * 1000 + DD:                                                                                     \
-    return bulk ? go(sdpa_int8_decode_kernel<GG, true, 8, DD>) : go(sdpa_int8_decode_kernel<GG, false, 8, DD>);
+    return bulk ? go(sdpa_int8_decode_kernel<GG, true, sdpa_warps(DD), DD>)                                \
+                : go(sdpa_int8_decode_kernel<GG, false, sdpa_warps(DD), DD>);
     SB_SDPA_GO(1, 128)
     SB_SDPA_GO(2, 128)
     SB_SDPA_GO(4, 128)

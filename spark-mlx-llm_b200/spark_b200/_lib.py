@@ -161,6 +161,11 @@ SIGNATURES = {
         [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _int,
          _int, _int, _i64, _int, _float, _c_void_p],
     ),
+    "sb_rope_kv_append_ring": (
+        _int,
+        [_c_void_p, _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _int,
+         _int, _int, _i64, _int, _float, _i64, _c_void_p],
+    ),
     "sb_swiglu": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _c_void_p]),
     "sb_gated_activation": (_int, [_c_void_p, _c_void_p, _c_void_p, _i64, _int, _c_void_p]),
     "sb_head_gate": (_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64, _int, _int, _c_void_p]),

@@ -16,15 +16,18 @@ directory (``spark_mlx_llm/loader.py:65-120``) and run as a greedy decoder:
 Per token and layer this runs ``sb_rms_norm``, the weight-streaming affine GEMV
 (``sb_linear_ex``: 4- or 8-bit, groups 32/64/128, any projection shape),
 ``sb_rope_kv_append`` (RoPE on the first rope_dims features, K/V quantized into
-the BASELINE INT8 cache), ``sb_int8_sdpa_decode`` (head_dim 128 or 256; a
-sliding layer attends to its last ``sliding_window`` positions of the cache),
+the BASELINE INT8 cache; ``sb_rope_kv_append_ring`` for a sliding layer's
+rotating cache of ``sliding_window`` slots), ``sb_int8_sdpa_decode`` (head_dim
+128 or 256; a sliding layer attends to its ring's filled slots),
 ``sb_head_gate``, the residual epilogue of ``out_proj``, the paired gate/up GEMV
 with the fused RMSNorm and GELU gate, ``down`` with its residual, and the
 final RMSNorm fused into the (tied, quantized) lm_head GEMV. KV: the BASELINE
 symmetric INT8 format (one fp16 scale per token and head) instead of the
-reference's bf16 or affine uint8/G32 cache; the sliding layers keep a linear
-cache and attend to a window of it, which is the RotatingKVCache
-(``model.py:362-370``) attention with more memory.
+reference's bf16 or affine uint8/G32 cache. Sliding layers keep the
+RotatingKVCache of ``model.py:362-370`` (``max_size=sliding_window, keep=0``):
+position p lands in slot p % window, so the slots always hold the last
+``window`` positions (``rotating=False`` instead keeps every position and moves
+the attention start, the same keys in position order).
 """
 
 import ctypes
@@ -189,8 +192,9 @@ class Spark25Model:
     """A loaded Spark2_5 checkpoint with its INT8 KV cache and decode buffers;
     ``step(tokens)`` runs one greedy-decode position for ``batch`` sequences."""
 
-    def __init__(self, cfg, weights, *, batch=1, capacity=None, device="cuda"):
+    def __init__(self, cfg, weights, *, batch=1, capacity=None, device="cuda", rotating=True):
         self.cfg, self.batch = cfg, batch
+        self.rotating = rotating
         self.device = torch.device(device)
         self.capacity = ((capacity or cfg.max_position_embeddings) + 15) // 16 * 16
         weights = sanitize(weights, cfg.tie_word_embeddings)
@@ -250,10 +254,14 @@ class Spark25Model:
         self.logits = torch.zeros(b, cfg.vocab_size, **bf)
         self.tokens = torch.zeros(b, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(b, dtype=torch.int32, device=dev)
-        self.k_cache = [torch.zeros(b, hkv, self.capacity, d, dtype=torch.int8, device=dev) for _ in self.layers]
-        self.v_cache = [torch.zeros_like(self.k_cache[0]) for _ in self.layers]
-        self.k_scale = [torch.ones(b, hkv, self.capacity, dtype=torch.float16, device=dev) for _ in self.layers]
-        self.v_scale = [torch.ones_like(self.k_scale[0]) for _ in self.layers]
+        # rows per head: a sliding layer's ring holds sliding_window slots (rows rounded to 16)
+        ring = (cfg.sliding_window + 15) // 16 * 16
+        self.rows = [min(ring, self.capacity) if lay["sliding"] and self.rotating else self.capacity
+                     for lay in self.layers]
+        self.k_cache = [torch.zeros(b, hkv, r, d, dtype=torch.int8, device=dev) for r in self.rows]
+        self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
+        self.k_scale = [torch.ones(b, hkv, r, dtype=torch.float16, device=dev) for r in self.rows]
+        self.v_scale = [torch.ones_like(s) for s in self.k_scale]
         ws = lib().sb_int8_sdpa_workspace_size(b, hq, hkv, self.capacity, d)
         descs = []
         for lay in self.layers:
@@ -305,16 +313,22 @@ class Spark25Model:
                                 cfg.rms_norm_eps, stream), "input_layernorm")
             check(L.sb_linear_ex(ctypes.byref(lay["qkv_d"]), stream), "q_k_v_proj")
             kc, vc, ks, vs = self.k_cache[li], self.v_cache[li], self.k_scale[li], self.v_scale[li]
-            check(L.sb_rope_kv_append(_ptr(self.qkv), self.qkv.shape[1], _ptr(self.positions), _ptr(self.q),
-                                      _ptr(kc), _ptr(ks), _ptr(vc), _ptr(vs), b, 1, hq, hkv, d, self.capacity,
-                                      lay["rope_dims"], lay["rope_base"], stream), "rope + cache append")
-            # a sliding layer attends to its last sliding_window positions: the
-            # same cache rows with the start moved (row stride unchanged)
-            start = max(0, length - cfg.sliding_window) if lay["sliding"] else 0
-            n = length - start
+            rows = self.rows[li]
+            rotating = lay["sliding"] and self.rotating
+            args = (_ptr(self.qkv), self.qkv.shape[1], _ptr(self.positions), _ptr(self.q), _ptr(kc), _ptr(ks),
+                    _ptr(vc), _ptr(vs), b, 1, hq, hkv, d, rows, lay["rope_dims"], lay["rope_base"])
+            if rotating:  # the ring's slots hold the last sliding_window positions
+                check(L.sb_rope_kv_append_ring(*args, cfg.sliding_window, stream), "rope + ring cache append")
+                start, n = 0, min(length, cfg.sliding_window)
+            else:
+                check(L.sb_rope_kv_append(*args, stream), "rope + cache append")
+                # a sliding layer attends to its last sliding_window positions:
+                # the same cache rows with the start moved (row stride unchanged)
+                start = max(0, length - cfg.sliding_window) if lay["sliding"] else 0
+                n = length - start
             check(L.sb_int8_sdpa_decode(_ptr(self.q), kc.data_ptr() + start * d, ks.data_ptr() + 2 * start,
                                         vc.data_ptr() + start * d, vs.data_ptr() + 2 * start, _ptr(self.attn), b, hq,
-                                        hkv, n, self.capacity, d, scale, self.workspace.data_ptr(),
+                                        hkv, n, rows, d, scale, self.workspace.data_ptr(),
                                         self.workspace.numel(), stream), "attention")
             check(L.sb_head_gate(_ptr(self.xn), _ptr(lay["g"]), _ptr(self.attn), _ptr(self.gated), b,
                                  cfg.hidden_size, hq, d, stream), "head gate")
@@ -346,10 +360,11 @@ class Spark25Model:
         return torch.stack(out, dim=1).cpu()
 
 
-def load(path, *, batch=1, capacity=None, device="cuda", model_config: Optional[dict[str, Any]] = None):
+def load(path, *, batch=1, capacity=None, device="cuda", rotating=True,
+         model_config: Optional[dict[str, Any]] = None):
     """Load a Spark2_5 MLX-affine checkpoint directory (``loader.load``,
     ``spark_mlx_llm/loader.py:65-120``: ``config.json`` + ``model*.safetensors``)."""
     config, weights = load_checkpoint_dir(path)
     config = dict(config, **(model_config or {}))
     cfg = Spark25Config.from_dict(config)
-    return Spark25Model(cfg, weights, batch=batch, capacity=capacity, device=device)
+    return Spark25Model(cfg, weights, batch=batch, capacity=capacity, device=device, rotating=rotating)

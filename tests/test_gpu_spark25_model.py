@@ -32,7 +32,10 @@ def _err(got, want):
     return np.abs(got - want) / (2e-2 + 1e-2 * np.abs(want))
 
 
-def test_spark25_checkpoint_decodes_like_the_oracle(tmp_path):
+@pytest.mark.parametrize("rotating", [True, False])
+def test_spark25_checkpoint_decodes_like_the_oracle(tmp_path, rotating):
+    """``rotating``: sliding layers on a ring of sliding_window slots (the
+    reference's RotatingKVCache) or on a linear cache with a moving start."""
     if not torch.cuda.is_available():
         pytest.skip("needs a CUDA device")
     from oracle.spark25 import Spark25Oracle
@@ -40,7 +43,9 @@ def test_spark25_checkpoint_decodes_like_the_oracle(tmp_path):
     from spark_b200.checkpoint import load_checkpoint_dir
 
     write_checkpoint(tmp_path, seed=5)
-    model = spark25.load(tmp_path, batch=BATCH, capacity=64)
+    model = spark25.load(tmp_path, batch=BATCH, capacity=64, rotating=rotating)
+    if rotating:
+        assert model.k_cache[0].shape[2] == 16 and model.k_cache[3].shape[2] == 64  # ring vs full layer
     config, weights = load_checkpoint_dir(tmp_path)
     orc = Spark25Oracle(model.cfg, spark25.sanitize(weights), BATCH)
     rng = np.random.default_rng(7)
