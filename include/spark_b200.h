@@ -203,7 +203,8 @@ int sb_int8_sdpa_decode_static(const void* q, const int8_t* k, const void* k_sca
  * The queries are the last q_len of `length` positions; causal != 0 applies
  * the bottom-right mask (query l sees keys [0, length - q_len + l]), else every
  * query sees keys [0, length). Scores, softmax and accumulation in fp32; the
- * probabilities times the V scale are rounded to fp16 for P.V. D = 128, H/KH
+ * probabilities times the V scale are rounded to fp16 for P.V. D = 128 or 256
+ * (the reference's fused path is D = 256; q 16-byte aligned at 256), H/KH
  * in {1, 2, 4, 8}, q_len <= length <= capacity, K/V caches 16-byte aligned.
  * No workspace.
  */
@@ -224,7 +225,7 @@ int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* k_scale, co
  * position; mask != NULL - bytes [q_len, mask_ld] (nonzero = visible, shared by
  * every batch row and head). Scores, softmax and accumulation in fp32; the
  * probabilities enter P.V as a bf16 hi + lo pair. A query with no visible key
- * gets zeros. D = 128, H/KH in {1, 2, 4, 8}, 16-byte aligned K/V. No workspace.
+ * gets zeros. D = 128 or 256, H/KH in {1, 2, 4, 8}, 16-byte aligned K/V. No workspace.
  */
 int sb_bf16_sdpa_multiquery(const void* q, const void* k, const void* v, void* out, int64_t batch,
                             int num_heads, int num_kv_heads, int64_t q_len, int64_t length,

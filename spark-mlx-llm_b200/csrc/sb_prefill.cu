@@ -29,22 +29,35 @@
 namespace sb {
 namespace prefill {
 
-constexpr int kD = 128;
 constexpr int kRows = 64;        // query rows per CTA
-constexpr int kKeys = 64;        // keys per tile
 constexpr int kWarps = 4;        // 16 query rows each
 constexpr int kThreads = kWarps * 32;
-constexpr int kHStride = kD * 2 + 16;                // 16-bit tile row stride (bytes): ldmatrix without bank conflicts
-constexpr int kHTile = kKeys * kHStride;             // one 16-bit tile (K or V)
-constexpr int kRawTile = kKeys * kD;                 // one int8 tile (K or V)
-// INT8 KV: [K | V] 16-bit code tiles, [2 buffers][K | V] int8 tiles, the tile's K and V scales (fp32)
-constexpr int kOffKh = 0;
-constexpr int kOffVh = kHTile;
-constexpr int kOffRaw = 2 * kHTile;
-constexpr int kOffScale = kOffRaw + 2 * 2 * kRawTile;
-constexpr int kSmemI8 = kOffScale + 2 * kKeys * 4;
-// bf16 KV: [2 buffers][K | V] bf16 tiles, loaded straight into the padded layout
-constexpr int kSmemBf = 2 * 2 * kHTile;
+
+// Per head dimension D (128 or 256): keys per tile (64 at 128; 32 at 256, where
+// a warp's 16 x 256 fp32 accumulator alone takes 128 registers), the 16-bit tile
+// row stride (bytes; ldmatrix without bank conflicts) and the shared-memory
+// layout. At 256 the query tile stays in shared memory and each k step reads its
+// fragments with ldmatrix instead of holding all of them in registers.
+template <int D>
+struct Geo {
+  static constexpr int kKeys = D == 128 ? 64 : 32;
+  static constexpr bool kQSmem = D > 128;
+  static constexpr int kHStride = D * 2 + 16;
+  static constexpr int kHTile = kKeys * kHStride;  // one 16-bit tile (K or V)
+  static constexpr int kRawTile = kKeys * D;       // one int8 tile (K or V)
+  static constexpr int kQTile = kQSmem ? kRows * kHStride : 0;
+  // INT8 KV: [K | V] 16-bit code tiles, [2 buffers][K | V] int8 tiles, the
+  // tile's K and V scales (fp32), [the query tile]
+  static constexpr int kOffKh = 0;
+  static constexpr int kOffVh = kHTile;
+  static constexpr int kOffRaw = 2 * kHTile;
+  static constexpr int kOffScale = kOffRaw + 2 * 2 * kRawTile;
+  static constexpr int kOffQI8 = kOffScale + 2 * kKeys * 4;
+  static constexpr int kSmemI8 = kOffQI8 + kQTile;
+  // bf16 KV: [2 buffers][K | V] bf16 tiles (loaded straight into the padded layout), [the query tile]
+  static constexpr int kOffQBf = 2 * 2 * kHTile;
+  static constexpr int kSmemBf = kOffQBf + kQTile;
+};
 
 struct Params {
   const __nv_bfloat16* q;
@@ -97,8 +110,11 @@ __device__ __forceinline__ void codes_to_half(uint32_t w, uint32_t& lo, uint32_t
 
 // KVB: bf16 K/V (no scales; bf16 operands, probabilities as a bf16 hi + lo pair for P.V);
 // else INT8 codes + fp16 scales (fp16 code tiles, probabilities times the V scale in fp16).
-template <int G, bool KVB>
+template <int G, bool KVB, int D>
 __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant__ Params p) {
+  using C = Geo<D>;
+  constexpr int kD = D, kKeys = C::kKeys, kHStride = C::kHStride, kHTile = C::kHTile, kRawTile = C::kRawTile;
+  constexpr int kOffKh = C::kOffKh, kOffVh = C::kOffVh, kOffRaw = C::kOffRaw, kOffScale = C::kOffScale;
   extern __shared__ __align__(128) uint8_t sm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
   const int g = lane >> 2, c = lane & 3;
@@ -170,9 +186,25 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
   };
 
   // q rows of the warp as A fragments (fp16 for INT8 KV, bf16 as stored for bf16 KV;
-  // rows beyond the query count are zero)
-  uint32_t qa[8][4];
-  {
+  // rows beyond the query count are zero): in registers at D = 128, else the
+  // CTA's query tile in shared memory (the same values, read per k step)
+  uint32_t qa[C::kQSmem ? 1 : kD / 16][4];
+  const uint32_t q_base = smem_u32(sm + (KVB ? C::kOffQBf : C::kOffQI8));
+  if constexpr (C::kQSmem) {
+    uint8_t* qs = sm + (KVB ? C::kOffQBf : C::kOffQI8);
+    for (int i = tid; i < kRows * (kD / 8); i += kThreads) {
+      const int r = i / (kD / 8), ch = i % (kD / 8);
+      uint4 w = make_uint4(0u, 0u, 0u, 0u);
+      if (row0 + r < nrows) w = *reinterpret_cast<const uint4*>(p.q + qkv_offset(row0 + r) + ch * 8);
+      if constexpr (!KVB) {
+        w.x = pack_half2(bf16_lo(w.x), bf16_hi(w.x));
+        w.y = pack_half2(bf16_lo(w.y), bf16_hi(w.y));
+        w.z = pack_half2(bf16_lo(w.z), bf16_hi(w.z));
+        w.w = pack_half2(bf16_lo(w.w), bf16_hi(w.w));
+      }
+      *reinterpret_cast<uint4*>(qs + r * kHStride + ch * 16) = w;  // read after the loop's first barrier
+    }
+  } else {
     const __nv_bfloat16* qra = ra < nrows ? p.q + qkv_offset(ra) : nullptr;
     const __nv_bfloat16* qrb = rb < nrows ? p.q + qkv_offset(rb) : nullptr;
 #pragma unroll
@@ -186,9 +218,9 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
         qa[ks][2 * h + 1] = KVB ? wb : pack_half2(bf16_lo(wb), bf16_hi(wb));
       }
   }
-  float o[16][4];
+  float o[kD / 8][4];
 #pragma unroll
-  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  for (int n = 0; n < kD / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
 
   if (kt0 < ntiles) load_tile(kt0, kt0 & 1);
@@ -228,24 +260,39 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
       kh_base = smem_u32(sm + kOffKh);
       vh_base = smem_u32(sm + kOffVh);
     }
-    if (warp_live && key0 <= warp_last && (p.window <= 0 || key0 + kKeys > warp_first - p.window + 1)) {
+    // a warp skips the tiles its rows cannot see: past its last position (causal)
+    // or before its first window (sliding); without the causal mask every tile counts
+    if (warp_live && (!p.causal || key0 <= warp_last) &&
+        (p.window <= 0 || key0 + kKeys > warp_first - p.window + 1)) {
       // ---- scores S = q . K^T for the warp's 16 rows x 64 keys
-      float s[8][4];
+      float s[kKeys / 8][4];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
+      for (int nt = 0; nt < kKeys / 8; ++nt) s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.f;
 #pragma unroll
-      for (int ks2 = 0; ks2 < 4; ++ks2)
+      for (int ks2 = 0; ks2 < kD / 32; ++ks2) {
+        uint32_t qf[2][4];
+        if constexpr (C::kQSmem) {
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+          for (int h = 0; h < 2; ++h)
+            ldsm_x4(qf[h], q_base + (warp * 16 + (lane & 15)) * kHStride + ((2 * ks2 + h) * 16 + (lane >> 4) * 8) * 2);
+        }
+#pragma unroll
+        for (int nt = 0; nt < kKeys / 8; ++nt) {
           uint32_t bk[4];
           ldsm_x4(bk, kh_base + (nt * 8 + (lane & 7)) * kHStride + (ks2 * 32 + (lane >> 3) * 8) * 2);
-          mma_16816<!KVB>(s[nt], qa[2 * ks2], bk[0], bk[1]);
-          mma_16816<!KVB>(s[nt], qa[2 * ks2 + 1], bk[2], bk[3]);
+          if constexpr (C::kQSmem) {
+            mma_16816<!KVB>(s[nt], qf[0], bk[0], bk[1]);
+            mma_16816<!KVB>(s[nt], qf[1], bk[2], bk[3]);
+          } else {
+            mma_16816<!KVB>(s[nt], qa[2 * ks2], bk[0], bk[1]);
+            mma_16816<!KVB>(s[nt], qa[2 * ks2 + 1], bk[2], bk[3]);
+          }
         }
+      }
       // ---- scale, mask, online softmax (log2 domain)
       float mx[2] = {m_run[0], m_run[1]};
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt)
+      for (int nt = 0; nt < kKeys / 8; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int kk = nt * 8 + 2 * c + (e & 1);
@@ -268,16 +315,16 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
         l_run[i] *= corr[i];
       }
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
+      for (int n = 0; n < kD / 8; ++n) {
         o[n][0] *= corr[0];
         o[n][1] *= corr[0];
         o[n][2] *= corr[1];
         o[n][3] *= corr[1];
       }
       // probabilities as the A operand of P.V
-      uint32_t pa[4][4], pl[4][4];
+      uint32_t pa[kKeys / 16][4], pl[kKeys / 16][4];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < kKeys / 8; ++nt) {
         float pr[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -302,9 +349,9 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
       }
       // ---- O += P . V (V transposed by ldmatrix.trans)
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
+      for (int j = 0; j < kKeys / 16; ++j)
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
+        for (int np = 0; np < kD / 16; ++np) {
           uint32_t bv[4];
           ldsm_x4_trans(bv, vh_base + (j * 16 + ((lane >> 3) & 1) * 8 + (lane & 7)) * kHStride +
                                 (np * 16 + (lane >> 4) * 8) * 2);
@@ -331,7 +378,7 @@ __global__ void __launch_bounds__(kThreads) prefill_kernel(const __grid_constant
   __nv_bfloat16* oa = ra < nrows ? p.out + qkv_offset(ra) : nullptr;
   __nv_bfloat16* ob = rb < nrows ? p.out + qkv_offset(rb) : nullptr;
 #pragma unroll
-  for (int n = 0; n < 16; ++n) {
+  for (int n = 0; n < kD / 8; ++n) {
     const int d = n * 8 + 2 * c;
     if (oa) *reinterpret_cast<__nv_bfloat162*>(oa + d) = __floats2bfloat162_rn(o[n][0] * inv_a, o[n][1] * inv_a);
     if (ob) *reinterpret_cast<__nv_bfloat162*>(ob + d) = __floats2bfloat162_rn(o[n][2] * inv_b, o[n][3] * inv_b);
@@ -498,29 +545,39 @@ using namespace sb::prefill;
 
 namespace {
 
-template <int G, bool KVB>
+template <int G, bool KVB, int D>
 int launch_prefill(const Params& p, int batch, int kv_heads, cudaStream_t stream) {
-  constexpr int smem = KVB ? kSmemBf : kSmemI8;
+  constexpr int smem = KVB ? Geo<D>::kSmemBf : Geo<D>::kSmemI8;
   static bool attr_done = false;  // per template instance; the attribute is per function
   if (!attr_done) {
-    const cudaError_t e = cudaFuncSetAttribute(prefill_kernel<G, KVB>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    const cudaError_t e =
+        cudaFuncSetAttribute(prefill_kernel<G, KVB, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return fail(SB_ECUDA, std::string("prefill attention attribute: ") + cudaGetErrorString(e));
     attr_done = true;
   }
-  return launch(KVB ? "bf16_sdpa_multiquery" : "int8_sdpa_prefill", prefill_kernel<G, KVB>,
+  return launch(KVB ? "bf16_sdpa_multiquery" : "int8_sdpa_prefill", prefill_kernel<G, KVB, D>,
                 dim3(p.tiles, kv_heads, batch), dim3(kThreads), smem, stream, p);
 }
 
 template <bool KVB>
-int launch_any(Params& p, int64_t batch, int num_kv_heads, int G, int64_t q_len, cudaStream_t s) {
+int launch_any(Params& p, int64_t batch, int num_kv_heads, int G, int64_t q_len, int head_dim, cudaStream_t s) {
   const int64_t tiles = (q_len * G + kRows - 1) / kRows;
   SB_REQUIRE(tiles <= 0x7fffffff, "too many query rows");
   p.tiles = static_cast<int>(tiles);
+  const int b = static_cast<int>(batch);
+  if (head_dim == 256) {
+    switch (G) {
+      case 1: return launch_prefill<1, KVB, 256>(p, b, num_kv_heads, s);
+      case 2: return launch_prefill<2, KVB, 256>(p, b, num_kv_heads, s);
+      case 4: return launch_prefill<4, KVB, 256>(p, b, num_kv_heads, s);
+      default: return launch_prefill<8, KVB, 256>(p, b, num_kv_heads, s);
+    }
+  }
   switch (G) {
-    case 1: return launch_prefill<1, KVB>(p, static_cast<int>(batch), num_kv_heads, s);
-    case 2: return launch_prefill<2, KVB>(p, static_cast<int>(batch), num_kv_heads, s);
-    case 4: return launch_prefill<4, KVB>(p, static_cast<int>(batch), num_kv_heads, s);
-    default: return launch_prefill<8, KVB>(p, static_cast<int>(batch), num_kv_heads, s);
+    case 1: return launch_prefill<1, KVB, 128>(p, b, num_kv_heads, s);
+    case 2: return launch_prefill<2, KVB, 128>(p, b, num_kv_heads, s);
+    case 4: return launch_prefill<4, KVB, 128>(p, b, num_kv_heads, s);
+    default: return launch_prefill<8, KVB, 128>(p, b, num_kv_heads, s);
   }
 }
 
@@ -529,7 +586,7 @@ int common_params(Params& p, const void* q, const void* k, const void* v, void* 
                   int num_kv_heads, int64_t q_len, int64_t length, int64_t capacity, int head_dim, float scale,
                   int causal, int layout) {
   SB_REQUIRE(q && k && v && out, "null pointer");
-  SB_REQUIRE(head_dim == kD, "head_dim must be 128");
+  SB_REQUIRE(head_dim == 128 || head_dim == 256, "head_dim must be 128 or 256");
   SB_REQUIRE(batch >= 1 && batch <= 65535, "batch must be in [1, 65535]");
   SB_REQUIRE(num_kv_heads >= 1 && num_kv_heads <= 65535 && num_heads % num_kv_heads == 0, "heads");
   const int G = num_heads / num_kv_heads;
@@ -541,6 +598,7 @@ int common_params(Params& p, const void* q, const void* k, const void* v, void* 
              "the K/V caches must be 16-byte aligned");
   SB_REQUIRE(reinterpret_cast<uintptr_t>(q) % 4 == 0 && reinterpret_cast<uintptr_t>(out) % 4 == 0,
              "q and out must be 4-byte aligned");
+  SB_REQUIRE(head_dim == 128 || reinterpret_cast<uintptr_t>(q) % 16 == 0, "q must be 16-byte aligned at head_dim 256");
   p = Params{};
   p.q = static_cast<const __nv_bfloat16*>(q);
   p.k = k;
@@ -570,7 +628,7 @@ extern "C" int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* 
     return st;
   p.ks = static_cast<const __half*>(k_scale);
   p.vs = static_cast<const __half*>(v_scale);
-  return launch_any<false>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, as_stream(stream));
+  return launch_any<false>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, head_dim, as_stream(stream));
 }
 
 extern "C" int sb_bf16_sdpa_multiquery(const void* q, const void* k, const void* v, void* out, int64_t batch,
@@ -587,7 +645,7 @@ extern "C" int sb_bf16_sdpa_multiquery(const void* q, const void* k, const void*
   p.window = window;
   p.mask = mask;
   p.mask_ld = static_cast<int>(mask ? mask_ld : 0);
-  return launch_any<true>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, as_stream(stream));
+  return launch_any<true>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, head_dim, as_stream(stream));
 }
 
 namespace {

@@ -43,12 +43,18 @@ def _kv(rng, b, kh, cap, d):
 
 
 CASES = [
-    # batch, heads, kv_heads, q_len, length, causal, layout
+    # batch, heads, kv_heads, q_len, length, causal, layout[, head_dim (default 128)]
     (1, 32, 8, 200, 200, True, 0),
     (2, 8, 8, 70, 150, True, 1),
     (1, 16, 2, 33, 600, True, 0),
     (1, 8, 4, 17, 90, False, 0),
     (2, 32, 8, 129, 129, True, 1),
+    (1, 8, 8, 70, 150, False, 0),  # no mask: warps see keys past their own positions
+    # head_dim 256: the reference model's 16 / 4 heads (int8_quantized_sdpa.py:226-230)
+    (1, 16, 4, 200, 200, True, 0, 256),
+    (2, 16, 4, 45, 301, True, 1, 256),
+    (1, 8, 8, 37, 100, False, 0, 256),
+    (1, 16, 2, 130, 513, True, 0, 256),
 ]
 
 
@@ -57,8 +63,8 @@ def test_prefill_attention_matches_oracle(case):
     _need_cuda()
     from spark_b200._lib import check, lib
 
-    b, h, kh, ql, n, causal, layout = case
-    d, cap = 128, ((n + 15) // 16) * 16 + 16
+    b, h, kh, ql, n, causal, layout, *rest = case
+    d, cap = (rest[0] if rest else 128), ((n + 15) // 16) * 16 + 16
     rng = np.random.default_rng(sum(case[:5]))
     k, ks, v, vs = _kv(rng, b, kh, cap, d)
     q = torch.randn(b, h, ql, d, generator=torch.Generator().manual_seed(1)).to(torch.bfloat16)
@@ -182,11 +188,15 @@ def test_chunked_prompt_matches_oracle():
 
 # ------------------------------------------------------------ bf16 multi-query attention
 BF16_CASES = [
-    # batch, heads, kv_heads, q_len, length, causal, window, sliding mask (window of a boolean mask), layout
+    # batch, heads, kv_heads, q_len, length, causal, window, sliding mask (window of a boolean mask), layout[, head_dim]
     (1, 16, 4, 8, 519, False, 0, 128, 0),  # the reference's verification geometry at D = 128, boolean sliding mask
     (2, 8, 8, 33, 200, True, 64, 0, 1),
     (1, 32, 8, 1, 77, False, 0, 0, 0),
     (1, 8, 1, 70, 300, True, 0, 0, 0),
+    # head_dim 256
+    (1, 16, 4, 8, 519, False, 0, 128, 0, 256),
+    (2, 16, 4, 33, 200, True, 64, 0, 1, 256),
+    (1, 8, 2, 70, 300, True, 0, 0, 0, 256),
 ]
 
 
@@ -195,8 +205,8 @@ def test_bf16_multiquery_matches_oracle(case):
     _need_cuda()
     from spark_b200._lib import check, lib
 
-    b, h, kh, ql, n, causal, window, mwin, layout = case
-    d = 128
+    b, h, kh, ql, n, causal, window, mwin, layout, *rest = case
+    d = rest[0] if rest else 128
     gen = torch.Generator().manual_seed(sum(case[:5]))
     q = torch.randn(b, h, ql, d, generator=gen).to(torch.bfloat16)
     k = torch.randn(b, kh, n, d, generator=gen).to(torch.bfloat16)
