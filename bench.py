@@ -561,27 +561,30 @@ def measure_ops(dev, peak_gbs, peak_tflops, peak_kind):
         rec(f"int8_sdpa_d256_b{bsz}_32k", cache + bsz * 16 * 256 * 4, us, 4.0 * bsz * 16 * ctx * 256,
             bound="hbm", batch=bsz, context=ctx, heads="16/4 x 256", l2_copies=len(copies))
         del copies
-    # ---- INT8-KV prefill attention (chunked prompt): 32/8 heads x 128, causal over the int8 cache
-    for q_len, length in ((1024, 1024), (512, 4096)):
+    # ---- INT8-KV prefill attention (chunked prompt), causal over the int8 cache: 32/8 heads x 128
+    # (the synthetic model) and 16/4 heads x 256 (the reference model's shape)
+    for q_len, length, hq, hkv, d in ((1024, 1024, 32, 8, 128), (512, 4096, 32, 8, 128),
+                                      (1024, 1024, 16, 4, 256)):
         cap = length
-        kc = torch.randint(-127, 128, (1, 8, cap, 128), generator=g, device=dev, dtype=torch.int8)
-        vc = torch.randint(-127, 128, (1, 8, cap, 128), generator=g, device=dev, dtype=torch.int8)
-        ks = (torch.rand(1, 8, cap, generator=g, device=dev) * 0.02 + 0.005).half()
-        vs = (torch.rand(1, 8, cap, generator=g, device=dev) * 0.02 + 0.005).half()
-        qv = torch.randn(1, 32, q_len, 128, generator=g, device=dev).bfloat16()
+        kc = torch.randint(-127, 128, (1, hkv, cap, d), generator=g, device=dev, dtype=torch.int8)
+        vc = torch.randint(-127, 128, (1, hkv, cap, d), generator=g, device=dev, dtype=torch.int8)
+        ks = (torch.rand(1, hkv, cap, generator=g, device=dev) * 0.02 + 0.005).half()
+        vs = (torch.rand(1, hkv, cap, generator=g, device=dev) * 0.02 + 0.005).half()
+        qv = torch.randn(1, hq, q_len, d, generator=g, device=dev).bfloat16()
         o = torch.empty_like(qv)
 
-        def launch(c, st, qv=qv, o=o, q_len=q_len, length=length, cap=cap):
+        def launch(c, st, qv=qv, o=o, q_len=q_len, length=length, cap=cap, hq=hq, hkv=hkv, d=d):
             kc, ks, vc, vs = c
             check(L.sb_int8_sdpa_prefill(qv.data_ptr(), kc.data_ptr(), ks.data_ptr(), vc.data_ptr(), vs.data_ptr(),
-                                         o.data_ptr(), 1, 32, 8, q_len, length, cap, 128, 128 ** -0.5, 1, 0, st),
+                                         o.data_ptr(), 1, hq, hkv, q_len, length, cap, d, d ** -0.5, 1, 0, st),
                   "int8 prefill")
 
         us = _graph_us(dev, launch, [(kc, ks, vc, vs)])
         first = length - q_len  # keys seen by query l: first + l + 1
         pairs = q_len * first + q_len * (q_len + 1) // 2
-        rec(f"prefill_int8_attn_{q_len}x{length}", 8 * length * 260 + 2 * 32 * q_len * 128 * 2, us,
-            4.0 * 32 * 128 * pairs, bound="tensor", q_len=q_len, length=length, causal=True,
+        name = f"prefill_int8_attn_{q_len}x{length}" + ("" if d == 128 else f"_d{d}")
+        rec(name, hkv * length * (2 * d + 4) + 2 * hq * q_len * d * 2, us,
+            4.0 * hq * d * pairs, bound="tensor", q_len=q_len, length=length, causal=True, heads=f"{hq}/{hkv} x {d}",
             kernel="mma.sync m16n8k16 flash attention over int8 K/V (fp16 operands)")
         del kc, vc, ks, vs
     torch.cuda.synchronize(dev)
