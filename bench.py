@@ -561,6 +561,37 @@ def measure_ops(dev, peak_gbs, peak_tflops, peak_kind):
         rec(f"int8_sdpa_d256_b{bsz}_32k", cache + bsz * 16 * 256 * 4, us, 4.0 * bsz * 16 * ctx * 256,
             bound="hbm", batch=bsz, context=ctx, heads="16/4 x 256", l2_copies=len(copies))
         del copies
+    # ---- decode attention over the reference's own KV format (MLX affine uint8, group 32, scale and
+    # bias per group: int8_quantized_sdpa's inputs) at the reference model's 16/4 heads x 256
+    for ctx in (4096, 32768):
+        hq, hkv, d, grp = 16, 4, 256, 32
+        per_tok = 2 * (d + 2 * 2 * (d // grp))  # K and V: codes + bf16 scales and biases
+        cache = hkv * ctx * per_tok
+        copies = []
+        for _ in range(ncopies(cache) if cache < L2_ROTATE_BYTES else 1):
+            t = []
+            for _kv in range(2):
+                t.append(torch.randint(0, 2 ** 31 - 1, (1, hkv, ctx, d // 4), generator=g, device=dev,
+                                       dtype=torch.int32))
+                t.append((torch.rand(1, hkv, ctx, d // grp, generator=g, device=dev) * 0.02 + 0.005).bfloat16())
+                t.append((torch.rand(1, hkv, ctx, d // grp, generator=g, device=dev) * -1.0).bfloat16())
+            copies.append(tuple(t))
+        qv = torch.randn(1, hq, 1, d, generator=g, device=dev).bfloat16()
+        o = torch.empty_like(qv)
+        wsb = L.sb_affine_sdpa_workspace_size(1, hq, 1, ctx, d)
+        ws = torch.zeros(max(wsb, 1), dtype=torch.uint8, device=dev)
+
+        def launch(c, st, qv=qv, o=o, ws=ws, wsb=wsb, ctx=ctx, hq=hq, hkv=hkv, d=d, grp=grp):
+            kp, ksc, kb, vp, vsc, vb = c
+            check(L.sb_affine_sdpa(qv.data_ptr(), 0, kp.data_ptr(), ksc.data_ptr(), kb.data_ptr(), vp.data_ptr(),
+                                   vsc.data_ptr(), vb.data_ptr(), o.data_ptr(), 1, hq, hkv, 1, ctx, d, d, grp, 8,
+                                   d ** -0.5, 1, ws.data_ptr(), wsb, st), "affine sdpa")
+
+        us = _graph_us(dev, launch, copies)
+        rec(f"affine_u8g32_sdpa_d256_b1_{ctx // 1024}k", cache + hq * d * 4, us, 4.0 * hq * ctx * d, bound="hbm",
+            batch=1, context=ctx, heads="16/4 x 256", kv_format="MLX affine uint8 G32 (the reference's tuples)",
+            kernel="scalar CUDA (one thread per token per pass)", l2_copies=len(copies))
+        del copies
     # ---- INT8-KV prefill attention (chunked prompt), causal over the int8 cache: 32/8 heads x 128
     # (the synthetic model) and 16/4 heads x 256 (the reference model's shape)
     for q_len, length, hq, hkv, d in ((1024, 1024, 32, 8, 128), (512, 4096, 32, 8, 128),

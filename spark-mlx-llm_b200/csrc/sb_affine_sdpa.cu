@@ -8,7 +8,10 @@
 // int8_quantized_sdpa.py:178-180), with the bottom-right causal mask for
 // multi-token queries.
 //
-// Layout on B200: one CTA per (query row, token split). A thread scores one
+// Single-query decode of the common shapes (head_dim 64/128/256, 4- or 8-bit
+// codes, bf16/fp16) runs affine_decode_kernel (one CTA per KV head and token
+// split, below). Other shapes:
+// one CTA per (query row, token split). A thread scores one
 // token per pass (sum over groups of sk * sum(q*code) + bk * sum(q), the
 // reassociation of _int8_sdpa_sources.py); the CTA keeps an online softmax
 // over 128-token chunks and accumulates P*V with threads across the head
@@ -192,7 +195,222 @@ __global__ void __launch_bounds__(kAffSdpaThreads) affine_sdpa_kernel(const Affi
   if (tid == 0) p.counters[row] = 0u;
 }
 
+// ---- single-query decode (L = 1, dk = dv = D in {64, 128, 256}, 4- or 8-bit codes, bf16/fp16):
+// one CTA per (batch, KV head, token split) serves the KV head's G query heads,
+// so every K/V byte is read once. Warp w takes tokens t_begin + w + 8i in
+// groups of 4 (their loads issued together); lane l owns head dimensions
+// [E*l, E*l + E) (E = D / 32: coalesced row reads) and the scale/bias of their
+// group. A score is the lanes' partial sums (sk * sum(q*code) + bk * sum(q),
+// per lane) added by a butterfly, so every lane holds every head's score; the
+// online softmax is in fp32 (exp2); P.V accumulates per lane. Warps merge in
+// shared memory and splits through the workspace (the last CTA of a KV head
+// adds them in split order).
+constexpr int kAffDecWarps = 8;
+
+template <int BITS, int E>
+__device__ __forceinline__ void load_codes(const uint32_t* row, int lane, float (&c)[E]) {
+  constexpr int kBytes = E * BITS / 8;  // bytes of the lane's codes
+  const uint8_t* base = reinterpret_cast<const uint8_t*>(row) + lane * kBytes;
+  uint32_t w[2] = {0u, 0u};
+  if constexpr (kBytes == 8) {
+    const uint2 v = __ldg(reinterpret_cast<const uint2*>(base));
+    w[0] = v.x;
+    w[1] = v.y;
+  } else if constexpr (kBytes == 4) {
+    w[0] = __ldg(reinterpret_cast<const uint32_t*>(base));
+  } else if constexpr (kBytes == 2) {
+    w[0] = __ldg(reinterpret_cast<const uint16_t*>(base));
+  } else {
+    w[0] = __ldg(base);
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const int bit = e * BITS;
+    c[e] = static_cast<float>((w[bit >> 5] >> (bit & 31)) & ((1u << BITS) - 1u));
+  }
+}
+
+template <typename T, int BITS, int G, int D>
+__global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 512 ? 2 : 1)
+    affine_decode_kernel(const AffineSdpaParams p) {
+  constexpr int E = D / 32;
+  constexpr int kU = 4;  // tokens per warp iteration
+  extern __shared__ float dsm[];  // [warps][G][D] partial O, then [warps][G] m and l
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, bkv = blockIdx.y;
+  const int b = bkv / p.kv_heads, kh = bkv % p.kv_heads;
+  const int words = D * BITS / 32, ngroups = D / p.group;
+  const int lg = (E * lane) / p.group;  // the lane's group
+  grid_dependency_wait();
+  const int t_begin = static_cast<int>(static_cast<long long>(p.n) * split / p.splits);
+  const int t_end = static_cast<int>(static_cast<long long>(p.n) * (split + 1) / p.splits);
+  const float sl2 = p.scale * 1.4426950408889634f;
+
+  float q[G][E], qs[G];
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+    const size_t qrow = (static_cast<size_t>(b) * p.heads + kh * G + gi) * D + E * lane;
+    qs[gi] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      q[gi][e] = ldf<T>(p.q, qrow + e);
+      qs[gi] += q[gi][e];
+    }
+  }
+  float m_run[G], l_run[G], o[G][E];
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+    m_run[gi] = -INFINITY;
+    l_run[gi] = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[gi][e] = 0.f;
+  }
+  const size_t tok0 = static_cast<size_t>(bkv) * p.n;  // token 0 of this (b, kv head)
+  for (int t0 = t_begin + warp; t0 < t_end; t0 += kU * kAffDecWarps) {
+    float kc[kU][E], vc[kU][E], sk[kU], bk[kU], sv[kU], bv[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int t = t0 + u * kAffDecWarps;
+      const size_t tok = tok0 + (t < t_end ? t : t_begin);
+      load_codes<BITS, E>(p.kp + tok * words, lane, kc[u]);
+      load_codes<BITS, E>(p.vp + tok * words, lane, vc[u]);
+      sk[u] = ldf<T>(p.ks, tok * ngroups + lg);
+      bk[u] = ldf<T>(p.kb, tok * ngroups + lg);
+      sv[u] = ldf<T>(p.vs, tok * ngroups + lg);
+      bv[u] = ldf<T>(p.vb, tok * ngroups + lg);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const bool live = t0 + u * kAffDecWarps < t_end;
+      float sc[G];
+#pragma unroll
+      for (int gi = 0; gi < G; ++gi) {
+        float dot = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; ++e) dot = fmaf(q[gi][e], kc[u][e], dot);
+        sc[gi] = fmaf(sk[u], dot, bk[u] * qs[gi]);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int gi = 0; gi < G; ++gi) sc[gi] += __shfl_xor_sync(0xffffffffu, sc[gi], off);
+      float v[E];
+#pragma unroll
+      for (int e = 0; e < E; ++e) v[e] = fmaf(sv[u], vc[u][e], bv[u]);
+#pragma unroll
+      for (int gi = 0; gi < G; ++gi) {
+        if (!live) continue;
+        const float s2 = sc[gi] * sl2;
+        const float mn = fmaxf(m_run[gi], s2);
+        const float alpha = m_run[gi] == -INFINITY ? 0.f : exp2f(m_run[gi] - mn);
+        const float pr = exp2f(s2 - mn);
+        l_run[gi] = fmaf(l_run[gi], alpha, pr);
+        m_run[gi] = mn;
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[gi][e] = fmaf(o[gi][e], alpha, pr * v[e]);
+      }
+    }
+  }
+  // ---- warps -> CTA (fixed warp order)
+  float* so = dsm;
+  float* sm_ = dsm + kAffDecWarps * G * D;
+  float* sl_ = sm_ + kAffDecWarps * G;
+#pragma unroll
+  for (int gi = 0; gi < G; ++gi) {
+#pragma unroll
+    for (int e = 0; e < E; ++e) so[(warp * G + gi) * D + E * lane + e] = o[gi][e];
+    if (lane == 0) {
+      sm_[warp * G + gi] = m_run[gi];
+      sl_[warp * G + gi] = l_run[gi];
+    }
+  }
+  __syncthreads();
+  grid_dependency_launch();
+  const bool single = p.splits == 1;
+  for (int idx = threadIdx.x; idx < G * D; idx += kAffDecWarps * 32) {
+    const int gi = idx / D, d = idx % D;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kAffDecWarps; ++w) mm = fmaxf(mm, sm_[w * G + gi]);
+    float ll = 0.f, oo = 0.f;
+    if (mm != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAffDecWarps; ++w) {
+        const float f = sm_[w * G + gi] == -INFINITY ? 0.f : exp2f(sm_[w * G + gi] - mm);
+        ll = fmaf(sl_[w * G + gi], f, ll);
+        oo = fmaf(so[(w * G + gi) * D + d], f, oo);
+      }
+    }
+    const size_t row = static_cast<size_t>(b) * p.heads + kh * G + gi;
+    if (single) {
+      static_cast<T*>(p.out)[row * D + d] = from_float<T>(ll > 0.f ? oo / ll : 0.f);
+    } else {
+      float* part = p.partial + (row * p.splits + split) * (D + 2);
+      part[d] = oo;
+      if (d == 0) {
+        part[D] = mm;
+        part[D + 1] = ll;
+      }
+    }
+  }
+  if (single) return;
+  __shared__ unsigned s_prev;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_prev = atomicAdd(p.counters + bkv, 1u);
+  __syncthreads();
+  if (s_prev != static_cast<unsigned>(p.splits - 1)) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < G * D; idx += kAffDecWarps * 32) {
+    const int gi = idx / D, d = idx % D;
+    const size_t row = static_cast<size_t>(b) * p.heads + kh * G + gi;
+    const float* base = p.partial + row * p.splits * (D + 2);
+    float mm = -INFINITY;
+    for (int sp = 0; sp < p.splits; ++sp) mm = fmaxf(mm, __ldcg(base + sp * (D + 2) + D));
+    float ll = 0.f, oo = 0.f;
+    for (int sp = 0; sp < p.splits; ++sp) {
+      const float ms = __ldcg(base + sp * (D + 2) + D);
+      const float w = ms == -INFINITY ? 0.f : exp2f(ms - mm);
+      ll = fmaf(__ldcg(base + sp * (D + 2) + D + 1), w, ll);
+      oo = fmaf(__ldcg(base + sp * (D + 2) + d), w, oo);
+    }
+    static_cast<T*>(p.out)[row * D + d] = from_float<T>(ll > 0.f ? oo / ll : 0.f);
+  }
+  if (threadIdx.x == 0) p.counters[bkv] = 0u;
+}
+
 namespace {
+
+template <typename T, int BITS, int G, int D>
+int launch_affine_decode(const AffineSdpaParams& p, cudaStream_t s) {
+  constexpr int smem = (kAffDecWarps * G * D + 2 * kAffDecWarps * G) * 4;
+  auto kernel = affine_decode_kernel<T, BITS, G, D>;
+  if (smem > 48 * 1024) {
+    const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return fail(SB_ECUDA, std::string("affine decode attribute: ") + cudaGetErrorString(e));
+  }
+  return launch("affine_sdpa_decode", kernel, dim3(p.splits, p.batch * p.kv_heads), dim3(kAffDecWarps * 32), smem,
+                s, p);
+}
+
+template <typename T, int BITS, int G>
+int affine_decode_by_dim(const AffineSdpaParams& p, cudaStream_t s) {
+  switch (p.dk) {
+    case 64: return launch_affine_decode<T, BITS, G, 64>(p, s);
+    case 128: return launch_affine_decode<T, BITS, G, 128>(p, s);
+    default: return launch_affine_decode<T, BITS, G, 256>(p, s);
+  }
+}
+
+template <typename T, int BITS>
+int affine_decode_by_gqa(const AffineSdpaParams& p, int G, cudaStream_t s) {
+  switch (G) {
+    case 1: return affine_decode_by_dim<T, BITS, 1>(p, s);
+    case 2: return affine_decode_by_dim<T, BITS, 2>(p, s);
+    case 4: return affine_decode_by_dim<T, BITS, 4>(p, s);
+    default: return affine_decode_by_dim<T, BITS, 8>(p, s);
+  }
+}
 
 int affine_splits(int64_t rows, int64_t n) {
   // about two waves of 4 CTAs per SM, at least 256 tokens per split
@@ -261,9 +479,26 @@ extern "C" int sb_affine_sdpa(const void* q, int dtype, const void* k_packed, co
     p.counters = static_cast<unsigned*>(workspace);
     p.partial = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes);
   }
+  cudaStream_t s = as_stream(stream);
+  // single-query decode of the common shapes: the KV-head-per-CTA kernel
+  const int G = num_heads / num_kv_heads;
+  const bool rows_aligned = reinterpret_cast<uintptr_t>(k_packed) % 8 == 0 &&
+                            reinterpret_cast<uintptr_t>(v_packed) % 8 == 0;
+  if (length == 1 && dk == dv && (dk == 64 || dk == 128 || dk == 256) && (bits == 4 || bits == 8) &&
+      (G == 1 || G == 2 || G == 4 || G == 8) && (dtype == SB_DTYPE_BF16 || dtype == SB_DTYPE_F16) &&
+      rows_aligned && batch * num_kv_heads < 65536) {
+    // one wave of CTAs (two per SM), at least 64 tokens per split, within the workspace's split count
+    const int64_t bkv = batch * num_kv_heads;
+    int64_t sp = std::max<int64_t>(1, (296 + bkv - 1) / bkv);
+    sp = std::min<int64_t>(sp, std::max<int64_t>(1, n / 64));
+    p.splits = static_cast<int>(std::min<int64_t>(sp, p.splits));
+    if (p.splits > 1 && p.counters == nullptr) p.splits = 1;
+    if (dtype == SB_DTYPE_BF16)
+      return bits == 4 ? affine_decode_by_gqa<__nv_bfloat16, 4>(p, G, s) : affine_decode_by_gqa<__nv_bfloat16, 8>(p, G, s);
+    return bits == 4 ? affine_decode_by_gqa<__half, 4>(p, G, s) : affine_decode_by_gqa<__half, 8>(p, G, s);
+  }
   const dim3 grid(static_cast<unsigned>(rows), p.splits);
   const dim3 block(kAffSdpaThreads);
-  cudaStream_t s = as_stream(stream);
   switch (dtype) {
     case SB_DTYPE_BF16:
       return launch("affine_sdpa", affine_sdpa_kernel<__nv_bfloat16>, grid, block, 0, s, p);

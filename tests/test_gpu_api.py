@@ -97,6 +97,12 @@ def affine_kv(rng, bsz, kvh, n, dim, group, bits):
         (2, 16, 4, 1, 5000, 128, 64, 4, None),     # several token splits
         (1, 8, 8, 3, 40, 128, 32, 8, "causal"),   # multi-token bottom-right causal
         (1, 4, 2, 1, 33, 64, 32, 2, "causal"),    # 2-bit codes
+        # single-query decode on the KV-head-per-CTA kernel: the reference model's 16/4 x 256,
+        # GQA 8 with group 128, GQA 1 at head_dim 64, a ragged short cache
+        (1, 16, 4, 1, 4096, 256, 32, 8, None),
+        (2, 8, 1, 1, 1000, 128, 128, 4, None),
+        (3, 8, 8, 1, 300, 64, 32, 8, None),
+        (1, 16, 4, 1, 37, 256, 32, 4, "causal"),
     ],
 )
 def test_int8_quantized_sdpa_affine_tuples(api, bsz, heads, kvh, length, n, dim, group, bits, mask):
