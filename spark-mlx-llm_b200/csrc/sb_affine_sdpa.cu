@@ -207,11 +207,12 @@ __global__ void __launch_bounds__(kAffSdpaThreads) affine_sdpa_kernel(const Affi
 // adds them in split order).
 constexpr int kAffDecWarps = 8;
 
+// the lane's E codes of a row as raw words (unpacked where they are used)
 template <int BITS, int E>
-__device__ __forceinline__ void load_codes(const uint32_t* row, int lane, float (&c)[E]) {
+__device__ __forceinline__ void load_codes(const uint32_t* row, int lane, uint32_t (&w)[2]) {
   constexpr int kBytes = E * BITS / 8;  // bytes of the lane's codes
   const uint8_t* base = reinterpret_cast<const uint8_t*>(row) + lane * kBytes;
-  uint32_t w[2] = {0u, 0u};
+  w[0] = w[1] = 0u;
   if constexpr (kBytes == 8) {
     const uint2 v = __ldg(reinterpret_cast<const uint2*>(base));
     w[0] = v.x;
@@ -223,15 +224,15 @@ __device__ __forceinline__ void load_codes(const uint32_t* row, int lane, float 
   } else {
     w[0] = __ldg(base);
   }
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    const int bit = e * BITS;
-    c[e] = static_cast<float>((w[bit >> 5] >> (bit & 31)) & ((1u << BITS) - 1u));
-  }
+}
+template <int BITS>
+__device__ __forceinline__ float code_at(const uint32_t (&w)[2], int e) {
+  const int bit = e * BITS;
+  return static_cast<float>((w[bit >> 5] >> (bit & 31)) & ((1u << BITS) - 1u));
 }
 
 template <typename T, int BITS, int G, int D>
-__global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 512 ? 2 : 1)
+__global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 1024 ? 2 : 1)
     affine_decode_kernel(const AffineSdpaParams p) {
   constexpr int E = D / 32;
   constexpr int kU = 4;  // tokens per warp iteration
@@ -267,7 +268,8 @@ __global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 512 ? 2 : 1)
   }
   const size_t tok0 = static_cast<size_t>(bkv) * p.n;  // token 0 of this (b, kv head)
   for (int t0 = t_begin + warp; t0 < t_end; t0 += kU * kAffDecWarps) {
-    float kc[kU][E], vc[kU][E], sk[kU], bk[kU], sv[kU], bv[kU];
+    uint32_t kc[kU][2], vc[kU][2];
+    float sk[kU], bk[kU], sv[kU], bv[kU];
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       const int t = t0 + u * kAffDecWarps;
@@ -287,7 +289,7 @@ __global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 512 ? 2 : 1)
       for (int gi = 0; gi < G; ++gi) {
         float dot = 0.f;
 #pragma unroll
-        for (int e = 0; e < E; ++e) dot = fmaf(q[gi][e], kc[u][e], dot);
+        for (int e = 0; e < E; ++e) dot = fmaf(q[gi][e], code_at<BITS>(kc[u], e), dot);
         sc[gi] = fmaf(sk[u], dot, bk[u] * qs[gi]);
       }
 #pragma unroll
@@ -296,7 +298,7 @@ __global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 512 ? 2 : 1)
         for (int gi = 0; gi < G; ++gi) sc[gi] += __shfl_xor_sync(0xffffffffu, sc[gi], off);
       float v[E];
 #pragma unroll
-      for (int e = 0; e < E; ++e) v[e] = fmaf(sv[u], vc[u][e], bv[u]);
+      for (int e = 0; e < E; ++e) v[e] = fmaf(sv[u], code_at<BITS>(vc[u], e), bv[u]);
 #pragma unroll
       for (int gi = 0; gi < G; ++gi) {
         if (!live) continue;
@@ -487,9 +489,11 @@ extern "C" int sb_affine_sdpa(const void* q, int dtype, const void* k_packed, co
   if (length == 1 && dk == dv && (dk == 64 || dk == 128 || dk == 256) && (bits == 4 || bits == 8) &&
       (G == 1 || G == 2 || G == 4 || G == 8) && (dtype == SB_DTYPE_BF16 || dtype == SB_DTYPE_F16) &&
       rows_aligned && batch * num_kv_heads < 65536) {
-    // one wave of CTAs (two per SM), at least 64 tokens per split, within the workspace's split count
+    // one wave of CTAs (two per SM up to G x D = 1024, else one), at least 64 tokens per split,
+    // within the workspace's split count
     const int64_t bkv = batch * num_kv_heads;
-    int64_t sp = std::max<int64_t>(1, (296 + bkv - 1) / bkv);
+    const int64_t slots = G * dk <= 1024 ? 296 : 148;
+    int64_t sp = std::max<int64_t>(1, (slots + bkv - 1) / bkv);
     sp = std::min<int64_t>(sp, std::max<int64_t>(1, n / 64));
     p.splits = static_cast<int>(std::min<int64_t>(sp, p.splits));
     if (p.splits > 1 && p.counters == nullptr) p.splits = 1;
