@@ -506,8 +506,7 @@ class SyntheticDecoder:
         return self._pf
 
     def _prefill_chunked(self, prompt, chunk):
-        cfg, b = self.cfg, self.batch
-        d, hq, hkv, cap = cfg.head_dim, self.hq, self.hkv, self.capacity
+        b, cap, hidden = self.batch, self.capacity, self.cfg.hidden
         total = prompt.shape[1]
         if total < 1 or total > cap:
             raise ValueError(f"prompt length {total} must be in [1, capacity {cap}]")
@@ -515,48 +514,96 @@ class SyntheticDecoder:
             raise ValueError("chunk must be positive")
         L = lib()
         stream = torch.cuda.current_stream(self.device).cuda_stream
-        nqkv = (hq + 2 * hkv) * d
-        hidden, inter, group = cfg.hidden, self.inter, cfg.mlp_group
-        scale = 1.0 / math.sqrt(d)
         t = self._prefill_buffers(b * min(chunk, total))
-        ws, wsb = t["ws"].data_ptr(), t["ws"].numel()
         self.reset(prompt[:, 0])
         for c0 in range(0, total, chunk):
             lc = min(chunk, total - c0)
-            m = b * lc
-            ids = prompt[:, c0:c0 + lc].reshape(-1).contiguous()
-            pos = torch.arange(c0, c0 + lc, device=self.device, dtype=torch.int32).repeat(b)
-            x, xn, qkv, q, attn, o = (t[k][:m] for k in ("x", "xn", "qkv", "q", "attn", "o"))
-            g, u, act = (t[k][:m] for k in ("g", "u", "act"))
-            check(L.sb_embed_rows(_ptr(self.embed), _ptr(ids), _ptr(x), m, hidden, cfg.vocab, stream), "embed")
-            for li, layer in enumerate(self.layers):
-                kc, ks, vc, vs = self.k_cache[li], self.k_scale[li], self.v_cache[li], self.v_scale[li]
-                check(L.sb_rms_norm(_ptr(x), _ptr(layer["in_norm"]), _ptr(xn), BF16, m, hidden, cfg.rms_eps, stream),
-                      "rms_norm")
-                check(L.sb_w8a16_per_channel(_ptr(xn), BF16, _ptr(layer["qkv_w"]), _ptr(layer["qkv_s"]), _ptr(qkv),
-                                             m, nqkv, hidden, ws, wsb, stream), "qkv")
-                check(L.sb_rope_kv_append(_ptr(qkv), nqkv, _ptr(pos), _ptr(q), _ptr(kc), _ptr(ks), _ptr(vc),
-                                          _ptr(vs), b, lc, hq, hkv, d, cap, d, cfg.rope_theta, stream), "rope")
-                check(L.sb_int8_sdpa_prefill(_ptr(q), _ptr(kc), _ptr(ks), _ptr(vc), _ptr(vs), _ptr(attn), b, hq, hkv,
-                                             lc, c0 + lc, cap, d, scale, 1, 1, stream), "prefill attention")
-                check(L.sb_w8a16_per_channel(_ptr(attn), BF16, _ptr(layer["o_w"]), _ptr(layer["o_s"]), _ptr(o), m,
-                                             hidden, hq * d, ws, wsb, stream), "o_proj")
-                check(L.sb_residual_add(_ptr(x), _ptr(o), m * hidden, stream), "residual")
-                check(L.sb_rms_norm(_ptr(x), _ptr(layer["post_norm"]), _ptr(xn), BF16, m, hidden, cfg.rms_eps,
-                                    stream), "rms_norm")
-                for (w, sc, bi), out in ((layer["gate"], g), (layer["up"], u)):
-                    check(L.sb_affine_linear(_ptr(xn), BF16, _ptr(w), _ptr(sc), _ptr(bi), _ptr(out), m, inter, hidden,
-                                             group, 4, ws, wsb, stream), "gate/up")
-                check(L.sb_swiglu(_ptr(g), _ptr(u), _ptr(act), m * inter, stream), "swiglu")
-                dw, ds, db = layer["down"]
-                check(L.sb_affine_linear(_ptr(act), BF16, _ptr(dw), _ptr(ds), _ptr(db), _ptr(o), m, hidden, inter,
-                                         group, 4, ws, wsb, stream), "down")
-                check(L.sb_residual_add(_ptr(x), _ptr(o), m * hidden, stream), "residual")
+            x = self._forward_rows(prompt[:, c0:c0 + lc], c0, t, stream)
             if c0 + lc == total:
                 self.x.copy_(x.view(b, lc, hidden)[:, lc - 1])
         self.positions.fill_(total)
         check(L.sb_linear_ex(ctypes.byref(self.head_desc), stream), "lm_head")
         check(L.sb_decode_advance(_ptr(self.keys), _ptr(self.tokens), _ptr(self.positions), b, 0, stream), "advance")
+
+    def _forward_rows(self, ids2d, c0, t, stream):
+        """Every layer for tokens ``ids2d [batch, lc]`` at positions c0..c0+lc-1
+        (their K/V appended to the cache, attention causal over positions <=
+        each row's); returns the output rows [batch * lc, hidden] (a view of
+        the buffers ``t``)."""
+        cfg, b = self.cfg, self.batch
+        d, hq, hkv, cap = cfg.head_dim, self.hq, self.hkv, self.capacity
+        L = lib()
+        nqkv = (hq + 2 * hkv) * d
+        hidden, inter, group = cfg.hidden, self.inter, cfg.mlp_group
+        scale = 1.0 / math.sqrt(d)
+        ws, wsb = t["ws"].data_ptr(), t["ws"].numel()
+        lc = ids2d.shape[1]
+        m = b * lc
+        ids = ids2d.reshape(-1).to(self.device, torch.int32).contiguous()
+        pos = torch.arange(c0, c0 + lc, device=self.device, dtype=torch.int32).repeat(b)
+        x, xn, qkv, q, attn, o = (t[k][:m] for k in ("x", "xn", "qkv", "q", "attn", "o"))
+        g, u, act = (t[k][:m] for k in ("g", "u", "act"))
+        check(L.sb_embed_rows(_ptr(self.embed), _ptr(ids), _ptr(x), m, hidden, cfg.vocab, stream), "embed")
+        for li, layer in enumerate(self.layers):
+            kc, ks, vc, vs = self.k_cache[li], self.k_scale[li], self.v_cache[li], self.v_scale[li]
+            check(L.sb_rms_norm(_ptr(x), _ptr(layer["in_norm"]), _ptr(xn), BF16, m, hidden, cfg.rms_eps, stream),
+                  "rms_norm")
+            check(L.sb_w8a16_per_channel(_ptr(xn), BF16, _ptr(layer["qkv_w"]), _ptr(layer["qkv_s"]), _ptr(qkv),
+                                         m, nqkv, hidden, ws, wsb, stream), "qkv")
+            check(L.sb_rope_kv_append(_ptr(qkv), nqkv, _ptr(pos), _ptr(q), _ptr(kc), _ptr(ks), _ptr(vc),
+                                      _ptr(vs), b, lc, hq, hkv, d, cap, d, cfg.rope_theta, stream), "rope")
+            check(L.sb_int8_sdpa_prefill(_ptr(q), _ptr(kc), _ptr(ks), _ptr(vc), _ptr(vs), _ptr(attn), b, hq, hkv,
+                                         lc, c0 + lc, cap, d, scale, 1, 1, stream), "prefill attention")
+            check(L.sb_w8a16_per_channel(_ptr(attn), BF16, _ptr(layer["o_w"]), _ptr(layer["o_s"]), _ptr(o), m,
+                                         hidden, hq * d, ws, wsb, stream), "o_proj")
+            check(L.sb_residual_add(_ptr(x), _ptr(o), m * hidden, stream), "residual")
+            check(L.sb_rms_norm(_ptr(x), _ptr(layer["post_norm"]), _ptr(xn), BF16, m, hidden, cfg.rms_eps,
+                                stream), "rms_norm")
+            for (w, sc, bi), out in ((layer["gate"], g), (layer["up"], u)):
+                check(L.sb_affine_linear(_ptr(xn), BF16, _ptr(w), _ptr(sc), _ptr(bi), _ptr(out), m, inter, hidden,
+                                         group, 4, ws, wsb, stream), "gate/up")
+            check(L.sb_swiglu(_ptr(g), _ptr(u), _ptr(act), m * inter, stream), "swiglu")
+            dw, ds, db = layer["down"]
+            check(L.sb_affine_linear(_ptr(act), BF16, _ptr(dw), _ptr(ds), _ptr(db), _ptr(o), m, hidden, inter,
+                                     group, 4, ws, wsb, stream), "down")
+            check(L.sb_residual_add(_ptr(x), _ptr(o), m * hidden, stream), "residual")
+        return x
+
+    def verify(self, tokens):
+        """Speculative verification (the target pass of a draft-and-verify loop,
+        ``dspark/generation.py:30-60``; batch 1, one GPU): run ``tokens`` = [anchor,
+        *draft] (1 to 8 ids) at positions ``positions[0]`` onward in one
+        multi-position pass - the M <= 8 weight-streaming kernels and the causal
+        multi-query attention over the INT8 cache - and return the greedy token
+        after each of them (host list, lowest index on ties). Their K/V rows are
+        written to the cache; rows past the accepted prefix are overwritten by
+        the next pass. Positions and tokens are not advanced (``commit``)."""
+        if self.batch != 1 or self.world != 1:
+            raise ValueError("verification runs at batch 1 on one GPU")
+        ids = torch.as_tensor(tokens, dtype=torch.int32).reshape(1, -1)
+        k1 = ids.shape[1]
+        if not 1 <= k1 <= 8:
+            raise ValueError("verify takes 1 to 8 tokens (the anchor and up to 7 drafts)")
+        pos0 = int(self.positions[0])
+        if pos0 + k1 > self.capacity:
+            raise ValueError("KV cache is full")
+        cfg = self.cfg
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        t = self._prefill_buffers(8)
+        x = self._forward_rows(ids, pos0, t, stream)
+        keys = torch.zeros(k1, dtype=torch.int64, device=self.device)
+        head = self._desc(x=_ptr(x), M=k1, N=self.vocab_shard, K=cfg.hidden, weight_format=SB_WEIGHT_BF16,
+                          weight=_ptr(self.head), norm_weight=_ptr(self.final_norm), epilogue=SB_EPI_ARGMAX,
+                          argmax_keys=_ptr(keys), argmax_offset=self.plan.vocab_rows[0],
+                          workspace=self.workspace.data_ptr(), workspace_bytes=self.workspace.numel())
+        check(lib().sb_linear_ex(ctypes.byref(head), stream), "lm_head (verify)")
+        return [tensor_parallel.key_index(int(k) & 0xFFFFFFFFFFFFFFFF) for k in keys.cpu().tolist()]
+
+    def commit(self, next_token, advance):
+        """After a verification pass: move the position by ``advance`` (the anchor
+        plus the accepted drafts) and make ``next_token`` the next input."""
+        self.positions.add_(int(advance))
+        self.tokens.fill_(int(next_token))
 
     def capture(self):
         """Capture one decode step (lm_head, argmax and position advance included)."""
