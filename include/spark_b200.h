@@ -214,6 +214,20 @@ int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* k_scale, co
                          int head_dim, float scale, int causal, int layout, void* stream);
 
 /*
+ * sb_int8_sdpa_prefill with the bottom-right causal mask and a sliding window:
+ * query l (position length - q_len + l) sees keys (position - window, position]
+ * (window 0: no window). The chunked prompt of a sliding-window layer
+ * (spark_mlx_llm/model.py:313-320, the mask of its RotatingKVCache chunk,
+ * :362-370) over the INT8 cache; arguments and layouts as sb_int8_sdpa_prefill.
+ * A query's keys start at row 0 of k / v, so a caller holding only a window of
+ * the cache passes pointers offset to its first row (row stride `capacity`).
+ */
+int sb_int8_sdpa_prefill_window(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                                const void* v_scale, void* out, int64_t batch, int num_heads,
+                                int num_kv_heads, int64_t q_len, int64_t length, int64_t capacity,
+                                int head_dim, float scale, int window, int layout, void* stream);
+
+/*
  * BF16 multi-query attention (speculative verification, sliding-window layers).
  * Replaces bf16_sdpa_multiquery (spark_mlx_ext/bf16_sdpa_multiquery.py:155-189)
  * and the BF16 scaled_dot_product_attention it falls back to:

@@ -631,6 +631,22 @@ extern "C" int sb_int8_sdpa_prefill(const void* q, const int8_t* k, const void* 
   return launch_any<false>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, head_dim, as_stream(stream));
 }
 
+extern "C" int sb_int8_sdpa_prefill_window(const void* q, const int8_t* k, const void* k_scale, const int8_t* v,
+                                           const void* v_scale, void* out, int64_t batch, int num_heads,
+                                           int num_kv_heads, int64_t q_len, int64_t length, int64_t capacity,
+                                           int head_dim, float scale, int window, int layout, void* stream) {
+  SB_REQUIRE(k_scale && v_scale, "null pointer");
+  SB_REQUIRE(window >= 0, "window must be >= 0");
+  Params p;
+  if (int st = common_params(p, q, k, v, out, batch, num_heads, num_kv_heads, q_len, length, capacity, head_dim,
+                             scale, 1, layout))
+    return st;
+  p.ks = static_cast<const __half*>(k_scale);
+  p.vs = static_cast<const __half*>(v_scale);
+  p.window = window;
+  return launch_any<false>(p, batch, num_kv_heads, num_heads / num_kv_heads, q_len, head_dim, as_stream(stream));
+}
+
 extern "C" int sb_bf16_sdpa_multiquery(const void* q, const void* k, const void* v, void* out, int64_t batch,
                                        int num_heads, int num_kv_heads, int64_t q_len, int64_t length,
                                        int64_t capacity, int head_dim, float scale, int causal, int window,

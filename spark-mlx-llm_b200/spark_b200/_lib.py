@@ -151,6 +151,11 @@ SIGNATURES = {
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _i64, _i64, _i64,
          _int, _float, _int, _int, _c_void_p],
     ),
+    "sb_int8_sdpa_prefill_window": (
+        _int,
+        [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _i64, _i64, _i64,
+         _int, _float, _int, _int, _c_void_p],
+    ),
     "sb_bf16_sdpa_multiquery": (
         _int,
         [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _int, _int, _i64, _i64, _i64, _int, _float, _int, _int,

@@ -17,17 +17,31 @@ Per token and layer this runs ``sb_rms_norm``, the weight-streaming affine GEMV
 (``sb_linear_ex``: 4- or 8-bit, groups 32/64/128, any projection shape),
 ``sb_rope_kv_append`` (RoPE on the first rope_dims features, K/V quantized into
 the BASELINE INT8 cache; ``sb_rope_kv_append_ring`` for a sliding layer's
-rotating cache of ``sliding_window`` slots), ``sb_int8_sdpa_decode`` (head_dim
-128 or 256; a sliding layer attends to its ring's filled slots),
+rotating cache), ``sb_int8_sdpa_decode`` (head_dim 128 or 256; a sliding layer
+attends to its last ``sliding_window`` positions),
 ``sb_head_gate``, the residual epilogue of ``out_proj``, the paired gate/up GEMV
 with the fused RMSNorm and GELU gate, ``down`` with its residual, and the
 final RMSNorm fused into the (tied, quantized) lm_head GEMV. KV: the BASELINE
 symmetric INT8 format (one fp16 scale per token and head) instead of the
-reference's bf16 or affine uint8/G32 cache. Sliding layers keep the
-RotatingKVCache of ``model.py:362-370`` (``max_size=sliding_window, keep=0``):
-position p lands in slot p % window, so the slots always hold the last
-``window`` positions (``rotating=False`` instead keeps every position and moves
-the attention start, the same keys in position order).
+reference's bf16 or affine uint8/G32 cache. Sliding layers keep a rotating
+cache like the RotatingKVCache of ``model.py:362-370`` (``keep=0``): a ring of
+R = sliding_window + chunk - 1 slots (rounded up to 16), position p in slot
+p % R, and every slot written twice - at row p % R and at its mirror row
+p % R + R - so the last ``n <= R`` positions are always one contiguous run of
+rows, in position order: a decode query attends to rows
+[(length - n) % R, ... + n) with n = min(length, sliding_window), and a prompt
+chunk to the sliding_window - 1 positions before it plus itself. (The
+reference's ring of exactly ``sliding_window`` slots is the case chunk = 1; a
+ring that would not be smaller than the cache becomes a linear cache.
+``rotating=False`` keeps every position and moves the attention start.)
+
+``prefill`` runs a prompt in chunks of ``chunk`` positions (512, the reference's
+prompt chunk, ``generation.py:78``) as one batched pass per layer: embedding
+rows, ``sb_rms_norm``, ``sb_affine_linear`` at M = batch x chunk (the
+tensor-core kernel beyond 8 rows), ``sb_rope_kv_append`` (ring) for the chunk,
+``sb_int8_sdpa_prefill_window`` (bottom-right causal, the sliding window on
+sliding layers), ``sb_head_gate``, the residual adds and ``sb_gated_activation``
+(GELU); the lm_head runs on the last position only.
 """
 
 import ctypes
@@ -40,7 +54,7 @@ import torch
 from ._lib import check, lib, sb_linear_ex_desc
 from .checkpoint import load_checkpoint_dir, to_torch
 
-__all__ = ["Spark25Config", "Spark25Model", "load", "sanitize"]
+__all__ = ["Spark25Config", "Spark25Model", "load", "ring_slots", "sanitize"]
 
 BF16 = 0
 AFFINE4, AFFINE8, BF16_W = 0, 1, 3
@@ -144,6 +158,16 @@ def _ptr(t):
     return t.data_ptr() if t is not None else None
 
 
+def ring_slots(window, chunk, capacity):
+    """Slots R of a sliding layer's ring for prompt chunks of up to ``chunk``
+    positions: a chunk attends to the window - 1 positions before it and itself,
+    so R >= window + chunk - 1 keeps all of them (rounded up to 16 rows). 0 (a
+    linear cache) when the mirrored ring (2R rows) would not be smaller than
+    ``capacity``."""
+    r = (window + chunk - 1 + 15) // 16 * 16
+    return r if 2 * r < capacity else 0
+
+
 class _Proj:
     """One linear layer: MLX affine (packed uint32 + bf16 scales/biases) or bf16."""
 
@@ -192,9 +216,12 @@ class Spark25Model:
     """A loaded Spark2_5 checkpoint with its INT8 KV cache and decode buffers;
     ``step(tokens)`` runs one greedy-decode position for ``batch`` sequences."""
 
-    def __init__(self, cfg, weights, *, batch=1, capacity=None, device="cuda", rotating=True):
+    def __init__(self, cfg, weights, *, batch=1, capacity=None, device="cuda", rotating=True, chunk=512):
         self.cfg, self.batch = cfg, batch
         self.rotating = rotating
+        if chunk < 1:
+            raise ValueError("chunk must be positive")
+        self.chunk = int(chunk)
         self.device = torch.device(device)
         self.capacity = ((capacity or cfg.max_position_embeddings) + 15) // 16 * 16
         weights = sanitize(weights, cfg.tie_word_embeddings)
@@ -254,10 +281,11 @@ class Spark25Model:
         self.logits = torch.zeros(b, cfg.vocab_size, **bf)
         self.tokens = torch.zeros(b, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(b, dtype=torch.int32, device=dev)
-        # rows per head: a sliding layer's ring holds sliding_window slots (rows rounded to 16)
-        ring = (cfg.sliding_window + 15) // 16 * 16
-        self.rows = [min(ring, self.capacity) if lay["sliding"] and self.rotating else self.capacity
-                     for lay in self.layers]
+        # rows per head: a sliding layer's ring of R slots is stored twice (rows [0, R) and
+        # the mirror [R, 2R)); a ring no smaller than the cache is a linear cache instead
+        ring = ring_slots(cfg.sliding_window, self.chunk, self.capacity) if self.rotating else 0
+        self.ring = [ring if lay["sliding"] else 0 for lay in self.layers]
+        self.rows = [2 * r if r else self.capacity for r in self.ring]
         self.k_cache = [torch.zeros(b, hkv, r, d, dtype=torch.int8, device=dev) for r in self.rows]
         self.v_cache = [torch.zeros_like(k) for k in self.k_cache]
         self.k_scale = [torch.ones(b, hkv, r, dtype=torch.float16, device=dev) for r in self.rows]
@@ -314,20 +342,13 @@ class Spark25Model:
             check(L.sb_linear_ex(ctypes.byref(lay["qkv_d"]), stream), "q_k_v_proj")
             kc, vc, ks, vs = self.k_cache[li], self.v_cache[li], self.k_scale[li], self.v_scale[li]
             rows = self.rows[li]
-            rotating = lay["sliding"] and self.rotating
-            args = (_ptr(self.qkv), self.qkv.shape[1], _ptr(self.positions), _ptr(self.q), _ptr(kc), _ptr(ks),
-                    _ptr(vc), _ptr(vs), b, 1, hq, hkv, d, rows, lay["rope_dims"], lay["rope_base"])
-            if rotating:  # the ring's slots hold the last sliding_window positions
-                check(L.sb_rope_kv_append_ring(*args, cfg.sliding_window, stream), "rope + ring cache append")
-                start, n = 0, min(length, cfg.sliding_window)
-            else:
-                check(L.sb_rope_kv_append(*args, stream), "rope + cache append")
-                # a sliding layer attends to its last sliding_window positions:
-                # the same cache rows with the start moved (row stride unchanged)
-                start = max(0, length - cfg.sliding_window) if lay["sliding"] else 0
-                n = length - start
-            check(L.sb_int8_sdpa_decode(_ptr(self.q), kc.data_ptr() + start * d, ks.data_ptr() + 2 * start,
-                                        vc.data_ptr() + start * d, vs.data_ptr() + 2 * start, _ptr(self.attn), b, hq,
+            self._append(li, _ptr(self.qkv), self.qkv.shape[1], _ptr(self.positions), _ptr(self.q), 1, stream)
+            # a sliding layer attends to its last sliding_window positions: one
+            # contiguous run of rows (row stride unchanged)
+            start = max(0, length - cfg.sliding_window) if lay["sliding"] else 0
+            n, row0 = length - start, self._row(li, start)
+            check(L.sb_int8_sdpa_decode(_ptr(self.q), kc.data_ptr() + row0 * d, ks.data_ptr() + 2 * row0,
+                                        vc.data_ptr() + row0 * d, vs.data_ptr() + 2 * row0, _ptr(self.attn), b, hq,
                                         hkv, n, rows, d, scale, self.workspace.data_ptr(),
                                         self.workspace.numel(), stream), "attention")
             check(L.sb_head_gate(_ptr(self.xn), _ptr(lay["g"]), _ptr(self.attn), _ptr(self.gated), b,
@@ -339,15 +360,135 @@ class Spark25Model:
         self.pos += 1
         return self.logits
 
-    def prefill(self, prompt):
-        """Run ``prompt [batch, L]`` position by position; returns the last logits."""
+    def _row(self, li, position):
+        """Cache row of ``position`` in layer ``li`` (its ring slot, or the position)."""
+        r = self.ring[li]
+        return position % r if r else position
+
+    def _append(self, li, qkv, ld, positions, q_out, seq_len, stream):
+        """RoPE + INT8 append of ``seq_len`` positions per sequence into layer
+        ``li``'s cache: at the positions (linear) or at their ring slots and the
+        slots' mirror rows (the same values written twice)."""
+        cfg, L = self.cfg, lib()
+        hq, hkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        lay, r = self.layers[li], self.ring[li]
+        kc, vc, ks, vs = self.k_cache[li], self.v_cache[li], self.k_scale[li], self.v_scale[li]
+        tail = (self.batch, seq_len, hq, hkv, d, self.rows[li], lay["rope_dims"], lay["rope_base"])
+        if not r:
+            check(L.sb_rope_kv_append(qkv, ld, positions, q_out, _ptr(kc), _ptr(ks), _ptr(vc), _ptr(vs), *tail,
+                                      stream), "rope + cache append")
+            return
+        for m in (0, r):  # the ring rows, then their mirrors
+            check(L.sb_rope_kv_append_ring(qkv, ld, positions, q_out, kc.data_ptr() + m * d, ks.data_ptr() + 2 * m,
+                                           vc.data_ptr() + m * d, vs.data_ptr() + 2 * m, *tail, r, stream),
+                  "rope + ring cache append")
+
+    def _prefill_buffers(self, m):
+        """Activation buffers for ``m`` prompt rows (kept; grown on demand)."""
+        have = getattr(self, "_pf", None)
+        if have is not None and have["rows"] >= m:
+            return have
+        cfg, dev = self.cfg, self.device
+        hq, hkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        hid, inter = cfg.hidden_size, cfg.intermediate_size
+
+        def buf(*shape):
+            return torch.empty(shape, dtype=torch.bfloat16, device=dev)
+
+        ws = 256
+        for lay in self.layers:
+            for proj in ("qkv", "out", "gate", "up", "down"):
+                pr = lay[proj]
+                ws = max(ws, lib().sb_affine_linear_workspace_size(m, pr.n, pr.k, pr.group, pr.bits))
+        self._pf = dict(rows=m, x=buf(m, hid), xn=buf(m, hid), qkv=buf(m, (hq + 2 * hkv) * d), q=buf(m, hq * d),
+                        attn=buf(m, hq * d), o=buf(m, hid), g=buf(m, inter), u=buf(m, inter), act=buf(m, inter),
+                        ids=torch.empty(m, dtype=torch.int32, device=dev),
+                        pos=torch.empty(m, dtype=torch.int32, device=dev),
+                        ws=torch.zeros(ws, dtype=torch.uint8, device=dev))
+        return self._pf
+
+    def _linear(self, proj, x, y, m, t, stream, what):
+        check(lib().sb_affine_linear(_ptr(x), BF16, _ptr(proj.weight), _ptr(proj.scales), _ptr(proj.biases),
+                                     _ptr(y), m, proj.n, proj.k, proj.group, proj.bits, t["ws"].data_ptr(),
+                                     t["ws"].numel(), stream), what)
+
+    def _prefill_chunk(self, ids, c0, lc, t, stream):
+        """Every layer for the tokens ``ids [batch, lc]`` at positions c0..c0+lc-1;
+        returns the hidden rows [batch * lc, hidden] (a view of ``t``)."""
+        cfg, b, L = self.cfg, self.batch, lib()
+        hq, hkv, d = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
+        hid, inter, eps = cfg.hidden_size, cfg.intermediate_size, cfg.rms_norm_eps
+        m = b * lc
+        x, xn, qkv, q, attn, o = (t[k][:m] for k in ("x", "xn", "qkv", "q", "attn", "o"))
+        g, u, act, tok, pos = (t[k][:m] for k in ("g", "u", "act", "ids", "pos"))
+        tok.copy_(ids.reshape(-1))
+        pos.copy_(torch.arange(c0, c0 + lc, dtype=torch.int32).repeat(b))
+        e = self.embed
+        if e.format == BF16_W:
+            check(L.sb_embed_rows(_ptr(e.weight), _ptr(tok), _ptr(x), m, hid, cfg.vocab_size, stream), "embedding")
+        else:
+            check(L.sb_embed_rows_affine(_ptr(e.weight), _ptr(e.scales), _ptr(e.biases), _ptr(tok), _ptr(x), m,
+                                         hid, cfg.vocab_size, e.group, e.bits, stream), "embedding")
+        scale = 1.0 / math.sqrt(d)
+        for li, lay in enumerate(self.layers):
+            check(L.sb_rms_norm(_ptr(x), _ptr(lay["in_norm"]), _ptr(xn), BF16, m, hid, eps, stream),
+                  "input_layernorm")
+            self._linear(lay["qkv"], xn, qkv, m, t, stream, "q_k_v_proj")
+            self._append(li, _ptr(qkv), qkv.shape[1], _ptr(pos), _ptr(q), lc, stream)
+            # keys: the sliding_window - 1 positions before the chunk (sliding) or
+            # every earlier position, then the chunk; one contiguous run of rows
+            start = max(0, c0 - cfg.sliding_window + 1) if lay["sliding"] else 0
+            n, row0 = c0 + lc - start, self._row(li, start)
+            kc, vc, ks, vs = self.k_cache[li], self.v_cache[li], self.k_scale[li], self.v_scale[li]
+            check(L.sb_int8_sdpa_prefill_window(_ptr(q), kc.data_ptr() + row0 * d, ks.data_ptr() + 2 * row0,
+                                                vc.data_ptr() + row0 * d, vs.data_ptr() + 2 * row0, _ptr(attn), b,
+                                                hq, hkv, lc, n, self.rows[li], d, scale,
+                                                cfg.sliding_window if lay["sliding"] else 0, 1, stream),
+                  "prefill attention")
+            check(L.sb_head_gate(_ptr(xn), _ptr(lay["g"]), _ptr(attn), _ptr(attn), m, hid, hq, d, stream),
+                  "head gate")
+            self._linear(lay["out"], attn, o, m, t, stream, "out_proj")
+            check(L.sb_residual_add(_ptr(x), _ptr(o), m * hid, stream), "residual")
+            check(L.sb_rms_norm(_ptr(x), _ptr(lay["post_norm"]), _ptr(xn), BF16, m, hid, eps, stream),
+                  "post_attention_layernorm")
+            self._linear(lay["gate"], xn, g, m, t, stream, "gate_proj")
+            self._linear(lay["up"], xn, u, m, t, stream, "up_proj")
+            check(L.sb_gated_activation(_ptr(g), _ptr(u), _ptr(act), m * inter, 1, stream), "gelu gate")
+            self._linear(lay["down"], act, o, m, t, stream, "down_proj")
+            check(L.sb_residual_add(_ptr(x), _ptr(o), m * hid, stream), "residual")
+        return x
+
+    def prefill(self, prompt, chunk=None):
+        """Run ``prompt [batch, L]`` from the current position; returns the logits
+        after its last position and advances the position by L. The prompt runs
+        in chunks of ``chunk`` positions (default: the model's ``chunk``, at most
+        it when a sliding layer has a ring); ``chunk=0`` feeds it position by
+        position through ``step``."""
         prompt = torch.as_tensor(prompt, dtype=torch.int32)
-        if prompt.ndim != 2 or prompt.shape[0] != self.batch:
-            raise ValueError("prompt must be [batch, L]")
-        logits = None
-        for i in range(prompt.shape[1]):
-            logits = self.step(prompt[:, i])
-        return logits
+        if prompt.ndim != 2 or prompt.shape[0] != self.batch or prompt.shape[1] < 1:
+            raise ValueError("prompt must be [batch, L] with L >= 1")
+        total = prompt.shape[1]
+        if chunk == 0:
+            logits = None
+            for i in range(total):
+                logits = self.step(prompt[:, i])
+            return logits
+        chunk = self.chunk if chunk is None else int(chunk)
+        if chunk < 1 or (chunk > self.chunk and any(self.ring)):
+            raise ValueError(f"chunk must be in [1, {self.chunk}] (the ring is sized for it)")
+        if self.pos + total > self.capacity:
+            raise ValueError("KV cache is full")
+        b, hid = self.batch, self.cfg.hidden_size
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        prompt = prompt.to(self.device)
+        t = self._prefill_buffers(b * min(chunk, total))
+        for c0 in range(0, total, chunk):
+            lc = min(chunk, total - c0)
+            x = self._prefill_chunk(prompt[:, c0:c0 + lc], self.pos + c0, lc, t, stream)
+        self.x.copy_(x.view(b, lc, hid)[:, lc - 1])
+        check(lib().sb_linear_ex(ctypes.byref(self.head_d), stream), "norm + lm_head")
+        self.pos += total
+        return self.logits
 
     def generate(self, prompt, steps):
         """Greedy decode: the ``steps`` tokens after ``prompt`` ([batch, steps], host)."""
@@ -360,11 +501,12 @@ class Spark25Model:
         return torch.stack(out, dim=1).cpu()
 
 
-def load(path, *, batch=1, capacity=None, device="cuda", rotating=True,
+def load(path, *, batch=1, capacity=None, device="cuda", rotating=True, chunk=512,
          model_config: Optional[dict[str, Any]] = None):
     """Load a Spark2_5 MLX-affine checkpoint directory (``loader.load``,
     ``spark_mlx_llm/loader.py:65-120``: ``config.json`` + ``model*.safetensors``)."""
     config, weights = load_checkpoint_dir(path)
     config = dict(config, **(model_config or {}))
     cfg = Spark25Config.from_dict(config)
-    return Spark25Model(cfg, weights, batch=batch, capacity=capacity, device=device, rotating=rotating)
+    return Spark25Model(cfg, weights, batch=batch, capacity=capacity, device=device, rotating=rotating,
+                        chunk=chunk)

@@ -82,6 +82,44 @@ def test_prefill_attention_matches_oracle(case):
     np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
 
 
+WINDOW_CASES = [
+    # batch, heads, kv_heads, q_len, length, window, layout, head_dim
+    (2, 16, 4, 37, 48, 12, 1, 256),   # a prompt chunk of a sliding layer (window < chunk)
+    (1, 16, 4, 8, 19, 12, 1, 256),    # chunk after the first: window - 1 earlier keys + the chunk
+    (1, 32, 8, 130, 700, 64, 0, 128),
+    (2, 8, 8, 70, 150, 200, 1, 128),  # a window longer than the context: plain causal
+]
+
+
+@pytest.mark.parametrize("case", WINDOW_CASES)
+def test_int8_prefill_window_matches_oracle(case):
+    """sb_int8_sdpa_prefill_window: bottom-right causal with a sliding window
+    over the INT8 cache vs the float64 masked attention over the dequantized
+    cache."""
+    _need_cuda()
+    from spark_b200._lib import check, lib
+
+    b, h, kh, ql, n, window, layout, d = case
+    cap = ((n + 15) // 16) * 16 + 16
+    rng = np.random.default_rng(sum(case[:6]))
+    k, ks, v, vs = _kv(rng, b, kh, cap, d)
+    q = torch.randn(b, h, ql, d, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    dev = [t.cuda() for t in (k, ks, v, vs)]
+    q_dev = (q if layout == 0 else q.permute(0, 2, 1, 3)).contiguous().cuda()
+    out = torch.empty_like(q_dev)
+    scale = 1.0 / math.sqrt(d)
+    check(lib().sb_int8_sdpa_prefill_window(q_dev.data_ptr(), dev[0].data_ptr(), dev[1].data_ptr(),
+                                             dev[2].data_ptr(), dev[3].data_ptr(), out.data_ptr(), b, h, kh, ql, n,
+                                             cap, d, scale, window, layout, torch.cuda.current_stream().cuda_stream),
+          "prefill window")
+    torch.cuda.synchronize()
+    got = _f32(out if layout == 0 else out.permute(0, 2, 1, 3))
+    kd = k[:, :, :n].numpy().astype(np.float64) * ks[:, :, :n].numpy().astype(np.float64)[..., None]
+    vd = v[:, :, :n].numpy().astype(np.float64) * vs[:, :, :n].numpy().astype(np.float64)[..., None]
+    ref = oracle_ops.sdpa_masked(_f32(q), kd, vd, scale, causal=True, window=window)
+    np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
+
+
 def test_prefill_attention_single_query_equals_decode_kernel():
     _need_cuda()
     from spark_b200 import ops

@@ -43,9 +43,9 @@ def test_spark25_checkpoint_decodes_like_the_oracle(tmp_path, rotating):
     from spark_b200.checkpoint import load_checkpoint_dir
 
     write_checkpoint(tmp_path, seed=5)
-    model = spark25.load(tmp_path, batch=BATCH, capacity=64, rotating=rotating)
-    if rotating:
-        assert model.k_cache[0].shape[2] == 16 and model.k_cache[3].shape[2] == 64  # ring vs full layer
+    model = spark25.load(tmp_path, batch=BATCH, capacity=64, rotating=rotating, chunk=4)
+    if rotating:  # a 16-slot ring stored twice vs the full layer's linear cache
+        assert model.k_cache[0].shape[2] == 32 and model.k_cache[3].shape[2] == 64
     config, weights = load_checkpoint_dir(tmp_path)
     orc = Spark25Oracle(model.cfg, spark25.sanitize(weights), BATCH)
     rng = np.random.default_rng(7)
@@ -74,6 +74,57 @@ def test_spark25_checkpoint_decodes_like_the_oracle(tmp_path, rotating):
     assert beyond <= 0.001 * total
     assert head_worst <= 1.0
     assert checked >= BATCH * (PROMPT + STEPS) - 2
+
+
+@pytest.mark.parametrize("rotating", [True, False])
+def test_spark25_chunked_prompt_like_the_oracle(tmp_path, rotating):
+    """The prompt in chunks of 8 positions (37 = 4 x 8 + 5; batched tensor-core
+    linears at M = 16 and 10, RoPE + append per chunk, the windowed INT8
+    multi-query attention; on a 32-slot ring the prompt wraps it), then decode
+    steps, against the oracle stepping the same tokens. Criteria as above; the
+    hidden state is checked after the prompt and after each decode step."""
+    if not torch.cuda.is_available():
+        pytest.skip("needs a CUDA device")
+    from oracle.spark25 import Spark25Oracle
+    from spark_b200 import spark25
+    from spark_b200.checkpoint import load_checkpoint_dir
+
+    prompt_len, steps = 37, 6
+    write_checkpoint(tmp_path, seed=6)
+    model = spark25.load(tmp_path, batch=BATCH, capacity=128, rotating=rotating, chunk=8)
+    assert model.ring[0] == (32 if rotating else 0) and model.ring[3] == 0
+    config, weights = load_checkpoint_dir(tmp_path)
+    orc = Spark25Oracle(model.cfg, spark25.sanitize(weights), BATCH)
+    rng = np.random.default_rng(8)
+    tokens = rng.integers(0, model.cfg.vocab_size, (BATCH, prompt_len))
+    got = model.prefill(torch.from_numpy(tokens.astype(np.int32))).float().cpu().numpy()
+    for i in range(prompt_len):
+        orc.step(tokens[:, i])
+    assert model.pos == prompt_len
+    worst, beyond, total, head_worst, checked = 0.0, 0, 0, 0.0, 0
+    for i in range(steps + 1):
+        if i:
+            got = model.step(torch.from_numpy(next_tok.astype(np.int32))).float().cpu().numpy()
+            orc.step(next_tok)
+        hidden = model.x.float().cpu().numpy()
+        e = _err(hidden, orc.last_hidden)
+        worst = max(worst, float(e.max()))
+        beyond += int((e > 1).sum())
+        total += e.size
+        want = orc.head(hidden)
+        head_worst = max(head_worst, float(_err(got, want).max()))
+        next_tok = got.argmax(axis=-1)
+        top2 = np.sort(want, axis=-1)[:, -2:]
+        for bi in range(BATCH):
+            if top2[bi, 1] - top2[bi, 0] > 1e-3:
+                assert next_tok[bi] == want[bi].argmax(), (i, bi)
+                checked += 1
+    print({"hidden_worst_error_over_tolerance": worst, "hidden_beyond": beyond, "elements": total,
+           "head_worst_error_over_tolerance": head_worst, "decisive_tokens": checked})
+    assert worst <= 1.5
+    assert beyond <= 0.001 * total
+    assert head_worst <= 1.0
+    assert checked >= BATCH * (steps + 1) - 2
 
 
 def test_spark25_rejects_incomplete_checkpoint(tmp_path):

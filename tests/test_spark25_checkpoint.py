@@ -92,3 +92,36 @@ def test_oracle_window_matters(tmp_path):
     outs = [(a.step(t), b.step(t)) for t in tokens]
     assert np.all(np.isfinite(outs[-1][0]))
     assert not np.array_equal(outs[-1][0], outs[-1][1])
+
+
+@pytest.mark.parametrize("window,chunk,prompt", [(12, 8, 37), (12, 4, 14), (5, 16, 70), (17, 1, 40)])
+def test_mirrored_ring_keeps_every_window_contiguous(window, chunk, prompt):
+    """Host logic of the rotating cache: position p written to ring slot p % R and
+    to its mirror row p % R + R. After each prompt chunk (and each decode step
+    after the prompt), the rows the attention reads - [start % R, start % R + n)
+    with start the first position in the window - hold exactly the positions
+    start .. start + n - 1 in order."""
+    from spark_b200.spark25 import ring_slots
+
+    r = ring_slots(window, chunk, 1 << 20)
+    assert r >= window + chunk - 1 and r % 16 == 0
+    assert ring_slots(window, chunk, 2 * r) == 0  # no smaller than the cache: linear
+    rows = [None] * (2 * r)
+
+    def append(p):
+        rows[p % r] = rows[p % r + r] = p
+
+    def check(c0, lc):
+        start = max(0, c0 - window + 1)
+        n = c0 + lc - start
+        assert n <= r
+        assert rows[start % r:start % r + n] == list(range(start, c0 + lc))
+
+    for c0 in range(0, prompt, chunk):
+        lc = min(chunk, prompt - c0)
+        for p in range(c0, c0 + lc):
+            append(p)
+        check(c0, lc)
+    for p in range(prompt, prompt + 3 * r):  # decode: one position per step
+        append(p)
+        check(p, 1)
