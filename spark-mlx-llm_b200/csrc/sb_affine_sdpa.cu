@@ -204,8 +204,10 @@ __global__ void __launch_bounds__(kAffSdpaThreads) affine_sdpa_kernel(const Affi
 // per lane) added by a butterfly, so every lane holds every head's score; the
 // online softmax is in fp32 (exp2); P.V accumulates per lane. Warps merge in
 // shared memory and splits through the workspace (the last CTA of a KV head
-// adds them in split order).
+// adds them in split order). A split's partial is [o (D floats), m, l, pad 2]:
+// the stride D + 4 keeps every partial row 16-byte aligned for float4 reads.
 constexpr int kAffDecWarps = 8;
+constexpr int kAffDecPad = 4;
 
 // the lane's E codes of a row as raw words (unpacked where they are used)
 template <int BITS, int E>
@@ -303,13 +305,19 @@ __global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 1024 ? 2 : 1)
       for (int gi = 0; gi < G; ++gi) {
         if (!live) continue;
         const float s2 = sc[gi] * sl2;
-        const float mn = fmaxf(m_run[gi], s2);
-        const float alpha = m_run[gi] == -INFINITY ? 0.f : exp2f(m_run[gi] - mn);
-        const float pr = exp2f(s2 - mn);
-        l_run[gi] = fmaf(l_run[gi], alpha, pr);
-        m_run[gi] = mn;
+        // rescale only when the maximum rises; the butterfly leaves every lane
+        // the same sum, so the branch is uniform across the warp
+        if (s2 > m_run[gi]) {
+          const float alpha = m_run[gi] == -INFINITY ? 0.f : exp2f(m_run[gi] - s2);
+          l_run[gi] *= alpha;
 #pragma unroll
-        for (int e = 0; e < E; ++e) o[gi][e] = fmaf(o[gi][e], alpha, pr * v[e]);
+          for (int e = 0; e < E; ++e) o[gi][e] *= alpha;
+          m_run[gi] = s2;
+        }
+        const float pr = exp2f(s2 - m_run[gi]);
+        l_run[gi] += pr;
+#pragma unroll
+        for (int e = 0; e < E; ++e) o[gi][e] = fmaf(pr, v[e], o[gi][e]);
       }
     }
   }
@@ -347,7 +355,7 @@ __global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 1024 ? 2 : 1)
     if (single) {
       static_cast<T*>(p.out)[row * D + d] = from_float<T>(ll > 0.f ? oo / ll : 0.f);
     } else {
-      float* part = p.partial + (row * p.splits + split) * (D + 2);
+      float* part = p.partial + (row * p.splits + split) * (D + kAffDecPad);
       part[d] = oo;
       if (d == 0) {
         part[D] = mm;
@@ -363,20 +371,53 @@ __global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 1024 ? 2 : 1)
   __syncthreads();
   if (s_prev != static_cast<unsigned>(p.splits - 1)) return;
   __threadfence();
-  for (int idx = threadIdx.x; idx < G * D; idx += kAffDecWarps * 32) {
-    const int gi = idx / D, d = idx % D;
-    const size_t row = static_cast<size_t>(b) * p.heads + kh * G + gi;
-    const float* base = p.partial + row * p.splits * (D + 2);
+  // Merge: one warp per query head turns the splits' maxima into weights
+  // w = exp2(m_sp - max) and the denominator sum(l_sp * w) (in shared memory,
+  // which the warp partials no longer use), then every thread adds four
+  // output columns over the splits with float4 loads.
+  constexpr int kPS = D + kAffDecPad;
+  const int S = p.splits;
+  const size_t row0 = static_cast<size_t>(b) * p.heads + kh * G;
+  float* sw = dsm;                             // [G][kAffSdpaMaxSplits]
+  float* sden = dsm + G * kAffSdpaMaxSplits;  // [G]
+  if (warp < G) {
+    const float* base = p.partial + (row0 + warp) * S * kPS;
     float mm = -INFINITY;
-    for (int sp = 0; sp < p.splits; ++sp) mm = fmaxf(mm, __ldcg(base + sp * (D + 2) + D));
-    float ll = 0.f, oo = 0.f;
-    for (int sp = 0; sp < p.splits; ++sp) {
-      const float ms = __ldcg(base + sp * (D + 2) + D);
+    for (int sp = lane; sp < S; sp += 32) mm = fmaxf(mm, __ldcg(base + sp * kPS + D));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
+    float ll = 0.f;
+    for (int sp = lane; sp < S; sp += 32) {
+      const float ms = __ldcg(base + sp * kPS + D);
       const float w = ms == -INFINITY ? 0.f : exp2f(ms - mm);
-      ll = fmaf(__ldcg(base + sp * (D + 2) + D + 1), w, ll);
-      oo = fmaf(__ldcg(base + sp * (D + 2) + d), w, oo);
+      sw[warp * kAffSdpaMaxSplits + sp] = w;
+      ll = fmaf(__ldcg(base + sp * kPS + D + 1), w, ll);
     }
-    static_cast<T*>(p.out)[row * D + d] = from_float<T>(ll > 0.f ? oo / ll : 0.f);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ll += __shfl_xor_sync(0xffffffffu, ll, off);
+    if (lane == 0) sden[warp] = ll;
+  }
+  __syncthreads();
+  for (int v4 = threadIdx.x; v4 < G * D / 4; v4 += kAffDecWarps * 32) {
+    const int gi = (4 * v4) / D, d = (4 * v4) % D;
+    const float* base = p.partial + (row0 + gi) * S * kPS + d;
+    const float* w = sw + gi * kAffSdpaMaxSplits;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int sp = 0; sp < S; ++sp) {
+      const float4 o4 = __ldcg(reinterpret_cast<const float4*>(base + static_cast<size_t>(sp) * kPS));
+      const float ws = w[sp];
+      acc.x = fmaf(o4.x, ws, acc.x);
+      acc.y = fmaf(o4.y, ws, acc.y);
+      acc.z = fmaf(o4.z, ws, acc.z);
+      acc.w = fmaf(o4.w, ws, acc.w);
+    }
+    const float ll = sden[gi];
+    T* dst = static_cast<T*>(p.out) + (row0 + gi) * D + d;
+    dst[0] = from_float<T>(ll > 0.f ? acc.x / ll : 0.f);
+    dst[1] = from_float<T>(ll > 0.f ? acc.y / ll : 0.f);
+    dst[2] = from_float<T>(ll > 0.f ? acc.z / ll : 0.f);
+    dst[3] = from_float<T>(ll > 0.f ? acc.w / ll : 0.f);
   }
   if (threadIdx.x == 0) p.counters[bkv] = 0u;
 }
@@ -421,9 +462,19 @@ int affine_splits(int64_t rows, int64_t n) {
   return std::max(1, std::min(s, kAffSdpaMaxSplits));
 }
 
+// Token splits of the single-query decode kernel: one wave of CTAs over the
+// (batch, KV head) pairs (two CTAs per SM up to G x D = 1024, else one), at
+// least 64 tokens per split, at most kAffSdpaMaxSplits.
+int64_t affine_decode_splits(int64_t bkv, int64_t n, int64_t slots) {
+  int64_t sp = std::max<int64_t>(1, (slots + bkv - 1) / bkv);
+  sp = std::min<int64_t>(sp, std::max<int64_t>(1, n / 64));
+  return std::min<int64_t>(sp, kAffSdpaMaxSplits);
+}
+
 size_t affine_ws_bytes(int64_t rows, int splits, int dv) {
   if (splits <= 1) return 0;
-  return kCounterBytes + static_cast<size_t>(rows) * splits * (dv + 2) * sizeof(float);
+  // (dv + 4 floats per partial: the decode kernel's aligned stride; the general kernel uses dv + 2)
+  return kCounterBytes + static_cast<size_t>(rows) * splits * (dv + kAffDecPad) * sizeof(float);
 }
 
 }  // namespace
@@ -434,7 +485,12 @@ using namespace sb;
 
 extern "C" size_t sb_affine_sdpa_workspace_size(int64_t batch, int num_heads, int64_t length, int64_t n, int dv) {
   const int64_t rows = batch * num_heads * length;
-  return affine_ws_bytes(rows, affine_splits(rows, n), dv);
+  int splits = affine_splits(rows, n);
+  // single-query decode: the most splits the decode kernel can plan (at least
+  // rows / 8 KV-head pairs, 296 CTA slots)
+  if (length == 1)
+    splits = std::max(splits, static_cast<int>(affine_decode_splits(std::max<int64_t>(1, (rows + 7) / 8), n, 296)));
+  return affine_ws_bytes(rows, splits, dv);
 }
 
 extern "C" int sb_affine_sdpa(const void* q, int dtype, const void* k_packed, const void* k_scales,
@@ -489,14 +545,14 @@ extern "C" int sb_affine_sdpa(const void* q, int dtype, const void* k_packed, co
   if (length == 1 && dk == dv && (dk == 64 || dk == 128 || dk == 256) && (bits == 4 || bits == 8) &&
       (G == 1 || G == 2 || G == 4 || G == 8) && (dtype == SB_DTYPE_BF16 || dtype == SB_DTYPE_F16) &&
       rows_aligned && batch * num_kv_heads < 65536) {
-    // one wave of CTAs (two per SM up to G x D = 1024, else one), at least 64 tokens per split,
-    // within the workspace's split count
     const int64_t bkv = batch * num_kv_heads;
-    const int64_t slots = G * dk <= 1024 ? 296 : 148;
-    int64_t sp = std::max<int64_t>(1, (slots + bkv - 1) / bkv);
-    sp = std::min<int64_t>(sp, std::max<int64_t>(1, n / 64));
-    p.splits = static_cast<int>(std::min<int64_t>(sp, p.splits));
-    if (p.splits > 1 && p.counters == nullptr) p.splits = 1;
+    p.splits = static_cast<int>(affine_decode_splits(bkv, n, G * dk <= 1024 ? 296 : 148));
+    // the merge reads the partials as float4: a workspace off 16 bytes (or too small) runs one split
+    if (p.splits > 1 && (workspace == nullptr || workspace_bytes < affine_ws_bytes(rows, p.splits, dv) ||
+                         rows > kMaxCounters || reinterpret_cast<uintptr_t>(workspace) % 16 != 0))
+      p.splits = 1;
+    p.counters = p.splits > 1 ? static_cast<unsigned*>(workspace) : nullptr;
+    p.partial = p.splits > 1 ? reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + kCounterBytes) : nullptr;
     if (dtype == SB_DTYPE_BF16)
       return bits == 4 ? affine_decode_by_gqa<__nv_bfloat16, 4>(p, G, s) : affine_decode_by_gqa<__nv_bfloat16, 8>(p, G, s);
     return bits == 4 ? affine_decode_by_gqa<__half, 4>(p, G, s) : affine_decode_by_gqa<__half, 8>(p, G, s);
