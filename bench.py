@@ -570,7 +570,7 @@ def measure_ops(dev, peak_gbs, peak_tflops, peak_kind):
         us = _graph_us(dev, launch, copies)
         rec(f"affine_u8g32_sdpa_d256_b1_{ctx // 1024}k", cache + hq * d * 4, us, 4.0 * hq * ctx * d, bound="hbm",
             batch=1, context=ctx, heads="16/4 x 256", kv_format="MLX affine uint8 G32 (the reference's tuples)",
-            kernel="CUDA cores: one CTA per KV head and token split, lanes on head-dimension slices",
+            kernel="mma.sync on fp16-dequantized 16-token tiles (ldmatrix), one CTA per KV head and token split",
             l2_copies=len(copies))
         del copies
     # ---- INT8-KV prefill attention (chunked prompt), causal over the int8 cache: 32/8 heads x 128

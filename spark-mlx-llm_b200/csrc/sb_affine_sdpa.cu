@@ -18,6 +18,7 @@
 // dimension (coalesced row reads). Splits publish (max, sum, o) partials and
 // the last CTA of a query merges them in split order (deterministic).
 #include <algorithm>
+#include <type_traits>
 
 #include "sb_common.cuh"
 
@@ -233,6 +234,103 @@ __device__ __forceinline__ float code_at(const uint32_t (&w)[2], int e) {
   return static_cast<float>((w[bit >> 5] >> (bit & 31)) & ((1u << BITS) - 1u));
 }
 
+// The end of a single-query decode CTA: the warp partials in shared memory
+// (dsm: [W][G][D] outputs, then [W][G] maxima and [W][G] sums, log2 domain;
+// written before a __syncthreads) -> the CTA's output, or its split partial,
+// and the last CTA of a (batch, KV head) merges the splits: one warp per query
+// head turns the split maxima into weights in shared memory, then each thread
+// adds four output columns over the splits with float4 loads.
+template <typename T, int G, int D, int W>
+__device__ __forceinline__ void affine_decode_finish(const AffineSdpaParams& p, float* dsm, int split, int bkv,
+                                                     int b, int kh) {
+  constexpr int kThreads = W * 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* so = dsm;
+  const float* sm_ = dsm + W * G * D;
+  const float* sl_ = sm_ + W * G;
+  grid_dependency_launch();
+  const bool single = p.splits == 1;
+  for (int idx = threadIdx.x; idx < G * D; idx += kThreads) {
+    const int gi = idx / D, d = idx % D;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < W; ++w) mm = fmaxf(mm, sm_[w * G + gi]);
+    float ll = 0.f, oo = 0.f;
+    if (mm != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < W; ++w) {
+        const float f = sm_[w * G + gi] == -INFINITY ? 0.f : exp2f(sm_[w * G + gi] - mm);
+        ll = fmaf(sl_[w * G + gi], f, ll);
+        oo = fmaf(so[(w * G + gi) * D + d], f, oo);
+      }
+    }
+    const size_t row = static_cast<size_t>(b) * p.heads + kh * G + gi;
+    if (single) {
+      static_cast<T*>(p.out)[row * D + d] = from_float<T>(ll > 0.f ? oo / ll : 0.f);
+    } else {
+      float* part = p.partial + (row * p.splits + split) * (D + kAffDecPad);
+      part[d] = oo;
+      if (d == 0) {
+        part[D] = mm;
+        part[D + 1] = ll;
+      }
+    }
+  }
+  if (single) return;
+  __shared__ unsigned s_prev;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_prev = atomicAdd(p.counters + bkv, 1u);
+  __syncthreads();
+  if (s_prev != static_cast<unsigned>(p.splits - 1)) return;
+  __threadfence();
+  constexpr int kPS = D + kAffDecPad;
+  const int S = p.splits;
+  const size_t row0 = static_cast<size_t>(b) * p.heads + kh * G;
+  float* sw = dsm;                             // [G][kAffSdpaMaxSplits]
+  float* sden = dsm + G * kAffSdpaMaxSplits;  // [G]
+  for (int gi = warp; gi < G; gi += W) {
+    const float* base = p.partial + (row0 + gi) * S * kPS;
+    float mm = -INFINITY;
+    for (int sp = lane; sp < S; sp += 32) mm = fmaxf(mm, __ldcg(base + sp * kPS + D));
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
+    float ll = 0.f;
+    for (int sp = lane; sp < S; sp += 32) {
+      const float ms = __ldcg(base + sp * kPS + D);
+      const float w = ms == -INFINITY ? 0.f : exp2f(ms - mm);
+      sw[gi * kAffSdpaMaxSplits + sp] = w;
+      ll = fmaf(__ldcg(base + sp * kPS + D + 1), w, ll);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ll += __shfl_xor_sync(0xffffffffu, ll, off);
+    if (lane == 0) sden[gi] = ll;
+  }
+  __syncthreads();
+  for (int v4 = threadIdx.x; v4 < G * D / 4; v4 += kThreads) {
+    const int gi = (4 * v4) / D, d = (4 * v4) % D;
+    const float* base = p.partial + (row0 + gi) * S * kPS + d;
+    const float* w = sw + gi * kAffSdpaMaxSplits;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int sp = 0; sp < S; ++sp) {
+      const float4 o4 = __ldcg(reinterpret_cast<const float4*>(base + static_cast<size_t>(sp) * kPS));
+      const float ws = w[sp];
+      acc.x = fmaf(o4.x, ws, acc.x);
+      acc.y = fmaf(o4.y, ws, acc.y);
+      acc.z = fmaf(o4.z, ws, acc.z);
+      acc.w = fmaf(o4.w, ws, acc.w);
+    }
+    const float ll = sden[gi];
+    T* dst = static_cast<T*>(p.out) + (row0 + gi) * D + d;
+    dst[0] = from_float<T>(ll > 0.f ? acc.x / ll : 0.f);
+    dst[1] = from_float<T>(ll > 0.f ? acc.y / ll : 0.f);
+    dst[2] = from_float<T>(ll > 0.f ? acc.z / ll : 0.f);
+    dst[3] = from_float<T>(ll > 0.f ? acc.w / ll : 0.f);
+  }
+  if (threadIdx.x == 0) p.counters[bkv] = 0u;
+}
+
 template <typename T, int BITS, int G, int D>
 __global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 1024 ? 2 : 1)
     affine_decode_kernel(const AffineSdpaParams p) {
@@ -335,91 +433,238 @@ __global__ void __launch_bounds__(kAffDecWarps * 32, G * D <= 1024 ? 2 : 1)
     }
   }
   __syncthreads();
-  grid_dependency_launch();
-  const bool single = p.splits == 1;
-  for (int idx = threadIdx.x; idx < G * D; idx += kAffDecWarps * 32) {
-    const int gi = idx / D, d = idx % D;
-    float mm = -INFINITY;
+  affine_decode_finish<T, G, D, kAffDecWarps>(p, dsm, split, bkv, b, kh);
+}
+
+// ---------------------------------------------------------------------------
+// Tensor-core single-query decode (head_dim 128 / 256). A CTA of kTcWarps warps
+// takes one (batch, KV head, token split); each warp walks its own 16-token
+// tiles of the split:
+//   1. loads the tile's packed K and V codes (16-byte chunks, one group each)
+//      and their scales and biases, and dequantizes them into fp16 rows in its
+//      shared-memory tiles: code -> 1024 + code under the fp16 exponent of 1024
+//      (prmt), minus 1024 (exact), then one fused s * c + b (fp16, one rounding);
+//   2. S = Q K^T with mma.sync m16n8k16: A = the G query heads (rows g < G, the
+//      rest zero) as fp16, B = the K tile through ldmatrix -> S[head, token];
+//   3. online softmax per head in fp32 (exp2 domain), P rounded to fp16;
+//   4. O^T += V^T P: A = the V tile through ldmatrix.trans (dims x tokens),
+//      B = P straight from S's accumulator layout -> O^T[dim, head] in fp32.
+// The warps' (O, max, sum) then meet in shared memory and the splits in the
+// workspace (affine_decode_finish).
+constexpr int kTcWarps = 4;
+constexpr int kTcTok = 16;  // tokens per warp tile
+
+template <int D>
+struct TcGeo {
+  static constexpr int kStride = D * 2 + 16;      // bytes per fp16 row (ldmatrix without bank conflicts)
+  static constexpr int kTile = kTcTok * kStride;  // one fp16 tile (K or V)
+  static constexpr int kWarpBytes = 2 * kTile;
+  static constexpr int kSmem = kTcWarps * kWarpBytes;
+  static constexpr int kMerge = (kTcWarps * 8 * D + 2 * kTcWarps * 8) * 4;  // finish's [W][G][D] + [W][G] x 2
+  static_assert(kMerge <= kSmem, "the merge reuses the tiles' shared memory");
+};
+
+__device__ __forceinline__ uint32_t tc_pack_half2(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t tc_dequant2(uint32_t biased, __half2 s2, __half2 b2) {
+  // biased = (1024 + c0, 1024 + c1) as fp16x2 -> (s c0 + b, s c1 + b)
+  const __half2 k1024 = __floats2half2_rn(1024.f, 1024.f);
+  const __half2 c = __hsub2(*reinterpret_cast<const __half2*>(&biased), k1024);
+  const __half2 r = __hfma2(c, s2, b2);
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+__device__ __forceinline__ void ldsm4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+template <typename T, int BITS, int G, int D>
+__global__ void __launch_bounds__(kTcWarps * 32, 2) affine_decode_tc_kernel(const AffineSdpaParams p) {
+  using C = TcGeo<D>;
+  constexpr int kRowBytes = D * BITS / 8;        // packed codes of one token
+  constexpr int kChunks = kRowBytes / 16;        // 16-byte chunks per token row
+  constexpr int kLaneChunks = kTcTok * kChunks / 32;
+  constexpr int kChunkDims = 16 * 8 / BITS;      // dims per chunk (16 or 32)
+  static_assert(kLaneChunks >= 1 && (kTcTok * kChunks) % 32 == 0, "tile chunks must spread over the lanes");
+  extern __shared__ __align__(128) uint8_t tsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, c = lane & 3;
+  const int split = blockIdx.x, bkv = blockIdx.y;
+  const int b = bkv / p.kv_heads, kh = bkv % p.kv_heads;
+  const int ngroups = D / p.group;
+  uint8_t* ktile = tsm + warp * C::kWarpBytes;
+  uint8_t* vtile = ktile + C::kTile;
+  const uint32_t kbase = smem_u32(ktile), vbase = smem_u32(vtile);
+  // ldmatrix lane address: matrix (lane / 8) -> token rows 0-7 / 8-15, dims +0 / +8
+  const int lm = lane >> 3;
+  const uint32_t lrow = static_cast<uint32_t>(((lane & 7) + (lm >> 1) * 8) * C::kStride + (lm & 1) * 16);
+  grid_dependency_wait();
+  const int t_begin = static_cast<int>(static_cast<long long>(p.n) * split / p.splits);
+  const int t_end = static_cast<int>(static_cast<long long>(p.n) * (split + 1) / p.splits);
+  const float sl2 = p.scale * 1.4426950408889634f;
+
+  // query rows as the A operand: row g = head g of the group (zero for g >= G)
+  uint32_t qa[D / 16][2];
+  {
+    const T* qrow = static_cast<const T*>(p.q) + (static_cast<size_t>(b) * p.heads + kh * G + (g < G ? g : 0)) * D;
 #pragma unroll
-    for (int w = 0; w < kAffDecWarps; ++w) mm = fmaxf(mm, sm_[w * G + gi]);
-    float ll = 0.f, oo = 0.f;
-    if (mm != -INFINITY) {
+    for (int ks = 0; ks < D / 16; ++ks) {
+      const int d0 = 16 * ks + 2 * c;
+      qa[ks][0] = g < G ? tc_pack_half2(to_float(qrow[d0]), to_float(qrow[d0 + 1])) : 0u;
+      qa[ks][1] = g < G ? tc_pack_half2(to_float(qrow[d0 + 8]), to_float(qrow[d0 + 9])) : 0u;
+    }
+  }
+  float o[D / 16][4];
 #pragma unroll
-      for (int w = 0; w < kAffDecWarps; ++w) {
-        const float f = sm_[w * G + gi] == -INFINITY ? 0.f : exp2f(sm_[w * G + gi] - mm);
-        ll = fmaf(sl_[w * G + gi], f, ll);
-        oo = fmaf(so[(w * G + gi) * D + d], f, oo);
+  for (int mt = 0; mt < D / 16; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // head g (the same in the four lanes of g)
+
+  const uint8_t* kp = reinterpret_cast<const uint8_t*>(p.kp) + static_cast<size_t>(bkv) * p.n * kRowBytes;
+  const uint8_t* vp = reinterpret_cast<const uint8_t*>(p.vp) + static_cast<size_t>(bkv) * p.n * kRowBytes;
+  const T* ksc = static_cast<const T*>(p.ks) + static_cast<size_t>(bkv) * p.n * ngroups;
+  const T* kbi = static_cast<const T*>(p.kb) + static_cast<size_t>(bkv) * p.n * ngroups;
+  const T* vsc = static_cast<const T*>(p.vs) + static_cast<size_t>(bkv) * p.n * ngroups;
+  const T* vbi = static_cast<const T*>(p.vb) + static_cast<size_t>(bkv) * p.n * ngroups;
+
+  for (int t0 = t_begin + warp * kTcTok; t0 < t_end; t0 += kTcWarps * kTcTok) {
+    // ---- 1. codes -> fp16 rows (tokens past the split repeat its last token; masked below)
+    uint4 kc[kLaneChunks], vc[kLaneChunks];
+    uint32_t ksb[kLaneChunks], vsb[kLaneChunks];  // scale bits | bias bits << 16
+#pragma unroll
+    for (int j = 0; j < kLaneChunks; ++j) {
+      const int idx = lane + 32 * j, row = idx / kChunks, col = idx % kChunks;
+      const int tok = min(t0 + row, t_end - 1);
+      const size_t off = static_cast<size_t>(tok) * kRowBytes + col * 16;
+      kc[j] = ldg_stream16(kp + off);
+      vc[j] = ldg_stream16(vp + off);
+      const size_t gi = static_cast<size_t>(tok) * ngroups + (col * kChunkDims) / p.group;
+      ksb[j] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(ksc + gi)) |
+               static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(kbi + gi)) << 16;
+      vsb[j] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(vsc + gi)) |
+               static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(vbi + gi)) << 16;
+    }
+    __syncwarp();  // the previous tile's ldmatrix reads are done before the tiles are rewritten
+#pragma unroll
+    for (int j = 0; j < kLaneChunks; ++j) {
+      const int idx = lane + 32 * j, row = idx / kChunks, col = idx % kChunks;
+#pragma unroll
+      for (int kv = 0; kv < 2; ++kv) {
+        const uint4 w = kv ? vc[j] : kc[j];
+        const uint32_t sb = kv ? vsb[j] : ksb[j], sbits = sb & 0xFFFFu, bbits = sb >> 16;
+        float sf, bf;
+        if constexpr (std::is_same<T, __half>::value) {
+          sf = __half2float(__ushort_as_half(static_cast<unsigned short>(sbits)));
+          bf = __half2float(__ushort_as_half(static_cast<unsigned short>(bbits)));
+        } else {
+          sf = __uint_as_float(sbits << 16);
+          bf = __uint_as_float(bbits << 16);
+        }
+        const __half2 s2 = __float2half2_rn(sf), b2 = __float2half2_rn(bf);
+        uint8_t* dst = (kv ? vtile : ktile) + row * C::kStride + col * kChunkDims * 2;
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        if constexpr (BITS == 8) {
+          uint32_t h[8];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            h[2 * i] = tc_dequant2(prmt(ws[i], 0x64646464u, 0x4140u), s2, b2);
+            h[2 * i + 1] = tc_dequant2(prmt(ws[i], 0x64646464u, 0x4342u), s2, b2);
+          }
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(h[0], h[1], h[2], h[3]);
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(h[4], h[5], h[6], h[7]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            // nibble j of the word is dim 8 i + j
+            const uint32_t lo = ws[i] & 0x0F0F0F0Fu, hi = (ws[i] >> 4) & 0x0F0F0F0Fu;
+            const uint32_t a = prmt(lo, hi, 0x5140u), bb = prmt(lo, hi, 0x7362u);  // nibbles 0-3, 4-7
+            reinterpret_cast<uint4*>(dst)[i] =
+                make_uint4(tc_dequant2(prmt(a, 0x64646464u, 0x4140u), s2, b2),
+                           tc_dequant2(prmt(a, 0x64646464u, 0x4342u), s2, b2),
+                           tc_dequant2(prmt(bb, 0x64646464u, 0x4140u), s2, b2),
+                           tc_dequant2(prmt(bb, 0x64646464u, 0x4342u), s2, b2));
+          }
+        }
       }
     }
-    const size_t row = static_cast<size_t>(b) * p.heads + kh * G + gi;
-    if (single) {
-      static_cast<T*>(p.out)[row * D + d] = from_float<T>(ll > 0.f ? oo / ll : 0.f);
-    } else {
-      float* part = p.partial + (row * p.splits + split) * (D + kAffDecPad);
-      part[d] = oo;
-      if (d == 0) {
-        part[D] = mm;
-        part[D + 1] = ll;
+    __syncwarp();
+    // ---- 2. S[head, token] for tokens t0 + (0..7) and t0 + (8..15)
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int ks = 0; ks < D / 16; ++ks) {
+      uint32_t kb[4];
+      ldsm4(kb, kbase + lrow + ks * 32);
+      const uint32_t a[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+      mma_16816<true>(s0, a, kb[0], kb[1]);
+      mma_16816<true>(s1, a, kb[2], kb[3]);
+    }
+    // ---- 3. online softmax of head g over the tile (lanes 4g..4g+3 hold its 16 tokens)
+    const int tk = t0 + 2 * c;
+    float x[4] = {tk < t_end ? s0[0] * sl2 : -INFINITY, tk + 1 < t_end ? s0[1] * sl2 : -INFINITY,
+                  tk + 8 < t_end ? s1[0] * sl2 : -INFINITY, tk + 9 < t_end ? s1[1] * sl2 : -INFINITY};
+    float tmax = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+    tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+    const float m_new = fmaxf(m_run, tmax);  // finite: token t0 is in the split
+    const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+    float pr[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) pr[i] = exp2f(x[i] - m_new);
+    l_run = fmaf(l_run, alpha, (pr[0] + pr[1]) + (pr[2] + pr[3]));
+    m_run = m_new;
+    // O^T columns are heads 2c and 2c + 1: their factors live in lanes 8c and 8c + 4
+    const float a0 = __shfl_sync(0xffffffffu, alpha, 8 * c), a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
+    if (__any_sync(0xffffffffu, a0 != 1.f || a1 != 1.f)) {
+#pragma unroll
+      for (int mt = 0; mt < D / 16; ++mt) {
+        o[mt][0] *= a0;
+        o[mt][1] *= a1;
+        o[mt][2] *= a0;
+        o[mt][3] *= a1;
       }
     }
-  }
-  if (single) return;
-  __shared__ unsigned s_prev;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_prev = atomicAdd(p.counters + bkv, 1u);
-  __syncthreads();
-  if (s_prev != static_cast<unsigned>(p.splits - 1)) return;
-  __threadfence();
-  // Merge: one warp per query head turns the splits' maxima into weights
-  // w = exp2(m_sp - max) and the denominator sum(l_sp * w) (in shared memory,
-  // which the warp partials no longer use), then every thread adds four
-  // output columns over the splits with float4 loads.
-  constexpr int kPS = D + kAffDecPad;
-  const int S = p.splits;
-  const size_t row0 = static_cast<size_t>(b) * p.heads + kh * G;
-  float* sw = dsm;                             // [G][kAffSdpaMaxSplits]
-  float* sden = dsm + G * kAffSdpaMaxSplits;  // [G]
-  if (warp < G) {
-    const float* base = p.partial + (row0 + warp) * S * kPS;
-    float mm = -INFINITY;
-    for (int sp = lane; sp < S; sp += 32) mm = fmaxf(mm, __ldcg(base + sp * kPS + D));
+    // ---- 4. O^T[dim, head] += V^T[dim, token] P[token, head]
+    const uint32_t pb0 = tc_pack_half2(pr[0], pr[1]), pb1 = tc_pack_half2(pr[2], pr[3]);
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, off));
-    float ll = 0.f;
-    for (int sp = lane; sp < S; sp += 32) {
-      const float ms = __ldcg(base + sp * kPS + D);
-      const float w = ms == -INFINITY ? 0.f : exp2f(ms - mm);
-      sw[warp * kAffSdpaMaxSplits + sp] = w;
-      ll = fmaf(__ldcg(base + sp * kPS + D + 1), w, ll);
+    for (int mt = 0; mt < D / 16; ++mt) {
+      uint32_t va[4];
+      ldsm4_trans(va, vbase + lrow + mt * 32);
+      mma_16816<true>(o[mt], va, pb0, pb1);
     }
+  }
+  // ---- warp partials -> shared memory (the tiles are free once every warp is done)
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  __syncthreads();
+  float* dsm = reinterpret_cast<float*>(tsm);
+  float* so = dsm;
+  float* sm_ = dsm + kTcWarps * G * D;
+  float* sl_ = sm_ + kTcWarps * G;
 #pragma unroll
-    for (int off = 16; off > 0; off >>= 1) ll += __shfl_xor_sync(0xffffffffu, ll, off);
-    if (lane == 0) sden[warp] = ll;
+  for (int mt = 0; mt < D / 16; ++mt) {
+    const int d0 = 16 * mt + g;
+    if (2 * c < G) {
+      so[(warp * G + 2 * c) * D + d0] = o[mt][0];
+      so[(warp * G + 2 * c) * D + d0 + 8] = o[mt][2];
+    }
+    if (2 * c + 1 < G) {
+      so[(warp * G + 2 * c + 1) * D + d0] = o[mt][1];
+      so[(warp * G + 2 * c + 1) * D + d0 + 8] = o[mt][3];
+    }
+  }
+  if (c == 0 && g < G) {
+    sm_[warp * G + g] = m_run;
+    sl_[warp * G + g] = l_run;
   }
   __syncthreads();
-  for (int v4 = threadIdx.x; v4 < G * D / 4; v4 += kAffDecWarps * 32) {
-    const int gi = (4 * v4) / D, d = (4 * v4) % D;
-    const float* base = p.partial + (row0 + gi) * S * kPS + d;
-    const float* w = sw + gi * kAffSdpaMaxSplits;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int sp = 0; sp < S; ++sp) {
-      const float4 o4 = __ldcg(reinterpret_cast<const float4*>(base + static_cast<size_t>(sp) * kPS));
-      const float ws = w[sp];
-      acc.x = fmaf(o4.x, ws, acc.x);
-      acc.y = fmaf(o4.y, ws, acc.y);
-      acc.z = fmaf(o4.z, ws, acc.z);
-      acc.w = fmaf(o4.w, ws, acc.w);
-    }
-    const float ll = sden[gi];
-    T* dst = static_cast<T*>(p.out) + (row0 + gi) * D + d;
-    dst[0] = from_float<T>(ll > 0.f ? acc.x / ll : 0.f);
-    dst[1] = from_float<T>(ll > 0.f ? acc.y / ll : 0.f);
-    dst[2] = from_float<T>(ll > 0.f ? acc.z / ll : 0.f);
-    dst[3] = from_float<T>(ll > 0.f ? acc.w / ll : 0.f);
-  }
-  if (threadIdx.x == 0) p.counters[bkv] = 0u;
+  affine_decode_finish<T, G, D, kTcWarps>(p, dsm, split, bkv, b, kh);
 }
 
 namespace {
@@ -436,12 +681,23 @@ int launch_affine_decode(const AffineSdpaParams& p, cudaStream_t s) {
                 s, p);
 }
 
+template <typename T, int BITS, int G, int D>
+int launch_affine_decode_tc(const AffineSdpaParams& p, cudaStream_t s) {
+  constexpr int smem = TcGeo<D>::kSmem;
+  auto kernel = affine_decode_tc_kernel<T, BITS, G, D>;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return fail(SB_ECUDA, std::string("affine decode attribute: ") + cudaGetErrorString(e));
+  return launch("affine_sdpa_decode_tc", kernel, dim3(p.splits, p.batch * p.kv_heads), dim3(kTcWarps * 32), smem,
+                s, p);
+}
+
+// head_dim 128 / 256 run the tensor-core kernel, 64 the CUDA-core one
 template <typename T, int BITS, int G>
 int affine_decode_by_dim(const AffineSdpaParams& p, cudaStream_t s) {
   switch (p.dk) {
     case 64: return launch_affine_decode<T, BITS, G, 64>(p, s);
-    case 128: return launch_affine_decode<T, BITS, G, 128>(p, s);
-    default: return launch_affine_decode<T, BITS, G, 256>(p, s);
+    case 128: return launch_affine_decode_tc<T, BITS, G, 128>(p, s);
+    default: return launch_affine_decode_tc<T, BITS, G, 256>(p, s);
   }
 }
 
@@ -540,13 +796,15 @@ extern "C" int sb_affine_sdpa(const void* q, int dtype, const void* k_packed, co
   cudaStream_t s = as_stream(stream);
   // single-query decode of the common shapes: the KV-head-per-CTA kernel
   const int G = num_heads / num_kv_heads;
-  const bool rows_aligned = reinterpret_cast<uintptr_t>(k_packed) % 8 == 0 &&
-                            reinterpret_cast<uintptr_t>(v_packed) % 8 == 0;
+  // code rows are read as 8-byte (head_dim 64) or 16-byte (128 / 256, the tensor-core kernel) chunks
+  const uintptr_t row_align = dk >= 128 ? 16 : 8;
+  const bool rows_aligned = reinterpret_cast<uintptr_t>(k_packed) % row_align == 0 &&
+                            reinterpret_cast<uintptr_t>(v_packed) % row_align == 0;
   if (length == 1 && dk == dv && (dk == 64 || dk == 128 || dk == 256) && (bits == 4 || bits == 8) &&
       (G == 1 || G == 2 || G == 4 || G == 8) && (dtype == SB_DTYPE_BF16 || dtype == SB_DTYPE_F16) &&
       rows_aligned && batch * num_kv_heads < 65536) {
     const int64_t bkv = batch * num_kv_heads;
-    p.splits = static_cast<int>(affine_decode_splits(bkv, n, G * dk <= 1024 ? 296 : 148));
+    p.splits = static_cast<int>(affine_decode_splits(bkv, n, 296));  // two CTAs per SM
     // the merge reads the partials as float4: a workspace off 16 bytes (or too small) runs one split
     if (p.splits > 1 && (workspace == nullptr || workspace_bytes < affine_ws_bytes(rows, p.splits, dv) ||
                          rows > kMaxCounters || reinterpret_cast<uintptr_t>(workspace) % 16 != 0))

@@ -103,6 +103,10 @@ def affine_kv(rng, bsz, kvh, n, dim, group, bits):
         (2, 8, 1, 1, 1000, 128, 128, 4, None),
         (3, 8, 8, 1, 300, 64, 32, 8, None),
         (1, 16, 4, 1, 37, 256, 32, 4, "causal"),
+        # the tensor-core kernel (head_dim 128 / 256) at GQA 1 and 2, ragged tiles
+        (1, 8, 8, 1, 333, 256, 64, 8, None),
+        (2, 16, 8, 1, 2000, 128, 32, 8, None),
+        (1, 32, 4, 1, 3001, 256, 32, 4, None),
     ],
 )
 def test_int8_quantized_sdpa_affine_tuples(api, bsz, heads, kvh, length, n, dim, group, bits, mask):
