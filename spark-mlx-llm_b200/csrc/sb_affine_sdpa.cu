@@ -8,9 +8,10 @@
 // int8_quantized_sdpa.py:178-180), with the bottom-right causal mask for
 // multi-token queries.
 //
-// Single-query decode of the common shapes (head_dim 64/128/256, 4- or 8-bit
-// codes, bf16/fp16) runs affine_decode_kernel (one CTA per KV head and token
-// split, below). Other shapes:
+// Single-query decode of the common shapes (4- or 8-bit codes, bf16/fp16,
+// GQA 1/2/4/8) runs affine_decode_tc_kernel at head_dim 128/256 (tensor cores
+// on fp16-dequantized tiles) and affine_decode_kernel at 64 (CUDA cores), both
+// one CTA per (batch, KV head, token split), below. Other shapes:
 // one CTA per (query row, token split). A thread scores one
 // token per pass (sum over groups of sk * sum(q*code) + bk * sum(q), the
 // reassociation of _int8_sdpa_sources.py); the CTA keeps an online softmax
