@@ -61,3 +61,32 @@ def test_host_side_calls_without_gpu(library):
     assert b"nonempty" in lib.sb_last_error_message()
     assert lib.sb_w8a8_linear(None, 0, None, None, None, 0, None, 1, 8, 33, None, 0, None) == _lib.SB_EINVAL
     assert b"multiple of 32" in lib.sb_last_error_message()
+
+
+def test_affine_sdpa_workspace_covers_the_decode_splits(library):
+    """Single-query decode over affine KV tuples plans up to 64 token splits
+    (one wave of two CTAs per SM over the (batch, KV head) pairs, at least 64
+    tokens each); each split's partial is head_dim + 4 floats per query head,
+    after the 128 KiB counter region."""
+    from spark_b200 import _lib
+
+    lib = _lib.lib()
+    counters = 128 * 1024
+    for batch, heads, n, dv in ((1, 16, 32768, 256), (1, 16, 4096, 256), (2, 32, 5000, 128), (1, 8, 700, 128)):
+        rows = batch * heads
+        splits = min(64, max(1, n // 64), -(-296 // max(1, -(-rows // 8))))
+        need = counters + rows * splits * (dv + 4) * 4 if splits > 1 else 0
+        assert lib.sb_affine_sdpa_workspace_size(batch, heads, 1, n, dv) >= need
+    assert lib.sb_affine_sdpa_workspace_size(1, 16, 1, 40, 256) == 0  # one split: no workspace
+
+
+def test_windowed_prefill_rejects_bad_arguments(library):
+    from spark_b200 import _lib
+
+    lib = _lib.lib()
+    args = [None] * 6 + [1, 16, 4, 8, 8, 16, 256, 0.0625]
+    assert lib.sb_int8_sdpa_prefill_window(*args, 12, 1, None) == _lib.SB_EINVAL
+    assert b"null pointer" in lib.sb_last_error_message()
+    fake = [16, 16, 16, 16, 16, 16]  # never dereferenced: the window check comes first
+    assert lib.sb_int8_sdpa_prefill_window(*fake, *args[6:], -1, 1, None) == _lib.SB_EINVAL
+    assert b"window" in lib.sb_last_error_message()
