@@ -26,3 +26,27 @@ def test_prompt_lookup_drafter():
     assert d([1, 2, 3, 4, 9, 1, 2, 3], 3) == [4, 9, 1]   # continuation of the earlier "1 2 3"
     assert d([7, 1, 2, 5, 1, 2], 2) == [5, 1]            # shorter n-grams when the long one is new
     assert d([1, 2, 3], 2) == []                          # nothing to copy
+
+
+def test_greedy_accept_matches_the_reference_cases():
+    """The cases of ``tests/golden/greedy_accept_cases.json``, produced by the
+    reference's own ``dspark/acceptance.py`` greedy_accept
+    (``tests/golden/make_acceptance_golden.py``): same accepted tokens and counts,
+    and the same error class on invalid inputs."""
+    import json
+    import os
+
+    path = os.path.join(os.path.dirname(__file__), "golden", "greedy_accept_cases.json")
+    with open(path) as f:
+        cases = json.load(f)["cases"]
+    assert len(cases) >= 200
+    for case in cases:
+        if "error" in case:
+            with pytest.raises(ValueError):
+                greedy_accept(case["draft"], case["target"])
+            assert case["error"] == "ValueError"
+            continue
+        r = greedy_accept(case["draft"], case["target"])
+        assert list(r.tokens) == case["tokens"]
+        assert (r.num_drafted, r.num_accepted, r.num_rejected) == (
+            case["num_drafted"], case["num_accepted"], case["num_rejected"])
