@@ -133,6 +133,29 @@ def test_int8_quantized_sdpa_affine_tuples(api, bsz, heads, kvh, length, n, dim,
     np.testing.assert_array_equal(to_f32(out2), to_f32(out))
 
 
+@pytest.mark.parametrize("dim,bits,heads,kvh", [(256, 8, 16, 4), (128, 4, 8, 1)])
+def test_int8_quantized_sdpa_affine_tuples_fp16(api, dim, bits, heads, kvh):
+    """fp16 queries and fp16 scales / biases (the same values as the bf16 case:
+    bf16 metadata converts to fp16 exactly) on the single-query decode kernels."""
+    ext, _ = api
+    rng = np.random.default_rng(dim + bits)
+    n, group = 1500, 32
+    q = formats.round_bf16(rng.standard_normal((1, heads, 1, dim)).astype(np.float32))
+    kp, ks, kb, _, _ = affine_kv(rng, 1, kvh, n, dim, group, bits)
+    vp, vs, vb, _, _ = affine_kv(rng, 1, kvh, n, dim, group, bits)
+    scale = 1.0 / np.sqrt(dim)
+    expected = ref.sdpa_affine(q, (kp, ks, kb), (vp, vs, vb), scale, group, bits)
+
+    def f16(a):
+        return torch.from_numpy(np.asarray(a, np.float32)).to(torch.float16).cuda()
+
+    keys = (u32_tensor(kp), f16(ks), f16(kb))
+    values = (u32_tensor(vp), f16(vs), f16(vb))
+    out = ext.int8_quantized_sdpa(f16(q), keys, values, scale=float(scale), group_size=group, bits=bits)
+    assert out.dtype == torch.float16
+    assert_close(to_f32(out), expected, what="affine-tuple sdpa fp16")
+
+
 def test_dispatch_sdpa_int8_pair(api):
     _, dispatch = api
     rng = np.random.default_rng(31)
