@@ -133,7 +133,7 @@ def test_int8_quantized_sdpa_affine_tuples(api, bsz, heads, kvh, length, n, dim,
     np.testing.assert_array_equal(to_f32(out2), to_f32(out))
 
 
-@pytest.mark.parametrize("dim,bits,heads,kvh", [(256, 8, 16, 4), (128, 4, 8, 1)])
+@pytest.mark.parametrize("dim,bits,heads,kvh", [(256, 8, 16, 4), (128, 4, 8, 1), (64, 8, 4, 2)])
 def test_int8_quantized_sdpa_affine_tuples_fp16(api, dim, bits, heads, kvh):
     """fp16 queries and fp16 scales / biases (the same values as the bf16 case:
     bf16 metadata converts to fp16 exactly) on the single-query decode kernels."""
