@@ -213,8 +213,10 @@ class _Proj:
 
 
 class Spark25Model:
-    """A loaded Spark2_5 checkpoint with its INT8 KV cache and decode buffers;
-    ``step(tokens)`` runs one greedy-decode position for ``batch`` sequences."""
+    """A loaded Spark2_5 checkpoint with its INT8 KV cache and decode buffers.
+    ``prefill(prompt)`` runs a prompt in chunks of up to ``chunk`` positions
+    (the sliding layers' rings are sized for it), ``step(tokens)`` one
+    greedy-decode position for ``batch`` sequences."""
 
     def __init__(self, cfg, weights, *, batch=1, capacity=None, device="cuda", rotating=True, chunk=512):
         self.cfg, self.batch = cfg, batch
