@@ -20,6 +20,7 @@ KV for ``dispatch_sdpa`` is either the B200 INT8 cache pair ``(int8 codes
 ``(packed, scales, biases)``.
 """
 
+import math
 from dataclasses import dataclass, fields
 from typing import NamedTuple
 
@@ -35,6 +36,7 @@ __all__ = [
     "SDPAConfig",
     "PreparedW8",
     "W8A16PerChannelLinear",
+    "W8MultirowProjection",
     "dispatch_linear",
     "dispatch_qkv",
     "dispatch_sdpa",
@@ -175,6 +177,46 @@ class W8A16PerChannelLinear(torch.nn.Module):
 
     def forward(self, x):
         return ext.w8a16_per_channel(x, self.weight, self.scales)
+
+
+class W8MultirowProjection(torch.nn.Module):
+    """W8 out/head projection for the 8-row verification pass, else the affine
+    layer (``spark_mlx_llm/ops/linear.py:479-528``).
+
+    ``fallback`` is the affine 8-bit :class:`QuantizedLinear`; ``weight`` (INT8
+    ``[N, K]``) and ``scales`` (fp32 ``[N]``) are its per-channel form, derived
+    at load time (:func:`unpack_affine_w8`). Exactly 8 BF16 rows on a CUDA
+    device run ``ext.w8a16_multirow`` (the M <= 8 weight-streaming kernel) with
+    the layer's scale dtype as the output dtype; M = 1 decode and prefill keep
+    the affine layer. The accepted shapes are the reference's: the measured
+    out_proj (2560 x 4096) and lm_head (131072 x 2560) geometries."""
+
+    GEOMETRY = ((131072, 2560), (2560, 4096))
+
+    def __init__(self, fallback, weight, scales):
+        super().__init__()
+        if (type(fallback) is not QuantizedLinear or fallback.bits != 8 or fallback.mode != "affine"
+                or fallback.bias is not None or fallback.biases is None
+                or fallback.scales.dtype not in (torch.bfloat16, torch.float32)
+                or fallback.biases.dtype != fallback.scales.dtype
+                or weight.dtype != torch.int8 or tuple(weight.shape) not in self.GEOMETRY
+                or scales.dtype != torch.float32 or tuple(scales.shape) != (weight.shape[0],)
+                or tuple(fallback.weight.shape) != (weight.shape[0], weight.shape[1] // 4)):
+            raise ValueError("Multirow W8 requires measured out/head per-channel geometry")
+        self.fallback = fallback
+        self.register_buffer("weight", weight)
+        self.register_buffer("scales", scales)
+
+    def takes_multirow(self, x):
+        """True when ``x`` is the 8-row BF16 verification input on a GPU."""
+        return (x.ndim >= 2 and math.prod(x.shape[:-1]) == 8 and x.shape[-1] == self.weight.shape[-1]
+                and x.dtype == torch.bfloat16 and x.device.type == "cuda")
+
+    def forward(self, x):
+        if self.takes_multirow(x):
+            return ext.w8a16_multirow(x, self.weight, self.scales, output_dtype=self.fallback.scales.dtype,
+                                      variant="nax", simdgroups=4)
+        return self.fallback(x)
 
 
 class PreparedW8:

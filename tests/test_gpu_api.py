@@ -156,6 +156,28 @@ def test_int8_quantized_sdpa_affine_tuples_fp16(api, dim, bits, heads, kvh):
     assert_close(to_f32(out), expected, what="affine-tuple sdpa fp16")
 
 
+def test_w8_multirow_projection_routes(api):
+    """``dispatch.W8MultirowProjection`` at the reference's out_proj geometry:
+    8 BF16 rows give exactly ``ext.w8a16_multirow``'s result, one row the
+    affine layer's."""
+    ext, dispatch = api
+    n, k, group = 2560, 4096, 64
+    rng = np.random.default_rng(51)
+    wq, ws = quant.quantize_w8_per_channel((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    s_bf16 = formats.round_bf16(np.asarray(ws, np.float32))
+    words = (np.asarray(wq, np.int16) + 128).astype(np.uint8).reshape(n, k // 4, 4)
+    words = words.astype(np.uint32) @ np.array([1, 1 << 8, 1 << 16, 1 << 24], np.uint32)
+    scales = np.repeat(s_bf16[:, None], k // group, axis=1)
+    layer = dispatch.QuantizedLinear(u32_tensor(words), bf16_tensor(scales), bf16_tensor(-128 * scales),
+                                     group_size=group, bits=8)
+    proj = dispatch.W8MultirowProjection(layer, *dispatch.unpack_affine_w8(layer, "out_proj"))
+    x8 = bf16_tensor(formats.round_bf16(rng.standard_normal((8, k)).astype(np.float32)))
+    direct = ext.w8a16_multirow(x8, proj.weight, proj.scales)
+    np.testing.assert_array_equal(to_f32(proj(x8)), to_f32(direct))
+    x1 = x8[:1].contiguous()
+    np.testing.assert_array_equal(to_f32(proj(x1)), to_f32(layer(x1)))
+
+
 def test_dispatch_sdpa_int8_pair(api):
     _, dispatch = api
     rng = np.random.default_rng(31)

@@ -81,3 +81,55 @@ def test_prepared_w8_caches_by_source_identity(golden):
     assert torch.equal(second[0], first[0])
     module = dispatch.W8A16PerChannelLinear.from_affine(layer)
     assert module.weight.dtype == torch.int8 and module.scales.dtype == torch.float32
+
+
+def _w8_layer(n, k, group=64, dtype=torch.bfloat16):
+    words = torch.zeros(n, k // 4, dtype=torch.int32)
+    scales = torch.full((n, k // group), 0.01, dtype=dtype)
+    return dispatch.QuantizedLinear(words, scales, -128 * scales, group_size=group, bits=8)
+
+
+def test_w8_multirow_projection_checks_its_inputs():
+    """``W8MultirowProjection`` (``ops/linear.py:479-528``) accepts an affine
+    8-bit layer with its per-channel INT8 form at the reference's measured
+    out_proj geometry, and raises the reference's error for anything else."""
+    n, k = 2560, 4096
+    layer = _w8_layer(n, k)
+    w, s = dispatch.unpack_affine_w8(layer, "out_proj")
+    proj = dispatch.W8MultirowProjection(layer, w, s)
+    assert proj.fallback is layer and proj.weight.dtype == torch.int8
+    bad = [
+        (SimpleNamespace(**vars(layer)), w, s),                 # not a QuantizedLinear
+        (_w8_layer(n, k, dtype=torch.float16), w, s),           # scales dtype
+        (layer, w.to(torch.int16), s),                          # weight dtype
+        (layer, w, s.double()),                                 # scales dtype
+        (layer, w, s[:-1]),                                     # scales shape
+        (_w8_layer(1024, k), *dispatch.unpack_affine_w8(_w8_layer(1024, k), "p")),  # unmeasured geometry
+    ]
+    four = dispatch.QuantizedLinear(torch.zeros(n, k // 8, dtype=torch.int32), layer.scales, layer.biases,
+                                    group_size=64, bits=4)
+    bad.append((four, w, s))                                    # not 8-bit
+    for args in bad:
+        with pytest.raises(ValueError, match="measured out/head"):
+            dispatch.W8MultirowProjection(*args)
+
+
+def test_w8_multirow_projection_routes_only_eight_gpu_rows():
+    layer = _w8_layer(2560, 4096)
+    proj = dispatch.W8MultirowProjection(layer, *dispatch.unpack_affine_w8(layer, "out_proj"))
+    calls = []
+
+    class Recorder(torch.nn.Module):
+        def forward(self, x):
+            calls.append(tuple(x.shape))
+            return x
+
+    proj.fallback = Recorder()
+    assert not proj.takes_multirow(torch.zeros(8, 4096, dtype=torch.bfloat16))   # CPU: affine layer
+    for shape in ((1, 4096), (2, 4, 4096), (7, 4096)):
+        x = torch.zeros(shape, dtype=torch.bfloat16)
+        assert not proj.takes_multirow(x)
+        proj(x)
+    assert calls == [(1, 4096), (2, 4, 4096), (7, 4096)]
+    meta = torch.empty(2, 4, 4096, dtype=torch.bfloat16, device="meta")
+    assert not proj.takes_multirow(meta)  # 8 rows, but not on a GPU
