@@ -36,6 +36,7 @@ __all__ = [
     "SDPAConfig",
     "PreparedW8",
     "W8A16PerChannelLinear",
+    "W8A8Projection",
     "W8MultirowProjection",
     "dispatch_linear",
     "dispatch_qkv",
@@ -216,6 +217,27 @@ class W8MultirowProjection(torch.nn.Module):
         if self.takes_multirow(x):
             return ext.w8a16_multirow(x, self.weight, self.scales, output_dtype=self.fallback.scales.dtype,
                                       variant="nax", simdgroups=4)
+        return self.fallback(x)
+
+
+class W8A8Projection(torch.nn.Module):
+    """W8A8 arithmetic for a W8 projection, with the affine layer as its
+    fallback (``spark_mlx_llm/ops/linear.py:531-562``): on a GPU every floating
+    input runs ``ext.W8A8Linear`` (per-token INT8 activations, INT32
+    accumulators, the W8A8 epilogue); other inputs run ``fallback``. Raises
+    ``RuntimeError`` when the W8A8 kernels are unavailable (no supported GPU),
+    as the reference does without its extension."""
+
+    def __init__(self, fallback, weight, scales):
+        super().__init__()
+        if not ext.is_w8a8_available():
+            raise RuntimeError("w8_qmv_backend='w8a8' requires a B200 (sm_100) GPU and libsparkb200")
+        self.fallback = fallback
+        self.projection = ext.W8A8Linear(weight, scales, getattr(fallback, "bias", None))
+
+    def forward(self, x):
+        if x.dtype in (torch.bfloat16, torch.float16, torch.float32) and x.device.type == "cuda":
+            return self.projection(x)
         return self.fallback(x)
 
 

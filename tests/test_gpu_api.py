@@ -178,6 +178,20 @@ def test_w8_multirow_projection_routes(api):
     np.testing.assert_array_equal(to_f32(proj(x1)), to_f32(layer(x1)))
 
 
+def test_w8a8_projection_routes(api):
+    """``dispatch.W8A8Projection`` on the GPU is ``ext.W8A8Linear`` (bit-equal)."""
+    ext, dispatch = api
+    rng = np.random.default_rng(52)
+    n, k = 256, 512
+    wq, ws = quant.quantize_w8_per_channel((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
+    weight = torch.from_numpy(np.asarray(wq, np.int8)).cuda()
+    scales = torch.from_numpy(np.asarray(ws, np.float32)).cuda()
+    layer = dispatch.W8A16PerChannelLinear(weight, scales)
+    proj = dispatch.W8A8Projection(layer, weight, scales)
+    x = bf16_tensor(formats.round_bf16(rng.standard_normal((3, k)).astype(np.float32)))
+    np.testing.assert_array_equal(to_f32(proj(x)), to_f32(ext.W8A8Linear(weight, scales)(x)))
+
+
 def test_dispatch_sdpa_int8_pair(api):
     _, dispatch = api
     rng = np.random.default_rng(31)

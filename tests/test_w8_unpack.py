@@ -133,3 +133,14 @@ def test_w8_multirow_projection_routes_only_eight_gpu_rows():
     assert calls == [(1, 4096), (2, 4, 4096), (7, 4096)]
     meta = torch.empty(2, 4, 4096, dtype=torch.bfloat16, device="meta")
     assert not proj.takes_multirow(meta)  # 8 rows, but not on a GPU
+
+
+def test_w8a8_projection_needs_the_gpu_kernels():
+    """``W8A8Projection`` (``ops/linear.py:531-562``) refuses to build without
+    the W8A8 kernels (here: no GPU), as the reference does without its extension."""
+    layer = _w8_layer(256, 512)
+    w, s = dispatch.unpack_affine_w8(layer, "o_proj")
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: covered by the GPU tests")
+    with pytest.raises(RuntimeError, match="w8a8"):
+        dispatch.W8A8Projection(layer, w, s)
