@@ -162,22 +162,46 @@ def unpack_affine_w8(layer, name, *, allow_fallback=False):
 
 
 class W8A16PerChannelLinear(torch.nn.Module):
-    """Signed INT8 weights with an FP32 scale per output row (ops/linear.py:413-476)."""
+    """Single-row W8 projection with its affine layer as the fallback
+    (``spark_mlx_llm/ops/linear.py:413-476``).
 
-    def __init__(self, weight, scales):
+    ``fallback`` is the bias-free affine 8-bit :class:`QuantizedLinear`;
+    ``weight`` (signed INT8 ``[N, K]``) and ``scales`` (fp32 ``[N]`` or
+    ``[N, 1]``) its per-channel form, derived at load time
+    (:func:`unpack_affine_w8`, :meth:`from_affine`). One BF16/FP16 row on a
+    GPU runs ``ext.w8a16_per_channel``; every other input runs the affine
+    layer. Same checks and errors as the reference."""
+
+    def __init__(self, fallback, weight, scales):
         super().__init__()
-        self.register_buffer("weight", weight)
-        self.register_buffer("scales", scales)
+        if (type(fallback) is not QuantizedLinear or fallback.mode != "affine" or fallback.bits != 8
+                or fallback.biases is None or fallback.bias is not None):
+            raise ValueError("W8A16 fallback must be a bias-free affine W8 QuantizedLinear")
+        if (weight.ndim != 2 or weight.dtype != torch.int8
+                or tuple(weight.shape) != (fallback.weight.shape[0], fallback.weight.shape[1] * 4)
+                or scales.dtype != torch.float32
+                or tuple(scales.shape) not in ((weight.shape[0],), (weight.shape[0], 1))):
+            raise ValueError("W8A16 needs matching signed INT8 [N,K] and FP32 [N] scales")
+        self.fallback = fallback
+        self.register_buffer("weight", weight.contiguous())
+        self.register_buffer("scales", scales.reshape(-1).contiguous())
 
     @classmethod
     def from_affine(cls, layer, name="projection"):
         """Build from an MLX affine W8 layer (the load-time conversion of
         ``QuantizedProjections.prepare``, ``ops/linear.py:725-731``)."""
         weight, scales = unpack_affine_w8(layer, name)
-        return cls(weight, scales)
+        return cls(layer, weight, scales)
+
+    @staticmethod
+    def supports_rows(num_rows, dtype, device_type="cuda"):
+        return num_rows == 1 and dtype in (torch.bfloat16, torch.float16) and device_type == "cuda"
 
     def forward(self, x):
-        return ext.w8a16_per_channel(x, self.weight, self.scales)
+        if x.ndim >= 1 and x.shape[-1] > 0 and self.supports_rows(x.numel() // x.shape[-1], x.dtype,
+                                                                  x.device.type):
+            return ext.w8a16_per_channel(x, self.weight, self.scales)
+        return self.fallback(x)
 
 
 class W8MultirowProjection(torch.nn.Module):

@@ -156,20 +156,40 @@ def test_int8_quantized_sdpa_affine_tuples_fp16(api, dim, bits, heads, kvh):
     assert_close(to_f32(out), expected, what="affine-tuple sdpa fp16")
 
 
-def test_w8_multirow_projection_routes(api):
-    """``dispatch.W8MultirowProjection`` at the reference's out_proj geometry:
-    8 BF16 rows give exactly ``ext.w8a16_multirow``'s result, one row the
-    affine layer's."""
-    ext, dispatch = api
-    n, k, group = 2560, 4096, 64
-    rng = np.random.default_rng(51)
+def _w8_affine_layer(dispatch, rng, n, k, group):
+    """An affine 8-bit layer in the reference's W8 checkpoint form (symmetric
+    per-channel codes stored as code + 128 with bias = -128 * scale)."""
     wq, ws = quant.quantize_w8_per_channel((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
     s_bf16 = formats.round_bf16(np.asarray(ws, np.float32))
     words = (np.asarray(wq, np.int16) + 128).astype(np.uint8).reshape(n, k // 4, 4)
     words = words.astype(np.uint32) @ np.array([1, 1 << 8, 1 << 16, 1 << 24], np.uint32)
     scales = np.repeat(s_bf16[:, None], k // group, axis=1)
-    layer = dispatch.QuantizedLinear(u32_tensor(words), bf16_tensor(scales), bf16_tensor(-128 * scales),
-                                     group_size=group, bits=8)
+    return dispatch.QuantizedLinear(u32_tensor(words), bf16_tensor(scales), bf16_tensor(-128 * scales),
+                                    group_size=group, bits=8)
+
+
+def test_w8a16_per_channel_linear_routes(api):
+    """``dispatch.W8A16PerChannelLinear``: one BF16 row is ``ext.w8a16_per_channel``
+    (bit-equal), several rows the affine layer's."""
+    ext, dispatch = api
+    rng = np.random.default_rng(53)
+    layer = _w8_affine_layer(dispatch, rng, 512, 1024, 64)
+    module = dispatch.W8A16PerChannelLinear.from_affine(layer, "o_proj")
+    x = bf16_tensor(formats.round_bf16(rng.standard_normal((4, 1024)).astype(np.float32)))
+    x1 = x[:1].contiguous()
+    np.testing.assert_array_equal(to_f32(module(x1)), to_f32(ext.w8a16_per_channel(x1, module.weight,
+                                                                                 module.scales)))
+    np.testing.assert_array_equal(to_f32(module(x)), to_f32(layer(x)))
+
+
+def test_w8_multirow_projection_routes(api):
+    """``dispatch.W8MultirowProjection`` at the reference's out_proj geometry:
+    8 BF16 rows give exactly ``ext.w8a16_multirow``'s result, one row the
+    affine layer's."""
+    ext, dispatch = api
+    n, k = 2560, 4096
+    rng = np.random.default_rng(51)
+    layer = _w8_affine_layer(dispatch, rng, n, k, 64)
     proj = dispatch.W8MultirowProjection(layer, *dispatch.unpack_affine_w8(layer, "out_proj"))
     x8 = bf16_tensor(formats.round_bf16(rng.standard_normal((8, k)).astype(np.float32)))
     direct = ext.w8a16_multirow(x8, proj.weight, proj.scales)
@@ -183,10 +203,8 @@ def test_w8a8_projection_routes(api):
     ext, dispatch = api
     rng = np.random.default_rng(52)
     n, k = 256, 512
-    wq, ws = quant.quantize_w8_per_channel((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
-    weight = torch.from_numpy(np.asarray(wq, np.int8)).cuda()
-    scales = torch.from_numpy(np.asarray(ws, np.float32)).cuda()
-    layer = dispatch.W8A16PerChannelLinear(weight, scales)
+    layer = _w8_affine_layer(dispatch, rng, n, k, 64)
+    weight, scales = dispatch.unpack_affine_w8(layer, "o_proj")
     proj = dispatch.W8A8Projection(layer, weight, scales)
     x = bf16_tensor(formats.round_bf16(rng.standard_normal((3, k)).astype(np.float32)))
     np.testing.assert_array_equal(to_f32(proj(x)), to_f32(ext.W8A8Linear(weight, scales)(x)))

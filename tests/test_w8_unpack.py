@@ -79,8 +79,10 @@ def test_prepared_w8_caches_by_source_identity(golden):
     second = prep(layer)
     assert second is not first
     assert torch.equal(second[0], first[0])
-    module = dispatch.W8A16PerChannelLinear.from_affine(layer)
+    qlayer = dispatch.QuantizedLinear(layer.weight, layer.scales, layer.biases, group_size=layer.group_size, bits=8)
+    module = dispatch.W8A16PerChannelLinear.from_affine(qlayer)
     assert module.weight.dtype == torch.int8 and module.scales.dtype == torch.float32
+    assert module.fallback is qlayer
 
 
 def _w8_layer(n, k, group=64, dtype=torch.bfloat16):
@@ -144,3 +146,35 @@ def test_w8a8_projection_needs_the_gpu_kernels():
         pytest.skip("a GPU is present: covered by the GPU tests")
     with pytest.raises(RuntimeError, match="w8a8"):
         dispatch.W8A8Projection(layer, w, s)
+
+
+def test_w8a16_per_channel_linear_checks_and_routes():
+    """``W8A16PerChannelLinear`` (``ops/linear.py:413-476``): the reference's
+    checks and errors; only one BF16/FP16 row on a GPU leaves the affine layer."""
+    layer = _w8_layer(64, 256)
+    w, s = dispatch.unpack_affine_w8(layer, "o_proj")
+    module = dispatch.W8A16PerChannelLinear(layer, w, s[:, None])
+    assert tuple(module.scales.shape) == (64,)
+    with pytest.raises(ValueError, match="bias-free affine W8"):
+        dispatch.W8A16PerChannelLinear(SimpleNamespace(**vars(layer)), w, s)
+    with pytest.raises(ValueError, match="bias-free affine W8"):
+        dispatch.W8A16PerChannelLinear(dispatch.QuantizedLinear(layer.weight, layer.scales, layer.biases,
+                                                                group_size=64, bits=4), w, s)
+    for bad_w, bad_s in ((w[:, :128], s), (w.to(torch.int16), s), (w, s.double()), (w, s[:-1])):
+        with pytest.raises(ValueError, match="matching signed INT8"):
+            dispatch.W8A16PerChannelLinear(layer, bad_w, bad_s)
+    assert dispatch.W8A16PerChannelLinear.supports_rows(1, torch.bfloat16)
+    assert not dispatch.W8A16PerChannelLinear.supports_rows(2, torch.bfloat16)
+    assert not dispatch.W8A16PerChannelLinear.supports_rows(1, torch.float32)
+    assert not dispatch.W8A16PerChannelLinear.supports_rows(1, torch.bfloat16, "cpu")
+    calls = []
+
+    class Recorder(torch.nn.Module):
+        def forward(self, x):
+            calls.append(tuple(x.shape))
+            return x
+
+    module.fallback = Recorder()
+    module(torch.zeros(1, 256, dtype=torch.bfloat16))  # one row, but on the CPU
+    module(torch.zeros(4, 256, dtype=torch.bfloat16))
+    assert calls == [(1, 256), (4, 256)]
