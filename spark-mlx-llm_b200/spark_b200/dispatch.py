@@ -35,6 +35,7 @@ __all__ = [
     "RoPE",
     "SDPAConfig",
     "PreparedW8",
+    "QuantizedProjections",
     "W8A16PerChannelLinear",
     "W8A8Projection",
     "W8MultirowProjection",
@@ -263,6 +264,88 @@ class W8A8Projection(torch.nn.Module):
         if x.dtype in (torch.bfloat16, torch.float16, torch.float32) and x.device.type == "cuda":
             return self.projection(x)
         return self.fallback(x)
+
+
+class QuantizedProjections:
+    """Load-time lifecycle of a model's W8 output projections and untied LM
+    head (``spark_mlx_llm/ops/linear.py:565-731``).
+
+    A model is any object with ``layers`` (each with ``self_attn.out_proj``),
+    ``args.tie_word_embeddings`` and, when untied, ``lm_head``. ``configure``
+    wraps every 8-bit affine :class:`QuantizedLinear` among them in the
+    adapter of the chosen ``w8_qmv_backend`` - ``"w8a16"``
+    (:class:`W8A16PerChannelLinear`), ``"multirow"``
+    (:class:`W8MultirowProjection`, the measured geometries only) or
+    ``"w8a8"`` (:class:`W8A8Projection`) - with the per-channel INT8 form
+    derived from the checkpoint tensors (:func:`unpack_affine_w8`). Layers
+    outside an adapter's format keep their affine projection (``"w8a16"`` and
+    ``"multirow"`` skip group-wise/asymmetric W8; ``"w8a8"`` rejects it).
+    ``"auto"`` and ``"native"`` leave the model unchanged, and so does a
+    backend whose kernels are unavailable. Every adapter is built before any
+    module is replaced."""
+
+    ADAPTERS = {"w8a16": W8A16PerChannelLinear, "multirow": W8MultirowProjection, "w8a8": W8A8Projection}
+    MULTIROW_PACKED = ((131072, 640), (2560, 1024))  # packed words of the measured head / out_proj
+
+    @staticmethod
+    def projections(model):
+        """``(checkpoint name, parent, attribute)`` of every W8 projection slot."""
+        for index, layer in enumerate(model.layers):
+            yield f"model.layers.{index}.self_attn.out_proj", layer.self_attn, "out_proj"
+        if not model.args.tie_word_embeddings:
+            yield "lm_head", model, "lm_head"
+
+    @staticmethod
+    def configure(model, backend):
+        LinearConfig(w8_qmv_backend=backend)  # the reference's choice check
+        if backend in ("auto", "native"):
+            return
+        if backend == "w8a8" and not ext.is_w8a8_available():
+            return
+        replacements = []
+        for name, parent, attribute in QuantizedProjections.projections(model):
+            layer = getattr(parent, attribute)
+            if type(layer) is not QuantizedLinear or layer.bits != 8:
+                continue
+            if backend == "multirow" and (
+                    tuple(layer.weight.shape) not in QuantizedProjections.MULTIROW_PACKED
+                    or layer.scales.dtype not in (torch.bfloat16, torch.float32) or layer.biases is None
+                    or layer.biases.dtype != layer.scales.dtype or layer.mode != "affine"
+                    or layer.bias is not None):
+                continue
+            if backend == "w8a16" and (layer.mode != "affine" or layer.bias is not None):
+                continue
+            pair = unpack_affine_w8(layer, name, allow_fallback=backend in ("w8a16", "multirow"))
+            if pair is None:
+                continue
+            replacements.append((parent, attribute, QuantizedProjections.ADAPTERS[backend](layer, *pair)))
+        for parent, attribute, projection in replacements:
+            setattr(parent, attribute, projection)
+
+    @staticmethod
+    def unwrap(model):
+        """Put every adapter's affine layer back."""
+        for _, parent, attribute in QuantizedProjections.projections(model):
+            projection = getattr(parent, attribute)
+            if type(projection) in tuple(QuantizedProjections.ADAPTERS.values()):
+                setattr(parent, attribute, projection.fallback)
+
+    @staticmethod
+    def scale_paths(model):
+        """Names of the fp32 scale tensors a dtype-casting loader must keep."""
+        paths = set()
+        for name, parent, attribute in QuantizedProjections.projections(model):
+            projection = getattr(parent, attribute)
+            if type(projection) in (W8A16PerChannelLinear, W8MultirowProjection):
+                paths.add(name + ".scales")
+            elif type(projection) is W8A8Projection:
+                paths.add(name + ".projection.scales")
+        return paths
+
+    @staticmethod
+    def prepare(model):
+        """``configure`` with the model's own ``args.w8_qmv_backend``."""
+        QuantizedProjections.configure(model, model.args.w8_qmv_backend)
 
 
 class PreparedW8:

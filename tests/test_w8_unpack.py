@@ -178,3 +178,57 @@ def test_w8a16_per_channel_linear_checks_and_routes():
     module(torch.zeros(1, 256, dtype=torch.bfloat16))  # one row, but on the CPU
     module(torch.zeros(4, 256, dtype=torch.bfloat16))
     assert calls == [(1, 256), (4, 256)]
+
+
+def _model(out_layers, lm_head=None, backend="w8a16"):
+    layers = [SimpleNamespace(self_attn=torch.nn.Module()) for _ in out_layers]
+    for layer, out in zip(layers, out_layers):
+        layer.self_attn.out_proj = out
+    model = SimpleNamespace(layers=layers, lm_head=lm_head,
+                            args=SimpleNamespace(tie_word_embeddings=lm_head is None, w8_qmv_backend=backend))
+    return model
+
+
+def test_quantized_projections_lifecycle():
+    """``QuantizedProjections`` (``ops/linear.py:565-731``): w8a16 wraps every
+    per-channel W8 out_proj and the untied head, skips group-wise W8 and W4,
+    scale_paths names the fp32 scales, unwrap restores the affine layers;
+    auto/native and an unknown backend leave the model alone or raise."""
+    per_channel = _w8_layer(64, 256)
+    grouped = _w8_layer(64, 256)
+    grouped.scales = grouped.scales.clone()
+    grouped.scales[0, 1] *= 2  # group-wise scales: not per-channel
+    grouped.biases = -128 * grouped.scales
+    four = dispatch.QuantizedLinear(torch.zeros(64, 32, dtype=torch.int32), grouped.scales, grouped.biases,
+                                    group_size=64, bits=4)
+    head = _w8_layer(128, 256)
+    model = _model([per_channel, grouped, four], lm_head=head)
+    for backend in ("auto", "native"):
+        dispatch.QuantizedProjections.configure(model, backend)
+        assert model.layers[0].self_attn.out_proj is per_channel
+    with pytest.raises(ValueError):
+        dispatch.QuantizedProjections.configure(model, "fast")
+    dispatch.QuantizedProjections.prepare(model)  # args.w8_qmv_backend = "w8a16"
+    outs = [layer.self_attn.out_proj for layer in model.layers]
+    assert type(outs[0]) is dispatch.W8A16PerChannelLinear and outs[0].fallback is per_channel
+    assert outs[1] is grouped and outs[2] is four
+    assert type(model.lm_head) is dispatch.W8A16PerChannelLinear
+    assert dispatch.QuantizedProjections.scale_paths(model) == {"model.layers.0.self_attn.out_proj.scales",
+                                                                 "lm_head.scales"}
+    dispatch.QuantizedProjections.unwrap(model)
+    assert model.layers[0].self_attn.out_proj is per_channel and model.lm_head is head
+    assert dispatch.QuantizedProjections.scale_paths(model) == set()
+
+
+def test_quantized_projections_multirow_and_w8a8_selection():
+    """multirow wraps only the measured out_proj geometry (2560 x 4096 here);
+    w8a8 without its kernels (no GPU) changes nothing."""
+    measured, other = _w8_layer(2560, 4096), _w8_layer(64, 256)
+    model = _model([measured, other])
+    if not torch.cuda.is_available():
+        dispatch.QuantizedProjections.configure(model, "w8a8")
+        assert model.layers[0].self_attn.out_proj is measured
+    dispatch.QuantizedProjections.configure(model, "multirow")
+    assert type(model.layers[0].self_attn.out_proj) is dispatch.W8MultirowProjection
+    assert model.layers[1].self_attn.out_proj is other
+    assert dispatch.QuantizedProjections.scale_paths(model) == {"model.layers.0.self_attn.out_proj.scales"}
