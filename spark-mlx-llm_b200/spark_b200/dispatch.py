@@ -8,6 +8,9 @@ Mirrors the reference's operator entry points for the decode path:
   n_kv_heads, head_dim, offset, config=None)``               (ops/qkv.py:18-87)
 * ``dispatch_sdpa(queries, keys, values, *, cache, scale, mask, config=None,
   is_sliding=False)``                                        (ops/sdpa.py:39-78)
+* ``dispatch_attention_output(x, output, gate_projection, output_projection)``
+                                                   (ops/attention_output.py:16-101)
+* ``dispatch_ffn(x, attention_output, norm, mlp, *, mlp_type)``  (ops/ffn.py:17-118)
 
 A ``projection`` is any object exposing the MLX ``nn.QuantizedLinear``
 attributes ``weight / scales / biases / group_size / bits / mode`` (affine,
@@ -39,6 +42,8 @@ __all__ = [
     "W8A16PerChannelLinear",
     "W8A8Projection",
     "W8MultirowProjection",
+    "dispatch_attention_output",
+    "dispatch_ffn",
     "dispatch_linear",
     "dispatch_qkv",
     "dispatch_sdpa",
@@ -383,6 +388,52 @@ def dispatch_linear(x, projection, *, config=None):
     if AffineParameters.accepts(projection):
         return AffineParameters.native(x, *AffineParameters.from_module(projection))
     return projection(x)
+
+
+def dispatch_attention_output(x, output, gate_projection, output_projection):
+    """Gated attention output (``spark_mlx_llm/ops/attention_output.py:16-101``):
+    ``out_proj(output * sigmoid(x @ g^T))`` with one gate per head.
+
+    ``x [B, L, hidden]`` is the block's normed input, ``output [B, H, L, D]``
+    the attention output. A bias-free BF16 ``torch.nn.Linear`` gate on the GPU
+    runs ``sb_head_gate`` (bf16 gate logits with fp32 accumulation, sigmoid in
+    fp32 rounded to bf16, the product rounded to bf16 - the reference's dtype
+    steps) and then the output projection through :func:`dispatch_linear`
+    (affine kernels, or the W8 adapters' own routes); any other gate module is
+    called as a module, as the reference does for custom modules."""
+    b, l = x.shape[0], x.shape[1]
+    heads, d = output.shape[1], output.shape[3]
+    attn = output.transpose(1, 2).contiguous()  # [B, L, H, D]
+    if (isinstance(gate_projection, torch.nn.Linear) and gate_projection.bias is None
+            and x.dtype == output.dtype == gate_projection.weight.dtype == torch.bfloat16
+            and x.device.type == "cuda"):
+        gated = ops.head_gate(x.reshape(b * l, x.shape[-1]), gate_projection.weight, attn.reshape(b * l, heads, d))
+        return dispatch_linear(gated.reshape(b, l, heads * d), output_projection)
+    gate = torch.sigmoid(gate_projection(x).float()).to(output.dtype)
+    return output_projection((attn * gate[..., None]).reshape(b, l, heads * d))
+
+
+def dispatch_ffn(x, attention_output, norm, mlp, *, mlp_type):
+    """Residual, RMSNorm and the gated GELU FFN (``spark_mlx_llm/ops/ffn.py:17-118``):
+    ``h = x + attention_output``; ``h + down(gelu(gate(n)) * up(n))`` with
+    ``n = rms_norm(h)``.
+
+    When ``mlp`` is exactly ``mlp_type`` with affine ``gate_proj`` /
+    ``up_proj`` / ``down_proj``, ``norm`` a ``torch.nn.RMSNorm`` and the input
+    on the GPU, the norm is ``sb_rms_norm``, the projections the affine
+    kernels and the gate ``sb_gated_activation`` (exact GELU); the residual adds
+    round once to the activation dtype. Other modules are called as modules."""
+    hidden = x + attention_output
+    projections = [getattr(mlp, name, None) for name in ("gate_proj", "up_proj", "down_proj")]
+    if (type(mlp) is not mlp_type or type(norm) is not torch.nn.RMSNorm or norm.weight is None
+            or norm.weight.dtype != hidden.dtype or hidden.device.type != "cuda" or hidden.dtype != torch.bfloat16
+            or not all(AffineParameters.accepts(p) for p in projections)):
+        return hidden + mlp(norm(hidden))
+    eps = norm.eps if norm.eps is not None else torch.finfo(hidden.dtype).eps
+    normed = ops.rms_norm(hidden, norm.weight, float(eps))
+    gate, up, down = projections
+    act = ops.gated_activation(dispatch_linear(normed, gate), dispatch_linear(normed, up), 1)
+    return hidden + dispatch_linear(act, down)
 
 
 def dispatch_qkv(x, projection, rope, *, q_size, kv_size, n_heads, n_kv_heads, head_dim, offset, config=None):
