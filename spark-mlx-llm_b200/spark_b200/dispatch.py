@@ -471,6 +471,13 @@ def dispatch_sdpa(queries, keys, values, *, cache, scale, mask, config=None, is_
       mask for ``mask="causal"``.
     * Affine tuple ``(packed, scales, biases)`` with ``cache.bits`` /
       ``cache.group_size``: ``int8_quantized_sdpa`` (decode or causal prefill).
+    * BF16 ``K/V [B,KH,N,D]`` tensors (the reference's bf16 caches, its
+      ``tuned_bf16_sdpa`` and ``verification_bf16_sdpa`` routes,
+      ``ops/sdpa.py:62-78``): the BF16 multi-query kernel for any query count,
+      with no mask, ``"causal"`` or a boolean ``[L, N]`` array (a sliding
+      layer's window arrives in that array), head_dim 128 / 256 and 1, 2, 4 or
+      8 query heads per KV head.
+    Other inputs raise ``ValueError``.
     """
     config = config if config is not None else SDPAConfig()
     if not isinstance(config, SDPAConfig):
@@ -487,5 +494,16 @@ def dispatch_sdpa(queries, keys, values, *, cache, scale, mask, config=None, is_
         return ext.int8_quantized_sdpa(queries, keys, values, scale=scale,
                                        group_size=getattr(cache, "group_size", 32), bits=getattr(cache, "bits", 8),
                                        mask=mask)
-    raise ValueError("dispatch_sdpa on B200 serves quantized KV caches: an (int8, fp16 scale) pair or an "
-                     "affine (packed, scales, biases) tuple")
+    if isinstance(keys, torch.Tensor) and isinstance(values, torch.Tensor):
+        causal = isinstance(mask, str) and mask == "causal"
+        if mask is not None and not causal and not isinstance(mask, torch.Tensor):
+            raise ValueError("mask must be None, 'causal' or a boolean [L, N] array")
+        g = queries.shape[1] // keys.shape[1] if keys.ndim == 4 and keys.shape[1] > 0 else 0
+        if (queries.dtype == keys.dtype == values.dtype == torch.bfloat16 and queries.ndim == 4
+                and queries.shape[-1] in (128, 256) and g in (1, 2, 4, 8) and queries.shape[1] == g * keys.shape[1]):
+            return ops.bf16_sdpa_multiquery(queries, keys, values, float(scale), causal, 0,
+                                            mask if isinstance(mask, torch.Tensor) else None)
+        raise ValueError("BF16 K/V attention needs bfloat16 Q/K/V, head_dim 128 or 256 and 1, 2, 4 or 8 "
+                         "query heads per KV head")
+    raise ValueError("dispatch_sdpa on B200 serves an (int8, fp16 scale) pair, an affine (packed, scales, "
+                     "biases) tuple or BF16 K/V tensors")

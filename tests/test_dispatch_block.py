@@ -40,3 +40,17 @@ def test_ffn_module_route():
     got = dispatch.dispatch_ffn(x, attn, norm, mlp, mlp_type=MLP)
     h = x + attn
     torch.testing.assert_close(got, h + mlp(norm(h)))
+
+
+def test_dispatch_sdpa_bf16_route_checks():
+    """BF16 K/V tensors route to the multi-query kernel only in its format;
+    everything else raises before any kernel call (here on the CPU)."""
+    q = torch.zeros(1, 16, 8, 256, dtype=torch.bfloat16)
+    k = torch.zeros(1, 4, 519, 256, dtype=torch.bfloat16)
+    for bad_q, bad_k in ((q.float(), k.float()), (q[..., :64], k[..., :64]), (q[:, :12], k)):
+        with pytest.raises(ValueError, match="BF16 K/V attention"):
+            dispatch.dispatch_sdpa(bad_q, bad_k, bad_k, cache=None, scale=0.0625, mask=None)
+    with pytest.raises(ValueError, match="mask must be"):
+        dispatch.dispatch_sdpa(q, k, k, cache=None, scale=0.0625, mask="sliding")
+    with pytest.raises(ValueError, match="serves"):
+        dispatch.dispatch_sdpa(q, [k], [k], cache=None, scale=0.0625, mask=None)
