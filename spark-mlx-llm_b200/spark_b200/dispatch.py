@@ -112,6 +112,64 @@ class AffineParameters(NamedTuple):
         """``mx.quantized_matmul(x, w, scales, biases, transpose=True, mode="affine")``."""
         return ops.affine_linear(x, weight, scales, biases, group_size, bits)
 
+    # The reference's W4 backend selection (ops/linear.py:116-257). Its routes
+    # are Metal schedules of one computation; here every route is the same
+    # weight-streaming kernel family, reached through the entry point the
+    # route names (w4a16_qmv, w4a16_multirow), so the choice keeps the
+    # reference's conditions and never changes the result's arithmetic.
+    @classmethod
+    def resolve(cls, layer, shape, dtype, config):
+        """``(projection callable, parameters)`` for ``x`` of ``shape``/``dtype``
+        under ``config``; ``multirow_packed`` needs no repacking here."""
+        params = cls.from_module(layer)
+        if config.w4_qmv_backend == "multirow_packed" and params.supports_multirow(shape, dtype, *params):
+            return cls.multirow_packed, params
+        return params.select(shape, dtype, config), params
+
+    def select(self, shape, dtype, config):
+        if config.w4_qmv_backend == "multirow" and self.supports_multirow(shape, dtype, *self):
+            return self.multirow
+        if config.w4_qmv_backend == "splitk" and self.supports_splitk(shape, dtype, *self):
+            return self.splitk
+        return self.native
+
+    @staticmethod
+    def _w4g32_bf16(shape, dtype, weight, scales, biases, group_size, bits):
+        return (bits == 4 and group_size == 32 and len(shape) >= 1 and weight.ndim == 2
+                and weight.shape[1] * 8 == shape[-1] and tuple(scales.shape) == (weight.shape[0], shape[-1] // 32)
+                and biases is not None and biases.shape == scales.shape
+                and dtype == scales.dtype == biases.dtype == torch.bfloat16
+                and weight.dtype in (torch.int32, torch.uint32) and _on_gpu(weight))
+
+    @staticmethod
+    def supports_splitk(shape, dtype, weight, scales, biases, group_size, bits):
+        """One BF16 row of a W4/G32 layer (``w4a16_qmv``: K % 512 == 0, N % 4 == 0)."""
+        return (AffineParameters._w4g32_bf16(shape, dtype, weight, scales, biases, group_size, bits)
+                and math.prod(shape[:-1]) == 1 and shape[-1] % 512 == 0 and weight.shape[0] % 4 == 0)
+
+    @staticmethod
+    def supports_multirow(shape, dtype, weight, scales, biases, group_size, bits):
+        """Eight BF16 rows of a W4/G32 layer (the verification pass)."""
+        return (len(shape) >= 2 and math.prod(shape[:-1]) == 8
+                and AffineParameters._w4g32_bf16(shape, dtype, weight, scales, biases, group_size, bits))
+
+    @staticmethod
+    def multirow(x, weight, scales, biases, group_size, bits):
+        return ext.w4a16_multirow(x, weight, scales, biases, algorithm="wide", k_lanes=8, simdgroups=8)
+
+    @staticmethod
+    def multirow_packed(x, weight, scales, biases, group_size, bits):
+        # the reference's prepared nax4 tile layout is a Metal layout; the B200 kernel reads the native one
+        return ext.w4a16_multirow(x, weight, scales, biases, algorithm="nax4")
+
+    @staticmethod
+    def splitk(x, weight, scales, biases, group_size, bits):
+        return ext.w4a16_qmv(x, weight, scales, biases)
+
+
+def _on_gpu(t):
+    return t.device.type == "cuda"
+
 
 class QuantizedLinear(torch.nn.Module):
     """Affine-quantized projection with the ``nn.QuantizedLinear`` attributes."""
@@ -386,7 +444,8 @@ def dispatch_linear(x, projection, *, config=None):
     if not isinstance(config, LinearConfig):
         raise TypeError("config must be a LinearConfig")
     if AffineParameters.accepts(projection):
-        return AffineParameters.native(x, *AffineParameters.from_module(projection))
+        project, params = AffineParameters.resolve(projection, tuple(x.shape), x.dtype, config)
+        return project(x, *params)
     return projection(x)
 
 

@@ -46,6 +46,17 @@ E = inspect.Parameter.empty
                                  ("offset", K, E), ("config", K, None)]),
         (dispatch.dispatch_sdpa, [("queries", P, E), ("keys", P, E), ("values", P, E), ("cache", K, E),
                                   ("scale", K, E), ("mask", K, E), ("config", K, None), ("is_sliding", K, False)]),
+        (dispatch.dispatch_attention_output, [("x", P, E), ("output", P, E), ("gate_projection", P, E),
+                                              ("output_projection", P, E)]),
+        (dispatch.dispatch_ffn, [("x", P, E), ("attention_output", P, E), ("norm", P, E), ("mlp", P, E),
+                                 ("mlp_type", K, E)]),
+        (dispatch.W8A16PerChannelLinear.__init__, [("self", P, E), ("fallback", P, E), ("weight", P, E),
+                                                   ("scales", P, E)]),
+        (dispatch.W8MultirowProjection.__init__, [("self", P, E), ("fallback", P, E), ("weight", P, E),
+                                                  ("scales", P, E)]),
+        (dispatch.W8A8Projection.__init__, [("self", P, E), ("fallback", P, E), ("weight", P, E),
+                                            ("scales", P, E)]),
+        (dispatch.AffineParameters.resolve, [("layer", P, E), ("shape", P, E), ("dtype", P, E), ("config", P, E)]),
     ],
 )
 def test_reference_signatures(fn, expected):

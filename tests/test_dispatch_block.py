@@ -54,3 +54,34 @@ def test_dispatch_sdpa_bf16_route_checks():
         dispatch.dispatch_sdpa(q, k, k, cache=None, scale=0.0625, mask="sliding")
     with pytest.raises(ValueError, match="serves"):
         dispatch.dispatch_sdpa(q, [k], [k], cache=None, scale=0.0625, mask=None)
+
+
+def test_affine_backend_selection(monkeypatch):
+    """``AffineParameters.resolve`` / ``select`` (``ops/linear.py:116-147``): the
+    W4 backends are chosen under the reference's conditions (W4/G32 BF16 on the
+    GPU; one row for split-K, eight for multirow) and every other input takes
+    the native route."""
+    from spark_b200.dispatch import AffineParameters, LinearConfig, QuantizedLinear
+
+    n, k = 256, 1024
+    layer = QuantizedLinear(torch.zeros(n, k // 8, dtype=torch.int32), torch.ones(n, k // 32, dtype=torch.bfloat16),
+                            torch.zeros(n, k // 32, dtype=torch.bfloat16), group_size=32, bits=4)
+    params = AffineParameters.from_module(layer)
+    bf16 = torch.bfloat16
+    # on the CPU every backend resolves to the native route
+    for backend in ("native", "splitk", "multirow", "multirow_packed"):
+        fn, _ = AffineParameters.resolve(layer, (8, k), bf16, LinearConfig(w4_qmv_backend=backend))
+        assert fn == AffineParameters.native
+    monkeypatch.setattr("spark_b200.dispatch._on_gpu", lambda t: True)
+    cfg = LinearConfig
+    assert params.select((1, 1, k), bf16, cfg(w4_qmv_backend="splitk")) == AffineParameters.splitk
+    assert params.select((2, k), bf16, cfg(w4_qmv_backend="splitk")) == AffineParameters.native
+    assert params.select((1, 8, k), bf16, cfg(w4_qmv_backend="multirow")) == AffineParameters.multirow
+    assert params.select((4, k), bf16, cfg(w4_qmv_backend="multirow")) == AffineParameters.native
+    assert params.select((8, k), torch.float16, cfg(w4_qmv_backend="multirow")) == AffineParameters.native
+    fn, _ = AffineParameters.resolve(layer, (8, k), bf16, cfg(w4_qmv_backend="multirow_packed"))
+    assert fn == AffineParameters.multirow_packed
+    g64 = QuantizedLinear(layer.weight, torch.ones(n, k // 64, dtype=bf16), torch.zeros(n, k // 64, dtype=bf16),
+                          group_size=64, bits=4)
+    assert AffineParameters.from_module(g64).select((8, k), bf16, cfg(w4_qmv_backend="multirow")) == \
+        AffineParameters.native
