@@ -52,18 +52,40 @@ __all__ = [
 
 
 class _Config:
-    """Field validation shared by the configs (ops/base.py OperatorConfig role)."""
+    """Field validation shared by the configs (``spark_mlx_llm/ops/base.py:14-53``,
+    ``OperatorConfig``): ``from_dict`` picks this config's fields out of a flat
+    model config, ``choices`` gives a field's allowed values, and
+    ``validate_values`` checks supplied fields only (booleans must be bool,
+    choice fields one of their choices), with the reference's messages."""
 
     _choices: dict = {}
 
     def __post_init__(self):
-        for f in fields(self):
-            value = getattr(self, f.name)
-            allowed = self._choices.get(f.name)
+        self.validate()
+
+    @classmethod
+    def from_dict(cls, values):
+        names = {f.name for f in fields(cls)}
+        return cls(**{name: values[name] for name in names if name in values})
+
+    @classmethod
+    def choices(cls, name):
+        return cls._choices[name]
+
+    @classmethod
+    def validate_values(cls, values):
+        for f in fields(cls):
+            if f.name not in values:
+                continue
+            value = values[f.name]
+            allowed = cls._choices.get(f.name)
+            if allowed is None and type(f.default) is bool and type(value) is not bool:
+                raise ValueError(f"{f.name} must be a boolean, got {value!r}")
             if allowed is not None and value not in allowed:
                 raise ValueError(f"{f.name} must be one of {allowed}, got {value!r}")
-            if allowed is None and not isinstance(value, bool):
-                raise ValueError(f"{f.name} must be bool")
+
+    def validate(self):
+        self.validate_values({f.name: getattr(self, f.name) for f in fields(self)})
 
 
 @dataclass(kw_only=True)
@@ -77,6 +99,12 @@ class LinearConfig(_Config):
     w4_qmv_backend: str = "native"
     _choices = {"w8_qmv_backend": ("auto", "native", "w8a16", "w8a8", "multirow"),
                 "w4_qmv_backend": ("native", "splitk", "multirow", "multirow_packed")}
+
+    @classmethod
+    def validate_values(cls, values):
+        if "qmv_backend" in values:
+            raise ValueError("qmv_backend was renamed to w8_qmv_backend; update the configuration")
+        super().validate_values(values)
 
 
 @dataclass(kw_only=True)

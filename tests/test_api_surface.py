@@ -119,3 +119,18 @@ def test_is_w8a8_available_without_gpu():
     if torch.cuda.is_available():
         pytest.skip("a GPU is present")
     assert ext.is_w8a8_available() is False
+
+
+def test_operator_config_helpers():
+    """``from_dict`` / ``choices`` / ``validate_values`` of the reference's
+    ``OperatorConfig`` (``ops/base.py:14-53``) on the dispatch configs."""
+    cfg = dispatch.LinearConfig.from_dict({"w8_qmv_backend": "multirow", "hidden_size": 2560})
+    assert cfg.w8_qmv_backend == "multirow" and cfg.w4_qmv_backend == "native"
+    assert dispatch.LinearConfig.choices("w4_qmv_backend") == ("native", "splitk", "multirow", "multirow_packed")
+    dispatch.LinearConfig.validate_values({"w8_qmv_backend": "w8a8"})  # a partial mapping is fine
+    with pytest.raises(ValueError, match="renamed to w8_qmv_backend"):
+        dispatch.LinearConfig.validate_values({"qmv_backend": "w8a16"})
+    with pytest.raises(ValueError, match="must be a boolean"):
+        dispatch.SDPAConfig(tuned_bf16_sdpa=1)
+    sd = dispatch.SDPAConfig.from_dict({"fused_quantized_sdpa_prefill": True, "other": 3})
+    assert sd.fused_quantized_sdpa_prefill and sd.fused_quantized_sdpa
