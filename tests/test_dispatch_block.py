@@ -2,7 +2,7 @@
 ``dispatch_attention_output`` (``ops/attention_output.py:16-101``) and
 ``dispatch_ffn`` (``ops/ffn.py:17-118``). CPU: inputs off the GPU or custom
 modules take the module route, which must compute the reference's formula;
-the fused GPU routes are checked in ``tests/test_gpu_spark25.py``."""
+the fused GPU routes are checked in ``tests/test_zzz_gpu_entry_routes.py``."""
 
 import pytest
 

@@ -133,83 +133,6 @@ def test_int8_quantized_sdpa_affine_tuples(api, bsz, heads, kvh, length, n, dim,
     np.testing.assert_array_equal(to_f32(out2), to_f32(out))
 
 
-@pytest.mark.parametrize("dim,bits,heads,kvh", [(256, 8, 16, 4), (128, 4, 8, 1), (64, 8, 4, 2)])
-def test_int8_quantized_sdpa_affine_tuples_fp16(api, dim, bits, heads, kvh):
-    """fp16 queries and fp16 scales / biases (the same values as the bf16 case:
-    bf16 metadata converts to fp16 exactly) on the single-query decode kernels."""
-    ext, _ = api
-    rng = np.random.default_rng(dim + bits)
-    n, group = 1500, 32
-    q = formats.round_bf16(rng.standard_normal((1, heads, 1, dim)).astype(np.float32))
-    kp, ks, kb, _, _ = affine_kv(rng, 1, kvh, n, dim, group, bits)
-    vp, vs, vb, _, _ = affine_kv(rng, 1, kvh, n, dim, group, bits)
-    scale = 1.0 / np.sqrt(dim)
-    expected = ref.sdpa_affine(q, (kp, ks, kb), (vp, vs, vb), scale, group, bits)
-
-    def f16(a):
-        return torch.from_numpy(np.asarray(a, np.float32)).to(torch.float16).cuda()
-
-    keys = (u32_tensor(kp), f16(ks), f16(kb))
-    values = (u32_tensor(vp), f16(vs), f16(vb))
-    out = ext.int8_quantized_sdpa(f16(q), keys, values, scale=float(scale), group_size=group, bits=bits)
-    assert out.dtype == torch.float16
-    assert_close(to_f32(out), expected, what="affine-tuple sdpa fp16")
-
-
-def _w8_affine_layer(dispatch, rng, n, k, group):
-    """An affine 8-bit layer in the reference's W8 checkpoint form (symmetric
-    per-channel codes stored as code + 128 with bias = -128 * scale)."""
-    wq, ws = quant.quantize_w8_per_channel((rng.standard_normal((n, k)) * 0.02).astype(np.float32))
-    s_bf16 = formats.round_bf16(np.asarray(ws, np.float32))
-    words = (np.asarray(wq, np.int16) + 128).astype(np.uint8).reshape(n, k // 4, 4)
-    words = words.astype(np.uint32) @ np.array([1, 1 << 8, 1 << 16, 1 << 24], np.uint32)
-    scales = np.repeat(s_bf16[:, None], k // group, axis=1)
-    return dispatch.QuantizedLinear(u32_tensor(words), bf16_tensor(scales), bf16_tensor(-128 * scales),
-                                    group_size=group, bits=8)
-
-
-def test_w8a16_per_channel_linear_routes(api):
-    """``dispatch.W8A16PerChannelLinear``: one BF16 row is ``ext.w8a16_per_channel``
-    (bit-equal), several rows the affine layer's."""
-    ext, dispatch = api
-    rng = np.random.default_rng(53)
-    layer = _w8_affine_layer(dispatch, rng, 512, 1024, 64)
-    module = dispatch.W8A16PerChannelLinear.from_affine(layer, "o_proj")
-    x = bf16_tensor(formats.round_bf16(rng.standard_normal((4, 1024)).astype(np.float32)))
-    x1 = x[:1].contiguous()
-    np.testing.assert_array_equal(to_f32(module(x1)), to_f32(ext.w8a16_per_channel(x1, module.weight,
-                                                                                 module.scales)))
-    np.testing.assert_array_equal(to_f32(module(x)), to_f32(layer(x)))
-
-
-def test_w8_multirow_projection_routes(api):
-    """``dispatch.W8MultirowProjection`` at the reference's out_proj geometry:
-    8 BF16 rows give exactly ``ext.w8a16_multirow``'s result, one row the
-    affine layer's."""
-    ext, dispatch = api
-    n, k = 2560, 4096
-    rng = np.random.default_rng(51)
-    layer = _w8_affine_layer(dispatch, rng, n, k, 64)
-    proj = dispatch.W8MultirowProjection(layer, *dispatch.unpack_affine_w8(layer, "out_proj"))
-    x8 = bf16_tensor(formats.round_bf16(rng.standard_normal((8, k)).astype(np.float32)))
-    direct = ext.w8a16_multirow(x8, proj.weight, proj.scales)
-    np.testing.assert_array_equal(to_f32(proj(x8)), to_f32(direct))
-    x1 = x8[:1].contiguous()
-    np.testing.assert_array_equal(to_f32(proj(x1)), to_f32(layer(x1)))
-
-
-def test_w8a8_projection_routes(api):
-    """``dispatch.W8A8Projection`` on the GPU is ``ext.W8A8Linear`` (bit-equal)."""
-    ext, dispatch = api
-    rng = np.random.default_rng(52)
-    n, k = 256, 512
-    layer = _w8_affine_layer(dispatch, rng, n, k, 64)
-    weight, scales = dispatch.unpack_affine_w8(layer, "o_proj")
-    proj = dispatch.W8A8Projection(layer, weight, scales)
-    x = bf16_tensor(formats.round_bf16(rng.standard_normal((3, k)).astype(np.float32)))
-    np.testing.assert_array_equal(to_f32(proj(x)), to_f32(ext.W8A8Linear(weight, scales)(x)))
-
-
 def test_dispatch_sdpa_int8_pair(api):
     _, dispatch = api
     rng = np.random.default_rng(31)

@@ -270,26 +270,6 @@ def test_bf16_multiquery_matches_oracle(case):
     np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
 
 
-def test_dispatch_sdpa_bf16_verification_route():
-    """``dispatch_sdpa`` with BF16 K/V tensors and a boolean window mask - the
-    reference's verification shape (16/4 heads x 256, 8 queries over 519 keys,
-    scale 1/16) - against the float64 masked attention."""
-    _need_cuda()
-    from spark_b200 import dispatch
-
-    gen = torch.Generator().manual_seed(21)
-    q = torch.randn(1, 16, 8, 256, generator=gen).to(torch.bfloat16)
-    k = torch.randn(1, 4, 519, 256, generator=gen).to(torch.bfloat16)
-    v = torch.randn(1, 4, 519, 256, generator=gen).to(torch.bfloat16)
-    pos = np.arange(519 - 8, 519)[:, None]
-    keys = np.arange(519)[None, :]
-    mask = (keys <= pos) & (keys > pos - 128)
-    out = dispatch.dispatch_sdpa(q.cuda(), k.cuda(), v.cuda(), cache=None, scale=0.0625,
-                                 mask=torch.from_numpy(mask).cuda(), is_sliding=True)
-    ref = oracle_ops.sdpa_masked(_f32(q), _f32(k), _f32(v), 0.0625, mask=mask)
-    np.testing.assert_allclose(_f32(out), ref, rtol=1e-2, atol=1e-2 * np.abs(ref).max())
-
-
 def test_ext_bf16_multiquery_masks():
     _need_cuda()
     from spark_b200 import ext

@@ -93,64 +93,3 @@ def test_head_gate_matches_oracle():
     _close(_f32(out), ref.head_gate(_f32(x), _f32(w), _f32(attn)))
 
 
-def _qlinear(gen, n, k, group=32, bits=4):
-    from spark_b200 import dispatch, quantize
-
-    w, s, b = quantize.quantize_affine_minmax(torch.randn(n, k, generator=gen, device="cuda") * 0.05, group, bits)
-    layer = dispatch.QuantizedLinear(w, s, b, group_size=group, bits=bits)
-    host = (w.cpu().numpy().view(np.uint32), _f32(s), _f32(b), group, bits)
-    return layer, host
-
-
-def test_dispatch_attention_output_fused_route():
-    """``dispatch.dispatch_attention_output`` with a bias-free BF16 gate Linear and
-    an affine out_proj: ``sb_head_gate`` then the affine kernel, against the
-    oracle's head gate and affine linear."""
-    _need_cuda()
-    from spark_b200 import dispatch
-
-    gen = torch.Generator(device="cuda").manual_seed(11)
-    b, l, hid, heads, d = 1, 3, 512, 4, 256
-    x = torch.randn(b, l, hid, generator=gen, device="cuda").bfloat16()
-    output = torch.randn(b, heads, l, d, generator=gen, device="cuda").bfloat16()
-    gate = torch.nn.Linear(hid, heads, bias=False, device="cuda", dtype=torch.bfloat16)
-    with torch.no_grad():
-        gate.weight.copy_(torch.randn(heads, hid, generator=gen, device="cuda") * 0.05)
-    out_proj, host = _qlinear(gen, hid, heads * d)
-    got = _f32(dispatch.dispatch_attention_output(x, output, gate, out_proj))
-    attn = _f32(output).transpose(0, 2, 1, 3).reshape(b * l, heads, d)
-    gated = formats.round_bf16(ref.head_gate(_f32(x).reshape(b * l, hid), _f32(gate.weight), attn).astype(np.float32))
-    want = ref.affine_linear(gated.reshape(b * l, heads * d), *host).reshape(b, l, hid)
-    _close(got, want)
-
-
-def test_dispatch_ffn_fused_route():
-    """``dispatch.dispatch_ffn`` with an RMSNorm and affine gate/up/down: the
-    residual, ``sb_rms_norm``, the affine kernels and the GELU gate, against the
-    oracle step by step (bf16 at each of the reference's rounding points)."""
-    _need_cuda()
-    from spark_b200 import dispatch
-
-    class MLP(torch.nn.Module):
-        def __init__(self, gate_proj, up_proj, down_proj):
-            super().__init__()
-            self.gate_proj, self.up_proj, self.down_proj = gate_proj, up_proj, down_proj
-
-    gen = torch.Generator(device="cuda").manual_seed(12)
-    hid, inter = 512, 1024
-    x = torch.randn(1, 3, hid, generator=gen, device="cuda").bfloat16()
-    attn = torch.randn(1, 3, hid, generator=gen, device="cuda").bfloat16()
-    norm = torch.nn.RMSNorm(hid, eps=1e-6, device="cuda", dtype=torch.bfloat16)
-    with torch.no_grad():
-        norm.weight.copy_(1 + 0.1 * torch.randn(hid, generator=gen, device="cuda"))
-    (gp, gh), (up, uh), (dp, dh) = (_qlinear(gen, inter, hid), _qlinear(gen, inter, hid), _qlinear(gen, hid, inter))
-    got = _f32(dispatch.dispatch_ffn(x, attn, norm, MLP(gp, up, dp), mlp_type=MLP))
-
-    def r(v):
-        return formats.round_bf16(np.asarray(v, np.float32)).astype(np.float64)
-
-    h = r(_f32(x) + _f32(attn))
-    n = r(ref.rms_norm(h, _f32(norm.weight), 1e-6))
-    a = r(ref.gelu_glu(r(ref.affine_linear(n, *gh)), r(ref.affine_linear(n, *uh))))
-    want = r(h + r(ref.affine_linear(a, *dh)))
-    _close(got, want)
