@@ -91,5 +91,3 @@ def test_head_gate_matches_oracle():
     attn = torch.randn(m, heads, d, generator=gen, device="cuda").bfloat16()
     out = ops.head_gate(x, w, attn)
     _close(_f32(out), ref.head_gate(_f32(x), _f32(w), _f32(attn)))
-
-
