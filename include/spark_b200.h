@@ -258,7 +258,14 @@ int sb_bf16_sdpa_multiquery(const void* q, const void* k, const void* v, void* o
  * scale * q.K, softmax and P.V accumulate in fp32; causal != 0 applies the
  * bottom-right causal mask (query l of L sees keys [0, N-L+l]). bits 2/4/8,
  * group 32/64/128, dk/dv multiples of the group <= 256, H % KH == 0.
- * Workspace: sb_affine_sdpa_workspace_size bytes (0 = single-split launch).
+ * Single-query decode at dk = dv = 128 or 256 (4/8-bit, BF16/F16 q, H/KH in
+ * {1, 2, 4, 8}, 16-byte aligned packed codes) runs on the tensor cores: K and
+ * V enter the dot products as fp16 values of scale * code + bias (one
+ * rounding, relative 2^-11; K/V magnitudes must lie within about 1e-4 ... 6.5e4),
+ * with fp32 scores, softmax and accumulation.
+ * Workspace: sb_affine_sdpa_workspace_size bytes (0 = single-split launch);
+ * it must be 16-byte aligned for the decode kernels' split merge (else they
+ * run one split).
  */
 int sb_affine_sdpa(const void* q, int dtype, const void* k_packed, const void* k_scales,
                    const void* k_biases, const void* v_packed, const void* v_scales,
