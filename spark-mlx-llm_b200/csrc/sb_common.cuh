@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "spark_b200.h"
@@ -24,6 +25,23 @@ int check_launch(const char* what);
   } while (0)
 
 inline cudaStream_t as_stream(void* stream) { return static_cast<cudaStream_t>(stream); }
+
+// Multiprocessor count of the current device, cached per device index (one
+// process may drive several GPUs with different counts); 148 if the query fails.
+inline int device_sm_count() {
+  constexpr int kDevs = 64;
+  static std::atomic<int> counts[kDevs];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev >= 0 && dev < kDevs) {
+    const int cached = counts[dev].load(std::memory_order_relaxed);
+    if (cached > 0) return cached;
+  }
+  int count = 0;
+  if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0) count = 148;
+  if (dev >= 0 && dev < kDevs) counts[dev].store(count, std::memory_order_relaxed);
+  return count;
+}
 
 // 2-D TMA descriptor over a row-major byte matrix [rows][row_bytes] with a
 // [box_rows x 128 B] box and the 128-byte swizzle (16-byte units of row i are

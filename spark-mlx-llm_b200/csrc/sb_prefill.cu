@@ -548,12 +548,16 @@ namespace {
 template <int G, bool KVB, int D>
 int launch_prefill(const Params& p, int batch, int kv_heads, cudaStream_t stream) {
   constexpr int smem = KVB ? Geo<D>::kSmemBf : Geo<D>::kSmemI8;
-  static bool attr_done = false;  // per template instance; the attribute is per function
-  if (!attr_done) {
+  // the shared-memory opt-in is per function and device: once per device index
+  static std::atomic<int> attr_done[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const bool cached = dev >= 0 && dev < 64 && attr_done[dev].load(std::memory_order_relaxed);
+  if (!cached) {
     const cudaError_t e =
         cudaFuncSetAttribute(prefill_kernel<G, KVB, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return fail(SB_ECUDA, std::string("prefill attention attribute: ") + cudaGetErrorString(e));
-    attr_done = true;
+    if (dev >= 0 && dev < 64) attr_done[dev].store(1, std::memory_order_relaxed);
   }
   return launch(KVB ? "bf16_sdpa_multiquery" : "int8_sdpa_prefill", prefill_kernel<G, KVB, D>,
                 dim3(p.tiles, kv_heads, batch), dim3(kThreads), smem, stream, p);

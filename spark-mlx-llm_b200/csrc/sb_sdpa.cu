@@ -538,20 +538,8 @@ __global__ void __launch_bounds__(kSdpaWarps * 32, D == 128 ? 16 / kSdpaWarps : 
 
 namespace {
 
-// Multiprocessor count of the current device (cached per device index: one
-// process may drive GPUs with different SM counts).
-int sdpa_sms() {
-  constexpr int kDevs = 64;
-  static int counts[kDevs] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
-  if (dev >= 0 && dev < kDevs && counts[dev] > 0) return counts[dev];
-  int count = 0;
-  if (dev < 0 || cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
-    count = 148;
-  if (dev >= 0 && dev < kDevs) counts[dev] = count;  // benign race: every writer stores the same value
-  return count;
-}
+// Multiprocessor count of the current device (cached per device index).
+int sdpa_sms() { return device_sm_count(); }
 
 // Launch plan: warps per CTA (sdpa_warps) and token splits per (batch, kv
 // head): one wave of CTAs (two per SM at head_dim 128, one at 256), raised to 16 splits (one thread-block cluster,

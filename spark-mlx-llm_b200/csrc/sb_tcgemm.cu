@@ -612,15 +612,7 @@ struct TcPlan {
   size_t smem;
 };
 
-int sm_count() {
-  static int count = 0;
-  if (count == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0) count = 148;
-  }
-  return count;
-}
+int sm_count() { return device_sm_count(); }
 
 int raw_tile_bytes(int tw) { return tw == TW_S8 ? 0 : kBM * 128; }
 

@@ -263,17 +263,7 @@ __global__ void __launch_bounds__(kI8Warps * 32, 4) i8_gemv_kernel(const __grid_
 
 namespace {
 
-int sms() {
-  static int count = 0;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
-      count = 148;
-  });
-  return count;
-}
+int sms() { return device_sm_count(); }
 
 struct I8Plan {
   int rowblocks, groups, splits;
