@@ -1044,14 +1044,22 @@ int max_active_clusters(const void* kernel, int parts, int threads, size_t smem,
   return n;
 }
 
-// One-time function attributes: the shared-memory opt-in and cluster sizes above 8.
+// Function attributes, once per kernel and device: the shared-memory opt-in and
+// cluster sizes above 8.
 bool prepare_kernel(const void* kernel, bool* large_clusters) {
+  struct Prepared {
+    const void* kernel;
+    int device;
+    bool large;
+  };
   static std::mutex mu;
-  static std::vector<std::pair<const void*, bool>> done;
+  static std::vector<Prepared> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
-  for (const auto& d : done)
-    if (d.first == kernel) {
-      *large_clusters = d.second;
+  for (const Prepared& d : done)
+    if (d.kernel == kernel && d.device == dev) {
+      *large_clusters = d.large;
       return true;
     }
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) != cudaSuccess) {
@@ -1060,7 +1068,7 @@ bool prepare_kernel(const void* kernel, bool* large_clusters) {
   }
   bool large = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
   if (!large) cudaGetLastError();
-  done.emplace_back(kernel, large);
+  done.push_back({kernel, dev, large});
   *large_clusters = large;
   return true;
 }

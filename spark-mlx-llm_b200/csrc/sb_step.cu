@@ -1757,15 +1757,21 @@ extern "C" int sb_step_run(const sb_step_desc* d, void* stream) {
   p.slots = std::min(kMaxSlots, (max_smem - fixed) / g.slot_bytes);
   SB_REQUIRE(p.slots >= 4, "not enough shared memory for the weight ring");
   const size_t smem = static_cast<size_t>(fixed) + static_cast<size_t>(p.slots) * g.slot_bytes;
-  static std::once_flag attr_once;
-  static cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once, [&] {
-    attr_err = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
-    if (attr_err == cudaSuccess)
-      attr_err = cudaFuncSetAttribute(step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                      cudaSharedmemCarveoutMaxShared);
-  });
-  if (attr_err != cudaSuccess) return fail(SB_ECUDA, std::string("step kernel attribute: ") + cudaGetErrorString(attr_err));
+  {
+    // the attributes are per function and device: set them once per device index
+    static std::atomic<int> attr_done[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_done[dev].load(std::memory_order_relaxed)) {
+      cudaError_t attr_err = cudaFuncSetAttribute(step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, max_smem);
+      if (attr_err == cudaSuccess)
+        attr_err = cudaFuncSetAttribute(step_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                        cudaSharedmemCarveoutMaxShared);
+      if (attr_err != cudaSuccess)
+        return fail(SB_ECUDA, std::string("step kernel attribute: ") + cudaGetErrorString(attr_err));
+      if (dev >= 0 && dev < 64) attr_done[dev].store(1, std::memory_order_relaxed);
+    }
+  }
   {
     // every CTA must be resident at once (grid-wide joins): one per SM
     int per_sm = 0;
