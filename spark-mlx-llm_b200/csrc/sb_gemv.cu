@@ -1009,19 +1009,22 @@ constexpr int kMaxParts = 16;  // CTAs per cluster sharing one row group's K ran
 
 struct ClusterFit {
   const void* kernel;
-  int parts, threads;
+  int device, parts, threads;
   size_t smem;
   int clusters;
 };
 
-// Largest number of co-resident clusters of `parts` CTAs (cached per kernel and size).
+// Largest number of co-resident clusters of `parts` CTAs (cached per kernel, size and device).
 int max_active_clusters(const void* kernel, int parts, int threads, size_t smem, int row_groups) {
   static std::mutex mu;
   static std::vector<ClusterFit> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
   {
     std::lock_guard<std::mutex> lock(mu);
     for (const ClusterFit& c : cache)
-      if (c.kernel == kernel && c.parts == parts && c.threads == threads && c.smem == smem) return c.clusters;
+      if (c.kernel == kernel && c.device == dev && c.parts == parts && c.threads == threads && c.smem == smem)
+        return c.clusters;
   }
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(parts, std::max(1, row_groups));
@@ -1040,7 +1043,7 @@ int max_active_clusters(const void* kernel, int parts, int threads, size_t smem,
     n = 0;
   }
   std::lock_guard<std::mutex> lock(mu);
-  cache.push_back({kernel, parts, threads, smem, n});
+  cache.push_back({kernel, dev, parts, threads, smem, n});
   return n;
 }
 
